@@ -1,0 +1,244 @@
+/*
+ * kudacuda.h -- stable C ABI of the B200 (sm_100a) KudaCuda decode library.
+ *
+ * Part 1 keeps every symbol of the reference ABI (include/kudacuda.h:19-267 of
+ * lijeuki/KudaCuda) with identical names, argument order and types, so the
+ * reference's ctypes bridge (python/kudacuda_sidecar.py:259-419) binds this
+ * library unchanged.  Part 2 adds versioned sm100 entry points (new names,
+ * never changed signatures -- the way the reference itself added
+ * kudacuda_qwen2_swiglu_nf4_bf16).
+ *
+ * Conventions (reference runtime/kudacuda_runtime.cu):
+ *   - device pointers and the stream are uint64_t (a cudaStream_t value);
+ *   - sizes are int64_t; epsilon and scale are float;
+ *   - return 0 on success and 1 on failure; the message is available from
+ *     kudacuda_last_error(handle) and is cleared by the next success;
+ *   - every op call before kudacuda_freeze fails;
+ *   - launches are asynchronous on the caller's stream and never synchronise
+ *     (the one exception, kudacuda_sm100_graph_step_host, says so);
+ *   - the caller owns all tensors and workspaces; the handle owns only its
+ *     graph and a small scratch area allocated once by kudacuda_freeze.
+ */
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#define KUDACUDA_API __attribute__((visibility("default")))
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ===================== Part 1: reference ABI ===================== */
+
+/* runtime/kudacuda_runtime.cu:266 -- create a handle bound to device_id. */
+KUDACUDA_API void* kudacuda_create(int device_id);
+
+/* runtime/kudacuda_runtime.cu:282 -- finish set-up; ops are accepted after it. */
+KUDACUDA_API int kudacuda_freeze(void* handle);
+
+/* runtime/kudacuda_runtime.cu:298-327 -- 1 if the tactic exists in this
+ * library's tactic table and accepts (batch_size, seq_len), else 0. */
+KUDACUDA_API int kudacuda_can_dispatch(void* handle, const char* tactic_name, int64_t batch_size,
+                                       int64_t seq_len);
+
+/* kernels/vector_add.cu:11-20 -- fp32 output = a + b. */
+KUDACUDA_API int kudacuda_vector_add(void* handle, uint64_t a, uint64_t b, uint64_t output, int64_t count,
+                                     uint64_t stream);
+
+/* kernels/common/rmsnorm.cuh:11-47 -- fp32 row-wise RMSNorm. */
+KUDACUDA_API int kudacuda_rmsnorm(void* handle, uint64_t input, uint64_t weight, uint64_t output, int64_t rows,
+                                  int64_t hidden, float epsilon, uint64_t stream);
+
+/* kernels/common/rmsnorm_qkv_reference.cuh:12-66 -- dense fp16 RMSNorm + [3H,H] QKV. */
+KUDACUDA_API int kudacuda_fused_rmsnorm_qkv(void* handle, uint64_t input, uint64_t norm_weight,
+                                            uint64_t qkv_weight, uint64_t bias, uint64_t output, int64_t rows,
+                                            int64_t hidden, float epsilon, uint64_t stream);
+
+/* runtime/kudacuda_runtime.cu:465 (v1), :541 (v2), :619 (v3) -- fp16 RMSNorm +
+ * NF4 Q/K/V + bias, Qwen2.5-3B contract rows=1, hidden=2048, q_out=2048,
+ * kv_out=256, blocksize=64.  All three run the same sm_100a kernel; v2/v3
+ * also write the fp32 normalised vector to normalized_workspace [rows, hidden]. */
+KUDACUDA_API int kudacuda_qwen2_fused_rmsnorm_qkv_nf4(
+    void* handle, uint64_t input, uint64_t norm_weight, uint64_t q_weight_packed, uint64_t q_absmax,
+    uint64_t q_bias, uint64_t k_weight_packed, uint64_t k_absmax, uint64_t k_bias, uint64_t v_weight_packed,
+    uint64_t v_absmax, uint64_t v_bias, uint64_t q_output, uint64_t k_output, uint64_t v_output, int64_t rows,
+    int64_t hidden, int64_t q_out, int64_t kv_out, int64_t blocksize, float epsilon, uint64_t stream);
+
+KUDACUDA_API int kudacuda_qwen2_fused_rmsnorm_qkv_nf4_v2(
+    void* handle, uint64_t input, uint64_t norm_weight, uint64_t q_weight_packed, uint64_t q_absmax,
+    uint64_t q_bias, uint64_t k_weight_packed, uint64_t k_absmax, uint64_t k_bias, uint64_t v_weight_packed,
+    uint64_t v_absmax, uint64_t v_bias, uint64_t normalized_workspace, uint64_t q_output, uint64_t k_output,
+    uint64_t v_output, int64_t rows, int64_t hidden, int64_t q_out, int64_t kv_out, int64_t blocksize,
+    float epsilon, uint64_t stream);
+
+KUDACUDA_API int kudacuda_qwen2_fused_rmsnorm_qkv_nf4_v3(
+    void* handle, uint64_t input, uint64_t norm_weight, uint64_t q_weight_packed, uint64_t q_absmax,
+    uint64_t q_bias, uint64_t k_weight_packed, uint64_t k_absmax, uint64_t k_bias, uint64_t v_weight_packed,
+    uint64_t v_absmax, uint64_t v_bias, uint64_t normalized_workspace, uint64_t q_output, uint64_t k_output,
+    uint64_t v_output, int64_t rows, int64_t hidden, int64_t q_out, int64_t kv_out, int64_t blocksize,
+    float epsilon, uint64_t stream);
+
+/* runtime/kudacuda_runtime.cu:697 (fp16), :753 (bf16) -- RMSNorm + NF4
+ * gate/up + SwiGLU, contract rows=1, hidden=2048, intermediate=11008, blocksize=64. */
+KUDACUDA_API int kudacuda_qwen2_swiglu_nf4(void* handle, uint64_t input, uint64_t norm_weight,
+                                           uint64_t gate_weight_packed, uint64_t gate_absmax,
+                                           uint64_t up_weight_packed, uint64_t up_absmax, uint64_t output,
+                                           int64_t rows, int64_t hidden, int64_t intermediate, int64_t blocksize,
+                                           float epsilon, uint64_t stream);
+
+KUDACUDA_API int kudacuda_qwen2_swiglu_nf4_bf16(void* handle, uint64_t input, uint64_t norm_weight,
+                                                uint64_t gate_weight_packed, uint64_t gate_absmax,
+                                                uint64_t up_weight_packed, uint64_t up_absmax, uint64_t output,
+                                                int64_t rows, int64_t hidden, int64_t intermediate,
+                                                int64_t blocksize, float epsilon, uint64_t stream);
+
+/* runtime/kudacuda_runtime.cu:808 -- fp16 GQA decode with a caller workspace
+ * of query_heads*8*(2+head_dim) floats; kv_capacity=512, length on device. */
+KUDACUDA_API int kudacuda_qwen2_gqa_decode_workspace_v3(void* handle, uint64_t query, uint64_t key_cache,
+                                                        uint64_t value_cache, uint64_t output, uint64_t workspace,
+                                                        uint64_t kv_len_device, int64_t batch_size,
+                                                        int64_t query_len, int64_t kv_capacity,
+                                                        int64_t query_heads, int64_t kv_heads, int64_t head_dim,
+                                                        float scale, uint64_t stream);
+
+/* runtime/kudacuda_runtime.cu:868 -- fp16 GQA decode, kv_len 1..2048. */
+KUDACUDA_API int kudacuda_qwen2_gqa_decode(void* handle, uint64_t query, uint64_t key_cache, uint64_t value_cache,
+                                           uint64_t output, int64_t batch_size, int64_t query_len, int64_t kv_len,
+                                           int64_t query_heads, int64_t kv_heads, int64_t head_dim, float scale,
+                                           uint64_t stream);
+
+/* runtime/kudacuda_runtime.cu:927 -- graph variant: length read from
+ * kv_len_device (int32) at run time, caches strided by kv_capacity. */
+KUDACUDA_API int kudacuda_qwen2_gqa_decode_graph(void* handle, uint64_t query, uint64_t key_cache,
+                                                 uint64_t value_cache, uint64_t output, int64_t batch_size,
+                                                 int64_t query_len, int64_t kv_capacity, int64_t query_heads,
+                                                 int64_t kv_heads, int64_t head_dim, float scale,
+                                                 uint64_t kv_len_device, uint64_t stream);
+
+/* runtime/kudacuda_runtime.cu:986, :1045 -- experimental variants, kv_len 1..512. */
+KUDACUDA_API int kudacuda_qwen2_gqa_decode_group_tiled(void* handle, uint64_t query, uint64_t key_cache,
+                                                       uint64_t value_cache, uint64_t output, int64_t batch_size,
+                                                       int64_t query_len, int64_t kv_len, int64_t query_heads,
+                                                       int64_t kv_heads, int64_t head_dim, float scale,
+                                                       uint64_t stream);
+
+KUDACUDA_API int kudacuda_qwen2_gqa_decode_vectorized(void* handle, uint64_t query, uint64_t key_cache,
+                                                      uint64_t value_cache, uint64_t output, int64_t batch_size,
+                                                      int64_t query_len, int64_t kv_len, int64_t query_heads,
+                                                      int64_t kv_heads, int64_t head_dim, float scale,
+                                                      uint64_t stream);
+
+/* runtime/kudacuda_runtime.cu:1104-1212 -- CUDA graph lifecycle on one handle. */
+KUDACUDA_API int kudacuda_begin_capture(void* handle, uint64_t stream);
+KUDACUDA_API int kudacuda_end_capture(void* handle, uint64_t stream);
+KUDACUDA_API int kudacuda_replay_graph(void* handle, uint64_t stream);
+KUDACUDA_API int kudacuda_reset_graph(void* handle);
+
+/* runtime/kudacuda_runtime.cu:1216-1222, :1224-1226. */
+KUDACUDA_API const char* kudacuda_last_error(void* handle);
+KUDACUDA_API void kudacuda_destroy(void* handle);
+
+/* ===================== Part 2: sm100 additions ===================== */
+/* dtype codes: 0 = float32, 1 = float16, 2 = bfloat16. */
+
+/* Generic batch-1 NF4 GEMV: output[r] = sum_k x[k] * W[r,k] (+ bias[r]).
+ * W is bitsandbytes NF4 (packed [rows*k/2] u8, 16-byte aligned; fp32 absmax
+ * [rows*k/blocksize]); k % 64 == 0, blocksize == 64.  Supported (x, out)
+ * dtypes: (2,2) (2,0) (1,1) (1,0) (0,0) (0,2); bias has the output dtype.
+ * No reference counterpart: the reference runs this GEMV in bitsandbytes
+ * (python/kudacuda_sidecar.py:947, :1746). */
+KUDACUDA_API int kudacuda_sm100_nf4_gemv(void* handle, uint64_t x, int x_dtype, uint64_t weight_packed,
+                                         uint64_t absmax, uint64_t bias, uint64_t output, int out_dtype,
+                                         int64_t rows, int64_t k, int64_t blocksize, uint64_t stream);
+
+/* o_proj / down_proj in Transformers order: residual[r] = bf16(residual[r] +
+ * bf16(x . W[r])), x and residual bf16.  Replaces bnb o_proj/down_proj plus
+ * the residual add (python/kudacuda_sidecar.py:947, :1746-1747). */
+KUDACUDA_API int kudacuda_sm100_nf4_linear_residual_bf16(void* handle, uint64_t x, uint64_t weight_packed,
+                                                         uint64_t absmax, uint64_t residual, int64_t rows,
+                                                         int64_t k, int64_t blocksize, uint64_t stream);
+
+/* Bit-exact NF4 dequant: out[i] = level[code(i)] * absmax[i/blocksize]
+ * (kernels/common/nf4_device.cuh:29-40), out dtype 0 (exact) or 2/1 (rounded). */
+KUDACUDA_API int kudacuda_sm100_nf4_dequantize(void* handle, uint64_t weight_packed, uint64_t absmax,
+                                               uint64_t output, int out_dtype, int64_t n, int64_t blocksize,
+                                               uint64_t stream);
+
+/* Blockwise NF4 quantiser (bitsandbytes' algorithm; blocksize 64). */
+KUDACUDA_API int kudacuda_sm100_nf4_quantize(void* handle, uint64_t input, int input_dtype,
+                                             uint64_t weight_packed, uint64_t absmax, int64_t n, int64_t blocksize,
+                                             uint64_t stream);
+
+/* Qwen2/Llama attention input block, bf16, Transformers rounding order:
+ * RMSNorm -> NF4 q/k/v (+ optional bf16 biases) -> RoPE (bf16 cos/sin tables
+ * [max_position][head_dim/2]) -> q to q_output [q_heads*head_dim], k/v appended
+ * to key/value_cache [kv_heads][kv_capacity][head_dim] at *position_device
+ * (int32).  Replaces the sidecar path python/kudacuda_sidecar.py:824-855 and
+ * GraphStaticCache.update (python/kudacuda_static_decode.py:147-153). */
+KUDACUDA_API int kudacuda_sm100_rmsnorm_qkv_rope_nf4_bf16(
+    void* handle, uint64_t input, uint64_t norm_weight, uint64_t q_weight_packed, uint64_t q_absmax,
+    uint64_t q_bias, uint64_t k_weight_packed, uint64_t k_absmax, uint64_t k_bias, uint64_t v_weight_packed,
+    uint64_t v_absmax, uint64_t v_bias, uint64_t rope_cos, uint64_t rope_sin, uint64_t position_device,
+    uint64_t q_output, uint64_t key_cache, uint64_t value_cache, int64_t hidden, int64_t q_heads,
+    int64_t kv_heads, int64_t head_dim, int64_t kv_capacity, int64_t max_position, int64_t blocksize,
+    float epsilon, uint64_t stream);
+
+/* MLP input block, bf16, Transformers rounding order: RMSNorm -> NF4 gate/up ->
+ * bf16(bf16(silu(g)) * u).  Any hidden/intermediate (k % 64 == 0). */
+KUDACUDA_API int kudacuda_sm100_swiglu_nf4_bf16(void* handle, uint64_t input, uint64_t norm_weight,
+                                                uint64_t gate_weight_packed, uint64_t gate_absmax,
+                                                uint64_t up_weight_packed, uint64_t up_absmax, uint64_t output,
+                                                int64_t hidden, int64_t intermediate, int64_t blocksize,
+                                                float epsilon, uint64_t stream);
+
+/* Split-KV GQA flash-decode (dtype 1 or 2), head_dim 128, query_heads /
+ * kv_heads in {1,2,4,8}, batch B independent sequences.  The length comes
+ * from kv_len_device (int32, graph-safe) when it is non-zero, else kv_len.
+ * Caches are [B][kv_heads][kv_stride][128].  workspace: at least
+ * kudacuda_sm100_gqa_workspace_bytes(...) bytes; tickets: B*kv_heads int32
+ * that are zero before the first call (the kernel leaves them zero). */
+KUDACUDA_API int kudacuda_sm100_gqa_decode(void* handle, uint64_t query, uint64_t key_cache, uint64_t value_cache,
+                                           uint64_t output, uint64_t workspace, int64_t workspace_bytes,
+                                           uint64_t tickets, uint64_t kv_len_device, int dtype, int64_t batch_size,
+                                           int64_t kv_len, int64_t kv_stride, int64_t query_heads,
+                                           int64_t kv_heads, int64_t head_dim, float scale, uint64_t stream);
+KUDACUDA_API int64_t kudacuda_sm100_gqa_workspace_bytes(int64_t batch_size, int64_t query_heads,
+                                                        int64_t kv_heads, int64_t kv_extent, int64_t head_dim);
+
+/* Final RMSNorm + tied bf16 lm_head [vocab, hidden] + greedy argmax on the
+ * device (lowest index on ties), token written to token_out (int32); logits
+ * (bf16 [vocab]) written when non-zero.  workspace >=
+ * kudacuda_sm100_lm_head_workspace_bytes(); ticket: one int32, zero before
+ * the first call.  Replaces lm_head + argmax in Transformers
+ * (tools/benchmark/benchmark_gemma.py:324, :350). */
+KUDACUDA_API int kudacuda_sm100_lm_head_argmax_bf16(void* handle, uint64_t hidden_state, uint64_t final_norm,
+                                                    uint64_t embedding, uint64_t logits, uint64_t token_out,
+                                                    uint64_t workspace, int64_t workspace_bytes, uint64_t ticket,
+                                                    int64_t vocab, int64_t hidden, float epsilon, uint64_t stream);
+KUDACUDA_API int64_t kudacuda_sm100_lm_head_workspace_bytes(void);
+
+/* output[0:hidden] = embedding[*token_device] (bf16 rows). */
+KUDACUDA_API int kudacuda_sm100_embedding_bf16(void* handle, uint64_t embedding, uint64_t token_device,
+                                               uint64_t output, int64_t vocab, int64_t hidden, uint64_t stream);
+
+/* One end-to-end step of a captured graph with host buffers: copy in_bytes
+ * from host_in to device_in, replay the handle's graph, copy out_bytes from
+ * device_out to host_out, and wait for the stream (this call synchronises). */
+KUDACUDA_API int kudacuda_sm100_graph_step_host(void* handle, const void* host_in, uint64_t device_in,
+                                                int64_t in_bytes, void* host_out, uint64_t device_out,
+                                                int64_t out_bytes, uint64_t stream);
+
+/* Device-side error word written by the kernels (bit 0: activation outside
+ * the f16 range, 1: position outside the cache, 2: kv length outside the
+ * cache, 3: token id outside the vocabulary).  Reading synchronises the
+ * handle's device; clear != 0 resets it. */
+KUDACUDA_API int kudacuda_sm100_error_word(void* handle, int* out_word, int clear);
+
+/* Library / build identification: "sm_100a". */
+KUDACUDA_API const char* kudacuda_sm100_target_arch(void);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,129 @@
+// kc_launch.h -- host-side launchers for the sm_100a kernels (internal; the
+// public surface is the C ABI in include/kudacuda.h).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace kc {
+
+// dtype codes shared by the C ABI and the kernels
+enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
+
+// Launch with programmatic stream serialization so the kernel's prologue
+// (table build, weight prefetch) overlaps the tail of the previous kernel.
+template <typename Kernel, typename... Args>
+inline cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+int device_sm_count();
+int current_device_index();
+
+// ---- NF4 GEMV family -------------------------------------------------------
+// dtype codes: 0 = f32, 1 = f16, 2 = bf16
+struct GemvMat {
+    const uint8_t* packed;
+    const float* absmax;
+    int rows;
+};
+
+// generic y = x W^T (+bias); x dtype xt, out/bias dtype ot
+cudaError_t nf4_gemv(const void* x, int xt, GemvMat w, const void* bias, void* out, int ot, int K,
+                     int* err, cudaStream_t s);
+// resid = bf16(resid + bf16(x W^T)), x bf16 (o_proj / down_proj, Transformers order)
+cudaError_t nf4_gemv_residual_bf16(const void* x, GemvMat w, void* resid, int K, int* err,
+                                   cudaStream_t s);
+// reference-ABI fused RMSNorm + Q/K/V (fp32-normalised), io dtype dt (1 or 2)
+cudaError_t nf4_qkv_ref(const void* x, const void* norm_w, int dt, float eps, GemvMat q, GemvMat k,
+                        GemvMat v, const void* qb, const void* kb, const void* vb, void* qo, void* ko,
+                        void* vo, float* norm_ws, int K, int* err, cudaStream_t s);
+// reference-ABI fused RMSNorm + gate/up SwiGLU, io dtype dt
+cudaError_t nf4_swiglu_ref(const void* x, const void* norm_w, int dt, float eps, GemvMat g, GemvMat u,
+                           void* out, int K, int* err, cudaStream_t s);
+// Transformers-order bf16 RMSNorm + gate/up SwiGLU
+cudaError_t nf4_swiglu_hf_bf16(const void* x, const void* norm_w, float eps, GemvMat g, GemvMat u,
+                               void* out, int K, int* err, cudaStream_t s);
+// Transformers-order bf16 RMSNorm + Q/K/V + bias + RoPE + KV append at *pos
+struct QkvRopeArgs {
+    const void* x;
+    const void* norm_w;
+    float eps;
+    GemvMat q, k, v;
+    const void *qb, *kb, *vb;  // bf16, may be null
+    const uint16_t* rope_cos;  // bf16 [max_pos][head_dim/2]
+    const uint16_t* rope_sin;
+    int max_pos;
+    const int32_t* pos_dev;
+    void* q_out;                // bf16 [q_heads*head_dim]
+    void* key_cache;            // bf16 [kv_heads][kv_cap][head_dim]
+    void* value_cache;
+    int q_heads, kv_heads, head_dim, kv_cap, K;
+    int* err;
+};
+cudaError_t nf4_qkv_rope_hf_bf16(const QkvRopeArgs& a, cudaStream_t s);
+
+cudaError_t nf4_dequantize(const uint8_t* packed, const float* absmax, int64_t n, int blocksize,
+                           void* out, int ot, cudaStream_t s);
+cudaError_t nf4_quantize(const void* in, int it, int64_t n, int blocksize, uint8_t* packed,
+                         float* absmax, cudaStream_t s);
+
+// ---- attention ---------------------------------------------------------------
+struct GqaArgs {
+    const void* q;       // [B][q_heads][d]
+    const void* kcache;  // [B][kv_heads][stride][d]
+    const void* vcache;
+    void* out;           // [B][q_heads][d]
+    float* partials;     // [B][q_heads][nsplit][d + 2]
+    int* counters;       // [B * kv_heads], zero between launches (null: separate combine)
+    const int32_t* kv_len_dev;  // null: use kv_len
+    int kv_len;
+    int stride;
+    int batch, q_heads, kv_heads, head_dim;
+    float scale;
+    int chunk, nsplit;
+    int* err;
+};
+// dt: 1 = f16, 2 = bf16.  Chooses split size from the capacity / length.
+void gqa_plan_splits(int kv_extent, int batch, int kv_heads, int max_splits, int* chunk, int* nsplit);
+cudaError_t gqa_decode(GqaArgs a, int dt, cudaStream_t s);
+size_t gqa_partials_floats(int batch, int q_heads, int nsplit, int head_dim);
+
+// ---- lm_head / embedding ------------------------------------------------------
+struct LmHeadArgs {
+    const void* hidden;      // bf16 [H] residual stream
+    const void* final_norm;  // bf16 [H]
+    const void* emb;         // bf16 [V][H] (tied embedding)
+    void* logits;            // bf16 [V] or null
+    int32_t* token_out;      // argmax token
+    float* partials;         // [2 * grid] scratch
+    int* counter;            // zero between launches
+    int vocab, H;
+    float eps;
+    int* err;
+};
+cudaError_t lm_head_argmax_bf16(const LmHeadArgs& a, cudaStream_t s);
+int lm_head_grid();
+cudaError_t embedding_gather_bf16(const void* emb, const int32_t* token_dev, void* out, int H, int vocab,
+                                  int* err, cudaStream_t s);
+
+// ---- small ABI-compatibility ops ---------------------------------------------
+cudaError_t vector_add_f32(const float* a, const float* b, float* out, int64_t n, cudaStream_t s);
+cudaError_t rmsnorm_f32(const float* x, const float* w, float* out, int64_t rows, int64_t hidden,
+                        float eps, cudaStream_t s);
+cudaError_t dense_rmsnorm_qkv_f16(const void* x, const void* norm_w, const void* w, const void* bias,
+                                  void* out, int64_t rows, int64_t hidden, float eps, cudaStream_t s);
+
+}  // namespace kc

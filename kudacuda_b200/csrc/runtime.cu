@@ -1,0 +1,809 @@
+// runtime.cu -- the C ABI (include/kudacuda.h): handle, contract guards, graph
+// lifecycle, and dispatch onto the sm_100a kernels.
+//
+// Mirrors runtime/kudacuda_runtime.cu of the reference: every entry point
+// null-checks pointers, enforces the exact shape contract of its tactic,
+// launches on the caller's stream, records failures in the per-handle
+// last_error and returns 0/1.  Nothing here synchronises except
+// kudacuda_sm100_graph_step_host and kudacuda_sm100_error_word, and nothing
+// allocates per call: the small scratch area the reference-ABI attention
+// entries need (they take no workspace argument) is allocated once by
+// kudacuda_freeze.
+#include "../../include/kudacuda.h"
+#include "kc_launch.h"
+#include "registry.h"
+
+#include <cstring>
+#include <new>
+#include <string>
+
+namespace kc {
+namespace {
+
+// scratch sizing for the reference-ABI GQA entries: batch 1, 16 query heads,
+// up to 2048 tokens in chunks of >= 16 -> at most 128 splits.
+constexpr int kRefGqaMaxSplits = 128;
+constexpr int kRefGqaHeads = 16;
+
+struct Handle {
+    explicit Handle(int dev) : device_id(dev) {}
+    ~Handle() {
+        if (graph_exec != nullptr) cudaGraphExecDestroy(graph_exec);
+        if (graph != nullptr) cudaGraphDestroy(graph);
+        if (scratch != nullptr) cudaFree(scratch);
+    }
+    void set_error(const std::string& m) { last_error = m; }
+    void set_cuda_error(const char* op, cudaError_t st) {
+        last_error = std::string(op) + ": " + cudaGetErrorString(st);
+    }
+
+    int device_id;
+    bool device_ready = false;
+    bool frozen = false;
+    bool capturing = false;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+    std::string last_error;
+    // scratch: [err word (256 B)][gqa tickets (256 B)][lm ticket (256 B)][gqa partials][lm partials]
+    char* scratch = nullptr;
+    int* err_word = nullptr;
+    int* gqa_tickets = nullptr;
+    int* lm_ticket = nullptr;
+    float* gqa_partials = nullptr;
+    float* lm_partials = nullptr;
+};
+
+Handle* as_handle(void* h) { return reinterpret_cast<Handle*>(h); }
+
+bool ready(Handle* h, const char* name) {
+    if (h == nullptr) return false;
+    if (!h->frozen) {
+        h->set_error(std::string(name) + " called before kudacuda_freeze");
+        return false;
+    }
+    return true;
+}
+
+int finish(Handle* h, const char* op, cudaError_t st) {
+    if (st != cudaSuccess) {
+        h->set_cuda_error(op, st);
+        return 1;
+    }
+    h->last_error.clear();
+    return 0;
+}
+
+template <typename T>
+T* P(uint64_t v) {
+    return reinterpret_cast<T*>(static_cast<uintptr_t>(v));
+}
+cudaStream_t S(uint64_t v) { return reinterpret_cast<cudaStream_t>(static_cast<uintptr_t>(v)); }
+
+size_t ref_gqa_partial_bytes() {
+    return gqa_partials_floats(1, kRefGqaHeads, kRefGqaMaxSplits, 128) * sizeof(float);
+}
+
+// Reference-ABI attention: fp16, batch 1, 16/2/128; stride = kv_len (direct)
+// or capacity (graph / device length).
+int run_ref_gqa(Handle* h, const char* op, uint64_t q, uint64_t k, uint64_t v, uint64_t out, int64_t kv_extent,
+                const int32_t* kv_len_dev, float scale, uint64_t stream, float* partials, int max_splits,
+                bool fused) {
+    GqaArgs a;
+    memset(&a, 0, sizeof(a));
+    a.q = P<const void>(q);
+    a.kcache = P<const void>(k);
+    a.vcache = P<const void>(v);
+    a.out = P<void>(out);
+    a.partials = partials;
+    a.counters = fused ? h->gqa_tickets : nullptr;
+    a.kv_len_dev = kv_len_dev;
+    a.kv_len = static_cast<int>(kv_extent);
+    a.stride = static_cast<int>(kv_extent);
+    a.batch = 1;
+    a.q_heads = 16;
+    a.kv_heads = 2;
+    a.head_dim = 128;
+    a.scale = scale;
+    a.err = h->err_word;
+    gqa_plan_splits(static_cast<int>(kv_extent), 1, 2, max_splits, &a.chunk, &a.nsplit);
+    return finish(h, op, gqa_decode(a, kF16, S(stream)));
+}
+
+}  // namespace
+}  // namespace kc
+
+using kc::as_handle;
+using kc::finish;
+using kc::GemvMat;
+using kc::Handle;
+using kc::P;
+using kc::ready;
+using kc::S;
+
+extern "C" {
+
+void* kudacuda_create(int device_id) {
+    auto* h = new (std::nothrow) Handle(device_id);
+    if (h == nullptr) return nullptr;
+    const cudaError_t st = cudaSetDevice(device_id);
+    if (st != cudaSuccess) {
+        h->set_cuda_error("cudaSetDevice", st);
+        return h;
+    }
+    h->device_ready = true;
+    return h;
+}
+
+int kudacuda_freeze(void* raw) {
+    Handle* h = as_handle(raw);
+    if (h == nullptr) return 1;
+    if (!h->device_ready) {
+        if (h->last_error.empty()) h->set_error("CUDA device is not ready");
+        return 1;
+    }
+    if (h->scratch == nullptr) {
+        const size_t lm_bytes = static_cast<size_t>(kc::lm_head_grid()) * 2 * sizeof(float);
+        const size_t total = 768 + kc::ref_gqa_partial_bytes() + lm_bytes;
+        cudaError_t st = cudaSetDevice(h->device_id);
+        if (st == cudaSuccess) st = cudaMalloc(reinterpret_cast<void**>(&h->scratch), total);
+        if (st == cudaSuccess) st = cudaMemset(h->scratch, 0, total);
+        if (st == cudaSuccess) st = cudaDeviceSynchronize();
+        if (st != cudaSuccess) {
+            if (h->scratch != nullptr) cudaFree(h->scratch);
+            h->scratch = nullptr;
+            h->set_cuda_error("kudacuda_freeze scratch", st);
+            return 1;
+        }
+        h->err_word = reinterpret_cast<int*>(h->scratch);
+        h->gqa_tickets = reinterpret_cast<int*>(h->scratch + 256);
+        h->lm_ticket = reinterpret_cast<int*>(h->scratch + 512);
+        h->gqa_partials = reinterpret_cast<float*>(h->scratch + 768);
+        h->lm_partials = reinterpret_cast<float*>(h->scratch + 768 + kc::ref_gqa_partial_bytes());
+    }
+    h->frozen = true;
+    h->last_error.clear();
+    return 0;
+}
+
+int kudacuda_can_dispatch(void* raw, const char* tactic_name, int64_t batch_size, int64_t seq_len) {
+    const Handle* h = as_handle(raw);
+    if (h == nullptr || !h->frozen || tactic_name == nullptr) return 0;
+    if (batch_size <= 0 || seq_len <= 0) return 0;
+    const kc::TacticEntry* t = kc::find_tactic(tactic_name);
+    if (t == nullptr) return 0;
+    if (t->max_batch > 0 && batch_size > t->max_batch) return 0;
+    if (t->seq_len > 0 && seq_len != t->seq_len) return 0;
+    return 1;
+}
+
+int kudacuda_vector_add(void* raw, uint64_t a, uint64_t b, uint64_t output, int64_t count, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_vector_add")) return 1;
+    if (a == 0 || b == 0 || output == 0) {
+        h->set_error("vector_add requires non-null device pointers");
+        return 1;
+    }
+    if (count <= 0) {
+        h->set_error("vector_add count must be positive");
+        return 1;
+    }
+    return finish(h, "vector_add_kernel", kc::vector_add_f32(P<const float>(a), P<const float>(b), P<float>(output), count, S(stream)));
+}
+
+int kudacuda_rmsnorm(void* raw, uint64_t input, uint64_t weight, uint64_t output, int64_t rows, int64_t hidden,
+                     float epsilon, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_rmsnorm")) return 1;
+    if (input == 0 || weight == 0 || output == 0) {
+        h->set_error("rmsnorm requires non-null device pointers");
+        return 1;
+    }
+    if (rows <= 0 || hidden <= 0) {
+        h->set_error("rmsnorm rows and hidden must be positive");
+        return 1;
+    }
+    if (!(epsilon > 0.0F)) {
+        h->set_error("rmsnorm epsilon must be positive");
+        return 1;
+    }
+    return finish(h, "rmsnorm_kernel",
+                  kc::rmsnorm_f32(P<const float>(input), P<const float>(weight), P<float>(output), rows, hidden, epsilon, S(stream)));
+}
+
+int kudacuda_fused_rmsnorm_qkv(void* raw, uint64_t input, uint64_t norm_weight, uint64_t qkv_weight, uint64_t bias,
+                               uint64_t output, int64_t rows, int64_t hidden, float epsilon, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_fused_rmsnorm_qkv")) return 1;
+    if (input == 0 || norm_weight == 0 || qkv_weight == 0 || output == 0) {
+        h->set_error("fused_rmsnorm_qkv requires non-null input, weights, and output pointers");
+        return 1;
+    }
+    if (rows <= 0 || hidden <= 0 || !(epsilon > 0.0F)) {
+        h->set_error("fused_rmsnorm_qkv requires positive rows, hidden, and epsilon");
+        return 1;
+    }
+    return finish(h, "fused_rmsnorm_qkv_kernel",
+                  kc::dense_rmsnorm_qkv_f16(P<const void>(input), P<const void>(norm_weight), P<const void>(qkv_weight),
+                                            P<const void>(bias), P<void>(output), rows, hidden, epsilon, S(stream)));
+}
+
+static int qkv_nf4_common(const char* name, const char* op, void* raw, uint64_t input, uint64_t norm_weight,
+                          uint64_t qw, uint64_t qa, uint64_t qb, uint64_t kw, uint64_t ka, uint64_t kb, uint64_t vw,
+                          uint64_t va, uint64_t vb, uint64_t ws, bool needs_ws, uint64_t qo, uint64_t ko, uint64_t vo,
+                          int64_t rows, int64_t hidden, int64_t q_out, int64_t kv_out, int64_t blocksize,
+                          float epsilon, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, name)) return 1;
+    if (input == 0 || norm_weight == 0 || qw == 0 || qa == 0 || qb == 0 || kw == 0 || ka == 0 || kb == 0 ||
+        vw == 0 || va == 0 || vb == 0 || qo == 0 || ko == 0 || vo == 0 || (needs_ws && ws == 0)) {
+        h->set_error(std::string(op) + " requires non-null device pointers");
+        return 1;
+    }
+    if (rows != 1 || hidden != 2048 || q_out != 2048 || kv_out != 256 || blocksize != 64 || !(epsilon > 0.0F)) {
+        h->set_error(std::string(op) +
+                     " requires rows=1, hidden=2048, q_out=2048, kv_out=256, blocksize=64, and positive epsilon");
+        return 1;
+    }
+    return finish(h, op,
+                  kc::nf4_qkv_ref(P<const void>(input), P<const void>(norm_weight), kc::kF16, epsilon,
+                                  GemvMat{P<const uint8_t>(qw), P<const float>(qa), static_cast<int>(q_out)},
+                                  GemvMat{P<const uint8_t>(kw), P<const float>(ka), static_cast<int>(kv_out)},
+                                  GemvMat{P<const uint8_t>(vw), P<const float>(va), static_cast<int>(kv_out)},
+                                  P<const void>(qb), P<const void>(kb), P<const void>(vb), P<void>(qo), P<void>(ko),
+                                  P<void>(vo), needs_ws ? P<float>(ws) : nullptr, static_cast<int>(hidden),
+                                  h->err_word, S(stream)));
+}
+
+int kudacuda_qwen2_fused_rmsnorm_qkv_nf4(void* raw, uint64_t input, uint64_t norm_weight, uint64_t qw, uint64_t qa,
+                                         uint64_t qb, uint64_t kw, uint64_t ka, uint64_t kb, uint64_t vw, uint64_t va,
+                                         uint64_t vb, uint64_t qo, uint64_t ko, uint64_t vo, int64_t rows,
+                                         int64_t hidden, int64_t q_out, int64_t kv_out, int64_t blocksize,
+                                         float epsilon, uint64_t stream) {
+    return qkv_nf4_common("kudacuda_qwen2_fused_rmsnorm_qkv_nf4", "qwen2_fused_rmsnorm_qkv_nf4", raw, input,
+                          norm_weight, qw, qa, qb, kw, ka, kb, vw, va, vb, 0, false, qo, ko, vo, rows, hidden, q_out,
+                          kv_out, blocksize, epsilon, stream);
+}
+
+int kudacuda_qwen2_fused_rmsnorm_qkv_nf4_v2(void* raw, uint64_t input, uint64_t norm_weight, uint64_t qw,
+                                            uint64_t qa, uint64_t qb, uint64_t kw, uint64_t ka, uint64_t kb,
+                                            uint64_t vw, uint64_t va, uint64_t vb, uint64_t ws, uint64_t qo,
+                                            uint64_t ko, uint64_t vo, int64_t rows, int64_t hidden, int64_t q_out,
+                                            int64_t kv_out, int64_t blocksize, float epsilon, uint64_t stream) {
+    return qkv_nf4_common("kudacuda_qwen2_fused_rmsnorm_qkv_nf4_v2", "qwen2_fused_rmsnorm_qkv_nf4_v2", raw, input,
+                          norm_weight, qw, qa, qb, kw, ka, kb, vw, va, vb, ws, true, qo, ko, vo, rows, hidden, q_out,
+                          kv_out, blocksize, epsilon, stream);
+}
+
+int kudacuda_qwen2_fused_rmsnorm_qkv_nf4_v3(void* raw, uint64_t input, uint64_t norm_weight, uint64_t qw,
+                                            uint64_t qa, uint64_t qb, uint64_t kw, uint64_t ka, uint64_t kb,
+                                            uint64_t vw, uint64_t va, uint64_t vb, uint64_t ws, uint64_t qo,
+                                            uint64_t ko, uint64_t vo, int64_t rows, int64_t hidden, int64_t q_out,
+                                            int64_t kv_out, int64_t blocksize, float epsilon, uint64_t stream) {
+    return qkv_nf4_common("kudacuda_qwen2_fused_rmsnorm_qkv_nf4_v3", "qwen2_fused_rmsnorm_qkv_nf4_v3", raw, input,
+                          norm_weight, qw, qa, qb, kw, ka, kb, vw, va, vb, ws, true, qo, ko, vo, rows, hidden, q_out,
+                          kv_out, blocksize, epsilon, stream);
+}
+
+static int swiglu_common(const char* name, const char* op, int dt, bool clear_on_success, void* raw, uint64_t input,
+                         uint64_t norm_weight, uint64_t gw, uint64_t ga, uint64_t uw, uint64_t ua, uint64_t out,
+                         int64_t rows, int64_t hidden, int64_t inter, int64_t blocksize, float epsilon,
+                         uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, name)) return 1;
+    if (input == 0 || norm_weight == 0 || gw == 0 || ga == 0 || uw == 0 || ua == 0 || out == 0) {
+        h->set_error(std::string(op) + " requires non-null device pointers");
+        return 1;
+    }
+    if (rows != 1 || hidden != 2048 || inter != 11008 || blocksize != 64 || !(epsilon > 0.0F)) {
+        h->set_error(std::string(op) +
+                     " requires rows=1, hidden=2048, intermediate=11008, blocksize=64, and positive epsilon");
+        return 1;
+    }
+    const cudaError_t st = kc::nf4_swiglu_ref(
+        P<const void>(input), P<const void>(norm_weight), dt, epsilon,
+        GemvMat{P<const uint8_t>(gw), P<const float>(ga), static_cast<int>(inter)},
+        GemvMat{P<const uint8_t>(uw), P<const float>(ua), static_cast<int>(inter)}, P<void>(out),
+        static_cast<int>(hidden), h->err_word, S(stream));
+    if (st != cudaSuccess) {
+        h->set_cuda_error(dt == kc::kF16 ? "nf4_swiglu" : "nf4_swiglu_bf16", st);
+        return 1;
+    }
+    // runtime/kudacuda_runtime.cu:750 -- the fp16 entry leaves last_error as is on success
+    if (clear_on_success) h->last_error.clear();
+    return 0;
+}
+
+int kudacuda_qwen2_swiglu_nf4(void* raw, uint64_t input, uint64_t norm_weight, uint64_t gw, uint64_t ga,
+                              uint64_t uw, uint64_t ua, uint64_t out, int64_t rows, int64_t hidden, int64_t inter,
+                              int64_t blocksize, float epsilon, uint64_t stream) {
+    return swiglu_common("kudacuda_qwen2_swiglu_nf4", "qwen2_swiglu_nf4", kc::kF16, false, raw, input, norm_weight, gw,
+                         ga, uw, ua, out, rows, hidden, inter, blocksize, epsilon, stream);
+}
+
+int kudacuda_qwen2_swiglu_nf4_bf16(void* raw, uint64_t input, uint64_t norm_weight, uint64_t gw, uint64_t ga,
+                                   uint64_t uw, uint64_t ua, uint64_t out, int64_t rows, int64_t hidden,
+                                   int64_t inter, int64_t blocksize, float epsilon, uint64_t stream) {
+    return swiglu_common("kudacuda_qwen2_swiglu_nf4_bf16", "qwen2_swiglu_nf4_bf16", kc::kBF16, true, raw, input,
+                         norm_weight, gw, ga, uw, ua, out, rows, hidden, inter, blocksize, epsilon, stream);
+}
+
+int kudacuda_qwen2_gqa_decode_workspace_v3(void* raw, uint64_t query, uint64_t key_cache, uint64_t value_cache,
+                                           uint64_t output, uint64_t workspace, uint64_t kv_len_device,
+                                           int64_t batch_size, int64_t query_len, int64_t kv_capacity,
+                                           int64_t query_heads, int64_t kv_heads, int64_t head_dim, float scale,
+                                           uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_qwen2_gqa_decode_workspace_v3")) return 1;
+    if (query == 0 || key_cache == 0 || value_cache == 0 || output == 0 || workspace == 0 || kv_len_device == 0) {
+        h->set_error("qwen2_gqa_decode_workspace_v3 requires non-null device pointers");
+        return 1;
+    }
+    if (batch_size != 1 || query_len != 1 || kv_capacity != 512 || query_heads != 16 || kv_heads != 2 ||
+        head_dim != 128 || !(scale > 0.0F)) {
+        h->set_error(
+            "qwen2_gqa_decode_workspace_v3 requires 1x1, capacity=512, heads=16/2, head_dim=128, and positive scale");
+        return 1;
+    }
+    // The caller's workspace holds query_heads * 8 * (2 + head_dim) floats
+    // (python/kudacuda_sidecar.py:685): 8 splits of 64 tokens, combined by a
+    // second kernel because there is no room for tickets.
+    return kc::run_ref_gqa(h, "qwen2_gqa_decode_workspace_v3_kernel", query, key_cache, value_cache, output, 512,
+                           P<const int32_t>(kv_len_device), scale, stream, P<float>(workspace), 8, false);
+}
+
+static int gqa_ref_direct(const char* name, const char* op, const char* guard_msg, int64_t max_len, void* raw,
+                          uint64_t query, uint64_t key_cache, uint64_t value_cache, uint64_t output,
+                          int64_t batch_size, int64_t query_len, int64_t kv_len, int64_t query_heads,
+                          int64_t kv_heads, int64_t head_dim, float scale, uint64_t stream,
+                          const int32_t* kv_len_dev) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, name)) return 1;
+    if (query == 0 || key_cache == 0 || value_cache == 0 || output == 0 ||
+        (kv_len_dev == nullptr && std::strstr(op, "graph") != nullptr)) {
+        h->set_error(std::string(op) + " requires non-null device pointers");
+        return 1;
+    }
+    if (batch_size != 1 || query_len != 1 || kv_len < 1 || kv_len > max_len || query_heads != 16 || kv_heads != 2 ||
+        head_dim != 128) {
+        h->set_error(guard_msg);
+        return 1;
+    }
+    if (!(scale > 0.0F)) {
+        h->set_error(std::string(op) + " scale must be positive");
+        return 1;
+    }
+    return kc::run_ref_gqa(h, (std::string(op) + "_kernel").c_str(), query, key_cache, value_cache, output, kv_len,
+                           kv_len_dev, scale, stream, h->gqa_partials, kc::kRefGqaMaxSplits, true);
+}
+
+int kudacuda_qwen2_gqa_decode(void* raw, uint64_t query, uint64_t key_cache, uint64_t value_cache, uint64_t output,
+                              int64_t batch_size, int64_t query_len, int64_t kv_len, int64_t query_heads,
+                              int64_t kv_heads, int64_t head_dim, float scale, uint64_t stream) {
+    return gqa_ref_direct("kudacuda_qwen2_gqa_decode", "qwen2_gqa_decode",
+                          "qwen2_gqa_decode requires batch=1, query_len=1, kv_len=1..2048, q_heads=16, kv_heads=2, "
+                          "head_dim=128",
+                          2048, raw, query, key_cache, value_cache, output, batch_size, query_len, kv_len, query_heads,
+                          kv_heads, head_dim, scale, stream, nullptr);
+}
+
+int kudacuda_qwen2_gqa_decode_graph(void* raw, uint64_t query, uint64_t key_cache, uint64_t value_cache,
+                                    uint64_t output, int64_t batch_size, int64_t query_len, int64_t kv_capacity,
+                                    int64_t query_heads, int64_t kv_heads, int64_t head_dim, float scale,
+                                    uint64_t kv_len_device, uint64_t stream) {
+    return gqa_ref_direct("kudacuda_qwen2_gqa_decode_graph", "qwen2_gqa_decode_graph",
+                          "qwen2_gqa_decode_graph requires batch=1, query_len=1, kv_capacity=1..512, q_heads=16, "
+                          "kv_heads=2, head_dim=128",
+                          512, raw, query, key_cache, value_cache, output, batch_size, query_len, kv_capacity,
+                          query_heads, kv_heads, head_dim, scale, stream, P<const int32_t>(kv_len_device));
+}
+
+int kudacuda_qwen2_gqa_decode_group_tiled(void* raw, uint64_t query, uint64_t key_cache, uint64_t value_cache,
+                                          uint64_t output, int64_t batch_size, int64_t query_len, int64_t kv_len,
+                                          int64_t query_heads, int64_t kv_heads, int64_t head_dim, float scale,
+                                          uint64_t stream) {
+    return gqa_ref_direct("kudacuda_qwen2_gqa_decode_group_tiled", "qwen2_gqa_decode_group_tiled",
+                          "qwen2_gqa_decode_group_tiled requires batch=1, query_len=1, kv_len=1..512, q_heads=16, "
+                          "kv_heads=2, head_dim=128",
+                          512, raw, query, key_cache, value_cache, output, batch_size, query_len, kv_len, query_heads,
+                          kv_heads, head_dim, scale, stream, nullptr);
+}
+
+int kudacuda_qwen2_gqa_decode_vectorized(void* raw, uint64_t query, uint64_t key_cache, uint64_t value_cache,
+                                         uint64_t output, int64_t batch_size, int64_t query_len, int64_t kv_len,
+                                         int64_t query_heads, int64_t kv_heads, int64_t head_dim, float scale,
+                                         uint64_t stream) {
+    return gqa_ref_direct("kudacuda_qwen2_gqa_decode_vectorized", "qwen2_gqa_decode_vectorized",
+                          "qwen2_gqa_decode_vectorized requires batch=1, query_len=1, kv_len=1..512, q_heads=16, "
+                          "kv_heads=2, head_dim=128",
+                          512, raw, query, key_cache, value_cache, output, batch_size, query_len, kv_len, query_heads,
+                          kv_heads, head_dim, scale, stream, nullptr);
+}
+
+int kudacuda_begin_capture(void* raw, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (h == nullptr || !h->frozen) {
+        if (h != nullptr) h->set_error("kudacuda_begin_capture requires a frozen handle");
+        return 1;
+    }
+    if (h->capturing) {
+        h->set_error("CUDA graph capture is already active");
+        return 1;
+    }
+    const cudaError_t st = cudaStreamBeginCapture(S(stream), cudaStreamCaptureModeGlobal);
+    if (st != cudaSuccess) {
+        h->set_cuda_error("cudaStreamBeginCapture", st);
+        return 1;
+    }
+    h->capturing = true;
+    h->last_error.clear();
+    return 0;
+}
+
+int kudacuda_end_capture(void* raw, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (h == nullptr || !h->capturing) {
+        if (h != nullptr) h->set_error("kudacuda_end_capture called without active capture");
+        return 1;
+    }
+    const cudaError_t end_st = cudaStreamEndCapture(S(stream), &h->graph);
+    h->capturing = false;
+    if (end_st != cudaSuccess) {
+        h->set_cuda_error("cudaStreamEndCapture", end_st);
+        return 1;
+    }
+    if (h->graph_exec != nullptr) {
+        cudaGraphExecDestroy(h->graph_exec);
+        h->graph_exec = nullptr;
+    }
+    const cudaError_t inst = cudaGraphInstantiate(&h->graph_exec, h->graph, 0);
+    cudaGraphDestroy(h->graph);
+    h->graph = nullptr;
+    if (inst != cudaSuccess) {
+        h->graph_exec = nullptr;
+        h->set_cuda_error("cudaGraphInstantiate", inst);
+        return 1;
+    }
+    h->last_error.clear();
+    return 0;
+}
+
+int kudacuda_replay_graph(void* raw, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (h == nullptr || h->graph_exec == nullptr) {
+        if (h != nullptr) h->set_error("kudacuda_replay_graph called before graph instantiation");
+        return 1;
+    }
+    return finish(h, "cudaGraphLaunch", cudaGraphLaunch(h->graph_exec, S(stream)));
+}
+
+int kudacuda_reset_graph(void* raw) {
+    Handle* h = as_handle(raw);
+    if (h == nullptr) return 1;
+    if (h->capturing) {
+        h->set_error("kudacuda_reset_graph called during active capture");
+        return 1;
+    }
+    if (h->graph_exec != nullptr) {
+        const cudaError_t st = cudaGraphExecDestroy(h->graph_exec);
+        if (st != cudaSuccess) {
+            h->set_cuda_error("cudaGraphExecDestroy", st);
+            return 1;
+        }
+        h->graph_exec = nullptr;
+    }
+    if (h->graph != nullptr) {
+        const cudaError_t st = cudaGraphDestroy(h->graph);
+        if (st != cudaSuccess) {
+            h->set_cuda_error("cudaGraphDestroy", st);
+            return 1;
+        }
+        h->graph = nullptr;
+    }
+    h->last_error.clear();
+    return 0;
+}
+
+const char* kudacuda_last_error(void* raw) {
+    const Handle* h = as_handle(raw);
+    if (h == nullptr) return "invalid KudaCuda handle";
+    return h->last_error.c_str();
+}
+
+void kudacuda_destroy(void* raw) { delete as_handle(raw); }
+
+// =========================== sm100 additions ===========================
+
+int kudacuda_sm100_nf4_gemv(void* raw, uint64_t x, int x_dtype, uint64_t w, uint64_t absmax, uint64_t bias,
+                            uint64_t output, int out_dtype, int64_t rows, int64_t k, int64_t blocksize,
+                            uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_nf4_gemv")) return 1;
+    if (x == 0 || w == 0 || absmax == 0 || output == 0) {
+        h->set_error("sm100_nf4_gemv requires non-null device pointers");
+        return 1;
+    }
+    if (rows < 1 || rows > (1 << 30) || k < 64 || k % 64 != 0 || k > 16384 || blocksize != 64) {
+        h->set_error("sm100_nf4_gemv requires rows>=1, k a multiple of 64 in 64..16384, blocksize=64");
+        return 1;
+    }
+    if ((w & 15u) != 0) {
+        h->set_error("sm100_nf4_gemv requires a 16-byte aligned packed weight");
+        return 1;
+    }
+    return finish(h, "nf4_gemv_kernel",
+                  kc::nf4_gemv(P<const void>(x), x_dtype, GemvMat{P<const uint8_t>(w), P<const float>(absmax), static_cast<int>(rows)},
+                               P<const void>(bias), P<void>(output), out_dtype, static_cast<int>(k), h->err_word, S(stream)));
+}
+
+int kudacuda_sm100_nf4_linear_residual_bf16(void* raw, uint64_t x, uint64_t w, uint64_t absmax, uint64_t residual,
+                                            int64_t rows, int64_t k, int64_t blocksize, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_nf4_linear_residual_bf16")) return 1;
+    if (x == 0 || w == 0 || absmax == 0 || residual == 0) {
+        h->set_error("sm100_nf4_linear_residual_bf16 requires non-null device pointers");
+        return 1;
+    }
+    if (rows < 1 || rows > (1 << 30) || k < 64 || k % 64 != 0 || k > 16384 || blocksize != 64 || (w & 15u) != 0) {
+        h->set_error("sm100_nf4_linear_residual_bf16 requires rows>=1, k%64==0 (<=16384), blocksize=64, aligned weight");
+        return 1;
+    }
+    return finish(h, "nf4_linear_residual_kernel",
+                  kc::nf4_gemv_residual_bf16(P<const void>(x), GemvMat{P<const uint8_t>(w), P<const float>(absmax), static_cast<int>(rows)},
+                                             P<void>(residual), static_cast<int>(k), h->err_word, S(stream)));
+}
+
+int kudacuda_sm100_nf4_dequantize(void* raw, uint64_t w, uint64_t absmax, uint64_t output, int out_dtype, int64_t n,
+                                  int64_t blocksize, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_nf4_dequantize")) return 1;
+    if (w == 0 || absmax == 0 || output == 0) {
+        h->set_error("sm100_nf4_dequantize requires non-null device pointers");
+        return 1;
+    }
+    if (n < 1 || blocksize < 1 || blocksize > (1 << 20) || out_dtype < 0 || out_dtype > 2) {
+        h->set_error("sm100_nf4_dequantize requires n>=1, a positive blocksize and dtype 0..2");
+        return 1;
+    }
+    return finish(h, "nf4_dequant_kernel",
+                  kc::nf4_dequantize(P<const uint8_t>(w), P<const float>(absmax), n, static_cast<int>(blocksize),
+                                     P<void>(output), out_dtype, S(stream)));
+}
+
+int kudacuda_sm100_nf4_quantize(void* raw, uint64_t input, int input_dtype, uint64_t w, uint64_t absmax, int64_t n,
+                                int64_t blocksize, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_nf4_quantize")) return 1;
+    if (input == 0 || w == 0 || absmax == 0) {
+        h->set_error("sm100_nf4_quantize requires non-null device pointers");
+        return 1;
+    }
+    if (n < 1 || blocksize != 64 || input_dtype < 0 || input_dtype > 2) {
+        h->set_error("sm100_nf4_quantize requires n>=1, blocksize=64 and dtype 0..2");
+        return 1;
+    }
+    return finish(h, "nf4_quantize_kernel",
+                  kc::nf4_quantize(P<const void>(input), input_dtype, n, 64, P<uint8_t>(w), P<float>(absmax), S(stream)));
+}
+
+int kudacuda_sm100_rmsnorm_qkv_rope_nf4_bf16(void* raw, uint64_t input, uint64_t norm_weight, uint64_t qw,
+                                             uint64_t qa, uint64_t qb, uint64_t kw, uint64_t ka, uint64_t kb,
+                                             uint64_t vw, uint64_t va, uint64_t vb, uint64_t rope_cos,
+                                             uint64_t rope_sin, uint64_t position_device, uint64_t q_output,
+                                             uint64_t key_cache, uint64_t value_cache, int64_t hidden,
+                                             int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                             int64_t kv_capacity, int64_t max_position, int64_t blocksize,
+                                             float epsilon, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_rmsnorm_qkv_rope_nf4_bf16")) return 1;
+    if (input == 0 || norm_weight == 0 || qw == 0 || qa == 0 || kw == 0 || ka == 0 || vw == 0 || va == 0 ||
+        rope_cos == 0 || rope_sin == 0 || position_device == 0 || q_output == 0 || key_cache == 0 || value_cache == 0) {
+        h->set_error("sm100_rmsnorm_qkv_rope_nf4_bf16 requires non-null device pointers (biases may be null)");
+        return 1;
+    }
+    if (hidden < 64 || hidden % 64 != 0 || hidden > 16384 || q_heads < 1 || kv_heads < 1 || q_heads % kv_heads != 0 ||
+        head_dim < 2 || head_dim % 2 != 0 || head_dim > 256 || kv_capacity < 1 || max_position < 1 ||
+        blocksize != 64 || !(epsilon > 0.0F)) {
+        h->set_error("sm100_rmsnorm_qkv_rope_nf4_bf16 requires hidden%64==0, q_heads%kv_heads==0, even head_dim, "
+                     "positive capacity/max_position/epsilon, blocksize=64");
+        return 1;
+    }
+    kc::QkvRopeArgs a;
+    memset(&a, 0, sizeof(a));
+    a.x = P<const void>(input);
+    a.norm_w = P<const void>(norm_weight);
+    a.eps = epsilon;
+    a.q = GemvMat{P<const uint8_t>(qw), P<const float>(qa), static_cast<int>(q_heads * head_dim)};
+    a.k = GemvMat{P<const uint8_t>(kw), P<const float>(ka), static_cast<int>(kv_heads * head_dim)};
+    a.v = GemvMat{P<const uint8_t>(vw), P<const float>(va), static_cast<int>(kv_heads * head_dim)};
+    a.qb = P<const void>(qb);
+    a.kb = P<const void>(kb);
+    a.vb = P<const void>(vb);
+    a.rope_cos = P<const uint16_t>(rope_cos);
+    a.rope_sin = P<const uint16_t>(rope_sin);
+    a.max_pos = static_cast<int>(max_position);
+    a.pos_dev = P<const int32_t>(position_device);
+    a.q_out = P<void>(q_output);
+    a.key_cache = P<void>(key_cache);
+    a.value_cache = P<void>(value_cache);
+    a.q_heads = static_cast<int>(q_heads);
+    a.kv_heads = static_cast<int>(kv_heads);
+    a.head_dim = static_cast<int>(head_dim);
+    a.kv_cap = static_cast<int>(kv_capacity);
+    a.K = static_cast<int>(hidden);
+    a.err = h->err_word;
+    return finish(h, "nf4_qkv_rope_kernel", kc::nf4_qkv_rope_hf_bf16(a, S(stream)));
+}
+
+int kudacuda_sm100_swiglu_nf4_bf16(void* raw, uint64_t input, uint64_t norm_weight, uint64_t gw, uint64_t ga,
+                                   uint64_t uw, uint64_t ua, uint64_t output, int64_t hidden, int64_t inter,
+                                   int64_t blocksize, float epsilon, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_swiglu_nf4_bf16")) return 1;
+    if (input == 0 || norm_weight == 0 || gw == 0 || ga == 0 || uw == 0 || ua == 0 || output == 0) {
+        h->set_error("sm100_swiglu_nf4_bf16 requires non-null device pointers");
+        return 1;
+    }
+    if (hidden < 64 || hidden % 64 != 0 || hidden > 16384 || inter < 1 || inter > (1 << 26) || blocksize != 64 ||
+        !(epsilon > 0.0F)) {
+        h->set_error("sm100_swiglu_nf4_bf16 requires hidden%64==0 (<=16384), intermediate>=1, blocksize=64, positive epsilon");
+        return 1;
+    }
+    return finish(h, "nf4_swiglu_hf_kernel",
+                  kc::nf4_swiglu_hf_bf16(P<const void>(input), P<const void>(norm_weight), epsilon,
+                                         GemvMat{P<const uint8_t>(gw), P<const float>(ga), static_cast<int>(inter)},
+                                         GemvMat{P<const uint8_t>(uw), P<const float>(ua), static_cast<int>(inter)},
+                                         P<void>(output), static_cast<int>(hidden), h->err_word, S(stream)));
+}
+
+int64_t kudacuda_sm100_gqa_workspace_bytes(int64_t batch_size, int64_t query_heads, int64_t kv_heads,
+                                           int64_t kv_extent, int64_t head_dim) {
+    if (batch_size < 1 || query_heads < 1 || kv_heads < 1 || kv_extent < 1 || head_dim < 1) return -1;
+    int chunk = 0, nsplit = 0;
+    kc::gqa_plan_splits(static_cast<int>(kv_extent), static_cast<int>(batch_size), static_cast<int>(kv_heads), 0,
+                        &chunk, &nsplit);
+    return static_cast<int64_t>(kc::gqa_partials_floats(static_cast<int>(batch_size), static_cast<int>(query_heads),
+                                                        nsplit, static_cast<int>(head_dim)) * sizeof(float));
+}
+
+int kudacuda_sm100_gqa_decode(void* raw, uint64_t query, uint64_t key_cache, uint64_t value_cache, uint64_t output,
+                              uint64_t workspace, int64_t workspace_bytes, uint64_t tickets, uint64_t kv_len_device,
+                              int dtype, int64_t batch_size, int64_t kv_len, int64_t kv_stride, int64_t query_heads,
+                              int64_t kv_heads, int64_t head_dim, float scale, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_gqa_decode")) return 1;
+    if (query == 0 || key_cache == 0 || value_cache == 0 || output == 0 || workspace == 0 || tickets == 0) {
+        h->set_error("sm100_gqa_decode requires non-null device pointers (kv_len_device may be null)");
+        return 1;
+    }
+    const int64_t group = kv_heads > 0 ? query_heads / kv_heads : 0;
+    if (batch_size < 1 || kv_heads < 1 || query_heads % kv_heads != 0 ||
+        !(group == 1 || group == 2 || group == 4 || group == 8) || head_dim != 128 || kv_stride < 1 ||
+        kv_stride > (1 << 20) || (kv_len_device == 0 && (kv_len < 1 || kv_len > kv_stride)) || !(scale > 0.0F) ||
+        (dtype != kc::kF16 && dtype != kc::kBF16)) {
+        h->set_error("sm100_gqa_decode requires head_dim=128, query_heads/kv_heads in {1,2,4,8}, 1<=kv_len<=kv_stride, "
+                     "positive scale, dtype f16 or bf16");
+        return 1;
+    }
+    kc::GqaArgs a;
+    memset(&a, 0, sizeof(a));
+    a.q = P<const void>(query);
+    a.kcache = P<const void>(key_cache);
+    a.vcache = P<const void>(value_cache);
+    a.out = P<void>(output);
+    a.partials = P<float>(workspace);
+    a.counters = P<int>(tickets);
+    a.kv_len_dev = P<const int32_t>(kv_len_device);
+    a.kv_len = static_cast<int>(kv_len_device != 0 ? kv_stride : kv_len);
+    a.stride = static_cast<int>(kv_stride);
+    a.batch = static_cast<int>(batch_size);
+    a.q_heads = static_cast<int>(query_heads);
+    a.kv_heads = static_cast<int>(kv_heads);
+    a.head_dim = 128;
+    a.scale = scale;
+    a.err = h->err_word;
+    const int extent = kv_len_device != 0 ? static_cast<int>(kv_stride) : static_cast<int>(kv_len);
+    kc::gqa_plan_splits(extent, a.batch, a.kv_heads, 0, &a.chunk, &a.nsplit);
+    const size_t need = kc::gqa_partials_floats(a.batch, a.q_heads, a.nsplit, 128) * sizeof(float);
+    if (workspace_bytes < static_cast<int64_t>(need)) {
+        h->set_error("sm100_gqa_decode workspace is smaller than kudacuda_sm100_gqa_workspace_bytes()");
+        return 1;
+    }
+    return finish(h, "gqa_split_kernel", kc::gqa_decode(a, dtype, S(stream)));
+}
+
+int64_t kudacuda_sm100_lm_head_workspace_bytes(void) {
+    return static_cast<int64_t>(kc::lm_head_grid()) * 2 * static_cast<int64_t>(sizeof(float));
+}
+
+int kudacuda_sm100_lm_head_argmax_bf16(void* raw, uint64_t hidden_state, uint64_t final_norm, uint64_t embedding,
+                                       uint64_t logits, uint64_t token_out, uint64_t workspace, int64_t workspace_bytes,
+                                       uint64_t ticket, int64_t vocab, int64_t hidden, float epsilon, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_lm_head_argmax_bf16")) return 1;
+    if (hidden_state == 0 || final_norm == 0 || embedding == 0 || token_out == 0 || workspace == 0 || ticket == 0) {
+        h->set_error("sm100_lm_head_argmax_bf16 requires non-null device pointers (logits may be null)");
+        return 1;
+    }
+    if (vocab < 1 || vocab > (1 << 30) || hidden < 8 || hidden % 8 != 0 || hidden > 8192 || !(epsilon > 0.0F) ||
+        (embedding & 15u) != 0) {
+        h->set_error("sm100_lm_head_argmax_bf16 requires vocab>=1, hidden%8==0 (<=8192), positive epsilon, aligned embedding");
+        return 1;
+    }
+    if (workspace_bytes < kudacuda_sm100_lm_head_workspace_bytes()) {
+        h->set_error("sm100_lm_head_argmax_bf16 workspace is smaller than kudacuda_sm100_lm_head_workspace_bytes()");
+        return 1;
+    }
+    kc::LmHeadArgs a;
+    memset(&a, 0, sizeof(a));
+    a.hidden = P<const void>(hidden_state);
+    a.final_norm = P<const void>(final_norm);
+    a.emb = P<const void>(embedding);
+    a.logits = P<void>(logits);
+    a.token_out = P<int32_t>(token_out);
+    a.partials = P<float>(workspace);
+    a.counter = P<int>(ticket);
+    a.vocab = static_cast<int>(vocab);
+    a.H = static_cast<int>(hidden);
+    a.eps = epsilon;
+    a.err = h->err_word;
+    return finish(h, "lm_head_argmax_kernel", kc::lm_head_argmax_bf16(a, S(stream)));
+}
+
+int kudacuda_sm100_embedding_bf16(void* raw, uint64_t embedding, uint64_t token_device, uint64_t output, int64_t vocab,
+                                  int64_t hidden, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_embedding_bf16")) return 1;
+    if (embedding == 0 || token_device == 0 || output == 0) {
+        h->set_error("sm100_embedding_bf16 requires non-null device pointers");
+        return 1;
+    }
+    if (vocab < 1 || vocab > (1 << 30) || hidden < 1 || hidden > (1 << 20)) {
+        h->set_error("sm100_embedding_bf16 requires positive vocab and hidden");
+        return 1;
+    }
+    return finish(h, "embedding_gather_kernel",
+                  kc::embedding_gather_bf16(P<const void>(embedding), P<const int32_t>(token_device), P<void>(output),
+                                            static_cast<int>(hidden), static_cast<int>(vocab), h->err_word, S(stream)));
+}
+
+int kudacuda_sm100_graph_step_host(void* raw, const void* host_in, uint64_t device_in, int64_t in_bytes,
+                                   void* host_out, uint64_t device_out, int64_t out_bytes, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (h == nullptr) return 1;
+    if (h->graph_exec == nullptr) {
+        h->set_error("kudacuda_sm100_graph_step_host called before graph instantiation");
+        return 1;
+    }
+    if (in_bytes < 0 || out_bytes < 0 || (in_bytes > 0 && (host_in == nullptr || device_in == 0)) ||
+        (out_bytes > 0 && (host_out == nullptr || device_out == 0))) {
+        h->set_error("kudacuda_sm100_graph_step_host requires buffers for positive sizes");
+        return 1;
+    }
+    cudaStream_t s = S(stream);
+    cudaError_t st = cudaSuccess;
+    if (in_bytes > 0) st = cudaMemcpyAsync(P<void>(device_in), host_in, static_cast<size_t>(in_bytes), cudaMemcpyHostToDevice, s);
+    if (st != cudaSuccess) return finish(h, "cudaMemcpyAsync(H2D)", st);
+    st = cudaGraphLaunch(h->graph_exec, s);
+    if (st != cudaSuccess) return finish(h, "cudaGraphLaunch", st);
+    if (out_bytes > 0) st = cudaMemcpyAsync(host_out, P<const void>(device_out), static_cast<size_t>(out_bytes), cudaMemcpyDeviceToHost, s);
+    if (st != cudaSuccess) return finish(h, "cudaMemcpyAsync(D2H)", st);
+    return finish(h, "cudaStreamSynchronize", cudaStreamSynchronize(s));
+}
+
+int kudacuda_sm100_error_word(void* raw, int* out_word, int clear) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_error_word")) return 1;
+    if (out_word == nullptr) {
+        h->set_error("sm100_error_word requires an output pointer");
+        return 1;
+    }
+    cudaError_t st = cudaSetDevice(h->device_id);
+    if (st == cudaSuccess) st = cudaMemcpy(out_word, h->err_word, sizeof(int), cudaMemcpyDeviceToHost);
+    if (st == cudaSuccess && clear) st = cudaMemset(h->err_word, 0, sizeof(int));
+    if (st == cudaSuccess && clear) st = cudaDeviceSynchronize();
+    return finish(h, "sm100_error_word", st);
+}
+
+const char* kudacuda_sm100_target_arch(void) { return "sm_100a"; }
+
+}  // extern "C"
