@@ -223,6 +223,12 @@ KUDACUDA_API int64_t kudacuda_sm100_lm_head_workspace_bytes(void);
 KUDACUDA_API int kudacuda_sm100_embedding_bf16(void* handle, uint64_t embedding, uint64_t token_device,
                                                uint64_t output, int64_t vocab, int64_t hidden, uint64_t stream);
 
+/* Device-resident decode loop: step_state is int32 {token, position, kv_len, -};
+ * sets token = *next_token, position += 1, kv_len = position + 1, and
+ * history[position] = token when history is non-zero (history_len entries). */
+KUDACUDA_API int kudacuda_sm100_decode_advance(void* handle, uint64_t step_state, uint64_t next_token,
+                                               uint64_t history, int64_t history_len, uint64_t stream);
+
 /* One end-to-end step of a captured graph with host buffers: copy in_bytes
  * from host_in to device_in, replay the handle's graph, copy out_bytes from
  * device_out to host_out, and wait for the stream (this call synchronises). */

@@ -81,11 +81,13 @@ __device__ void gqa_combine_group(const GqaArgs& a, int b, int kvh) {
             if (ms == -INFINITY) continue;
             const float w = exp2f(ms - m);
             l += w * __ldcg(p + 1);
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(p + 2) + lane);
-            acc[0] += w * v.x;
-            acc[1] += w * v.y;
-            acc[2] += w * v.z;
-            acc[3] += w * v.w;
+            // partials are 130 floats apart, so acc (offset 2) is only 8-byte aligned
+            const float2 v0 = __ldcg(reinterpret_cast<const float2*>(p + 2) + 2 * lane);
+            const float2 v1 = __ldcg(reinterpret_cast<const float2*>(p + 2) + 2 * lane + 1);
+            acc[0] += w * v0.x;
+            acc[1] += w * v0.y;
+            acc[2] += w * v1.x;
+            acc[3] += w * v1.y;
         }
         const float inv = l > 0.0F ? 1.0F / l : 0.0F;
         const int64_t o = (static_cast<int64_t>(b) * a.q_heads + qh) * kHeadDim + 4 * lane;
@@ -198,7 +200,9 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a)
             dst[0] = ml_s[h][0];
             dst[1] = ml_s[h][1];
         }
-        reinterpret_cast<float4*>(dst + 2)[lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        float2* acc2 = reinterpret_cast<float2*>(dst + 2);  // 8-byte aligned (130-float stride)
+        acc2[2 * lane] = make_float2(acc[0], acc[1]);
+        acc2[2 * lane + 1] = make_float2(acc[2], acc[3]);
     }
 
     if (a.counters == nullptr) return;

@@ -116,6 +116,8 @@ struct LmHeadArgs {
 };
 cudaError_t lm_head_argmax_bf16(const LmHeadArgs& a, cudaStream_t s);
 int lm_head_grid();
+cudaError_t decode_advance(int32_t* state, const int32_t* next_token, int32_t* history, int history_len,
+                           cudaStream_t s);
 cudaError_t embedding_gather_bf16(const void* emb, const int32_t* token_dev, void* out, int H, int vocab,
                                   int* err, cudaStream_t s);
 

@@ -161,6 +161,29 @@ cudaError_t lm_head_argmax_bf16(const LmHeadArgs& a, cudaStream_t s) {
 }
 
 // ---------------------------------------------------------------------------
+// Device-resident decode loop step: state = {token, position, kv_len, -};
+// after the lm_head wrote next_token, feed it back as the next input, move
+// the position on, and append the token to the history.  This replaces the
+// host-side argmax/torch.cat/.item() loop of the reference benchmark
+// (tools/benchmark/benchmark_gemma.py:328-352).
+__global__ void decode_advance_kernel(int32_t* state, const int32_t* next_token, int32_t* history, int history_len) {
+    pdl_launch_dependents();
+    pdl_wait_on_producer();
+    if (threadIdx.x != 0) return;
+    const int32_t tok = *next_token;
+    const int32_t pos = state[1] + 1;
+    state[0] = tok;
+    state[1] = pos;
+    state[2] = pos + 1;
+    if (history != nullptr && pos >= 0 && pos < history_len) history[pos] = tok;
+}
+
+cudaError_t decode_advance(int32_t* state, const int32_t* next_token, int32_t* history, int history_len,
+                           cudaStream_t s) {
+    return launch_pdl(decode_advance_kernel, dim3(1), dim3(32), 0, s, state, next_token, history, history_len);
+}
+
+// ---------------------------------------------------------------------------
 __global__ void embedding_gather_kernel(const uint16_t* emb, const int32_t* token_dev, uint16_t* out, int H,
                                         int vocab, int* err) {
     pdl_launch_dependents();

@@ -41,11 +41,30 @@ cudaError_t run_gemv(Nf4GemvArgs& a, cudaStream_t s) {
     }
     a.ntasks = gemv_tasks(EPI, a);
     if (a.ntasks <= 0) return cudaSuccess;
+    const int dev = current_device_index();
+    // Bulk-copy ring kernel when every row segment and absmax slice is
+    // 16-byte aligned (K % 256 == 0, aligned bases); direct-load kernel else.
+    bool tma_ok = (a.K % 256) == 0;
+    for (int i = 0; i < 3; ++i)
+        if (a.m[i].packed != nullptr && !aligned16(a.m[i].absmax)) tma_ok = false;
+    if (tma_ok) {
+        const size_t smem = kTmaRingBytes + static_cast<size_t>(a.K) * 2;
+        if (smem > 160 * 1024) return cudaErrorInvalidValue;
+        auto kernel = nf4_gemv_tma_kernel<IN, XT, EPI, OT>;
+        static std::atomic<bool> tma_attr[64];
+        if (!tma_attr[dev].load(std::memory_order_acquire)) {
+            const cudaError_t st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+            if (st != cudaSuccess) return st;
+            tma_attr[dev].store(true, std::memory_order_release);
+        }
+        int blocks = (a.ntasks + kTmaWarps - 1) / kTmaWarps;
+        if (blocks > device_sm_count() * 2) blocks = device_sm_count() * 2;
+        return launch_pdl(kernel, dim3(blocks), dim3(kTmaWarps * 32), smem, s, a);
+    }
     const size_t smem = static_cast<size_t>(a.K) * 2;
     auto kernel = nf4_gemv_kernel<IN, XT, EPI, OT>;
     // function attributes are per device: set once on each device used
     static std::atomic<bool> attr_set[64];
-    const int dev = current_device_index();
     if (!attr_set[dev].load(std::memory_order_acquire)) {
         const cudaError_t st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
         if (st != cudaSuccess) return st;

@@ -49,6 +49,7 @@ const TacticEntry kTactics[] = {
     {"qwen2_gqa_decode_sm100_bf16_splitkv_v1", "kudacuda_sm100_gqa_decode", 0, 1},
     {"lm_head_argmax_sm100_bf16_v1", "kudacuda_sm100_lm_head_argmax_bf16", 1, 1},
     {"qwen2_static_decode_graph_sm100_v1", "kudacuda_replay_graph", 1, 1},
+    {"decode_advance_sm100_v1", "kudacuda_sm100_decode_advance", 1, 1},
 };
 
 constexpr int kTacticCount = static_cast<int>(sizeof(kTactics) / sizeof(kTactics[0]));

@@ -766,6 +766,19 @@ int kudacuda_sm100_embedding_bf16(void* raw, uint64_t embedding, uint64_t token_
                                             static_cast<int>(hidden), static_cast<int>(vocab), h->err_word, S(stream)));
 }
 
+int kudacuda_sm100_decode_advance(void* raw, uint64_t step_state, uint64_t next_token, uint64_t history,
+                                  int64_t history_len, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_decode_advance")) return 1;
+    if (step_state == 0 || next_token == 0 || (history != 0 && history_len < 1)) {
+        h->set_error("sm100_decode_advance requires step_state, next_token and a sized history");
+        return 1;
+    }
+    return finish(h, "decode_advance_kernel",
+                  kc::decode_advance(P<int32_t>(step_state), P<const int32_t>(next_token), P<int32_t>(history),
+                                     static_cast<int>(history != 0 ? history_len : 0), S(stream)));
+}
+
 int kudacuda_sm100_graph_step_host(void* raw, const void* host_in, uint64_t device_in, int64_t in_bytes,
                                    void* host_out, uint64_t device_out, int64_t out_bytes, uint64_t stream) {
     Handle* h = as_handle(raw);

@@ -1,0 +1,430 @@
+"""NF4 batch-1 decode engine for Qwen2/Llama-architecture models on sm_100a.
+
+One decode step (one token) is the op sequence below, every op a C-ABI call
+into the sm_100a library:
+
+    embedding[token]                          -> x (bf16 residual stream)
+    per layer:
+      RMSNorm + NF4 q/k/v (+bias) + RoPE + KV append at pos   (1 kernel)
+      split-KV GQA over kv_len = pos + 1, last CTA combines    (1 kernel)
+      NF4 o_proj + residual add                               (1 kernel)
+      RMSNorm + NF4 gate/up + SwiGLU                          (1 kernel)
+      NF4 down_proj + residual add                            (1 kernel)
+    final RMSNorm + tied bf16 lm_head + argmax                (1 kernel)
+    advance: token <- argmax, pos += 1                        (1 kernel)
+
+The whole step is captured once into a CUDA graph through the reference's
+graph ABI (kudacuda_begin_capture / end_capture / replay_graph) and replayed
+per token; every kernel is launched with programmatic dependent launch so its
+weight streaming starts while the previous kernel finishes.  All buffers are
+allocated before capture and never move, so the graph key (pointer identity,
+python/kudacuda_graph_plan.py:14-28 of the reference) stays valid.
+
+The per-token state lives on the device as int32 {token, position, kv_len}.
+The host either leaves the loop on the device (replay N times, read the token
+history once) or drives it step by step through
+kudacuda_sm100_graph_step_host (host token in, host token out), which is the
+reference benchmark's per-token loop (tools/benchmark/benchmark_gemma.py:328-352).
+
+Tensor parallelism (Megatron-style: column-parallel q/k/v/gate/up, row-parallel
+o/down, sum-allreduce of the partial residual update) is provided by
+kudacuda_b200.tensor_parallel on top of the same plan.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field, replace
+from typing import Any, Optional
+
+from .kudacuda_sidecar import KudaCudaBridge, NativeCudaError
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    name: str
+    hidden: int
+    layers: int
+    q_heads: int
+    kv_heads: int
+    head_dim: int
+    intermediate: int
+    vocab: int
+    rope_theta: float
+    eps: float
+    qkv_bias: bool
+    tie_embeddings: bool
+
+    @property
+    def q_out(self) -> int:
+        return self.q_heads * self.head_dim
+
+    @property
+    def kv_out(self) -> int:
+        return self.kv_heads * self.head_dim
+
+    def nf4_layer_params(self) -> int:
+        h, i = self.hidden, self.intermediate
+        return h * self.q_out + 2 * h * self.kv_out + self.q_out * h + 2 * h * i + i * h
+
+    def weight_bytes_per_token(self) -> dict[str, int]:
+        """Algorithmic bytes read per decode token (weights; KV separate)."""
+
+        p = self.nf4_layer_params() * self.layers
+        nf4 = p // 2 + p // 16  # packed nibbles + fp32 absmax per 64
+        lm = self.vocab * self.hidden * 2 if self.tie_embeddings else (self.vocab * self.hidden * 9) // 16
+        norms = self.layers * 2 * self.hidden * 2 + self.hidden * 2
+        bias = self.layers * (self.q_out + 2 * self.kv_out) * 2 if self.qkv_bias else 0
+        return {"nf4_absmax": nf4, "lm_head": lm, "norms_bias": norms + bias}
+
+    def kv_bytes_per_token(self, kv_len: int) -> int:
+        # K and V rows of every layer up to kv_len, plus the appended row
+        return self.layers * 2 * self.kv_heads * self.head_dim * 2 * (kv_len + 1)
+
+
+QWEN25_3B = DecoderConfig("qwen2.5-3b", 2048, 36, 16, 2, 128, 11008, 151936, 1.0e6, 1.0e-6, True, True)
+LLAMA3_8B = DecoderConfig("llama-3-8b", 4096, 32, 32, 8, 128, 14336, 128256, 5.0e5, 1.0e-5, False, False)
+
+
+def tiny_config(layers: int = 2, vocab: int = 4096) -> DecoderConfig:
+    """Config-1/2 layer shapes with few layers and a small vocabulary (tests)."""
+
+    return replace(QWEN25_3B, name=f"qwen2.5-3b-{layers}l", layers=layers, vocab=vocab)
+
+
+@dataclass
+class NF4Linear:
+    packed: Any  # uint8 [rows * k / 2, 1] (bitsandbytes Params4bit storage)
+    absmax: Any  # float32 [rows * k / 64]
+    rows: int
+    k: int
+
+    def as_tuple(self, bias: Any = None) -> tuple:
+        return (self.packed, self.absmax, bias)
+
+
+@dataclass
+class LayerWeights:
+    in_norm: Any
+    post_norm: Any
+    q: NF4Linear
+    k: NF4Linear
+    v: NF4Linear
+    o: NF4Linear
+    gate: NF4Linear
+    up: NF4Linear
+    down: NF4Linear
+    q_bias: Any = None
+    k_bias: Any = None
+    v_bias: Any = None
+
+
+@dataclass
+class ModelWeights:
+    config: DecoderConfig
+    layers: list[LayerWeights]
+    embedding: Any  # bf16 [vocab, hidden]
+    final_norm: Any  # bf16 [hidden]
+    lm_head: Optional[NF4Linear] = None  # untied NF4 lm_head (Llama)
+
+
+def _randn_bf16(torch: Any, shape: tuple, std: float, gen: Any, device: Any, mean: float = 0.0) -> Any:
+    t = torch.randn(shape, generator=gen, device=device, dtype=torch.float32)
+    return (t * std + mean).to(torch.bfloat16)
+
+
+def quantize_nf4(bridge: KudaCudaBridge, torch: Any, w_bf16: Any, stream_ptr: int) -> NF4Linear:
+    rows, k = int(w_bf16.shape[0]), int(w_bf16.shape[1])
+    n = rows * k
+    packed = torch.empty((n // 2, 1), dtype=torch.uint8, device=w_bf16.device)
+    absmax = torch.empty((n // 64,), dtype=torch.float32, device=w_bf16.device)
+    bridge.dispatch_nf4_quantize(w_bf16.contiguous(), packed, absmax, stream_ptr=stream_ptr)
+    return NF4Linear(packed, absmax, rows, k)
+
+
+def random_weights(bridge: KudaCudaBridge, config: DecoderConfig, *, seed: int = 20260824, device: Any = "cuda:0",
+                   torch_module: Any = None, shard: tuple[int, int] = (0, 1)) -> ModelWeights:
+    """Synthetic weights of the BASELINE distribution: linears N(0, 0.02) in
+    bf16, NF4-quantised (blocksize 64) on the device by the library's own
+    quantiser; norms 1 + N(0, 0.02); q/k/v biases N(0, 0.02); embedding
+    N(0, 0.02).  ``shard=(rank, world)`` keeps only this rank's tensor-parallel
+    slices (column-parallel q/k/v/gate/up, row-parallel o/down), generated
+    from the full matrices so every world size sees the same model."""
+
+    if torch_module is None:
+        import torch as torch_module
+    torch = torch_module
+    rank, world = shard
+    gen = torch.Generator(device=device)
+    gen.manual_seed(int(seed))
+    stream_ptr = int(torch.cuda.current_stream(device).cuda_stream)
+    c = config
+    qh, kvh = c.q_heads // world, c.kv_heads // world
+    i_loc = c.intermediate // world
+
+    def cols(w: Any, start: int, count: int) -> Any:  # row-parallel: slice K
+        return w[:, start:start + count].contiguous()
+
+    def rows(w: Any, start: int, count: int) -> Any:  # column-parallel: slice N
+        return w[start:start + count].contiguous()
+
+    layers = []
+    for _ in range(c.layers):
+        in_norm = _randn_bf16(torch, (c.hidden,), 0.02, gen, device, 1.0)
+        post_norm = _randn_bf16(torch, (c.hidden,), 0.02, gen, device, 1.0)
+        wq = _randn_bf16(torch, (c.q_out, c.hidden), 0.02, gen, device)
+        wk = _randn_bf16(torch, (c.kv_out, c.hidden), 0.02, gen, device)
+        wv = _randn_bf16(torch, (c.kv_out, c.hidden), 0.02, gen, device)
+        wo = _randn_bf16(torch, (c.hidden, c.q_out), 0.02, gen, device)
+        wg = _randn_bf16(torch, (c.intermediate, c.hidden), 0.02, gen, device)
+        wu = _randn_bf16(torch, (c.intermediate, c.hidden), 0.02, gen, device)
+        wd = _randn_bf16(torch, (c.hidden, c.intermediate), 0.02, gen, device)
+        biases = [None, None, None]
+        if c.qkv_bias:
+            biases = [_randn_bf16(torch, (n,), 0.02, gen, device) for n in (c.q_out, c.kv_out, c.kv_out)]
+        d = c.head_dim
+        q_sl, kv_sl, i_sl = (rank * qh * d, qh * d), (rank * kvh * d, kvh * d), (rank * i_loc, i_loc)
+        layers.append(
+            LayerWeights(
+                in_norm=in_norm,
+                post_norm=post_norm,
+                q=quantize_nf4(bridge, torch, rows(wq, *q_sl), stream_ptr),
+                k=quantize_nf4(bridge, torch, rows(wk, *kv_sl), stream_ptr),
+                v=quantize_nf4(bridge, torch, rows(wv, *kv_sl), stream_ptr),
+                o=quantize_nf4(bridge, torch, cols(wo, *q_sl), stream_ptr),
+                gate=quantize_nf4(bridge, torch, rows(wg, *i_sl), stream_ptr),
+                up=quantize_nf4(bridge, torch, rows(wu, *i_sl), stream_ptr),
+                down=quantize_nf4(bridge, torch, cols(wd, *i_sl), stream_ptr),
+                q_bias=None if biases[0] is None else rows(biases[0], *q_sl),
+                k_bias=None if biases[1] is None else rows(biases[1], *kv_sl),
+                v_bias=None if biases[2] is None else rows(biases[2], *kv_sl),
+            )
+        )
+        del wq, wk, wv, wo, wg, wu, wd
+    embedding = _randn_bf16(torch, (c.vocab, c.hidden), 0.02, gen, device)
+    final_norm = _randn_bf16(torch, (c.hidden,), 0.02, gen, device, 1.0)
+    lm_head = None
+    if not c.tie_embeddings:
+        w_lm = _randn_bf16(torch, (c.vocab, c.hidden), 0.02, gen, device)
+        lm_head = quantize_nf4(bridge, torch, w_lm, stream_ptr)
+        del w_lm
+    torch.cuda.synchronize(device)
+    return ModelWeights(c, layers, embedding, final_norm, lm_head)
+
+
+def rope_tables(torch: Any, max_pos: int, head_dim: int, theta: float, device: Any) -> tuple[Any, Any]:
+    """Transformers' default RoPE tables (Qwen2RotaryEmbedding / LlamaRotaryEmbedding):
+    inv_freq = 1 / theta^(2i/d) in fp32, freqs = pos * inv_freq, cos/sin rounded to
+    bf16; the first d/2 columns (emb = cat(freqs, freqs))."""
+
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
+    freqs = torch.outer(torch.arange(max_pos, dtype=torch.float32), inv_freq.float())
+    return (freqs.cos().to(torch.bfloat16).contiguous().to(device), freqs.sin().to(torch.bfloat16).contiguous().to(device))
+
+
+@dataclass
+class DecodeBuffers:
+    state: Any  # int32 [4]: token, position, kv_len, (pad)
+    x: Any  # bf16 [hidden]
+    q: Any  # bf16 [q_heads * d]
+    attn: Any  # bf16 [q_heads * d]
+    h: Any  # bf16 [intermediate]
+    kcache: Any  # bf16 [layers, kv_heads, cap, d]
+    vcache: Any
+    gqa_ws: Any
+    gqa_tickets: Any
+    gqa_ws_bytes: int
+    lm_ws: Any
+    lm_ticket: Any
+    logits: Any  # bf16 [vocab]
+    next_token: Any  # int32 [1]
+    history: Any  # int32 [max_tokens]
+    rope_cos: Any
+    rope_sin: Any
+    lm_scratch: Any = None  # f32 logits for an NF4 lm_head
+
+
+class StaticDecodePlan:
+    """Fixed-shape decode step for one model on one device: buffers, the op
+    sequence, and its CUDA graph.  ``kv_bucket`` is the cache capacity (the
+    reference's graph KV bucket, python/kudacuda_static_decode.py:100-145)."""
+
+    def __init__(self, bridge: KudaCudaBridge, weights: ModelWeights, *, kv_bucket: int = 512,
+                 max_tokens: Optional[int] = None, device: Any = "cuda:0", torch_module: Any = None,
+                 allreduce: Any = None, keep_logits: bool = True) -> None:
+        if torch_module is None:
+            import torch as torch_module
+        self.torch = torch_module
+        self.bridge = bridge
+        self.weights = weights
+        self.config = weights.config
+        self.device = device
+        self.kv_bucket = int(kv_bucket)
+        self.allreduce = allreduce  # callable(tensor, stream) for tensor-parallel partial sums
+        self.keep_logits = keep_logits
+        torch = self.torch
+        c = self.config
+        L0 = weights.layers[0]
+        self.q_heads = L0.q.rows // c.head_dim
+        self.kv_heads = L0.k.rows // c.head_dim
+        self.inter = L0.gate.rows
+        max_tokens = int(max_tokens or self.kv_bucket)
+        bf16 = torch.bfloat16
+        cap = self.kv_bucket
+        ws, tickets, nbytes = bridge.gqa_workspace(batch=1, query_heads=self.q_heads, kv_heads=self.kv_heads,
+                                                   kv_extent=cap, device=device, torch_module=torch)
+        lm_bytes = bridge.lm_head_workspace_bytes()
+        cos, sin = rope_tables(torch, max(cap, max_tokens) + 1, c.head_dim, c.rope_theta, device)
+        self.buffers = DecodeBuffers(
+            state=torch.zeros(4, dtype=torch.int32, device=device),
+            x=torch.zeros(c.hidden, dtype=bf16, device=device),
+            q=torch.zeros(self.q_heads * c.head_dim, dtype=bf16, device=device),
+            attn=torch.zeros(self.q_heads * c.head_dim, dtype=bf16, device=device),
+            h=torch.zeros(self.inter, dtype=bf16, device=device),
+            kcache=torch.zeros((c.layers, self.kv_heads, cap, c.head_dim), dtype=bf16, device=device),
+            vcache=torch.zeros((c.layers, self.kv_heads, cap, c.head_dim), dtype=bf16, device=device),
+            gqa_ws=ws,
+            gqa_tickets=tickets,
+            gqa_ws_bytes=nbytes,
+            lm_ws=torch.zeros(lm_bytes // 4, dtype=torch.float32, device=device),
+            lm_ticket=torch.zeros(1, dtype=torch.int32, device=device),
+            logits=torch.zeros(c.vocab, dtype=bf16, device=device),
+            next_token=torch.zeros(1, dtype=torch.int32, device=device),
+            history=torch.zeros(max_tokens, dtype=torch.int32, device=device),
+            rope_cos=cos,
+            rope_sin=sin,
+        )
+        self.captured = False
+        self.launches_per_step = 0
+
+    # ------------------------------------------------------------------ one step
+    def record(self, stream_ptr: int) -> int:
+        """Enqueue one decode step on the stream; returns the number of kernels."""
+
+        b, c, w, br = self.buffers, self.config, self.weights, self.bridge
+        pos_dev = b.state[1:2]
+        kvlen_dev = b.state[2:3]
+        n = 0
+        br.dispatch_embedding(w.embedding, b.state[0:1], b.x, stream_ptr=stream_ptr)
+        n += 1
+        scale = 1.0 / math.sqrt(c.head_dim)
+        for li, L in enumerate(w.layers):
+            kc, vc = b.kcache[li], b.vcache[li]
+            br.dispatch_attention_input(b.x, L.in_norm, L.q.as_tuple(L.q_bias), L.k.as_tuple(L.k_bias),
+                                        L.v.as_tuple(L.v_bias), b.rope_cos, b.rope_sin, pos_dev, b.q, kc, vc,
+                                        q_heads=self.q_heads, kv_heads=self.kv_heads, head_dim=c.head_dim,
+                                        kv_capacity=self.kv_bucket, epsilon=c.eps, stream_ptr=stream_ptr)
+            br.dispatch_gqa_decode_splitkv(b.q, kc, vc, b.attn, b.gqa_ws, b.gqa_tickets, kv_len_device=kvlen_dev,
+                                           batch=1, kv_len=self.kv_bucket, kv_stride=self.kv_bucket,
+                                           query_heads=self.q_heads, kv_heads=self.kv_heads, scale=scale,
+                                           stream_ptr=stream_ptr, workspace_bytes=b.gqa_ws_bytes)
+            n += 2
+            n += self._residual_linear(b.attn, L.o, stream_ptr)
+            br.dispatch_swiglu_bf16(b.x, L.post_norm, (L.gate.packed, L.gate.absmax), (L.up.packed, L.up.absmax), b.h,
+                                    epsilon=c.eps, stream_ptr=stream_ptr)
+            n += 1
+            n += self._residual_linear(b.h, L.down, stream_ptr)
+        n += self._lm_head(stream_ptr)
+        br.dispatch_decode_advance(b.state, b.next_token, history=b.history, stream_ptr=stream_ptr)
+        n += 1
+        self.launches_per_step = n
+        return n
+
+    def _residual_linear(self, x: Any, lin: NF4Linear, stream_ptr: int) -> int:
+        if self.allreduce is None:
+            self.bridge.dispatch_nf4_linear_residual(x, lin.packed, lin.absmax, self.buffers.x, rows=lin.rows, k=lin.k,
+                                                     stream_ptr=stream_ptr)
+            return 1
+        return self.allreduce.residual_linear(self, x, lin, stream_ptr)
+
+    def _lm_head(self, stream_ptr: int) -> int:
+        b, w, c = self.buffers, self.weights, self.config
+        if w.lm_head is None:
+            self.bridge.dispatch_lm_head_argmax(b.x, w.final_norm, w.embedding, b.next_token, b.lm_ws, b.lm_ticket,
+                                                logits=b.logits if self.keep_logits else None, epsilon=c.eps,
+                                                stream_ptr=stream_ptr)
+            return 1
+        raise NativeCudaError("untied NF4 lm_head is served by the tensor-parallel plan")
+
+    # ------------------------------------------------------------------ state
+    def set_state(self, token: int, position: int) -> None:
+        torch = self.torch
+        self.buffers.state.copy_(torch.tensor([token, position, position + 1, 0], dtype=torch.int32),
+                                 non_blocking=False)
+
+    def reset_cache(self) -> None:
+        self.buffers.kcache.zero_()
+        self.buffers.vcache.zero_()
+
+    # ------------------------------------------------------------------ graph
+    def capture(self, stream: Any) -> None:
+        """Warm every kernel once eagerly (lazy attribute set-up), restore the
+        state, then capture one step into the handle's graph."""
+
+        torch = self.torch
+        sp = int(stream.cuda_stream)
+        saved_state = self.buffers.state.clone()
+        saved_hist = self.buffers.history.clone()
+        with torch.cuda.stream(stream):
+            self.record(sp)
+        stream.synchronize()
+        word = self.bridge.error_word(clear=True)
+        if word:
+            raise NativeCudaError(f"decode step raised device error word {word:#x}")
+        self.buffers.state.copy_(saved_state)
+        self.buffers.history.copy_(saved_hist)
+        torch.cuda.synchronize(self.device)
+        self.bridge.reset_graph()
+        self.bridge.begin_capture(stream_ptr=sp)
+        try:
+            self.record(sp)
+        except Exception:
+            try:
+                self.bridge.end_capture(stream_ptr=sp)
+            finally:
+                self.bridge.reset_graph()
+            raise
+        self.bridge.end_capture(stream_ptr=sp)
+        self.captured = True
+
+    def replay(self, stream: Any) -> None:
+        self.bridge.replay_graph(stream_ptr=int(stream.cuda_stream))
+
+    # ------------------------------------------------------------------ generation
+    def prefill(self, prompt: list[int], stream: Any) -> int:
+        """Feed the prompt through decode steps (positions 0..n-1); returns the
+        first generated token.  Requires a captured graph."""
+
+        if not self.captured:
+            raise NativeCudaError("capture the decode graph before prefill")
+        if len(prompt) + 1 > self.kv_bucket:
+            raise ValueError("prompt does not fit the KV bucket")
+        torch = self.torch
+        for i, tok in enumerate(prompt):
+            self.buffers.state.copy_(torch.tensor([tok, i, i + 1, 0], dtype=torch.int32), non_blocking=False)
+            self.replay(stream)
+        stream.synchronize()
+        return int(self.buffers.next_token.item())
+
+    def generate_device(self, steps: int, stream: Any) -> None:
+        """Replay the graph ``steps`` times with no host interaction; the
+        generated tokens accumulate in buffers.history."""
+
+        for _ in range(int(steps)):
+            self.replay(stream)
+
+
+def greedy_generate(plan: StaticDecodePlan, prompt: list[int], new_tokens: int, stream: Any) -> list[int]:
+    """Prompt via decode steps, then ``new_tokens`` greedy tokens on the device."""
+
+    plan.reset_cache()
+    plan.buffers.history.zero_()
+    first = plan.prefill(prompt, stream)
+    n = len(prompt)
+    if n + new_tokens > plan.buffers.history.numel() or n + new_tokens > plan.kv_bucket:
+        raise ValueError("generation exceeds the KV bucket / history")
+    plan.buffers.history[n] = first
+    # state after prefill: token = first, position = n
+    plan.generate_device(new_tokens - 1, stream)
+    stream.synchronize()
+    return [int(t) for t in plan.buffers.history[n:n + new_tokens].cpu().tolist()]

@@ -51,7 +51,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "kudacuda_sm100_nf4_linear_residual_bf16": (_i32, [_p, _u64, _u64, _u64, _u64, _i64, _i64, _i64, _u64]),
     "kudacuda_sm100_nf4_dequantize": (_i32, [_p, _u64, _u64, _u64, _i32, _i64, _i64, _u64]),
     "kudacuda_sm100_nf4_quantize": (_i32, [_p, _u64, _i32, _u64, _u64, _i64, _i64, _u64]),
-    "kudacuda_sm100_rmsnorm_qkv_rope_nf4_bf16": (_i32, [_p] + [_u64] * 17 + [_i64] * 8 + [_f32, _u64]),
+    "kudacuda_sm100_rmsnorm_qkv_rope_nf4_bf16": (_i32, [_p] + [_u64] * 17 + [_i64] * 7 + [_f32, _u64]),
     "kudacuda_sm100_swiglu_nf4_bf16": (_i32, [_p] + [_u64] * 7 + [_i64] * 3 + [_f32, _u64]),
     "kudacuda_sm100_gqa_decode": (
         _i32,
@@ -64,6 +64,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     ),
     "kudacuda_sm100_lm_head_workspace_bytes": (_i64, []),
     "kudacuda_sm100_embedding_bf16": (_i32, [_p, _u64, _u64, _u64, _i64, _i64, _u64]),
+    "kudacuda_sm100_decode_advance": (_i32, [_p, _u64, _u64, _u64, _i64, _u64]),
     "kudacuda_sm100_graph_step_host": (_i32, [_p, _p, _u64, _i64, _p, _u64, _i64, _u64]),
     "kudacuda_sm100_error_word": (_i32, [_p, ctypes.POINTER(ctypes.c_int), _i32]),
     "kudacuda_sm100_target_arch": (ctypes.c_char_p, []),
