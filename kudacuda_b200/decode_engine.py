@@ -365,6 +365,9 @@ class StaticDecodePlan:
         sp = int(stream.cuda_stream)
         saved_state = self.buffers.state.clone()
         saved_hist = self.buffers.history.clone()
+        # the warm-up step runs on a valid state (token 0 at position 0)
+        self.buffers.state.copy_(torch.tensor([0, 0, 1, 0], dtype=torch.int32))
+        torch.cuda.synchronize(self.device)
         with torch.cuda.stream(stream):
             self.record(sp)
         stream.synchronize()
