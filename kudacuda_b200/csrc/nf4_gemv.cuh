@@ -316,130 +316,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) nf4_gemv_kernel(const Nf4Gemv
     }
 }
 
-// ---------------------------------------------------------------------------
-// Bulk-copy (TMA) variant: the production path whenever K % 256 == 0 and the
-// packed/absmax bases are 16-byte aligned.
-//
-// Every warp owns a private 6-stage ring in shared memory.  Lane 0 streams the
-// warp's row pairs through it with cp.async.bulk, one 1024-element segment
-// (2 x 512 B of packed nibbles + 2 x 64 B of absmax) per stage, completing on
-// a per-stage mbarrier; all 32 lanes consume the stage (lane l owns 16-byte
-// chunk l of each row) and lane 0 refills the slot with the segment six steps
-// ahead.  Because the weights are static, the first six segments are
-// requested before griddepcontrol.wait, i.e. while the previous kernel in
-// the stream is still running.  Each warp keeps ~7 KB in flight, ~110 KB per
-// SM at two CTAs per SM, which covers HBM latency at full bandwidth.
-constexpr int kSegElems = 1024;
-constexpr int kSegBytes = kSegElems / 2;
-constexpr int kSegAbsBytes = kSegElems / kBlocksize * 4;
-constexpr int kStageBytes = 2 * kSegBytes + 2 * kSegAbsBytes;  // 1152
-constexpr int kRingStages = 6;
-constexpr int kTmaWarps = 8;
-constexpr size_t kTmaRingBytes = static_cast<size_t>(kTmaWarps) * kRingStages * kStageBytes;
-
-template <int EPI>
-__device__ __forceinline__ void tma_issue_step(const Nf4GemvArgs& a, uint8_t* ring, uint64_t* bars, int gw,
-                                               int nwarps_total, int nseg, int step) {
-    const int tloc = step / nseg;
-    const int seg = step - tloc * nseg;
-    const RowPair p = decode_task<EPI>(a, gw + tloc * nwarps_total);
-    const int e0 = seg * kSegElems;
-    const int ne = min(kSegElems, a.K - e0);
-    const uint32_t pb = static_cast<uint32_t>(ne / 2);
-    const uint32_t ab = static_cast<uint32_t>(ne / kBlocksize * 4);
-    uint8_t* st = ring + (step % kRingStages) * kStageBytes;
-    uint64_t* bar = &bars[step % kRingStages];
-    mbar_arrive_expect_tx(bar, 2 * (pb + ab));
-    bulk_g2s(st, p.w0 + e0 / 2, pb, bar);
-    bulk_g2s(st + kSegBytes, p.w1 + e0 / 2, pb, bar);
-    bulk_g2s(st + 2 * kSegBytes, p.a0 + e0 / kBlocksize, ab, bar);
-    bulk_g2s(st + 2 * kSegBytes + kSegAbsBytes, p.a1 + e0 / kBlocksize, ab, bar);
-}
-
-template <int IN, int XT, int EPI, int OT>
-__global__ void __launch_bounds__(kTmaWarps * 32, 2) nf4_gemv_tma_kernel(const Nf4GemvArgs a) {
-    __shared__ __align__(16) uint32_t lut[kLutWords];
-    __shared__ float red[32];
-    __shared__ __align__(8) uint64_t bars[kTmaWarps][kRingStages];
-    extern __shared__ __align__(128) uint8_t dyn[];
-
-    const int tid = threadIdx.x;
-    const int lane = tid & 31;
-    const int warp = tid >> 5;
-    uint8_t* ring = dyn + static_cast<size_t>(warp) * kRingStages * kStageBytes;
-    uint4* xs = reinterpret_cast<uint4*>(dyn + kTmaRingBytes);
-    uint64_t* wbar = bars[warp];
-
-    const int nseg = (a.K + kSegElems - 1) / kSegElems;
-    const int nwarps_total = gridDim.x * kTmaWarps;
-    const int gw = blockIdx.x + gridDim.x * warp;
-    const int ntask_w = gw < a.ntasks ? (a.ntasks - gw + nwarps_total - 1) / nwarps_total : 0;
-    const int nsteps = ntask_w * nseg;
-
-    if (lane == 0) {
-        for (int s = 0; s < kRingStages; ++s) mbar_init(&wbar[s], 1);
-        fence_mbar_init();
-        // weights are static: start streaming before waiting on the producer
-        for (int s = 0; s < kRingStages && s < nsteps; ++s) tma_issue_step<EPI>(a, ring, wbar, gw, nwarps_total, nseg, s);
-    }
-    build_pair_lut(lut, tid, blockDim.x);
-    pdl_launch_dependents();
-    pdl_wait_on_producer();
-    stage_x<IN, XT>(a, xs, red);  // ends with __syncthreads (covers table and barrier init)
-
-    const uint32_t lane_off = static_cast<uint32_t>(lane) << 2;
-    float acc0 = 0.0F, acc1 = 0.0F;
-    int step = 0;
-    for (; step < nsteps; ++step) {
-        const int slot = step % kRingStages;
-        if (!mbar_wait_bounded(&wbar[slot], static_cast<uint32_t>(step / kRingStages) & 1u)) break;
-        const int tloc = step / nseg;
-        const int seg = step - tloc * nseg;
-        const int e0 = seg * kSegElems;
-        const int ne = min(kSegElems, a.K - e0);
-        const uint8_t* st = ring + slot * kStageBytes;
-        if (16 * lane < ne / 2) {
-            uint32_t xr[16];
-            load_x32(xs, (e0 >> 5) + lane, xr);
-            const uint4 wa = *reinterpret_cast<const uint4*>(st + 16 * lane);
-            const uint4 wb = *reinterpret_cast<const uint4*>(st + kSegBytes + 16 * lane);
-            const float sa = reinterpret_cast<const float*>(st + 2 * kSegBytes)[lane >> 1];
-            const float sb = reinterpret_cast<const float*>(st + 2 * kSegBytes + kSegAbsBytes)[lane >> 1];
-            float e0a = 0.0F, o0a = 0.0F, e1a = 0.0F, o1a = 0.0F;
-            nf4_word_dot(lut, lane_off, wa.x, xr + 0, e0a, o0a);
-            nf4_word_dot(lut, lane_off, wb.x, xr + 0, e1a, o1a);
-            nf4_word_dot(lut, lane_off, wa.y, xr + 4, e0a, o0a);
-            nf4_word_dot(lut, lane_off, wb.y, xr + 4, e1a, o1a);
-            nf4_word_dot(lut, lane_off, wa.z, xr + 8, e0a, o0a);
-            nf4_word_dot(lut, lane_off, wb.z, xr + 8, e1a, o1a);
-            nf4_word_dot(lut, lane_off, wa.w, xr + 12, e0a, o0a);
-            nf4_word_dot(lut, lane_off, wb.w, xr + 12, e1a, o1a);
-            acc0 = fmaf(e0a + o0a, sa, acc0);
-            acc1 = fmaf(e1a + o1a, sb, acc1);
-        }
-        __syncwarp();
-        if (lane == 0 && step + kRingStages < nsteps) {
-            fence_proxy_async_smem();  // order this warp's reads of the slot before the refill
-            tma_issue_step<EPI>(a, ring, wbar, gw, nwarps_total, nseg, step + kRingStages);
-        }
-        if (seg == nseg - 1) {
-            const float s0 = warp_sum(acc0);
-            const float s1 = warp_sum(acc1);
-            if (lane == 0) epilogue<EPI, OT>(a, decode_task<EPI>(a, gw + tloc * nwarps_total), s0, s1);
-            acc0 = 0.0F;
-            acc1 = 0.0F;
-        }
-    }
-    if (step < nsteps) {
-        // a stage never completed: record it, then wait (bounded) for the
-        // copies this warp still has in flight before leaving
-        if (lane == 0 && a.err != nullptr) atomicOr(a.err, 16);
-        const int last = min(nsteps, step + kRingStages);
-        for (int s = step; s < last; ++s)
-            mbar_wait_bounded(&wbar[s % kRingStages], static_cast<uint32_t>(s / kRingStages) & 1u);
-    }
-}
-
 // Number of two-row tasks for each epilogue.
 inline int gemv_tasks(int epi, const Nf4GemvArgs& a) {
     switch (epi) {

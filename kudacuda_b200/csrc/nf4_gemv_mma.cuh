@@ -1,0 +1,382 @@
+// nf4_gemv_mma.cuh -- the production NF4 GEMV for sm_100a: codebook-pair
+// table lookups feed f16 tensor-core fragments (mma.m16n8k16, f32 accumulate).
+//
+// Why the tensor core for a batch-1 GEMV: the op is HBM-bound (0.5625 B per
+// weight) only if dequantisation costs under ~2.5 instructions per weight at
+// 148 SMs x 1.9 GHz.  One shared-memory lookup of a packed byte returns
+// half2(level[hi], level[lo]) -- exactly one A-fragment register of an
+// m16n8k16 f16 mma -- so a byte costs two integer ops (table offset) and one
+// LDS, and the tensor core does the multiply-accumulate in fp32 with no
+// f16->f32 conversions.  The B operand is the activation vector (column 0;
+// columns 1..7 carry copies and are ignored at batch 1).
+//
+// Tiling.  A tile is 16 weight rows: rows 0-7 ("A" group) and 8-15 ("B"
+// group) are chosen per epilogue so that lane (g, 0) ends with the pair the
+// epilogue needs -- RoPE partners (i, i+64), SwiGLU partners (gate j, up j),
+// K/V partners (k j, v j), or plain consecutive rows.  The CTA's 8 warps
+// split K (64-element absmax blocks) and reduce their fragments through
+// shared memory; CTAs loop over tiles so the 32 KB table is built once.
+//
+// K permutation inside a 64-element block (all rows of a tile agree, so the
+// dot product is unchanged): thread (g, t) of the warp owns bytes
+// [8t, 8t+8) of each of its two rows' 32-byte block; k-step s uses byte 2s
+// for k-slots (2t, 2t+1) and byte 2s+1 for k-slots (2t+8, 2t+9), i.e.
+// block elements 16t+4s+{0,1} and 16t+4s+{2,3}; the B fragment for the same
+// slots is activation pair 8t+2s and 8t+2s+1 of the block.  The block's
+// fp32 partial is scaled by the row's absmax and added to fp32 totals.
+#pragma once
+
+#include "nf4_gemv.cuh"
+
+namespace kc {
+
+constexpr int kMmaWarps = 8;
+constexpr int kMmaThreads = kMmaWarps * 32;
+constexpr int kMmaGroup = 2;  // 64-element blocks per prefetch step
+
+__device__ __forceinline__ void mma_f16_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Table offsets of byte j of a packed word (128-byte entry stride, lane slot).
+__device__ __forceinline__ uint32_t lut_off_b0(uint32_t w, uint32_t lane_off) { return ((w << 7) & 0x7f80u) | lane_off; }
+__device__ __forceinline__ uint32_t lut_off_b1(uint32_t w, uint32_t lane_off) { return ((w >> 1) & 0x7f80u) | lane_off; }
+__device__ __forceinline__ uint32_t lut_off_b2(uint32_t w, uint32_t lane_off) { return ((w >> 9) & 0x7f80u) | lane_off; }
+__device__ __forceinline__ uint32_t lut_off_b3(uint32_t w, uint32_t lane_off) { return ((w >> 17) & 0x7f80u) | lane_off; }
+
+struct TileRows {
+    const uint8_t* wA;  // packed base of row group A (8 rows, stride K/2)
+    const uint8_t* wB;
+    const float* sA;    // absmax base of row group A (stride K/64)
+    const float* sB;
+    int rA, rB;         // first row index of each group (epilogue bookkeeping)
+    int nA, nB;         // valid rows in each group (tails)
+    int kind;
+};
+
+template <int EPI>
+__device__ __forceinline__ TileRows decode_tile(const Nf4GemvArgs& a, int t) {
+    TileRows r;
+    const int64_t rb = a.K / 2, ab = a.K / kBlocksize;
+    auto set = [&](int mA, int rowA, int nA, int mB, int rowB, int nB) {
+        r.wA = a.m[mA].packed + rb * rowA;
+        r.sA = a.m[mA].absmax + ab * rowA;
+        r.wB = a.m[mB].packed + rb * rowB;
+        r.sB = a.m[mB].absmax + ab * rowB;
+        r.rA = rowA;
+        r.rB = rowB;
+        r.nA = nA;
+        r.nB = nB;
+    };
+    auto clamp8 = [](int rows, int start) { return max(0, min(8, rows - start)); };
+    if constexpr (EPI == kEpiStore || EPI == kEpiResidHF) {
+        const int r0 = 16 * t;
+        const int rows = a.m[0].rows;
+        set(0, r0, clamp8(rows, r0), 0, r0 + 8, clamp8(rows, r0 + 8));
+        r.kind = 0;
+    } else if constexpr (EPI == kEpiQkvRef) {
+        const int qt = (a.m[0].rows + 15) / 16;
+        if (t < qt) {
+            const int r0 = 16 * t;
+            set(0, r0, clamp8(a.m[0].rows, r0), 0, r0 + 8, clamp8(a.m[0].rows, r0 + 8));
+            r.kind = 0;
+        } else {
+            const int j0 = 8 * (t - qt);
+            set(1, j0, clamp8(a.m[1].rows, j0), 2, j0, clamp8(a.m[2].rows, j0));
+            r.kind = 1;
+        }
+    } else if constexpr (EPI == kEpiQkvRopeHF) {
+        const int half = a.head_dim / 2;  // 64: 8 tiles per head
+        const int per_head = half / 8;
+        const int qt = a.q_heads * per_head;
+        const int kt = a.kv_heads * per_head;
+        if (t < qt + kt) {
+            const int s = t < qt ? 0 : 1;
+            const int u = t < qt ? t : t - qt;
+            const int head = u / per_head;
+            const int i0 = 8 * (u - head * per_head);
+            const int row = head * a.head_dim + i0;
+            set(s, row, 8, s, row + half, 8);
+            r.kind = s;
+        } else {
+            const int r0 = 16 * (t - qt - kt);
+            const int rows = a.m[2].rows;
+            set(2, r0, clamp8(rows, r0), 2, r0 + 8, clamp8(rows, r0 + 8));
+            r.kind = 2;
+        }
+    } else {  // SwiGLU: gate rows in A, up rows in B
+        const int j0 = 8 * t;
+        set(0, j0, clamp8(a.m[0].rows, j0), 1, j0, clamp8(a.m[1].rows, j0));
+        r.kind = 0;
+    }
+    return r;
+}
+
+template <int EPI>
+__host__ __device__ inline int mma_tiles(const Nf4GemvArgs& a) {
+    if constexpr (EPI == kEpiStore || EPI == kEpiResidHF) return (a.m[0].rows + 15) / 16;
+    else if constexpr (EPI == kEpiQkvRef) return (a.m[0].rows + 15) / 16 + (a.m[1].rows + 7) / 8;
+    else if constexpr (EPI == kEpiQkvRopeHF) return (a.q_heads + a.kv_heads) * (a.head_dim / 16) + (a.m[2].rows + 15) / 16;
+    else return (a.m[0].rows + 7) / 8;
+}
+
+// Epilogue for one row pair (row A value vA, row B value vB) owned by lane g.
+template <int EPI, int OT>
+__device__ __forceinline__ void mma_epilogue(const Nf4GemvArgs& a, const TileRows& r, int g, float vA, float vB) {
+    const bool okA = g < r.nA, okB = g < r.nB;
+    if constexpr (EPI == kEpiStore || EPI == kEpiResidHF || EPI == kEpiQkvRef) {
+        RowPair p;
+        p.r0 = r.rA + g;
+        p.r1 = r.rB + g;
+        if constexpr (EPI == kEpiQkvRef) {
+            if (r.kind == 1) {
+                if (okA) store_elem<OT>(a.out[1], p.r0, vA + load_elem<OT>(a.bias[1], p.r0));
+                if (okB) store_elem<OT>(a.out[2], p.r1, vB + load_elem<OT>(a.bias[2], p.r1));
+                return;
+            }
+            if (okA) store_elem<OT>(a.out[0], p.r0, vA + load_elem<OT>(a.bias[0], p.r0));
+            if (okB) store_elem<OT>(a.out[0], p.r1, vB + load_elem<OT>(a.bias[0], p.r1));
+        } else if constexpr (EPI == kEpiStore) {
+            if (okA) store_elem<OT>(a.out[0], p.r0, vA + (a.bias[0] ? load_elem<OT>(a.bias[0], p.r0) : 0.0F));
+            if (okB) store_elem<OT>(a.out[0], p.r1, vB + (a.bias[0] ? load_elem<OT>(a.bias[0], p.r1) : 0.0F));
+        } else {
+            uint16_t* res = static_cast<uint16_t*>(a.resid);
+            if (okA) res[p.r0] = f32_to_bf16_bits(bf16_bits_to_f32(res[p.r0]) + round_bf16(vA));
+            if (okB) res[p.r1] = f32_to_bf16_bits(bf16_bits_to_f32(res[p.r1]) + round_bf16(vB));
+        }
+    } else if constexpr (EPI == kEpiQkvRopeHF) {
+        RowPair p;
+        p.r0 = r.rA + g;
+        p.r1 = r.rB + g;
+        if (r.kind == 2) {
+            // V rows: no rotation; both groups are plain rows
+            const int pos = *a.pos_dev;
+            if (pos < 0 || pos >= a.kv_cap || pos >= a.max_pos) {
+                if (a.err != nullptr) atomicOr(a.err, 2);
+                return;
+            }
+            uint16_t* vc = static_cast<uint16_t*>(a.out[2]);
+            float y[2] = {round_bf16(vA), round_bf16(vB)};
+            const int rows[2] = {p.r0, p.r1};
+            const bool ok[2] = {okA, okB};
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                if (!ok[i]) continue;
+                float v = y[i];
+                if (a.bias[2] != nullptr) v = round_bf16(v + load_elem<kBF16>(a.bias[2], rows[i]));
+                const int h = rows[i] / a.head_dim, d = rows[i] - h * a.head_dim;
+                vc[(static_cast<int64_t>(h) * a.kv_cap + pos) * a.head_dim + d] = f32_to_bf16_bits(v);
+            }
+            return;
+        }
+        p.kind = r.kind;
+        epilogue<kEpiQkvRopeHF, OT>(a, p, vA, vB);
+    } else if constexpr (EPI == kEpiSwiGluRef || EPI == kEpiSwiGluHF) {
+        if (!okA) return;
+        RowPair p;
+        p.r0 = r.rA + g;
+        p.r1 = p.r0;
+        p.kind = 0;
+        epilogue<EPI, OT>(a, p, vA, vB);
+    }
+}
+
+// Stage the activation vector as plain (unswizzled) f16 pairs.
+template <int IN, int XT>
+__device__ __forceinline__ void stage_x_plain(const Nf4GemvArgs& a, uint32_t* xp, float* red) {
+    const int tid = threadIdx.x, nthreads = blockDim.x, K = a.K;
+    float inv = 1.0F;
+    if constexpr (IN != kInRaw) {
+        float ss = 0.0F;
+        for (int i = tid; i < K; i += nthreads) {
+            const float v = load_elem<XT>(a.x, i);
+            ss += v * v;
+        }
+        ss = warp_sum(ss);
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        __syncthreads();
+        if (tid < 32) {
+            float v = tid < (nthreads >> 5) ? red[tid] : 0.0F;
+            v = warp_sum(v);
+            if (tid == 0) red[0] = 1.0F / sqrtf(v / static_cast<float>(K) + a.eps);
+        }
+        __syncthreads();
+        inv = red[0];
+    }
+    bool overflow = false;
+    for (int j = tid; j < K / 2; j += nthreads) {
+        float v[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int i = 2 * j + h;
+            float x = load_elem<XT>(a.x, i);
+            if constexpr (IN == kInNormRef) {
+                x = x * inv * load_elem<XT>(a.norm_w, i);
+                if (a.norm_ws != nullptr && blockIdx.x == 0) a.norm_ws[i] = x;
+            } else if constexpr (IN == kInNormHF) {
+                x = round_bf16(load_elem<XT>(a.norm_w, i) * round_bf16(x * inv));
+            }
+            overflow |= !(fabsf(x) <= 65504.0F);
+            v[h] = x;
+        }
+        xp[j] = static_cast<uint32_t>(f32_to_f16_bits(v[0])) | (static_cast<uint32_t>(f32_to_f16_bits(v[1])) << 16);
+    }
+    if (overflow && a.err != nullptr) atomicOr(a.err, 1);
+    __syncthreads();
+}
+
+struct MmaStepRegs {
+    uint2 wA[kMmaGroup];
+    uint2 wB[kMmaGroup];
+    float sA[kMmaGroup];
+    float sB[kMmaGroup];
+};
+
+__device__ __forceinline__ uint2 ld_stream_u2(const void* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+// Load one prefetch step: kMmaGroup blocks starting at block b of the warp's
+// rows g (group A) and g (group B); blocks at or past `bend` are skipped.
+__device__ __forceinline__ void mma_load_step(MmaStepRegs& R, const TileRows& tr, int g, int t, int64_t rb, int64_t ab,
+                                              int b, int bend) {
+    const int gA = min(g, max(tr.nA - 1, 0));
+    const int gB = min(g, max(tr.nB - 1, 0));
+    const uint8_t* pA = tr.wA + rb * gA + 8 * t;
+    const uint8_t* pB = tr.wB + rb * gB + 8 * t;
+    const float* qA = tr.sA + ab * gA;
+    const float* qB = tr.sB + ab * gB;
+#pragma unroll
+    for (int j = 0; j < kMmaGroup; ++j) {
+        const int blk = b + j;
+        if (blk < bend) {
+            R.wA[j] = ld_stream_u2(pA + 32 * static_cast<int64_t>(blk));
+            R.wB[j] = ld_stream_u2(pB + 32 * static_cast<int64_t>(blk));
+            R.sA[j] = __ldg(qA + blk);
+            R.sB[j] = __ldg(qB + blk);
+        } else {
+            R.wA[j] = make_uint2(0x77777777u, 0x77777777u);  // level 0.0 codes
+            R.wB[j] = make_uint2(0x77777777u, 0x77777777u);
+            R.sA[j] = 0.0F;
+            R.sB[j] = 0.0F;
+        }
+    }
+}
+
+__device__ __forceinline__ void mma_compute_step(const MmaStepRegs& R, const uint32_t* lut, uint32_t lane_off,
+                                                 const uint32_t* xp, int t, int b, int bend, float* tot) {
+#pragma unroll
+    for (int j = 0; j < kMmaGroup; ++j) {
+        const int blk = b + j;
+        if (blk >= bend) break;  // warp-uniform: the staged activations end at this warp's last block
+        const uint4 x0 = *reinterpret_cast<const uint4*>(xp + 32 * blk + 8 * t);
+        const uint4 x1 = *reinterpret_cast<const uint4*>(xp + 32 * blk + 8 * t + 4);
+        float c[4] = {0.0F, 0.0F, 0.0F, 0.0F};
+        const uint32_t wa0 = R.wA[j].x, wa1 = R.wA[j].y, wb0 = R.wB[j].x, wb1 = R.wB[j].y;
+        // k-step 0: bytes 0,1   k-step 1: bytes 2,3   k-step 2: bytes 4,5   k-step 3: bytes 6,7
+        mma_f16_16816(c, lut_at(lut, lut_off_b0(wa0, lane_off)), lut_at(lut, lut_off_b0(wb0, lane_off)),
+                      lut_at(lut, lut_off_b1(wa0, lane_off)), lut_at(lut, lut_off_b1(wb0, lane_off)), x0.x, x0.y);
+        mma_f16_16816(c, lut_at(lut, lut_off_b2(wa0, lane_off)), lut_at(lut, lut_off_b2(wb0, lane_off)),
+                      lut_at(lut, lut_off_b3(wa0, lane_off)), lut_at(lut, lut_off_b3(wb0, lane_off)), x0.z, x0.w);
+        mma_f16_16816(c, lut_at(lut, lut_off_b0(wa1, lane_off)), lut_at(lut, lut_off_b0(wb1, lane_off)),
+                      lut_at(lut, lut_off_b1(wa1, lane_off)), lut_at(lut, lut_off_b1(wb1, lane_off)), x1.x, x1.y);
+        mma_f16_16816(c, lut_at(lut, lut_off_b2(wa1, lane_off)), lut_at(lut, lut_off_b2(wb1, lane_off)),
+                      lut_at(lut, lut_off_b3(wa1, lane_off)), lut_at(lut, lut_off_b3(wb1, lane_off)), x1.z, x1.w);
+        tot[0] = fmaf(c[0], R.sA[j], tot[0]);
+        tot[1] = fmaf(c[1], R.sA[j], tot[1]);
+        tot[2] = fmaf(c[2], R.sB[j], tot[2]);
+        tot[3] = fmaf(c[3], R.sB[j], tot[3]);
+    }
+}
+
+template <int IN, int XT, int EPI, int OT>
+__global__ void __launch_bounds__(kMmaThreads, 2) nf4_gemv_mma_kernel(const Nf4GemvArgs a) {
+    __shared__ __align__(16) uint32_t lut[kLutWords];
+    __shared__ float red[32];
+    __shared__ __align__(16) float part[kMmaWarps][32][4];
+    extern __shared__ __align__(16) uint32_t xp[];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(lane) << 2;
+    const int nblk = a.K / kBlocksize;
+    // this warp's slice of the K blocks (same step count for every warp)
+    const int b_begin = (nblk * warp) / kMmaWarps;
+    const int b_end = (nblk * (warp + 1)) / kMmaWarps;
+    const int per_warp_max = (nblk + kMmaWarps - 1) / kMmaWarps;
+    const int steps_per_tile = (per_warp_max + kMmaGroup - 1) / kMmaGroup;
+    const int ntiles = mma_tiles<EPI>(a);
+    const int64_t rb = a.K / 2, ab = nblk;
+
+    build_pair_lut(lut, tid, blockDim.x);
+    // weights are static: fetch this warp's first step before waiting on the producer
+    MmaStepRegs R0, R1;
+    int tile = blockIdx.x;
+    TileRows tr = decode_tile<EPI>(a, tile < ntiles ? tile : 0);
+    if (tile < ntiles) mma_load_step(R0, tr, g, t, rb, ab, b_begin, b_end);
+    pdl_launch_dependents();
+    pdl_wait_on_producer();
+    stage_x_plain<IN, XT>(a, xp, red);  // ends with __syncthreads (also covers the table)
+
+    int step = 0;  // step index within the current tile
+    while (tile < ntiles) {
+        float tot[4] = {0.0F, 0.0F, 0.0F, 0.0F};
+        for (step = 0; step < steps_per_tile; step += 2) {
+            // R0 holds `step`; fetch step+1 (or the next tile's first step) into R1
+            const bool has1 = step + 1 < steps_per_tile;
+            TileRows nt = tr;
+            int ntile = tile;
+            if (has1) {
+                mma_load_step(R1, tr, g, t, rb, ab, b_begin + (step + 1) * kMmaGroup, b_end);
+            } else {
+                ntile = tile + gridDim.x;
+                if (ntile < ntiles) {
+                    nt = decode_tile<EPI>(a, ntile);
+                    mma_load_step(R1, nt, g, t, rb, ab, b_begin, b_end);
+                }
+            }
+            mma_compute_step(R0, lut, lane_off, xp, t, b_begin + step * kMmaGroup, b_end, tot);
+            if (has1) {
+                // R1 holds step+1; fetch step+2 (or the next tile's first step) into R0
+                const bool has2 = step + 2 < steps_per_tile;
+                if (has2) {
+                    mma_load_step(R0, tr, g, t, rb, ab, b_begin + (step + 2) * kMmaGroup, b_end);
+                } else {
+                    ntile = tile + gridDim.x;
+                    if (ntile < ntiles) {
+                        nt = decode_tile<EPI>(a, ntile);
+                        mma_load_step(R0, nt, g, t, rb, ab, b_begin, b_end);
+                    }
+                }
+                mma_compute_step(R1, lut, lane_off, xp, t, b_begin + (step + 1) * kMmaGroup, b_end, tot);
+            } else {
+                // next tile's first step sits in R1: move it to R0
+                R0 = R1;
+            }
+        }
+        // ---- cross-warp reduction of the fragments, then the epilogue
+        *reinterpret_cast<float4*>(&part[warp][lane][0]) = make_float4(tot[0], tot[1], tot[2], tot[3]);
+        __syncthreads();
+        if (warp == 0 && t == 0) {
+            float vA = 0.0F, vB = 0.0F;
+#pragma unroll
+            for (int w = 0; w < kMmaWarps; ++w) {
+                vA += part[w][lane][0];  // column 0 (batch 0), row group A
+                vB += part[w][lane][2];  // column 0, row group B
+            }
+            mma_epilogue<EPI, OT>(a, tr, g, vA, vB);
+        }
+        __syncthreads();
+        tile += gridDim.x;
+        if (tile < ntiles) tr = decode_tile<EPI>(a, tile);
+    }
+}
+
+}  // namespace kc

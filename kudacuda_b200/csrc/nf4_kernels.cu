@@ -2,8 +2,10 @@
 // the bit-exact dequantiser and the on-device NF4 quantiser.
 #include "kc_launch.h"
 #include "nf4_gemv.cuh"
+#include "nf4_gemv_mma.cuh"
 
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 
 namespace kc {
@@ -42,24 +44,23 @@ cudaError_t run_gemv(Nf4GemvArgs& a, cudaStream_t s) {
     a.ntasks = gemv_tasks(EPI, a);
     if (a.ntasks <= 0) return cudaSuccess;
     const int dev = current_device_index();
-    // Bulk-copy ring kernel when every row segment and absmax slice is
-    // 16-byte aligned (K % 256 == 0, aligned bases); direct-load kernel else.
-    bool tma_ok = (a.K % 256) == 0;
-    for (int i = 0; i < 3; ++i)
-        if (a.m[i].packed != nullptr && !aligned16(a.m[i].absmax)) tma_ok = false;
-    if (tma_ok) {
-        const size_t smem = kTmaRingBytes + static_cast<size_t>(a.K) * 2;
-        if (smem > 160 * 1024) return cudaErrorInvalidValue;
-        auto kernel = nf4_gemv_tma_kernel<IN, XT, EPI, OT>;
-        static std::atomic<bool> tma_attr[64];
-        if (!tma_attr[dev].load(std::memory_order_acquire)) {
-            const cudaError_t st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    // Tensor-core kernel (table lookups -> mma fragments) unless the
+    // measurement override asks for the CUDA-core variant.
+    static const char* forced = std::getenv("KUDACUDA_NF4_GEMV_TACTIC");
+    const bool use_mma = !(forced != nullptr && std::strcmp(forced, "fma") == 0);
+    if (use_mma) {
+        const size_t smem = static_cast<size_t>(a.K) * 2;
+        if (smem > 64 * 1024) return cudaErrorInvalidValue;
+        auto kernel = nf4_gemv_mma_kernel<IN, XT, EPI, OT>;
+        static std::atomic<bool> mma_attr[64];
+        if (!mma_attr[dev].load(std::memory_order_acquire)) {
+            const cudaError_t st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
             if (st != cudaSuccess) return st;
-            tma_attr[dev].store(true, std::memory_order_release);
+            mma_attr[dev].store(true, std::memory_order_release);
         }
-        int blocks = (a.ntasks + kTmaWarps - 1) / kTmaWarps;
-        if (blocks > device_sm_count() * 2) blocks = device_sm_count() * 2;
-        return launch_pdl(kernel, dim3(blocks), dim3(kTmaWarps * 32), smem, s, a);
+        const int tiles = mma_tiles<EPI>(a);
+        int blocks = tiles < device_sm_count() * 2 ? tiles : device_sm_count() * 2;
+        return launch_pdl(kernel, dim3(blocks), dim3(kMmaThreads), smem, s, a);
     }
     const size_t smem = static_cast<size_t>(a.K) * 2;
     auto kernel = nf4_gemv_kernel<IN, XT, EPI, OT>;

@@ -1,0 +1,201 @@
+"""Per-op microbenchmark of the sm_100a kernels (device time per launch).
+
+Each op is launched ``--launches`` times inside one CUDA graph, cycling over
+``--copies`` independent weight sets so the bytes read per graph replay exceed
+the 126 MB L2 (every launch streams from HBM); the graph is replayed
+``--reps`` times between two CUDA events on its stream.  Algorithmic bytes are
+those the op must read/write once (NF4 packed + absmax + activations, or the
+KV rows for attention).
+
+    python -m kudacuda_b200.microbench --op swiglu [--copies 12 --launches 36 --reps 20]
+    ops: gemv_11008x2048 gemv_2048x11008 qkv_rope oproj down swiglu gqa512 gqa2048 lm_head all
+
+The same command with ``--reps 1 --launches 4`` is the small case used for ncu
+captures (see profiles/).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import sys
+from typing import Any, Callable
+
+from .kudacuda_sidecar import KudaCudaBridge
+
+
+def _peak() -> float:
+    import json as _j
+    from pathlib import Path
+
+    p = Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
+    return float(_j.loads(p.read_text())["hbm_gbs"]) if p.exists() else 6650.0
+
+
+class OpCase:
+    def __init__(self, name: str, nbytes: int, launch: Callable[[int, int], None]) -> None:
+        self.name = name
+        self.nbytes = nbytes
+        self.launch = launch  # launch(copy_index, stream_ptr)
+
+
+def _nf4(torch, rows: int, k: int, copies: int, device: str) -> list[tuple[Any, Any]]:
+    out = []
+    for _ in range(copies):
+        packed = torch.randint(0, 256, (rows * k // 2, 1), dtype=torch.uint8, device=device)
+        absmax = torch.rand(rows * k // 64, device=device) * 0.05 + 0.01
+        out.append((packed, absmax))
+    return out
+
+
+def build_cases(torch, bridge: KudaCudaBridge, names: list[str], copies: int, device: str) -> list[OpCase]:
+    bf16 = torch.bfloat16
+    cases = []
+    H, I, V = 2048, 11008, 151936
+
+    def vec(n, scale=1.0):
+        return (torch.randn(n, device=device) * scale).to(bf16)
+
+    for name in names:
+        if name.startswith("gemv_"):
+            rows, k = (int(v) for v in name[5:].split("x"))
+            W = _nf4(torch, rows, k, copies, device)
+            x, y = vec(k), torch.empty(rows, dtype=bf16, device=device)
+            nb = rows * k // 2 + rows * k // 16 + 2 * k + 2 * rows
+
+            def f(i, sp, W=W, x=x, y=y, rows=rows, k=k):
+                p, a = W[i % len(W)]
+                bridge.dispatch_nf4_gemv(x, p, a, y, rows=rows, k=k, stream_ptr=sp)
+
+            cases.append(OpCase(name, nb, f))
+        elif name in ("oproj", "down"):
+            rows, k = (H, H) if name == "oproj" else (H, I)
+            W = _nf4(torch, rows, k, copies, device)
+            x, r = vec(k), vec(rows)
+            nb = rows * k // 2 + rows * k // 16 + 2 * k + 4 * rows
+
+            def f(i, sp, W=W, x=x, r=r, rows=rows, k=k):
+                p, a = W[i % len(W)]
+                bridge.dispatch_nf4_linear_residual(x, p, a, r, rows=rows, k=k, stream_ptr=sp)
+
+            cases.append(OpCase(name, nb, f))
+        elif name == "swiglu":
+            G = _nf4(torch, I, H, copies, device)
+            U = _nf4(torch, I, H, copies, device)
+            x, nw, h = vec(H), (1 + vec(H, 0.02).float()).to(bf16), torch.empty(I, dtype=bf16, device=device)
+            nb = 2 * (I * H // 2 + I * H // 16) + 4 * H + 2 * I
+
+            def f(i, sp, G=G, U=U, x=x, nw=nw, h=h):
+                bridge.dispatch_swiglu_bf16(x, nw, G[i % len(G)], U[i % len(U)], h, epsilon=1e-6, stream_ptr=sp)
+
+            cases.append(OpCase(name, nb, f))
+        elif name == "qkv_rope":
+            from .decode_engine import rope_tables
+
+            Q = _nf4(torch, 2048, H, copies, device)
+            K = _nf4(torch, 256, H, copies, device)
+            Vv = _nf4(torch, 256, H, copies, device)
+            x, nw = vec(H), (1 + vec(H, 0.02).float()).to(bf16)
+            qb, kb, vb = vec(2048, 0.02), vec(256, 0.02), vec(256, 0.02)
+            cos, sin = rope_tables(torch, 1024, 128, 1e6, device)
+            pos = torch.tensor([100], dtype=torch.int32, device=device)
+            qo = torch.empty(2048, dtype=bf16, device=device)
+            kc = torch.zeros((2, 512, 128), dtype=bf16, device=device)
+            vc = torch.zeros((2, 512, 128), dtype=bf16, device=device)
+            nb = 2560 * H // 2 + 2560 * H // 16 + 4 * H + 2 * 2560 * 2
+
+            def f(i, sp, Q=Q, K=K, Vv=Vv):
+                j = i % len(Q)
+                bridge.dispatch_attention_input(x, nw, (*Q[j], qb), (*K[j], kb), (*Vv[j], vb), cos, sin, pos, qo, kc, vc,
+                                                q_heads=16, kv_heads=2, head_dim=128, kv_capacity=512, epsilon=1e-6,
+                                                stream_ptr=sp)
+
+            cases.append(OpCase(name, nb, f))
+        elif name.startswith("gqa"):
+            L = int(name[3:])
+            KC = [torch.randn((2, L, 128), device=device).to(bf16) for _ in range(copies)]
+            VC = [torch.randn((2, L, 128), device=device).to(bf16) for _ in range(copies)]
+            q, out = vec(16 * 128), torch.empty(16 * 128, dtype=bf16, device=device)
+            kvl = torch.tensor([L], dtype=torch.int32, device=device)
+            ws, tk, nbytes = bridge.gqa_workspace(batch=1, query_heads=16, kv_heads=2, kv_extent=L, device=device,
+                                                  torch_module=torch)
+            nb = 2 * 2 * L * 128 * 2 + 2 * 2 * 16 * 128
+
+            def f(i, sp, KC=KC, VC=VC, L=L, q=q, out=out, kvl=kvl, ws=ws, tk=tk, nbytes=nbytes):
+                j = i % len(KC)
+                bridge.dispatch_gqa_decode_splitkv(q, KC[j], VC[j], out, ws, tk, kv_len_device=kvl, kv_len=L,
+                                                   kv_stride=L, query_heads=16, kv_heads=2, stream_ptr=sp,
+                                                   workspace_bytes=nbytes)
+
+            cases.append(OpCase(name, nb, f))
+        elif name == "lm_head":
+            n_emb = max(1, min(copies, 2))
+            E = [torch.randn((V, H), device=device).to(bf16) for _ in range(n_emb)]
+            x, fn = vec(H), (1 + vec(H, 0.02).float()).to(bf16)
+            tok = torch.zeros(1, dtype=torch.int32, device=device)
+            lg = torch.empty(V, dtype=bf16, device=device)
+            ws = torch.zeros(bridge.lm_head_workspace_bytes() // 4, device=device)
+            tk = torch.zeros(1, dtype=torch.int32, device=device)
+            nb = V * H * 2 + 2 * V
+
+            def f(i, sp, E=E):
+                bridge.dispatch_lm_head_argmax(x, fn, E[i % len(E)], tok, ws, tk, logits=lg, epsilon=1e-6, stream_ptr=sp)
+
+            cases.append(OpCase(name, nb, f))
+        else:
+            raise SystemExit(f"unknown op {name}")
+    return cases
+
+
+def time_case(torch, bridge: KudaCudaBridge, case: OpCase, launches: int, reps: int, stream) -> dict:
+    sp = int(stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        for i in range(launches):  # eager warm-up (lazy per-kernel set-up)
+            case.launch(i, sp)
+    stream.synchronize()
+    bridge.begin_capture(stream_ptr=sp)
+    for i in range(launches):
+        case.launch(i, sp)
+    bridge.end_capture(stream_ptr=sp)
+    bridge.replay_graph(stream_ptr=sp)
+    stream.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(reps):
+        bridge.replay_graph(stream_ptr=sp)
+    e.record(stream)
+    e.synchronize()
+    us = s.elapsed_time(e) * 1e3 / (reps * launches)
+    gbs = case.nbytes / (us * 1e-6) / 1e9
+    bridge.reset_graph()
+    return {"op": case.name, "us_per_launch": round(us, 3), "bytes": case.nbytes, "gbs": round(gbs, 1),
+            "frac_of_measured_hbm": round(gbs / _peak(), 4)}
+
+
+def main(argv=None) -> int:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--op", default="all")
+    p.add_argument("--copies", type=int, default=12)
+    p.add_argument("--launches", type=int, default=36)
+    p.add_argument("--reps", type=int, default=20)
+    p.add_argument("--device", default="cuda:0")
+    args = p.parse_args(argv)
+    import torch
+
+    torch.cuda.set_device(torch.device(args.device))
+    names = (["gemv_11008x2048", "gemv_2048x11008", "qkv_rope", "oproj", "down", "swiglu", "gqa512", "gqa2048",
+              "lm_head"] if args.op == "all" else args.op.split(","))
+    bridge = KudaCudaBridge(device_id=torch.device(args.device).index or 0)
+    stream = torch.cuda.Stream()
+    for case in build_cases(torch, bridge, names, args.copies, args.device):
+        print(json.dumps(time_case(torch, bridge, case, args.launches, args.reps, stream)), flush=True)
+    err = bridge.error_word(clear=True)
+    if err:
+        print(json.dumps({"device_error_word": err}))
+        return 1
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,197 @@
+"""GPU parity of the composed decode step (configs 2 and 3 semantics) against
+the oracle.
+
+* op-by-op: every op of one decoder layer runs through the bridge on the
+  plan's own buffers and is compared with the oracle fed the GPU's previous
+  output (isolates each kernel inside the composition);
+* the whole oracle layer (kc_layer_step_hf) against the GPU layer;
+* graph replay against eager execution (must be bit-identical);
+* greedy decode: teacher-forced top-1 agreement with the oracle.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.test_gpu_kernels import ATOL, RTOL, bf16_ulp, close, close_chain
+
+pytestmark = pytest.mark.gpu
+
+
+def _b16(t) -> np.ndarray:
+    import torch
+
+    torch.cuda.synchronize()
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def _nf4(lin):
+    return (lin.packed.reshape(-1).cpu().numpy(), lin.absmax.cpu().numpy())
+
+
+def _layer_np(L):
+    return {"in_norm": _b16(L.in_norm), "post_norm": _b16(L.post_norm), "q": _nf4(L.q), "k": _nf4(L.k),
+            "v": _nf4(L.v), "o": _nf4(L.o), "gate": _nf4(L.gate), "up": _nf4(L.up), "down": _nf4(L.down),
+            "q_b": None if L.q_bias is None else _b16(L.q_bias),
+            "k_b": None if L.k_bias is None else _b16(L.k_bias),
+            "v_b": None if L.v_bias is None else _b16(L.v_bias)}
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    import torch
+
+    from kudacuda_b200.decode_engine import StaticDecodePlan, random_weights, tiny_config
+    from kudacuda_b200.kudacuda_sidecar import KudaCudaBridge
+
+    torch.cuda.set_device(0)
+    cfg = tiny_config(layers=2, vocab=4096)
+    bridge = KudaCudaBridge(device_id=0)
+    weights = random_weights(bridge, cfg, seed=11, device="cuda:0")
+    plan = StaticDecodePlan(bridge, weights, kv_bucket=64, max_tokens=64, device="cuda:0")
+    stream = torch.cuda.Stream()
+    plan.capture(stream)
+    yield cfg, bridge, weights, plan, stream
+    bridge.reset_graph()
+    bridge.shutdown()
+
+
+def _lin_ref(x_bits, lin_np, rows, k, bias=None):
+    y = O.bf16_bits(O.nf4_gemv(O.bf16_to_f32(x_bits), lin_np[0], lin_np[1], rows, k))
+    if bias is not None:
+        y = O.bf16_bits(O.bf16_to_f32(y) + O.bf16_to_f32(bias))
+    return y
+
+
+@pytest.mark.parametrize("pos", [0, 5])
+def test_layer_ops_compose_like_oracle(tiny, pos):
+    import torch
+
+    cfg, bridge, w, plan, stream = tiny
+    b = plan.buffers
+    sp = int(stream.cuda_stream)
+    d, qh, kvh, H, I = cfg.head_dim, cfg.q_heads, cfg.kv_heads, cfg.hidden, cfg.intermediate
+    plan.reset_cache()
+    if pos > 0:  # earlier positions hold random K/V rows
+        g = torch.Generator(device="cuda:0").manual_seed(pos)
+        b.kcache[0, :, :pos] = torch.randn((kvh, pos, d), generator=g, device="cuda:0").to(torch.bfloat16)
+        b.vcache[0, :, :pos] = torch.randn((kvh, pos, d), generator=g, device="cuda:0").to(torch.bfloat16)
+    plan.set_state(123, pos)
+    L = w.layers[0]
+    Lnp = _layer_np(L)
+    cos, sin = _b16(b.rope_cos), _b16(b.rope_sin)
+    with torch.cuda.stream(stream):
+        bridge.dispatch_embedding(w.embedding, b.state[0:1], b.x, stream_ptr=sp)
+    x0 = _b16(b.x).copy()
+    np.testing.assert_array_equal(x0, _b16(w.embedding[123]))
+
+    with torch.cuda.stream(stream):
+        bridge.dispatch_attention_input(b.x, L.in_norm, L.q.as_tuple(L.q_bias), L.k.as_tuple(L.k_bias),
+                                        L.v.as_tuple(L.v_bias), b.rope_cos, b.rope_sin, b.state[1:2], b.q,
+                                        b.kcache[0], b.vcache[0], q_heads=qh, kv_heads=kvh, head_dim=d,
+                                        kv_capacity=plan.kv_bucket, epsilon=cfg.eps, stream_ptr=sp)
+    xn = O.rmsnorm_hf_bf16(x0, Lnp["in_norm"], cfg.eps)
+    q_lin = _lin_ref(xn, Lnp["q"], qh * d, H, Lnp["q_b"])
+    k_lin = _lin_ref(xn, Lnp["k"], kvh * d, H, Lnp["k_b"])
+    v_lin = _lin_ref(xn, Lnp["v"], kvh * d, H, Lnp["v_b"])
+    q_ref = O.rope_hf_bf16(q_lin, qh, d, cos[pos], sin[pos])
+    k_ref = O.rope_hf_bf16(k_lin, kvh, d, cos[pos], sin[pos])
+    qm = np.abs(O.bf16_to_f32(q_lin)).reshape(qh, 2, 64).max(axis=1).repeat(2, axis=0).reshape(-1)
+    close_chain(O.bf16_to_f32(_b16(b.q)), O.bf16_to_f32(q_ref), intermediates=(qm, qm, qm))
+    kc = _b16(b.kcache[0])
+    vc = _b16(b.vcache[0])
+    km = np.abs(O.bf16_to_f32(k_lin)).reshape(kvh, 2, 64).max(axis=1).repeat(2, axis=0).reshape(-1)
+    close_chain(O.bf16_to_f32(kc[:, pos].reshape(-1)), O.bf16_to_f32(k_ref), intermediates=(km, km, km))
+    close_chain(O.bf16_to_f32(vc[:, pos].reshape(-1)), O.bf16_to_f32(v_lin))
+
+    with torch.cuda.stream(stream):
+        bridge.dispatch_gqa_decode_splitkv(b.q, b.kcache[0], b.vcache[0], b.attn, b.gqa_ws, b.gqa_tickets,
+                                           kv_len_device=b.state[2:3], kv_len=plan.kv_bucket,
+                                           kv_stride=plan.kv_bucket, query_heads=qh, kv_heads=kvh,
+                                           scale=1.0 / math.sqrt(d), stream_ptr=sp, workspace_bytes=b.gqa_ws_bytes)
+    attn_ref = O.gqa_decode(_b16(b.q), np.ascontiguousarray(kc), np.ascontiguousarray(vc), O.BF16, qh, kvh, d,
+                            pos + 1, plan.kv_bucket, 1.0 / math.sqrt(d))
+    attn = _b16(b.attn)
+    close(O.bf16_to_f32(attn), O.bf16_to_f32(attn_ref), atol=3.5e-3, rtol=3.5e-3)
+
+    with torch.cuda.stream(stream):
+        bridge.dispatch_nf4_linear_residual(b.attn, L.o.packed, L.o.absmax, b.x, rows=H, k=qh * d, stream_ptr=sp)
+    o_ref = _lin_ref(attn, Lnp["o"], H, qh * d)
+    x1_ref = O.bf16_bits(O.bf16_to_f32(x0) + O.bf16_to_f32(o_ref))
+    x1 = _b16(b.x).copy()
+    close_chain(O.bf16_to_f32(x1), O.bf16_to_f32(x1_ref), intermediates=(O.bf16_to_f32(o_ref),))
+
+    with torch.cuda.stream(stream):
+        bridge.dispatch_swiglu_bf16(b.x, L.post_norm, (L.gate.packed, L.gate.absmax), (L.up.packed, L.up.absmax), b.h,
+                                    epsilon=cfg.eps, stream_ptr=sp)
+    xn2 = O.rmsnorm_hf_bf16(x1, Lnp["post_norm"], cfg.eps)
+    gref = O.bf16_to_f32(_lin_ref(xn2, Lnp["gate"], I, H))
+    uref = O.bf16_to_f32(_lin_ref(xn2, Lnp["up"], I, H))
+    act = O.bf16_to_f32(O.bf16_bits(gref / (1.0 + np.exp(-gref))))
+    h_ref = O.bf16_bits(act * uref)
+    h = _b16(b.h).copy()
+    close_chain(O.bf16_to_f32(h), O.bf16_to_f32(h_ref), intermediates=(gref, uref, act))
+
+    with torch.cuda.stream(stream):
+        bridge.dispatch_nf4_linear_residual(b.h, L.down.packed, L.down.absmax, b.x, rows=H, k=I, stream_ptr=sp)
+    d_ref = _lin_ref(h, Lnp["down"], H, I)
+    x2_ref = O.bf16_bits(O.bf16_to_f32(x1) + O.bf16_to_f32(d_ref))
+    close_chain(O.bf16_to_f32(_b16(b.x)), O.bf16_to_f32(x2_ref), intermediates=(O.bf16_to_f32(d_ref),))
+    assert bridge.error_word(clear=True) == 0
+
+
+def test_graph_replay_is_bit_identical_to_eager(tiny):
+    import torch
+
+    cfg, bridge, w, plan, stream = tiny
+    outs = []
+    for mode in ("eager", "graph"):
+        plan.reset_cache()
+        plan.set_state(77, 3)
+        if mode == "eager":
+            with torch.cuda.stream(stream):
+                plan.record(int(stream.cuda_stream))
+        else:
+            plan.replay(stream)
+        stream.synchronize()
+        outs.append((_b16(plan.buffers.x).copy(), _b16(plan.buffers.logits).copy(),
+                     plan.buffers.state.cpu().numpy().copy()))
+    for a, b in zip(*outs):
+        np.testing.assert_array_equal(a, b)
+
+
+def test_greedy_decode_teacher_forced_top1(tiny):
+    """Greedy tokens of the graph decode against the oracle's argmax on the
+    same prefix (teacher forcing); logits within tolerance at every step."""
+
+    import torch
+
+    from kudacuda_b200.decode_engine import greedy_generate
+
+    cfg, bridge, w, plan, stream = tiny
+    prompt = [5, 17, 300, 4000]
+    n_new = 8
+    toks = greedy_generate(plan, prompt, n_new, stream)
+    seq = prompt + toks
+    layers = [_layer_np(L) for L in w.layers]
+    emb = _b16(w.embedding).reshape(cfg.vocab, cfg.hidden)
+    fn = _b16(w.final_norm)
+    cos, sin = _b16(plan.buffers.rope_cos), _b16(plan.buffers.rope_sin)
+    ocfg = dict(hidden=cfg.hidden, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                inter=cfg.intermediate, eps=cfg.eps)
+    kcs = [np.zeros((cfg.kv_heads, plan.kv_bucket, cfg.head_dim), dtype=np.uint16) for _ in layers]
+    vcs = [np.zeros_like(kcs[0]) for _ in layers]
+    agree = 0
+    for pos in range(len(seq) - 1):
+        x = emb[seq[pos]].copy()
+        for li, layer in enumerate(layers):
+            O.layer_step_hf(layer, ocfg, x, kcs[li], vcs[li], plan.kv_bucket, pos, cos[pos], sin[pos])
+        tok, _ = O.lm_head_argmax(x, fn, emb, cfg.eps)
+        if pos >= len(prompt) - 1:
+            agree += int(tok == seq[pos + 1])
+    rate = agree / n_new
+    assert rate >= 0.75, f"teacher-forced top-1 agreement {rate:.2f}"
