@@ -13,6 +13,10 @@ enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
 
 // Launch with programmatic stream serialization so the kernel's prologue
 // (table build, weight prefetch) overlaps the tail of the previous kernel.
+// KUDACUDA_DISABLE_PDL=1 launches with plain stream order (compatibility /
+// debugging control; every kernel still executes in full).
+bool pdl_enabled();
+
 template <typename Kernel, typename... Args>
 inline cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                               Args... args) {
@@ -25,7 +29,7 @@ inline cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem,
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 

@@ -56,6 +56,7 @@ struct TileRows {
     const float* sB;
     int rA, rB;         // first row index of each group (epilogue bookkeeping)
     int nA, nB;         // valid rows in each group (tails)
+    int mA, mB;         // matrix index of each group
     int kind;
 };
 
@@ -72,6 +73,8 @@ __device__ __forceinline__ TileRows decode_tile(const Nf4GemvArgs& a, int t) {
         r.rB = rowB;
         r.nA = nA;
         r.nB = nB;
+        r.mA = mA;
+        r.mB = mB;
     };
     auto clamp8 = [](int rows, int start) { return max(0, min(8, rows - start)); };
     if constexpr (EPI == kEpiStore || EPI == kEpiResidHF) {
@@ -186,10 +189,20 @@ __device__ __forceinline__ void mma_epilogue(const Nf4GemvArgs& a, const TileRow
     }
 }
 
+// Consumer-group barrier: named barrier 1 over the first N threads (the
+// producer warp of the TMA kernel never joins it); N == 0 is the whole CTA.
+template <int N>
+__device__ __forceinline__ void group_sync() {
+    if constexpr (N == 0) __syncthreads();
+    else asm volatile("bar.sync 1, %0;" ::"n"(N) : "memory");
+}
+
 // Stage the activation vector as plain (unswizzled) f16 pairs.
-template <int IN, int XT>
+
+template <int IN, int XT, int GROUP = 0>
 __device__ __forceinline__ void stage_x_plain(const Nf4GemvArgs& a, uint32_t* xp, float* red) {
-    const int tid = threadIdx.x, nthreads = blockDim.x, K = a.K;
+    const int tid = threadIdx.x, K = a.K;
+    const int nthreads = GROUP == 0 ? static_cast<int>(blockDim.x) : GROUP;
     float inv = 1.0F;
     if constexpr (IN != kInRaw) {
         float ss = 0.0F;
@@ -199,13 +212,13 @@ __device__ __forceinline__ void stage_x_plain(const Nf4GemvArgs& a, uint32_t* xp
         }
         ss = warp_sum(ss);
         if ((tid & 31) == 0) red[tid >> 5] = ss;
-        __syncthreads();
+        group_sync<GROUP>();
         if (tid < 32) {
             float v = tid < (nthreads >> 5) ? red[tid] : 0.0F;
             v = warp_sum(v);
             if (tid == 0) red[0] = 1.0F / sqrtf(v / static_cast<float>(K) + a.eps);
         }
-        __syncthreads();
+        group_sync<GROUP>();
         inv = red[0];
     }
     bool overflow = false;
@@ -227,7 +240,7 @@ __device__ __forceinline__ void stage_x_plain(const Nf4GemvArgs& a, uint32_t* xp
         xp[j] = static_cast<uint32_t>(f32_to_f16_bits(v[0])) | (static_cast<uint32_t>(f32_to_f16_bits(v[1])) << 16);
     }
     if (overflow && a.err != nullptr) atomicOr(a.err, 1);
-    __syncthreads();
+    group_sync<GROUP>();
 }
 
 struct MmaStepRegs {
@@ -376,6 +389,184 @@ __global__ void __launch_bounds__(kMmaThreads, 2) nf4_gemv_mma_kernel(const Nf4G
         __syncthreads();
         tile += gridDim.x;
         if (tile < ntiles) tr = decode_tile<EPI>(a, tile);
+    }
+}
+
+}  // namespace kc
+
+namespace kc {
+
+// ---------------------------------------------------------------------------
+// Warp-specialised TMA variant (the production path when K % 256 == 0).
+//
+// One producer warp streams each 16-row tile through a 10-stage shared-memory
+// ring with 2D bulk-tensor loads: per stage, a 512-element K slice of both
+// 8-row groups (4 boxes of 8 rows x 128 B with 128-byte swizzle) and their
+// absmax (2 boxes of 8 rows x 8 fp32), completing on the stage's "full"
+// mbarrier.  Eight consumer warps each take one 64-element block of the
+// slice (the K split), read their A fragments conflict-free thanks to the
+// swizzle, run the table->mma math, and release the stage on its "empty"
+// mbarrier.  ~50 KB of weights are in flight per CTA with no register cost;
+// the producer starts streaming before griddepcontrol.wait because weights
+// are static.  No multicast is used anywhere.
+
+struct GemvMaps {
+    CUtensorMap w[3];  // packed nibbles, [rows][K/2] uint8, box 8 x 128 B, 128B swizzle
+    CUtensorMap s[3];  // absmax, [rows][K/64] fp32, box 8 x 8
+};
+
+constexpr int kTmaCons = 8;
+constexpr int kTmaThreads = (kTmaCons + 1) * 32;
+constexpr int kTmaStages = 10;
+constexpr int kSlice = 512;               // K elements per stage
+constexpr int kBoxBytes = 1024;           // 8 rows x 128 B
+constexpr int kAbsBoxBytes = 256;         // 8 rows x 8 fp32
+constexpr int kTStageBytes = 5 * 1024;    // 4 packed boxes + 2 absmax boxes, padded to keep boxes 1 KB aligned
+constexpr size_t kTRingBytes = static_cast<size_t>(kTmaStages) * kTStageBytes;
+constexpr uint32_t kTStageTx = 4 * kBoxBytes + 2 * kAbsBoxBytes;
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <int IN, int XT, int EPI, int OT>
+__global__ void __launch_bounds__(kTmaThreads, 2) nf4_gemv_tma_kernel(const Nf4GemvArgs a,
+                                                                     const __grid_constant__ GemvMaps maps) {
+    __shared__ __align__(16) uint32_t lut[kLutWords];
+    __shared__ float red[32];
+    __shared__ __align__(16) float part[kTmaCons][32][4];
+    __shared__ __align__(8) uint64_t full_bar[kTmaStages];
+    __shared__ __align__(8) uint64_t empty_bar[kTmaStages];
+    extern __shared__ __align__(16) uint8_t dyn_raw[];
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~uintptr_t(1023));
+    uint32_t* xp = reinterpret_cast<uint32_t*>(ring + kTRingBytes);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nblk = a.K / kBlocksize;
+    const int nslices = (a.K + kSlice - 1) / kSlice;
+    const int ntiles = mma_tiles<EPI>(a);
+
+    if (tid == 0) {
+        for (int i = 0; i < kTmaStages; ++i) {
+            mbar_init(&full_bar[i], 1);
+            mbar_init(&empty_bar[i], kTmaCons);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    if (warp == kTmaCons) {
+        // ---------------- producer: weights are static, no need to wait on the previous kernel
+        if (lane == 0) {
+            int slot = 0;
+            uint32_t phase = 0;
+            for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+                const TileRows tr = decode_tile<EPI>(a, tile);
+                for (int sl = 0; sl < nslices; ++sl) {
+                    if (!mbar_wait_bounded(&empty_bar[slot], phase ^ 1u)) {
+                        if (a.err != nullptr) atomicOr(a.err, 16);
+                        return;
+                    }
+                    uint8_t* st = ring + slot * kTStageBytes;
+                    uint64_t* fb = &full_bar[slot];
+                    mbar_arrive_expect_tx(fb, kTStageTx);
+                    const int x0 = sl * (kSlice / 2);
+                    tma_load_2d(st, &maps.w[tr.mA], x0, tr.rA, fb);
+                    tma_load_2d(st + kBoxBytes, &maps.w[tr.mA], x0 + 128, tr.rA, fb);
+                    tma_load_2d(st + 2 * kBoxBytes, &maps.w[tr.mB], x0, tr.rB, fb);
+                    tma_load_2d(st + 3 * kBoxBytes, &maps.w[tr.mB], x0 + 128, tr.rB, fb);
+                    tma_load_2d(st + 4 * kBoxBytes, &maps.s[tr.mA], sl * (kSlice / kBlocksize), tr.rA, fb);
+                    tma_load_2d(st + 4 * kBoxBytes + kAbsBoxBytes, &maps.s[tr.mB], sl * (kSlice / kBlocksize), tr.rB,
+                                fb);
+                    if (++slot == kTmaStages) {
+                        slot = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers (warps 0..7)
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(lane) << 2;
+    build_pair_lut(lut, tid, kTmaCons * 32);
+    pdl_wait_on_producer();
+    stage_x_plain<IN, XT, kTmaCons * 32>(a, xp, red);  // ends with the consumer barrier (covers the table)
+
+    // this warp's fragment offsets inside a stage (128-byte swizzle: 16-byte
+    // chunk c of box row r sits at chunk c ^ (r & 7))
+    const int box = warp >> 2;
+    const int chunk = 2 * (warp & 3) + (t >> 1);
+    const int frag_off = box * kBoxBytes + g * 128 + ((chunk ^ g) << 4) + 8 * (t & 1);
+    const int abs_off = 4 * kBoxBytes + g * 32 + warp * 4;
+
+    int slot = 0;
+    uint32_t phase = 0;
+    bool failed = false;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const TileRows tr = decode_tile<EPI>(a, tile);
+        float tot[4] = {0.0F, 0.0F, 0.0F, 0.0F};
+        for (int sl = 0; sl < nslices; ++sl) {
+            if (!failed && !mbar_wait_bounded(&full_bar[slot], phase)) {
+                failed = true;
+                if (lane == 0 && a.err != nullptr) atomicOr(a.err, 16);
+            }
+            const int blk = sl * (kSlice / kBlocksize) + warp;
+            if (!failed && blk < nblk) {
+                const uint8_t* st = ring + slot * kTStageBytes;
+                const uint2 wa = *reinterpret_cast<const uint2*>(st + frag_off);
+                const uint2 wb = *reinterpret_cast<const uint2*>(st + 2 * kBoxBytes + frag_off);
+                const float sa = *reinterpret_cast<const float*>(st + abs_off);
+                const float sb = *reinterpret_cast<const float*>(st + abs_off + kAbsBoxBytes);
+                const uint4 x0 = *reinterpret_cast<const uint4*>(xp + 32 * blk + 8 * t);
+                const uint4 x1 = *reinterpret_cast<const uint4*>(xp + 32 * blk + 8 * t + 4);
+                float c[4] = {0.0F, 0.0F, 0.0F, 0.0F};
+                mma_f16_16816(c, lut_at(lut, lut_off_b0(wa.x, lane_off)), lut_at(lut, lut_off_b0(wb.x, lane_off)),
+                              lut_at(lut, lut_off_b1(wa.x, lane_off)), lut_at(lut, lut_off_b1(wb.x, lane_off)), x0.x,
+                              x0.y);
+                mma_f16_16816(c, lut_at(lut, lut_off_b2(wa.x, lane_off)), lut_at(lut, lut_off_b2(wb.x, lane_off)),
+                              lut_at(lut, lut_off_b3(wa.x, lane_off)), lut_at(lut, lut_off_b3(wb.x, lane_off)), x0.z,
+                              x0.w);
+                mma_f16_16816(c, lut_at(lut, lut_off_b0(wa.y, lane_off)), lut_at(lut, lut_off_b0(wb.y, lane_off)),
+                              lut_at(lut, lut_off_b1(wa.y, lane_off)), lut_at(lut, lut_off_b1(wb.y, lane_off)), x1.x,
+                              x1.y);
+                mma_f16_16816(c, lut_at(lut, lut_off_b2(wa.y, lane_off)), lut_at(lut, lut_off_b2(wb.y, lane_off)),
+                              lut_at(lut, lut_off_b3(wa.y, lane_off)), lut_at(lut, lut_off_b3(wb.y, lane_off)), x1.z,
+                              x1.w);
+                tot[0] = fmaf(c[0], sa, tot[0]);
+                tot[1] = fmaf(c[1], sa, tot[1]);
+                tot[2] = fmaf(c[2], sb, tot[2]);
+                tot[3] = fmaf(c[3], sb, tot[3]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty_bar[slot]);
+            if (++slot == kTmaStages) {
+                slot = 0;
+                phase ^= 1u;
+            }
+        }
+        *reinterpret_cast<float4*>(&part[warp][lane][0]) = make_float4(tot[0], tot[1], tot[2], tot[3]);
+        group_sync<kTmaCons * 32>();
+        if (warp == 0 && t == 0) {
+            float vA = 0.0F, vB = 0.0F;
+#pragma unroll
+            for (int w = 0; w < kTmaCons; ++w) {
+                vA += part[w][lane][0];
+                vB += part[w][lane][2];
+            }
+            mma_epilogue<EPI, OT>(a, tr, g, vA, vB);
+        }
+        group_sync<kTmaCons * 32>();
     }
 }
 

@@ -2,6 +2,7 @@
 // the bit-exact dequantiser and the on-device NF4 quantiser.
 #include "kc_launch.h"
 #include "nf4_gemv.cuh"
+#include "kc_tma.h"
 #include "nf4_gemv_mma.cuh"
 
 #include <atomic>
@@ -9,6 +10,11 @@
 #include <cstring>
 
 namespace kc {
+
+bool pdl_enabled() {
+    static const bool enabled = std::getenv("KUDACUDA_DISABLE_PDL") == nullptr;
+    return enabled;
+}
 
 int current_device_index() {
     int dev = 0;
@@ -48,6 +54,39 @@ cudaError_t run_gemv(Nf4GemvArgs& a, cudaStream_t s) {
     // measurement override asks for the CUDA-core variant.
     static const char* forced = std::getenv("KUDACUDA_NF4_GEMV_TACTIC");
     const bool use_mma = !(forced != nullptr && std::strcmp(forced, "fma") == 0);
+    // TMA ring kernel when the tensor maps are legal: absmax rows must be
+    // 16-byte strided (K % 256 == 0) and every base 16-byte aligned.
+    bool tma_ok = use_mma && (a.K % 256) == 0 && !(forced != nullptr && std::strcmp(forced, "mma") == 0);
+    GemvMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    for (int i = 0; i < 3 && tma_ok; ++i) {
+        if (a.m[i].packed == nullptr) continue;
+        if (!aligned16(a.m[i].packed) || !aligned16(a.m[i].absmax)) {
+            tma_ok = false;
+            break;
+        }
+        const uint64_t rows = static_cast<uint64_t>(a.m[i].rows);
+        if (encode_tmap_2d(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, a.m[i].packed, a.K / 2, rows, a.K / 2, 128, 8,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B) != cudaSuccess ||
+            encode_tmap_2d(&maps.s[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.m[i].absmax, a.K / kBlocksize, rows,
+                           a.K / kBlocksize * 4, 8, 8, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B) != cudaSuccess)
+            tma_ok = false;
+    }
+    if (tma_ok) {
+        const size_t smem = 1024 + kTRingBytes + static_cast<size_t>(a.K) * 2;
+        if (smem > 160 * 1024) return cudaErrorInvalidValue;
+        auto kernel = nf4_gemv_tma_kernel<IN, XT, EPI, OT>;
+        static std::atomic<bool> tma_attr[64];
+        if (!tma_attr[dev].load(std::memory_order_acquire)) {
+            const cudaError_t st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+            if (st != cudaSuccess) return st;
+            tma_attr[dev].store(true, std::memory_order_release);
+        }
+        const int tiles = mma_tiles<EPI>(a);
+        int blocks = tiles < device_sm_count() * 2 ? tiles : device_sm_count() * 2;
+        return launch_pdl(kernel, dim3(blocks), dim3(kTmaThreads), smem, s, a, maps);
+    }
     if (use_mma) {
         const size_t smem = static_cast<size_t>(a.K) * 2;
         if (smem > 64 * 1024) return cudaErrorInvalidValue;
@@ -250,7 +289,9 @@ __constant__ float kNf4Midpoints[15];
 template <int IT>
 __global__ void nf4_quantize_kernel(const void* __restrict__ in, int64_t n, uint8_t* __restrict__ packed,
                                     float* __restrict__ absmax) {
-    pdl_launch_dependents();
+    // No early launch_dependents: the GEMV kernels read weights before their
+    // griddepcontrol.wait, so a kernel that writes weights releases its
+    // dependents only by completing.
     pdl_wait_on_producer();
     const int lane = threadIdx.x & 31;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);

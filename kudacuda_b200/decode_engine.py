@@ -347,14 +347,22 @@ class StaticDecodePlan:
         raise NativeCudaError("untied NF4 lm_head is served by the tensor-parallel plan")
 
     # ------------------------------------------------------------------ state
-    def set_state(self, token: int, position: int) -> None:
+    def set_state(self, token: int, position: int, stream: Any = None) -> None:
+        """Write {token, position, kv_len} to the device state, ordered after
+        all work already queued on ``stream`` (and the current stream)."""
+
         torch = self.torch
+        if stream is not None:
+            stream.synchronize()
+        torch.cuda.synchronize(self.device)
         self.buffers.state.copy_(torch.tensor([token, position, position + 1, 0], dtype=torch.int32),
                                  non_blocking=False)
 
     def reset_cache(self) -> None:
+        self.torch.cuda.synchronize(self.device)
         self.buffers.kcache.zero_()
         self.buffers.vcache.zero_()
+        self.torch.cuda.synchronize(self.device)
 
     # ------------------------------------------------------------------ graph
     def capture(self, stream: Any) -> None:
@@ -403,11 +411,17 @@ class StaticDecodePlan:
         if len(prompt) + 1 > self.kv_bucket:
             raise ValueError("prompt does not fit the KV bucket")
         torch = self.torch
+        # host state in, replay, next token out -- all on the replay stream
+        # (kudacuda_sm100_graph_step_host), so a state write can never land
+        # while the previous step is still running
+        host_in = torch.zeros(4, dtype=torch.int32).pin_memory()
+        host_out = torch.zeros(1, dtype=torch.int32).pin_memory()
+        torch.cuda.synchronize(self.device)
+        sp = int(stream.cuda_stream)
         for i, tok in enumerate(prompt):
-            self.buffers.state.copy_(torch.tensor([tok, i, i + 1, 0], dtype=torch.int32), non_blocking=False)
-            self.replay(stream)
-        stream.synchronize()
-        return int(self.buffers.next_token.item())
+            host_in[0], host_in[1], host_in[2] = int(tok), i, i + 1
+            self.bridge.graph_step_host(host_in, self.buffers.state, host_out, self.buffers.next_token, stream_ptr=sp)
+        return int(host_out[0])
 
     def generate_device(self, steps: int, stream: Any) -> None:
         """Replay the graph ``steps`` times with no host interaction; the
@@ -420,6 +434,7 @@ class StaticDecodePlan:
 def greedy_generate(plan: StaticDecodePlan, prompt: list[int], new_tokens: int, stream: Any) -> list[int]:
     """Prompt via decode steps, then ``new_tokens`` greedy tokens on the device."""
 
+    stream.synchronize()
     plan.reset_cache()
     plan.buffers.history.zero_()
     first = plan.prefill(prompt, stream)

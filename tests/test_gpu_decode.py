@@ -75,12 +75,13 @@ def test_layer_ops_compose_like_oracle(tiny, pos):
     b = plan.buffers
     sp = int(stream.cuda_stream)
     d, qh, kvh, H, I = cfg.head_dim, cfg.q_heads, cfg.kv_heads, cfg.hidden, cfg.intermediate
+    stream.synchronize()
     plan.reset_cache()
     if pos > 0:  # earlier positions hold random K/V rows
         g = torch.Generator(device="cuda:0").manual_seed(pos)
         b.kcache[0, :, :pos] = torch.randn((kvh, pos, d), generator=g, device="cuda:0").to(torch.bfloat16)
         b.vcache[0, :, :pos] = torch.randn((kvh, pos, d), generator=g, device="cuda:0").to(torch.bfloat16)
-    plan.set_state(123, pos)
+    plan.set_state(123, pos, stream)
     L = w.layers[0]
     Lnp = _layer_np(L)
     cos, sin = _b16(b.rope_cos), _b16(b.rope_sin)
@@ -144,6 +145,43 @@ def test_layer_ops_compose_like_oracle(tiny, pos):
     assert bridge.error_word(clear=True) == 0
 
 
+def norm_close(actual: np.ndarray, expected: np.ndarray, rel: float = 1e-2) -> None:
+    """Composed outputs (a whole layer or more): the random-init model turns a
+    1-ulp bf16 difference in 5% of a layer's inputs into multi-ulp
+    differences in ~25% of its outputs (measured on the oracle itself), so
+    the 1e-2 relative tolerance is applied norm-wise: ||gpu - ref|| <=
+    rel * ||ref||, and no element further than rel * max|ref| + 2e-3."""
+
+    a = actual.astype(np.float64)
+    e = expected.astype(np.float64)
+    rel_norm = np.linalg.norm(a - e) / max(np.linalg.norm(e), 1e-30)
+    assert rel_norm <= rel, f"norm-wise relative error {rel_norm:.3e}"
+    assert np.max(np.abs(a - e)) <= rel * np.max(np.abs(e)) + ATOL, f"max abs err {np.max(np.abs(a - e)):.3e}"
+
+
+def test_full_layer_norm_wise_against_oracle_layer(tiny):
+    """Whole decoder layers on the GPU (graph replay) against the oracle's
+    kc_layer_step_hf chain, config-2 shapes, norm-wise tolerance."""
+
+    cfg, bridge, w, plan, stream = tiny
+    plan.reset_cache()
+    plan.set_state(123, 0, stream)
+    plan.replay(stream)
+    stream.synchronize()
+    emb = _b16(w.embedding).reshape(cfg.vocab, cfg.hidden)
+    x = emb[123].copy()
+    cos, sin = _b16(plan.buffers.rope_cos), _b16(plan.buffers.rope_sin)
+    ocfg = dict(hidden=cfg.hidden, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                inter=cfg.intermediate, eps=cfg.eps)
+    for L in w.layers:
+        kc = np.zeros((cfg.kv_heads, plan.kv_bucket, cfg.head_dim), dtype=np.uint16)
+        vc = np.zeros_like(kc)
+        O.layer_step_hf(_layer_np(L), ocfg, x, kc, vc, plan.kv_bucket, 0, cos[0], sin[0])
+    norm_close(O.bf16_to_f32(_b16(plan.buffers.x)), O.bf16_to_f32(x))
+    _, logits_ref = O.lm_head_argmax(x, _b16(w.final_norm), emb, cfg.eps, want_logits=True)
+    norm_close(O.bf16_to_f32(_b16(plan.buffers.logits)), O.bf16_to_f32(logits_ref))
+
+
 def test_graph_replay_is_bit_identical_to_eager(tiny):
     import torch
 
@@ -151,7 +189,7 @@ def test_graph_replay_is_bit_identical_to_eager(tiny):
     outs = []
     for mode in ("eager", "graph"):
         plan.reset_cache()
-        plan.set_state(77, 3)
+        plan.set_state(77, 3, stream)
         if mode == "eager":
             with torch.cuda.stream(stream):
                 plan.record(int(stream.cuda_stream))
