@@ -20,6 +20,15 @@
 // (batch, kv head) to finish -- found with a self-resetting atomic ticket --
 // combines the partials, or a separate combine kernel does when the caller's
 // workspace has no room for tickets (the workspace_v3 ABI).
+//
+// Contexts up to 2048 tokens take the cluster kernel instead: the (at most 8)
+// chunk CTAs of one (batch, kv head) form a thread-block cluster, keep their
+// partial (max, sum, acc) in shared memory and combine them through
+// distributed shared memory after a cluster barrier -- no global partials,
+// no atomic ticket, no extra L2 round trips on the critical path.
+#include <atomic>
+#include <cstdlib>
+
 #include "kc_common.cuh"
 #include "kc_launch.h"
 
@@ -28,6 +37,7 @@ namespace kc {
 constexpr int kHeadDim = 128;
 constexpr int kGqaThreads = 256;
 constexpr int kGqaMaxChunk = 256;
+constexpr int kGqaMinChunk = 64;
 constexpr int kPartialStride = kHeadDim + 2;
 constexpr float kLog2e = 1.4426950408889634F;
 
@@ -63,7 +73,10 @@ __device__ __forceinline__ void load_vec4(const void* base, int64_t elem, float*
     }
 }
 
-// Combine the nsplit partials of the G heads of one (batch, kv head).
+// Combine the nsplit partials of the G heads of one (batch, kv head).  Lane
+// s of a warp owns split s (mod 32) for the max and the softmax weights; the
+// weights are then broadcast so every lane accumulates its 4 dims over all
+// splits with independent (batched) loads.
 template <int DT, int G>
 __device__ void gqa_combine_group(const GqaArgs& a, int b, int kvh) {
     const int lane = threadIdx.x & 31;
@@ -72,23 +85,35 @@ __device__ void gqa_combine_group(const GqaArgs& a, int b, int kvh) {
         const int qh = kvh * G + h;
         const float* base = a.partials + (static_cast<int64_t>(b) * a.q_heads + qh) * a.nsplit * kPartialStride;
         float m = -INFINITY;
-        for (int s = 0; s < a.nsplit; ++s) m = fmaxf(m, __ldcg(base + s * kPartialStride));
+        for (int s = lane; s < a.nsplit; s += 32) m = fmaxf(m, __ldcg(base + s * kPartialStride));
+        m = warp_max(m);
         float l = 0.0F;
         float acc[4] = {0.0F, 0.0F, 0.0F, 0.0F};
-        for (int s = 0; s < a.nsplit; ++s) {
-            const float* p = base + s * kPartialStride;
-            const float ms = __ldcg(p);
-            if (ms == -INFINITY) continue;
-            const float w = exp2f(ms - m);
-            l += w * __ldcg(p + 1);
-            // partials are 130 floats apart, so acc (offset 2) is only 8-byte aligned
-            const float2 v0 = __ldcg(reinterpret_cast<const float2*>(p + 2) + 2 * lane);
-            const float2 v1 = __ldcg(reinterpret_cast<const float2*>(p + 2) + 2 * lane + 1);
-            acc[0] += w * v0.x;
-            acc[1] += w * v0.y;
-            acc[2] += w * v1.x;
-            acc[3] += w * v1.y;
+        for (int s0 = 0; s0 < a.nsplit; s0 += 32) {
+            const int s = s0 + lane;
+            float w = 0.0F;
+            if (s < a.nsplit) {
+                const float ms = __ldcg(base + s * kPartialStride);
+                if (ms != -INFINITY) {
+                    w = exp2f(ms - m);
+                    l += w * __ldcg(base + s * kPartialStride + 1);
+                }
+            }
+            const int cnt = min(32, a.nsplit - s0);
+#pragma unroll 4
+            for (int i = 0; i < cnt; ++i) {
+                const float wi = __shfl_sync(0xffffffffu, w, i);
+                // partials are 130 floats apart, so acc (offset 2) is only 8-byte aligned
+                const float* p = base + (s0 + i) * kPartialStride + 2;
+                const float2 v0 = __ldcg(reinterpret_cast<const float2*>(p) + 2 * lane);
+                const float2 v1 = __ldcg(reinterpret_cast<const float2*>(p) + 2 * lane + 1);
+                acc[0] = fmaf(wi, v0.x, acc[0]);
+                acc[1] = fmaf(wi, v0.y, acc[1]);
+                acc[2] = fmaf(wi, v1.x, acc[2]);
+                acc[3] = fmaf(wi, v1.y, acc[3]);
+            }
         }
+        l = warp_sum(l);
         const float inv = l > 0.0F ? 1.0F / l : 0.0F;
         const int64_t o = (static_cast<int64_t>(b) * a.q_heads + qh) * kHeadDim + 4 * lane;
 #pragma unroll
@@ -96,6 +121,10 @@ __device__ void gqa_combine_group(const GqaArgs& a, int b, int kvh) {
     }
 }
 
+// One CTA per (batch, kv head, chunk).  Thread 0 stages the chunk's K rows
+// and V rows (token-contiguous, so each is ONE bulk copy of n * 256 bytes)
+// into shared memory on two mbarriers; scores start as soon as K lands while
+// V is still in flight.  Dynamic shared memory: 2 * chunk * 256 bytes.
 template <int DT, int G>
 __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a) {
     constexpr int LPH = 32 / G;          // lanes per head in the score phase
@@ -103,13 +132,21 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a)
     __shared__ __align__(16) float s_s[G][kGqaMaxChunk];
     __shared__ float ml_s[G][2];
     __shared__ int last_s;
-
-    pdl_launch_dependents();
-    pdl_wait_on_producer();
+    __shared__ __align__(8) uint64_t kv_bar[2];
+    extern __shared__ __align__(16) uint8_t kv_rows[];
 
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
+    if (tid == 0) {
+        mbar_init(&kv_bar[0], 1);
+        mbar_init(&kv_bar[1], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+    pdl_wait_on_producer();
+
     const int b = blockIdx.x / a.kv_heads;
     const int kvh = blockIdx.x - b * a.kv_heads;
     const int split = blockIdx.y;
@@ -124,6 +161,24 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a)
     n = n < 0 ? 0 : (n > a.chunk ? a.chunk : n);
 
     const int64_t kv_base = (static_cast<int64_t>(b) * a.kv_heads + kvh) * a.stride * kHeadDim;
+    const uint16_t* ks = reinterpret_cast<const uint16_t*>(kv_rows);
+    const uint16_t* vs = ks + static_cast<int64_t>(a.chunk) * kHeadDim;
+    if (tid == 0 && n > 0) {
+        const uint32_t bytes = static_cast<uint32_t>(n) * kHeadDim * 2;
+        const int64_t row0 = kv_base + static_cast<int64_t>(t0) * kHeadDim;
+        mbar_arrive_expect_tx(&kv_bar[0], bytes);
+        bulk_g2s(const_cast<uint16_t*>(ks), static_cast<const uint16_t*>(a.kcache) + row0, bytes, &kv_bar[0]);
+        mbar_arrive_expect_tx(&kv_bar[1], bytes);
+        bulk_g2s(const_cast<uint16_t*>(vs), static_cast<const uint16_t*>(a.vcache) + row0, bytes, &kv_bar[1]);
+    }
+    // A wait that runs out records bit 16, waits once more (bounded) for the
+    // copy still in flight, and leaves the chunk empty.
+    auto wait_rows = [&](uint64_t* bar) {
+        if (n == 0 || mbar_wait_bounded(bar, 0)) return;
+        if (a.err != nullptr) atomicOr(a.err, 16);
+        mbar_wait_bounded(bar, 0);
+        n = 0;
+    };
 
     // ---- scores: lane (h, part) owns DPL dims of query head h ----
     {
@@ -141,20 +196,21 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a)
         }
 #pragma unroll
         for (int i = 0; i < DPL; ++i) qv[i] *= qscale;
+        wait_rows(&kv_bar[0]);
         for (int j = warp; j < n; j += kGqaThreads / 32) {
-            const int64_t koff = kv_base + static_cast<int64_t>(t0 + j) * kHeadDim + part * DPL;
+            const int64_t koff = static_cast<int64_t>(j) * kHeadDim + part * DPL;
             float dot = 0.0F;
             if constexpr (DPL >= 8) {
 #pragma unroll
                 for (int i = 0; i < DPL; i += 8) {
                     float kv[8];
-                    load_vec8<DT>(a.kcache, koff + i, kv);
+                    load_vec8<DT>(ks, koff + i, kv);
 #pragma unroll
                     for (int e = 0; e < 8; ++e) dot = fmaf(qv[i + e], kv[e], dot);
                 }
             } else {
                 float kv[4];
-                load_vec4<DT>(a.kcache, koff, kv);
+                load_vec4<DT>(ks, koff, kv);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) dot = fmaf(qv[e], kv[e], dot);
             }
@@ -182,14 +238,16 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a)
             ml_s[h][1] = l;
         }
     }
+    wait_rows(&kv_bar[1]);
     __syncthreads();
 
     // ---- P.V: warp h accumulates head h, lane owns dims 4*lane..4*lane+3 ----
     for (int h = warp; h < G; h += kGqaThreads / 32) {
         float acc[4] = {0.0F, 0.0F, 0.0F, 0.0F};
+#pragma unroll 4
         for (int j = 0; j < n; ++j) {
             float v[4];
-            load_vec4<DT>(a.vcache, kv_base + static_cast<int64_t>(t0 + j) * kHeadDim + 4 * lane, v);
+            load_vec4<DT>(vs, static_cast<int64_t>(j) * kHeadDim + 4 * lane, v);
             const float p = s_s[h][j];
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[i] = fmaf(p, v[i], acc[i]);
@@ -222,6 +280,311 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a)
     gqa_combine_group<DT, G>(a, b, kvh);
 }
 
+// ---------------------------------------------------------------------------
+// Cluster kernel: grid (batch * kv_heads, S), cluster (1, S, 1), S <= 8.
+//
+//   * every thread j < n issues the bulk copy of K row j and V row j into
+//     shared rows of 272 bytes (256 + 16 padding), so the mma fragment loads
+//     below hit 32 distinct banks;
+//   * scores = q . K^T on the tensor core (mma.m16n8k16, heads in rows 0..G-1,
+//     8 tokens per n-tile, fp32 accumulate, exact bf16/f16 products);
+//   * P.V on the tensor core with P split into hi + lo halves of the input
+//     type (P = hi + lo to ~16 significant bits), so the product keeps fp32
+//     level accuracy while V stays in its storage type; V fragments come from
+//     ldmatrix.trans of the padded rows;
+//   * each CTA writes (max, sum, acc) into the cluster leader's (rank 0)
+//     shared memory and arrives on the leader's mbarrier; the leader combines
+//     and stores.  Only the leader's shared memory is read remotely, and it
+//     leaves last.
+constexpr int kGqaClusterThreads = 512;
+constexpr int kGqaClusterWarps = kGqaClusterThreads / 32;
+constexpr int kGqaMaxCluster = 8;
+constexpr int kRowPad = kHeadDim * 2 + 16;  // padded shared row: 272 bytes
+
+template <int DT>
+__device__ __forceinline__ void mma_16816_dt(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                             uint32_t b1) {
+    if constexpr (DT == kBF16) {
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+            "{%0, %1, %2, %3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    } else {
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+            "{%0, %1, %2, %3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    }
+}
+// two fp32 -> packed pair of the storage type (round to nearest even)
+template <int DT>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    if constexpr (DT == kBF16)
+        return static_cast<uint32_t>(f32_to_bf16_bits(lo)) | (static_cast<uint32_t>(f32_to_bf16_bits(hi)) << 16);
+    else
+        return static_cast<uint32_t>(f32_to_f16_bits(lo)) | (static_cast<uint32_t>(f32_to_f16_bits(hi)) << 16);
+}
+template <int DT>
+__device__ __forceinline__ float round_dt(float v) {
+    if constexpr (DT == kBF16) return round_bf16(v);
+    else return f16_bits_to_f32(f32_to_f16_bits(v));
+}
+// P pair (p0, p1) -> hi pair and lo pair (p = hi + lo)
+template <int DT>
+__device__ __forceinline__ void split_pair(float p0, float p1, uint32_t& hi, uint32_t& lo) {
+    const float h0 = round_dt<DT>(p0), h1 = round_dt<DT>(p1);
+    hi = pack2<DT>(h0, h1);
+    lo = pack2<DT>(p0 - h0, p1 - h1);
+}
+__device__ __forceinline__ void ldmatrix_x2_trans(uint32_t& r0, uint32_t& r1, uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+template <int DT, int G>
+__global__ void __launch_bounds__(kGqaClusterThreads) gqa_cluster_kernel(const GqaArgs a) {
+    __shared__ __align__(16) float s_s[2][8][kGqaMaxChunk];  // score halves (dims 0-63, 64-127); then P in [0]
+    __shared__ __align__(8) float gat_ml[kGqaMaxCluster][G][2];  // leader: gathered (max, sum)
+    __shared__ float ml_s[G][2];
+    __shared__ __align__(8) uint64_t gat_bar;  // leader: one arrival per CTA of the cluster
+    extern __shared__ __align__(16) uint8_t kv_rows[];
+
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int S = a.nsplit;
+    const int split = blockIdx.y;  // == rank in the cluster
+    if (tid == 0) {
+        mbar_init(&gat_bar, S);
+        fence_mbar_init();
+    }
+    // announce this CTA (its barrier is initialised) to the cluster; the
+    // matching wait comes right before the first remote access
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    pdl_launch_dependents();
+    pdl_wait_on_producer();
+
+    const int b = blockIdx.x / a.kv_heads;
+    const int kvh = blockIdx.x - b * a.kv_heads;
+    const int t0 = split * a.chunk;
+    const int64_t kv_base = (static_cast<int64_t>(b) * a.kv_heads + kvh) * a.stride * kHeadDim;
+    uint8_t* ks = kv_rows;
+    uint8_t* vs = kv_rows + static_cast<size_t>(a.chunk) * kRowPad;
+    // leader: gathered partial accumulators [rank][head][dim], after the rows
+    // (same offset in every CTA of the launch, so mapa finds the leader's copy)
+    float* gat_acc = reinterpret_cast<float*>(kv_rows + 2 * static_cast<size_t>(a.chunk) * kRowPad);
+    // rows this CTA may read: the chunk, clipped to the cache's row extent
+    const int avail = min(a.chunk, max(0, a.stride - t0));
+
+    // ---- one global round trip: q fragments, the device length, and every
+    // K/V row of the chunk (16-byte loads, 16 per row, into padded rows)
+    uint32_t qa[8][2];
+    {
+        const uint32_t* qw = static_cast<const uint32_t*>(a.q) +
+                             ((static_cast<int64_t>(b) * a.q_heads + kvh * G + (g < G ? g : 0)) * kHeadDim) / 2;
+#pragma unroll
+        for (int s8 = 0; s8 < 8; ++s8) {
+            qa[s8][0] = g < G ? qw[8 * s8 + t] : 0u;
+            qa[s8][1] = g < G ? qw[8 * s8 + t + 4] : 0u;
+        }
+    }
+    int kv_len = a.kv_len_dev != nullptr ? *a.kv_len_dev : a.kv_len;
+    {
+        const uint4* kg = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.kcache) + kv_base +
+                                                         static_cast<int64_t>(t0) * kHeadDim);
+        const uint4* vg = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.vcache) + kv_base +
+                                                         static_cast<int64_t>(t0) * kHeadDim);
+        const int nvec = avail * (kHeadDim * 2 / 16);  // 16-byte pieces per cache
+        for (int base = tid; base < nvec; base += 4 * kGqaClusterThreads) {
+            uint4 kr[4], vr[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = base + u * kGqaClusterThreads;
+                if (i < nvec) {
+                    kr[u] = kg[i];
+                    vr[u] = vg[i];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = base + u * kGqaClusterThreads;
+                if (i < nvec) {
+                    const int row = i >> 4, piece = i & 15;
+                    *reinterpret_cast<uint4*>(ks + row * kRowPad + 16 * piece) = kr[u];
+                    *reinterpret_cast<uint4*>(vs + row * kRowPad + 16 * piece) = vr[u];
+                }
+            }
+        }
+    }
+    if (kv_len < 1 || kv_len > a.stride) {
+        if (a.err != nullptr && tid == 0) atomicOr(a.err, 4);
+        kv_len = kv_len < 1 ? 0 : a.stride;
+    }
+    int n = kv_len - t0;
+    n = n < 0 ? 0 : (n > a.chunk ? a.chunk : n);
+    const int n16 = (n + 15) & ~15;
+    // V rows n..n16-1 take part in the last P.V k-step with P = 0: make them
+    // finite (they hold stale cache rows or nothing at all); the barrier orders
+    // the row stores above before these
+    __syncthreads();
+    for (int i = tid; i < (n16 - n) * 16; i += kGqaClusterThreads)
+        *reinterpret_cast<uint4*>(vs + (n + (i >> 4)) * kRowPad + 16 * (i & 15)) = make_uint4(0u, 0u, 0u, 0u);
+    __syncthreads();
+
+    // ---- scores: unit (n-tile of 8 tokens, dim half) per warp; four mma
+    // k-steps on two independent accumulators
+    const float qscale = a.scale * kLog2e;
+    for (int unit = warp; unit < (n16 >> 3) * 2; unit += kGqaClusterWarps) {
+        const int nt = unit >> 1, half = unit & 1;
+        float c0[4] = {0.0F, 0.0F, 0.0F, 0.0F}, c1[4] = {0.0F, 0.0F, 0.0F, 0.0F};
+        const uint8_t* krow = ks + (nt * 8 + g) * kRowPad + 4 * t + 128 * half;
+#pragma unroll
+        for (int s4 = 0; s4 < 4; s4 += 2) {
+            // q fragments of k-steps 4*half + s4 and + 1 (selects keep qa in registers)
+            const uint32_t qA0 = half ? qa[4 + s4][0] : qa[s4][0], qA1 = half ? qa[4 + s4][1] : qa[s4][1];
+            const uint32_t qB0 = half ? qa[5 + s4][0] : qa[s4 + 1][0], qB1 = half ? qa[5 + s4][1] : qa[s4 + 1][1];
+            mma_16816_dt<DT>(c0, qA0, 0u, qA1, 0u, *reinterpret_cast<const uint32_t*>(krow + 32 * s4),
+                             *reinterpret_cast<const uint32_t*>(krow + 32 * s4 + 16));
+            mma_16816_dt<DT>(c1, qB0, 0u, qB1, 0u, *reinterpret_cast<const uint32_t*>(krow + 32 * s4 + 32),
+                             *reinterpret_cast<const uint32_t*>(krow + 32 * s4 + 48));
+        }
+        if (g < G) {
+            *reinterpret_cast<float2*>(&s_s[half][g][nt * 8 + 2 * t]) =
+                make_float2((c0[0] + c1[0]) * qscale, (c0[1] + c1[1]) * qscale);
+        }
+    }
+    __syncthreads();
+
+    // ---- per-head chunk softmax (log2 domain); probabilities zero past n
+    for (int h = warp; h < G; h += kGqaClusterWarps) {
+        float m = -INFINITY;
+        for (int j = lane; j < n; j += 32) m = fmaxf(m, s_s[0][h][j] + s_s[1][h][j]);
+        m = warp_max(m);
+        float l = 0.0F;
+        for (int j = lane; j < n16; j += 32) {
+            const float p = j < n ? exp2f(s_s[0][h][j] + s_s[1][h][j] - m) : 0.0F;
+            s_s[0][h][j] = p;
+            l += p;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            ml_s[h][0] = n > 0 ? m : -INFINITY;
+            ml_s[h][1] = l;
+        }
+    }
+    __syncthreads();
+
+    // ---- P.V: warp w owns dims 8w..8w+7; k-steps of 16 tokens alternate
+    // between two accumulators
+    float o0[4] = {0.0F, 0.0F, 0.0F, 0.0F}, o1[4] = {0.0F, 0.0F, 0.0F, 0.0F};
+    {
+        const uint32_t vbase = smem_u32(vs) + static_cast<uint32_t>((lane & 15) * kRowPad + 16 * warp);
+        const float* prow = &s_s[0][g < G ? g : 0][2 * t];
+        const int nk = n16 >> 4;
+        for (int kk = 0; kk < nk; kk += 2) {
+            // k-steps kk (accumulator 0) and kk + 1 (accumulator 1, if present)
+            const bool two = kk + 1 < nk;
+            uint32_t b0, b1, b2 = 0u, b3 = 0u;
+            ldmatrix_x2_trans(b0, b1, vbase + static_cast<uint32_t>(kk * 16 * kRowPad));
+            if (two) ldmatrix_x2_trans(b2, b3, vbase + static_cast<uint32_t>((kk + 1) * 16 * kRowPad));
+            float2 pa = make_float2(0.0F, 0.0F), pb = pa, pc = pa, pd = pa;
+            if (g < G) {
+                pa = *reinterpret_cast<const float2*>(prow + kk * 16);
+                pb = *reinterpret_cast<const float2*>(prow + kk * 16 + 8);
+                if (two) {
+                    pc = *reinterpret_cast<const float2*>(prow + kk * 16 + 16);
+                    pd = *reinterpret_cast<const float2*>(prow + kk * 16 + 24);
+                }
+            }
+            uint32_t ah0, al0, ah2, al2, ch0, cl0, ch2, cl2;
+            split_pair<DT>(pa.x, pa.y, ah0, al0);
+            split_pair<DT>(pb.x, pb.y, ah2, al2);
+            split_pair<DT>(pc.x, pc.y, ch0, cl0);
+            split_pair<DT>(pd.x, pd.y, ch2, cl2);
+            mma_16816_dt<DT>(o0, ah0, 0u, ah2, 0u, b0, b1);
+            if (two) mma_16816_dt<DT>(o1, ch0, 0u, ch2, 0u, b2, b3);
+            mma_16816_dt<DT>(o0, al0, 0u, al2, 0u, b0, b1);
+            if (two) mma_16816_dt<DT>(o1, cl0, 0u, cl2, 0u, b2, b3);
+        }
+    }
+
+    // ---- push (acc, max, sum) into the leader's gather slot [split]
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (g < G) {
+        const uint32_t dst = mapa_shared(smem_u32(gat_acc + (split * G + g) * kHeadDim + 8 * warp + 2 * t), 0);
+        asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(dst), "f"(o0[0] + o1[0]), "f"(o0[1] + o1[1])
+                     : "memory");
+    }
+    if (tid < G) {
+        const uint32_t dst = mapa_shared(smem_u32(&gat_ml[split][tid][0]), 0);
+        asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(dst), "f"(ml_s[tid][0]), "f"(ml_s[tid][1])
+                     : "memory");
+    }
+    __syncthreads();
+    if (tid == 0) mbar_arrive_remote(mapa_shared(smem_u32(&gat_bar), 0));
+    if (split != 0) return;  // only the leader's shared memory is read remotely
+
+    // ---- leader: combine the S partials (loops unrolled over the cluster bound)
+    bool ok = true;
+    {
+        uint32_t i = 0;
+        for (; i < kMbarPollLimit; ++i)
+            if (mbar_try_wait_cluster(&gat_bar, 0)) break;
+        ok = i < kMbarPollLimit;
+        if (!ok && tid == 0 && a.err != nullptr) atomicOr(a.err, 16);
+    }
+    if (!ok) return;
+    for (int u = tid; u < G * kHeadDim; u += kGqaClusterThreads) {
+        const int h = u / kHeadDim, d = u - h * kHeadDim;
+        float mr[kGqaMaxCluster], lr[kGqaMaxCluster], ar[kGqaMaxCluster];
+        float m = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kGqaMaxCluster; ++r) {
+            mr[r] = -INFINITY;
+            lr[r] = 0.0F;
+            ar[r] = 0.0F;
+            if (r < S) {
+                const float2 ml = *reinterpret_cast<const float2*>(&gat_ml[r][h][0]);
+                mr[r] = ml.x;
+                lr[r] = ml.y;
+                ar[r] = gat_acc[(r * G + h) * kHeadDim + d];
+            }
+            m = fmaxf(m, mr[r]);
+        }
+        float l = 0.0F, acc = 0.0F;
+#pragma unroll
+        for (int r = 0; r < kGqaMaxCluster; ++r) {
+            const float w = mr[r] == -INFINITY ? 0.0F : exp2f(mr[r] - m);
+            l = fmaf(w, lr[r], l);
+            acc = fmaf(w, ar[r], acc);
+        }
+        const float inv = l > 0.0F ? 1.0F / l : 0.0F;
+        store_elem<DT>(a.out, (static_cast<int64_t>(b) * a.q_heads + kvh * G + h) * kHeadDim + d, acc * inv);
+    }
+}
+
 template <int DT, int G>
 __global__ void __launch_bounds__(kGqaThreads) gqa_combine_kernel(const GqaArgs a) {
     pdl_launch_dependents();
@@ -236,7 +599,9 @@ void gqa_plan_splits(int kv_extent, int batch, int kv_heads, int max_splits, int
     const int target = (2 * device_sm_count() + ctas_per_split - 1) / ctas_per_split;
     int c = (kv_extent + target - 1) / (target > 0 ? target : 1);
     c = ((c + 15) / 16) * 16;
-    if (c < 16) c = 16;
+    // a chunk is one bulk copy per cache: below 64 tokens the fixed per-CTA
+    // latency dominates and the partials to combine grow
+    if (c < kGqaMinChunk) c = kGqaMinChunk;
     if (c > kGqaMaxChunk) c = kGqaMaxChunk;
     int s = (kv_extent + c - 1) / c;
     if (max_splits > 0 && s > max_splits) {
@@ -253,10 +618,76 @@ size_t gqa_partials_floats(int batch, int q_heads, int nsplit, int head_dim) {
 }
 
 namespace {
+// KUDACUDA_GQA_SPLIT_ONLY=1 keeps every call on the split kernel (measurement).
+bool cluster_gqa_enabled() {
+    static const bool on = std::getenv("KUDACUDA_GQA_SPLIT_ONLY") == nullptr;
+    return on;
+}
+
+// Cluster plan for extents up to 2048 tokens: S = min(8, ceil(extent / 64))
+// CTAs of chunk = ceil(extent / S) rounded up to 16 tokens (<= 256).
+bool gqa_cluster_plan(int extent, int* chunk, int* nsplit) {
+    if (extent < 1 || extent > kGqaMaxCluster * kGqaMaxChunk) return false;
+    int S = (extent + kGqaMinChunk - 1) / kGqaMinChunk;
+    if (S > kGqaMaxCluster) S = kGqaMaxCluster;
+    int c = (extent + S - 1) / S;
+    c = ((c + 15) / 16) * 16;
+    if (c > kGqaMaxChunk) return false;
+    *chunk = c;
+    *nsplit = (extent + c - 1) / c;
+    return true;
+}
+
+template <int DT, int G>
+cudaError_t gqa_cluster_launch(GqaArgs a, cudaStream_t s) {
+    auto kernel = gqa_cluster_kernel<DT, G>;
+    static std::atomic<bool> attr_set[64];
+    const int dev = current_device_index();
+    if (!attr_set[dev].load(std::memory_order_acquire)) {
+        const cudaError_t st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    2 * kGqaMaxChunk * kRowPad + kGqaMaxCluster * G * kHeadDim * 4);
+        if (st != cudaSuccess) return st;
+        attr_set[dev].store(true, std::memory_order_release);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.batch * a.kv_heads, a.nsplit);
+    cfg.blockDim = dim3(kGqaClusterThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(2) * a.chunk * kRowPad + kGqaMaxCluster * G * kHeadDim * 4;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = static_cast<unsigned>(a.nsplit);
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
 template <int DT, int G>
 cudaError_t gqa_launch(const GqaArgs& a, cudaStream_t s) {
+    // The fused-combine path (tickets given) may take the cluster kernel; the
+    // explicit workspace path (separate combine, the workspace_v3 contract)
+    // keeps its partials in the caller's workspace.
+    if (a.counters != nullptr && cluster_gqa_enabled()) {
+        GqaArgs c = a;
+        if (gqa_cluster_plan(a.kv_len_dev != nullptr ? a.stride : a.kv_len, &c.chunk, &c.nsplit))
+            return gqa_cluster_launch<DT, G>(c, s);
+    }
     const dim3 grid(a.batch * a.kv_heads, a.nsplit);
-    cudaError_t st = launch_pdl(gqa_split_kernel<DT, G>, grid, dim3(kGqaThreads), 0, s, a);
+    auto kernel = gqa_split_kernel<DT, G>;
+    static std::atomic<bool> attr_set[64];
+    const int dev = current_device_index();
+    if (!attr_set[dev].load(std::memory_order_acquire)) {
+        const cudaError_t st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    2 * kGqaMaxChunk * kHeadDim * 2);
+        if (st != cudaSuccess) return st;
+        attr_set[dev].store(true, std::memory_order_release);
+    }
+    const size_t smem = static_cast<size_t>(2) * a.chunk * kHeadDim * 2;
+    cudaError_t st = launch_pdl(kernel, grid, dim3(kGqaThreads), smem, s, a);
     if (st != cudaSuccess || a.counters != nullptr) return st;
     return launch_pdl(gqa_combine_kernel<DT, G>, dim3(a.batch * a.kv_heads), dim3(kGqaThreads), 0, s, a);
 }

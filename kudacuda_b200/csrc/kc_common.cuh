@@ -185,13 +185,16 @@ __device__ __forceinline__ float warp_max(float v) {
 // (e << 7) | (lane << 2) in a 32 KB table.
 constexpr int kLutWords = 256 * 32;
 
+// `lut` must be 16-byte aligned: each thread writes four replicas of an
+// entry with one 16-byte store.
 __device__ __forceinline__ void build_pair_lut(uint32_t* lut, int tid, int nthreads) {
-    for (int i = tid; i < kLutWords; i += nthreads) {
-        const int e = i >> 5;
+    for (int i = tid; i < kLutWords / 4; i += nthreads) {
+        const int e = i >> 3;  // 8 x 16 bytes per 128-byte entry
         const __half lo = __float2half_rn(kNf4Levels[e >> 4]);
         const __half hi = __float2half_rn(kNf4Levels[e & 15]);
-        lut[i] = static_cast<uint32_t>(__half_as_ushort(lo)) |
-                 (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+        const uint32_t w = static_cast<uint32_t>(__half_as_ushort(lo)) |
+                           (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+        reinterpret_cast<uint4*>(lut)[i] = make_uint4(w, w, w, w);
     }
 }
 

@@ -34,6 +34,10 @@ inline cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem,
 }
 
 int device_sm_count();
+// shared-memory capacities of the current device (cached per device)
+size_t device_smem_per_sm();
+size_t device_smem_per_block_optin();
+size_t device_smem_reserved_per_block();
 int current_device_index();
 
 // ---- NF4 GEMV family -------------------------------------------------------

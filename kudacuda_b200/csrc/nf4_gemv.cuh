@@ -67,6 +67,8 @@ struct Nf4GemvArgs {
     int kv_cap;
     int max_pos;
     int* err;  // optional error word; bit 0: f16 range, bit 1: position out of range
+    int xvec;    // x and norm_w are 16-byte aligned: stage them with 16-byte vector loads
+    int stages;  // TMA kernel: shared-memory ring depth chosen by the host
 };
 
 struct RowPair {

@@ -34,9 +34,11 @@ constexpr int kMmaWarps = 8;
 constexpr int kMmaThreads = kMmaWarps * 32;
 constexpr int kMmaGroup = 2;  // 64-element blocks per prefetch step
 
+// A pure function of its operands (no side effects), so the asm is not
+// volatile: the compiler may interleave independent accumulator chains.
 __device__ __forceinline__ void mma_f16_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                               uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
         "{%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -243,6 +245,123 @@ __device__ __forceinline__ void stage_x_plain(const Nf4GemvArgs& a, uint32_t* xp
     group_sync<GROUP>();
 }
 
+// Vector staging: the activation (and norm weight) vectors are read as
+// octets of 8 elements (one 16-byte load for f16/bf16, two for fp32), up to
+// kStageRound octets per thread issued back to back, so staging costs one
+// global round trip per pass for K <= kStageRound * 8 * threads instead of a
+// chain of dependent scalar loads.  Same arithmetic as stage_x_plain.
+constexpr int kStageRound = 4;
+
+template <int XT>
+struct Octet {
+    uint4 v[XT == kF32 ? 2 : 1];
+};
+template <int XT>
+__device__ __forceinline__ void ld_octet(const void* base, int o, Octet<XT>& r) {
+    const uint4* p = static_cast<const uint4*>(base) + (XT == kF32 ? 2 : 1) * o;
+    r.v[0] = p[0];
+    if constexpr (XT == kF32) r.v[1] = p[1];
+}
+template <int XT>
+__device__ __forceinline__ float octet_at(const Octet<XT>& r, int i) {
+    if constexpr (XT == kF32) {
+        const uint4& w = r.v[i >> 2];
+        const uint32_t u = (i & 3) == 0 ? w.x : (i & 3) == 1 ? w.y : (i & 3) == 2 ? w.z : w.w;
+        return __uint_as_float(u);
+    } else {
+        const uint4& w = r.v[0];
+        const int q = i >> 1;
+        const uint32_t u = q == 0 ? w.x : q == 1 ? w.y : q == 2 ? w.z : w.w;
+        const uint16_t h = static_cast<uint16_t>((i & 1) ? (u >> 16) : (u & 0xffffu));
+        if constexpr (XT == kBF16) return bf16_bits_to_f32(h);
+        else return f16_bits_to_f32(h);
+    }
+}
+
+template <int IN, int XT, int GROUP = 0>
+__device__ __forceinline__ void stage_x_vec(const Nf4GemvArgs& a, uint32_t* xp, float* red) {
+    const int tid = threadIdx.x;
+    const int nthreads = GROUP == 0 ? static_cast<int>(blockDim.x) : GROUP;
+    const int noct = a.K >> 3;
+    float inv = 1.0F;
+    if constexpr (IN != kInRaw) {
+        float ss = 0.0F;
+        for (int base = tid; base < noct; base += kStageRound * nthreads) {
+            Octet<XT> r[kStageRound];
+#pragma unroll
+            for (int u = 0; u < kStageRound; ++u)
+                if (base + u * nthreads < noct) ld_octet<XT>(a.x, base + u * nthreads, r[u]);
+#pragma unroll
+            for (int u = 0; u < kStageRound; ++u) {
+                if (base + u * nthreads < noct) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float v = octet_at<XT>(r[u], i);
+                        ss += v * v;
+                    }
+                }
+            }
+        }
+        ss = warp_sum(ss);
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        group_sync<GROUP>();
+        if (tid < 32) {
+            float v = tid < (nthreads >> 5) ? red[tid] : 0.0F;
+            v = warp_sum(v);
+            if (tid == 0) red[0] = 1.0F / sqrtf(v / static_cast<float>(a.K) + a.eps);
+        }
+        group_sync<GROUP>();
+        inv = red[0];
+    }
+    bool overflow = false;
+    for (int base = tid; base < noct; base += kStageRound * nthreads) {
+        Octet<XT> r[kStageRound];
+        Octet<XT> nw[kStageRound];
+#pragma unroll
+        for (int u = 0; u < kStageRound; ++u) {
+            const int o = base + u * nthreads;
+            if (o < noct) {
+                ld_octet<XT>(a.x, o, r[u]);
+                if constexpr (IN != kInRaw) ld_octet<XT>(a.norm_w, o, nw[u]);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kStageRound; ++u) {
+            const int o = base + u * nthreads;
+            if (o >= noct) continue;
+            uint32_t w[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float v[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int i = 2 * q + h;
+                    float x = octet_at<XT>(r[u], i);
+                    if constexpr (IN == kInNormRef) {
+                        x = x * inv * octet_at<XT>(nw[u], i);
+                        if (a.norm_ws != nullptr && blockIdx.x == 0) a.norm_ws[8 * o + i] = x;
+                    } else if constexpr (IN == kInNormHF) {
+                        x = round_bf16(octet_at<XT>(nw[u], i) * round_bf16(x * inv));
+                    }
+                    overflow |= !(fabsf(x) <= 65504.0F);
+                    v[h] = x;
+                }
+                w[q] = static_cast<uint32_t>(f32_to_f16_bits(v[0])) |
+                       (static_cast<uint32_t>(f32_to_f16_bits(v[1])) << 16);
+            }
+            *reinterpret_cast<uint4*>(xp + 4 * o) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+    if (overflow && a.err != nullptr) atomicOr(a.err, 1);
+    group_sync<GROUP>();
+}
+
+template <int IN, int XT, int GROUP = 0>
+__device__ __forceinline__ void stage_x_pairs(const Nf4GemvArgs& a, uint32_t* xp, float* red) {
+    if (a.xvec) stage_x_vec<IN, XT, GROUP>(a, xp, red);
+    else stage_x_plain<IN, XT, GROUP>(a, xp, red);
+}
+
 struct MmaStepRegs {
     uint2 wA[kMmaGroup];
     uint2 wB[kMmaGroup];
@@ -336,7 +455,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) nf4_gemv_mma_kernel(const Nf4G
     if (tile < ntiles) mma_load_step(R0, tr, g, t, rb, ab, b_begin, b_end);
     pdl_launch_dependents();
     pdl_wait_on_producer();
-    stage_x_plain<IN, XT>(a, xp, red);  // ends with __syncthreads (also covers the table)
+    stage_x_pairs<IN, XT>(a, xp, red);  // ends with __syncthreads (also covers the table)
 
     int step = 0;  // step index within the current tile
     while (tile < ntiles) {
@@ -399,31 +518,36 @@ namespace kc {
 // ---------------------------------------------------------------------------
 // Warp-specialised TMA variant (the production path when K % 256 == 0).
 //
-// One producer warp streams each 16-row tile through a 10-stage shared-memory
-// ring with 2D bulk-tensor loads: per stage, a 512-element K slice of both
-// 8-row groups (4 boxes of 8 rows x 128 B with 128-byte swizzle) and their
-// absmax (2 boxes of 8 rows x 8 fp32), completing on the stage's "full"
-// mbarrier.  Eight consumer warps each take one 64-element block of the
-// slice (the K split), read their A fragments conflict-free thanks to the
-// swizzle, run the table->mma math, and release the stage on its "empty"
-// mbarrier.  ~50 KB of weights are in flight per CTA with no register cost;
-// the producer starts streaming before griddepcontrol.wait because weights
-// are static.  No multicast is used anywhere.
+// One producer warp streams each 16-row tile through a shared-memory ring of
+// `a.stages` stages with 2D bulk-tensor loads: per stage, a 1024-element K
+// slice of both 8-row groups (8 boxes of 8 rows x 128 B with 128-byte
+// swizzle) and their absmax (2 boxes of 8 rows x 16 fp32), completing on the
+// stage's "full" mbarrier.  Eight consumer warps each take two consecutive
+// 64-element blocks of the slice (the K split), read their A fragments
+// conflict-free thanks to the swizzle, run the table->mma math, and release
+// the stage on its "empty" mbarrier.  At the end of a tile the warps' column
+// sums meet in shared memory (double-buffered by tile parity, one barrier per
+// tile) and warp 0 adds them in warp order (bit-reproducible) and applies the
+// epilogue.  The host sizes the ring from the shared-memory budget (up to 16
+// stages = 144 KB in flight per CTA); the producer starts streaming before
+// griddepcontrol.wait because weights are static.  No multicast is used
+// anywhere.
 
 struct GemvMaps {
     CUtensorMap w[3];  // packed nibbles, [rows][K/2] uint8, box 8 x 128 B, 128B swizzle
-    CUtensorMap s[3];  // absmax, [rows][K/64] fp32, box 8 x 8
+    CUtensorMap s[3];  // absmax, [rows][K/64] fp32, box 8 x 16
 };
 
 constexpr int kTmaCons = 8;
 constexpr int kTmaThreads = (kTmaCons + 1) * 32;
-constexpr int kTmaStages = 10;
-constexpr int kSlice = 512;               // K elements per stage
-constexpr int kBoxBytes = 1024;           // 8 rows x 128 B
-constexpr int kAbsBoxBytes = 256;         // 8 rows x 8 fp32
-constexpr int kTStageBytes = 5 * 1024;    // 4 packed boxes + 2 absmax boxes, padded to keep boxes 1 KB aligned
-constexpr size_t kTRingBytes = static_cast<size_t>(kTmaStages) * kTStageBytes;
-constexpr uint32_t kTStageTx = 4 * kBoxBytes + 2 * kAbsBoxBytes;
+constexpr int kSlice = 1024;                              // K elements per stage
+constexpr int kSliceBlocks = kSlice / kBlocksize;         // 16: two per consumer warp
+constexpr int kBoxBytes = 1024;                           // 8 rows x 128 B = 4 blocks of a row group
+constexpr int kAbsBoxBytes = 8 * kSliceBlocks * 4;        // 8 rows x 16 fp32
+constexpr int kTStageBytes = 8 * kBoxBytes + 2 * kAbsBoxBytes;  // 9 KB: every stage stays 1 KB aligned
+constexpr uint32_t kTStageTx = kTStageBytes;
+constexpr int kTMaxStages = 16;
+constexpr int kTMinStages = 2;
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -435,18 +559,43 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// Table offset of byte 0 with one bit-field insert.
+__device__ __forceinline__ uint32_t lut_off_b0_bfi(uint32_t w, uint32_t lane_off) {
+    uint32_t d;
+    asm("bfi.b32 %0, %1, %2, 7, 8;" : "=r"(d) : "r"(w), "r"(lane_off));
+    return d;
+}
+
+// One 64-element block of both row groups: four mma k-steps; returns the
+// batch-column sums (c0: row g, c2: row g + 8).
+__device__ __forceinline__ float2 tma_block_dot(const uint32_t* lut, uint32_t lane_off, uint2 wa, uint2 wb, uint4 x0,
+                                                uint4 x1) {
+    float c[4] = {0.0F, 0.0F, 0.0F, 0.0F};
+    mma_f16_16816(c, lut_at(lut, lut_off_b0_bfi(wa.x, lane_off)), lut_at(lut, lut_off_b0_bfi(wb.x, lane_off)),
+                  lut_at(lut, lut_off_b1(wa.x, lane_off)), lut_at(lut, lut_off_b1(wb.x, lane_off)), x0.x, x0.y);
+    mma_f16_16816(c, lut_at(lut, lut_off_b2(wa.x, lane_off)), lut_at(lut, lut_off_b2(wb.x, lane_off)),
+                  lut_at(lut, lut_off_b3(wa.x, lane_off)), lut_at(lut, lut_off_b3(wb.x, lane_off)), x0.z, x0.w);
+    mma_f16_16816(c, lut_at(lut, lut_off_b0_bfi(wa.y, lane_off)), lut_at(lut, lut_off_b0_bfi(wb.y, lane_off)),
+                  lut_at(lut, lut_off_b1(wa.y, lane_off)), lut_at(lut, lut_off_b1(wb.y, lane_off)), x1.x, x1.y);
+    mma_f16_16816(c, lut_at(lut, lut_off_b2(wa.y, lane_off)), lut_at(lut, lut_off_b2(wb.y, lane_off)),
+                  lut_at(lut, lut_off_b3(wa.y, lane_off)), lut_at(lut, lut_off_b3(wb.y, lane_off)), x1.z, x1.w);
+    return make_float2(c[0], c[2]);
+}
 
 template <int IN, int XT, int EPI, int OT>
 __global__ void __launch_bounds__(kTmaThreads, 2) nf4_gemv_tma_kernel(const Nf4GemvArgs a,
                                                                      const __grid_constant__ GemvMaps maps) {
     __shared__ __align__(16) uint32_t lut[kLutWords];
     __shared__ float red[32];
-    __shared__ __align__(16) float part[kTmaCons][32][4];
-    __shared__ __align__(8) uint64_t full_bar[kTmaStages];
-    __shared__ __align__(8) uint64_t empty_bar[kTmaStages];
+    // column-0 fragment sums (rows g, g + 8) per warp, double-buffered by
+    // tile parity so one consumer barrier per tile suffices
+    __shared__ __align__(8) float2 part[2][kTmaCons][8];
+    __shared__ __align__(8) uint64_t full_bar[kTMaxStages];
+    __shared__ __align__(8) uint64_t empty_bar[kTMaxStages];
     extern __shared__ __align__(16) uint8_t dyn_raw[];
+    const int nst = a.stages;
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~uintptr_t(1023));
-    uint32_t* xp = reinterpret_cast<uint32_t*>(ring + kTRingBytes);
+    uint32_t* xp = reinterpret_cast<uint32_t*>(ring + static_cast<size_t>(nst) * kTStageBytes);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nblk = a.K / kBlocksize;
@@ -454,7 +603,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2) nf4_gemv_tma_kernel(const Nf4G
     const int ntiles = mma_tiles<EPI>(a);
 
     if (tid == 0) {
-        for (int i = 0; i < kTmaStages; ++i) {
+        for (int i = 0; i < nst; ++i) {
             mbar_init(&full_bar[i], 1);
             mbar_init(&empty_bar[i], kTmaCons);
         }
@@ -479,14 +628,14 @@ __global__ void __launch_bounds__(kTmaThreads, 2) nf4_gemv_tma_kernel(const Nf4G
                     uint64_t* fb = &full_bar[slot];
                     mbar_arrive_expect_tx(fb, kTStageTx);
                     const int x0 = sl * (kSlice / 2);
-                    tma_load_2d(st, &maps.w[tr.mA], x0, tr.rA, fb);
-                    tma_load_2d(st + kBoxBytes, &maps.w[tr.mA], x0 + 128, tr.rA, fb);
-                    tma_load_2d(st + 2 * kBoxBytes, &maps.w[tr.mB], x0, tr.rB, fb);
-                    tma_load_2d(st + 3 * kBoxBytes, &maps.w[tr.mB], x0 + 128, tr.rB, fb);
-                    tma_load_2d(st + 4 * kBoxBytes, &maps.s[tr.mA], sl * (kSlice / kBlocksize), tr.rA, fb);
-                    tma_load_2d(st + 4 * kBoxBytes + kAbsBoxBytes, &maps.s[tr.mB], sl * (kSlice / kBlocksize), tr.rB,
-                                fb);
-                    if (++slot == kTmaStages) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        tma_load_2d(st + i * kBoxBytes, &maps.w[tr.mA], x0 + 128 * i, tr.rA, fb);
+                        tma_load_2d(st + (4 + i) * kBoxBytes, &maps.w[tr.mB], x0 + 128 * i, tr.rB, fb);
+                    }
+                    tma_load_2d(st + 8 * kBoxBytes, &maps.s[tr.mA], sl * kSliceBlocks, tr.rA, fb);
+                    tma_load_2d(st + 8 * kBoxBytes + kAbsBoxBytes, &maps.s[tr.mB], sl * kSliceBlocks, tr.rB, fb);
+                    if (++slot == nst) {
                         slot = 0;
                         phase ^= 1u;
                     }
@@ -501,72 +650,71 @@ __global__ void __launch_bounds__(kTmaThreads, 2) nf4_gemv_tma_kernel(const Nf4G
     const uint32_t lane_off = static_cast<uint32_t>(lane) << 2;
     build_pair_lut(lut, tid, kTmaCons * 32);
     pdl_wait_on_producer();
-    stage_x_plain<IN, XT, kTmaCons * 32>(a, xp, red);  // ends with the consumer barrier (covers the table)
+    stage_x_pairs<IN, XT, kTmaCons * 32>(a, xp, red);  // ends with the consumer barrier (covers the table)
 
-    // this warp's fragment offsets inside a stage (128-byte swizzle: 16-byte
-    // chunk c of box row r sits at chunk c ^ (r & 7))
-    const int box = warp >> 2;
-    const int chunk = 2 * (warp & 3) + (t >> 1);
-    const int frag_off = box * kBoxBytes + g * 128 + ((chunk ^ g) << 4) + 8 * (t & 1);
-    const int abs_off = 4 * kBoxBytes + g * 32 + warp * 4;
+    // Warp w takes blocks 2w and 2w+1 of each slice: both sit in 128-byte
+    // box column w >> 1, at 16-byte chunks c0 and c0 + 2 of their rows
+    // (128-byte swizzle: chunk c of box row r sits at chunk c ^ (r & 7)).
+    const int boxcol = (warp >> 1) * kBoxBytes;
+    const int c0 = 2 * ((2 * warp) & 3) + (t >> 1);
+    const int f0 = boxcol + g * 128 + ((c0 ^ g) << 4) + 8 * (t & 1);
+    const int f1 = boxcol + g * 128 + (((c0 + 2) ^ g) << 4) + 8 * (t & 1);
+    const int abs_off = 8 * kBoxBytes + g * (kSliceBlocks * 4) + 2 * warp * 4;
 
-    int slot = 0;
+    int slot = 0, buf = 0;
     uint32_t phase = 0;
     bool failed = false;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         const TileRows tr = decode_tile<EPI>(a, tile);
-        float tot[4] = {0.0F, 0.0F, 0.0F, 0.0F};
+        float totA = 0.0F, totB = 0.0F;
         for (int sl = 0; sl < nslices; ++sl) {
             if (!failed && !mbar_wait_bounded(&full_bar[slot], phase)) {
                 failed = true;
                 if (lane == 0 && a.err != nullptr) atomicOr(a.err, 16);
             }
-            const int blk = sl * (kSlice / kBlocksize) + warp;
+            // nblk is a multiple of 4 (K % 256 == 0), so block 2w+1 is valid whenever block 2w is
+            const int blk = sl * kSliceBlocks + 2 * warp;
             if (!failed && blk < nblk) {
                 const uint8_t* st = ring + slot * kTStageBytes;
-                const uint2 wa = *reinterpret_cast<const uint2*>(st + frag_off);
-                const uint2 wb = *reinterpret_cast<const uint2*>(st + 2 * kBoxBytes + frag_off);
-                const float sa = *reinterpret_cast<const float*>(st + abs_off);
-                const float sb = *reinterpret_cast<const float*>(st + abs_off + kAbsBoxBytes);
-                const uint4 x0 = *reinterpret_cast<const uint4*>(xp + 32 * blk + 8 * t);
-                const uint4 x1 = *reinterpret_cast<const uint4*>(xp + 32 * blk + 8 * t + 4);
-                float c[4] = {0.0F, 0.0F, 0.0F, 0.0F};
-                mma_f16_16816(c, lut_at(lut, lut_off_b0(wa.x, lane_off)), lut_at(lut, lut_off_b0(wb.x, lane_off)),
-                              lut_at(lut, lut_off_b1(wa.x, lane_off)), lut_at(lut, lut_off_b1(wb.x, lane_off)), x0.x,
-                              x0.y);
-                mma_f16_16816(c, lut_at(lut, lut_off_b2(wa.x, lane_off)), lut_at(lut, lut_off_b2(wb.x, lane_off)),
-                              lut_at(lut, lut_off_b3(wa.x, lane_off)), lut_at(lut, lut_off_b3(wb.x, lane_off)), x0.z,
-                              x0.w);
-                mma_f16_16816(c, lut_at(lut, lut_off_b0(wa.y, lane_off)), lut_at(lut, lut_off_b0(wb.y, lane_off)),
-                              lut_at(lut, lut_off_b1(wa.y, lane_off)), lut_at(lut, lut_off_b1(wb.y, lane_off)), x1.x,
-                              x1.y);
-                mma_f16_16816(c, lut_at(lut, lut_off_b2(wa.y, lane_off)), lut_at(lut, lut_off_b2(wb.y, lane_off)),
-                              lut_at(lut, lut_off_b3(wa.y, lane_off)), lut_at(lut, lut_off_b3(wb.y, lane_off)), x1.z,
-                              x1.w);
-                tot[0] = fmaf(c[0], sa, tot[0]);
-                tot[1] = fmaf(c[1], sa, tot[1]);
-                tot[2] = fmaf(c[2], sb, tot[2]);
-                tot[3] = fmaf(c[3], sb, tot[3]);
+                const uint2 wa0 = *reinterpret_cast<const uint2*>(st + f0);
+                const uint2 wb0 = *reinterpret_cast<const uint2*>(st + 4 * kBoxBytes + f0);
+                const uint2 wa1 = *reinterpret_cast<const uint2*>(st + f1);
+                const uint2 wb1 = *reinterpret_cast<const uint2*>(st + 4 * kBoxBytes + f1);
+                const float2 sa = *reinterpret_cast<const float2*>(st + abs_off);
+                const float2 sb = *reinterpret_cast<const float2*>(st + abs_off + kAbsBoxBytes);
+                const uint4* xb = reinterpret_cast<const uint4*>(xp + 32 * blk + 8 * t);
+                const uint4 x00 = xb[0], x01 = xb[1];
+                const uint4 x10 = xb[8], x11 = xb[9];  // next block: 32 words further
+                const float2 p0 = tma_block_dot(lut, lane_off, wa0, wb0, x00, x01);
+                const float2 p1 = tma_block_dot(lut, lane_off, wa1, wb1, x10, x11);
+                totA = fmaf(p0.x, sa.x, totA);
+                totB = fmaf(p0.y, sb.x, totB);
+                totA = fmaf(p1.x, sa.y, totA);
+                totB = fmaf(p1.y, sb.y, totB);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty_bar[slot]);
-            if (++slot == kTmaStages) {
+            if (++slot == nst) {
                 slot = 0;
                 phase ^= 1u;
             }
         }
-        *reinterpret_cast<float4*>(&part[warp][lane][0]) = make_float4(tot[0], tot[1], tot[2], tot[3]);
+        // batch column 0 of the C fragment lives in lanes t == 0
+        if (t == 0) part[buf][warp][g] = make_float2(totA, totB);
         group_sync<kTmaCons * 32>();
         if (warp == 0 && t == 0) {
             float vA = 0.0F, vB = 0.0F;
 #pragma unroll
             for (int w = 0; w < kTmaCons; ++w) {
-                vA += part[w][lane][0];
-                vB += part[w][lane][2];
+                const float2 pv = part[buf][w][g];
+                vA += pv.x;
+                vB += pv.y;
             }
             mma_epilogue<EPI, OT>(a, tr, g, vA, vB);
         }
-        group_sync<kTmaCons * 32>();
+        // the next tile writes the other buffer; warp 0 reaches that tile's
+        // barrier only after this epilogue, which protects this buffer
+        buf ^= 1;
     }
 }
 

@@ -35,6 +35,32 @@ int device_sm_count() {
 }
 
 namespace {
+int device_attr_cached(int (&cache)[64], cudaDeviceAttr attr, int fallback) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fallback;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, attr, dev) != cudaSuccess || n <= 0) n = fallback;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+}  // namespace
+
+size_t device_smem_per_sm() {
+    static int cached[64] = {0};
+    return static_cast<size_t>(device_attr_cached(cached, cudaDevAttrMaxSharedMemoryPerMultiprocessor, 228 * 1024));
+}
+size_t device_smem_per_block_optin() {
+    static int cached[64] = {0};
+    return static_cast<size_t>(device_attr_cached(cached, cudaDevAttrMaxSharedMemoryPerBlockOptin, 227 * 1024));
+}
+size_t device_smem_reserved_per_block() {
+    static int cached[64] = {0};
+    return static_cast<size_t>(device_attr_cached(cached, cudaDevAttrReservedSharedMemoryPerBlock, 1024));
+}
+
+namespace {
 
 inline Nf4Matrix to_mat(GemvMat g) { return Nf4Matrix{g.packed, g.absmax, g.rows}; }
 
@@ -49,6 +75,7 @@ cudaError_t run_gemv(Nf4GemvArgs& a, cudaStream_t s) {
     }
     a.ntasks = gemv_tasks(EPI, a);
     if (a.ntasks <= 0) return cudaSuccess;
+    a.xvec = aligned16(a.x) && (a.norm_w == nullptr || aligned16(a.norm_w)) ? 1 : 0;
     const int dev = current_device_index();
     // Tensor-core kernel (table lookups -> mma fragments) unless the
     // measurement override asks for the CUDA-core variant.
@@ -69,23 +96,46 @@ cudaError_t run_gemv(Nf4GemvArgs& a, cudaStream_t s) {
         if (encode_tmap_2d(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, a.m[i].packed, a.K / 2, rows, a.K / 2, 128, 8,
                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B) != cudaSuccess ||
             encode_tmap_2d(&maps.s[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.m[i].absmax, a.K / kBlocksize, rows,
-                           a.K / kBlocksize * 4, 8, 8, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           a.K / kBlocksize * 4, kSliceBlocks, 8, CU_TENSOR_MAP_SWIZZLE_NONE,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B) != cudaSuccess)
             tma_ok = false;
     }
     if (tma_ok) {
-        const size_t smem = 1024 + kTRingBytes + static_cast<size_t>(a.K) * 2;
-        if (smem > 160 * 1024) return cudaErrorInvalidValue;
         auto kernel = nf4_gemv_tma_kernel<IN, XT, EPI, OT>;
-        static std::atomic<bool> tma_attr[64];
-        if (!tma_attr[dev].load(std::memory_order_acquire)) {
-            const cudaError_t st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        // per device: the kernel's static shared memory and the SM's budget
+        static std::atomic<int> static_smem[64];
+        int fixed = static_smem[dev].load(std::memory_order_acquire);
+        if (fixed == 0) {
+            cudaFuncAttributes fa;
+            cudaError_t st = cudaFuncGetAttributes(&fa, kernel);
             if (st != cudaSuccess) return st;
-            tma_attr[dev].store(true, std::memory_order_release);
+            st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(device_smem_per_block_optin() - fa.sharedSizeBytes));
+            if (st != cudaSuccess) return st;
+            fixed = static_cast<int>(fa.sharedSizeBytes);
+            static_smem[dev].store(fixed, std::memory_order_release);
         }
+        // Two resident CTAs per SM when there are more tiles than SMs, else
+        // one CTA per SM with a deeper ring; the ring takes what is left
+        // after the table, barriers, 1 KB alignment slack and the activations.
         const int tiles = mma_tiles<EPI>(a);
-        int blocks = tiles < device_sm_count() * 2 ? tiles : device_sm_count() * 2;
-        return launch_pdl(kernel, dim3(blocks), dim3(kTmaThreads), smem, s, a, maps);
+        const int sms = device_sm_count();
+        const int per_sm = tiles > sms ? 2 : 1;
+        const size_t xbytes = static_cast<size_t>(a.K) * 2;
+        const size_t cta_budget = device_smem_per_sm() / per_sm - device_smem_reserved_per_block();
+        const size_t dyn_cap = device_smem_per_block_optin() - fixed;
+        size_t dyn_budget = cta_budget > static_cast<size_t>(fixed) ? cta_budget - fixed : 0;
+        if (dyn_budget > dyn_cap) dyn_budget = dyn_cap;
+        const size_t ring_budget = dyn_budget > 1024 + xbytes ? dyn_budget - 1024 - xbytes : 0;
+        int stages = static_cast<int>(ring_budget / kTStageBytes);
+        if (stages > kTMaxStages) stages = kTMaxStages;
+        if (stages >= kTMinStages) {
+            a.stages = stages;
+            const size_t smem = 1024 + static_cast<size_t>(stages) * kTStageBytes + xbytes;
+            const int blocks = tiles < sms * per_sm ? tiles : sms * per_sm;
+            return launch_pdl(kernel, dim3(blocks), dim3(kTmaThreads), smem, s, a, maps);
+        }
+        // activations too large for a ring next to them: register-prefetch kernel below
     }
     if (use_mma) {
         const size_t smem = static_cast<size_t>(a.K) * 2;

@@ -21,7 +21,7 @@ namespace kc {
 namespace {
 
 // scratch sizing for the reference-ABI GQA entries: batch 1, 16 query heads,
-// up to 2048 tokens in chunks of >= 16 -> at most 128 splits.
+// at most 128 splits (chunks of 64..256 tokens cover up to 32768 tokens).
 constexpr int kRefGqaMaxSplits = 128;
 constexpr int kRefGqaHeads = 16;
 
