@@ -238,8 +238,9 @@ KUDACUDA_API int kudacuda_sm100_graph_step_host(void* handle, const void* host_i
 
 /* Device-side error word written by the kernels (bit 0: activation outside
  * the f16 range, 1: position outside the cache, 2: kv length outside the
- * cache, 3: token id outside the vocabulary).  Reading synchronises the
- * handle's device; clear != 0 resets it. */
+ * cache, 3: token id outside the vocabulary, 4: a bounded wait on a barrier
+ * or an async copy ran out).  Reading synchronises the handle's device;
+ * clear != 0 resets it. */
 KUDACUDA_API int kudacuda_sm100_error_word(void* handle, int* out_word, int clear);
 
 /* Library / build identification: "sm_100a". */
