@@ -243,6 +243,24 @@ KUDACUDA_API int kudacuda_sm100_graph_step_host(void* handle, const void* host_i
  * clear != 0 resets it. */
 KUDACUDA_API int kudacuda_sm100_error_word(void* handle, int* out_word, int clear);
 
+/* Allocation-free GQA decode.  No reference counterpart: it exists for
+ * callers that cannot allocate device memory for a workspace (e.g. a host
+ * runtime without a device allocator at hand, or code that may not allocate
+ * after start-up).  Same arithmetic and arguments as kudacuda_sm100_gqa_decode
+ * minus the workspace and tickets: it always runs the split-KV kernel, whose
+ * partials and tickets live in a fixed 1 MiB file-scope device array
+ * (limit: batch * query_heads * splits * 130 floats <= 262144 and
+ * batch * kv_heads <= 1024; larger requests fail with a message).  The first
+ * call on each device looks the array up and zeroes its tickets, so it must
+ * come before any stream capture on that device.  Calls that overlap in time
+ * share the array and race: serialise them.  It allocates nothing and does
+ * not synchronise. */
+KUDACUDA_API int kudacuda_sm100_gqa_decode_static(void* handle, uint64_t query, uint64_t key_cache,
+                                                  uint64_t value_cache, uint64_t output, uint64_t kv_len_device,
+                                                  int dtype, int64_t batch_size, int64_t kv_len, int64_t kv_stride,
+                                                  int64_t query_heads, int64_t kv_heads, int64_t head_dim, float scale,
+                                                  uint64_t stream);
+
 /* Library / build identification: "sm_100a". */
 KUDACUDA_API const char* kudacuda_sm100_target_arch(void);
 

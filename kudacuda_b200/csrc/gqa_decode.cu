@@ -671,7 +671,7 @@ cudaError_t gqa_launch(const GqaArgs& a, cudaStream_t s) {
     // The fused-combine path (tickets given) may take the cluster kernel; the
     // explicit workspace path (separate combine, the workspace_v3 contract)
     // keeps its partials in the caller's workspace.
-    if (a.counters != nullptr && cluster_gqa_enabled()) {
+    if (a.counters != nullptr && !a.split_only && cluster_gqa_enabled()) {
         GqaArgs c = a;
         if (gqa_cluster_plan(a.kv_len_dev != nullptr ? a.stride : a.kv_len, &c.chunk, &c.nsplit))
             return gqa_cluster_launch<DT, G>(c, s);
@@ -702,6 +702,55 @@ cudaError_t gqa_dispatch_group(const GqaArgs& a, cudaStream_t s) {
     }
 }
 }  // namespace
+
+// ---------------------------------------------------------------------------
+// Allocation-free scratch for gqa_decode_static_scratch: split-KV partials
+// (at most kStaticGqaPartialFloats floats = 1 MiB, e.g. 16 query heads x 126
+// splits x 130 floats) followed by at most kStaticGqaTickets tickets.  A
+// file-scope __device__ array is zero-filled when the module loads; the
+// tickets must start at zero and self-reset after every call, and the first
+// call on each device zeroes them once more on the caller's stream.  Two calls
+// that overlap in time (different streams, or graphs replayed concurrently)
+// share this array and race; callers serialise them.
+constexpr size_t kStaticGqaPartialFloats = 262144;
+constexpr int kStaticGqaTickets = 1024;
+__device__ __align__(256) float g_static_gqa_scratch[kStaticGqaPartialFloats + kStaticGqaTickets];
+
+namespace {
+// Per-device address of the scratch, looked up once (cudaGetSymbolAddress
+// does not allocate; the first call on a device must come before any stream
+// capture on it).
+cudaError_t static_gqa_scratch(cudaStream_t s, float** partials, int** tickets) {
+    static std::atomic<float*> cached[64];
+    const int dev = current_device_index();
+    float* base = cached[dev].load(std::memory_order_acquire);
+    if (base == nullptr) {
+        void* p = nullptr;
+        cudaError_t st = cudaGetSymbolAddress(&p, g_static_gqa_scratch);
+        if (st != cudaSuccess) return st;
+        base = static_cast<float*>(p);
+        st = cudaMemsetAsync(base + kStaticGqaPartialFloats, 0, kStaticGqaTickets * sizeof(int), s);
+        if (st != cudaSuccess) return st;
+        cached[dev].store(base, std::memory_order_release);
+    }
+    *partials = base;
+    *tickets = reinterpret_cast<int*>(base + kStaticGqaPartialFloats);
+    return cudaSuccess;
+}
+}  // namespace
+
+cudaError_t gqa_decode_static_scratch(GqaArgs a, int dt, cudaStream_t s) {
+    if (a.batch <= 0 || a.kv_heads <= 0 || a.q_heads <= 0 || a.stride <= 0) return cudaErrorInvalidValue;
+    const int extent = a.kv_len_dev != nullptr ? a.stride : a.kv_len;
+    gqa_plan_splits(extent, a.batch, a.kv_heads, 0, &a.chunk, &a.nsplit);
+    if (gqa_partials_floats(a.batch, a.q_heads, a.nsplit, kHeadDim) > kStaticGqaPartialFloats ||
+        static_cast<int64_t>(a.batch) * a.kv_heads > kStaticGqaTickets)
+        return cudaErrorInvalidValue;
+    cudaError_t st = static_gqa_scratch(s, &a.partials, &a.counters);
+    if (st != cudaSuccess) return st;
+    a.split_only = 1;
+    return gqa_decode(a, dt, s);
+}
 
 cudaError_t gqa_decode(GqaArgs a, int dt, cudaStream_t s) {
     if (a.head_dim != kHeadDim || a.kv_heads <= 0 || a.q_heads % a.kv_heads != 0 || a.batch <= 0 ||

@@ -103,10 +103,16 @@ struct GqaArgs {
     float scale;
     int chunk, nsplit;
     int* err;
+    int split_only;  // 1: always the split-KV kernel with its global partials (never the cluster kernel)
 };
 // dt: 1 = f16, 2 = bf16.  Chooses split size from the capacity / length.
 void gqa_plan_splits(int kv_extent, int batch, int kv_heads, int max_splits, int* chunk, int* nsplit);
 cudaError_t gqa_decode(GqaArgs a, int dt, cudaStream_t s);
+// Allocation-free split-KV decode: partials and tickets live in a fixed
+// file-scope device array (see gqa_decode.cu); a.partials/a.counters are
+// ignored.  Plans its own splits; fails with cudaErrorInvalidValue when the
+// partials or tickets would not fit.
+cudaError_t gqa_decode_static_scratch(GqaArgs a, int dt, cudaStream_t s);
 size_t gqa_partials_floats(int batch, int q_heads, int nsplit, int head_dim);
 
 // ---- lm_head / embedding ------------------------------------------------------

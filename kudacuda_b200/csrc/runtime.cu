@@ -711,6 +711,49 @@ int kudacuda_sm100_gqa_decode(void* raw, uint64_t query, uint64_t key_cache, uin
     return finish(h, "gqa_split_kernel", kc::gqa_decode(a, dtype, S(stream)));
 }
 
+int kudacuda_sm100_gqa_decode_static(void* raw, uint64_t query, uint64_t key_cache, uint64_t value_cache,
+                                     uint64_t output, uint64_t kv_len_device, int dtype, int64_t batch_size,
+                                     int64_t kv_len, int64_t kv_stride, int64_t query_heads, int64_t kv_heads,
+                                     int64_t head_dim, float scale, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_gqa_decode_static")) return 1;
+    if (query == 0 || key_cache == 0 || value_cache == 0 || output == 0) {
+        h->set_error("sm100_gqa_decode_static requires non-null device pointers (kv_len_device may be null)");
+        return 1;
+    }
+    const int64_t group = kv_heads > 0 ? query_heads / kv_heads : 0;
+    if (batch_size < 1 || kv_heads < 1 || query_heads % kv_heads != 0 ||
+        !(group == 1 || group == 2 || group == 4 || group == 8) || head_dim != 128 || kv_stride < 1 ||
+        kv_stride > (1 << 20) || (kv_len_device == 0 && (kv_len < 1 || kv_len > kv_stride)) || !(scale > 0.0F) ||
+        (dtype != kc::kF16 && dtype != kc::kBF16)) {
+        h->set_error("sm100_gqa_decode_static requires head_dim=128, query_heads/kv_heads in {1,2,4,8}, "
+                     "1<=kv_len<=kv_stride, positive scale, dtype f16 or bf16");
+        return 1;
+    }
+    kc::GqaArgs a;
+    memset(&a, 0, sizeof(a));
+    a.q = P<const void>(query);
+    a.kcache = P<const void>(key_cache);
+    a.vcache = P<const void>(value_cache);
+    a.out = P<void>(output);
+    a.kv_len_dev = P<const int32_t>(kv_len_device);
+    a.kv_len = static_cast<int>(kv_len_device != 0 ? kv_stride : kv_len);
+    a.stride = static_cast<int>(kv_stride);
+    a.batch = static_cast<int>(batch_size);
+    a.q_heads = static_cast<int>(query_heads);
+    a.kv_heads = static_cast<int>(kv_heads);
+    a.head_dim = 128;
+    a.scale = scale;
+    a.err = h->err_word;
+    const cudaError_t st = kc::gqa_decode_static_scratch(a, dtype, S(stream));
+    if (st == cudaErrorInvalidValue) {
+        h->set_error("sm100_gqa_decode_static: partials or tickets exceed the fixed scratch (1 MiB of partials, "
+                     "1024 tickets); use kudacuda_sm100_gqa_decode with a caller workspace");
+        return 1;
+    }
+    return finish(h, "gqa_split_kernel (static scratch)", st);
+}
+
 int64_t kudacuda_sm100_lm_head_workspace_bytes(void) {
     return static_cast<int64_t>(kc::lm_head_grid()) * 2 * static_cast<int64_t>(sizeof(float));
 }

@@ -58,6 +58,9 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         [_p, _u64, _u64, _u64, _u64, _u64, _i64, _u64, _u64, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _u64],
     ),
     "kudacuda_sm100_gqa_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64, _i64]),
+    "kudacuda_sm100_gqa_decode_static": (
+        _i32, [_p, _u64, _u64, _u64, _u64, _u64, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _u64]
+    ),
     "kudacuda_sm100_lm_head_argmax_bf16": (
         _i32,
         [_p, _u64, _u64, _u64, _u64, _u64, _u64, _i64, _u64, _i64, _i64, _f32, _u64],
