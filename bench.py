@@ -139,12 +139,17 @@ def run_gpu(args) -> dict | None:
     torch.cuda.synchronize(device)
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    # cudaProfilerStart/Stop bracket the timed replays (no-ops unless a
+    # profiler runs with --profile-from-start off): the committed launch list
+    # covers exactly the timed decode steps
     with ClockSampler(local) as clocks:
+        torch.cuda.profiler.start()
         start.record(stream)
         for _ in range(args.steps):
             plan.replay(stream)
         end.record(stream)
         end.synchronize()
+        torch.cuda.profiler.stop()
     torch.cuda.synchronize(device)
     if dist is not None:
         dist.barrier()
@@ -295,8 +300,24 @@ def dominant_kernel_roofline(torch, bridge, plan, stream) -> dict:
         "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
         "bytes_per_launch": algo,
         "us_per_launch": round(us, 3),
-        "traffic": None,
+        "traffic": _profiled_traffic("nf4_gemv_tma_swiglu_11008x2048.md"),
+        "traffic_source": "profiles/nf4_gemv_tma_swiglu_11008x2048.md (ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch)",
     }
+
+
+def _profiled_traffic(name: str):
+    """DRAM bytes per launch recorded in a committed ncu summary (the line
+    `| traffic_bytes_per_launch | N |`), or None when absent."""
+
+    p = Path(__file__).resolve().parent / "profiles" / name
+    try:
+        for line in p.read_text().splitlines():
+            cells = [c.strip() for c in line.strip().strip("|").split("|")]
+            if len(cells) == 2 and cells[0] == "traffic_bytes_per_launch":
+                return int(cells[1])
+    except (OSError, ValueError):
+        return None
+    return None
 
 
 # ============================================================================ CPU (oracle port)
