@@ -37,6 +37,7 @@ import math
 from dataclasses import dataclass, field, replace
 from typing import Any, Optional
 
+from .kudacuda_graph_plan import DecodeGraphKey, KudaCudaGraphPlan
 from .kudacuda_sidecar import KudaCudaBridge, NativeCudaError
 
 
@@ -294,8 +295,42 @@ class StaticDecodePlan:
             rope_cos=cos,
             rope_sin=sin,
         )
-        self.captured = False
+        self.graph_plan = KudaCudaGraphPlan(bridge)
+        self.graph_key: Optional[DecodeGraphKey] = None
         self.launches_per_step = 0
+
+    @property
+    def captured(self) -> bool:
+        return self.graph_plan.captured
+
+    def make_graph_key(self) -> DecodeGraphKey:
+        """The static contract of the captured step: shapes, bucket and every
+        device pointer the graph bakes in (buffers, caches, weights)."""
+
+        b, w, c = self.buffers, self.weights, self.config
+        ptrs = [t.data_ptr() for t in (b.state, b.x, b.q, b.attn, b.h, b.kcache, b.vcache, b.gqa_ws, b.gqa_tickets,
+                                       b.lm_ws, b.lm_ticket, b.logits, b.next_token, b.history, b.rope_cos, b.rope_sin,
+                                       w.embedding, w.final_norm)]
+        for L in w.layers:
+            ptrs += [L.in_norm.data_ptr(), L.post_norm.data_ptr()]
+            for lin in (L.q, L.k, L.v, L.o, L.gate, L.up, L.down):
+                ptrs += [lin.packed.data_ptr(), lin.absmax.data_ptr()]
+            ptrs += [0 if t is None else t.data_ptr() for t in (L.q_bias, L.k_bias, L.v_bias)]
+        d = c.head_dim
+        return DecodeGraphKey(
+            device_id=int(self.torch.device(self.device).index or 0),
+            tactic_name="decode_step_sm100_v1",
+            layer_count=c.layers,
+            query_shape=(1, self.q_heads, 1, d),
+            key_shape=(1, self.kv_heads, self.kv_bucket, d),
+            value_shape=(1, self.kv_heads, self.kv_bucket, d),
+            output_shape=(1, self.q_heads, 1, d),
+            kv_bucket=self.kv_bucket,
+            pointers=tuple(int(p) for p in ptrs),
+            model_fingerprint=c.name,
+            dtype="bfloat16",
+            quantization="nf4-blocksize64-fp32absmax",
+        )
 
     # ------------------------------------------------------------------ one step
     def record(self, stream_ptr: int) -> int:
@@ -386,20 +421,35 @@ class StaticDecodePlan:
         self.buffers.history.copy_(saved_hist)
         torch.cuda.synchronize(self.device)
         self.bridge.reset_graph()
-        self.bridge.begin_capture(stream_ptr=sp)
+        self.graph_plan.invalidate()
+        key = self.make_graph_key()
+        self.graph_plan.begin_capture(key, stream_ptr=sp)
         try:
             self.record(sp)
         except Exception:
             try:
-                self.bridge.end_capture(stream_ptr=sp)
+                self.graph_plan.end_capture(key, stream_ptr=sp)
             finally:
+                self.graph_plan.invalidate()
                 self.bridge.reset_graph()
             raise
-        self.bridge.end_capture(stream_ptr=sp)
-        self.captured = True
+        self.graph_plan.end_capture(key, stream_ptr=sp)
+        self.graph_key = key
 
     def replay(self, stream: Any) -> None:
-        self.bridge.replay_graph(stream_ptr=int(stream.cuda_stream))
+        """Replay the captured step under its key (a different stream is a
+        GraphContractError); ``verify_key()`` re-derives the key when the
+        caller may have swapped tensors."""
+
+        if self.graph_key is None:
+            raise NativeCudaError("no captured decode graph")
+        self.graph_plan.replay(self.graph_key, stream_ptr=int(stream.cuda_stream))
+
+    def verify_key(self) -> None:
+        from .kudacuda_graph_plan import GraphContractError
+
+        if self.graph_key is None or self.make_graph_key() != self.graph_key:
+            raise GraphContractError("decode graph key changed since capture (tensors were replaced)")
 
     # ------------------------------------------------------------------ generation
     def prefill(self, prompt: list[int], stream: Any) -> int:
