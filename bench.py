@@ -15,6 +15,14 @@ rank decodes its own independent sequence (data-parallel replicas of batch-1
 decode, no collective): value = all ranks' tokens / max time (weak scaling).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+``--workload llama8b-tp`` instead runs BASELINE config 5: the Llama-3-8B
+architecture (32 layers, hidden 4096, 32/8 heads, intermediate 14336, vocab
+128256, untied NF4 lm_head) tensor-parallel over the N ranks -- column-
+parallel q/k/v and gate/up, row-parallel o_proj and down with an NCCL
+allreduce of fp32 partials after each, vocab-parallel lm_head with an
+allgather of (value, index) argmax pairs -- all inside the step's CUDA graph;
+one sequence, strong scaling (value = tokens/s of that sequence).
 """
 
 from __future__ import annotations
@@ -447,6 +455,122 @@ def run_reference(args) -> dict | None:
     }
 
 
+def run_tp(args) -> dict | None:
+    """Config 5: Llama-3-8B-architecture NF4 decode, tensor-parallel over the ranks."""
+
+    import datetime
+
+    import torch
+
+    from kudacuda_b200.decode_engine import LLAMA3_8B, StaticDecodePlan, random_weights
+    from kudacuda_b200.kudacuda_sidecar import KudaCudaBridge
+
+    rank, world, local = _dist_env()
+    torch.cuda.set_device(local)
+    device = f"cuda:{local}"
+    dist = None
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        group = dist.group.WORLD
+    cfg = LLAMA3_8B
+    if cfg.kv_heads % world or cfg.q_heads % world or cfg.intermediate % world or cfg.vocab % world:
+        raise SystemExit(f"Llama-3-8B does not shard over {world} ranks")
+    bridge = KudaCudaBridge(device_id=local)
+    weights = random_weights(bridge, cfg, seed=SEED, device=device, shard=(rank, world))
+    prompt_len = 128
+    bucket = 512
+    if prompt_len + args.warmup + args.steps + 2 > bucket:
+        raise SystemExit(f"prompt + warmup + steps must fit the KV bucket of {bucket}")
+    plan = StaticDecodePlan(bridge, weights, kv_bucket=bucket, max_tokens=bucket, device=device,
+                            allreduce=(rank, world, group))
+    stream = torch.cuda.Stream(device=device)
+    plan.capture(stream)
+    g = torch.Generator().manual_seed(SEED)
+    prompt = torch.randint(0, cfg.vocab, (prompt_len,), generator=g).tolist()  # same prompt on every rank
+    plan.reset_cache()
+    plan.prefill(prompt, stream)
+    for _ in range(args.warmup):
+        plan.replay(stream)
+    stream.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            plan.replay(stream)
+        end.record(stream)
+        end.synchronize()
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end)
+    if dist is not None:
+        dist.barrier()
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    err = bridge.error_word(clear=True)
+    # the ranks must agree on every generated token
+    hist = plan.buffers.history[prompt_len:prompt_len + args.warmup + args.steps].clone()
+    agree = True
+    if dist is not None:
+        other = hist.clone()
+        dist.broadcast(other, src=0)
+        agree = bool(torch.equal(other, hist))
+        flag = torch.tensor([1 if agree else 0], device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        agree = bool(flag.item())
+    plan.graph_plan.invalidate()  # release the graph (it holds NCCL work) before the process group
+    plan._torch_graph.reset() if plan._torch_graph is not None else None
+    out = None
+    if rank == 0:
+        wb = cfg.weight_bytes_per_token()
+        kv = cfg.kv_bytes_per_token(prompt_len + args.warmup + args.steps // 2)
+        bytes_token = sum(wb.values()) + kv
+        peak, peak_src = _peaks()
+        ms_step = ms / args.steps
+        value = args.steps / (ms / 1e3)
+        out = {
+            "metric": "batch-1 decode tok/s (tensor-parallel)",
+            "value": round(value, 2),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "nf4-weights/bf16-activations/f32-accumulate",
+            "data": "synthetic (random-init weights N(0,0.02) NF4-quantised on device; uniform-random prompt)",
+            "config": {
+                "workload": "config5: Llama-3-8B-architecture NF4 decode, batch 1, tensor-parallel, static CUDA graph",
+                "prompt_len": prompt_len,
+                "kv_bucket": bucket,
+                "parallelism": f"tp{world}",
+                "l2": "inputs larger than L2 (4.2 GB of weights per step / world)",
+            },
+            "hbm_roofline_per_token": {
+                "bytes_per_token_all_ranks": bytes_token,
+                "bytes_per_gpu": bytes_token // world,
+                "achieved_gbs_per_gpu": round(bytes_token / world / (ms_step * 1e-3) / 1e9, 1),
+                "frac_of_measured_peak": round(bytes_token / world / (ms_step * 1e-3) / 1e9 / peak, 4),
+                "peak_source": peak_src,
+            },
+            "ranks_agree_on_tokens": agree,
+            "device_error_word": err,
+            "clocks": clocks.summary(),
+        }
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
@@ -455,10 +579,16 @@ def main(argv=None) -> int:
     p.add_argument("--impl", choices=["kudacuda_b200", "reference"], default="kudacuda_b200")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", choices=["qwen3b", "llama8b-tp"], default="qwen3b")
     args = p.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
-    out = run_reference(args) if args.impl == "reference" else run_gpu(args)
+    if args.impl == "reference":
+        out = run_reference(args)
+    elif args.workload == "llama8b-tp":
+        out = run_tp(args)
+    else:
+        out = run_gpu(args)
     if out is not None:
         print(json.dumps(out), flush=True)
     return 0

@@ -243,6 +243,29 @@ KUDACUDA_API int kudacuda_sm100_graph_step_host(void* handle, const void* host_i
  * clear != 0 resets it. */
 KUDACUDA_API int kudacuda_sm100_error_word(void* handle, int* out_word, int clear);
 
+/* Tensor-parallel step ops (no reference counterpart; the reference runs one
+ * GPU).  rmsnorm_nf4_gemv: Transformers-order RMSNorm of bf16 input fused into
+ * an NF4 GEMV (output f32 or bf16), used for a vocab-parallel NF4 lm_head.
+ * residual_add_f32: residual = bf16(residual + bf16(partial_sum)) after the
+ * allreduce of a row-parallel GEMV's fp32 partials.  argmax_shard_f32: greedy
+ * argmax over this rank's slice of fp32 logits (compared after rounding to
+ * bf16, lowest index on ties), writing one {float value; int32 index} pair
+ * with index = index_base + local index; the ticket is an int32 that starts
+ * at zero and resets itself.  select_token: lowest-index maximum over count
+ * gathered pairs -> int32 next token. */
+KUDACUDA_API int kudacuda_sm100_rmsnorm_nf4_gemv(void* handle, uint64_t input, uint64_t norm_weight,
+                                                 uint64_t weight_packed, uint64_t absmax, uint64_t output,
+                                                 int output_dtype, int64_t rows, int64_t hidden, float epsilon,
+                                                 uint64_t stream);
+KUDACUDA_API int kudacuda_sm100_residual_add_f32(void* handle, uint64_t partial_sum, uint64_t residual, int64_t n,
+                                                 uint64_t stream);
+KUDACUDA_API int64_t kudacuda_sm100_argmax_workspace_bytes(void);
+KUDACUDA_API int kudacuda_sm100_argmax_shard_f32(void* handle, uint64_t logits, int64_t n, int64_t index_base,
+                                                 uint64_t workspace, int64_t workspace_bytes, uint64_t ticket,
+                                                 uint64_t out_pair, uint64_t stream);
+KUDACUDA_API int kudacuda_sm100_select_token(void* handle, uint64_t pairs, int64_t count, uint64_t next_token,
+                                             uint64_t stream);
+
 /* Allocation-free GQA decode.  No reference counterpart: it exists for
  * callers that cannot allocate device memory for a workspace (e.g. a host
  * runtime without a device allocator at hand, or code that may not allocate

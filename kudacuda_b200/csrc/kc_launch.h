@@ -115,6 +115,20 @@ cudaError_t gqa_decode(GqaArgs a, int dt, cudaStream_t s);
 cudaError_t gqa_decode_static_scratch(GqaArgs a, int dt, cudaStream_t s);
 size_t gqa_partials_floats(int batch, int q_heads, int nsplit, int head_dim);
 
+// ---- tensor-parallel step ops (tp_ops.cu) ---------------------------------------
+struct ArgPair {
+    float value;
+    int32_t index;
+};
+cudaError_t residual_add_f32_bf16(const float* partial, void* resid, int n, cudaStream_t s);
+cudaError_t argmax_shard_f32(const float* logits, int n, int index_base, float* ws, int* ticket, ArgPair* out,
+                             cudaStream_t s);
+int argmax_shard_workspace_floats();
+cudaError_t select_token(const ArgPair* pairs, int count, int32_t* next_token, cudaStream_t s);
+// RMSNorm (Transformers' bf16 rounding points) fused into an NF4 GEMV; out f32 or bf16
+cudaError_t nf4_rmsnorm_gemv_bf16(const void* x, const void* norm_w, float eps, GemvMat w, void* out, int ot, int K,
+                                  int* err, cudaStream_t s);
+
 // ---- lm_head / embedding ------------------------------------------------------
 struct LmHeadArgs {
     const void* hidden;      // bf16 [H] residual stream

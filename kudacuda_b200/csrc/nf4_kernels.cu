@@ -197,6 +197,21 @@ cudaError_t nf4_gemv(const void* x, int xt, GemvMat w, const void* bias, void* o
     return cudaErrorInvalidValue;
 }
 
+cudaError_t nf4_rmsnorm_gemv_bf16(const void* x, const void* norm_w, float eps, GemvMat w, void* out, int ot, int K,
+                                  int* err, cudaStream_t s) {
+    Nf4GemvArgs a = blank_args();
+    a.m[0] = to_mat(w);
+    a.K = K;
+    a.x = x;
+    a.norm_w = norm_w;
+    a.eps = eps;
+    a.out[0] = out;
+    a.err = err;
+    if (ot == kF32) return run_gemv<kInNormHF, kBF16, kEpiStore, kF32>(a, s);
+    if (ot == kBF16) return run_gemv<kInNormHF, kBF16, kEpiStore, kBF16>(a, s);
+    return cudaErrorInvalidValue;
+}
+
 cudaError_t nf4_gemv_residual_bf16(const void* x, GemvMat w, void* resid, int K, int* err,
                                    cudaStream_t s) {
     Nf4GemvArgs a = blank_args();

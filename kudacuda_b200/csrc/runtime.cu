@@ -754,6 +754,75 @@ int kudacuda_sm100_gqa_decode_static(void* raw, uint64_t query, uint64_t key_cac
     return finish(h, "gqa_split_kernel (static scratch)", st);
 }
 
+int kudacuda_sm100_rmsnorm_nf4_gemv(void* raw, uint64_t input, uint64_t norm_weight, uint64_t weight_packed,
+                                    uint64_t absmax, uint64_t output, int output_dtype, int64_t rows, int64_t hidden,
+                                    float epsilon, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_rmsnorm_nf4_gemv")) return 1;
+    if (input == 0 || norm_weight == 0 || weight_packed == 0 || absmax == 0 || output == 0) {
+        h->set_error("sm100_rmsnorm_nf4_gemv requires non-null device pointers");
+        return 1;
+    }
+    if (rows < 1 || rows > (1 << 30) || hidden < 64 || hidden % 64 != 0 || hidden > 32768 || !(epsilon > 0.0F) ||
+        (output_dtype != kc::kF32 && output_dtype != kc::kBF16)) {
+        h->set_error("sm100_rmsnorm_nf4_gemv requires positive rows, hidden a multiple of 64 (<= 32768), "
+                     "positive epsilon and an f32 or bf16 output");
+        return 1;
+    }
+    return finish(h, "nf4_gemv (rmsnorm input)",
+                  kc::nf4_rmsnorm_gemv_bf16(P<const void>(input), P<const void>(norm_weight), epsilon,
+                                            GemvMat{P<const uint8_t>(weight_packed), P<const float>(absmax),
+                                                    static_cast<int>(rows)},
+                                            P<void>(output), output_dtype, static_cast<int>(hidden), h->err_word,
+                                            S(stream)));
+}
+
+int kudacuda_sm100_residual_add_f32(void* raw, uint64_t partial_sum, uint64_t residual, int64_t n, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_residual_add_f32")) return 1;
+    if (partial_sum == 0 || residual == 0 || n < 1 || n > (1 << 30)) {
+        h->set_error("sm100_residual_add_f32 requires non-null pointers and a positive length");
+        return 1;
+    }
+    return finish(h, "residual_add_f32_kernel",
+                  kc::residual_add_f32_bf16(P<const float>(partial_sum), P<void>(residual), static_cast<int>(n),
+                                            S(stream)));
+}
+
+int64_t kudacuda_sm100_argmax_workspace_bytes(void) {
+    return static_cast<int64_t>(kc::argmax_shard_workspace_floats()) * static_cast<int64_t>(sizeof(float));
+}
+
+int kudacuda_sm100_argmax_shard_f32(void* raw, uint64_t logits, int64_t n, int64_t index_base, uint64_t workspace,
+                                    int64_t workspace_bytes, uint64_t ticket, uint64_t out_pair, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_argmax_shard_f32")) return 1;
+    if (logits == 0 || workspace == 0 || ticket == 0 || out_pair == 0 || n < 1 || n > (1 << 30) || index_base < 0 ||
+        index_base > (1 << 30)) {
+        h->set_error("sm100_argmax_shard_f32 requires non-null pointers, 1 <= n and a non-negative index base");
+        return 1;
+    }
+    if (workspace_bytes < kudacuda_sm100_argmax_workspace_bytes()) {
+        h->set_error("sm100_argmax_shard_f32 workspace is smaller than kudacuda_sm100_argmax_workspace_bytes()");
+        return 1;
+    }
+    return finish(h, "argmax_shard_kernel",
+                  kc::argmax_shard_f32(P<const float>(logits), static_cast<int>(n), static_cast<int>(index_base),
+                                       P<float>(workspace), P<int>(ticket), P<kc::ArgPair>(out_pair), S(stream)));
+}
+
+int kudacuda_sm100_select_token(void* raw, uint64_t pairs, int64_t count, uint64_t next_token, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_select_token")) return 1;
+    if (pairs == 0 || next_token == 0 || count < 1 || count > 4096) {
+        h->set_error("sm100_select_token requires non-null pointers and 1 <= count <= 4096");
+        return 1;
+    }
+    return finish(h, "select_token_kernel",
+                  kc::select_token(P<const kc::ArgPair>(pairs), static_cast<int>(count), P<int32_t>(next_token),
+                                   S(stream)));
+}
+
 int64_t kudacuda_sm100_lm_head_workspace_bytes(void) {
     return static_cast<int64_t>(kc::lm_head_grid()) * 2 * static_cast<int64_t>(sizeof(float));
 }

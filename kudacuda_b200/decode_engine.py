@@ -205,9 +205,10 @@ def random_weights(bridge: KudaCudaBridge, config: DecoderConfig, *, seed: int =
     embedding = _randn_bf16(torch, (c.vocab, c.hidden), 0.02, gen, device)
     final_norm = _randn_bf16(torch, (c.hidden,), 0.02, gen, device, 1.0)
     lm_head = None
-    if not c.tie_embeddings:
+    if not c.tie_embeddings:  # vocab-parallel: this rank's rows of the NF4 lm_head
         w_lm = _randn_bf16(torch, (c.vocab, c.hidden), 0.02, gen, device)
-        lm_head = quantize_nf4(bridge, torch, w_lm, stream_ptr)
+        v_loc = c.vocab // world
+        lm_head = quantize_nf4(bridge, torch, rows(w_lm, rank * v_loc, v_loc), stream_ptr)
         del w_lm
     torch.cuda.synchronize(device)
     return ModelWeights(c, layers, embedding, final_norm, lm_head)
@@ -221,6 +222,104 @@ def rope_tables(torch: Any, max_pos: int, head_dim: int, theta: float, device: A
     inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
     freqs = torch.outer(torch.arange(max_pos, dtype=torch.float32), inv_freq.float())
     return (freqs.cos().to(torch.bfloat16).contiguous().to(device), freqs.sin().to(torch.bfloat16).contiguous().to(device))
+
+
+class TensorParallel:
+    """Row-parallel reductions and the vocab-parallel NF4 lm_head of a
+    tensor-parallel decode step (Megatron-style sharding: column-parallel
+    q/k/v and gate/up, row-parallel o_proj and down).
+
+    * ``residual_linear``: the row-parallel GEMV writes this rank's fp32
+      partial, an allreduce(sum) adds the ranks' partials, and the residual
+      add applies the single-GPU epilogue's roundings:
+      ``x = bf16(x + bf16(sum))``.
+    * ``lm_head``: RMSNorm + NF4 GEMV over this rank's vocabulary rows (fp32
+      logits), local argmax on bf16-rounded logits, allgather of the
+      (value, index) pairs, lowest-index maximum -> next token.
+
+    ``group`` is a torch.distributed process group (NCCL for GPUs) or None
+    for one rank; collectives run on the decode stream so they are captured
+    in the step's CUDA graph.
+    """
+
+    def __init__(self, plan: "StaticDecodePlan", *, rank: int = 0, world: int = 1, group: Any = None) -> None:
+        torch = plan.torch
+        self.rank, self.world, self.group = int(rank), int(world), group
+        c, dev = plan.config, plan.device
+        self.partial = torch.zeros(c.hidden, dtype=torch.float32, device=dev)
+        lm = plan.weights.lm_head
+        self.v_loc = lm.rows if lm is not None else 0
+        self.logits = torch.zeros(max(self.v_loc, 1), dtype=torch.float32, device=dev)
+        br = plan.bridge
+        self.arg_ws = torch.zeros(br.argmax_workspace_bytes() // 4, dtype=torch.float32, device=dev)
+        self.arg_ticket = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.pair = torch.zeros(2, dtype=torch.int32, device=dev)  # {float value bits, int32 index}
+        self.gathered = torch.zeros(2 * self.world, dtype=torch.int32, device=dev)
+
+    def _allreduce(self, t: Any) -> None:
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(t, group=self.group)
+
+    def residual_linear(self, plan: "StaticDecodePlan", x: Any, lin: "NF4Linear", stream_ptr: int) -> int:
+        br = plan.bridge
+        if self.world == 1:
+            br.dispatch_nf4_linear_residual(x, lin.packed, lin.absmax, plan.buffers.x, rows=lin.rows, k=lin.k,
+                                            stream_ptr=stream_ptr)
+            return 1
+        br.dispatch_nf4_gemv(x, lin.packed, lin.absmax, self.partial, rows=lin.rows, k=lin.k, stream_ptr=stream_ptr)
+        self._allreduce(self.partial)
+        br.dispatch_residual_add_f32(self.partial, plan.buffers.x, stream_ptr=stream_ptr)
+        return 2
+
+    def lm_head(self, plan: "StaticDecodePlan", stream_ptr: int) -> int:
+        b, w, c, br = plan.buffers, plan.weights, plan.config, plan.bridge
+        br.dispatch_rmsnorm_nf4_gemv(b.x, w.final_norm, (w.lm_head.packed, w.lm_head.absmax), self.logits,
+                                     epsilon=c.eps, stream_ptr=stream_ptr)
+        br.dispatch_argmax_shard(self.logits, self.arg_ws, self.arg_ticket, self.pair,
+                                 index_base=self.rank * self.v_loc, stream_ptr=stream_ptr)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(self.gathered, self.pair, group=self.group)
+            br.dispatch_select_token(self.gathered, b.next_token, count=self.world, stream_ptr=stream_ptr)
+        else:
+            br.dispatch_select_token(self.pair, b.next_token, count=1, stream_ptr=stream_ptr)
+        return 3
+
+
+class _TorchGraphBridge:
+    """begin/end/replay on a torch.cuda.CUDAGraph (thread-local capture), for
+    steps that contain NCCL collectives issued through torch.distributed."""
+
+    def __init__(self, torch_module: Any) -> None:
+        self.torch = torch_module
+        self.graph = None
+        self._ctx = None
+
+    def begin_capture(self, *, stream_ptr: int) -> None:
+        torch = self.torch
+        self.graph = torch.cuda.CUDAGraph()
+        stream = torch.cuda.ExternalStream(int(stream_ptr))
+        self._ctx = torch.cuda.stream(stream)
+        self._ctx.__enter__()
+        self.graph.capture_begin(capture_error_mode="thread_local")
+
+    def end_capture(self, *, stream_ptr: int) -> None:
+        try:
+            self.graph.capture_end()
+        finally:
+            self._ctx.__exit__(None, None, None)
+            self._ctx = None
+
+    def replay_graph(self, *, stream_ptr: int) -> None:
+        torch = self.torch
+        with torch.cuda.stream(torch.cuda.ExternalStream(int(stream_ptr))):
+            self.graph.replay()
+
+    def reset(self) -> None:
+        self.graph = None
 
 
 @dataclass
@@ -261,7 +360,7 @@ class StaticDecodePlan:
         self.config = weights.config
         self.device = device
         self.kv_bucket = int(kv_bucket)
-        self.allreduce = allreduce  # callable(tensor, stream) for tensor-parallel partial sums
+        self.allreduce = allreduce  # (rank, world, process group) for tensor parallelism, or None
         self.keep_logits = keep_logits
         torch = self.torch
         c = self.config
@@ -298,6 +397,16 @@ class StaticDecodePlan:
         self.graph_plan = KudaCudaGraphPlan(bridge)
         self.graph_key: Optional[DecodeGraphKey] = None
         self.launches_per_step = 0
+        # tensor parallelism / untied NF4 lm_head: ``allreduce`` may be a
+        # (rank, world, group) tuple; steps with collectives are captured as a
+        # torch CUDA graph (thread-local capture) instead of the handle's graph
+        self.tp: Optional[TensorParallel] = None
+        if allreduce is not None or weights.lm_head is not None:
+            rank, world, group = allreduce if isinstance(allreduce, tuple) else (0, 1, None)
+            self.tp = TensorParallel(self, rank=rank, world=world, group=group)
+        self._torch_graph = _TorchGraphBridge(torch_module) if self.tp is not None and self.tp.world > 1 else None
+        if self._torch_graph is not None:
+            self.graph_plan = KudaCudaGraphPlan(self._torch_graph)
 
     @property
     def captured(self) -> bool:
@@ -366,11 +475,11 @@ class StaticDecodePlan:
         return n
 
     def _residual_linear(self, x: Any, lin: NF4Linear, stream_ptr: int) -> int:
-        if self.allreduce is None:
+        if self.tp is None:
             self.bridge.dispatch_nf4_linear_residual(x, lin.packed, lin.absmax, self.buffers.x, rows=lin.rows, k=lin.k,
                                                      stream_ptr=stream_ptr)
             return 1
-        return self.allreduce.residual_linear(self, x, lin, stream_ptr)
+        return self.tp.residual_linear(self, x, lin, stream_ptr)
 
     def _lm_head(self, stream_ptr: int) -> int:
         b, w, c = self.buffers, self.weights, self.config
@@ -379,7 +488,9 @@ class StaticDecodePlan:
                                                 logits=b.logits if self.keep_logits else None, epsilon=c.eps,
                                                 stream_ptr=stream_ptr)
             return 1
-        raise NativeCudaError("untied NF4 lm_head is served by the tensor-parallel plan")
+        if self.tp is None:
+            raise NativeCudaError("an untied NF4 lm_head needs the tensor-parallel hook")
+        return self.tp.lm_head(self, stream_ptr)
 
     # ------------------------------------------------------------------ state
     def set_state(self, token: int, position: int, stream: Any = None) -> None:
@@ -420,7 +531,10 @@ class StaticDecodePlan:
         self.buffers.state.copy_(saved_state)
         self.buffers.history.copy_(saved_hist)
         torch.cuda.synchronize(self.device)
-        self.bridge.reset_graph()
+        if self._torch_graph is None:
+            self.bridge.reset_graph()
+        else:
+            self._torch_graph.reset()
         self.graph_plan.invalidate()
         key = self.make_graph_key()
         self.graph_plan.begin_capture(key, stream_ptr=sp)
@@ -431,7 +545,8 @@ class StaticDecodePlan:
                 self.graph_plan.end_capture(key, stream_ptr=sp)
             finally:
                 self.graph_plan.invalidate()
-                self.bridge.reset_graph()
+                if self._torch_graph is None:
+                    self.bridge.reset_graph()
             raise
         self.graph_plan.end_capture(key, stream_ptr=sp)
         self.graph_key = key
@@ -461,17 +576,35 @@ class StaticDecodePlan:
         if len(prompt) + 1 > self.kv_bucket:
             raise ValueError("prompt does not fit the KV bucket")
         torch = self.torch
-        # host state in, replay, next token out -- all on the replay stream
-        # (kudacuda_sm100_graph_step_host), so a state write can never land
-        # while the previous step is still running
-        host_in = torch.zeros(4, dtype=torch.int32).pin_memory()
-        host_out = torch.zeros(1, dtype=torch.int32).pin_memory()
         torch.cuda.synchronize(self.device)
-        sp = int(stream.cuda_stream)
+        nxt = 0
         for i, tok in enumerate(prompt):
-            host_in[0], host_in[1], host_in[2] = int(tok), i, i + 1
-            self.bridge.graph_step_host(host_in, self.buffers.state, host_out, self.buffers.next_token, stream_ptr=sp)
-        return int(host_out[0])
+            nxt = self.step_host(int(tok), i, stream)
+        return nxt
+
+    def step_host(self, token: int, position: int, stream: Any) -> int:
+        """One decode step driven from the host: state in, replay, next token
+        out, all on the replay stream (so a state write never lands while the
+        previous step still runs); host-synchronous.  Uses the library's
+        one-call kudacuda_sm100_graph_step_host for the handle's graph."""
+
+        torch = self.torch
+        if getattr(self, "_host_in", None) is None:
+            self._host_in = torch.zeros(4, dtype=torch.int32).pin_memory()
+            self._host_out = torch.zeros(1, dtype=torch.int32).pin_memory()
+        hi, ho = self._host_in, self._host_out
+        hi[0], hi[1], hi[2] = int(token), int(position), int(position) + 1
+        sp = int(stream.cuda_stream)
+        if self._torch_graph is None:
+            self.bridge.graph_step_host(hi, self.buffers.state, ho, self.buffers.next_token, stream_ptr=sp)
+        else:
+            with torch.cuda.stream(stream):
+                self.buffers.state.copy_(hi, non_blocking=True)
+            self.replay(stream)
+            with torch.cuda.stream(stream):
+                ho.copy_(self.buffers.next_token, non_blocking=True)
+            stream.synchronize()
+        return int(ho[0])
 
     def generate_device(self, steps: int, stream: Any) -> None:
         """Replay the graph ``steps`` times with no host interaction; the

@@ -1056,6 +1056,36 @@ class KudaCudaBridge:
     def lm_head_workspace_bytes(self) -> int:
         return int(self.lib.kudacuda_sm100_lm_head_workspace_bytes())
 
+    # ---------------------------------------------------------------- tensor-parallel step ops
+    def dispatch_rmsnorm_nf4_gemv(self, x: Any, norm_weight: Any, weight: tuple, output: Any, *, epsilon: float,
+                                  stream_ptr: int) -> None:
+        packed, absmax = weight[0], weight[1]
+        rows = int(output.numel())
+        od = _DTYPE_CODE[_dtype_name(output.dtype)]
+        self._call("kudacuda_sm100_rmsnorm_nf4_gemv", self._tensor_pointer(x, "input"),
+                   self._tensor_pointer(norm_weight, "norm_weight"), self._tensor_pointer(packed, "weight_packed"),
+                   self._tensor_pointer(absmax, "absmax"), self._tensor_pointer(output, "output"), od, rows,
+                   int(x.numel()), float(epsilon), _normalize_cuda_handle(stream_ptr))
+
+    def dispatch_residual_add_f32(self, partial_sum: Any, residual: Any, *, stream_ptr: int) -> None:
+        self._call("kudacuda_sm100_residual_add_f32", self._tensor_pointer(partial_sum, "partial_sum"),
+                   self._tensor_pointer(residual, "residual"), int(residual.numel()),
+                   _normalize_cuda_handle(stream_ptr))
+
+    def argmax_workspace_bytes(self) -> int:
+        return int(self.lib.kudacuda_sm100_argmax_workspace_bytes())
+
+    def dispatch_argmax_shard(self, logits: Any, workspace: Any, ticket: Any, out_pair: Any, *, index_base: int,
+                              stream_ptr: int) -> None:
+        self._call("kudacuda_sm100_argmax_shard_f32", self._tensor_pointer(logits, "logits"), int(logits.numel()),
+                   int(index_base), self._tensor_pointer(workspace, "workspace"),
+                   int(workspace.numel()) * int(workspace.element_size()), self._tensor_pointer(ticket, "ticket"),
+                   self._tensor_pointer(out_pair, "out_pair"), _normalize_cuda_handle(stream_ptr))
+
+    def dispatch_select_token(self, pairs: Any, next_token: Any, *, count: int, stream_ptr: int) -> None:
+        self._call("kudacuda_sm100_select_token", self._tensor_pointer(pairs, "pairs"), int(count),
+                   self._tensor_pointer(next_token, "next_token"), _normalize_cuda_handle(stream_ptr))
+
     def error_word(self, *, clear: bool = True) -> int:
         word = ctypes.c_int(0)
         self._raise_if_failed(self.lib.kudacuda_sm100_error_word(self.engine_handle, ctypes.byref(word), int(clear)),

@@ -58,6 +58,11 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         [_p, _u64, _u64, _u64, _u64, _u64, _i64, _u64, _u64, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _u64],
     ),
     "kudacuda_sm100_gqa_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64, _i64]),
+    "kudacuda_sm100_rmsnorm_nf4_gemv": (_i32, [_p, _u64, _u64, _u64, _u64, _u64, _i32, _i64, _i64, _f32, _u64]),
+    "kudacuda_sm100_residual_add_f32": (_i32, [_p, _u64, _u64, _i64, _u64]),
+    "kudacuda_sm100_argmax_workspace_bytes": (_i64, []),
+    "kudacuda_sm100_argmax_shard_f32": (_i32, [_p, _u64, _i64, _i64, _u64, _i64, _u64, _u64, _u64]),
+    "kudacuda_sm100_select_token": (_i32, [_p, _u64, _i64, _u64, _u64]),
     "kudacuda_sm100_gqa_decode_static": (
         _i32, [_p, _u64, _u64, _u64, _u64, _u64, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _u64]
     ),
