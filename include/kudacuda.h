@@ -284,6 +284,55 @@ KUDACUDA_API int kudacuda_sm100_gqa_decode_static(void* handle, uint64_t query, 
                                                   int64_t query_heads, int64_t kv_heads, int64_t head_dim, float scale,
                                                   uint64_t stream);
 
+/* Persistent decode of all decoder layers (no reference counterpart: the
+ * reference launches one kernel per op and leaves o_proj/down to bitsandbytes,
+ * python/kudacuda_sidecar.py:947, :1746).
+ *
+ * nf4_retile copies bitsandbytes NF4 weights (packed uint8 [rows * k / 2],
+ * fp32 absmax [rows * k / 64]) into the stream layout the persistent kernel
+ * reads: groups of 64 rows x 64-element blocks, 2048 code bytes + 256 absmax
+ * bytes per (group, block), rows within a group ordered for the epilogue.
+ * mode 0: one matrix (rows % 64 == 0); mode 1: gate (matrix 0) and up
+ * (matrix 1), equal rows % 32 == 0; mode 2: q, k, v with RoPE partners of
+ * each q/k head (head_dim % 64 == 0) in one group.  Outputs hold
+ * groups * 64 * k / 2 code bytes and groups * 64 * k / 64 floats;
+ * nf4_retile_groups returns groups (or -1 for unsupported shapes).
+ *
+ * decode_layers_persistent runs every layer of one batch-1 Qwen2/Llama decode
+ * step (RMSNorm, QKV + bias + RoPE + KV append at state[1], GQA attention
+ * over state[2] tokens, o_proj + residual, RMSNorm, gate/up SwiGLU,
+ * down + residual; Transformers' bf16 rounding points) in one cooperative
+ * launch of one CTA per SM.  layer_table is a device int64 [layers][16] of
+ * pointers: qkv codes, qkv absmax, o codes, o absmax, gate/up codes, gate/up
+ * absmax, down codes, down absmax (all from nf4_retile), input norm, post
+ * norm, q bias, k bias, v bias (0 when absent), this layer's K cache and
+ * V cache ([kv_heads][kv_capacity][head_dim] bf16), 0.  x (bf16 [hidden]) is
+ * read as the step's input and holds the last layer's output afterwards.
+ * scratch (size from decode_persistent_scratch_bytes, zeroed once by the
+ * caller) holds partial sums and counters that reset themselves at the end of
+ * each step; the result is deterministic (fixed summation order).
+ * Requires head_dim 128, q_heads/kv_heads <= 8, hidden and intermediate
+ * multiples of 64.  Device waits are bounded: a wait that runs out sets bit 4
+ * of the error word and ends the step early instead of hanging. */
+KUDACUDA_API int64_t kudacuda_sm100_nf4_retile_groups(int mode, int64_t rows0, int64_t rows1, int64_t rows2,
+                                                      int64_t head_dim);
+KUDACUDA_API int kudacuda_sm100_nf4_retile(void* handle, int mode, uint64_t packed0, uint64_t absmax0, int64_t rows0,
+                                           uint64_t packed1, uint64_t absmax1, int64_t rows1, uint64_t packed2,
+                                           uint64_t absmax2, int64_t rows2, int64_t k, int64_t head_dim,
+                                           uint64_t out_codes, uint64_t out_absmax, uint64_t stream);
+KUDACUDA_API int64_t kudacuda_sm100_decode_persistent_scratch_bytes(void* handle, int64_t layers, int64_t hidden,
+                                                                   int64_t q_heads, int64_t kv_heads,
+                                                                   int64_t head_dim, int64_t intermediate,
+                                                                   int64_t kv_capacity);
+KUDACUDA_API int kudacuda_sm100_decode_layers_persistent(void* handle, uint64_t layer_table, int64_t layers,
+                                                         uint64_t x, uint64_t state, uint64_t rope_cos,
+                                                         uint64_t rope_sin, int64_t max_pos, uint64_t scratch,
+                                                         int64_t scratch_bytes,
+                                                         int64_t hidden, int64_t q_heads, int64_t kv_heads,
+                                                         int64_t head_dim, int64_t intermediate,
+                                                         int64_t kv_capacity, float eps, float scale,
+                                                         uint64_t stream);
+
 /* Library / build identification: "sm_100a". */
 KUDACUDA_API const char* kudacuda_sm100_target_arch(void);
 

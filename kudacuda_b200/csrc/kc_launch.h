@@ -156,4 +156,34 @@ cudaError_t rmsnorm_f32(const float* x, const float* w, float* out, int64_t rows
 cudaError_t dense_rmsnorm_qkv_f16(const void* x, const void* norm_w, const void* w, const void* bias,
                                   void* out, int64_t rows, int64_t hidden, float eps, cudaStream_t s);
 
+// ---- persistent decode of all layers (decode_persistent.cu) ----------------------
+// Weight stream layout ("group tiles"), built once from the bitsandbytes layout.
+enum RetileMode : int {
+    kRetilePlain = 0,    // rows 64g .. 64g + 63                    (o_proj, down, generic)
+    kRetileSwiGlu = 1,   // gate rows 32g .. +31, then up rows 32g .. +31
+    kRetileQkvRope = 2,  // q / k heads with RoPE partners 32 rows apart, then plain v rows
+};
+int retile_groups(int mode, int rows0, int rows1, int rows2, int head_dim);
+cudaError_t nf4_retile(int mode, const uint8_t* const* packed, const float* const* absmax, const int* rows, int K,
+                       int head_dim, uint8_t* out_codes, float* out_absmax, cudaStream_t stream);
+
+struct PersistDims {
+    int layers, hidden, q_heads, kv_heads, head_dim, intermediate, kv_capacity;
+};
+struct PersistLaunch {
+    const uint64_t* layer_table;  // device [layers][16]
+    PersistDims dims;
+    int max_pos;
+    float eps, scale;
+    const int32_t* state;  // {token, pos, kv_len, pad}
+    uint16_t* x;  // bf16 [hidden]: the step's input, then the last layer's output
+    const uint16_t* rope_cos;
+    const uint16_t* rope_sin;
+    void* scratch;
+    int* err;
+};
+int64_t decode_persistent_scratch_bytes(const PersistDims& d, int sms);
+const char* decode_persistent_check(const PersistDims& d, int sms);
+cudaError_t decode_layers_persistent(const PersistLaunch& p, cudaStream_t stream);
+
 }  // namespace kc

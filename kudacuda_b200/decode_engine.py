@@ -344,6 +344,72 @@ class DecodeBuffers:
     lm_scratch: Any = None  # f32 logits for an NF4 lm_head
 
 
+class PersistentLayers:
+    """Device data of the persistent decode path for one plan: every layer's
+    q/k/v, o, gate/up and down weights copied once into the stream layout of
+    ``kudacuda_sm100_decode_layers_persistent`` (the bitsandbytes tensors stay
+    as they are for the per-op ABI), the device layer table and the kernel's
+    self-resetting scratch."""
+
+    SLOTS = 16
+
+    def __init__(self, plan: "StaticDecodePlan") -> None:
+        torch = plan.torch
+        br, c, w, b = plan.bridge, plan.config, plan.weights, plan.buffers
+        dev = plan.device
+        self.plan = plan
+        sp = int(torch.cuda.current_stream(dev).cuda_stream)
+        d = c.head_dim
+        self.tiles: list[tuple[Any, ...]] = []
+        table = torch.zeros((c.layers, self.SLOTS), dtype=torch.int64)
+        for li, L in enumerate(w.layers):
+            ops = (
+                (br.RETILE_QKV_ROPE, [(L.q.packed, L.q.absmax, L.q.rows), (L.k.packed, L.k.absmax, L.k.rows),
+                                      (L.v.packed, L.v.absmax, L.v.rows)], L.q.k),
+                (br.RETILE_PLAIN, [(L.o.packed, L.o.absmax, L.o.rows)], L.o.k),
+                (br.RETILE_SWIGLU, [(L.gate.packed, L.gate.absmax, L.gate.rows),
+                                    (L.up.packed, L.up.absmax, L.up.rows)], L.gate.k),
+                (br.RETILE_PLAIN, [(L.down.packed, L.down.absmax, L.down.rows)], L.down.k),
+            )
+            row: list[int] = []
+            for mode, mats, k in ops:
+                rows = tuple(m[2] for m in mats) + (0,) * (3 - len(mats))
+                groups = br.retile_groups(mode, rows, d)
+                if groups < 1:
+                    raise NativeCudaError(f"persistent decode cannot re-tile layer {li} (mode {mode}, rows {rows})")
+                codes = torch.empty(groups * 64 * k // 2, dtype=torch.uint8, device=dev)
+                absm = torch.empty(groups * 64 * k // 64, dtype=torch.float32, device=dev)
+                br.dispatch_nf4_retile(mode, mats, codes, absm, k=k, head_dim=d, stream_ptr=sp)
+                self.tiles.append((codes, absm))
+                row += [codes.data_ptr(), absm.data_ptr()]
+            ptr = lambda t: 0 if t is None else int(t.data_ptr())  # noqa: E731
+            row += [ptr(L.in_norm), ptr(L.post_norm), ptr(L.q_bias), ptr(L.k_bias), ptr(L.v_bias),
+                    int(b.kcache[li].data_ptr()), int(b.vcache[li].data_ptr()), 0]
+            table[li] = torch.tensor(row, dtype=torch.int64)
+        self.table = table.to(dev)
+        nbytes = br.persistent_scratch_bytes(layers=c.layers, hidden=c.hidden, q_heads=plan.q_heads,
+                                             kv_heads=plan.kv_heads, head_dim=d, intermediate=plan.inter,
+                                             kv_capacity=plan.kv_bucket)
+        self.scratch = torch.zeros((nbytes + 3) // 4, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+
+    def pointers(self) -> list[int]:
+        out = [int(self.table.data_ptr()), int(self.scratch.data_ptr())]
+        for codes, absm in self.tiles:
+            out += [int(codes.data_ptr()), int(absm.data_ptr())]
+        return out
+
+    def record(self, stream_ptr: int) -> int:
+        p, b, c = self.plan, self.plan.buffers, self.plan.config
+        p.bridge.dispatch_decode_layers_persistent(
+            self.table, b.x, b.state, b.rope_cos, b.rope_sin, self.scratch, layers=c.layers,
+            max_pos=int(b.rope_cos.shape[0]), hidden=c.hidden, q_heads=p.q_heads, kv_heads=p.kv_heads,
+            head_dim=c.head_dim, intermediate=p.inter, kv_capacity=p.kv_bucket, epsilon=c.eps,
+            scale=1.0 / math.sqrt(c.head_dim), stream_ptr=stream_ptr)
+        return 1
+
+
+
 class StaticDecodePlan:
     """Fixed-shape decode step for one model on one device: buffers, the op
     sequence, and its CUDA graph.  ``kv_bucket`` is the cache capacity (the
@@ -351,7 +417,7 @@ class StaticDecodePlan:
 
     def __init__(self, bridge: KudaCudaBridge, weights: ModelWeights, *, kv_bucket: int = 512,
                  max_tokens: Optional[int] = None, device: Any = "cuda:0", torch_module: Any = None,
-                 allreduce: Any = None, keep_logits: bool = True) -> None:
+                 allreduce: Any = None, keep_logits: bool = True, persistent: bool = False) -> None:
         if torch_module is None:
             import torch as torch_module
         self.torch = torch_module
@@ -407,6 +473,13 @@ class StaticDecodePlan:
         self._torch_graph = _TorchGraphBridge(torch_module) if self.tp is not None and self.tp.world > 1 else None
         if self._torch_graph is not None:
             self.graph_plan = KudaCudaGraphPlan(self._torch_graph)
+        # persistent path: all layers of a step in one cooperative launch over
+        # weights re-tiled once into the kernel's stream layout
+        self.persistent: Optional[PersistentLayers] = None
+        if persistent:
+            if self.tp is not None:
+                raise NativeCudaError("the persistent decode path has no tensor-parallel variant")
+            self.persistent = PersistentLayers(self)
 
     @property
     def captured(self) -> bool:
@@ -420,6 +493,8 @@ class StaticDecodePlan:
         ptrs = [t.data_ptr() for t in (b.state, b.x, b.q, b.attn, b.h, b.kcache, b.vcache, b.gqa_ws, b.gqa_tickets,
                                        b.lm_ws, b.lm_ticket, b.logits, b.next_token, b.history, b.rope_cos, b.rope_sin,
                                        w.embedding, w.final_norm)]
+        if self.persistent is not None:
+            ptrs += self.persistent.pointers()
         for L in w.layers:
             ptrs += [L.in_norm.data_ptr(), L.post_norm.data_ptr()]
             for lin in (L.q, L.k, L.v, L.o, L.gate, L.up, L.down):
@@ -428,7 +503,7 @@ class StaticDecodePlan:
         d = c.head_dim
         return DecodeGraphKey(
             device_id=int(self.torch.device(self.device).index or 0),
-            tactic_name="decode_step_sm100_v1",
+            tactic_name="decode_step_sm100_persistent_v1" if self.persistent is not None else "decode_step_sm100_v1",
             layer_count=c.layers,
             query_shape=(1, self.q_heads, 1, d),
             key_shape=(1, self.kv_heads, self.kv_bucket, d),
@@ -452,6 +527,13 @@ class StaticDecodePlan:
         br.dispatch_embedding(w.embedding, b.state[0:1], b.x, stream_ptr=stream_ptr)
         n += 1
         scale = 1.0 / math.sqrt(c.head_dim)
+        if self.persistent is not None:
+            n += self.persistent.record(stream_ptr)
+            n += self._lm_head(stream_ptr)
+            br.dispatch_decode_advance(b.state, b.next_token, history=b.history, stream_ptr=stream_ptr)
+            n += 1
+            self.launches_per_step = n
+            return n
         for li, L in enumerate(w.layers):
             kc, vc = b.kcache[li], b.vcache[li]
             br.dispatch_attention_input(b.x, L.in_norm, L.q.as_tuple(L.q_bias), L.k.as_tuple(L.k_bias),

@@ -1086,6 +1086,53 @@ class KudaCudaBridge:
         self._call("kudacuda_sm100_select_token", self._tensor_pointer(pairs, "pairs"), int(count),
                    self._tensor_pointer(next_token, "next_token"), _normalize_cuda_handle(stream_ptr))
 
+    # ---------------------------------------------------------------- persistent decode of all layers
+    RETILE_PLAIN, RETILE_SWIGLU, RETILE_QKV_ROPE = 0, 1, 2
+
+    def retile_groups(self, mode: int, rows: tuple[int, int, int], head_dim: int = 0) -> int:
+        """Row groups of the persistent stream layout, or -1 for an unsupported shape."""
+
+        self._check_open()
+        return int(self.lib.kudacuda_sm100_nf4_retile_groups(int(mode), int(rows[0]), int(rows[1]), int(rows[2]),
+                                                             int(head_dim)))
+
+    def dispatch_nf4_retile(self, mode: int, mats: list[tuple[Any, Any, int]], out_codes: Any, out_absmax: Any, *,
+                            k: int, head_dim: int = 0, stream_ptr: int) -> None:
+        """Copy bitsandbytes NF4 matrices ``(packed, absmax, rows)`` into the
+        persistent kernel's group-tile stream layout."""
+
+        args: list[int] = []
+        for i in range(3):
+            if i < len(mats):
+                packed, absmax, rows = mats[i]
+                args += [self._tensor_pointer(packed, "packed"), self._tensor_pointer(absmax, "absmax"), int(rows)]
+            else:
+                args += [0, 0, 0]
+        self._call("kudacuda_sm100_nf4_retile", int(mode), *args, int(k), int(head_dim),
+                   self._tensor_pointer(out_codes, "out_codes"), self._tensor_pointer(out_absmax, "out_absmax"),
+                   _normalize_cuda_handle(stream_ptr))
+
+    def persistent_scratch_bytes(self, *, layers: int, hidden: int, q_heads: int, kv_heads: int, head_dim: int,
+                                 intermediate: int, kv_capacity: int) -> int:
+        self._check_open()
+        n = int(self.lib.kudacuda_sm100_decode_persistent_scratch_bytes(
+            self.engine_handle, int(layers), int(hidden), int(q_heads), int(kv_heads), int(head_dim),
+            int(intermediate), int(kv_capacity)))
+        if n < 0:
+            raise NativeCudaError(f"kudacuda_sm100_decode_persistent_scratch_bytes: {self._native_error()}")
+        return n
+
+    def dispatch_decode_layers_persistent(self, layer_table: Any, x: Any, state: Any, rope_cos: Any, rope_sin: Any,
+                                          scratch: Any, *, layers: int, max_pos: int,
+                                          hidden: int, q_heads: int, kv_heads: int, head_dim: int, intermediate: int,
+                                          kv_capacity: int, epsilon: float, scale: float, stream_ptr: int) -> None:
+        self._call("kudacuda_sm100_decode_layers_persistent", self._tensor_pointer(layer_table, "layer_table"),
+                   int(layers), self._tensor_pointer(x, "x"), self._tensor_pointer(state, "state"), self._tensor_pointer(rope_cos, "rope_cos"),
+                   self._tensor_pointer(rope_sin, "rope_sin"), int(max_pos), self._tensor_pointer(scratch, "scratch"),
+                   int(scratch.numel()) * int(scratch.element_size()), int(hidden), int(q_heads), int(kv_heads),
+                   int(head_dim), int(intermediate), int(kv_capacity), float(epsilon), float(scale),
+                   _normalize_cuda_handle(stream_ptr))
+
     def error_word(self, *, clear: bool = True) -> int:
         word = ctypes.c_int(0)
         self._raise_if_failed(self.lib.kudacuda_sm100_error_word(self.engine_handle, ctypes.byref(word), int(clear)),

@@ -10,6 +10,10 @@ KV rows for attention).
     python -m kudacuda_b200.microbench --op swiglu [--copies 12 --launches 36 --reps 20]
     ops: gemv_11008x2048 gemv_2048x11008 qkv_rope oproj down swiglu gqa512 gqa2048 lm_head all
 
+    python -m kudacuda_b200.microbench --op persistent --layers 36 --kv 512 [--launches 3 --reps 20]
+      the persistent all-layers kernel alone (Qwen2.5-3B layer shapes, random
+      NF4 weights), launched directly on its stream at position kv - 1
+
 The same command with ``--reps 1 --launches 4`` is the small case used for ncu
 captures (see profiles/).
 """
@@ -173,6 +177,38 @@ def time_case(torch, bridge: KudaCudaBridge, case: OpCase, launches: int, reps: 
             "frac_of_measured_hbm": round(gbs / _peak(), 4)}
 
 
+def time_persistent(torch, layers: int, kv: int, launches: int, reps: int, device: str) -> dict:
+    from .decode_engine import StaticDecodePlan, random_weights, tiny_config
+
+    cfg = tiny_config(layers=layers, vocab=4096)
+    bridge = KudaCudaBridge(device_id=torch.device(device).index or 0)
+    w = random_weights(bridge, cfg, seed=20260824, device=device)
+    plan = StaticDecodePlan(bridge, w, kv_bucket=max(kv, 16), max_tokens=max(kv, 16), device=device, persistent=True)
+    stream = torch.cuda.Stream()
+    sp = int(stream.cuda_stream)
+    plan.set_state(1, kv - 1, stream)
+    with torch.cuda.stream(stream):
+        for _ in range(launches):
+            plan.persistent.record(sp)
+    stream.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            plan.persistent.record(sp)
+    e.record(stream)
+    e.synchronize()
+    us = s.elapsed_time(e) * 1e3 / max(reps, 1)
+    wb = cfg.weight_bytes_per_token()
+    nbytes = (wb["nf4_absmax"] + wb["norms_bias"] - cfg.hidden * 2 + 2 * cfg.hidden * 2 +
+              layers * 2 * plan.kv_heads * cfg.head_dim * 2 * kv)
+    gbs = nbytes / (us * 1e-6) / 1e9
+    err = bridge.error_word(clear=True)
+    return {"op": f"persistent_{layers}l_kv{kv}", "us_per_launch": round(us, 3), "us_per_layer": round(us / layers, 3),
+            "bytes": nbytes, "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / _peak(), 4),
+            "device_error_word": err}
+
+
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--op", default="all")
@@ -180,10 +216,16 @@ def main(argv=None) -> int:
     p.add_argument("--launches", type=int, default=36)
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--device", default="cuda:0")
+    p.add_argument("--layers", type=int, default=36, help="--op persistent: decoder layers")
+    p.add_argument("--kv", type=int, default=512, help="--op persistent: tokens attended (kv_len)")
     args = p.parse_args(argv)
     import torch
 
     torch.cuda.set_device(torch.device(args.device))
+    if args.op == "persistent":
+        r = time_persistent(torch, args.layers, args.kv, max(args.launches, 1), args.reps, args.device)
+        print(json.dumps(r), flush=True)
+        return 1 if r["device_error_word"] else 0
     names = (["gemv_11008x2048", "gemv_2048x11008", "qkv_rope", "oproj", "down", "swiglu", "gqa512", "gqa2048",
               "lm_head"] if args.op == "all" else args.op.split(","))
     bridge = KudaCudaBridge(device_id=torch.device(args.device).index or 0)

@@ -63,6 +63,16 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "kudacuda_sm100_argmax_workspace_bytes": (_i64, []),
     "kudacuda_sm100_argmax_shard_f32": (_i32, [_p, _u64, _i64, _i64, _u64, _i64, _u64, _u64, _u64]),
     "kudacuda_sm100_select_token": (_i32, [_p, _u64, _i64, _u64, _u64]),
+    "kudacuda_sm100_nf4_retile_groups": (_i64, [_i32, _i64, _i64, _i64, _i64]),
+    "kudacuda_sm100_nf4_retile": (
+        _i32, [_p, _i32, _u64, _u64, _i64, _u64, _u64, _i64, _u64, _u64, _i64, _i64, _i64, _u64, _u64, _u64]
+    ),
+    "kudacuda_sm100_decode_persistent_scratch_bytes": (_i64, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _i64]),
+    "kudacuda_sm100_decode_layers_persistent": (
+        _i32,
+        [_p, _u64, _i64, _u64, _u64, _u64, _u64, _i64, _u64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _f32,
+         _u64],
+    ),
     "kudacuda_sm100_gqa_decode_static": (
         _i32, [_p, _u64, _u64, _u64, _u64, _u64, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _u64]
     ),

@@ -277,3 +277,82 @@ def lm_head_argmax(x: np.ndarray, final_norm: np.ndarray, emb: np.ndarray, eps: 
         _ptr(x), _ptr(final_norm), _ptr(emb), ctypes.c_int64(vocab), ctypes.c_int64(hidden), ctypes.c_float(eps), _ptr(logits)
     )
     return int(tok), logits
+
+
+# ---------------------------------------------------------------- persistent-decode weight layout
+# The "group tile" stream layout consumed by kudacuda_sm100_decode_layers_persistent
+# (no reference counterpart: a load-time re-layout of the bitsandbytes NF4
+# storage, kernels/common/nf4_device.cuh:29-40, that keeps every code byte and
+# absmax value bit-exact and only moves them).  Restated here in numpy as the
+# checker of the device re-tile kernel.
+RETILE_PLAIN, RETILE_SWIGLU, RETILE_QKV_ROPE = 0, 1, 2
+
+
+def retile_rows(mode: int, rows: tuple[int, int, int], head_dim: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """(matrix index, source row) of every group row, each shaped [groups, 64].
+
+    plain: group g rows 64g .. 64g+63 of matrix 0; SwiGLU: rows 0..31 are gate
+    rows 32g.., rows 32..63 the matching up rows; q/k/v: each q head then each
+    k head in groups of 32 RoPE pairs (row r < 32 is element 32m + r of the
+    head's first half, row r + 32 its partner in the second half), then plain
+    64-row groups of v."""
+
+    rr = np.arange(64)
+    if mode == RETILE_PLAIN:
+        groups = rows[0] // 64
+        m = np.zeros((groups, 64), dtype=np.int64)
+        r = np.arange(groups)[:, None] * 64 + rr[None, :]
+        return m, r
+    if mode == RETILE_SWIGLU:
+        groups = rows[0] // 32
+        m = np.broadcast_to((rr >= 32).astype(np.int64), (groups, 64)).copy()
+        r = np.arange(groups)[:, None] * 32 + (rr & 31)[None, :]
+        return m, r
+    if mode == RETILE_QKV_ROPE:
+        hd = head_dim
+        gph = hd // 64
+        qg, kg, vg = rows[0] // hd * gph, rows[1] // hd * gph, rows[2] // 64
+        ms, rs = [], []
+        for grp in range(qg + kg + vg):
+            if grp < qg + kg:
+                mat = 0 if grp < qg else 1
+                u = grp if grp < qg else grp - qg
+                head, mm = divmod(u, gph)
+                ms.append(np.full(64, mat))
+                rs.append(head * hd + 32 * mm + (rr & 31) + np.where(rr >= 32, hd // 2, 0))
+            else:
+                ms.append(np.full(64, 2))
+                rs.append(64 * (grp - qg - kg) + rr)
+        return np.stack(ms).astype(np.int64), np.stack(rs).astype(np.int64)
+    raise ValueError(f"unknown re-tile mode {mode}")
+
+
+def retile_nf4(mode: int, mats: list[tuple[np.ndarray, np.ndarray, int]], k: int, head_dim: int = 0):
+    """bitsandbytes (packed [rows*k/2] u8, absmax [rows*k/64] f32, rows) matrices ->
+    (codes u8 [groups * (k/64) * 2048], absmax f32 [groups * (k/64) * 64]).
+
+    Chunk (group, block b): 4 tiles x 32 lanes x 16 bytes, lane 4g + t holding
+    bytes [32b + 8t, +8) of group rows 16*tile + g then 16*tile + 8 + g; then 64
+    absmax ordered [half][g][tile] (row 16*tile + 8*half + g)."""
+
+    rows = tuple(m[2] for m in mats) + (0,) * (3 - len(mats))
+    msel, rsel = retile_rows(mode, rows, head_dim)
+    groups, nbpt = msel.shape[0], k // 64
+    packed = [np.asarray(p, dtype=np.uint8).reshape(n, k // 2) for p, _, n in mats]
+    absm = [np.asarray(a, dtype=np.float32).reshape(n, nbpt) for _, a, n in mats]
+    data = np.zeros((64, groups, k // 2), dtype=np.uint8)
+    amax = np.zeros((64, groups, nbpt), dtype=np.float32)
+    for gr in range(64):
+        for mi in range(len(mats)):
+            sel = msel[:, gr] == mi
+            data[gr, sel] = packed[mi][rsel[sel, gr]]
+            amax[gr, sel] = absm[mi][rsel[sel, gr]]
+    data = data.reshape(64, groups, nbpt, 4, 8)  # [group row][group][block][t][8 bytes]
+    ia = (16 * np.arange(4)[:, None] + np.arange(8)[None, :])  # [tile, g] -> group row of lane (g, t)'s row A
+    codes = np.empty((groups, nbpt, 4, 8, 4, 16), dtype=np.uint8)  # [group][block][tile][g][t][16]
+    codes[..., :8] = data[ia].transpose(2, 3, 0, 1, 4, 5)
+    codes[..., 8:] = data[ia + 8].transpose(2, 3, 0, 1, 4, 5)
+    ab = np.empty((groups, nbpt, 2, 8, 4), dtype=np.float32)  # [group][block][half][g][tile]
+    for h in range(2):
+        ab[:, :, h] = amax[(16 * np.arange(4)[None, :] + 8 * h + np.arange(8)[:, None])].transpose(2, 3, 0, 1)
+    return codes.reshape(-1), ab.reshape(-1)
