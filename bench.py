@@ -627,6 +627,220 @@ def run_tp(args) -> dict | None:
     return out
 
 
+def run_batched(args) -> dict | None:
+    """batched decode of the Qwen2.5-3B-architecture model,
+    B independent sequences with uniform-random prompt lengths 32-512 in
+    per-sequence 2048-token bf16 caches (random N(0,1) cache rows stand in for
+    the prompts' keys and values).  A step advances every sequence by one
+    token: one replay of the batched graph (tcgen05 GEMMs over the padded
+    batch, per-sequence epilogues, split-KV attention with per-sequence
+    lengths, lm_head GEMM + per-sequence argmax).  value = B * K / time.
+    With N GPUs each rank runs its own batch (replicas, weak scaling)."""
+
+    import torch
+
+    from kudacuda_b200.decode_engine import QWEN25_3B, BatchedDecodePlan, random_weights
+    from kudacuda_b200.kudacuda_sidecar import KudaCudaBridge
+
+    rank, world, local = _dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    device = f"cuda:{local}"
+    cfg = QWEN25_3B
+    B = args.batch
+    cap = 2048
+    bridge = KudaCudaBridge(device_id=local)
+    weights = random_weights(bridge, cfg, seed=SEED, device=device)
+    plan = BatchedDecodePlan(bridge, weights, batch=B, kv_bucket=cap, max_tokens=cap, device=device)
+    stream = torch.cuda.Stream(device=device)
+    plan.capture(stream)
+    g = torch.Generator().manual_seed(SEED + 17 * rank + B)
+    lens = torch.randint(32, 513, (B,), generator=g)
+    toks = torch.randint(0, cfg.vocab, (B,), generator=g)
+    if int(lens.max()) + 2 * (args.warmup + args.steps) + 2 > cap:
+        raise SystemExit("prompt + warmup + steps must fit the 2048-token cache")
+    gd = torch.Generator(device=device).manual_seed(SEED + rank)
+    for li in range(cfg.layers):  # random cache rows (rows >= a sequence's length are never read)
+        plan.buffers.kcache[li].normal_(generator=gd)
+        plan.buffers.vcache[li].normal_(generator=gd)
+
+    plan.set_state(toks.tolist(), lens.tolist(), stream)
+    for _ in range(args.warmup):
+        plan.replay(stream)
+    stream.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.profiler.start()
+        start.record(stream)
+        for _ in range(args.steps):
+            plan.replay(stream)
+        end.record(stream)
+        end.synchronize()
+        torch.cuda.profiler.stop()
+    torch.cuda.synchronize(device)
+    if dist is not None:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    if dist is not None:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    err = bridge.error_word(clear=True)
+    if err:
+        raise SystemExit(f"device error word {err:#x} after the timed region")
+
+    # ---- end to end through the C ABI: per step the host writes every
+    # sequence's {token, position, kv_len} from pinned memory (B x 16 bytes),
+    # the graph replays, and the host reads the advanced state back
+    host_in = plan.buffers.state.cpu().pin_memory()
+    host_out = torch.zeros_like(host_in).pin_memory()
+    sp = int(stream.cuda_stream)
+    for _ in range(args.warmup):
+        bridge.graph_step_host(host_in, plan.buffers.state, host_out, plan.buffers.state, stream_ptr=sp)
+        host_in.copy_(host_out)
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        bridge.graph_step_host(host_in, plan.buffers.state, host_out, plan.buffers.state, stream_ptr=sp)
+        host_in.copy_(host_out)
+    e2e_s = time.perf_counter() - t0
+    if dist is not None:
+        t = torch.tensor([e2e_s], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    if bridge.error_word(clear=True):
+        raise SystemExit("device error word set in the end-to-end loop")
+
+    roof = batched_gemm_roofline(torch, bridge, plan, stream)
+    out = None
+    if rank == 0:
+        wb = cfg.weight_bytes_per_token()
+        kv_bytes = sum(cfg.kv_bytes_per_token(int(L) + args.warmup + args.steps // 2) for L in lens.tolist())
+        bytes_step = sum(wb.values()) + kv_bytes
+        ms_step = ms / args.steps
+        peak, peak_src = _peaks()
+        out = {
+            "metric": "batched decode tok/s",
+            "value": round(world * B * args.steps / (ms / 1e3), 1),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "nf4-weights/bf16-dequant/bf16-activations/f32-accumulate",
+            "data": "synthetic (random-init weights N(0,0.02) NF4-quantised on device; random N(0,1) cache rows)",
+            "config": {
+                "workload": f"config4: Qwen2.5-3B-architecture NF4 batched decode, batch {B}, 2048-token caches",
+                "batch": B,
+                "n_pad": plan.n_pad,
+                "prompt_lens": [int(lens.min()), int(lens.max())],
+                "mean_kv_len_timed": round(float(lens.float().mean()) + args.warmup + args.steps / 2.0, 1),
+                "global_batch": world * B,
+                "parallelism": f"dp{world} (independent batches)",
+                "l2": "inputs larger than L2 (2.2 GB of weights read per step)",
+                "ksplit": {"qkv": plan.ks_qkv, "o": plan.ks_o, "gate_up": plan.ks_gu, "down": plan.ks_dn,
+                           "lm_head": plan.ks_lm},
+            },
+            "hbm_roofline_per_step": {
+                "bytes_per_step": bytes_step,
+                "achieved_gbs": round(bytes_step / (ms_step / 1e3) / 1e9, 1),
+                "frac_of_measured_peak": round(bytes_step / (ms_step / 1e3) / 1e9 / peak, 4),
+                "peak_source": peak_src,
+            },
+            "e2e": {
+                "value": round(world * B * args.steps / e2e_s, 1),
+                "unit": UNIT,
+                "h2d_bytes_per_step": 16 * B,
+                "d2h_bytes_per_step": 16 * B,
+                "api": "kudacuda_sm100_graph_step_host (host int32 [B][4] state in and out, per step)",
+            },
+            "roofline": roof,
+            "gpu_launches": plan.launches_per_step * args.steps,
+            "launches_per_step": plan.launches_per_step,
+            "clocks": clocks.summary(),
+        }
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    bridge.reset_graph()
+    return out
+
+
+def batched_gemm_roofline(torch, bridge, plan, stream) -> dict:
+    """Average duration of the tcgen05 GEMM over the gate|up weights of every
+    layer (36 launches inside one graph, 914 MB of NF4 > L2), timed with CUDA
+    events on its stream.  Algorithmic bytes per launch: NF4 codes + absmax,
+    the batch's bf16 activations and bf16 outputs; flops 2 * rows * K * B."""
+
+    cfg = plan.config
+    b = plan.buffers
+    sp = int(stream.cuda_stream)
+    rows, k = 2 * plan.inter, cfg.hidden
+
+    def launch_all():
+        for gu in plan.gu:
+            bridge.dispatch_batch_gemm(gu.packed, gu.absmax, b.xn, b.partials, weight_type=0, rows=rows, k=k,
+                                       n_pad=plan.n_pad, ksplit=plan.ks_gu, stream_ptr=sp)
+
+    with torch.cuda.stream(stream):
+        launch_all()
+    stream.synchronize()
+    bridge.begin_capture(stream_ptr=sp)
+    launch_all()
+    bridge.end_capture(stream_ptr=sp)
+    reps = 10
+    bridge.replay_graph(stream_ptr=sp)
+    stream.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(reps):
+        bridge.replay_graph(stream_ptr=sp)
+    e.record(stream)
+    e.synchronize()
+    us = s.elapsed_time(e) * 1e3 / (reps * cfg.layers)
+    algo = rows * k // 2 + rows * k // 16 + plan.batch * k * 2 + plan.batch * rows * 2
+    flops = 2.0 * rows * k * plan.batch
+    peak, src = _peaks()
+    achieved = algo / (us * 1e-6) / 1e9
+    tf = _peak_tflops()
+    plan.capture(stream)  # the handle holds one graph: recapture the step
+    return {
+        "kernel": "nf4_gemm_tc_kernel (NF4 -> bf16 dequant in shared memory, tcgen05.mma M=128 x N=n_pad, TMEM)",
+        "bound": "hbm",
+        "achieved": round(achieved, 1),
+        "peak": peak,
+        "unit": "GB/s",
+        "frac": round(achieved / peak, 4),
+        "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
+        "bytes_per_launch": algo,
+        "us_per_launch": round(us, 3),
+        "tensor_tflops": round(flops / (us * 1e-6) / 1e12, 2),
+        "tensor_frac_of_bf16_peak": round(flops / (us * 1e-6) / 1e12 / tf, 4),
+        "traffic": None,
+    }
+
+
+def _peak_tflops() -> float:
+    try:
+        return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+    except (OSError, ValueError, KeyError):
+        return 1590.0
+
+
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
@@ -635,7 +849,8 @@ def main(argv=None) -> int:
     p.add_argument("--impl", choices=["kudacuda_b200", "reference"], default="kudacuda_b200")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=["qwen3b", "llama8b-tp"], default="qwen3b")
+    p.add_argument("--workload", choices=["qwen3b", "llama8b-tp", "qwen3b-batched"], default="qwen3b")
+    p.add_argument("--batch", type=int, default=64, help="sequences per step for --workload qwen3b-batched")
     p.add_argument("--path", choices=["persistent", "per-op"], default="persistent",
                    help="persistent: all layers in one cooperative launch; per-op: one launch per op")
     args = p.parse_args(argv)
@@ -645,6 +860,8 @@ def main(argv=None) -> int:
         out = run_reference(args)
     elif args.workload == "llama8b-tp":
         out = run_tp(args)
+    elif args.workload == "qwen3b-batched":
+        out = run_batched(args)
     else:
         out = run_gpu(args)
     if out is not None:

@@ -333,6 +333,70 @@ KUDACUDA_API int kudacuda_sm100_decode_layers_persistent(void* handle, uint64_t 
                                                          int64_t kv_capacity, float eps, float scale,
                                                          uint64_t stream);
 
+/* Batched decode: B independent sequences advance one token per step.  No
+ * reference counterpart (the reference's projections and its GQA contract,
+ * python/kudacuda_sidecar.py:145-153, are batch 1); the arithmetic is what
+ * Transformers does with bitsandbytes NF4 weights on a batch: every weight is
+ * dequantised to bf16 (level * absmax in fp32, rounded once), the matmul runs
+ * in bf16 with fp32 accumulation, activations are rounded to bf16 at the
+ * batch-1 points.  Activations are bf16 [n_pad][K] with zero rows from B up
+ * (n_pad in {16, 32, 64}, B <= n_pad).
+ *
+ * batch_gemm: partials[(s * total_rows + row_offset + r) * n_pad + b] =
+ *   sum over split s's share of K of W[r][k] * x[b][k] (fp32), on the tcgen05
+ *   tensor cores (weight as the 128-row M operand, the batch as N, fp32
+ *   accumulator in TMEM).  weight_type 0: NF4 packed [rows][k/2] + fp32 absmax
+ *   [rows][k/64]; 1: bf16 [rows][k] (absmax unused).  ksplit in [1, k/64];
+ *   batch_gemm_ksplit suggests one.  Several matrices may share one partials
+ *   buffer through row_offset.
+ * The epilogues sum the splits in split order (deterministic):
+ *   batch_qkv_rope: partials rows q | k | v; bias, RoPE at pos[b] (int32 [B]),
+ *     q -> q_out [B][qh][hd], k/v appended to caches [B][kvh][kv_capacity][hd]
+ *     at pos[b];
+ *   batch_residual: x[b][r] = bf16(x[b][r] + bf16(sum));
+ *   batch_swiglu: out[b][j] = bf16(bf16(silu(bf16 gate)) * bf16 up) over
+ *     partials rows gate (intermediate) | up (intermediate);
+ *   batch_argmax_advance: per sequence, the lowest-index maximum of the
+ *     bf16-rounded logits; state is int32 [B][4] = {token, pos, kv_len, pad}
+ *     and becomes {argmax, pos + 1, pos + 2, pad}; history [B][history_len]
+ *     (optional) records the token at its new position.
+ * batch_embedding: x[b] = embedding[state[b].token]; batch_state_views copies
+ * state's pos and kv_len columns to pos[B] and kv_len[B] for the RoPE
+ * epilogue and gqa_decode_batch (kudacuda_sm100_gqa_decode, bf16, with a
+ * per-sequence int32 length array; workspace and tickets as for
+ * kudacuda_sm100_gqa_decode with kv_len = kv_stride). */
+KUDACUDA_API int64_t kudacuda_sm100_batch_gemm_ksplit(int64_t rows, int64_t k);
+KUDACUDA_API int kudacuda_sm100_batch_gemm(void* handle, int weight_type, uint64_t weight, uint64_t absmax,
+                                           int64_t rows, int64_t k, uint64_t x, int64_t n_pad, int64_t ksplit,
+                                           uint64_t partials, int64_t row_offset, int64_t total_rows,
+                                           uint64_t stream);
+KUDACUDA_API int kudacuda_sm100_batch_rmsnorm(void* handle, uint64_t x, uint64_t weight, uint64_t out,
+                                              int64_t batch, int64_t hidden, float eps, uint64_t stream);
+KUDACUDA_API int kudacuda_sm100_batch_qkv_rope(void* handle, uint64_t partials, int64_t ksplit, int64_t n_pad,
+                                               int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                               uint64_t q_bias, uint64_t k_bias, uint64_t v_bias, uint64_t rope_cos,
+                                               uint64_t rope_sin, int64_t max_pos, uint64_t pos, uint64_t q_out,
+                                               uint64_t key_cache, uint64_t value_cache, int64_t kv_capacity,
+                                               uint64_t stream);
+KUDACUDA_API int kudacuda_sm100_batch_residual(void* handle, uint64_t partials, int64_t ksplit, int64_t rows,
+                                               int64_t n_pad, int64_t batch, uint64_t x, uint64_t stream);
+KUDACUDA_API int kudacuda_sm100_batch_swiglu(void* handle, uint64_t partials, int64_t ksplit, int64_t intermediate,
+                                             int64_t n_pad, int64_t batch, uint64_t out, uint64_t stream);
+KUDACUDA_API int64_t kudacuda_sm100_batch_argmax_workspace_bytes(int64_t batch);
+KUDACUDA_API int kudacuda_sm100_batch_argmax_advance(void* handle, uint64_t partials, int64_t ksplit, int64_t vocab,
+                                                     int64_t n_pad, int64_t batch, uint64_t workspace,
+                                                     int64_t workspace_bytes, uint64_t state, uint64_t history,
+                                                     int64_t history_len, uint64_t stream);
+KUDACUDA_API int kudacuda_sm100_batch_embedding(void* handle, uint64_t embedding, uint64_t state, uint64_t x,
+                                                int64_t batch, int64_t hidden, int64_t vocab, uint64_t stream);
+KUDACUDA_API int kudacuda_sm100_batch_state_views(void* handle, uint64_t state, int64_t batch, uint64_t pos,
+                                                  uint64_t kv_len, uint64_t stream);
+KUDACUDA_API int kudacuda_sm100_gqa_decode_batch(void* handle, uint64_t query, uint64_t key_cache,
+                                                 uint64_t value_cache, uint64_t output, uint64_t workspace,
+                                                 int64_t workspace_bytes, uint64_t tickets, uint64_t kv_len_array,
+                                                 int64_t batch_size, int64_t kv_stride, int64_t query_heads,
+                                                 int64_t kv_heads, int64_t head_dim, float scale, uint64_t stream);
+
 /* Library / build identification: "sm_100a". */
 KUDACUDA_API const char* kudacuda_sm100_target_arch(void);
 

@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a)
     const int kvh = blockIdx.x - b * a.kv_heads;
     const int split = blockIdx.y;
 
-    int kv_len = a.kv_len_dev != nullptr ? *a.kv_len_dev : a.kv_len;
+    int kv_len = a.kv_len_dev != nullptr ? a.kv_len_dev[a.kv_len_per_batch ? b : 0] : a.kv_len;
     if (kv_len < 1 || kv_len > a.stride) {
         if (a.err != nullptr && tid == 0) atomicOr(a.err, 4);
         kv_len = kv_len < 1 ? 0 : a.stride;
@@ -395,8 +395,13 @@ __global__ void __launch_bounds__(kGqaClusterThreads) gqa_cluster_kernel(const G
     // leader: gathered partial accumulators [rank][head][dim], after the rows
     // (same offset in every CTA of the launch, so mapa finds the leader's copy)
     float* gat_acc = reinterpret_cast<float*>(kv_rows + 2 * static_cast<size_t>(a.chunk) * kRowPad);
-    // rows this CTA may read: the chunk, clipped to the cache's row extent
-    const int avail = min(a.chunk, max(0, a.stride - t0));
+    // rows this CTA may read: the chunk, clipped to the cache's row extent;
+    // with per-sequence lengths (batched decode, where most sequences are far
+    // shorter than the cache) also clipped to that sequence's length, at the
+    // price of one dependent load before the K/V loads
+    int row_end = a.stride;
+    if (a.kv_len_per_batch && a.kv_len_dev != nullptr) row_end = min(row_end, max(0, a.kv_len_dev[b]));
+    const int avail = min(a.chunk, max(0, row_end - t0));
 
     // ---- one global round trip: q fragments, the device length, and every
     // K/V row of the chunk (16-byte loads, 16 per row, into padded rows)
@@ -410,7 +415,7 @@ __global__ void __launch_bounds__(kGqaClusterThreads) gqa_cluster_kernel(const G
             qa[s8][1] = g < G ? qw[8 * s8 + t + 4] : 0u;
         }
     }
-    int kv_len = a.kv_len_dev != nullptr ? *a.kv_len_dev : a.kv_len;
+    int kv_len = a.kv_len_dev != nullptr ? a.kv_len_dev[a.kv_len_per_batch ? b : 0] : a.kv_len;
     {
         const uint4* kg = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.kcache) + kv_base +
                                                          static_cast<int64_t>(t0) * kHeadDim);

@@ -97,6 +97,7 @@ struct GqaArgs {
     float* partials;     // [B][q_heads][nsplit][d + 2]
     int* counters;       // [B * kv_heads], zero between launches (null: separate combine)
     const int32_t* kv_len_dev;  // null: use kv_len
+    int kv_len_per_batch;       // 1: kv_len_dev is an array [batch] (batched decode), 0: one shared length
     int kv_len;
     int stride;
     int batch, q_heads, kv_heads, head_dim;
@@ -182,6 +183,43 @@ struct PersistLaunch {
     void* scratch;
     int* err;
 };
+// ---- batched decode (batched.cu) ----------------------------------------------
+// NF4 (weight_type 0) or bf16 (1) weights [rows][K] times bf16 activations
+// [n_pad][K] (rows >= batch zero) on the tcgen05 tensor cores: fp32 split-K
+// partials[(split * total_rows + row_offset + r) * n_pad + b].
+int batch_gemm_ksplit(int rows, int K);
+cudaError_t batch_gemm(int weight_type, const void* weight, const float* absmax, int rows, int K, const uint16_t* x,
+                       int n_pad, int ksplit, float* partials, int row_offset, int total_rows, int* err,
+                       cudaStream_t s);
+cudaError_t batch_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* out, int batch, int H, float eps,
+                          cudaStream_t s);
+struct BatchQkv {
+    const float* partials;  // [ksplit][(qh + 2 kvh) * hd][n_pad]
+    int ksplit, n_pad, batch;
+    int q_heads, kv_heads, head_dim, cap, max_pos;
+    const uint16_t* q_bias;
+    const uint16_t* k_bias;
+    const uint16_t* v_bias;
+    const uint16_t* rope_cos;
+    const uint16_t* rope_sin;
+    const int32_t* pos;  // [batch]
+    uint16_t* q_out;     // [batch][qh][hd]
+    uint16_t* kcache;    // [batch][kvh][cap][hd]
+    uint16_t* vcache;
+    int* err;
+};
+cudaError_t batch_qkv_epilogue(const BatchQkv& q, cudaStream_t s);
+cudaError_t batch_residual(const float* partials, int ksplit, int rows, int n_pad, int batch, uint16_t* x,
+                           cudaStream_t s);
+cudaError_t batch_swiglu(const float* partials, int ksplit, int inter, int n_pad, int batch, uint16_t* h,
+                         cudaStream_t s);
+int batch_argmax_workspace_floats(int batch);
+cudaError_t batch_argmax_advance(const float* partials, int ksplit, int vocab, int n_pad, int batch, float* ws,
+                                 int32_t* state, int32_t* history, int history_len, cudaStream_t s);
+cudaError_t batch_embedding(const uint16_t* emb, const int32_t* state, uint16_t* x, int batch, int H, int vocab,
+                            int* err, cudaStream_t s);
+cudaError_t batch_state_views(const int32_t* state, int batch, int32_t* pos, int32_t* kv_len, cudaStream_t s);
+
 int64_t decode_persistent_scratch_bytes(const PersistDims& d, int sms);
 const char* decode_persistent_check(const PersistDims& d, int sms);
 cudaError_t decode_layers_persistent(const PersistLaunch& p, cudaStream_t stream);

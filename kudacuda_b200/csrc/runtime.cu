@@ -1035,6 +1035,218 @@ int kudacuda_sm100_decode_layers_persistent(void* raw, uint64_t layer_table, int
     return finish(h, "decode_layers_kernel", kc::decode_layers_persistent(p, S(stream)));
 }
 
+// ---------------------------------------------------------------- batched decode
+namespace {
+bool npad_ok(int64_t n_pad) { return n_pad == 16 || n_pad == 32 || n_pad == 64; }
+}  // namespace
+
+int64_t kudacuda_sm100_batch_gemm_ksplit(int64_t rows, int64_t k) {
+    if (rows < 1 || k < 64 || k % 64 != 0 || rows > (1 << 24) || k > (1 << 20)) return -1;
+    return kc::batch_gemm_ksplit(static_cast<int>(rows), static_cast<int>(k));
+}
+
+int kudacuda_sm100_batch_gemm(void* raw, int weight_type, uint64_t weight, uint64_t absmax, int64_t rows, int64_t k,
+                              uint64_t x, int64_t n_pad, int64_t ksplit, uint64_t partials, int64_t row_offset,
+                              int64_t total_rows, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_gemm")) return 1;
+    if (weight == 0 || x == 0 || partials == 0 || (weight_type == 0 && absmax == 0) ||
+        (weight_type != 0 && weight_type != 1) || rows < 1 || rows > (1 << 24) || k < 64 || k % 64 != 0 ||
+        k > (1 << 20) || !npad_ok(n_pad) || ksplit < 1 || ksplit > k / 64 || row_offset < 0 ||
+        total_rows > (1 << 24) || row_offset + rows > total_rows) {
+        h->set_error("sm100_batch_gemm requires weight_type 0 (NF4 + absmax) or 1 (bf16), K % 64 == 0, n_pad in "
+                     "{16, 32, 64}, 1 <= ksplit <= K/64, row_offset + rows <= total_rows, non-null pointers");
+        return 1;
+    }
+    return finish(h, "nf4_gemm_tc_kernel",
+                  kc::batch_gemm(weight_type, P<const void>(weight), P<const float>(absmax), static_cast<int>(rows),
+                                 static_cast<int>(k), P<const uint16_t>(x), static_cast<int>(n_pad),
+                                 static_cast<int>(ksplit), P<float>(partials), static_cast<int>(row_offset),
+                                 static_cast<int>(total_rows), h->err_word, S(stream)));
+}
+
+int kudacuda_sm100_batch_rmsnorm(void* raw, uint64_t x, uint64_t weight, uint64_t out, int64_t batch, int64_t hidden,
+                                 float eps, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_rmsnorm")) return 1;
+    if (x == 0 || weight == 0 || out == 0 || batch < 1 || batch > 64 || hidden < 8 || hidden % 8 != 0 ||
+        hidden > (1 << 20) || !(eps > 0.0F)) {
+        h->set_error("sm100_batch_rmsnorm requires non-null pointers, 1 <= batch <= 64, hidden % 8 == 0, eps > 0");
+        return 1;
+    }
+    return finish(h, "batch_rmsnorm_kernel",
+                  kc::batch_rmsnorm(P<const uint16_t>(x), P<const uint16_t>(weight), P<uint16_t>(out),
+                                    static_cast<int>(batch), static_cast<int>(hidden), eps, S(stream)));
+}
+
+int kudacuda_sm100_batch_qkv_rope(void* raw, uint64_t partials, int64_t ksplit, int64_t n_pad, int64_t batch,
+                                  int64_t q_heads, int64_t kv_heads, int64_t head_dim, uint64_t q_bias, uint64_t k_bias,
+                                  uint64_t v_bias, uint64_t rope_cos, uint64_t rope_sin, int64_t max_pos, uint64_t pos,
+                                  uint64_t q_out, uint64_t key_cache, uint64_t value_cache, int64_t kv_capacity,
+                                  uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_qkv_rope")) return 1;
+    if (partials == 0 || rope_cos == 0 || rope_sin == 0 || pos == 0 || q_out == 0 || key_cache == 0 ||
+        value_cache == 0 || ksplit < 1 || ksplit > 64 || !npad_ok(n_pad) || batch < 1 || batch > n_pad ||
+        q_heads < 1 || kv_heads < 1 || head_dim < 2 || head_dim % 2 != 0 || head_dim > 512 || max_pos < 1 ||
+        kv_capacity < 1) {
+        h->set_error("sm100_batch_qkv_rope requires non-null pointers (biases may be null), 1 <= batch <= n_pad, "
+                     "n_pad in {16, 32, 64}, even head_dim");
+        return 1;
+    }
+    kc::BatchQkv q;
+    memset(&q, 0, sizeof(q));
+    q.partials = P<const float>(partials);
+    q.ksplit = static_cast<int>(ksplit);
+    q.n_pad = static_cast<int>(n_pad);
+    q.batch = static_cast<int>(batch);
+    q.q_heads = static_cast<int>(q_heads);
+    q.kv_heads = static_cast<int>(kv_heads);
+    q.head_dim = static_cast<int>(head_dim);
+    q.cap = static_cast<int>(kv_capacity);
+    q.max_pos = static_cast<int>(max_pos);
+    q.q_bias = P<const uint16_t>(q_bias);
+    q.k_bias = P<const uint16_t>(k_bias);
+    q.v_bias = P<const uint16_t>(v_bias);
+    q.rope_cos = P<const uint16_t>(rope_cos);
+    q.rope_sin = P<const uint16_t>(rope_sin);
+    q.pos = P<const int32_t>(pos);
+    q.q_out = P<uint16_t>(q_out);
+    q.kcache = P<uint16_t>(key_cache);
+    q.vcache = P<uint16_t>(value_cache);
+    q.err = h->err_word;
+    return finish(h, "batch_qkv_epilogue_kernel", kc::batch_qkv_epilogue(q, S(stream)));
+}
+
+int kudacuda_sm100_batch_residual(void* raw, uint64_t partials, int64_t ksplit, int64_t rows, int64_t n_pad,
+                                  int64_t batch, uint64_t x, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_residual")) return 1;
+    if (partials == 0 || x == 0 || ksplit < 1 || ksplit > 64 || rows < 1 || rows > (1 << 24) || !npad_ok(n_pad) ||
+        batch < 1 || batch > n_pad) {
+        h->set_error("sm100_batch_residual requires non-null pointers, 1 <= batch <= n_pad, n_pad in {16, 32, 64}");
+        return 1;
+    }
+    return finish(h, "batch_residual_kernel",
+                  kc::batch_residual(P<const float>(partials), static_cast<int>(ksplit), static_cast<int>(rows),
+                                     static_cast<int>(n_pad), static_cast<int>(batch), P<uint16_t>(x), S(stream)));
+}
+
+int kudacuda_sm100_batch_swiglu(void* raw, uint64_t partials, int64_t ksplit, int64_t intermediate, int64_t n_pad,
+                                int64_t batch, uint64_t out, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_swiglu")) return 1;
+    if (partials == 0 || out == 0 || ksplit < 1 || ksplit > 64 || intermediate < 1 || intermediate > (1 << 23) ||
+        !npad_ok(n_pad) || batch < 1 || batch > n_pad) {
+        h->set_error("sm100_batch_swiglu requires non-null pointers, 1 <= batch <= n_pad, n_pad in {16, 32, 64}");
+        return 1;
+    }
+    return finish(h, "batch_swiglu_kernel",
+                  kc::batch_swiglu(P<const float>(partials), static_cast<int>(ksplit), static_cast<int>(intermediate),
+                                   static_cast<int>(n_pad), static_cast<int>(batch), P<uint16_t>(out), S(stream)));
+}
+
+int64_t kudacuda_sm100_batch_argmax_workspace_bytes(int64_t batch) {
+    if (batch < 1 || batch > 64) return -1;
+    return static_cast<int64_t>(kc::batch_argmax_workspace_floats(static_cast<int>(batch))) * 4;
+}
+
+int kudacuda_sm100_batch_argmax_advance(void* raw, uint64_t partials, int64_t ksplit, int64_t vocab, int64_t n_pad,
+                                        int64_t batch, uint64_t workspace, int64_t workspace_bytes, uint64_t state,
+                                        uint64_t history, int64_t history_len, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_argmax_advance")) return 1;
+    if (partials == 0 || workspace == 0 || state == 0 || ksplit < 1 || ksplit > 64 || vocab < 1 ||
+        vocab > (1 << 24) || !npad_ok(n_pad) || batch < 1 || batch > n_pad || history_len < 0 ||
+        history_len > (1 << 24) || (history != 0 && history_len < 1)) {
+        h->set_error("sm100_batch_argmax_advance requires non-null pointers (history may be null), "
+                     "1 <= batch <= n_pad, n_pad in {16, 32, 64}");
+        return 1;
+    }
+    if (workspace_bytes < kudacuda_sm100_batch_argmax_workspace_bytes(batch)) {
+        h->set_error("sm100_batch_argmax_advance workspace is smaller than kudacuda_sm100_batch_argmax_workspace_bytes()");
+        return 1;
+    }
+    return finish(h, "batch_argmax_stage1/2",
+                  kc::batch_argmax_advance(P<const float>(partials), static_cast<int>(ksplit), static_cast<int>(vocab),
+                                           static_cast<int>(n_pad), static_cast<int>(batch), P<float>(workspace),
+                                           P<int32_t>(state), P<int32_t>(history), static_cast<int>(history_len),
+                                           S(stream)));
+}
+
+int kudacuda_sm100_batch_embedding(void* raw, uint64_t embedding, uint64_t state, uint64_t x, int64_t batch,
+                                   int64_t hidden, int64_t vocab, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_embedding")) return 1;
+    if (embedding == 0 || state == 0 || x == 0 || batch < 1 || batch > 64 || hidden < 8 || hidden % 8 != 0 ||
+        hidden > (1 << 20) || vocab < 1 || vocab > (1 << 24)) {
+        h->set_error("sm100_batch_embedding requires non-null pointers, 1 <= batch <= 64, hidden % 8 == 0");
+        return 1;
+    }
+    return finish(h, "batch_embedding_kernel",
+                  kc::batch_embedding(P<const uint16_t>(embedding), P<const int32_t>(state), P<uint16_t>(x),
+                                      static_cast<int>(batch), static_cast<int>(hidden), static_cast<int>(vocab),
+                                      h->err_word, S(stream)));
+}
+
+int kudacuda_sm100_batch_state_views(void* raw, uint64_t state, int64_t batch, uint64_t pos, uint64_t kv_len,
+                                     uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_state_views")) return 1;
+    if (state == 0 || pos == 0 || kv_len == 0 || batch < 1 || batch > 64) {
+        h->set_error("sm100_batch_state_views requires non-null pointers and 1 <= batch <= 64");
+        return 1;
+    }
+    return finish(h, "batch_state_views_kernel",
+                  kc::batch_state_views(P<const int32_t>(state), static_cast<int>(batch), P<int32_t>(pos),
+                                        P<int32_t>(kv_len), S(stream)));
+}
+
+int kudacuda_sm100_gqa_decode_batch(void* raw, uint64_t query, uint64_t key_cache, uint64_t value_cache,
+                                    uint64_t output, uint64_t workspace, int64_t workspace_bytes, uint64_t tickets,
+                                    uint64_t kv_len_array, int64_t batch_size, int64_t kv_stride, int64_t query_heads,
+                                    int64_t kv_heads, int64_t head_dim, float scale, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_gqa_decode_batch")) return 1;
+    if (query == 0 || key_cache == 0 || value_cache == 0 || output == 0 || workspace == 0 || tickets == 0 ||
+        kv_len_array == 0) {
+        h->set_error("sm100_gqa_decode_batch requires non-null device pointers");
+        return 1;
+    }
+    const int64_t group = kv_heads > 0 ? query_heads / kv_heads : 0;
+    if (batch_size < 1 || batch_size > 4096 || kv_heads < 1 || query_heads % kv_heads != 0 ||
+        !(group == 1 || group == 2 || group == 4 || group == 8) || head_dim != 128 || kv_stride < 1 ||
+        kv_stride > (1 << 20) || !(scale > 0.0F)) {
+        h->set_error("sm100_gqa_decode_batch requires head_dim=128, query_heads/kv_heads in {1,2,4,8}, positive scale");
+        return 1;
+    }
+    kc::GqaArgs a;
+    memset(&a, 0, sizeof(a));
+    a.q = P<const void>(query);
+    a.kcache = P<const void>(key_cache);
+    a.vcache = P<const void>(value_cache);
+    a.out = P<void>(output);
+    a.partials = P<float>(workspace);
+    a.counters = P<int>(tickets);
+    a.kv_len_dev = P<const int32_t>(kv_len_array);
+    a.kv_len_per_batch = 1;
+    a.kv_len = static_cast<int>(kv_stride);
+    a.stride = static_cast<int>(kv_stride);
+    a.batch = static_cast<int>(batch_size);
+    a.q_heads = static_cast<int>(query_heads);
+    a.kv_heads = static_cast<int>(kv_heads);
+    a.head_dim = 128;
+    a.scale = scale;
+    a.err = h->err_word;
+    kc::gqa_plan_splits(static_cast<int>(kv_stride), a.batch, a.kv_heads, 0, &a.chunk, &a.nsplit);
+    const size_t need = kc::gqa_partials_floats(a.batch, a.q_heads, a.nsplit, 128) * sizeof(float);
+    if (workspace_bytes < static_cast<int64_t>(need)) {
+        h->set_error("sm100_gqa_decode_batch workspace is smaller than kudacuda_sm100_gqa_workspace_bytes()");
+        return 1;
+    }
+    return finish(h, "gqa decode (per-sequence lengths)", kc::gqa_decode(a, kc::kBF16, S(stream)));
+}
+
 const char* kudacuda_sm100_target_arch(void) { return "sm_100a"; }
 
 }  // extern "C"

@@ -711,3 +711,284 @@ def greedy_generate(plan: StaticDecodePlan, prompt: list[int], new_tokens: int, 
     plan.generate_device(new_tokens - 1, stream)
     stream.synchronize()
     return [int(t) for t in plan.buffers.history[n:n + new_tokens].cpu().tolist()]
+
+
+# ---------------------------------------------------------------------- batched decode
+@dataclass
+class BatchedBuffers:
+    state: Any  # int32 [B, 4]: token, position, kv_len, (pad) per sequence
+    pos: Any  # int32 [B] (the positions, for the RoPE epilogue)
+    kv_len: Any  # int32 [B] (the lengths, for attention)
+    x: Any  # bf16 [B, hidden] residual stream
+    xn: Any  # bf16 [n_pad, hidden] normalised activations (rows >= B stay zero)
+    q: Any  # bf16 [B, q_heads * d]
+    attn: Any  # bf16 [n_pad, q_heads * d]
+    h: Any  # bf16 [n_pad, intermediate]
+    partials: Any  # f32 split-K partial sums, shared by every GEMM of the step
+    kcache: Any  # bf16 [layers, B, kv_heads, cap, d]
+    vcache: Any
+    gqa_ws: Any
+    gqa_tickets: Any
+    arg_ws: Any
+    history: Any  # int32 [B, max_tokens]
+    rope_cos: Any
+    rope_sin: Any
+
+
+class BatchedDecodePlan:
+    """Fixed-shape decode step for B independent sequences (each with its own
+    position and KV length) on one device.  Every projection is one tensor-core
+    GEMM over the padded batch (``kudacuda_sm100_batch_gemm``: NF4 dequantised
+    to bf16 in shared memory, tcgen05 MMA, fp32 accumulator in TMEM) followed
+    by a small epilogue; q|k|v and gate|up are concatenated once at plan build
+    so each is one GEMM.  The lm_head is the same GEMM over the bf16 tied
+    embedding (or the NF4 lm_head), then a per-sequence argmax that advances
+    each sequence's state.  The step is captured into the handle's CUDA graph.
+
+    Arithmetic per sequence is the Transformers + bitsandbytes batched forward
+    (weights dequantised to bf16, bf16 matmul with fp32 accumulation); the
+    reference's sidecar admits batch 1 only (python/kudacuda_sidecar.py:145-153)."""
+
+    TACTIC = "decode_step_sm100_batched_tcgen05_v1"
+
+    def __init__(self, bridge: KudaCudaBridge, weights: ModelWeights, *, batch: int, kv_bucket: int = 2048,
+                 max_tokens: Optional[int] = None, device: Any = "cuda:0", torch_module: Any = None) -> None:
+        if torch_module is None:
+            import torch as torch_module
+        self.torch = torch = torch_module
+        self.bridge = bridge
+        self.weights = weights
+        self.config = c = weights.config
+        self.device = device
+        self.batch = B = int(batch)
+        if not 1 <= B <= 64:
+            raise ValueError("batched decode supports 1..64 sequences")
+        self.n_pad = 16 if B <= 16 else (32 if B <= 32 else 64)
+        self.kv_bucket = cap = int(kv_bucket)
+        L0 = weights.layers[0]
+        self.q_heads = L0.q.rows // c.head_dim
+        self.kv_heads = L0.k.rows // c.head_dim
+        self.inter = L0.gate.rows
+        d = c.head_dim
+        max_tokens = int(max_tokens or cap)
+        bf16 = torch.bfloat16
+        # q|k|v and gate|up concatenated by rows (NF4 rows and their absmax concatenate)
+        self.qkv: list[NF4Linear] = []
+        self.gu: list[NF4Linear] = []
+        for L in weights.layers:
+            self.qkv.append(NF4Linear(torch.cat([L.q.packed, L.k.packed, L.v.packed]),
+                                      torch.cat([L.q.absmax, L.k.absmax, L.v.absmax]),
+                                      L.q.rows + L.k.rows + L.v.rows, L.q.k))
+            self.gu.append(NF4Linear(torch.cat([L.gate.packed, L.up.packed]), torch.cat([L.gate.absmax, L.up.absmax]),
+                                     L.gate.rows + L.up.rows, L.gate.k))
+        self.qkv_rows = self.qkv[0].rows
+        ks = bridge.batch_gemm_ksplit
+        self.ks_qkv = ks(self.qkv_rows, c.hidden)
+        self.ks_o = ks(c.hidden, L0.o.k)
+        self.ks_gu = ks(2 * self.inter, c.hidden)
+        self.ks_dn = ks(c.hidden, self.inter)
+        self.ks_lm = ks(c.vocab, c.hidden)
+        part = max(self.ks_qkv * self.qkv_rows, self.ks_o * c.hidden, self.ks_gu * 2 * self.inter,
+                   self.ks_dn * c.hidden, self.ks_lm * c.vocab) * self.n_pad
+        ws, tickets, _ = bridge.gqa_workspace(batch=B, query_heads=self.q_heads, kv_heads=self.kv_heads,
+                                              kv_extent=cap, device=device, torch_module=torch)
+        cos, sin = rope_tables(torch, max(cap, max_tokens) + 1, d, c.rope_theta, device)
+        self.buffers = BatchedBuffers(
+            state=torch.zeros((B, 4), dtype=torch.int32, device=device),
+            pos=torch.zeros(B, dtype=torch.int32, device=device),
+            kv_len=torch.zeros(B, dtype=torch.int32, device=device),
+            x=torch.zeros((B, c.hidden), dtype=bf16, device=device),
+            xn=torch.zeros((self.n_pad, c.hidden), dtype=bf16, device=device),
+            q=torch.zeros((B, self.q_heads * d), dtype=bf16, device=device),
+            attn=torch.zeros((self.n_pad, self.q_heads * d), dtype=bf16, device=device),
+            h=torch.zeros((self.n_pad, self.inter), dtype=bf16, device=device),
+            partials=torch.zeros(part, dtype=torch.float32, device=device),
+            kcache=torch.zeros((c.layers, B, self.kv_heads, cap, d), dtype=bf16, device=device),
+            vcache=torch.zeros((c.layers, B, self.kv_heads, cap, d), dtype=bf16, device=device),
+            gqa_ws=ws,
+            gqa_tickets=tickets,
+            arg_ws=torch.zeros(bridge.batch_argmax_workspace_bytes(B) // 4, dtype=torch.float32, device=device),
+            history=torch.zeros((B, max_tokens), dtype=torch.int32, device=device),
+            rope_cos=cos,
+            rope_sin=sin,
+        )
+        self.graph_plan = KudaCudaGraphPlan(bridge)
+        self.graph_key: Optional[DecodeGraphKey] = None
+        self.launches_per_step = 0
+
+    @property
+    def captured(self) -> bool:
+        return self.graph_plan.captured
+
+    def make_graph_key(self) -> DecodeGraphKey:
+        b, w, c = self.buffers, self.weights, self.config
+        ptrs = [t.data_ptr() for t in (b.state, b.pos, b.kv_len, b.x, b.xn, b.q, b.attn, b.h, b.partials, b.kcache,
+                                       b.vcache, b.gqa_ws, b.gqa_tickets, b.arg_ws, b.history, b.rope_cos, b.rope_sin,
+                                       w.embedding, w.final_norm)]
+        for li, L in enumerate(w.layers):
+            ptrs += [L.in_norm.data_ptr(), L.post_norm.data_ptr()]
+            for lin in (self.qkv[li], L.o, self.gu[li], L.down):
+                ptrs += [lin.packed.data_ptr(), lin.absmax.data_ptr()]
+            ptrs += [0 if t is None else t.data_ptr() for t in (L.q_bias, L.k_bias, L.v_bias)]
+        if w.lm_head is not None:
+            ptrs += [w.lm_head.packed.data_ptr(), w.lm_head.absmax.data_ptr()]
+        d = c.head_dim
+        return DecodeGraphKey(
+            device_id=int(self.torch.device(self.device).index or 0),
+            tactic_name=self.TACTIC,
+            layer_count=c.layers,
+            query_shape=(self.batch, self.q_heads, 1, d),
+            key_shape=(self.batch, self.kv_heads, self.kv_bucket, d),
+            value_shape=(self.batch, self.kv_heads, self.kv_bucket, d),
+            output_shape=(self.batch, self.q_heads, 1, d),
+            kv_bucket=self.kv_bucket,
+            pointers=tuple(int(p) for p in ptrs),
+            model_fingerprint=c.name,
+            dtype="bfloat16",
+            quantization="nf4-blocksize64-fp32absmax",
+        )
+
+    def _gemm(self, lin: NF4Linear, x: Any, ksplit: int, sp: int) -> None:
+        self.bridge.dispatch_batch_gemm(lin.packed, lin.absmax, x, self.buffers.partials, weight_type=0,
+                                        rows=lin.rows, k=lin.k, n_pad=self.n_pad, ksplit=ksplit, stream_ptr=sp)
+
+    def record(self, stream_ptr: int) -> int:
+        """Enqueue one batched decode step; returns the number of kernels."""
+
+        b, c, w, br = self.buffers, self.config, self.weights, self.bridge
+        sp, B, npad = stream_ptr, self.batch, self.n_pad
+        d = c.head_dim
+        scale = 1.0 / math.sqrt(d)
+        br.dispatch_batch_embedding(w.embedding, b.state, b.x, batch=B, hidden=c.hidden, vocab=c.vocab, stream_ptr=sp)
+        br.dispatch_batch_state_views(b.state, b.pos, b.kv_len, batch=B, stream_ptr=sp)
+        n = 2
+        for li, L in enumerate(w.layers):
+            br.dispatch_batch_rmsnorm(b.x, L.in_norm, b.xn, batch=B, hidden=c.hidden, epsilon=c.eps, stream_ptr=sp)
+            self._gemm(self.qkv[li], b.xn, self.ks_qkv, sp)
+            br.dispatch_batch_qkv_rope(b.partials, L.q_bias, L.k_bias, L.v_bias, b.rope_cos, b.rope_sin, b.pos, b.q,
+                                       b.kcache[li], b.vcache[li], ksplit=self.ks_qkv, n_pad=npad, batch=B,
+                                       q_heads=self.q_heads, kv_heads=self.kv_heads, head_dim=d,
+                                       max_pos=int(b.rope_cos.shape[0]), kv_capacity=self.kv_bucket, stream_ptr=sp)
+            br.dispatch_gqa_decode_batch(b.q, b.kcache[li], b.vcache[li], b.attn, b.gqa_ws, b.gqa_tickets, b.kv_len,
+                                         batch=B, kv_stride=self.kv_bucket, query_heads=self.q_heads,
+                                         kv_heads=self.kv_heads, head_dim=d, scale=scale, stream_ptr=sp)
+            self._gemm(L.o, b.attn, self.ks_o, sp)
+            br.dispatch_batch_residual(b.partials, b.x, ksplit=self.ks_o, rows=c.hidden, n_pad=npad, batch=B,
+                                       stream_ptr=sp)
+            br.dispatch_batch_rmsnorm(b.x, L.post_norm, b.xn, batch=B, hidden=c.hidden, epsilon=c.eps, stream_ptr=sp)
+            self._gemm(self.gu[li], b.xn, self.ks_gu, sp)
+            br.dispatch_batch_swiglu(b.partials, b.h, ksplit=self.ks_gu, intermediate=self.inter, n_pad=npad, batch=B,
+                                     stream_ptr=sp)
+            self._gemm(L.down, b.h, self.ks_dn, sp)
+            br.dispatch_batch_residual(b.partials, b.x, ksplit=self.ks_dn, rows=c.hidden, n_pad=npad, batch=B,
+                                       stream_ptr=sp)
+            n += 11
+        br.dispatch_batch_rmsnorm(b.x, w.final_norm, b.xn, batch=B, hidden=c.hidden, epsilon=c.eps, stream_ptr=sp)
+        if w.lm_head is None:
+            br.dispatch_batch_gemm(w.embedding, None, b.xn, b.partials, weight_type=1, rows=c.vocab, k=c.hidden,
+                                   n_pad=npad, ksplit=self.ks_lm, stream_ptr=sp)
+        else:
+            self._gemm(w.lm_head, b.xn, self.ks_lm, sp)
+        br.dispatch_batch_argmax_advance(b.partials, b.arg_ws, b.state, b.history, ksplit=self.ks_lm, vocab=c.vocab,
+                                         n_pad=npad, batch=B, stream_ptr=sp)
+        n += 4
+        self.launches_per_step = n
+        return n
+
+    # ------------------------------------------------------------------ state
+    def set_state(self, tokens: Any, positions: Any, stream: Any = None) -> None:
+        """Write per-sequence {token, position, kv_len = position + 1} after all queued work."""
+
+        torch = self.torch
+        if stream is not None:
+            stream.synchronize()
+        torch.cuda.synchronize(self.device)
+        tok = torch.as_tensor(list(tokens), dtype=torch.int32)
+        pos = torch.as_tensor(list(positions), dtype=torch.int32)
+        if tok.numel() != self.batch or pos.numel() != self.batch:
+            raise ValueError("one token and one position per sequence")
+        self.buffers.state.copy_(torch.stack([tok, pos, pos + 1, torch.zeros_like(pos)], dim=1))
+        torch.cuda.synchronize(self.device)
+
+    def reset_cache(self) -> None:
+        self.torch.cuda.synchronize(self.device)
+        self.buffers.kcache.zero_()
+        self.buffers.vcache.zero_()
+        self.torch.cuda.synchronize(self.device)
+
+    # ------------------------------------------------------------------ graph
+    def capture(self, stream: Any) -> None:
+        """Warm every kernel once eagerly on a valid state (token 0 at position
+        0 for every sequence), restore the state, capture one step."""
+
+        torch = self.torch
+        sp = int(stream.cuda_stream)
+        saved_state = self.buffers.state.clone()
+        saved_hist = self.buffers.history.clone()
+        self.buffers.state.zero_()
+        self.buffers.state[:, 2] = 1
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.stream(stream):
+            self.record(sp)
+        stream.synchronize()
+        word = self.bridge.error_word(clear=True)
+        if word:
+            raise NativeCudaError(f"batched decode step raised device error word {word:#x}")
+        self.buffers.state.copy_(saved_state)
+        self.buffers.history.copy_(saved_hist)
+        torch.cuda.synchronize(self.device)
+        self.bridge.reset_graph()
+        self.graph_plan.invalidate()
+        key = self.make_graph_key()
+        self.graph_plan.begin_capture(key, stream_ptr=sp)
+        try:
+            self.record(sp)
+        except Exception:
+            try:
+                self.graph_plan.end_capture(key, stream_ptr=sp)
+            finally:
+                self.graph_plan.invalidate()
+                self.bridge.reset_graph()
+            raise
+        self.graph_plan.end_capture(key, stream_ptr=sp)
+        self.graph_key = key
+
+    def replay(self, stream: Any) -> None:
+        if self.graph_key is None:
+            raise NativeCudaError("no captured batched decode graph")
+        self.graph_plan.replay(self.graph_key, stream_ptr=int(stream.cuda_stream))
+
+    def step_tokens(self, tokens: Any, positions: Any, stream: Any) -> list[int]:
+        """One step driven from the host (prompts, teacher forcing): per-sequence
+        token and position in, every sequence's next token out."""
+
+        self.set_state(tokens, positions, stream)
+        self.replay(stream)
+        stream.synchronize()
+        return [int(t) for t in self.buffers.state[:, 0].cpu().tolist()]
+
+
+def batched_greedy_generate(plan: BatchedDecodePlan, prompts: list[list[int]], new_tokens: int,
+                            stream: Any) -> list[list[int]]:
+    """Ragged prompts through batched steps: while a sequence is inside its
+    prompt its next prompt token is forced, afterwards it continues from its
+    own greedy token.  Returns ``new_tokens`` generated tokens per sequence."""
+
+    if len(prompts) != plan.batch:
+        raise ValueError("one prompt per sequence")
+    plan.reset_cache()
+    lens = [len(p) for p in prompts]
+    total = max(lens) + new_tokens
+    if total > plan.kv_bucket:
+        raise ValueError("generation exceeds the KV bucket")
+    seqs = [list(p) for p in prompts]
+    cur = [p[0] for p in prompts]
+    for t in range(total - 1):
+        nxt = plan.step_tokens(cur, [t] * plan.batch, stream)
+        for i in range(plan.batch):
+            if t + 1 < lens[i]:
+                cur[i] = prompts[i][t + 1]
+            else:
+                seqs[i].append(nxt[i])
+                cur[i] = nxt[i]
+    return [s[lens[i]:lens[i] + new_tokens] for i, s in enumerate(seqs)]

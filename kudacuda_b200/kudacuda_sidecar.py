@@ -1133,6 +1133,97 @@ class KudaCudaBridge:
                    int(head_dim), int(intermediate), int(kv_capacity), float(epsilon), float(scale),
                    _normalize_cuda_handle(stream_ptr))
 
+    # ---------------------------------------------------------------- batched decode (B sequences per step)
+    def batch_gemm_ksplit(self, rows: int, k: int) -> int:
+        n = int(self.lib.kudacuda_sm100_batch_gemm_ksplit(int(rows), int(k)))
+        if n < 1:
+            raise ValueError(f"batch_gemm_ksplit: unsupported shape rows={rows} k={k}")
+        return n
+
+    def dispatch_batch_gemm(self, weight: Any, absmax: Any, x: Any, partials: Any, *, weight_type: int, rows: int,
+                            k: int, n_pad: int, ksplit: int, row_offset: int = 0, total_rows: int | None = None,
+                            stream_ptr: int) -> None:
+        """fp32 split-K partials of W . x^T for a padded batch on the tensor cores
+        (weight_type 0: NF4 + absmax, 1: bf16)."""
+
+        total = int(rows if total_rows is None else total_rows)
+        if int(x.numel()) != int(n_pad) * int(k):
+            raise ValueError("x must be [n_pad, k]")
+        if int(partials.numel()) < int(ksplit) * total * int(n_pad):
+            raise ValueError("partials must hold ksplit * total_rows * n_pad floats")
+        self._call("kudacuda_sm100_batch_gemm", int(weight_type), self._tensor_pointer(weight, "weight"),
+                   self._optional_pointer(absmax, "absmax"), int(rows), int(k), self._tensor_pointer(x, "x"),
+                   int(n_pad), int(ksplit), self._tensor_pointer(partials, "partials"), int(row_offset), total,
+                   _normalize_cuda_handle(stream_ptr))
+
+    def dispatch_batch_rmsnorm(self, x: Any, weight: Any, out: Any, *, batch: int, hidden: int, epsilon: float,
+                               stream_ptr: int) -> None:
+        self._call("kudacuda_sm100_batch_rmsnorm", self._tensor_pointer(x, "x"), self._tensor_pointer(weight, "weight"),
+                   self._tensor_pointer(out, "out"), int(batch), int(hidden), float(epsilon),
+                   _normalize_cuda_handle(stream_ptr))
+
+    def dispatch_batch_qkv_rope(self, partials: Any, q_bias: Any, k_bias: Any, v_bias: Any, rope_cos: Any,
+                                rope_sin: Any, pos: Any, q_out: Any, key_cache: Any, value_cache: Any, *, ksplit: int,
+                                n_pad: int, batch: int, q_heads: int, kv_heads: int, head_dim: int, max_pos: int,
+                                kv_capacity: int, stream_ptr: int) -> None:
+        self._call("kudacuda_sm100_batch_qkv_rope", self._tensor_pointer(partials, "partials"), int(ksplit), int(n_pad),
+                   int(batch), int(q_heads), int(kv_heads), int(head_dim), self._optional_pointer(q_bias, "q_bias"),
+                   self._optional_pointer(k_bias, "k_bias"), self._optional_pointer(v_bias, "v_bias"),
+                   self._tensor_pointer(rope_cos, "rope_cos"), self._tensor_pointer(rope_sin, "rope_sin"), int(max_pos),
+                   self._tensor_pointer(pos, "pos"), self._tensor_pointer(q_out, "q_out"),
+                   self._tensor_pointer(key_cache, "key_cache"), self._tensor_pointer(value_cache, "value_cache"),
+                   int(kv_capacity), _normalize_cuda_handle(stream_ptr))
+
+    def dispatch_batch_residual(self, partials: Any, x: Any, *, ksplit: int, rows: int, n_pad: int, batch: int,
+                                stream_ptr: int) -> None:
+        self._call("kudacuda_sm100_batch_residual", self._tensor_pointer(partials, "partials"), int(ksplit), int(rows),
+                   int(n_pad), int(batch), self._tensor_pointer(x, "x"), _normalize_cuda_handle(stream_ptr))
+
+    def dispatch_batch_swiglu(self, partials: Any, out: Any, *, ksplit: int, intermediate: int, n_pad: int,
+                              batch: int, stream_ptr: int) -> None:
+        self._call("kudacuda_sm100_batch_swiglu", self._tensor_pointer(partials, "partials"), int(ksplit),
+                   int(intermediate), int(n_pad), int(batch), self._tensor_pointer(out, "out"),
+                   _normalize_cuda_handle(stream_ptr))
+
+    def batch_argmax_workspace_bytes(self, batch: int) -> int:
+        n = int(self.lib.kudacuda_sm100_batch_argmax_workspace_bytes(int(batch)))
+        if n < 0:
+            raise ValueError(f"batch_argmax_workspace_bytes: unsupported batch {batch}")
+        return n
+
+    def dispatch_batch_argmax_advance(self, partials: Any, workspace: Any, state: Any, history: Any = None, *,
+                                      ksplit: int, vocab: int, n_pad: int, batch: int, stream_ptr: int) -> None:
+        hist_len = int(history.shape[-1]) if history is not None else 0
+        self._call("kudacuda_sm100_batch_argmax_advance", self._tensor_pointer(partials, "partials"), int(ksplit),
+                   int(vocab), int(n_pad), int(batch), self._tensor_pointer(workspace, "workspace"),
+                   int(workspace.numel()) * int(workspace.element_size()), self._tensor_pointer(state, "state"),
+                   self._optional_pointer(history, "history"), hist_len, _normalize_cuda_handle(stream_ptr))
+
+    def dispatch_batch_embedding(self, embedding: Any, state: Any, x: Any, *, batch: int, hidden: int, vocab: int,
+                                 stream_ptr: int) -> None:
+        self._call("kudacuda_sm100_batch_embedding", self._tensor_pointer(embedding, "embedding"),
+                   self._tensor_pointer(state, "state"), self._tensor_pointer(x, "x"), int(batch), int(hidden),
+                   int(vocab), _normalize_cuda_handle(stream_ptr))
+
+    def dispatch_batch_state_views(self, state: Any, pos: Any, kv_len: Any, *, batch: int, stream_ptr: int) -> None:
+        self._call("kudacuda_sm100_batch_state_views", self._tensor_pointer(state, "state"), int(batch),
+                   self._tensor_pointer(pos, "pos"), self._tensor_pointer(kv_len, "kv_len"),
+                   _normalize_cuda_handle(stream_ptr))
+
+    def dispatch_gqa_decode_batch(self, query: Any, key_cache: Any, value_cache: Any, output: Any, workspace: Any,
+                                  tickets: Any, kv_len: Any, *, batch: int, kv_stride: int, query_heads: int,
+                                  kv_heads: int, head_dim: int = 128, scale: float | None = None,
+                                  stream_ptr: int) -> None:
+        """Split-KV GQA decode of B sequences with per-sequence lengths kv_len (int32 [B])."""
+
+        sc = float(scale) if scale is not None else 1.0 / math.sqrt(head_dim)
+        self._call("kudacuda_sm100_gqa_decode_batch", self._tensor_pointer(query, "query"),
+                   self._tensor_pointer(key_cache, "key_cache"), self._tensor_pointer(value_cache, "value_cache"),
+                   self._tensor_pointer(output, "output"), self._tensor_pointer(workspace, "workspace"),
+                   int(workspace.numel()) * int(workspace.element_size()), self._tensor_pointer(tickets, "tickets"),
+                   self._tensor_pointer(kv_len, "kv_len"), int(batch), int(kv_stride), int(query_heads),
+                   int(kv_heads), int(head_dim), sc, _normalize_cuda_handle(stream_ptr))
+
     def error_word(self, *, clear: bool = True) -> int:
         word = ctypes.c_int(0)
         self._raise_if_failed(self.lib.kudacuda_sm100_error_word(self.engine_handle, ctypes.byref(word), int(clear)),

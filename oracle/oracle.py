@@ -356,3 +356,25 @@ def retile_nf4(mode: int, mats: list[tuple[np.ndarray, np.ndarray, int]], k: int
     for h in range(2):
         ab[:, :, h] = amax[(16 * np.arange(4)[None, :] + 8 * h + np.arange(8)[:, None])].transpose(2, 3, 0, 1)
     return codes.reshape(-1), ab.reshape(-1)
+
+
+# ---------------------------------------------------------------- batched decode GEMM
+def batch_gemm_ref(packed: np.ndarray, absmax: np.ndarray | None, rows: int, k: int, x_bits: np.ndarray,
+                   weight_type: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """Batched projection as Transformers runs it on bitsandbytes NF4 weights
+    for a batch (the reference itself projects one token at a time,
+    tests/nf4_tiled_gemv_smoke.cu:86-94): W is dequantised to bf16
+    (kernels/common/nf4_device.cuh:29-40 in fp32, rounded once), then
+    y[r][b] = sum_k W[r][k] * x[b][k], here exactly in float64.
+
+    weight_type 0: packed NF4 + absmax; 1: packed holds bf16 bits [rows][k].
+    x_bits: bf16 bits [n][k].  Returns (y [rows][n] float64, the sum of
+    |W[r][k] * x[b][k]| [rows][n], the scale an fp32-accumulation error bound
+    is relative to)."""
+
+    if weight_type == 0:
+        w = bf16_to_f32(bf16_bits(nf4_dequant(packed, absmax, rows * k))).reshape(rows, k).astype(np.float64)
+    else:
+        w = bf16_to_f32(np.asarray(packed, dtype=np.uint16)).reshape(rows, k).astype(np.float64)
+    x = bf16_to_f32(np.asarray(x_bits, dtype=np.uint16)).reshape(-1, k).astype(np.float64)
+    return w @ x.T, np.abs(w) @ np.abs(x).T

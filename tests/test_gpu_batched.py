@@ -1,0 +1,223 @@
+"""GPU parity of the batched decode path (B independent sequences per step),
+through the C ABI via the bridge.
+
+* the tcgen05 GEMM (kudacuda_sm100_batch_gemm) against the oracle's batched
+  projection (bf16-dequantised NF4 times bf16 activations, exact in float64):
+  every element within 1e-4 of the sum of |w * x| (fp32 accumulation over up
+  to 11008 terms), padded batch columns exactly zero, rows of the shared
+  partials buffer outside the matrix untouched;
+* one whole batched step against the oracle's per-sequence layer, with every
+  sequence at its own position over its own random cache (norm-wise 1e-2);
+* graph replay against eager execution: bit-identical (fixed split order);
+* ragged-prompt greedy decode: teacher-forced top-1 agreement.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.test_gpu_decode import _b16, _layer_np, norm_close
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def bridge():
+    import torch
+
+    from kudacuda_b200.kudacuda_sidecar import KudaCudaBridge
+
+    torch.cuda.set_device(0)
+    br = KudaCudaBridge(device_id=0)
+    yield br
+    br.shutdown()
+
+
+@pytest.mark.parametrize(
+    "rows,k,batch,n_pad,ksplit,weight_type",
+    [
+        (128, 64, 16, 16, 1, 0),      # one tile, one K block
+        (300, 256, 5, 16, 1, 0),      # ragged M tile, one split
+        (300, 2048, 20, 32, 3, 0),    # uneven split of 32 K blocks
+        (2560, 2048, 64, 64, 0, 0),   # q|k|v rows, full batch, suggested split
+        (2048, 11008, 33, 64, 0, 0),  # down_proj shape
+        (1000, 512, 3, 16, 2, 1),     # bf16 weights (lm_head form)
+    ],
+)
+def test_batch_gemm_against_oracle(bridge, rows, k, batch, n_pad, ksplit, weight_type):
+    import torch
+
+    dev = "cuda:0"
+    g = torch.Generator(device="cpu").manual_seed(rows * 7 + k + batch)
+    w = (torch.randn((rows, k), generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.zeros((n_pad, k), dtype=torch.bfloat16)
+    x[:batch] = torch.randn((batch, k), generator=g).to(torch.bfloat16)
+    if weight_type == 0:
+        packed, absmax = O.nf4_quantize(O.bf16_to_f32(w.view(torch.int16).numpy().view(np.uint16)).reshape(-1))
+        wd = torch.from_numpy(np.ascontiguousarray(packed)).to(dev)
+        ad = torch.from_numpy(np.ascontiguousarray(absmax)).to(dev)
+    else:
+        packed, absmax = w.view(torch.int16).numpy().view(np.uint16), None
+        wd, ad = w.to(dev), None
+    if ksplit == 0:
+        ksplit = bridge.batch_gemm_ksplit(rows, k)
+    assert 1 <= ksplit <= k // 64
+    total = rows + 40  # the matrix sits at row_offset 17 inside a larger partials buffer
+    sentinel = 12345.0
+    part = torch.full((ksplit * total * n_pad,), sentinel, dtype=torch.float32, device=dev)
+    xd = x.to(dev)
+    s = torch.cuda.Stream()
+    bridge.dispatch_batch_gemm(wd, ad, xd, part, weight_type=weight_type, rows=rows, k=k, n_pad=n_pad, ksplit=ksplit,
+                               row_offset=17, total_rows=total, stream_ptr=int(s.cuda_stream))
+    s.synchronize()
+    assert bridge.error_word(clear=True) == 0
+    p = part.view(ksplit, total, n_pad).cpu().numpy().astype(np.float64)
+    assert np.all(p[:, :17] == sentinel) and np.all(p[:, 17 + rows:] == sentinel)
+    got = p[:, 17:17 + rows].sum(axis=0)
+    ref, mag = O.batch_gemm_ref(packed, absmax, rows, k, x.view(torch.int16).numpy().view(np.uint16),
+                                weight_type=weight_type)
+    assert np.all(got[:, batch:] == 0.0)
+    err = np.abs(got - ref)
+    bound = 1e-4 * mag + 1e-6
+    worst = np.unravel_index(np.argmax(err / bound), err.shape)
+    assert np.all(err <= bound), f"row {worst[0]} seq {worst[1]}: {got[worst]} vs {ref[worst]}"
+
+
+@pytest.fixture(scope="module")
+def batched_one_layer(bridge):
+    import torch
+
+    from kudacuda_b200.decode_engine import BatchedDecodePlan, random_weights, tiny_config
+
+    cfg = tiny_config(layers=1, vocab=4096)
+    weights = random_weights(bridge, cfg, seed=31, device="cuda:0")
+    plan = BatchedDecodePlan(bridge, weights, batch=5, kv_bucket=128, max_tokens=128, device="cuda:0")
+    stream = torch.cuda.Stream()
+    plan.capture(stream)
+    yield cfg, weights, plan, stream
+    bridge.reset_graph()
+
+
+def test_batched_step_against_oracle_per_sequence(bridge, batched_one_layer):
+    """Five sequences at positions 0, 9, 100, 37, 126 over their own random caches."""
+
+    import torch
+
+    cfg, w, plan, stream = batched_one_layer
+    positions = [0, 9, 100, 37, 126]
+    tokens = [321, 5, 4095, 77, 1000]
+    plan.reset_cache()
+    rng = np.random.default_rng(41)
+    shape = tuple(plan.buffers.kcache.shape)
+    kc0 = O.bf16_bits(rng.normal(0, 1, shape).astype(np.float32))
+    vc0 = O.bf16_bits(rng.normal(0, 1, shape).astype(np.float32))
+    plan.buffers.kcache.copy_(torch.from_numpy(kc0.view(np.int16)).view(torch.bfloat16).to(plan.device))
+    plan.buffers.vcache.copy_(torch.from_numpy(vc0.view(np.int16)).view(torch.bfloat16).to(plan.device))
+    plan.set_state(tokens, positions, stream)
+    plan.replay(stream)
+    stream.synchronize()
+    assert bridge.error_word(clear=True) == 0
+    emb = _b16(w.embedding).reshape(cfg.vocab, cfg.hidden)
+    cos, sin = _b16(plan.buffers.rope_cos), _b16(plan.buffers.rope_sin)
+    ocfg = dict(hidden=cfg.hidden, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                inter=cfg.intermediate, eps=cfg.eps)
+    layer = _layer_np(w.layers[0])
+    xs = _b16(plan.buffers.x)
+    kc_gpu, vc_gpu = _b16(plan.buffers.kcache), _b16(plan.buffers.vcache)
+    state = plan.buffers.state.cpu().numpy()
+    fn = _b16(w.final_norm)
+    for b, (tok, pos) in enumerate(zip(tokens, positions)):
+        x = emb[tok].copy()
+        kc, vc = kc0[0, b].copy(), vc0[0, b].copy()
+        O.layer_step_hf(layer, ocfg, x, kc, vc, plan.kv_bucket, pos, cos[pos], sin[pos])
+        norm_close(O.bf16_to_f32(xs[b]), O.bf16_to_f32(x))
+        norm_close(O.bf16_to_f32(kc_gpu[0, b][:, pos]), O.bf16_to_f32(kc[:, pos]))
+        norm_close(O.bf16_to_f32(vc_gpu[0, b][:, pos]), O.bf16_to_f32(vc[:, pos]))
+        np.testing.assert_array_equal(kc_gpu[0, b][:, :pos], kc0[0, b][:, :pos])
+        np.testing.assert_array_equal(kc_gpu[0, b][:, pos + 1:], kc0[0, b][:, pos + 1:])
+        assert list(state[b][1:3]) == [pos + 1, pos + 2]
+        ref_tok, logits = O.lm_head_argmax(x, fn, emb, cfg.eps, want_logits=True)
+        if ref_tok != state[b][0]:  # a near-tie may flip by a rounding step
+            lf = O.bf16_to_f32(logits)
+            assert lf[state[b][0]] >= lf[ref_tok] - 2e-2 * abs(lf[ref_tok]) - 2e-3
+
+
+def test_batched_graph_matches_eager_bit_identical(bridge, batched_one_layer):
+    import torch
+
+    cfg, w, plan, stream = batched_one_layer
+    outs = []
+    for mode in ("eager", "graph", "graph"):
+        plan.reset_cache()
+        plan.set_state([1, 2, 3, 4, 5], [3, 0, 7, 1, 2], stream)
+        if mode == "eager":
+            with torch.cuda.stream(stream):
+                plan.record(int(stream.cuda_stream))
+        else:
+            plan.replay(stream)
+        stream.synchronize()
+        outs.append((_b16(plan.buffers.x).copy(), _b16(plan.buffers.kcache).copy(),
+                     plan.buffers.state.cpu().numpy().copy()))
+    for other in outs[1:]:
+        for a, b in zip(outs[0], other):
+            np.testing.assert_array_equal(a, b)
+    assert bridge.error_word(clear=True) == 0
+
+
+def test_batched_greedy_ragged_prompts_teacher_forced(bridge):
+    import torch
+
+    from kudacuda_b200.decode_engine import BatchedDecodePlan, batched_greedy_generate, random_weights, tiny_config
+
+    cfg = tiny_config(layers=2, vocab=4096)
+    w = random_weights(bridge, cfg, seed=13, device="cuda:0")
+    plan = BatchedDecodePlan(bridge, w, batch=3, kv_bucket=64, max_tokens=64, device="cuda:0")
+    stream = torch.cuda.Stream()
+    plan.capture(stream)
+    prompts = [[5, 17, 300, 4000], [9], [1, 2, 3, 4, 5, 6]]
+    n_new = 6
+    outs = batched_greedy_generate(plan, prompts, n_new, stream)
+    assert bridge.error_word(clear=True) == 0
+    layers = [_layer_np(L) for L in w.layers]
+    emb = _b16(w.embedding).reshape(cfg.vocab, cfg.hidden)
+    fn = _b16(w.final_norm)
+    cos, sin = _b16(plan.buffers.rope_cos), _b16(plan.buffers.rope_sin)
+    ocfg = dict(hidden=cfg.hidden, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                inter=cfg.intermediate, eps=cfg.eps)
+    agree, total = 0, 0
+    for prompt, gen in zip(prompts, outs):
+        assert len(gen) == n_new
+        seq = prompt + gen
+        kcs = [np.zeros((cfg.kv_heads, plan.kv_bucket, cfg.head_dim), dtype=np.uint16) for _ in layers]
+        vcs = [np.zeros_like(kcs[0]) for _ in layers]
+        for pos in range(len(seq) - 1):
+            x = emb[seq[pos]].copy()
+            for li, layer in enumerate(layers):
+                O.layer_step_hf(layer, ocfg, x, kcs[li], vcs[li], plan.kv_bucket, pos, cos[pos], sin[pos])
+            tok, _ = O.lm_head_argmax(x, fn, emb, cfg.eps)
+            if pos >= len(prompt) - 1:
+                agree += int(tok == seq[pos + 1])
+                total += 1
+    rate = agree / total
+    assert rate >= 0.75, f"teacher-forced top-1 agreement {rate:.2f}"
+    bridge.reset_graph()
+
+
+def test_batched_rejects_bad_arguments(bridge):
+    import torch
+
+    from kudacuda_b200.kudacuda_sidecar import NativeCudaError
+
+    x = torch.zeros((16, 128), dtype=torch.bfloat16, device="cuda:0")
+    w = torch.zeros((128, 128), dtype=torch.bfloat16, device="cuda:0")
+    part = torch.zeros(16 * 128 * 4, dtype=torch.float32, device="cuda:0")
+    with pytest.raises(NativeCudaError):  # n_pad 8 is not a supported N here
+        bridge.dispatch_batch_gemm(w, None, x[:8], part, weight_type=1, rows=128, k=128, n_pad=8, ksplit=1,
+                                   stream_ptr=0)
+    with pytest.raises(NativeCudaError):  # ksplit above K/64
+        bridge.dispatch_batch_gemm(w, None, x, part, weight_type=1, rows=128, k=128, n_pad=16, ksplit=3,
+                                   stream_ptr=0)
+    with pytest.raises(ValueError):
+        bridge.batch_argmax_workspace_bytes(65)
