@@ -231,12 +231,13 @@ __global__ void __launch_bounds__(kTcThreads) nf4_gemm_tc_kernel(const TcArgs a)
     }
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (!ok && lane == 0 && a.err != nullptr) atomicOr(a.err, 16);
-    // warp w reads TMEM lanes 32 (w % 4) .. + 31 (tile rows), columns half (w / 4) of n
+    // warp w reads TMEM lanes 32 (w % 4) .. + 31 (tile rows); the n columns go
+    // in 16-column chunks, chunk c to warps 4 (c % 2) .. + 3 (n = 16: one chunk,
+    // read by warps 0-3 alone)
     {
         const int lrow = 32 * (warp & 3) + lane;
         const int grow2 = tile * kTcM + lrow;
-        const int cbeg = (warp >> 2) * (n / 2), cend = cbeg + n / 2;
-        for (int c0 = cbeg; c0 < cend; c0 += 16) {
+        for (int c0 = 16 * (warp >> 2); c0 < n; c0 += 32) {
             float v[16];
             const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + static_cast<uint32_t>(c0);
             tmem_ld16(taddr, v);
