@@ -18,22 +18,25 @@
 // 16-byte core matrices; the two 8-element K halves 128 B apart, 8-row groups
 // 256 B apart) and stage the activations' 64-element slice beside it; one
 // thread issues four tcgen05.mma (K = 16 each) into a 128 x N fp32 TMEM
-// accumulator and commits to an mbarrier.  Two stages: the dequant of block
-// i + 1 overlaps the MMAs of block i, and each thread's weight loads for
-// block i + 1 are in flight while it dequantises block i.  The accumulator is
+// accumulator and commits to an mbarrier.  Weights, absmax and activations
+// stream through a cp.async ring several K blocks deep (enough bytes in flight
+// per SM to cover HBM latency); the dequant of block i + 1 overlaps the MMAs
+// of block i (two A tiles).  bf16 weights (the tied lm_head) skip the dequant:
+// cp.async places them in the canonical layout directly.  The accumulator is
 // read with tcgen05.ld and written as fp32 split-K partials; small epilogue
 // kernels sum the splits in a fixed order (deterministic) and finish each op.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
 
 #include "kc_common.cuh"
 #include "kc_launch.h"
+#include "kc_tma.h"
 
 namespace kc {
 namespace {
 
-constexpr int kTcThreads = 256;
 constexpr int kTcM = 128;
 constexpr int kBlockK = 64;
 constexpr int kATileBytes = kTcM * kBlockK * 2;  // 16 KB of bf16 per stage
@@ -47,21 +50,6 @@ struct TcArgs {
     int* err;
 };
 
-// Canonical K-major, no-swizzle UMMA layout of a (rows x 16) K step: element
-// (r, k) at (r / 8) * 256 + (k / 8) * 128 + (r % 8) * 16 + (k % 8) * 2 bytes.
-__device__ __forceinline__ uint32_t kmajor_chunk(int r, int half) {  // byte offset of the 8-element chunk
-    return static_cast<uint32_t>((r >> 3) * 256 + half * 128 + (r & 7) * 16);
-}
-// Shared-memory matrix descriptor (sm_100): start >> 4, LBO >> 4 (K halves),
-// SBO >> 4 (8-row groups), version 1, base offset 0, layout SWIZZLE_NONE.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-    d |= static_cast<uint64_t>(128u >> 4) << 16;
-    d |= static_cast<uint64_t>(256u >> 4) << 32;
-    d |= static_cast<uint64_t>(1u) << 46;
-    return d;
-}
 // Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both
 // K-major, N >> 3 at bit 17, M >> 4 at bit 24.
 __device__ __forceinline__ uint32_t umma_idesc_bf16(int n) {
@@ -90,58 +78,135 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// bf16 pair (lo = element 2j, hi = element 2j + 1) of a dequantised NF4 byte;
-// lut is the 16-level codebook in shared memory (16 words in 16 banks: a warp's
-// lookups never conflict, unlike divergent constant-memory reads)
-__device__ __forceinline__ uint32_t nf4_pair_bf16(const float* lut, uint32_t byte, float s) {
-    const float e = lut[(byte >> 4) & 15u] * s;  // even element: high nibble
-    const float o = lut[byte & 15u] * s;
-    return static_cast<uint32_t>(f32_to_bf16_bits(e)) | (static_cast<uint32_t>(f32_to_bf16_bits(o)) << 16);
+// ---- tensor memory access, bounded mbarrier waits, TMA
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
-
-// One thread's share of a K block: 32 weights of one row (16 code bytes and
-// the block's absmax for NF4, 64 bytes for bf16)
-struct WLoad {
-    uint4 v[4];
-    float s;
-};
-__device__ __forceinline__ void load_weights(const TcArgs& a, bool row_ok, int grow, int nblk, int kb, int half,
-                                             WLoad& w) {
-    if (!row_ok) return;
-    if (a.weight_type == 0) {
-        w.v[0] = *reinterpret_cast<const uint4*>(a.packed + static_cast<int64_t>(grow) * (a.K / 2) + kb * 32 +
-                                                 half * 16);
-        w.s = a.absmax[static_cast<int64_t>(grow) * nblk + kb];
-    } else {
-        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.packed) +
-                                                          static_cast<int64_t>(grow) * a.K + kb * 64 + half * 32);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) w.v[q] = src[q];
+__device__ __forceinline__ void bar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// try_wait with a suspend-time hint of 1 us: wakes when the phase completes,
+// gives up after ~2^17 tries (~0.1 s) or as soon as another thread of the CTA
+// has given up (abort flag), so a protocol error ends the kernel instead of
+// hanging the GPU.
+__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                         bool honour_abort = true) {
+    for (uint32_t i = 0; i < (1u << 17); ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity), "r"(1000u)
+            : "memory");
+        if (ok) return true;
+        if (honour_abort && *abort_flag) return false;
     }
+    *abort_flag = 1;
+    return false;
+}
+// Shared-memory matrix descriptor, K-major with the 128-byte swizzle (the
+// layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B): rows 128 B apart, 8-row
+// groups 1024 B apart (SBO), LBO unused (1), version 1, layout type 2.  A K
+// step of 16 bf16 advances the start address by 32 B inside the swizzle atom.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+// byte offset of 16-byte chunk c (0..7) of row r in a 128-byte-swizzled K-major tile
+__device__ __forceinline__ uint32_t sw128_chunk(int r, int c) {
+    return static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);  // lo -> low half
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+// two fp32 products in one instruction (each lane rounds like a scalar fmul)
+__device__ __forceinline__ float2 mul_f32x2(float2 a, float s) {
+    uint64_t d;
+    const float2 sv = make_float2(s, s);
+    asm("mul.rn.f32x2 %0, %1, %2;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&sv)));
+    return *reinterpret_cast<const float2*>(&d);
 }
 
-__global__ void __launch_bounds__(kTcThreads) nf4_gemm_tc_kernel(const TcArgs a) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ __align__(8) uint64_t mma_bar[2];
+// ---- the tensor-core GEMM
+// One CTA = one 128-row tile x one split of K, ten warps:
+//   warp 0   TMA producer: per 64-element K block, the weight tile (NF4 codes
+//            128 x 32 B row-major, or bf16 128 x 128 B swizzled) and the
+//            activations' block (n x 128 B swizzled) into a ring stage;
+//   warp 1   MMA issuer: four tcgen05.mma (K = 16) per block into the TMEM
+//            accumulator, tcgen05.commit frees the ring stage and the A tile;
+//   warps 2-9 (NF4) dequantise: thread (row r, half h) reads its 16 code
+//            bytes, looks up byte -> (level[hi], level[lo]) in a pair table
+//            (16 lane-indexed copies: conflict-free 64-bit lookups), scales by
+//            the block's absmax in fp32, rounds to bf16 and writes the
+//            swizzled A tile; then they read the accumulator out.
+// Barriers: raw_full (TMA bytes landed), raw_empty (MMAs of that stage done),
+// a_full (256 dequant arrivals), a_empty (MMAs of that A tile done), done.
+constexpr int kGThreads = 320;
+constexpr int kPairCopies = 16;
+constexpr int kPairTableBytes = 256 * kPairCopies * 8;  // 32 KB
+constexpr int kMaxRaw = 4;
+
+template <int WT>
+struct GemmSmem {
+    static __host__ __device__ int raw_stages(int n) { return (WT == 0 && n == 64) ? 3 : 4; }
+    static __host__ __device__ int w_bytes() { return WT == 0 ? kTcM * 32 : kATileBytes; }
+    static __host__ __device__ int raw_bytes(int n) { return w_bytes() + n * kBlockK * 2; }  // multiple of 1024
+    static __host__ __device__ int fixed_bytes() { return WT == 0 ? kPairTableBytes + 2 * kATileBytes : 0; }
+    static __host__ __device__ int bytes(int n) { return 1024 + fixed_bytes() + raw_stages(n) * raw_bytes(n); }
+};
+
+template <int WT>
+__global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w,
+                                                            const __grid_constant__ CUtensorMap map_x,
+                                                            const TcArgs a) {
+    using G = GemmSmem<WT>;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t raw_full[kMaxRaw], raw_empty[kMaxRaw], a_full[2], a_empty[2], done_bar;
     __shared__ uint32_t tmem_slot;
-    __shared__ float lut[16];
+    __shared__ int abort_flag;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (tid < 16) lut[tid] = kNf4Levels[tid];
     const int n = a.n_pad;
-    const int bstage = n * kBlockK * 2;  // B bytes per stage
-    uint8_t* const a_base = smem;
-    uint8_t* const b_base = smem + 2 * kATileBytes;
-    const int ncols = n <= 32 ? 32 : 64;  // TMEM columns: a power of two >= 32 covering N
+    const int R = G::raw_stages(n);
+    const int rb = G::raw_bytes(n);
+    // 1024-byte aligned base (the swizzled tiles need it)
+    uint8_t* const base = smem_raw + (((smem_u32(smem_raw) + 1023u) & ~1023u) - smem_u32(smem_raw));
+    uint8_t* const table = base;                          // NF4: pair table
+    uint8_t* const atile = base + kPairTableBytes;        // NF4: two dequantised A tiles
+    uint8_t* const raw = base + G::fixed_bytes();         // ring of R stages
+    const int ncols = n <= 32 ? 32 : 64;
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
                      "r"(ncols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    if (tid == 0) {
-        mbar_init(&mma_bar[0], 1);
-        mbar_init(&mma_bar[1], 1);
+    if (tid == 32) {
+        for (int i = 0; i < kMaxRaw; ++i) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], 1);
+        }
+        mbar_init(&a_full[0], 256);
+        mbar_init(&a_full[1], 256);
+        mbar_init(&a_empty[0], 1);
+        mbar_init(&a_empty[1], 1);
+        mbar_init(&done_bar, 1);
+        abort_flag = 0;
         fence_mbar_init();
+    }
+    if (WT == 0 && warp >= 2) {  // entry e, copy c: (level[e >> 4], level[e & 15]) at (e * 16 + c) * 8
+        for (int i = tid - 64; i < 256 * kPairCopies; i += 256) {
+            const int e = i / kPairCopies;
+            *reinterpret_cast<float2*>(table + i * 8) = make_float2(kNf4Levels[e >> 4], kNf4Levels[e & 15]);
+        }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -152,105 +217,113 @@ __global__ void __launch_bounds__(kTcThreads) nf4_gemm_tc_kernel(const TcArgs a)
     const int nblk = a.K / kBlockK;
     const int kb0 = static_cast<int>(static_cast<int64_t>(ks) * nblk / a.ksplit);
     const int kb1 = static_cast<int>(static_cast<int64_t>(ks + 1) * nblk / a.ksplit);
-    const int r = tid >> 1, half = tid & 1;  // dequant: row r of the tile, K half `half` of the block
-    const int grow = tile * kTcM + r;
-    const bool row_ok = grow < a.rows;
-    const uint32_t idesc = umma_idesc_bf16(n);
-    uint32_t phase0 = 0u, phase1 = 0u;
-    bool ok = true;
+    const int nit = kb1 - kb0;
+    volatile int* const abort_p = &abort_flag;
 
     pdl_launch_dependents();
     pdl_wait_on_producer();
-    WLoad cur, nxt;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) cur.v[q] = nxt.v[q] = make_uint4(0u, 0u, 0u, 0u);
-    cur.s = nxt.s = 0.F;
-    if (kb0 < kb1) load_weights(a, row_ok, grow, nblk, kb0, half, cur);
-    for (int kb = kb0, it = 0; kb < kb1; ++kb, ++it) {
-        const int st = it & 1;
-        if (kb + 1 < kb1) load_weights(a, row_ok, grow, nblk, kb + 1, half, nxt);  // in flight during this block
-        if (it >= 2) {  // the MMAs that read this stage two blocks ago must be done
-            uint32_t& ph = st ? phase1 : phase0;
-            if (!mbar_wait_bounded(&mma_bar[st], ph)) ok = false;
-            ph ^= 1u;
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t tx = static_cast<uint32_t>(rb);
+            for (int it = 0; it < nit; ++it) {
+                const int j = it % R, m = it / R;
+                if (m >= 1) bar_wait(&raw_empty[j], (m - 1) & 1, abort_p);
+                uint8_t* stg = raw + j * rb;
+                mbar_arrive_expect_tx(&raw_full[j], tx);
+                tma_load_2d(stg, &map_w, WT == 0 ? (kb0 + it) * 32 : (kb0 + it) * kBlockK, tile * kTcM, &raw_full[j]);
+                tma_load_2d(stg + G::w_bytes(), &map_x, (kb0 + it) * kBlockK, 0, &raw_full[j]);
+            }
+            // every copy has landed before the CTA may exit (normally already true)
+            for (int j = 0; j < R; ++j) {
+                const int issued = (nit - j + R - 1) / R;  // loads that went to stage j
+                if (issued > 0) bar_wait(&raw_full[j], (issued - 1) & 1, abort_p, false);
+            }
         }
-        // ---- A: 32 weights of row r (K half `half`) -> bf16 into the canonical layout
-        uint32_t w[16];
-        if (a.weight_type == 0) {
-            const uint32_t cw[4] = {cur.v[0].x, cur.v[0].y, cur.v[0].z, cur.v[0].w};
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_bf16(n);
+            for (int it = 0; it < nit; ++it) {
+                const int j = it % R, s = it & 1;
+                bar_wait(&raw_full[j], (it / R) & 1, abort_p);
+                if (WT == 0) bar_wait(&a_full[s], (it >> 1) & 1, abort_p);
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                uint8_t* const stg = raw + j * rb;
+                const uint32_t sa = smem_u32(WT == 0 ? atile + s * kATileBytes : stg);
+                const uint32_t sb = smem_u32(stg + G::w_bytes());
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-#pragma unroll
-                for (int bb = 0; bb < 4; ++bb) w[q * 4 + bb] = nf4_pair_bf16(lut, (cw[q] >> (8 * bb)) & 0xFFu, cur.s);
-        } else {
+                for (int k = 0; k < 4; ++k)
+                    umma_bf16(tmem, umma_desc_sw128(sa + 32 * k), umma_desc_sw128(sb + 32 * k), idesc,
+                              (it > 0 || k > 0) ? 1u : 0u);
+                if (WT == 0) umma_commit(&a_empty[s]);
+                umma_commit(&raw_empty[j]);
+            }
+            umma_commit(&done_bar);
+        }
+    } else if (WT == 0) {
+        // ---- dequantise: thread (r, h) owns 32 weights of row r per block
+        const int dq = tid - 64, r = dq >> 1, h = dq & 1;
+        const int grow = tile * kTcM + r;
+        const bool row_ok = grow < a.rows;
+        const float* arow = a.absmax + static_cast<int64_t>(row_ok ? grow : 0) * nblk;
+        const bool vec4 = (nblk & 3) == 0;
+        const uint8_t* const tl = table + (lane & 15) * 8;
+        float4 cur4 = make_float4(0.F, 0.F, 0.F, 0.F), nxt4 = cur4;
+        int cur_g = -1;
+        for (int it = 0; it < nit; ++it) {
+            const int kb = kb0 + it, j = it % R, s = it & 1;
+            // absmax: float4 of four blocks, the next four prefetched (scalar when rows are not 16-B aligned)
+            float sc = 0.F;
+            if (row_ok) {
+                if (vec4) {
+                    const int g = kb >> 2;
+                    if (g != cur_g) {
+                        cur4 = cur_g < 0 ? *reinterpret_cast<const float4*>(arow + 4 * g) : nxt4;
+                        cur_g = g;
+                        if (4 * (g + 1) < kb1) nxt4 = *reinterpret_cast<const float4*>(arow + 4 * (g + 1));
+                    }
+                    const int q = kb & 3;
+                    sc = q == 0 ? cur4.x : q == 1 ? cur4.y : q == 2 ? cur4.z : cur4.w;
+                } else {
+                    sc = arow[kb];
+                }
+            }
+            bar_wait(&raw_full[j], (it / R) & 1, abort_p);
+            const uint4 cv = *reinterpret_cast<const uint4*>(raw + j * rb + r * 32 + h * 16);
+            if (it >= 2) bar_wait(&a_empty[s], ((it >> 1) - 1) & 1, abort_p);
+            uint8_t* const as = atile + s * kATileBytes;
+            const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                w[4 * q] = cur.v[q].x;
-                w[4 * q + 1] = cur.v[q].y;
-                w[4 * q + 2] = cur.v[q].z;
-                w[4 * q + 3] = cur.v[q].w;
-            }
-        }
-        // elements [32 half, 32 half + 32): K steps 2 half and 2 half + 1, two 8-element chunks each
-        uint8_t* const as = a_base + st * kATileBytes;
+                uint32_t o[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int kstep = 2 * half + (c >> 1), kh = c & 1;
-            *reinterpret_cast<uint4*>(as + kstep * (kTcM * 32) + kmajor_chunk(r, kh)) =
-                make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-        }
-        // ---- B: the activations' 64-element slice, n rows
-        uint8_t* const bs = b_base + st * bstage;
-        for (int i = tid; i < n * 8; i += kTcThreads) {
-            const int row = i >> 3, c = i & 7;  // chunk c of 8 elements
-            const uint4 v = *reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(row) * a.K + kb * 64 + c * 8);
-            *reinterpret_cast<uint4*>(bs + (c >> 1) * (n * 32) + kmajor_chunk(row, c & 1)) = v;
-        }
-        fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core (async proxy)
-        __syncthreads();
-        if (tid == 0) {
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const uint64_t da = umma_desc(smem_u32(as + s * (kTcM * 32)));
-                const uint64_t db = umma_desc(smem_u32(bs + s * (n * 32)));
-                umma_bf16(tmem, da, db, idesc, (it > 0 || s > 0) ? 1u : 0u);
+                for (int bb = 0; bb < 4; ++bb) {
+                    const uint32_t byte = (cw[q] >> (8 * bb)) & 0xFFu;
+                    const float2 lv = mul_f32x2(*reinterpret_cast<const float2*>(tl + byte * (kPairCopies * 8)), sc);
+                    o[bb] = pack_bf16x2(lv.x, lv.y);  // even element (high nibble) in the low half
+                }
+                *reinterpret_cast<uint4*>(as + sw128_chunk(r, 4 * h + q)) = make_uint4(o[0], o[1], o[2], o[3]);
             }
-            umma_commit(&mma_bar[st]);
-        }
-        cur = nxt;
-    }
-    // ---- wait for the last MMAs, then read the 128 x n accumulator
-    const int nit = kb1 - kb0;
-    if (nit > 0) {
-        const int st = (nit - 1) & 1;
-        if (!mbar_wait_bounded(&mma_bar[st], st ? phase1 : phase0)) ok = false;
-        if (nit >= 2) {  // the other stage's last commit is older and already complete
-            if (!mbar_wait_bounded(&mma_bar[st ^ 1], st ? phase0 : phase1)) ok = false;
+            fence_proxy_async_smem();  // generic stores -> visible to the tensor core
+            bar_arrive(&a_full[s]);
         }
     }
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (!ok && lane == 0 && a.err != nullptr) atomicOr(a.err, 16);
-    // warp w reads TMEM lanes 32 (w % 4) .. + 31 (tile rows); the n columns go
-    // in 16-column chunks, chunk c to warps 4 (c % 2) .. + 3 (n = 16: one chunk,
-    // read by warps 0-3 alone)
-    {
+    // ---- epilogue: warps 2-9 read the 128 x n accumulator (warp w: TMEM lanes 32 (w % 4) ..)
+    if (warp >= 2) {
+        bar_wait(&done_bar, 0u, abort_p, false);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int lrow = 32 * (warp & 3) + lane;
         const int grow2 = tile * kTcM + lrow;
-        for (int c0 = 16 * (warp >> 2); c0 < n; c0 += 32) {
+        for (int c0 = 16 * ((warp - 2) >> 2); c0 < n; c0 += 32) {
             float v[16];
-            const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + static_cast<uint32_t>(c0);
-            tmem_ld16(taddr, v);
+            tmem_ld16(tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + static_cast<uint32_t>(c0), v);
             if (grow2 < a.rows) {
                 float* dst = a.partials + (static_cast<int64_t>(ks) * a.total_rows + a.row_offset + grow2) * n + c0;
-                const bool any = nit > 0;
 #pragma unroll
-                for (int i = 0; i < 16; i += 4)
-                    *reinterpret_cast<float4*>(dst + i) = any ? make_float4(v[i], v[i + 1], v[i + 2], v[i + 3])
-                                                              : make_float4(0.F, 0.F, 0.F, 0.F);
+                for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
             }
         }
     }
+    if (tid == 0 && *abort_p && a.err != nullptr) atomicOr(a.err, 16);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0) {
@@ -477,23 +550,60 @@ int ew_grid(int64_t total) {
 }  // namespace
 
 int batch_gemm_ksplit(int rows, int K) {
+    // about two CTAs per SM, but at least 8 K blocks per CTA where K allows:
+    // a CTA streams its blocks through the cp.async ring, so fatter CTAs keep
+    // more bytes in flight and write fewer fp32 partials
     const int mtiles = (rows + kTcM - 1) / kTcM;
     const int nblk = K / kBlockK;
     const int target = 2 * device_sm_count();
     int ks = (target + mtiles - 1) / mtiles;
-    if (ks > nblk) ks = nblk;
+    const int cap = nblk / 8 > 1 ? nblk / 8 : 1;
+    if (ks > cap) ks = cap;
     if (ks > 16) ks = 16;
     return ks < 1 ? 1 : ks;
 }
+
+namespace {
+template <int WT>
+cudaError_t launch_gemm(const TcArgs& a, int ksplit, cudaStream_t s) {
+    CUtensorMap mw, mx;
+    cudaError_t st;
+    if (WT == 0)
+        st = encode_tmap_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.packed, a.K / 2, a.rows, a.K / 2, 32, kTcM,
+                            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    else
+        st = encode_tmap_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.packed, a.K, a.rows,
+                            static_cast<uint64_t>(a.K) * 2, kBlockK, kTcM, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    if (st != cudaSuccess) return st;
+    st = encode_tmap_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, a.K, a.n_pad, static_cast<uint64_t>(a.K) * 2,
+                        kBlockK, a.n_pad, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
+    if (st != cudaSuccess) return st;
+    static thread_local int attr_dev[2] = {-1, -1};
+    int dev = 0;
+    st = cudaGetDevice(&dev);
+    if (st != cudaSuccess) return st;
+    if (attr_dev[WT] != dev) {  // the largest footprint (n_pad 64 or 32) once per device
+        const int mx_bytes = GemmSmem<WT>::bytes(64) > GemmSmem<WT>::bytes(32) ? GemmSmem<WT>::bytes(64)
+                                                                                : GemmSmem<WT>::bytes(32);
+        st = cudaFuncSetAttribute(gemm_tc_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx_bytes);
+        if (st != cudaSuccess) return st;
+        attr_dev[WT] = dev;
+    }
+    return launch_pdl(gemm_tc_kernel<WT>, dim3((a.rows + kTcM - 1) / kTcM, ksplit), dim3(kGThreads),
+                      static_cast<size_t>(GemmSmem<WT>::bytes(a.n_pad)), s, mw, mx, a);
+}
+}  // namespace
 
 cudaError_t batch_gemm(int weight_type, const void* weight, const float* absmax, int rows, int K, const uint16_t* x,
                        int n_pad, int ksplit, float* partials, int row_offset, int total_rows, int* err,
                        cudaStream_t s) {
     if (rows < 1 || K < kBlockK || K % kBlockK != 0 || !(n_pad == 16 || n_pad == 32 || n_pad == 64) || ksplit < 1 ||
-        ksplit > K / kBlockK || row_offset < 0 || row_offset + rows > total_rows)
+        ksplit > K / kBlockK || row_offset < 0 || row_offset + rows > total_rows ||
+        (weight_type != 0 && weight_type != 1) || (weight_type == 0 && absmax == nullptr))
         return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(x) |
-         reinterpret_cast<uintptr_t>(partials)) & 15u)
+         reinterpret_cast<uintptr_t>(partials) | reinterpret_cast<uintptr_t>(absmax)) & 15u)
         return cudaErrorMisalignedAddress;
     TcArgs a;
     a.packed = static_cast<const uint8_t*>(weight);
@@ -508,11 +618,7 @@ cudaError_t batch_gemm(int weight_type, const void* weight, const float* absmax,
     a.row_offset = row_offset;
     a.total_rows = total_rows;
     a.err = err;
-    const int smem = 2 * kATileBytes + 2 * n_pad * kBlockK * 2;
-    cudaError_t st = cudaFuncSetAttribute(nf4_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (st != cudaSuccess) return st;
-    return launch_pdl(nf4_gemm_tc_kernel, dim3((rows + kTcM - 1) / kTcM, ksplit), dim3(kTcThreads),
-                      static_cast<size_t>(smem), s, a);
+    return weight_type == 0 ? launch_gemm<0>(a, ksplit, s) : launch_gemm<1>(a, ksplit, s);
 }
 
 cudaError_t batch_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* out, int batch, int H, float eps,

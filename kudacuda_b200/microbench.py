@@ -9,6 +9,7 @@ KV rows for attention).
 
     python -m kudacuda_b200.microbench --op swiglu [--copies 12 --launches 36 --reps 20]
     ops: gemv_11008x2048 gemv_2048x11008 qkv_rope oproj down swiglu gqa512 gqa2048 lm_head all
+         bgemm_<rows>x<k>_n<n_pad>[_ks<ksplit>][_bf16]  (batched tensor-core GEMM, e.g. bgemm_22016x2048_n64)
 
     python -m kudacuda_b200.microbench --op persistent --layers 36 --kv 512 [--launches 3 --reps 20]
       the persistent all-layers kernel alone (Qwen2.5-3B layer shapes, random
@@ -133,6 +134,27 @@ def build_cases(torch, bridge: KudaCudaBridge, names: list[str], copies: int, de
                                                    workspace_bytes=nbytes)
 
             cases.append(OpCase(name, nb, f))
+        elif name.startswith("bgemm_"):
+            # batched tensor-core GEMM: bgemm_<rows>x<k>_n<n_pad>[_ks<ksplit>][_bf16]
+            parts = name.split("_")
+            rows, k = (int(v) for v in parts[1].split("x"))
+            npad = int(parts[2][1:])
+            ks = next((int(p[2:]) for p in parts[3:] if p.startswith("ks")), 0) or bridge.batch_gemm_ksplit(rows, k)
+            wt = 1 if "bf16" in parts[3:] else 0
+            if wt == 0:
+                W = _nf4(torch, rows, k, copies, device)
+            else:
+                W = [(torch.randn((rows, k), device=device).to(bf16), None) for _ in range(copies)]
+            xb = torch.randn((npad, k), device=device).to(bf16)
+            part = torch.empty(ks * rows * npad, dtype=torch.float32, device=device)
+            nb = (rows * k // 2 + rows * k // 16 if wt == 0 else rows * k * 2) + npad * k * 2 + npad * rows * 2
+
+            def f(i, sp, W=W, xb=xb, part=part, rows=rows, k=k, npad=npad, ks=ks, wt=wt):
+                p, a = W[i % len(W)]
+                bridge.dispatch_batch_gemm(p, a, xb, part, weight_type=wt, rows=rows, k=k, n_pad=npad, ksplit=ks,
+                                           stream_ptr=sp)
+
+            cases.append(OpCase(f"{name}(ks{ks})", nb, f))
         elif name == "lm_head":
             n_emb = max(1, min(copies, 2))
             E = [torch.randn((V, H), device=device).to(bf16) for _ in range(n_emb)]
