@@ -793,7 +793,7 @@ def batched_gemm_roofline(torch, bridge, plan, stream) -> dict:
 
     def launch_all():
         for gu in plan.gu:
-            bridge.dispatch_batch_gemm(gu.packed, gu.absmax, b.xn, b.partials, weight_type=0, rows=rows, k=k,
+            bridge.dispatch_batch_gemm(gu.data, None, b.xn, b.partials, weight_type=2, rows=rows, k=k,
                                        n_pad=plan.n_pad, ksplit=plan.ks_gu, stream_ptr=sp)
 
     with torch.cuda.stream(stream):
@@ -819,7 +819,7 @@ def batched_gemm_roofline(torch, bridge, plan, stream) -> dict:
     tf = _peak_tflops()
     plan.capture(stream)  # the handle holds one graph: recapture the step
     return {
-        "kernel": "nf4_gemm_tc_kernel (NF4 -> bf16 dequant in shared memory, tcgen05.mma M=128 x N=n_pad, TMEM)",
+        "kernel": "gemm_tc_kernel<2> (re-tiled NF4 by bulk copy, bf16 dequant in shared memory, tcgen05.mma M=128 x N=n_pad, TMEM)",
         "bound": "hbm",
         "achieved": round(achieved, 1),
         "peak": peak,

@@ -346,7 +346,8 @@ KUDACUDA_API int kudacuda_sm100_decode_layers_persistent(void* handle, uint64_t 
  *   sum over split s's share of K of W[r][k] * x[b][k] (fp32), on the tcgen05
  *   tensor cores (weight as the 128-row M operand, the batch as N, fp32
  *   accumulator in TMEM).  weight_type 0: NF4 packed [rows][k/2] + fp32 absmax
- *   [rows][k/64]; 1: bf16 [rows][k] (absmax unused).  ksplit in [1, k/64];
+ *   [rows][k/64]; 1: bf16 [rows][k] (absmax unused); 2: NF4 re-tiled by
+ *   batch_retile (absmax unused, the fastest NF4 form).  ksplit in [1, k/64];
  *   batch_gemm_ksplit suggests one.  Several matrices may share one partials
  *   buffer through row_offset.
  * The epilogues sum the splits in split order (deterministic):
@@ -366,6 +367,14 @@ KUDACUDA_API int kudacuda_sm100_decode_layers_persistent(void* handle, uint64_t 
  * per-sequence int32 length array; workspace and tickets as for
  * kudacuda_sm100_gqa_decode with kv_len = kv_stride). */
 KUDACUDA_API int64_t kudacuda_sm100_batch_gemm_ksplit(int64_t rows, int64_t k);
+/* batch_retile: copy a bitsandbytes NF4 matrix into the GEMM's streaming form
+ * (weight_type 2): per 128-row tile and 64-element K block one contiguous
+ * 4,608-byte record (codes [128][32 B], then the block's absmax [128] fp32;
+ * rows past the matrix zero), so each block arrives with one bulk copy.
+ * Bit-exact: every code byte and absmax value is moved, none changed. */
+KUDACUDA_API int64_t kudacuda_sm100_batch_retile_bytes(int64_t rows, int64_t k);
+KUDACUDA_API int kudacuda_sm100_batch_retile(void* handle, uint64_t packed, uint64_t absmax, int64_t rows, int64_t k,
+                                             uint64_t out, int64_t out_bytes, uint64_t stream);
 KUDACUDA_API int kudacuda_sm100_batch_gemm(void* handle, int weight_type, uint64_t weight, uint64_t absmax,
                                            int64_t rows, int64_t k, uint64_t x, int64_t n_pad, int64_t ksplit,
                                            uint64_t partials, int64_t row_offset, int64_t total_rows,

@@ -29,6 +29,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstring>
 
 #include "kc_common.cuh"
 #include "kc_launch.h"
@@ -122,20 +123,6 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
 __device__ __forceinline__ uint32_t sw128_chunk(int r, int c) {
     return static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);  // lo -> low half
-    return *reinterpret_cast<const uint32_t*>(&v);
-}
-// two fp32 products in one instruction (each lane rounds like a scalar fmul)
-__device__ __forceinline__ float2 mul_f32x2(float2 a, float s) {
-    uint64_t d;
-    const float2 sv = make_float2(s, s);
-    asm("mul.rn.f32x2 %0, %1, %2;"
-        : "=l"(d)
-        : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&sv)));
-    return *reinterpret_cast<const float2*>(&d);
-}
-
 // ---- the tensor-core GEMM
 // One CTA = one 128-row tile x one split of K, ten warps:
 //   warp 0   TMA producer: per 64-element K block, the weight tile (NF4 codes
@@ -153,15 +140,29 @@ __device__ __forceinline__ float2 mul_f32x2(float2 a, float s) {
 constexpr int kGThreads = 320;
 constexpr int kPairCopies = 16;
 constexpr int kPairTableBytes = 256 * kPairCopies * 8;  // 32 KB
+constexpr int kMaxA = 2;
 constexpr int kMaxRaw = 4;
+
+// Weight forms: WT 0 NF4 in the bitsandbytes layout (codes by 2D TMA, absmax
+// by the dequant threads from global memory), WT 1 bf16, WT 2 NF4 re-tiled at
+// load (one contiguous 4,608-byte record per 128-row tile and K block: the
+// codes [128][32 B] then the absmax [128] fp32, fetched by one bulk copy).
+constexpr int kRetileRecord = kTcM * 32 + kTcM * 4;  // 4608
 
 template <int WT>
 struct GemmSmem {
-    static __host__ __device__ int raw_stages(int n) { return (WT == 0 && n == 64) ? 3 : 4; }
-    static __host__ __device__ int w_bytes() { return WT == 0 ? kTcM * 32 : kATileBytes; }
-    static __host__ __device__ int raw_bytes(int n) { return w_bytes() + n * kBlockK * 2; }  // multiple of 1024
-    static __host__ __device__ int fixed_bytes() { return WT == 0 ? kPairTableBytes + 2 * kATileBytes : 0; }
-    static __host__ __device__ int bytes(int n) { return 1024 + fixed_bytes() + raw_stages(n) * raw_bytes(n); }
+    static constexpr bool kNf4 = WT != 1;
+    static __host__ __device__ int raw_stages(int n) { return (kNf4 && n == 64) ? 3 : 4; }
+    // two dequantised A tiles (within two CTAs per SM; deeper measured slower)
+    static __host__ __device__ int a_stages(int n) { return kNf4 ? 2 : 0; }
+    static __host__ __device__ int w_bytes() { return WT == 0 ? kTcM * 32 : WT == 1 ? kATileBytes : kRetileRecord; }
+    // stage = [weights][activations] (WT 0, 1) or [activations][record] (WT 2); the swizzled tiles start
+    // on 1024-byte boundaries
+    static __host__ __device__ int b_off(int n) { return WT == 2 ? 0 : w_bytes(); }
+    static __host__ __device__ int w_off(int n) { return WT == 2 ? n * kBlockK * 2 : 0; }
+    static __host__ __device__ int raw_bytes(int n) { return (w_bytes() + n * kBlockK * 2 + 1023) / 1024 * 1024; }
+    static __host__ __device__ int fixed_bytes(int n) { return kNf4 ? kPairTableBytes + a_stages(n) * kATileBytes : 0; }
+    static __host__ __device__ int bytes(int n) { return 1024 + fixed_bytes(n) + raw_stages(n) * raw_bytes(n); }
 };
 
 template <int WT>
@@ -170,18 +171,19 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
                                                             const TcArgs a) {
     using G = GemmSmem<WT>;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t raw_full[kMaxRaw], raw_empty[kMaxRaw], a_full[2], a_empty[2], done_bar;
+    __shared__ __align__(8) uint64_t raw_full[kMaxRaw], raw_empty[kMaxRaw], a_full[kMaxA], a_empty[kMaxA], done_bar;
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n = a.n_pad;
     const int R = G::raw_stages(n);
+    const int SA = G::a_stages(n);
     const int rb = G::raw_bytes(n);
     // 1024-byte aligned base (the swizzled tiles need it)
     uint8_t* const base = smem_raw + (((smem_u32(smem_raw) + 1023u) & ~1023u) - smem_u32(smem_raw));
     uint8_t* const table = base;                          // NF4: pair table
-    uint8_t* const atile = base + kPairTableBytes;        // NF4: two dequantised A tiles
-    uint8_t* const raw = base + G::fixed_bytes();         // ring of R stages
+    uint8_t* const atile = base + kPairTableBytes;        // NF4: SA dequantised A tiles
+    uint8_t* const raw = base + G::fixed_bytes(n);        // ring of R stages
     const int ncols = n <= 32 ? 32 : 64;
 
     if (warp == 0) {
@@ -194,15 +196,15 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
             mbar_init(&raw_full[i], 1);
             mbar_init(&raw_empty[i], 1);
         }
-        mbar_init(&a_full[0], 256);
-        mbar_init(&a_full[1], 256);
-        mbar_init(&a_empty[0], 1);
-        mbar_init(&a_empty[1], 1);
+        for (int i = 0; i < kMaxA; ++i) {
+            mbar_init(&a_full[i], 256);
+            mbar_init(&a_empty[i], 1);
+        }
         mbar_init(&done_bar, 1);
         abort_flag = 0;
         fence_mbar_init();
     }
-    if (WT == 0 && warp >= 2) {  // entry e, copy c: (level[e >> 4], level[e & 15]) at (e * 16 + c) * 8
+    if (G::kNf4 && warp >= 2) {  // entry e, copy c: (level[e >> 4], level[e & 15]) at (e * 16 + c) * 8
         for (int i = tid - 64; i < 256 * kPairCopies; i += 256) {
             const int e = i / kPairCopies;
             *reinterpret_cast<float2*>(table + i * 8) = make_float2(kNf4Levels[e >> 4], kNf4Levels[e & 15]);
@@ -224,14 +226,20 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
     pdl_wait_on_producer();
     if (warp == 0) {
         if (lane == 0) {
-            const uint32_t tx = static_cast<uint32_t>(rb);
+            const uint32_t tx = static_cast<uint32_t>(G::w_bytes() + n * kBlockK * 2);
             for (int it = 0; it < nit; ++it) {
                 const int j = it % R, m = it / R;
                 if (m >= 1) bar_wait(&raw_empty[j], (m - 1) & 1, abort_p);
                 uint8_t* stg = raw + j * rb;
                 mbar_arrive_expect_tx(&raw_full[j], tx);
-                tma_load_2d(stg, &map_w, WT == 0 ? (kb0 + it) * 32 : (kb0 + it) * kBlockK, tile * kTcM, &raw_full[j]);
-                tma_load_2d(stg + G::w_bytes(), &map_x, (kb0 + it) * kBlockK, 0, &raw_full[j]);
+                if (WT == 2)
+                    bulk_g2s(stg + G::w_off(n),
+                             a.packed + (static_cast<int64_t>(tile) * nblk + kb0 + it) * kRetileRecord,
+                             kRetileRecord, &raw_full[j]);
+                else
+                    tma_load_2d(stg, &map_w, WT == 0 ? (kb0 + it) * 32 : (kb0 + it) * kBlockK, tile * kTcM,
+                                &raw_full[j]);
+                tma_load_2d(stg + G::b_off(n), &map_x, (kb0 + it) * kBlockK, 0, &raw_full[j]);
             }
             // every copy has landed before the CTA may exit (normally already true)
             for (int j = 0; j < R; ++j) {
@@ -243,37 +251,38 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_bf16(n);
             for (int it = 0; it < nit; ++it) {
-                const int j = it % R, s = it & 1;
+                const int j = it % R, s = G::kNf4 ? it % SA : 0;
                 bar_wait(&raw_full[j], (it / R) & 1, abort_p);
-                if (WT == 0) bar_wait(&a_full[s], (it >> 1) & 1, abort_p);
+                if (G::kNf4) bar_wait(&a_full[s], (it / SA) & 1, abort_p);
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 uint8_t* const stg = raw + j * rb;
-                const uint32_t sa = smem_u32(WT == 0 ? atile + s * kATileBytes : stg);
-                const uint32_t sb = smem_u32(stg + G::w_bytes());
+                const uint32_t sa = smem_u32(G::kNf4 ? atile + s * kATileBytes : stg);
+                const uint32_t sb = smem_u32(stg + G::b_off(n));
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
                     umma_bf16(tmem, umma_desc_sw128(sa + 32 * k), umma_desc_sw128(sb + 32 * k), idesc,
                               (it > 0 || k > 0) ? 1u : 0u);
-                if (WT == 0) umma_commit(&a_empty[s]);
+                if (G::kNf4) umma_commit(&a_empty[s]);
                 umma_commit(&raw_empty[j]);
             }
             umma_commit(&done_bar);
         }
-    } else if (WT == 0) {
+    } else if (G::kNf4) {
         // ---- dequantise: thread (r, h) owns 32 weights of row r per block
         const int dq = tid - 64, r = dq >> 1, h = dq & 1;
         const int grow = tile * kTcM + r;
         const bool row_ok = grow < a.rows;
-        const float* arow = a.absmax + static_cast<int64_t>(row_ok ? grow : 0) * nblk;
-        const bool vec4 = (nblk & 3) == 0;
-        const uint8_t* const tl = table + (lane & 15) * 8;
+        const float* arow = WT == 0 ? a.absmax + static_cast<int64_t>(row_ok ? grow : 0) * nblk : nullptr;
+        const bool vec4 = WT == 0 && (nblk & 3) == 0;
+        const uint32_t tl_u32 = smem_u32(table) + static_cast<uint32_t>((lane & (kPairCopies - 1)) * 8);
+        const uint32_t raw_u32 = smem_u32(raw), atile_u32 = smem_u32(atile);
         float4 cur4 = make_float4(0.F, 0.F, 0.F, 0.F), nxt4 = cur4;
         int cur_g = -1;
         for (int it = 0; it < nit; ++it) {
-            const int kb = kb0 + it, j = it % R, s = it & 1;
+            const int kb = kb0 + it, j = it % R, s = it % SA;
             // absmax: float4 of four blocks, the next four prefetched (scalar when rows are not 16-B aligned)
             float sc = 0.F;
-            if (row_ok) {
+            if (WT == 0 && row_ok) {
                 if (vec4) {
                     const int g = kb >> 2;
                     if (g != cur_g) {
@@ -288,20 +297,36 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
                 }
             }
             bar_wait(&raw_full[j], (it / R) & 1, abort_p);
-            const uint4 cv = *reinterpret_cast<const uint4*>(raw + j * rb + r * 32 + h * 16);
-            if (it >= 2) bar_wait(&a_empty[s], ((it >> 1) - 1) & 1, abort_p);
-            uint8_t* const as = atile + s * kATileBytes;
-            const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
+            uint32_t cw[4];
+            const uint32_t rec = raw_u32 + static_cast<uint32_t>(j * rb + G::w_off(n));
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(cw[0]), "=r"(cw[1]), "=r"(cw[2]), "=r"(cw[3])
+                         : "r"(rec + static_cast<uint32_t>(r * 32 + h * 16)));
+            if (WT == 2) asm volatile("ld.shared.f32 %0, [%1];" : "=f"(sc) : "r"(rec + static_cast<uint32_t>(kTcM * 32 + r * 4)));
+            if (it >= SA) bar_wait(&a_empty[s], ((it / SA) - 1) & 1, abort_p);
+            const uint32_t as = atile_u32 + static_cast<uint32_t>(s * kATileBytes);
+            const uint64_t ss = (static_cast<uint64_t>(__float_as_uint(sc)) << 32) | __float_as_uint(sc);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 uint32_t o[4];
+                const uint32_t w = cw[q];
+                // byte bb of w -> table offset byte * 128 (+ this lane's copy)
+                const uint32_t off[4] = {(w << 7) & 0x7F80u, (w >> 1) & 0x7F80u, (w >> 9) & 0x7F80u,
+                                         (w >> 17) & 0x7F80u};
 #pragma unroll
                 for (int bb = 0; bb < 4; ++bb) {
-                    const uint32_t byte = (cw[q] >> (8 * bb)) & 0xFFu;
-                    const float2 lv = mul_f32x2(*reinterpret_cast<const float2*>(tl + byte * (kPairCopies * 8)), sc);
-                    o[bb] = pack_bf16x2(lv.x, lv.y);  // even element (high nibble) in the low half
+                    // (level[hi], level[lo]) * absmax in fp32, rounded to a bf16 pair (even element low)
+                    asm("{\n\t.reg .b64 t;\n\t.reg .f32 lo, hi;\n\t"
+                        "ld.shared.b64 t, [%1];\n\t"
+                        "mul.rn.f32x2 t, t, %2;\n\t"
+                        "mov.b64 {lo, hi}, t;\n\t"
+                        "cvt.rn.bf16x2.f32 %0, hi, lo;\n\t}"
+                        : "=r"(o[bb])
+                        : "r"(tl_u32 + off[bb]), "l"(ss));
                 }
-                *reinterpret_cast<uint4*>(as + sw128_chunk(r, 4 * h + q)) = make_uint4(o[0], o[1], o[2], o[3]);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(as + sw128_chunk(r, 4 * h + q)),
+                             "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3])
+                             : "memory");
             }
             fence_proxy_async_smem();  // generic stores -> visible to the tensor core
             bar_arrive(&a_full[s]);
@@ -364,93 +389,144 @@ __global__ void __launch_bounds__(256) batch_rmsnorm_kernel(const uint16_t* x, c
             f32_to_bf16_bits(round_bf16(bf16_bits_to_f32(w[i]) * round_bf16(bf16_bits_to_f32(xb[i]) * inv)));
 }
 
-// bias + RoPE (Transformers' rotate_half with bf16 rounding) + K/V append at pos[b]
+// The epilogues work on tiles of consecutive rows x the padded batch: the
+// split-K partial sums [split][row][n_pad] are read row-contiguous (coalesced),
+// summed in split order (deterministic), staged in shared memory, and written
+// per sequence along the row (coalesced).
+constexpr int kEpiRows = 32;
+
+// sums of `nrows` rows starting at `row0` into t[row][b] (padded stride n_pad + 1);
+// the split loads of an element are independent (issued together), the adds
+// run in split order
+__device__ __forceinline__ void sum_tile(const float* partials, int ksplit, int rows, int n_pad, int row0, int nrows,
+                                         float* t) {
+    const int total = nrows * n_pad;
+    const int64_t kstride = static_cast<int64_t>(rows) * n_pad;
+    for (int e = threadIdx.x; e < total; e += blockDim.x) {
+        const int i = e / n_pad, b = e - i * n_pad;
+        const float* p = partials + static_cast<int64_t>(row0 + i) * n_pad + b;
+        float v = 0.F;
+        int k = 0;
+        for (; k + 4 <= ksplit; k += 4) {
+            const float a0 = __ldg(p + k * kstride), a1 = __ldg(p + (k + 1) * kstride);
+            const float a2 = __ldg(p + (k + 2) * kstride), a3 = __ldg(p + (k + 3) * kstride);
+            v += a0;
+            v += a1;
+            v += a2;
+            v += a3;
+        }
+        for (; k < ksplit; ++k) v += __ldg(p + k * kstride);
+        t[i * (n_pad + 1) + b] = v;
+    }
+}
+// rows per epilogue CTA: about 512 (row, sequence) elements
+__host__ __device__ __forceinline__ int epi_rows(int n_pad) { return n_pad >= 64 ? 8 : n_pad >= 32 ? 16 : 32; }
+
+// bias + RoPE (Transformers' rotate_half with bf16 rounding) + K/V append at
+// pos[b]; one CTA per (head of q | k | v, group of kQkvPairs dimension pairs
+// (i, i + head_dim / 2))
+constexpr int kQkvPairs = 16;
 __global__ void __launch_bounds__(256) batch_qkv_epilogue_kernel(const BatchQkv a) {
+    __shared__ float tq[2 * kQkvPairs * 65];  // [2 x kQkvPairs rows][n_pad + 1]
     pdl_launch_dependents();
     pdl_wait_on_producer();
-    const int hd = a.head_dim, half = hd / 2;
+    const int hd = a.head_dim, half = hd / 2, np1 = a.n_pad + 1;
     const int rows = (a.q_heads + 2 * a.kv_heads) * hd;
-    const int pairs = (a.q_heads + a.kv_heads) * half;  // RoPE pairs of q and k
-    const int vrows = a.kv_heads * hd;
-    const int per_b = pairs + vrows;
-    const int64_t total = static_cast<int64_t>(a.batch) * per_b;
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int b = static_cast<int>(idx / per_b), u = static_cast<int>(idx - static_cast<int64_t>(b) * per_b);
-        const int pos = a.pos[b];
-        if (pos < 0 || pos >= a.cap || pos >= a.max_pos) {
-            if (a.err != nullptr) atomicOr(a.err, 2);
-            continue;
-        }
-        if (u < pairs) {
-            const bool isq = u < a.q_heads * half;
-            const int uu = isq ? u : u - a.q_heads * half;
-            const int head = uu / half, i = uu - head * half;
-            const int base = (isq ? 0 : a.q_heads * hd) + head * hd;
-            float y0 = round_bf16(split_sum(a.partials, a.ksplit, rows, a.n_pad, base + i, b));
-            float y1 = round_bf16(split_sum(a.partials, a.ksplit, rows, a.n_pad, base + i + half, b));
-            const uint16_t* bias = isq ? a.q_bias : a.k_bias;
+    const int groups = half / kQkvPairs;
+    const int head = blockIdx.x / groups;  // 0 .. q_heads + 2 kv_heads - 1
+    const int i0 = (blockIdx.x - head * groups) * kQkvPairs;
+    sum_tile(a.partials, a.ksplit, rows, a.n_pad, head * hd + i0, kQkvPairs, tq);
+    sum_tile(a.partials, a.ksplit, rows, a.n_pad, head * hd + half + i0, kQkvPairs, tq + kQkvPairs * np1);
+    __syncthreads();
+    const bool isq = head < a.q_heads, isk = !isq && head < a.q_heads + a.kv_heads;
+    if (isq || isk) {
+        const uint16_t* bias = isq ? a.q_bias : a.k_bias;
+        const int hh = isq ? head : head - a.q_heads;
+        for (int e = threadIdx.x; e < a.batch * kQkvPairs; e += blockDim.x) {
+            const int b = e / kQkvPairs, ii = e - b * kQkvPairs, i = i0 + ii;
+            const int pos = a.pos[b];
+            if (pos < 0 || pos >= a.cap || pos >= a.max_pos) {
+                if (a.err != nullptr) atomicOr(a.err, 2);
+                continue;
+            }
+            float y0 = round_bf16(tq[ii * np1 + b]), y1 = round_bf16(tq[(kQkvPairs + ii) * np1 + b]);
             if (bias != nullptr) {
-                y0 = round_bf16(y0 + bf16_bits_to_f32(bias[head * hd + i]));
-                y1 = round_bf16(y1 + bf16_bits_to_f32(bias[head * hd + i + half]));
+                y0 = round_bf16(y0 + bf16_bits_to_f32(bias[hh * hd + i]));
+                y1 = round_bf16(y1 + bf16_bits_to_f32(bias[hh * hd + i + half]));
             }
             const float c = bf16_bits_to_f32(a.rope_cos[static_cast<int64_t>(pos) * half + i]);
             const float sn = bf16_bits_to_f32(a.rope_sin[static_cast<int64_t>(pos) * half + i]);
             const float lo = round_bf16(round_bf16(y0 * c) + round_bf16(-y1 * sn));
             const float hi = round_bf16(round_bf16(y1 * c) + round_bf16(y0 * sn));
-            if (isq) {
-                uint16_t* q = a.q_out + (static_cast<int64_t>(b) * a.q_heads + head) * hd;
-                q[i] = f32_to_bf16_bits(lo);
-                q[i + half] = f32_to_bf16_bits(hi);
-            } else {
-                uint16_t* kc = a.kcache + ((static_cast<int64_t>(b) * a.kv_heads + head) * a.cap + pos) * hd;
-                kc[i] = f32_to_bf16_bits(lo);
-                kc[i + half] = f32_to_bf16_bits(hi);
+            uint16_t* dst = isq ? a.q_out + (static_cast<int64_t>(b) * a.q_heads + hh) * hd
+                                : a.kcache + ((static_cast<int64_t>(b) * a.kv_heads + hh) * a.cap + pos) * hd;
+            dst[i] = f32_to_bf16_bits(lo);
+            dst[i + half] = f32_to_bf16_bits(hi);
+        }
+    } else {
+        const int hh = head - a.q_heads - a.kv_heads;
+        for (int e = threadIdx.x; e < a.batch * 2 * kQkvPairs; e += blockDim.x) {
+            const int b = e / (2 * kQkvPairs), q = e - b * 2 * kQkvPairs;
+            const int d = q < kQkvPairs ? i0 + q : half + i0 + q - kQkvPairs;
+            const int pos = a.pos[b];
+            if (pos < 0 || pos >= a.cap || pos >= a.max_pos) {
+                if (a.err != nullptr) atomicOr(a.err, 2);
+                continue;
             }
-        } else {
-            const int vr = u - pairs, head = vr / hd, d = vr - head * hd;
-            float y = round_bf16(split_sum(a.partials, a.ksplit, rows, a.n_pad, (a.q_heads + a.kv_heads) * hd + vr, b));
-            if (a.v_bias != nullptr) y = round_bf16(y + bf16_bits_to_f32(a.v_bias[vr]));
-            a.vcache[((static_cast<int64_t>(b) * a.kv_heads + head) * a.cap + pos) * hd + d] = f32_to_bf16_bits(y);
+            float y = round_bf16(tq[q * np1 + b]);
+            if (a.v_bias != nullptr) y = round_bf16(y + bf16_bits_to_f32(a.v_bias[hh * hd + d]));
+            a.vcache[((static_cast<int64_t>(b) * a.kv_heads + hh) * a.cap + pos) * hd + d] = f32_to_bf16_bits(y);
         }
     }
 }
 
-// x[b][r] = bf16(x[b][r] + bf16(sum))   (o_proj, down)
+// x[b][r] = bf16(x[b][r] + bf16(sum))   (o_proj, down); 32 rows per CTA
 __global__ void __launch_bounds__(256) batch_residual_kernel(const float* partials, int ksplit, int rows, int n_pad,
                                                              int batch, uint16_t* x) {
+    __shared__ float t[kEpiRows * 65];
     pdl_launch_dependents();
     pdl_wait_on_producer();
-    const int64_t total = static_cast<int64_t>(batch) * rows;
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int b = static_cast<int>(idx / rows), r = static_cast<int>(idx - static_cast<int64_t>(b) * rows);
-        uint16_t* xp = x + static_cast<int64_t>(b) * rows + r;
-        *xp = f32_to_bf16_bits(bf16_bits_to_f32(*xp) + round_bf16(split_sum(partials, ksplit, rows, n_pad, r, b)));
+    const int er = epi_rows(n_pad);
+    const int row0 = blockIdx.x * er;
+    const int nr = min(er, rows - row0);
+    sum_tile(partials, ksplit, rows, n_pad, row0, nr, t);
+    __syncthreads();
+    for (int e = threadIdx.x; e < batch * er; e += blockDim.x) {
+        const int b = e / er, i = e - b * er;
+        if (i < nr) {
+            uint16_t* xp = x + static_cast<int64_t>(b) * rows + row0 + i;
+            *xp = f32_to_bf16_bits(bf16_bits_to_f32(*xp) + round_bf16(t[i * (n_pad + 1) + b]));
+        }
     }
 }
 
-// h[b][j] = bf16(bf16(silu(bf16 gate_j)) * bf16 up_j); rows = gate (inter) | up (inter)
+// h[b][j] = bf16(bf16(silu(bf16 gate_j)) * bf16 up_j); rows = gate (inter) | up (inter); 32 j per CTA
 __global__ void __launch_bounds__(256) batch_swiglu_kernel(const float* partials, int ksplit, int inter, int n_pad,
                                                            int batch, uint16_t* h) {
+    __shared__ float tg[kEpiRows * 65], tu[kEpiRows * 65];
     pdl_launch_dependents();
     pdl_wait_on_producer();
-    const int rows = 2 * inter;
-    const int64_t total = static_cast<int64_t>(batch) * inter;
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int b = static_cast<int>(idx / inter), j = static_cast<int>(idx - static_cast<int64_t>(b) * inter);
-        const float g = round_bf16(split_sum(partials, ksplit, rows, n_pad, j, b));
-        const float u = round_bf16(split_sum(partials, ksplit, rows, n_pad, inter + j, b));
-        const float act = round_bf16(g / (1.0F + expf(-g)));
-        h[static_cast<int64_t>(b) * inter + j] = f32_to_bf16_bits(act * u);
+    const int er = epi_rows(n_pad);
+    const int j0 = blockIdx.x * er;
+    const int nr = min(er, inter - j0);
+    sum_tile(partials, ksplit, 2 * inter, n_pad, j0, nr, tg);
+    sum_tile(partials, ksplit, 2 * inter, n_pad, inter + j0, nr, tu);
+    __syncthreads();
+    for (int e = threadIdx.x; e < batch * er; e += blockDim.x) {
+        const int b = e / er, i = e - b * er;
+        if (i < nr) {
+            const float g = round_bf16(tg[i * (n_pad + 1) + b]);
+            const float u = round_bf16(tu[i * (n_pad + 1) + b]);
+            const float act = round_bf16(g / (1.0F + expf(-g)));
+            h[static_cast<int64_t>(b) * inter + j0 + i] = f32_to_bf16_bits(act * u);
+        }
     }
 }
 
 // Per-sequence greedy argmax over bf16-rounded logits (lowest index on ties):
 // stage 1 -- one (value, index) candidate per (CTA, sequence).  Lanes run over
 // sequences (coalesced partial reads), warps over vocabulary rows.
-constexpr int kArgCtas = 128;
+constexpr int kArgCtas = 512;
 __device__ __forceinline__ void arg_better(float& bv, int& bi, float v, int i) {
     if (v > bv || (v == bv && i < bi)) {
         bv = v;
@@ -466,12 +542,24 @@ __global__ void __launch_bounds__(256) batch_argmax_stage1(const float* partials
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float bv[2] = {-INFINITY, -INFINITY};
     int bi[2] = {0x7fffffff, 0x7fffffff};
-    for (int r = blockIdx.x * 8 + warp; r < vocab; r += kArgCtas * 8) {
+    // rows r, r + stride, ... of this warp, four at a time (independent loads; the
+    // candidates are merged in row order, so ties keep the lowest index)
+    const int stride = kArgCtas * 8;
+    for (int r = blockIdx.x * 8 + warp; r < vocab; r += 4 * stride) {
+        float v[4][2];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int b = lane + 32 * h;
-            if (b < batch) arg_better(bv[h], bi[h], round_bf16(split_sum(partials, ksplit, vocab, n_pad, r, b)), r);
-        }
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int rr = r + u * stride, b = lane + 32 * h;
+                v[u][h] = (rr < vocab && b < batch) ? round_bf16(split_sum(partials, ksplit, vocab, n_pad, rr, b))
+                                                    : -INFINITY;
+            }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                if (r + u * stride < vocab && lane + 32 * h < batch) arg_better(bv[h], bi[h], v[u][h], r + u * stride);
     }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -541,13 +629,50 @@ __global__ void batch_state_views_kernel(const int32_t* state, int batch, int32_
     }
 }
 
-int ew_grid(int64_t total) {
-    const int64_t g = (total + 255) / 256;
-    const int64_t cap = static_cast<int64_t>(device_sm_count()) * 8;
-    return static_cast<int>(g < 1 ? 1 : (g > cap ? cap : g));
-}
 
 }  // namespace
+
+namespace {
+// re-tile: record (t, kb) = codes of rows 128 t .. + 127, bytes 32 kb .. + 31,
+// then their absmax of block kb; rows past the matrix are zero
+__global__ void batch_retile_kernel(const uint8_t* packed, const float* absmax, int rows, int K, uint8_t* out) {
+    const int nblk = K / kBlockK;
+    const int tiles = (rows + kTcM - 1) / kTcM;
+    const int64_t units = static_cast<int64_t>(tiles) * nblk * (kRetileRecord / 16);
+    for (int64_t u = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; u < units;
+         u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t recn = u / (kRetileRecord / 16);
+        const int w = static_cast<int>(u - recn * (kRetileRecord / 16));  // 16-byte unit inside the record
+        const int t = static_cast<int>(recn / nblk), kb = static_cast<int>(recn - static_cast<int64_t>(t) * nblk);
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (w < kTcM * 2) {  // codes: row w / 2, half w % 2
+            const int row = t * kTcM + (w >> 1);
+            if (row < rows)
+                v = *reinterpret_cast<const uint4*>(packed + static_cast<int64_t>(row) * (K / 2) + kb * 32 + (w & 1) * 16);
+        } else {  // absmax of four rows
+            const int r0 = t * kTcM + (w - kTcM * 2) * 4;
+            float f[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) f[i] = r0 + i < rows ? absmax[static_cast<int64_t>(r0 + i) * nblk + kb] : 0.F;
+            v = make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+        }
+        *reinterpret_cast<uint4*>(out + recn * kRetileRecord + w * 16) = v;
+    }
+}
+}  // namespace
+
+int64_t batch_retile_bytes(int rows, int K) {
+    return static_cast<int64_t>((rows + kTcM - 1) / kTcM) * (K / kBlockK) * kRetileRecord;
+}
+
+cudaError_t batch_retile(const uint8_t* packed, const float* absmax, int rows, int K, uint8_t* out, cudaStream_t s) {
+    if (rows < 1 || K < kBlockK || K % kBlockK != 0) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(packed) | reinterpret_cast<uintptr_t>(out)) & 15u) return cudaErrorMisalignedAddress;
+    const int64_t units = batch_retile_bytes(rows, K) / 16;
+    const int64_t g = (units + 255) / 256;
+    const int grid = static_cast<int>(g < 4096 ? g : 4096);
+    return launch_pdl(batch_retile_kernel, dim3(grid), dim3(256), 0, s, packed, absmax, rows, K, out);
+}
 
 int batch_gemm_ksplit(int rows, int K) {
     // about two CTAs per SM, but at least 8 K blocks per CTA where K allows:
@@ -568,7 +693,9 @@ template <int WT>
 cudaError_t launch_gemm(const TcArgs& a, int ksplit, cudaStream_t s) {
     CUtensorMap mw, mx;
     cudaError_t st;
-    if (WT == 0)
+    if (WT == 2)
+        st = cudaSuccess;  // the re-tiled records come by bulk copy; map_w is unused
+    else if (WT == 0)
         st = encode_tmap_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.packed, a.K / 2, a.rows, a.K / 2, 32, kTcM,
                             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     else
@@ -576,16 +703,18 @@ cudaError_t launch_gemm(const TcArgs& a, int ksplit, cudaStream_t s) {
                             static_cast<uint64_t>(a.K) * 2, kBlockK, kTcM, CU_TENSOR_MAP_SWIZZLE_128B,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (st != cudaSuccess) return st;
+    if (WT == 2) memset(&mw, 0, sizeof(mw));
     st = encode_tmap_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, a.K, a.n_pad, static_cast<uint64_t>(a.K) * 2,
                         kBlockK, a.n_pad, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
     if (st != cudaSuccess) return st;
-    static thread_local int attr_dev[2] = {-1, -1};
+    static thread_local int attr_dev[3] = {-1, -1, -1};
     int dev = 0;
     st = cudaGetDevice(&dev);
     if (st != cudaSuccess) return st;
-    if (attr_dev[WT] != dev) {  // the largest footprint (n_pad 64 or 32) once per device
-        const int mx_bytes = GemmSmem<WT>::bytes(64) > GemmSmem<WT>::bytes(32) ? GemmSmem<WT>::bytes(64)
-                                                                                : GemmSmem<WT>::bytes(32);
+    if (attr_dev[WT] != dev) {  // the largest footprint over n_pad once per device
+        int mx_bytes = GemmSmem<WT>::bytes(16);
+        if (GemmSmem<WT>::bytes(32) > mx_bytes) mx_bytes = GemmSmem<WT>::bytes(32);
+        if (GemmSmem<WT>::bytes(64) > mx_bytes) mx_bytes = GemmSmem<WT>::bytes(64);
         st = cudaFuncSetAttribute(gemm_tc_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx_bytes);
         if (st != cudaSuccess) return st;
         attr_dev[WT] = dev;
@@ -600,7 +729,7 @@ cudaError_t batch_gemm(int weight_type, const void* weight, const float* absmax,
                        cudaStream_t s) {
     if (rows < 1 || K < kBlockK || K % kBlockK != 0 || !(n_pad == 16 || n_pad == 32 || n_pad == 64) || ksplit < 1 ||
         ksplit > K / kBlockK || row_offset < 0 || row_offset + rows > total_rows ||
-        (weight_type != 0 && weight_type != 1) || (weight_type == 0 && absmax == nullptr))
+        weight_type < 0 || weight_type > 2 || (weight_type == 0 && absmax == nullptr))
         return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(x) |
          reinterpret_cast<uintptr_t>(partials) | reinterpret_cast<uintptr_t>(absmax)) & 15u)
@@ -618,6 +747,7 @@ cudaError_t batch_gemm(int weight_type, const void* weight, const float* absmax,
     a.row_offset = row_offset;
     a.total_rows = total_rows;
     a.err = err;
+    if (weight_type == 2) return launch_gemm<2>(a, ksplit, s);
     return weight_type == 0 ? launch_gemm<0>(a, ksplit, s) : launch_gemm<1>(a, ksplit, s);
 }
 
@@ -627,21 +757,25 @@ cudaError_t batch_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* out, i
 }
 
 cudaError_t batch_qkv_epilogue(const BatchQkv& q, cudaStream_t s) {
-    const int64_t total =
-        static_cast<int64_t>(q.batch) * ((q.q_heads + q.kv_heads) * (q.head_dim / 2) + q.kv_heads * q.head_dim);
-    return launch_pdl(batch_qkv_epilogue_kernel, dim3(ew_grid(total)), dim3(256), 0, s, q);
+    if (q.n_pad > 64 || q.head_dim % (2 * kQkvPairs) != 0) return cudaErrorInvalidValue;
+    const int groups = q.head_dim / 2 / kQkvPairs;
+    return launch_pdl(batch_qkv_epilogue_kernel, dim3((q.q_heads + 2 * q.kv_heads) * groups), dim3(256), 0, s, q);
 }
 
 cudaError_t batch_residual(const float* partials, int ksplit, int rows, int n_pad, int batch, uint16_t* x,
                            cudaStream_t s) {
-    return launch_pdl(batch_residual_kernel, dim3(ew_grid(static_cast<int64_t>(batch) * rows)), dim3(256), 0, s,
-                      partials, ksplit, rows, n_pad, batch, x);
+    if (n_pad > 64) return cudaErrorInvalidValue;
+    const int er = epi_rows(n_pad);
+    return launch_pdl(batch_residual_kernel, dim3((rows + er - 1) / er), dim3(256), 0, s, partials, ksplit,
+                      rows, n_pad, batch, x);
 }
 
 cudaError_t batch_swiglu(const float* partials, int ksplit, int inter, int n_pad, int batch, uint16_t* h,
                          cudaStream_t s) {
-    return launch_pdl(batch_swiglu_kernel, dim3(ew_grid(static_cast<int64_t>(batch) * inter)), dim3(256), 0, s,
-                      partials, ksplit, inter, n_pad, batch, h);
+    if (n_pad > 64) return cudaErrorInvalidValue;
+    const int er = epi_rows(n_pad);
+    return launch_pdl(batch_swiglu_kernel, dim3((inter + er - 1) / er), dim3(256), 0, s, partials, ksplit,
+                      inter, n_pad, batch, h);
 }
 
 int batch_argmax_workspace_floats(int batch) { return 2 * batch * kArgCtas; }

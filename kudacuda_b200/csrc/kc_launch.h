@@ -184,10 +184,14 @@ struct PersistLaunch {
     int* err;
 };
 // ---- batched decode (batched.cu) ----------------------------------------------
-// NF4 (weight_type 0) or bf16 (1) weights [rows][K] times bf16 activations
+// NF4 (weight_type 0), bf16 (1) or re-tiled NF4 (2) weights [rows][K] times bf16 activations
 // [n_pad][K] (rows >= batch zero) on the tcgen05 tensor cores: fp32 split-K
 // partials[(split * total_rows + row_offset + r) * n_pad + b].
 int batch_gemm_ksplit(int rows, int K);
+// NF4 re-tiled for the GEMM (weight_type 2): per 128-row tile and 64-element
+// K block one 4,608-byte record (codes [128][32 B], absmax [128] fp32)
+int64_t batch_retile_bytes(int rows, int K);
+cudaError_t batch_retile(const uint8_t* packed, const float* absmax, int rows, int K, uint8_t* out, cudaStream_t s);
 cudaError_t batch_gemm(int weight_type, const void* weight, const float* absmax, int rows, int K, const uint16_t* x,
                        int n_pad, int ksplit, float* partials, int row_offset, int total_rows, int* err,
                        cudaStream_t s);

@@ -1050,11 +1050,11 @@ int kudacuda_sm100_batch_gemm(void* raw, int weight_type, uint64_t weight, uint6
                               int64_t total_rows, uint64_t stream) {
     Handle* h = as_handle(raw);
     if (!ready(h, "kudacuda_sm100_batch_gemm")) return 1;
-    if (weight == 0 || x == 0 || partials == 0 || (weight_type == 0 && absmax == 0) ||
-        (weight_type != 0 && weight_type != 1) || rows < 1 || rows > (1 << 24) || k < 64 || k % 64 != 0 ||
+    if (weight == 0 || x == 0 || partials == 0 || (weight_type == 0 && absmax == 0) || weight_type < 0 ||
+        weight_type > 2 || rows < 1 || rows > (1 << 24) || k < 64 || k % 64 != 0 ||
         k > (1 << 20) || !npad_ok(n_pad) || ksplit < 1 || ksplit > k / 64 || row_offset < 0 ||
         total_rows > (1 << 24) || row_offset + rows > total_rows) {
-        h->set_error("sm100_batch_gemm requires weight_type 0 (NF4 + absmax) or 1 (bf16), K % 64 == 0, n_pad in "
+        h->set_error("sm100_batch_gemm requires weight_type 0 (NF4 + absmax), 1 (bf16) or 2 (re-tiled NF4), K % 64 == 0, n_pad in "
                      "{16, 32, 64}, 1 <= ksplit <= K/64, row_offset + rows <= total_rows, non-null pointers");
         return 1;
     }
@@ -1063,6 +1063,26 @@ int kudacuda_sm100_batch_gemm(void* raw, int weight_type, uint64_t weight, uint6
                                  static_cast<int>(k), P<const uint16_t>(x), static_cast<int>(n_pad),
                                  static_cast<int>(ksplit), P<float>(partials), static_cast<int>(row_offset),
                                  static_cast<int>(total_rows), h->err_word, S(stream)));
+}
+
+int64_t kudacuda_sm100_batch_retile_bytes(int64_t rows, int64_t k) {
+    if (rows < 1 || k < 64 || k % 64 != 0 || rows > (1 << 24) || k > (1 << 20)) return -1;
+    return kc::batch_retile_bytes(static_cast<int>(rows), static_cast<int>(k));
+}
+
+int kudacuda_sm100_batch_retile(void* raw, uint64_t packed, uint64_t absmax, int64_t rows, int64_t k, uint64_t out,
+                                int64_t out_bytes, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_retile")) return 1;
+    const int64_t need = kudacuda_sm100_batch_retile_bytes(rows, k);
+    if (packed == 0 || absmax == 0 || out == 0 || need < 0 || out_bytes < need) {
+        h->set_error("sm100_batch_retile requires non-null pointers, K % 64 == 0 and out_bytes >= "
+                     "kudacuda_sm100_batch_retile_bytes(rows, k)");
+        return 1;
+    }
+    return finish(h, "batch_retile_kernel",
+                  kc::batch_retile(P<const uint8_t>(packed), P<const float>(absmax), static_cast<int>(rows),
+                                   static_cast<int>(k), P<uint8_t>(out), S(stream)));
 }
 
 int kudacuda_sm100_batch_rmsnorm(void* raw, uint64_t x, uint64_t weight, uint64_t out, int64_t batch, int64_t hidden,

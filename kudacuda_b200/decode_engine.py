@@ -715,6 +715,29 @@ def greedy_generate(plan: StaticDecodePlan, prompt: list[int], new_tokens: int, 
 
 # ---------------------------------------------------------------------- batched decode
 @dataclass
+class RetiledNF4:
+    data: Any  # uint8: one 4,608-byte record per 128-row tile and 64-element K block
+    rows: int
+    k: int
+
+
+def retile_nf4(bridge: KudaCudaBridge, torch: Any, lins: list[NF4Linear], stream_ptr: int) -> RetiledNF4:
+    """Row-concatenate NF4 matrices (same K) and copy them into the batched
+    GEMM's streaming form (kudacuda_sm100_batch_retile)."""
+
+    rows = sum(l.rows for l in lins)
+    k = lins[0].k
+    if len(lins) == 1:
+        packed, absmax = lins[0].packed, lins[0].absmax
+    else:
+        packed = torch.cat([l.packed.reshape(-1) for l in lins])
+        absmax = torch.cat([l.absmax.reshape(-1) for l in lins])
+    out = torch.empty(bridge.batch_retile_bytes(rows, k), dtype=torch.uint8, device=packed.device)
+    bridge.dispatch_batch_retile(packed, absmax, out, rows=rows, k=k, stream_ptr=stream_ptr)
+    return RetiledNF4(out, rows, k)
+
+
+@dataclass
 class BatchedBuffers:
     state: Any  # int32 [B, 4]: token, position, kv_len, (pad) per sequence
     pos: Any  # int32 [B] (the positions, for the RoPE epilogue)
@@ -740,8 +763,9 @@ class BatchedDecodePlan:
     position and KV length) on one device.  Every projection is one tensor-core
     GEMM over the padded batch (``kudacuda_sm100_batch_gemm``: NF4 dequantised
     to bf16 in shared memory, tcgen05 MMA, fp32 accumulator in TMEM) followed
-    by a small epilogue; q|k|v and gate|up are concatenated once at plan build
-    so each is one GEMM.  The lm_head is the same GEMM over the bf16 tied
+    by a small epilogue; every NF4 matrix is re-tiled once at plan build into
+    the GEMM's streaming form, q|k|v and gate|up concatenated so each is one
+    GEMM.  The lm_head is the same GEMM over the bf16 tied
     embedding (or the NF4 lm_head), then a per-sequence argmax that advances
     each sequence's state.  The step is captured into the handle's CUDA graph.
 
@@ -772,15 +796,21 @@ class BatchedDecodePlan:
         d = c.head_dim
         max_tokens = int(max_tokens or cap)
         bf16 = torch.bfloat16
-        # q|k|v and gate|up concatenated by rows (NF4 rows and their absmax concatenate)
-        self.qkv: list[NF4Linear] = []
-        self.gu: list[NF4Linear] = []
+        # every projection re-tiled once into the GEMM's streaming form (one
+        # contiguous record per 128-row tile and K block); q|k|v and gate|up
+        # are concatenated by rows first (NF4 rows and their absmax concatenate)
+        sp0 = int(torch.cuda.current_stream(device).cuda_stream)
+        self.qkv: list[RetiledNF4] = []
+        self.gu: list[RetiledNF4] = []
+        self.o: list[RetiledNF4] = []
+        self.down: list[RetiledNF4] = []
         for L in weights.layers:
-            self.qkv.append(NF4Linear(torch.cat([L.q.packed, L.k.packed, L.v.packed]),
-                                      torch.cat([L.q.absmax, L.k.absmax, L.v.absmax]),
-                                      L.q.rows + L.k.rows + L.v.rows, L.q.k))
-            self.gu.append(NF4Linear(torch.cat([L.gate.packed, L.up.packed]), torch.cat([L.gate.absmax, L.up.absmax]),
-                                     L.gate.rows + L.up.rows, L.gate.k))
+            self.qkv.append(retile_nf4(bridge, torch, [L.q, L.k, L.v], sp0))
+            self.gu.append(retile_nf4(bridge, torch, [L.gate, L.up], sp0))
+            self.o.append(retile_nf4(bridge, torch, [L.o], sp0))
+            self.down.append(retile_nf4(bridge, torch, [L.down], sp0))
+        self.lm_nf4 = retile_nf4(bridge, torch, [weights.lm_head], sp0) if weights.lm_head is not None else None
+        torch.cuda.synchronize(device)
         self.qkv_rows = self.qkv[0].rows
         ks = bridge.batch_gemm_ksplit
         self.ks_qkv = ks(self.qkv_rows, c.hidden)
@@ -827,11 +857,10 @@ class BatchedDecodePlan:
                                        w.embedding, w.final_norm)]
         for li, L in enumerate(w.layers):
             ptrs += [L.in_norm.data_ptr(), L.post_norm.data_ptr()]
-            for lin in (self.qkv[li], L.o, self.gu[li], L.down):
-                ptrs += [lin.packed.data_ptr(), lin.absmax.data_ptr()]
+            ptrs += [t.data.data_ptr() for t in (self.qkv[li], self.o[li], self.gu[li], self.down[li])]
             ptrs += [0 if t is None else t.data_ptr() for t in (L.q_bias, L.k_bias, L.v_bias)]
-        if w.lm_head is not None:
-            ptrs += [w.lm_head.packed.data_ptr(), w.lm_head.absmax.data_ptr()]
+        if self.lm_nf4 is not None:
+            ptrs.append(self.lm_nf4.data.data_ptr())
         d = c.head_dim
         return DecodeGraphKey(
             device_id=int(self.torch.device(self.device).index or 0),
@@ -848,9 +877,9 @@ class BatchedDecodePlan:
             quantization="nf4-blocksize64-fp32absmax",
         )
 
-    def _gemm(self, lin: NF4Linear, x: Any, ksplit: int, sp: int) -> None:
-        self.bridge.dispatch_batch_gemm(lin.packed, lin.absmax, x, self.buffers.partials, weight_type=0,
-                                        rows=lin.rows, k=lin.k, n_pad=self.n_pad, ksplit=ksplit, stream_ptr=sp)
+    def _gemm(self, lin: "RetiledNF4", x: Any, ksplit: int, sp: int) -> None:
+        self.bridge.dispatch_batch_gemm(lin.data, None, x, self.buffers.partials, weight_type=2, rows=lin.rows,
+                                        k=lin.k, n_pad=self.n_pad, ksplit=ksplit, stream_ptr=sp)
 
     def record(self, stream_ptr: int) -> int:
         """Enqueue one batched decode step; returns the number of kernels."""
@@ -872,14 +901,14 @@ class BatchedDecodePlan:
             br.dispatch_gqa_decode_batch(b.q, b.kcache[li], b.vcache[li], b.attn, b.gqa_ws, b.gqa_tickets, b.kv_len,
                                          batch=B, kv_stride=self.kv_bucket, query_heads=self.q_heads,
                                          kv_heads=self.kv_heads, head_dim=d, scale=scale, stream_ptr=sp)
-            self._gemm(L.o, b.attn, self.ks_o, sp)
+            self._gemm(self.o[li], b.attn, self.ks_o, sp)
             br.dispatch_batch_residual(b.partials, b.x, ksplit=self.ks_o, rows=c.hidden, n_pad=npad, batch=B,
                                        stream_ptr=sp)
             br.dispatch_batch_rmsnorm(b.x, L.post_norm, b.xn, batch=B, hidden=c.hidden, epsilon=c.eps, stream_ptr=sp)
             self._gemm(self.gu[li], b.xn, self.ks_gu, sp)
             br.dispatch_batch_swiglu(b.partials, b.h, ksplit=self.ks_gu, intermediate=self.inter, n_pad=npad, batch=B,
                                      stream_ptr=sp)
-            self._gemm(L.down, b.h, self.ks_dn, sp)
+            self._gemm(self.down[li], b.h, self.ks_dn, sp)
             br.dispatch_batch_residual(b.partials, b.x, ksplit=self.ks_dn, rows=c.hidden, n_pad=npad, batch=B,
                                        stream_ptr=sp)
             n += 11
@@ -888,7 +917,7 @@ class BatchedDecodePlan:
             br.dispatch_batch_gemm(w.embedding, None, b.xn, b.partials, weight_type=1, rows=c.vocab, k=c.hidden,
                                    n_pad=npad, ksplit=self.ks_lm, stream_ptr=sp)
         else:
-            self._gemm(w.lm_head, b.xn, self.ks_lm, sp)
+            self._gemm(self.lm_nf4, b.xn, self.ks_lm, sp)
         br.dispatch_batch_argmax_advance(b.partials, b.arg_ws, b.state, b.history, ksplit=self.ks_lm, vocab=c.vocab,
                                          n_pad=npad, batch=B, stream_ptr=sp)
         n += 4

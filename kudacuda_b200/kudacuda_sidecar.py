@@ -1140,11 +1140,24 @@ class KudaCudaBridge:
             raise ValueError(f"batch_gemm_ksplit: unsupported shape rows={rows} k={k}")
         return n
 
+    def batch_retile_bytes(self, rows: int, k: int) -> int:
+        n = int(self.lib.kudacuda_sm100_batch_retile_bytes(int(rows), int(k)))
+        if n < 0:
+            raise ValueError(f"batch_retile_bytes: unsupported shape rows={rows} k={k}")
+        return n
+
+    def dispatch_batch_retile(self, packed: Any, absmax: Any, out: Any, *, rows: int, k: int, stream_ptr: int) -> None:
+        """bitsandbytes NF4 -> the batched GEMM's streaming form (weight_type 2)."""
+
+        self._call("kudacuda_sm100_batch_retile", self._tensor_pointer(packed, "packed"),
+                   self._tensor_pointer(absmax, "absmax"), int(rows), int(k), self._tensor_pointer(out, "out"),
+                   int(out.numel()) * int(out.element_size()), _normalize_cuda_handle(stream_ptr))
+
     def dispatch_batch_gemm(self, weight: Any, absmax: Any, x: Any, partials: Any, *, weight_type: int, rows: int,
                             k: int, n_pad: int, ksplit: int, row_offset: int = 0, total_rows: int | None = None,
                             stream_ptr: int) -> None:
         """fp32 split-K partials of W . x^T for a padded batch on the tensor cores
-        (weight_type 0: NF4 + absmax, 1: bf16)."""
+        (weight_type 0: NF4 + absmax, 1: bf16, 2: NF4 re-tiled by dispatch_batch_retile)."""
 
         total = int(rows if total_rows is None else total_rows)
         if int(x.numel()) != int(n_pad) * int(k):

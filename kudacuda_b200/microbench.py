@@ -9,7 +9,7 @@ KV rows for attention).
 
     python -m kudacuda_b200.microbench --op swiglu [--copies 12 --launches 36 --reps 20]
     ops: gemv_11008x2048 gemv_2048x11008 qkv_rope oproj down swiglu gqa512 gqa2048 lm_head all
-         bgemm_<rows>x<k>_n<n_pad>[_ks<ksplit>][_bf16]  (batched tensor-core GEMM, e.g. bgemm_22016x2048_n64)
+         bgemm_<rows>x<k>_n<n_pad>[_ks<ksplit>][_bf16|_rt]  (batched tensor-core GEMM; _rt: re-tiled NF4)
 
     python -m kudacuda_b200.microbench --op persistent --layers 36 --kv 512 [--launches 3 --reps 20]
       the persistent all-layers kernel alone (Qwen2.5-3B layer shapes, random
@@ -140,9 +140,16 @@ def build_cases(torch, bridge: KudaCudaBridge, names: list[str], copies: int, de
             rows, k = (int(v) for v in parts[1].split("x"))
             npad = int(parts[2][1:])
             ks = next((int(p[2:]) for p in parts[3:] if p.startswith("ks")), 0) or bridge.batch_gemm_ksplit(rows, k)
-            wt = 1 if "bf16" in parts[3:] else 0
+            wt = 1 if "bf16" in parts[3:] else (2 if "rt" in parts[3:] else 0)
             if wt == 0:
                 W = _nf4(torch, rows, k, copies, device)
+            elif wt == 2:  # re-tiled streaming form
+                W = []
+                for p_, a_ in _nf4(torch, rows, k, copies, device):
+                    rt = torch.empty(bridge.batch_retile_bytes(rows, k), dtype=torch.uint8, device=device)
+                    bridge.dispatch_batch_retile(p_, a_, rt, rows=rows, k=k, stream_ptr=0)
+                    W.append((rt, None))
+                torch.cuda.synchronize()
             else:
                 W = [(torch.randn((rows, k), device=device).to(bf16), None) for _ in range(copies)]
             xb = torch.randn((npad, k), device=device).to(bf16)

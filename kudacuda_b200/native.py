@@ -75,6 +75,8 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     ),
     "kudacuda_sm100_batch_gemm_ksplit": (_i64, [_i64, _i64]),
     "kudacuda_sm100_batch_gemm": (_i32, [_p, _i32, _u64, _u64, _i64, _i64, _u64, _i64, _i64, _u64, _i64, _i64, _u64]),
+    "kudacuda_sm100_batch_retile_bytes": (_i64, [_i64, _i64]),
+    "kudacuda_sm100_batch_retile": (_i32, [_p, _u64, _u64, _i64, _i64, _u64, _i64, _u64]),
     "kudacuda_sm100_batch_rmsnorm": (_i32, [_p, _u64, _u64, _u64, _i64, _i64, _f32, _u64]),
     "kudacuda_sm100_batch_qkv_rope": (
         _i32, [_p, _u64, _i64, _i64, _i64, _i64, _i64, _i64] + [_u64] * 5 + [_i64] + [_u64] * 4 + [_i64, _u64]

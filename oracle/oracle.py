@@ -378,3 +378,21 @@ def batch_gemm_ref(packed: np.ndarray, absmax: np.ndarray | None, rows: int, k: 
         w = bf16_to_f32(np.asarray(packed, dtype=np.uint16)).reshape(rows, k).astype(np.float64)
     x = bf16_to_f32(np.asarray(x_bits, dtype=np.uint16)).reshape(-1, k).astype(np.float64)
     return w @ x.T, np.abs(w) @ np.abs(x).T
+
+
+def batch_retile(packed: np.ndarray, absmax: np.ndarray, rows: int, k: int) -> np.ndarray:
+    """The batched GEMM's streaming form of an NF4 matrix (a load-time move of
+    the bitsandbytes storage, kernels/common/nf4_device.cuh:29-40, no value
+    changed): per 128-row tile t and 64-element K block kb one 4,608-byte
+    record = codes of rows 128t..128t+127, bytes 32kb..32kb+31 ([128][32]),
+    then those rows' absmax of block kb (128 fp32); rows past the matrix zero."""
+
+    nblk = k // 64
+    tiles = (rows + 127) // 128
+    codes = np.zeros((tiles * 128, k // 2), dtype=np.uint8)
+    codes[:rows] = np.asarray(packed, dtype=np.uint8).reshape(rows, k // 2)
+    am = np.zeros((tiles * 128, nblk), dtype=np.float32)
+    am[:rows] = np.asarray(absmax, dtype=np.float32).reshape(rows, nblk)
+    c = codes.reshape(tiles, 128, nblk, 32).transpose(0, 2, 1, 3).reshape(tiles, nblk, 4096)
+    a = am.reshape(tiles, 128, nblk).transpose(0, 2, 1).copy().view(np.uint8).reshape(tiles, nblk, 512)
+    return np.concatenate([c, a], axis=2).reshape(-1)

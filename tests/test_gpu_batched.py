@@ -1,6 +1,8 @@
 """GPU parity of the batched decode path (B independent sequences per step),
 through the C ABI via the bridge.
 
+* the device re-tile (kudacuda_sm100_batch_retile) against the oracle's numpy
+  restatement, bit-exact;
 * the tcgen05 GEMM (kudacuda_sm100_batch_gemm) against the oracle's batched
   projection (bf16-dequantised NF4 times bf16 activations, exact in float64):
   every element within 1e-4 of the sum of |w * x| (fp32 accumulation over up
@@ -44,6 +46,10 @@ def bridge():
         (2560, 2048, 64, 64, 0, 0),   # q|k|v rows, full batch, suggested split
         (2048, 11008, 33, 64, 0, 0),  # down_proj shape
         (1000, 512, 3, 16, 2, 1),     # bf16 weights (lm_head form)
+        (300, 256, 5, 16, 1, 2),      # re-tiled NF4, ragged last tile
+        (2560, 2048, 64, 64, 0, 2),   # re-tiled q|k|v
+        (2048, 11008, 40, 64, 0, 2),  # re-tiled down_proj
+        (4352, 2048, 30, 32, 3, 2),   # re-tiled, n_pad 32, uneven split
     ],
 )
 def test_batch_gemm_against_oracle(bridge, rows, k, batch, n_pad, ksplit, weight_type):
@@ -54,10 +60,16 @@ def test_batch_gemm_against_oracle(bridge, rows, k, batch, n_pad, ksplit, weight
     w = (torch.randn((rows, k), generator=g) * 0.02).to(torch.bfloat16)
     x = torch.zeros((n_pad, k), dtype=torch.bfloat16)
     x[:batch] = torch.randn((batch, k), generator=g).to(torch.bfloat16)
-    if weight_type == 0:
+    if weight_type in (0, 2):
         packed, absmax = O.nf4_quantize(O.bf16_to_f32(w.view(torch.int16).numpy().view(np.uint16)).reshape(-1))
         wd = torch.from_numpy(np.ascontiguousarray(packed)).to(dev)
         ad = torch.from_numpy(np.ascontiguousarray(absmax)).to(dev)
+        if weight_type == 2:
+            rt = torch.empty(bridge.batch_retile_bytes(rows, k), dtype=torch.uint8, device=dev)
+            bridge.dispatch_batch_retile(wd, ad, rt, rows=rows, k=k, stream_ptr=0)
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(rt.cpu().numpy(), O.batch_retile(packed, absmax, rows, k))
+            wd, ad = rt, None
     else:
         packed, absmax = w.view(torch.int16).numpy().view(np.uint16), None
         wd, ad = w.to(dev), None
@@ -77,7 +89,7 @@ def test_batch_gemm_against_oracle(bridge, rows, k, batch, n_pad, ksplit, weight
     assert np.all(p[:, :17] == sentinel) and np.all(p[:, 17 + rows:] == sentinel)
     got = p[:, 17:17 + rows].sum(axis=0)
     ref, mag = O.batch_gemm_ref(packed, absmax, rows, k, x.view(torch.int16).numpy().view(np.uint16),
-                                weight_type=weight_type)
+                                weight_type=min(weight_type, 1) if weight_type != 2 else 0)
     assert np.all(got[:, batch:] == 0.0)
     err = np.abs(got - ref)
     bound = 1e-4 * mag + 1e-6
