@@ -627,6 +627,160 @@ def run_tp(args) -> dict | None:
     return out
 
 
+def run_tp_batched(args) -> dict | None:
+    """Config 5 at batch B (BASELINE: batch 32): the Llama-3-8B-architecture
+    NF4 model tensor-parallel over the ranks with the batched tensor-core
+    path -- column-parallel q/k/v and gate/up, row-parallel o_proj and down
+    (split sums allreduced over NCCL), vocabulary-parallel NF4 lm_head (per
+    sequence argmax pairs, allgather, select) -- all in one captured graph.
+    B sequences at position 128 (random cache rows stand in for the 128-token
+    prompts); a step advances every sequence by one token; value = B * K /
+    time (strong scaling: the same work at every world size)."""
+
+    import datetime
+
+    import torch
+
+    from kudacuda_b200.decode_engine import LLAMA3_8B, BatchedDecodePlan, random_weights
+    from kudacuda_b200.kudacuda_sidecar import KudaCudaBridge
+
+    rank, world, local = _dist_env()
+    torch.cuda.set_device(local)
+    device = f"cuda:{local}"
+    dist = None
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        group = dist.group.WORLD
+    cfg = LLAMA3_8B
+    if cfg.kv_heads % world or cfg.q_heads % world or cfg.intermediate % world or cfg.vocab % world:
+        raise SystemExit(f"Llama-3-8B does not shard over {world} ranks")
+    B = args.batch
+    prompt_len, bucket = 128, 512
+    if prompt_len + 2 * (args.warmup + args.steps) + 2 > bucket:
+        raise SystemExit(f"prompt + warmup + steps must fit the KV bucket of {bucket}")
+    bridge = KudaCudaBridge(device_id=local)
+    weights = random_weights(bridge, cfg, seed=SEED, device=device, shard=(rank, world))
+    plan = BatchedDecodePlan(bridge, weights, batch=B, kv_bucket=bucket, max_tokens=bucket, device=device,
+                             allreduce=(rank, world, group))
+    stream = torch.cuda.Stream(device=device)
+    plan.capture(stream)
+    gd = torch.Generator(device=device).manual_seed(SEED + rank)
+    for li in range(cfg.layers):
+        plan.buffers.kcache[li].normal_(generator=gd)
+        plan.buffers.vcache[li].normal_(generator=gd)
+    g = torch.Generator().manual_seed(SEED)
+    toks = torch.randint(0, cfg.vocab, (B,), generator=g).tolist()  # the same on every rank
+    plan.set_state(toks, [prompt_len] * B, stream)
+    for _ in range(args.warmup):
+        plan.replay(stream)
+    stream.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            plan.replay(stream)
+        end.record(stream)
+        end.synchronize()
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end)
+    if dist is not None:
+        dist.barrier()
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    err = bridge.error_word(clear=True)
+    # ---- end to end: per step the host writes every sequence's state from
+    # pinned memory and reads the advanced state back, around the graph replay
+    host_in = plan.buffers.state.cpu().pin_memory()
+    host_out = torch.zeros_like(host_in).pin_memory()
+    for phase in ("warm", "timed"):
+        if dist is not None:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.warmup if phase == "warm" else args.steps):
+            with torch.cuda.stream(stream):
+                plan.buffers.state.copy_(host_in, non_blocking=True)
+            plan.replay(stream)
+            with torch.cuda.stream(stream):
+                host_out.copy_(plan.buffers.state, non_blocking=True)
+            stream.synchronize()
+            host_in.copy_(host_out)
+        e2e_s = time.perf_counter() - t0
+    if dist is not None:
+        t = torch.tensor([e2e_s], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    # the ranks must agree on every sequence's tokens
+    st = plan.buffers.state.clone()
+    agree = True
+    if dist is not None:
+        other = st.clone()
+        dist.broadcast(other, src=0)
+        flag = torch.tensor([1 if torch.equal(other, st) else 0], device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        agree = bool(flag.item())
+    plan.release()  # the graph holds NCCL work: release it before the process group
+    out = None
+    if rank == 0:
+        wb = cfg.weight_bytes_per_token()
+        kv = B * cfg.kv_bytes_per_token(prompt_len + args.warmup + args.steps // 2)
+        bytes_step = sum(wb.values()) + kv
+        peak, peak_src = _peaks()
+        ms_step = ms / args.steps
+        out = {
+            "metric": "batched decode tok/s (tensor-parallel)",
+            "value": round(B * args.steps / (ms / 1e3), 1),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "nf4-weights/bf16-dequant/bf16-activations/f32-accumulate",
+            "data": "synthetic (random-init weights N(0,0.02) NF4-quantised on device; random N(0,1) cache rows)",
+            "config": {
+                "workload": f"config5: Llama-3-8B-architecture NF4 decode, batch {B}, tensor-parallel, static CUDA graph",
+                "batch": B,
+                "kv_len_timed": [prompt_len, prompt_len + args.warmup + args.steps],
+                "kv_bucket": bucket,
+                "parallelism": f"tp{world}",
+                "l2": "inputs larger than L2 (4.5 GB of weights per step / world)",
+            },
+            "hbm_roofline_per_step": {
+                "bytes_per_step_all_ranks": bytes_step,
+                "bytes_per_gpu": bytes_step // world,
+                "achieved_gbs_per_gpu": round(bytes_step / world / (ms_step * 1e-3) / 1e9, 1),
+                "frac_of_measured_peak": round(bytes_step / world / (ms_step * 1e-3) / 1e9 / peak, 4),
+                "peak_source": peak_src,
+            },
+            "e2e": {
+                "value": round(B * args.steps / e2e_s, 1),
+                "unit": "tok/s",
+                "h2d_bytes_per_step": 16 * B,
+                "d2h_bytes_per_step": 16 * B,
+                "api": "host int32 [B][4] state in, graph replay, state out, per step",
+            },
+            "ranks_agree_on_tokens": agree,
+            "device_error_word": err,
+            "gpu_launches": plan.launches_per_step * args.steps,
+            "launches_per_step": plan.launches_per_step,
+            "clocks": clocks.summary(),
+        }
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
 def run_batched(args) -> dict | None:
     """batched decode of the Qwen2.5-3B-architecture model,
     B independent sequences with uniform-random prompt lengths 32-512 in
@@ -850,7 +1004,8 @@ def main(argv=None) -> int:
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--workload", choices=["qwen3b", "llama8b-tp", "qwen3b-batched"], default="qwen3b")
-    p.add_argument("--batch", type=int, default=64, help="sequences per step for --workload qwen3b-batched")
+    p.add_argument("--batch", type=int, default=None,
+                   help="sequences per step: --workload qwen3b-batched (default 64) or llama8b-tp (default 1)")
     p.add_argument("--path", choices=["persistent", "per-op"], default="persistent",
                    help="persistent: all layers in one cooperative launch; per-op: one launch per op")
     args = p.parse_args(argv)
@@ -859,8 +1014,9 @@ def main(argv=None) -> int:
     if args.impl == "reference":
         out = run_reference(args)
     elif args.workload == "llama8b-tp":
-        out = run_tp(args)
+        out = run_tp(args) if args.batch in (None, 1) else run_tp_batched(args)
     elif args.workload == "qwen3b-batched":
+        args.batch = args.batch or 64
         out = run_batched(args)
     else:
         out = run_gpu(args)

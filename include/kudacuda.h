@@ -400,6 +400,25 @@ KUDACUDA_API int kudacuda_sm100_batch_embedding(void* handle, uint64_t embedding
                                                 int64_t batch, int64_t hidden, int64_t vocab, uint64_t stream);
 KUDACUDA_API int kudacuda_sm100_batch_state_views(void* handle, uint64_t state, int64_t batch, uint64_t pos,
                                                   uint64_t kv_len, uint64_t stream);
+/* Tensor parallelism around the NCCL collectives of a batched step:
+ * batch_split_sum: out[r][b] = sum of the splits of a row-parallel GEMM's
+ *   partials (split order), fp32 [rows][n_pad] -- the rank's partial that the
+ *   caller allreduces, then adds with batch_residual (ksplit 1);
+ * batch_argmax_pairs: per sequence, this rank's lowest-index maximum of the
+ *   bf16-rounded logits of its vocabulary slice, as int32 pairs
+ *   {float bits, index_base + local index} [batch][2];
+ * batch_select_advance: per sequence, the lowest-index maximum over the
+ *   ranks' gathered pairs [world][batch][2], then the state advance of
+ *   batch_argmax_advance. */
+KUDACUDA_API int kudacuda_sm100_batch_split_sum(void* handle, uint64_t partials, int64_t ksplit, int64_t rows,
+                                                int64_t n_pad, uint64_t out, uint64_t stream);
+KUDACUDA_API int kudacuda_sm100_batch_argmax_pairs(void* handle, uint64_t partials, int64_t ksplit, int64_t vocab,
+                                                   int64_t n_pad, int64_t batch, uint64_t workspace,
+                                                   int64_t workspace_bytes, int64_t index_base, uint64_t pairs,
+                                                   uint64_t stream);
+KUDACUDA_API int kudacuda_sm100_batch_select_advance(void* handle, uint64_t gathered, int64_t world, int64_t batch,
+                                                     uint64_t state, uint64_t history, int64_t history_len,
+                                                     uint64_t stream);
 KUDACUDA_API int kudacuda_sm100_gqa_decode_batch(void* handle, uint64_t query, uint64_t key_cache,
                                                  uint64_t value_cache, uint64_t output, uint64_t workspace,
                                                  int64_t workspace_bytes, uint64_t tickets, uint64_t kv_len_array,

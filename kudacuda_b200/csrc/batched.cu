@@ -602,6 +602,62 @@ __global__ void __launch_bounds__(32) batch_argmax_stage2(const float* cand_v, c
     }
 }
 
+// ---- tensor parallelism: the pieces around the NCCL collectives
+// out[r][b] = sum over splits of partials[s][r][b] (split order), every column
+// of the padded batch; the rank's row-parallel partial before the allreduce
+__global__ void __launch_bounds__(256) batch_split_sum_kernel(const float* partials, int ksplit, int64_t n, float* out) {
+    pdl_launch_dependents();
+    pdl_wait_on_producer();
+    for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < n;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float v = 0.F;
+        for (int k = 0; k < ksplit; ++k) v += __ldg(partials + k * n + e);
+        out[e] = v;
+    }
+}
+// stage 2 of the argmax, vocabulary-parallel form: the rank's best (value, global
+// index) per sequence as an int32 pair {float bits, index}
+__global__ void __launch_bounds__(32) batch_argmax_pairs_stage2(const float* cand_v, const int* cand_i, int index_base,
+                                                                int32_t* pairs) {
+    pdl_launch_dependents();
+    pdl_wait_on_producer();
+    const int b = blockIdx.x, lane = threadIdx.x;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = lane; c < kArgCtas; c += 32) arg_better(best, bi, cand_v[b * kArgCtas + c], cand_i[b * kArgCtas + c]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        arg_better(best, bi, ov, oi);
+    }
+    if (lane == 0) {
+        pairs[2 * b] = __float_as_int(best);
+        pairs[2 * b + 1] = bi + index_base;
+    }
+}
+// per sequence: the lowest-index maximum over the ranks' pairs gathered as
+// [world][batch][2]; then the state advance of batch_argmax_stage2
+__global__ void batch_select_advance_kernel(const int32_t* gathered, int world, int batch, int32_t* state,
+                                            int32_t* history, int history_len) {
+    pdl_launch_dependents();
+    pdl_wait_on_producer();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= batch) return;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int r = 0; r < world; ++r) {
+        const int32_t* p = gathered + (static_cast<int64_t>(r) * batch + b) * 2;
+        arg_better(best, bi, __int_as_float(p[0]), p[1]);
+    }
+    int32_t* st = state + 4 * b;
+    const int pos = st[1] + 1;
+    st[0] = bi;
+    st[1] = pos;
+    st[2] = pos + 1;
+    if (history != nullptr && pos < history_len) history[static_cast<int64_t>(b) * history_len + pos] = bi;
+}
+
 // x[b][:] = embedding[state[b].token][:]
 __global__ void __launch_bounds__(256) batch_embedding_kernel(const uint16_t* emb, const int32_t* state, uint16_t* x,
                                                               int H, int vocab, int* err) {
@@ -789,6 +845,30 @@ cudaError_t batch_argmax_advance(const float* partials, int ksplit, int vocab, i
     if (st != cudaSuccess) return st;
     return launch_pdl(batch_argmax_stage2, dim3(batch), dim3(32), 0, s, static_cast<const float*>(cv),
                       static_cast<const int*>(ci), state, history, history_len);
+}
+
+cudaError_t batch_split_sum(const float* partials, int ksplit, int rows, int n_pad, float* out, cudaStream_t s) {
+    const int64_t n = static_cast<int64_t>(rows) * n_pad;
+    const int64_t g = (n + 255) / 256;
+    return launch_pdl(batch_split_sum_kernel, dim3(static_cast<unsigned>(g < 2048 ? g : 2048)), dim3(256), 0, s,
+                      partials, ksplit, n, out);
+}
+
+cudaError_t batch_argmax_pairs(const float* partials, int ksplit, int vocab, int n_pad, int batch, float* ws,
+                               int index_base, int32_t* pairs, cudaStream_t s) {
+    float* cv = ws;
+    int* ci = reinterpret_cast<int*>(ws + batch * kArgCtas);
+    cudaError_t st =
+        launch_pdl(batch_argmax_stage1, dim3(kArgCtas), dim3(256), 0, s, partials, ksplit, vocab, n_pad, batch, cv, ci);
+    if (st != cudaSuccess) return st;
+    return launch_pdl(batch_argmax_pairs_stage2, dim3(batch), dim3(32), 0, s, static_cast<const float*>(cv),
+                      static_cast<const int*>(ci), index_base, pairs);
+}
+
+cudaError_t batch_select_advance(const int32_t* gathered, int world, int batch, int32_t* state, int32_t* history,
+                                 int history_len, cudaStream_t s) {
+    return launch_pdl(batch_select_advance_kernel, dim3((batch + 63) / 64), dim3(64), 0, s, gathered, world, batch,
+                      state, history, history_len);
 }
 
 cudaError_t batch_embedding(const uint16_t* emb, const int32_t* state, uint16_t* x, int batch, int H, int vocab,

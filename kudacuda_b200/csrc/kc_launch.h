@@ -223,6 +223,12 @@ cudaError_t batch_argmax_advance(const float* partials, int ksplit, int vocab, i
 cudaError_t batch_embedding(const uint16_t* emb, const int32_t* state, uint16_t* x, int batch, int H, int vocab,
                             int* err, cudaStream_t s);
 cudaError_t batch_state_views(const int32_t* state, int batch, int32_t* pos, int32_t* kv_len, cudaStream_t s);
+// tensor parallelism around the NCCL collectives
+cudaError_t batch_split_sum(const float* partials, int ksplit, int rows, int n_pad, float* out, cudaStream_t s);
+cudaError_t batch_argmax_pairs(const float* partials, int ksplit, int vocab, int n_pad, int batch, float* ws,
+                               int index_base, int32_t* pairs, cudaStream_t s);
+cudaError_t batch_select_advance(const int32_t* gathered, int world, int batch, int32_t* state, int32_t* history,
+                                 int history_len, cudaStream_t s);
 
 int64_t decode_persistent_scratch_bytes(const PersistDims& d, int sms);
 const char* decode_persistent_check(const PersistDims& d, int sms);

@@ -1194,6 +1194,55 @@ int kudacuda_sm100_batch_argmax_advance(void* raw, uint64_t partials, int64_t ks
                                            S(stream)));
 }
 
+int kudacuda_sm100_batch_split_sum(void* raw, uint64_t partials, int64_t ksplit, int64_t rows, int64_t n_pad,
+                                   uint64_t out, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_split_sum")) return 1;
+    if (partials == 0 || out == 0 || ksplit < 1 || ksplit > 64 || rows < 1 || rows > (1 << 24) || !npad_ok(n_pad)) {
+        h->set_error("sm100_batch_split_sum requires non-null pointers, 1 <= ksplit <= 64, n_pad in {16, 32, 64}");
+        return 1;
+    }
+    return finish(h, "batch_split_sum_kernel",
+                  kc::batch_split_sum(P<const float>(partials), static_cast<int>(ksplit), static_cast<int>(rows),
+                                      static_cast<int>(n_pad), P<float>(out), S(stream)));
+}
+
+int kudacuda_sm100_batch_argmax_pairs(void* raw, uint64_t partials, int64_t ksplit, int64_t vocab, int64_t n_pad,
+                                      int64_t batch, uint64_t workspace, int64_t workspace_bytes, int64_t index_base,
+                                      uint64_t pairs, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_argmax_pairs")) return 1;
+    if (partials == 0 || workspace == 0 || pairs == 0 || ksplit < 1 || ksplit > 64 || vocab < 1 ||
+        vocab > (1 << 24) || !npad_ok(n_pad) || batch < 1 || batch > n_pad || index_base < 0 ||
+        index_base + vocab > (int64_t{1} << 30)) {
+        h->set_error("sm100_batch_argmax_pairs requires non-null pointers, 1 <= batch <= n_pad, n_pad in {16, 32, 64}");
+        return 1;
+    }
+    if (workspace_bytes < kudacuda_sm100_batch_argmax_workspace_bytes(batch)) {
+        h->set_error("sm100_batch_argmax_pairs workspace is smaller than kudacuda_sm100_batch_argmax_workspace_bytes()");
+        return 1;
+    }
+    return finish(h, "batch_argmax_stage1/pairs",
+                  kc::batch_argmax_pairs(P<const float>(partials), static_cast<int>(ksplit), static_cast<int>(vocab),
+                                         static_cast<int>(n_pad), static_cast<int>(batch), P<float>(workspace),
+                                         static_cast<int>(index_base), P<int32_t>(pairs), S(stream)));
+}
+
+int kudacuda_sm100_batch_select_advance(void* raw, uint64_t gathered, int64_t world, int64_t batch, uint64_t state,
+                                        uint64_t history, int64_t history_len, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_select_advance")) return 1;
+    if (gathered == 0 || state == 0 || world < 1 || world > 1024 || batch < 1 || batch > 64 || history_len < 0 ||
+        history_len > (1 << 24) || (history != 0 && history_len < 1)) {
+        h->set_error("sm100_batch_select_advance requires non-null pointers (history may be null), 1 <= batch <= 64");
+        return 1;
+    }
+    return finish(h, "batch_select_advance_kernel",
+                  kc::batch_select_advance(P<const int32_t>(gathered), static_cast<int>(world), static_cast<int>(batch),
+                                           P<int32_t>(state), P<int32_t>(history), static_cast<int>(history_len),
+                                           S(stream)));
+}
+
 int kudacuda_sm100_batch_embedding(void* raw, uint64_t embedding, uint64_t state, uint64_t x, int64_t batch,
                                    int64_t hidden, int64_t vocab, uint64_t stream) {
     Handle* h = as_handle(raw);

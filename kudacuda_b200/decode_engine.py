@@ -756,6 +756,9 @@ class BatchedBuffers:
     history: Any  # int32 [B, max_tokens]
     rope_cos: Any
     rope_sin: Any
+    red: Any = None  # f32 [hidden, n_pad]: a row-parallel partial, allreduced (tensor parallelism)
+    pairs: Any = None  # int32 [B, 2]: this rank's (value bits, index) per sequence (vocab-parallel lm_head)
+    gathered: Any = None  # int32 [world, B, 2]
 
 
 class BatchedDecodePlan:
@@ -776,7 +779,8 @@ class BatchedDecodePlan:
     TACTIC = "decode_step_sm100_batched_tcgen05_v1"
 
     def __init__(self, bridge: KudaCudaBridge, weights: ModelWeights, *, batch: int, kv_bucket: int = 2048,
-                 max_tokens: Optional[int] = None, device: Any = "cuda:0", torch_module: Any = None) -> None:
+                 max_tokens: Optional[int] = None, device: Any = "cuda:0", torch_module: Any = None,
+                 allreduce: Any = None) -> None:
         if torch_module is None:
             import torch as torch_module
         self.torch = torch = torch_module
@@ -817,9 +821,10 @@ class BatchedDecodePlan:
         self.ks_o = ks(c.hidden, L0.o.k)
         self.ks_gu = ks(2 * self.inter, c.hidden)
         self.ks_dn = ks(c.hidden, self.inter)
-        self.ks_lm = ks(c.vocab, c.hidden)
+        lm_rows = weights.lm_head.rows if weights.lm_head is not None else c.vocab
+        self.ks_lm = ks(lm_rows, c.hidden)
         part = max(self.ks_qkv * self.qkv_rows, self.ks_o * c.hidden, self.ks_gu * 2 * self.inter,
-                   self.ks_dn * c.hidden, self.ks_lm * c.vocab) * self.n_pad
+                   self.ks_dn * c.hidden, self.ks_lm * lm_rows) * self.n_pad
         ws, tickets, _ = bridge.gqa_workspace(batch=B, query_heads=self.q_heads, kv_heads=self.kv_heads,
                                               kv_extent=cap, device=device, torch_module=torch)
         cos, sin = rope_tables(torch, max(cap, max_tokens) + 1, d, c.rope_theta, device)
@@ -842,13 +847,48 @@ class BatchedDecodePlan:
             rope_cos=cos,
             rope_sin=sin,
         )
-        self.graph_plan = KudaCudaGraphPlan(bridge)
+        # tensor parallelism (Megatron sharding as in TensorParallel): the
+        # row-parallel o_proj/down partials are summed over splits, allreduced
+        # and added; the NF4 lm_head is vocabulary-parallel (per-sequence
+        # argmax pairs, allgather, select)
+        rank, world, group = allreduce if isinstance(allreduce, tuple) else (0, 1, None)
+        self.tp_rank, self.tp_world, self.tp_group = int(rank), int(world), group
+        if self.tp_world > 1 or weights.lm_head is not None:
+            self.buffers.red = torch.zeros(c.hidden * self.n_pad, dtype=torch.float32, device=device)
+            self.buffers.pairs = torch.zeros((B, 2), dtype=torch.int32, device=device)
+            self.buffers.gathered = torch.zeros((self.tp_world, B, 2), dtype=torch.int32, device=device)
+        self._torch_graph = _TorchGraphBridge(torch) if self.tp_world > 1 else None
+        self.graph_plan = KudaCudaGraphPlan(self._torch_graph if self._torch_graph is not None else bridge)
         self.graph_key: Optional[DecodeGraphKey] = None
         self.launches_per_step = 0
 
     @property
     def captured(self) -> bool:
         return self.graph_plan.captured
+
+    def _row_parallel_residual(self, ksplit: int, sp: int) -> int:
+        """x += this layer's row-parallel output: the split sum of every rank, allreduced."""
+
+        b, c, br = self.buffers, self.config, self.bridge
+        if self.tp_world == 1:
+            br.dispatch_batch_residual(b.partials, b.x, ksplit=ksplit, rows=c.hidden, n_pad=self.n_pad,
+                                       batch=self.batch, stream_ptr=sp)
+            return 1
+        import torch.distributed as dist
+
+        br.dispatch_batch_split_sum(b.partials, b.red, ksplit=ksplit, rows=c.hidden, n_pad=self.n_pad, stream_ptr=sp)
+        dist.all_reduce(b.red, group=self.tp_group)
+        br.dispatch_batch_residual(b.red, b.x, ksplit=1, rows=c.hidden, n_pad=self.n_pad, batch=self.batch,
+                                   stream_ptr=sp)
+        return 2
+
+    def release(self) -> None:
+        """Drop the captured graph (before destroying a process group whose
+        collectives it holds)."""
+
+        self.graph_plan.invalidate()
+        if self._torch_graph is not None:
+            self._torch_graph.reset()
 
     def make_graph_key(self) -> DecodeGraphKey:
         b, w, c = self.buffers, self.weights, self.config
@@ -902,25 +942,35 @@ class BatchedDecodePlan:
                                          batch=B, kv_stride=self.kv_bucket, query_heads=self.q_heads,
                                          kv_heads=self.kv_heads, head_dim=d, scale=scale, stream_ptr=sp)
             self._gemm(self.o[li], b.attn, self.ks_o, sp)
-            br.dispatch_batch_residual(b.partials, b.x, ksplit=self.ks_o, rows=c.hidden, n_pad=npad, batch=B,
-                                       stream_ptr=sp)
+            n += self._row_parallel_residual(self.ks_o, sp) - 1
             br.dispatch_batch_rmsnorm(b.x, L.post_norm, b.xn, batch=B, hidden=c.hidden, epsilon=c.eps, stream_ptr=sp)
             self._gemm(self.gu[li], b.xn, self.ks_gu, sp)
             br.dispatch_batch_swiglu(b.partials, b.h, ksplit=self.ks_gu, intermediate=self.inter, n_pad=npad, batch=B,
                                      stream_ptr=sp)
             self._gemm(self.down[li], b.h, self.ks_dn, sp)
-            br.dispatch_batch_residual(b.partials, b.x, ksplit=self.ks_dn, rows=c.hidden, n_pad=npad, batch=B,
-                                       stream_ptr=sp)
+            n += self._row_parallel_residual(self.ks_dn, sp) - 1
             n += 11
         br.dispatch_batch_rmsnorm(b.x, w.final_norm, b.xn, batch=B, hidden=c.hidden, epsilon=c.eps, stream_ptr=sp)
         if w.lm_head is None:
             br.dispatch_batch_gemm(w.embedding, None, b.xn, b.partials, weight_type=1, rows=c.vocab, k=c.hidden,
                                    n_pad=npad, ksplit=self.ks_lm, stream_ptr=sp)
-        else:
+            br.dispatch_batch_argmax_advance(b.partials, b.arg_ws, b.state, b.history, ksplit=self.ks_lm,
+                                             vocab=c.vocab, n_pad=npad, batch=B, stream_ptr=sp)
+            n += 4
+        else:  # vocabulary-parallel NF4 lm_head: this rank's rows, argmax pairs, gather, select
+            v_loc = self.lm_nf4.rows
             self._gemm(self.lm_nf4, b.xn, self.ks_lm, sp)
-        br.dispatch_batch_argmax_advance(b.partials, b.arg_ws, b.state, b.history, ksplit=self.ks_lm, vocab=c.vocab,
-                                         n_pad=npad, batch=B, stream_ptr=sp)
-        n += 4
+            br.dispatch_batch_argmax_pairs(b.partials, b.arg_ws, b.pairs, ksplit=self.ks_lm, vocab=v_loc, n_pad=npad,
+                                           batch=B, index_base=self.tp_rank * v_loc, stream_ptr=sp)
+            if self.tp_world > 1:
+                import torch.distributed as dist
+
+                dist.all_gather_into_tensor(b.gathered, b.pairs, group=self.tp_group)
+                gathered = b.gathered
+            else:
+                gathered = b.pairs
+            br.dispatch_batch_select_advance(gathered, b.state, b.history, world=self.tp_world, batch=B, stream_ptr=sp)
+            n += 5
         self.launches_per_step = n
         return n
 
@@ -966,7 +1016,10 @@ class BatchedDecodePlan:
         self.buffers.state.copy_(saved_state)
         self.buffers.history.copy_(saved_hist)
         torch.cuda.synchronize(self.device)
-        self.bridge.reset_graph()
+        if self._torch_graph is None:
+            self.bridge.reset_graph()
+        else:
+            self._torch_graph.reset()
         self.graph_plan.invalidate()
         key = self.make_graph_key()
         self.graph_plan.begin_capture(key, stream_ptr=sp)
@@ -977,7 +1030,8 @@ class BatchedDecodePlan:
                 self.graph_plan.end_capture(key, stream_ptr=sp)
             finally:
                 self.graph_plan.invalidate()
-                self.bridge.reset_graph()
+                if self._torch_graph is None:
+                    self.bridge.reset_graph()
             raise
         self.graph_plan.end_capture(key, stream_ptr=sp)
         self.graph_key = key

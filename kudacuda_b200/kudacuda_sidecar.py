@@ -1223,6 +1223,27 @@ class KudaCudaBridge:
                    self._tensor_pointer(pos, "pos"), self._tensor_pointer(kv_len, "kv_len"),
                    _normalize_cuda_handle(stream_ptr))
 
+    def dispatch_batch_split_sum(self, partials: Any, out: Any, *, ksplit: int, rows: int, n_pad: int,
+                                 stream_ptr: int) -> None:
+        if int(out.numel()) < int(rows) * int(n_pad):
+            raise ValueError("out must hold rows * n_pad floats")
+        self._call("kudacuda_sm100_batch_split_sum", self._tensor_pointer(partials, "partials"), int(ksplit), int(rows),
+                   int(n_pad), self._tensor_pointer(out, "out"), _normalize_cuda_handle(stream_ptr))
+
+    def dispatch_batch_argmax_pairs(self, partials: Any, workspace: Any, pairs: Any, *, ksplit: int, vocab: int,
+                                    n_pad: int, batch: int, index_base: int, stream_ptr: int) -> None:
+        self._call("kudacuda_sm100_batch_argmax_pairs", self._tensor_pointer(partials, "partials"), int(ksplit),
+                   int(vocab), int(n_pad), int(batch), self._tensor_pointer(workspace, "workspace"),
+                   int(workspace.numel()) * int(workspace.element_size()), int(index_base),
+                   self._tensor_pointer(pairs, "pairs"), _normalize_cuda_handle(stream_ptr))
+
+    def dispatch_batch_select_advance(self, gathered: Any, state: Any, history: Any = None, *, world: int, batch: int,
+                                      stream_ptr: int) -> None:
+        hist_len = int(history.shape[-1]) if history is not None else 0
+        self._call("kudacuda_sm100_batch_select_advance", self._tensor_pointer(gathered, "gathered"), int(world),
+                   int(batch), self._tensor_pointer(state, "state"), self._optional_pointer(history, "history"),
+                   hist_len, _normalize_cuda_handle(stream_ptr))
+
     def dispatch_gqa_decode_batch(self, query: Any, key_cache: Any, value_cache: Any, output: Any, workspace: Any,
                                   tickets: Any, kv_len: Any, *, batch: int, kv_stride: int, query_heads: int,
                                   kv_heads: int, head_dim: int = 128, scale: float | None = None,

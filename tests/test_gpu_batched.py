@@ -233,3 +233,96 @@ def test_batched_rejects_bad_arguments(bridge):
                                    stream_ptr=0)
     with pytest.raises(ValueError):
         bridge.batch_argmax_workspace_bytes(65)
+
+
+def test_batch_tp_pieces_exact(bridge):
+    """The tensor-parallel pieces: split sums in split order, per-sequence
+    argmax pairs with a rank's index base, and the select over ranks (lowest
+    index on ties) with the state advance."""
+
+    import torch
+
+    dev = "cuda:0"
+    rng = np.random.default_rng(3)
+    ks, rows, npad, batch, vocab, world = 3, 300, 32, 20, 1000, 3
+    part = torch.from_numpy(rng.normal(0, 1, (ks, rows, npad)).astype(np.float32)).to(dev)
+    out = torch.zeros(rows * npad, dtype=torch.float32, device=dev)
+    bridge.dispatch_batch_split_sum(part, out, ksplit=ks, rows=rows, n_pad=npad, stream_ptr=0)
+    p = part.cpu().numpy()
+    ref = (p[0] + p[1]) + p[2]
+    np.testing.assert_array_equal(out.view(rows, npad).cpu().numpy(), ref)
+    # argmax pairs over a vocabulary slice with planted ties
+    logits = rng.normal(0, 1, (1, vocab, npad)).astype(np.float32)
+    logits[0, 700, :batch] = 9.0
+    logits[0, 200, 3] = 9.0  # tie for sequence 3: the lower index wins
+    lt = torch.from_numpy(logits).to(dev)
+    ws = torch.zeros(bridge.batch_argmax_workspace_bytes(batch) // 4, dtype=torch.float32, device=dev)
+    pairs = torch.zeros((batch, 2), dtype=torch.int32, device=dev)
+    bridge.dispatch_batch_argmax_pairs(lt, ws, pairs, ksplit=1, vocab=vocab, n_pad=npad, batch=batch,
+                                       index_base=5000, stream_ptr=0)
+    pr = pairs.cpu().numpy()
+    assert pr[3, 1] == 5200 and all(pr[b, 1] == 5700 for b in range(batch) if b != 3)
+    assert np.all(pr[:, 0].view(np.float32) == 9.0)
+    # select over three ranks' pairs, then the state advance
+    g = np.zeros((world, batch, 2), dtype=np.int32)
+    vals = rng.normal(0, 1, (world, batch)).astype(np.float32)
+    vals[2, 4] = vals[0, 4] = 50.0  # tie across ranks: rank 0's (lower) index wins
+    g[:, :, 0] = vals.view(np.int32)
+    g[:, :, 1] = np.arange(world)[:, None] * 1000 + np.arange(batch)[None, :]
+    gathered = torch.from_numpy(g).to(dev)
+    state = torch.tensor([[1, 10 + b, 11 + b, 0] for b in range(batch)], dtype=torch.int32, device=dev)
+    hist = torch.zeros((batch, 64), dtype=torch.int32, device=dev)
+    bridge.dispatch_batch_select_advance(gathered, state, hist, world=world, batch=batch, stream_ptr=0)
+    st = state.cpu().numpy()
+    best = np.argmax(vals, axis=0)
+    for b in range(batch):
+        assert st[b, 0] == g[best[b], b, 1] and st[b, 1] == 11 + b and st[b, 2] == 12 + b
+        assert hist[b, 11 + b].item() == st[b, 0]
+    assert st[4, 0] == 4  # rank 0's index on the tie
+    assert bridge.error_word(clear=True) == 0
+
+
+def test_batched_untied_nf4_lm_head_against_oracle(bridge):
+    """An untied NF4 lm_head (the Llama form) goes through the vocabulary-
+    parallel pieces (argmax pairs + select) even on one rank; each sequence's
+    token must be the oracle's argmax or within a rounding step of it."""
+
+    import dataclasses
+
+    import torch
+
+    from kudacuda_b200.decode_engine import BatchedDecodePlan, random_weights, tiny_config
+
+    cfg = dataclasses.replace(tiny_config(layers=1, vocab=4096), tie_embeddings=False, name="tiny-untied")
+    w = random_weights(bridge, cfg, seed=17, device="cuda:0")
+    assert w.lm_head is not None
+    plan = BatchedDecodePlan(bridge, w, batch=4, kv_bucket=64, max_tokens=64, device="cuda:0")
+    stream = torch.cuda.Stream()
+    plan.capture(stream)
+    tokens, positions = [7, 100, 2000, 4000], [0, 5, 17, 63]
+    plan.reset_cache()
+    plan.set_state(tokens, positions, stream)
+    plan.replay(stream)
+    stream.synchronize()
+    assert bridge.error_word(clear=True) == 0
+    emb = _b16(w.embedding).reshape(cfg.vocab, cfg.hidden)
+    cos, sin = _b16(plan.buffers.rope_cos), _b16(plan.buffers.rope_sin)
+    ocfg = dict(hidden=cfg.hidden, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                inter=cfg.intermediate, eps=cfg.eps)
+    layer = _layer_np(w.layers[0])
+    lm = O.bf16_to_f32(O.bf16_bits(O.nf4_dequant(w.lm_head.packed.reshape(-1).cpu().numpy(),
+                                                 w.lm_head.absmax.cpu().numpy(), cfg.vocab * cfg.hidden)))
+    lm = lm.reshape(cfg.vocab, cfg.hidden).astype(np.float64)
+    st = plan.buffers.state.cpu().numpy()
+    for b, (tok, pos) in enumerate(zip(tokens, positions)):
+        x = emb[tok].copy()
+        kc = np.zeros((cfg.kv_heads, plan.kv_bucket, cfg.head_dim), dtype=np.uint16)
+        vc = np.zeros_like(kc)
+        O.layer_step_hf(layer, ocfg, x, kc, vc, plan.kv_bucket, pos, cos[pos], sin[pos])
+        xn = O.bf16_to_f32(O.rmsnorm_hf_bf16(x, _b16(w.final_norm), cfg.eps)).astype(np.float64)
+        logits = O.bf16_to_f32(O.bf16_bits((lm @ xn).astype(np.float32)))
+        ref = int(np.argmax(logits))
+        got = int(st[b, 0])
+        assert got == ref or logits[got] >= logits[ref] - 2e-2 * abs(logits[ref]) - 2e-3
+        assert st[b, 1] == pos + 1
+    plan.release()
