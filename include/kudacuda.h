@@ -365,7 +365,11 @@ KUDACUDA_API int kudacuda_sm100_decode_layers_persistent(void* handle, uint64_t 
  * state's pos and kv_len columns to pos[B] and kv_len[B] for the RoPE
  * epilogue and gqa_decode_batch (kudacuda_sm100_gqa_decode, bf16, with a
  * per-sequence int32 length array; workspace and tickets as for
- * kudacuda_sm100_gqa_decode with kv_len = kv_stride). */
+ * kudacuda_sm100_gqa_decode with kv_len = kv_stride).
+ * shared_cache = 1 (batch_qkv_rope, gqa_decode_batch): every batch entry
+ * appends to and attends over ONE cache [kvh][kv_capacity][hd] -- the batch
+ * is the tokens of one prompt at positions pos[b] with causal lengths
+ * kv_len[b] = pos[b] + 1 (prefill through the batched path). */
 KUDACUDA_API int64_t kudacuda_sm100_batch_gemm_ksplit(int64_t rows, int64_t k);
 /* batch_retile: copy a bitsandbytes NF4 matrix into the GEMM's streaming form
  * (weight_type 2): per 128-row tile and 64-element K block one contiguous
@@ -386,7 +390,7 @@ KUDACUDA_API int kudacuda_sm100_batch_qkv_rope(void* handle, uint64_t partials, 
                                                uint64_t q_bias, uint64_t k_bias, uint64_t v_bias, uint64_t rope_cos,
                                                uint64_t rope_sin, int64_t max_pos, uint64_t pos, uint64_t q_out,
                                                uint64_t key_cache, uint64_t value_cache, int64_t kv_capacity,
-                                               uint64_t stream);
+                                               int shared_cache, uint64_t stream);
 KUDACUDA_API int kudacuda_sm100_batch_residual(void* handle, uint64_t partials, int64_t ksplit, int64_t rows,
                                                int64_t n_pad, int64_t batch, uint64_t x, uint64_t stream);
 KUDACUDA_API int kudacuda_sm100_batch_swiglu(void* handle, uint64_t partials, int64_t ksplit, int64_t intermediate,
@@ -423,7 +427,8 @@ KUDACUDA_API int kudacuda_sm100_gqa_decode_batch(void* handle, uint64_t query, u
                                                  uint64_t value_cache, uint64_t output, uint64_t workspace,
                                                  int64_t workspace_bytes, uint64_t tickets, uint64_t kv_len_array,
                                                  int64_t batch_size, int64_t kv_stride, int64_t query_heads,
-                                                 int64_t kv_heads, int64_t head_dim, float scale, uint64_t stream);
+                                                 int64_t kv_heads, int64_t head_dim, float scale, int shared_cache,
+                                                 uint64_t stream);
 
 /* Library / build identification: "sm_100a". */
 KUDACUDA_API const char* kudacuda_sm100_target_arch(void);

@@ -459,7 +459,7 @@ __global__ void __launch_bounds__(256) batch_qkv_epilogue_kernel(const BatchQkv 
             const float lo = round_bf16(round_bf16(y0 * c) + round_bf16(-y1 * sn));
             const float hi = round_bf16(round_bf16(y1 * c) + round_bf16(y0 * sn));
             uint16_t* dst = isq ? a.q_out + (static_cast<int64_t>(b) * a.q_heads + hh) * hd
-                                : a.kcache + ((static_cast<int64_t>(b) * a.kv_heads + hh) * a.cap + pos) * hd;
+                                : a.kcache + ((static_cast<int64_t>(a.shared_cache ? 0 : b) * a.kv_heads + hh) * a.cap + pos) * hd;
             dst[i] = f32_to_bf16_bits(lo);
             dst[i + half] = f32_to_bf16_bits(hi);
         }
@@ -475,7 +475,8 @@ __global__ void __launch_bounds__(256) batch_qkv_epilogue_kernel(const BatchQkv 
             }
             float y = round_bf16(tq[q * np1 + b]);
             if (a.v_bias != nullptr) y = round_bf16(y + bf16_bits_to_f32(a.v_bias[hh * hd + d]));
-            a.vcache[((static_cast<int64_t>(b) * a.kv_heads + hh) * a.cap + pos) * hd + d] = f32_to_bf16_bits(y);
+            a.vcache[((static_cast<int64_t>(a.shared_cache ? 0 : b) * a.kv_heads + hh) * a.cap + pos) * hd + d] =
+                f32_to_bf16_bits(y);
         }
     }
 }

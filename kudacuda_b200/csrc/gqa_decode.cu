@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a)
     int n = kv_len - t0;
     n = n < 0 ? 0 : (n > a.chunk ? a.chunk : n);
 
-    const int64_t kv_base = (static_cast<int64_t>(b) * a.kv_heads + kvh) * a.stride * kHeadDim;
+    const int64_t kv_base = (static_cast<int64_t>(a.kv_shared ? 0 : b) * a.kv_heads + kvh) * a.stride * kHeadDim;
     const uint16_t* ks = reinterpret_cast<const uint16_t*>(kv_rows);
     const uint16_t* vs = ks + static_cast<int64_t>(a.chunk) * kHeadDim;
     if (tid == 0 && n > 0) {
@@ -389,7 +389,7 @@ __global__ void __launch_bounds__(kGqaClusterThreads) gqa_cluster_kernel(const G
     const int b = blockIdx.x / a.kv_heads;
     const int kvh = blockIdx.x - b * a.kv_heads;
     const int t0 = split * a.chunk;
-    const int64_t kv_base = (static_cast<int64_t>(b) * a.kv_heads + kvh) * a.stride * kHeadDim;
+    const int64_t kv_base = (static_cast<int64_t>(a.kv_shared ? 0 : b) * a.kv_heads + kvh) * a.stride * kHeadDim;
     uint8_t* ks = kv_rows;
     uint8_t* vs = kv_rows + static_cast<size_t>(a.chunk) * kRowPad;
     // leader: gathered partial accumulators [rank][head][dim], after the rows

@@ -98,6 +98,7 @@ struct GqaArgs {
     int* counters;       // [B * kv_heads], zero between launches (null: separate combine)
     const int32_t* kv_len_dev;  // null: use kv_len
     int kv_len_per_batch;       // 1: kv_len_dev is an array [batch] (batched decode), 0: one shared length
+    int kv_shared;              // 1: every batch entry reads cache 0 (the queries of one sequence's prompt)
     int kv_len;
     int stride;
     int batch, q_heads, kv_heads, head_dim;
@@ -208,8 +209,9 @@ struct BatchQkv {
     const uint16_t* rope_sin;
     const int32_t* pos;  // [batch]
     uint16_t* q_out;     // [batch][qh][hd]
-    uint16_t* kcache;    // [batch][kvh][cap][hd]
+    uint16_t* kcache;    // [batch][kvh][cap][hd], or one [kvh][cap][hd] cache when shared
     uint16_t* vcache;
+    int shared_cache;    // 1: every batch entry appends to cache 0 (the tokens of one prompt)
     int* err;
 };
 cudaError_t batch_qkv_epilogue(const BatchQkv& q, cudaStream_t s);

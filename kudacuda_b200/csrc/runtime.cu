@@ -1103,7 +1103,7 @@ int kudacuda_sm100_batch_qkv_rope(void* raw, uint64_t partials, int64_t ksplit, 
                                   int64_t q_heads, int64_t kv_heads, int64_t head_dim, uint64_t q_bias, uint64_t k_bias,
                                   uint64_t v_bias, uint64_t rope_cos, uint64_t rope_sin, int64_t max_pos, uint64_t pos,
                                   uint64_t q_out, uint64_t key_cache, uint64_t value_cache, int64_t kv_capacity,
-                                  uint64_t stream) {
+                                  int shared_cache, uint64_t stream) {
     Handle* h = as_handle(raw);
     if (!ready(h, "kudacuda_sm100_batch_qkv_rope")) return 1;
     if (partials == 0 || rope_cos == 0 || rope_sin == 0 || pos == 0 || q_out == 0 || key_cache == 0 ||
@@ -1134,6 +1134,7 @@ int kudacuda_sm100_batch_qkv_rope(void* raw, uint64_t partials, int64_t ksplit, 
     q.q_out = P<uint16_t>(q_out);
     q.kcache = P<uint16_t>(key_cache);
     q.vcache = P<uint16_t>(value_cache);
+    q.shared_cache = shared_cache != 0 ? 1 : 0;
     q.err = h->err_word;
     return finish(h, "batch_qkv_epilogue_kernel", kc::batch_qkv_epilogue(q, S(stream)));
 }
@@ -1274,7 +1275,8 @@ int kudacuda_sm100_batch_state_views(void* raw, uint64_t state, int64_t batch, u
 int kudacuda_sm100_gqa_decode_batch(void* raw, uint64_t query, uint64_t key_cache, uint64_t value_cache,
                                     uint64_t output, uint64_t workspace, int64_t workspace_bytes, uint64_t tickets,
                                     uint64_t kv_len_array, int64_t batch_size, int64_t kv_stride, int64_t query_heads,
-                                    int64_t kv_heads, int64_t head_dim, float scale, uint64_t stream) {
+                                    int64_t kv_heads, int64_t head_dim, float scale, int shared_cache,
+                                    uint64_t stream) {
     Handle* h = as_handle(raw);
     if (!ready(h, "kudacuda_sm100_gqa_decode_batch")) return 1;
     if (query == 0 || key_cache == 0 || value_cache == 0 || output == 0 || workspace == 0 || tickets == 0 ||
@@ -1299,6 +1301,7 @@ int kudacuda_sm100_gqa_decode_batch(void* raw, uint64_t query, uint64_t key_cach
     a.counters = P<int>(tickets);
     a.kv_len_dev = P<const int32_t>(kv_len_array);
     a.kv_len_per_batch = 1;
+    a.kv_shared = shared_cache != 0 ? 1 : 0;
     // the split-KV kernel: splits past a sequence's length exit at once, where
     // the cluster kernel's CTAs would all take part in its barriers (measured
     // at batch 64, 2048-token caches, lengths 63-510: 5.55 vs 6.35 ms per step)

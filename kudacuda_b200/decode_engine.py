@@ -780,7 +780,11 @@ class BatchedDecodePlan:
 
     def __init__(self, bridge: KudaCudaBridge, weights: ModelWeights, *, batch: int, kv_bucket: int = 2048,
                  max_tokens: Optional[int] = None, device: Any = "cuda:0", torch_module: Any = None,
-                 allreduce: Any = None) -> None:
+                 allreduce: Any = None, shared_cache: Optional[tuple] = None) -> None:
+        """``shared_cache=(kcache, vcache)``, bf16 [layers, kv_heads, cap, d]:
+        the batch is the tokens of ONE sequence's prompt (positions and causal
+        lengths per entry), appending to and attending over that one cache --
+        e.g. a StaticDecodePlan's (prefill through the batched path)."""
         if torch_module is None:
             import torch as torch_module
         self.torch = torch = torch_module
@@ -792,6 +796,9 @@ class BatchedDecodePlan:
         if not 1 <= B <= 64:
             raise ValueError("batched decode supports 1..64 sequences")
         self.n_pad = 16 if B <= 16 else (32 if B <= 32 else 64)
+        self.shared = shared_cache is not None
+        if self.shared:
+            kv_bucket = int(shared_cache[0].shape[2])
         self.kv_bucket = cap = int(kv_bucket)
         L0 = weights.layers[0]
         self.q_heads = L0.q.rows // c.head_dim
@@ -838,8 +845,10 @@ class BatchedDecodePlan:
             attn=torch.zeros((self.n_pad, self.q_heads * d), dtype=bf16, device=device),
             h=torch.zeros((self.n_pad, self.inter), dtype=bf16, device=device),
             partials=torch.zeros(part, dtype=torch.float32, device=device),
-            kcache=torch.zeros((c.layers, B, self.kv_heads, cap, d), dtype=bf16, device=device),
-            vcache=torch.zeros((c.layers, B, self.kv_heads, cap, d), dtype=bf16, device=device),
+            kcache=(shared_cache[0] if self.shared else
+                    torch.zeros((c.layers, B, self.kv_heads, cap, d), dtype=bf16, device=device)),
+            vcache=(shared_cache[1] if self.shared else
+                    torch.zeros((c.layers, B, self.kv_heads, cap, d), dtype=bf16, device=device)),
             gqa_ws=ws,
             gqa_tickets=tickets,
             arg_ws=torch.zeros(bridge.batch_argmax_workspace_bytes(B) // 4, dtype=torch.float32, device=device),
@@ -937,10 +946,12 @@ class BatchedDecodePlan:
             br.dispatch_batch_qkv_rope(b.partials, L.q_bias, L.k_bias, L.v_bias, b.rope_cos, b.rope_sin, b.pos, b.q,
                                        b.kcache[li], b.vcache[li], ksplit=self.ks_qkv, n_pad=npad, batch=B,
                                        q_heads=self.q_heads, kv_heads=self.kv_heads, head_dim=d,
-                                       max_pos=int(b.rope_cos.shape[0]), kv_capacity=self.kv_bucket, stream_ptr=sp)
+                                       max_pos=int(b.rope_cos.shape[0]), kv_capacity=self.kv_bucket,
+                                       shared_cache=self.shared, stream_ptr=sp)
             br.dispatch_gqa_decode_batch(b.q, b.kcache[li], b.vcache[li], b.attn, b.gqa_ws, b.gqa_tickets, b.kv_len,
                                          batch=B, kv_stride=self.kv_bucket, query_heads=self.q_heads,
-                                         kv_heads=self.kv_heads, head_dim=d, scale=scale, stream_ptr=sp)
+                                         kv_heads=self.kv_heads, head_dim=d, scale=scale, shared_cache=self.shared,
+                                         stream_ptr=sp)
             self._gemm(self.o[li], b.attn, self.ks_o, sp)
             n += self._row_parallel_residual(self.ks_o, sp) - 1
             br.dispatch_batch_rmsnorm(b.x, L.post_norm, b.xn, batch=B, hidden=c.hidden, epsilon=c.eps, stream_ptr=sp)
@@ -1049,6 +1060,62 @@ class BatchedDecodePlan:
         self.replay(stream)
         stream.synchronize()
         return [int(t) for t in self.buffers.state[:, 0].cpu().tolist()]
+
+
+class BatchedPrefill:
+    """Prompt prefill through the batched tensor-core path into a
+    StaticDecodePlan's KV cache (the reference prefills token by token through
+    Transformers, and its static-cache guard rejects multi-token steps,
+    python/kudacuda_sidecar.py:791-792): the prompt goes in chunks of ``chunk``
+    tokens, each chunk one batched step whose entries are the chunk's tokens at
+    positions 64c + i with causal lengths, all appending to and attending over
+    the decode plan's one cache.  The last chunk is padded with copies of the
+    last token at the positions after the prompt (their cache rows are
+    overwritten by the decode steps before any step reads them).  Afterwards
+    the decode plan's state holds the first generated token at position
+    len(prompt), so decoding continues with replay / generate_device.
+
+    Capturing the chunk step runs it once eagerly at position 0 of the cache,
+    so build this before the cache holds anything that must be kept."""
+
+    def __init__(self, decode_plan: "StaticDecodePlan", *, chunk: int = 64) -> None:
+        torch = decode_plan.torch
+        self.decode = decode_plan
+        self.chunk = int(chunk)
+        b = decode_plan.buffers
+        # a handle of its own: a handle holds one graph, the decode plan's
+        br = decode_plan.bridge
+        self.bridge = KudaCudaBridge(device_id=br.device_id, lib_path=br.library_path, native_lib=br.lib)
+        self.plan = BatchedDecodePlan(self.bridge, decode_plan.weights, batch=self.chunk,
+                                      max_tokens=decode_plan.kv_bucket, device=decode_plan.device, torch_module=torch,
+                                      shared_cache=(b.kcache, b.vcache))
+        self.stream = torch.cuda.Stream(device=decode_plan.device)
+        self.plan.capture(self.stream)
+
+    def prefill(self, prompt: list[int], stream: Any) -> int:
+        """Run the prompt; returns the first generated token (also left in the
+        decode plan's state at position len(prompt))."""
+
+        T = len(prompt)
+        C = self.chunk
+        nchunks = (T + C - 1) // C
+        if T < 1 or nchunks * C > self.decode.kv_bucket:
+            raise ValueError("prompt (padded to whole chunks) must fit the KV bucket")
+        stream.synchronize()
+        nxt = 0
+        for ci in range(nchunks):
+            toks = list(prompt[ci * C:(ci + 1) * C])
+            n = len(toks)
+            toks += [toks[-1]] * (C - n)
+            self.plan.set_state(toks, [ci * C + i for i in range(C)], self.stream)
+            self.plan.replay(self.stream)
+            if ci == nchunks - 1:
+                self.stream.synchronize()
+                nxt = int(self.plan.buffers.state[n - 1, 0].item())
+        if self.bridge.error_word(clear=True):
+            raise NativeCudaError("batched prefill raised the device error word")
+        self.decode.set_state(nxt, T, stream)
+        return nxt
 
 
 def batched_greedy_generate(plan: BatchedDecodePlan, prompts: list[list[int]], new_tokens: int,

@@ -1178,14 +1178,14 @@ class KudaCudaBridge:
     def dispatch_batch_qkv_rope(self, partials: Any, q_bias: Any, k_bias: Any, v_bias: Any, rope_cos: Any,
                                 rope_sin: Any, pos: Any, q_out: Any, key_cache: Any, value_cache: Any, *, ksplit: int,
                                 n_pad: int, batch: int, q_heads: int, kv_heads: int, head_dim: int, max_pos: int,
-                                kv_capacity: int, stream_ptr: int) -> None:
+                                kv_capacity: int, shared_cache: bool = False, stream_ptr: int) -> None:
         self._call("kudacuda_sm100_batch_qkv_rope", self._tensor_pointer(partials, "partials"), int(ksplit), int(n_pad),
                    int(batch), int(q_heads), int(kv_heads), int(head_dim), self._optional_pointer(q_bias, "q_bias"),
                    self._optional_pointer(k_bias, "k_bias"), self._optional_pointer(v_bias, "v_bias"),
                    self._tensor_pointer(rope_cos, "rope_cos"), self._tensor_pointer(rope_sin, "rope_sin"), int(max_pos),
                    self._tensor_pointer(pos, "pos"), self._tensor_pointer(q_out, "q_out"),
                    self._tensor_pointer(key_cache, "key_cache"), self._tensor_pointer(value_cache, "value_cache"),
-                   int(kv_capacity), _normalize_cuda_handle(stream_ptr))
+                   int(kv_capacity), 1 if shared_cache else 0, _normalize_cuda_handle(stream_ptr))
 
     def dispatch_batch_residual(self, partials: Any, x: Any, *, ksplit: int, rows: int, n_pad: int, batch: int,
                                 stream_ptr: int) -> None:
@@ -1247,7 +1247,7 @@ class KudaCudaBridge:
     def dispatch_gqa_decode_batch(self, query: Any, key_cache: Any, value_cache: Any, output: Any, workspace: Any,
                                   tickets: Any, kv_len: Any, *, batch: int, kv_stride: int, query_heads: int,
                                   kv_heads: int, head_dim: int = 128, scale: float | None = None,
-                                  stream_ptr: int) -> None:
+                                  shared_cache: bool = False, stream_ptr: int) -> None:
         """Split-KV GQA decode of B sequences with per-sequence lengths kv_len (int32 [B])."""
 
         sc = float(scale) if scale is not None else 1.0 / math.sqrt(head_dim)
@@ -1256,7 +1256,7 @@ class KudaCudaBridge:
                    self._tensor_pointer(output, "output"), self._tensor_pointer(workspace, "workspace"),
                    int(workspace.numel()) * int(workspace.element_size()), self._tensor_pointer(tickets, "tickets"),
                    self._tensor_pointer(kv_len, "kv_len"), int(batch), int(kv_stride), int(query_heads),
-                   int(kv_heads), int(head_dim), sc, _normalize_cuda_handle(stream_ptr))
+                   int(kv_heads), int(head_dim), sc, 1 if shared_cache else 0, _normalize_cuda_handle(stream_ptr))
 
     def error_word(self, *, clear: bool = True) -> int:
         word = ctypes.c_int(0)

@@ -15,6 +15,10 @@ KV rows for attention).
       the persistent all-layers kernel alone (Qwen2.5-3B layer shapes, random
       NF4 weights), launched directly on its stream at position kv - 1
 
+    python -m kudacuda_b200.microbench --op prefill --prompt 512
+      time to first token: batched prefill (64-token chunks on the tensor
+      cores) against the decode-loop prefill, full Qwen2.5-3B architecture
+
 The same command with ``--reps 1 --launches 4`` is the small case used for ncu
 captures (see profiles/).
 """
@@ -238,6 +242,44 @@ def time_persistent(torch, layers: int, kv: int, launches: int, reps: int, devic
             "device_error_word": err}
 
 
+def time_prefill(torch, prompt_len: int, device: str) -> dict:
+    """Time to first token for a ``prompt_len``-token prompt on the Qwen2.5-3B
+    architecture (36 layers, full vocabulary): the batched prefill (chunks of 64
+    tokens through the tensor-core path into the decode plan's cache) against
+    the decode-loop prefill (one persistent-kernel step per prompt token).
+    Host-synchronous end to end, wall clock, after one warm-up of each."""
+
+    import time
+
+    from .decode_engine import QWEN25_3B, BatchedPrefill, StaticDecodePlan, random_weights
+
+    bridge = KudaCudaBridge(device_id=torch.device(device).index or 0)
+    w = random_weights(bridge, QWEN25_3B, seed=20260824, device=device)
+    cap = max(512, ((prompt_len + 64 + 63) // 64) * 64)
+    plan = StaticDecodePlan(bridge, w, kv_bucket=cap, max_tokens=cap, device=device, persistent=True)
+    pre = BatchedPrefill(plan, chunk=64)
+    stream = torch.cuda.Stream()
+    plan.capture(stream)
+    g = torch.Generator().manual_seed(5)
+    prompt = torch.randint(0, QWEN25_3B.vocab, (prompt_len,), generator=g).tolist()
+    out = {"op": f"prefill_qwen25_3b_T{prompt_len}"}
+    for name, fn in (("batched", lambda: pre.prefill(prompt, stream)), ("decode_loop", lambda: plan.prefill(prompt, stream))):
+        fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        tok = fn()
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        out[f"{name}_ms"] = round(dt * 1e3, 2)
+        out[f"{name}_prompt_tok_s"] = round(prompt_len / dt, 1)
+        out[f"{name}_first_token"] = int(tok)
+    out["device_error_word"] = bridge.error_word(clear=True)
+    pre.plan.release()
+    pre.bridge.shutdown()
+    bridge.reset_graph()
+    return out
+
+
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--op", default="all")
@@ -247,10 +289,15 @@ def main(argv=None) -> int:
     p.add_argument("--device", default="cuda:0")
     p.add_argument("--layers", type=int, default=36, help="--op persistent: decoder layers")
     p.add_argument("--kv", type=int, default=512, help="--op persistent: tokens attended (kv_len)")
+    p.add_argument("--prompt", type=int, default=512, help="--op prefill: prompt tokens")
     args = p.parse_args(argv)
     import torch
 
     torch.cuda.set_device(torch.device(args.device))
+    if args.op == "prefill":
+        r = time_prefill(torch, args.prompt, args.device)
+        print(json.dumps(r), flush=True)
+        return 1 if r["device_error_word"] else 0
     if args.op == "persistent":
         r = time_persistent(torch, args.layers, args.kv, max(args.launches, 1), args.reps, args.device)
         print(json.dumps(r), flush=True)

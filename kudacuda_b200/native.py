@@ -79,7 +79,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "kudacuda_sm100_batch_retile": (_i32, [_p, _u64, _u64, _i64, _i64, _u64, _i64, _u64]),
     "kudacuda_sm100_batch_rmsnorm": (_i32, [_p, _u64, _u64, _u64, _i64, _i64, _f32, _u64]),
     "kudacuda_sm100_batch_qkv_rope": (
-        _i32, [_p, _u64, _i64, _i64, _i64, _i64, _i64, _i64] + [_u64] * 5 + [_i64] + [_u64] * 4 + [_i64, _u64]
+        _i32, [_p, _u64, _i64, _i64, _i64, _i64, _i64, _i64] + [_u64] * 5 + [_i64] + [_u64] * 4 + [_i64, _i32, _u64]
     ),
     "kudacuda_sm100_batch_residual": (_i32, [_p, _u64, _i64, _i64, _i64, _i64, _u64, _u64]),
     "kudacuda_sm100_batch_swiglu": (_i32, [_p, _u64, _i64, _i64, _i64, _i64, _u64, _u64]),
@@ -93,7 +93,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "kudacuda_sm100_batch_argmax_pairs": (_i32, [_p, _u64, _i64, _i64, _i64, _i64, _u64, _i64, _i64, _u64, _u64]),
     "kudacuda_sm100_batch_select_advance": (_i32, [_p, _u64, _i64, _i64, _u64, _u64, _i64, _u64]),
     "kudacuda_sm100_gqa_decode_batch": (
-        _i32, [_p, _u64, _u64, _u64, _u64, _u64, _i64, _u64, _u64, _i64, _i64, _i64, _i64, _i64, _f32, _u64]
+        _i32, [_p, _u64, _u64, _u64, _u64, _u64, _i64, _u64, _u64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _u64]
     ),
     "kudacuda_sm100_gqa_decode_static": (
         _i32, [_p, _u64, _u64, _u64, _u64, _u64, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _u64]

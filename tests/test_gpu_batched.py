@@ -326,3 +326,64 @@ def test_batched_untied_nf4_lm_head_against_oracle(bridge):
         assert got == ref or logits[got] >= logits[ref] - 2e-2 * abs(logits[ref]) - 2e-3
         assert st[b, 1] == pos + 1
     plan.release()
+
+
+def test_batched_prefill_then_persistent_decode_teacher_forced():
+    """A 70-token prompt through the batched path (two chunks, the second
+    padded) into a persistent decode plan's cache, then greedy decode on the
+    device: teacher-forced top-1 agreement with the oracle over the generated
+    tokens, and the prompt's cache rows close to the oracle's."""
+
+    import torch
+
+    from kudacuda_b200.decode_engine import BatchedPrefill, StaticDecodePlan, random_weights, tiny_config
+    from kudacuda_b200.kudacuda_sidecar import KudaCudaBridge
+
+    cfg = tiny_config(layers=2, vocab=4096)
+    br = KudaCudaBridge(device_id=0)
+    w = random_weights(br, cfg, seed=23, device="cuda:0")
+    plan = StaticDecodePlan(br, w, kv_bucket=256, max_tokens=256, device="cuda:0", persistent=True)
+    stream = torch.cuda.Stream()
+    plan.reset_cache()
+    pre = BatchedPrefill(plan, chunk=64)
+    plan.capture(stream)
+    rng = np.random.default_rng(8)
+    prompt = [int(t) for t in rng.integers(0, cfg.vocab, 70)]
+    plan.reset_cache()
+    plan.buffers.history.zero_()
+    first = pre.prefill(prompt, stream)
+    n_new = 8
+    plan.buffers.history[len(prompt)] = first
+    plan.generate_device(n_new - 1, stream)
+    stream.synchronize()
+    assert br.error_word(clear=True) == 0
+    gen = [int(t) for t in plan.buffers.history[len(prompt):len(prompt) + n_new].cpu().tolist()]
+    seq = prompt + gen
+    layers = [_layer_np(L) for L in w.layers]
+    emb = _b16(w.embedding).reshape(cfg.vocab, cfg.hidden)
+    fn = _b16(w.final_norm)
+    cos, sin = _b16(plan.buffers.rope_cos), _b16(plan.buffers.rope_sin)
+    ocfg = dict(hidden=cfg.hidden, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                inter=cfg.intermediate, eps=cfg.eps)
+    kcs = [np.zeros((cfg.kv_heads, plan.kv_bucket, cfg.head_dim), dtype=np.uint16) for _ in layers]
+    vcs = [np.zeros_like(kcs[0]) for _ in layers]
+    agree = 0
+    kc_gpu = _b16(plan.buffers.kcache)
+    for pos in range(len(seq) - 1):
+        x = emb[seq[pos]].copy()
+        for li, layer in enumerate(layers):
+            O.layer_step_hf(layer, ocfg, x, kcs[li], vcs[li], plan.kv_bucket, pos, cos[pos], sin[pos])
+        tok, _ = O.lm_head_argmax(x, fn, emb, cfg.eps)
+        if pos >= len(prompt) - 1:
+            agree += int(tok == seq[pos + 1])
+    # the prompt's key rows (positions 0..69): layer 0's come straight from the
+    # embeddings (the 1e-2 bar); layer 1's are composed through a random-init
+    # layer, whose rounding differences grow to ~1e-2 on their own (2e-2 bar)
+    norm_close(O.bf16_to_f32(kc_gpu[0][:, :len(prompt)]), O.bf16_to_f32(kcs[0][:, :len(prompt)]))
+    norm_close(O.bf16_to_f32(kc_gpu[1][:, :len(prompt)]), O.bf16_to_f32(kcs[1][:, :len(prompt)]), rel=2e-2)
+    rate = agree / n_new
+    assert rate >= 0.75, f"teacher-forced top-1 agreement {rate:.2f}"
+    pre.plan.release()
+    pre.bridge.shutdown()
+    br.reset_graph()
+    br.shutdown()
