@@ -984,7 +984,9 @@ def batched_gemm_roofline(torch, bridge, plan, stream) -> dict:
         "us_per_launch": round(us, 3),
         "tensor_tflops": round(flops / (us * 1e-6) / 1e12, 2),
         "tensor_frac_of_bf16_peak": round(flops / (us * 1e-6) / 1e12 / tf, 4),
-        "traffic": None,
+        "traffic": _profiled_traffic("batched_gemm_tc_qwen25_3b_gate_up_n64.md"),
+        "traffic_source": "profiles/batched_gemm_tc_qwen25_3b_gate_up_n64.md (ncu dram__bytes_read.sum + "
+                          "dram__bytes_write.sum, one gate|up launch at n_pad 64)",
     }
 
 
