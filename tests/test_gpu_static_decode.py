@@ -98,5 +98,30 @@ def test_runner_matches_transformers_eager_on_the_same_nf4_weights():
     # free-running greedy generation through the runner also starts with the same token
     gen = runner.generate(prompt, 8)
     assert gen[0] == seq[PROMPT_LEN] or gen[0] == p16[0]
+
+    # the batched tensor-core path on the same weights (one sequence): its
+    # arithmetic is the bf16 eager path's (weights dequantised to bf16, bf16
+    # matmul with fp32 accumulation), so it tracks the bf16 forward closely
+    from kudacuda_b200.decode_engine import BatchedDecodePlan
+
+    bbridge = KudaCudaBridge(device_id=0)
+    bplan = BatchedDecodePlan(bbridge, w, batch=1, kv_bucket=256, max_tokens=256, device="cuda:0")
+    bstream = torch.cuda.Stream()
+    bplan.capture(bstream)
+    bplan.reset_cache()
+    batched = []
+    for pos in range(len(seq) - 1):
+        nxt = bplan.step_tokens([seq[pos]], [pos], bstream)[0]
+        if pos >= PROMPT_LEN - 1:
+            batched.append(nxt)
+    b32, b16 = agree(batched, p32), agree(batched, p16)
+    print(f"batched path: vs fp32-eager {b32:.4f}, vs bf16-eager {b16:.4f}")
+    assert bbridge.error_word(clear=True) == 0
+    bmsg = f"batched/fp32 {b32:.4f} batched/bf16 {b16:.4f} bf16/fp32 {ref_noise:.4f}"
+    assert b32 >= AGREEMENT and b16 >= AGREEMENT, bmsg
+    assert b32 >= ref_noise - FLOOR_MARGIN, bmsg
+    bplan.release()
+    bbridge.reset_graph()
+    bbridge.shutdown()
     runner.invalidate("test done")
     assert not runner.captured
