@@ -13,17 +13,16 @@
 //
 // GEMM tiling: one CTA owns 128 weight rows (the MMA's M) x the padded batch N
 // (16, 32 or 64) for a range of 64-element K blocks (split-K, so every op has
-// enough CTAs).  Per block, 256 threads dequantise the 128 x 64 weight tile into
-// shared memory in the canonical K-major no-swizzle UMMA layout (8-row x
-// 16-byte core matrices; the two 8-element K halves 128 B apart, 8-row groups
-// 256 B apart) and stage the activations' 64-element slice beside it; one
-// thread issues four tcgen05.mma (K = 16 each) into a 128 x N fp32 TMEM
-// accumulator and commits to an mbarrier.  Weights, absmax and activations
-// stream through a cp.async ring several K blocks deep (enough bytes in flight
-// per SM to cover HBM latency); the dequant of block i + 1 overlaps the MMAs
-// of block i (two A tiles).  bf16 weights (the tied lm_head) skip the dequant:
-// cp.async places them in the canonical layout directly.  The accumulator is
-// read with tcgen05.ld and written as fp32 split-K partials; small epilogue
+// enough CTAs).  A producer warp brings each block's weights and the
+// activations' block (2D TMA, 128-byte swizzle) into a shared ring; for NF4,
+// eight warps dequantise the 128 x 64 tile into a 128-byte-swizzled K-major
+// bf16 tile (two in flight); one thread issues four tcgen05.mma (K = 16
+// each) into a 128 x N fp32 TMEM accumulator and commits to mbarriers that
+// free the ring stage and the tile.  bf16 weights (the tied lm_head) skip the
+// dequant: TMA places them in the swizzled layout the tensor core reads.  NF4
+// comes either in the bitsandbytes layout or re-tiled at load into one
+// contiguous record per tile and block (one bulk copy).  The accumulator is
+// read with tcgen05.ld and written as fp32 split-K partials; the epilogue
 // kernels sum the splits in a fixed order (deterministic) and finish each op.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -43,8 +42,8 @@ constexpr int kBlockK = 64;
 constexpr int kATileBytes = kTcM * kBlockK * 2;  // 16 KB of bf16 per stage
 
 struct TcArgs {
-    const uint8_t* packed;  // NF4 [rows][K/2] (weight_type 0) or bf16 [rows][K] (weight_type 1)
-    const float* absmax;    // [rows][K/64] (NF4)
+    const uint8_t* packed;  // NF4 [rows][K/2] (weight_type 0), bf16 [rows][K] (1), re-tiled records (2)
+    const float* absmax;    // [rows][K/64] (weight_type 0)
     const uint16_t* x;      // bf16 [n_pad][K], rows >= batch are zero
     float* partials;        // [ksplit][total_rows][n_pad]; this matrix's rows start at row_offset
     int rows, K, n_pad, ksplit, weight_type, row_offset, total_rows;
