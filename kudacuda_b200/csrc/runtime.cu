@@ -1302,10 +1302,12 @@ int kudacuda_sm100_gqa_decode_batch(void* raw, uint64_t query, uint64_t key_cach
     a.kv_len_dev = P<const int32_t>(kv_len_array);
     a.kv_len_per_batch = 1;
     a.kv_shared = shared_cache != 0 ? 1 : 0;
-    // the split-KV kernel: splits past a sequence's length exit at once, where
-    // the cluster kernel's CTAs would all take part in its barriers (measured
-    // at batch 64, 2048-token caches, lengths 63-510: 5.55 vs 6.35 ms per step)
-    a.split_only = 1;
+    // many (sequence, KV head) pairs: the split-KV kernel, whose splits past a
+    // sequence's length exit at once, where the cluster kernel's CTAs would all
+    // take part in its barriers (batch 64, 2048-token caches, lengths 63-510:
+    // 5.55 vs 6.35 ms per step); few pairs: the cluster kernel (batch 16:
+    // 3.90 vs 4.08 ms per step)
+    a.split_only = batch_size * kv_heads >= 64 ? 1 : 0;
     a.kv_len = static_cast<int>(kv_stride);
     a.stride = static_cast<int>(kv_stride);
     a.batch = static_cast<int>(batch_size);
