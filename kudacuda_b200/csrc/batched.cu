@@ -134,8 +134,10 @@ __device__ __forceinline__ uint32_t sw128_chunk(int r, int c) {
 //            (16 lane-indexed copies: conflict-free 64-bit lookups), scales by
 //            the block's absmax in fp32, rounds to bf16 and writes the
 //            swizzled A tile; then they read the accumulator out.
-// Barriers: raw_full (TMA bytes landed), raw_empty (MMAs of that stage done),
-// a_full (256 dequant arrivals), a_empty (MMAs of that A tile done), done.
+// Barriers: raw_full (TMA bytes landed), raw_empty (the MMAs of that stage's
+// block are done: frees the stage for the producer and, for the dequant warps,
+// the A tile that block read), a_full (256 dequant arrivals), done; one
+// tcgen05.commit per block.
 constexpr int kGThreads = 320;
 constexpr int kPairCopies = 16;
 constexpr int kPairTableBytes = 256 * kPairCopies * 8;  // 32 KB
@@ -170,7 +172,7 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
                                                             const TcArgs a) {
     using G = GemmSmem<WT>;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t raw_full[kMaxRaw], raw_empty[kMaxRaw], a_full[kMaxA], a_empty[kMaxA], done_bar;
+    __shared__ __align__(8) uint64_t raw_full[kMaxRaw], raw_empty[kMaxRaw], a_full[kMaxA], done_bar;
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -195,10 +197,7 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
             mbar_init(&raw_full[i], 1);
             mbar_init(&raw_empty[i], 1);
         }
-        for (int i = 0; i < kMaxA; ++i) {
-            mbar_init(&a_full[i], 256);
-            mbar_init(&a_empty[i], 1);
-        }
+        for (int i = 0; i < kMaxA; ++i) mbar_init(&a_full[i], 256);
         mbar_init(&done_bar, 1);
         abort_flag = 0;
         fence_mbar_init();
@@ -261,7 +260,8 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
                 for (int k = 0; k < 4; ++k)
                     umma_bf16(tmem, umma_desc_sw128(sa + 32 * k), umma_desc_sw128(sb + 32 * k), idesc,
                               (it > 0 || k > 0) ? 1u : 0u);
-                if (G::kNf4) umma_commit(&a_empty[s]);
+                // raw_empty[j] frees the ring stage and, for the dequant warps,
+                // the A tile this block read
                 umma_commit(&raw_empty[j]);
             }
             umma_commit(&done_bar);
@@ -302,7 +302,14 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
                          : "=r"(cw[0]), "=r"(cw[1]), "=r"(cw[2]), "=r"(cw[3])
                          : "r"(rec + static_cast<uint32_t>(r * 32 + h * 16)));
             if (WT == 2) asm volatile("ld.shared.f32 %0, [%1];" : "=f"(sc) : "r"(rec + static_cast<uint32_t>(kTcM * 32 + r * 4)));
-            if (it >= SA) bar_wait(&a_empty[s], ((it / SA) - 1) & 1, abort_p);
+            // the MMAs of block it - SA (the last reader of A tile s) are done: they
+            // committed to the ring stage of that block.  No phase of that barrier
+            // can pass unseen: its next phase needs block it - SA + R's MMAs, which
+            // need this thread's dequant of a later block (R >= SA).
+            if (it >= SA) {
+                const int ib = it - SA;
+                bar_wait(&raw_empty[ib % R], (ib / R) & 1, abort_p);
+            }
             const uint32_t as = atile_u32 + static_cast<uint32_t>(s * kATileBytes);
             const uint64_t ss = (static_cast<uint64_t>(__float_as_uint(sc)) << 32) | __float_as_uint(sc);
 #pragma unroll
