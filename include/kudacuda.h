@@ -383,6 +383,37 @@ KUDACUDA_API int kudacuda_sm100_batch_gemm(void* handle, int weight_type, uint64
                                            int64_t rows, int64_t k, uint64_t x, int64_t n_pad, int64_t ksplit,
                                            uint64_t partials, int64_t row_offset, int64_t total_rows,
                                            uint64_t stream);
+/* The GEMM with its epilogue fused (NF4 weights, weight_type 0 or 2): every
+ * split writes its fp32 partial tile, takes a per-tile ticket, and the last
+ * split of each 128-row tile sums the tile's splits in split order (the same
+ * bits as batch_gemm + the separate epilogue) and finishes the op.  tickets:
+ * int32 [ceil(rows / 128)], zero before the first call (the kernel resets
+ * them); partials: ksplit * rows * n_pad floats.
+ *   batch_gemm_residual: resid[b][r] = bf16(resid[b][r] + bf16(sum));
+ *   batch_gemm_swiglu: weights of 2 * intermediate rows in 64-row tiles, each
+ *     tile = gate rows 64t..64t+63 then up rows 64t..64t+63; out[b][j] =
+ *     bf16(bf16(silu(bf16 gate_j)) * bf16 up_j);
+ *   batch_gemm_qkv_rope: weights q | k | v by 128-row heads; the
+ *     batch_qkv_rope epilogue per head. */
+KUDACUDA_API int kudacuda_sm100_batch_gemm_residual(void* handle, int weight_type, uint64_t weight, uint64_t absmax,
+                                                    int64_t rows, int64_t k, uint64_t x, int64_t n_pad,
+                                                    int64_t ksplit, int64_t batch, uint64_t partials,
+                                                    int64_t partials_bytes, uint64_t tickets, uint64_t resid,
+                                                    uint64_t stream);
+KUDACUDA_API int kudacuda_sm100_batch_gemm_swiglu(void* handle, int weight_type, uint64_t weight, uint64_t absmax,
+                                                  int64_t intermediate, int64_t k, uint64_t x, int64_t n_pad,
+                                                  int64_t ksplit, int64_t batch, uint64_t partials,
+                                                  int64_t partials_bytes, uint64_t tickets, uint64_t out,
+                                                  uint64_t stream);
+KUDACUDA_API int kudacuda_sm100_batch_gemm_qkv_rope(void* handle, int weight_type, uint64_t weight, uint64_t absmax,
+                                                    int64_t k, uint64_t x, int64_t n_pad, int64_t ksplit,
+                                                    int64_t batch, uint64_t partials, int64_t partials_bytes,
+                                                    uint64_t tickets, int64_t q_heads, int64_t kv_heads,
+                                                    int64_t head_dim, uint64_t q_bias, uint64_t k_bias,
+                                                    uint64_t v_bias, uint64_t rope_cos, uint64_t rope_sin,
+                                                    int64_t max_pos, uint64_t pos, uint64_t q_out, uint64_t key_cache,
+                                                    uint64_t value_cache, int64_t kv_capacity, int shared_cache,
+                                                    uint64_t stream);
 KUDACUDA_API int kudacuda_sm100_batch_rmsnorm(void* handle, uint64_t x, uint64_t weight, uint64_t out,
                                               int64_t batch, int64_t hidden, float eps, uint64_t stream);
 KUDACUDA_API int kudacuda_sm100_batch_qkv_rope(void* handle, uint64_t partials, int64_t ksplit, int64_t n_pad,

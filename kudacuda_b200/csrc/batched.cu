@@ -48,6 +48,7 @@ struct TcArgs {
     float* partials;        // [ksplit][total_rows][n_pad]; this matrix's rows start at row_offset
     int rows, K, n_pad, ksplit, weight_type, row_offset, total_rows;
     int* err;
+    BatchEpilogue e;        // fused epilogue (mode 0: none, the partials are the output)
 };
 
 // Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both
@@ -165,6 +166,83 @@ struct GemmSmem {
     static __host__ __device__ int fixed_bytes(int n) { return kNf4 ? kPairTableBytes + a_stages(n) * kATileBytes : 0; }
     static __host__ __device__ int bytes(int n) { return 1024 + fixed_bytes(n) + raw_stages(n) * raw_bytes(n); }
 };
+
+// Fused epilogue, run by the last CTA of a tile to finish its split (ticket):
+// the tile's split partials summed in split order (the order the separate
+// epilogue kernels use, so the results are the same bits) into t[row][b],
+// then the op's finish for every sequence.
+__device__ void fused_epilogue(const TcArgs& a, int tile, float* t) {
+    const BatchEpilogue& e = a.e;
+    const int n = a.n_pad, np1 = n + 1, tid = threadIdx.x;
+    const int nr = min(kTcM, a.rows - tile * kTcM);
+    const int64_t kstride = static_cast<int64_t>(a.total_rows) * n;
+    for (int idx = tid; idx < nr * n; idx += kGThreads) {
+        const int r = idx / n, b = idx - r * n;
+        const float* p = a.partials + static_cast<int64_t>(a.row_offset + tile * kTcM + r) * n + b;
+        float v = 0.F;
+        for (int k = 0; k < a.ksplit; ++k) v += __ldcg(p + k * kstride);
+        t[r * np1 + b] = v;
+    }
+    __syncthreads();
+    if (e.mode == 1) {  // x[b][row] = bf16(x + bf16(sum))
+        for (int idx = tid; idx < e.batch * nr; idx += kGThreads) {
+            const int b = idx / nr, r = idx - b * nr;
+            uint16_t* xp = e.resid + static_cast<int64_t>(b) * a.rows + tile * kTcM + r;
+            *xp = f32_to_bf16_bits(bf16_bits_to_f32(*xp) + round_bf16(t[r * np1 + b]));
+        }
+    } else if (e.mode == 2) {  // tile = 64 gate rows | the same 64 up rows
+        const int half = kTcM / 2, inter = a.rows / 2;
+        for (int idx = tid; idx < e.batch * half; idx += kGThreads) {
+            const int b = idx / half, i = idx - b * half;
+            const float g = round_bf16(t[i * np1 + b]);
+            const float u = round_bf16(t[(half + i) * np1 + b]);
+            const float act = round_bf16(g / (1.0F + expf(-g)));
+            e.hout[static_cast<int64_t>(b) * inter + tile * half + i] = f32_to_bf16_bits(act * u);
+        }
+    } else if (e.mode == 3) {  // tile = one head of q | k | v (head_dim 128)
+        const int hd = kTcM, half = hd / 2, head = tile;
+        const bool isq = head < e.q_heads, isk = !isq && head < e.q_heads + e.kv_heads;
+        if (isq || isk) {
+            const uint16_t* bias = isq ? e.q_bias : e.k_bias;
+            const int hh = isq ? head : head - e.q_heads;
+            for (int idx = tid; idx < e.batch * half; idx += kGThreads) {
+                const int b = idx / half, i = idx - b * half;
+                const int pos = e.pos[b];
+                if (pos < 0 || pos >= e.cap || pos >= e.max_pos) {
+                    if (a.err != nullptr) atomicOr(a.err, 2);
+                    continue;
+                }
+                float y0 = round_bf16(t[i * np1 + b]), y1 = round_bf16(t[(i + half) * np1 + b]);
+                if (bias != nullptr) {
+                    y0 = round_bf16(y0 + bf16_bits_to_f32(bias[hh * hd + i]));
+                    y1 = round_bf16(y1 + bf16_bits_to_f32(bias[hh * hd + i + half]));
+                }
+                const float c = bf16_bits_to_f32(e.rope_cos[static_cast<int64_t>(pos) * half + i]);
+                const float sn = bf16_bits_to_f32(e.rope_sin[static_cast<int64_t>(pos) * half + i]);
+                const float lo = round_bf16(round_bf16(y0 * c) + round_bf16(-y1 * sn));
+                const float hi = round_bf16(round_bf16(y1 * c) + round_bf16(y0 * sn));
+                uint16_t* dst = isq ? e.q_out + (static_cast<int64_t>(b) * e.q_heads + hh) * hd
+                                    : e.kcache + ((static_cast<int64_t>(e.shared_cache ? 0 : b) * e.kv_heads + hh) * e.cap + pos) * hd;
+                dst[i] = f32_to_bf16_bits(lo);
+                dst[i + half] = f32_to_bf16_bits(hi);
+            }
+        } else {
+            const int hh = head - e.q_heads - e.kv_heads;
+            for (int idx = tid; idx < e.batch * hd; idx += kGThreads) {
+                const int b = idx / hd, d = idx - b * hd;
+                const int pos = e.pos[b];
+                if (pos < 0 || pos >= e.cap || pos >= e.max_pos) {
+                    if (a.err != nullptr) atomicOr(a.err, 2);
+                    continue;
+                }
+                float y = round_bf16(t[d * np1 + b]);
+                if (e.v_bias != nullptr) y = round_bf16(y + bf16_bits_to_f32(e.v_bias[hh * hd + d]));
+                e.vcache[((static_cast<int64_t>(e.shared_cache ? 0 : b) * e.kv_heads + hh) * e.cap + pos) * hd + d] =
+                    f32_to_bf16_bits(y);
+            }
+        }
+    }
+}
 
 template <int WT>
 __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w,
@@ -356,6 +434,21 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
     }
     if (tid == 0 && *abort_p && a.err != nullptr) atomicOr(a.err, 16);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    if (G::kNf4 && a.e.mode != 0) {
+        // the last CTA of this tile's splits finishes the op (the tickets reset
+        // themselves); its shared memory (table, A tiles: 64 KB, all reads and
+        // MMAs done) stages the sums
+        __shared__ int last_split;
+        __threadfence();  // this thread's partial stores before the ticket
+        __syncthreads();
+        if (tid == 0) last_split = atomicAdd(a.e.tickets + tile, 1) == a.ksplit - 1 ? 1 : 0;
+        __syncthreads();
+        if (last_split) {
+            __threadfence();
+            fused_epilogue(a, tile, reinterpret_cast<float*>(table));
+            if (tid == 0) a.e.tickets[tile] = 0;
+        }
+    }
     __syncthreads();
     if (warp == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -789,7 +882,7 @@ cudaError_t launch_gemm(const TcArgs& a, int ksplit, cudaStream_t s) {
 
 cudaError_t batch_gemm(int weight_type, const void* weight, const float* absmax, int rows, int K, const uint16_t* x,
                        int n_pad, int ksplit, float* partials, int row_offset, int total_rows, int* err,
-                       cudaStream_t s) {
+                       cudaStream_t s, const BatchEpilogue* epi) {
     if (rows < 1 || K < kBlockK || K % kBlockK != 0 || !(n_pad == 16 || n_pad == 32 || n_pad == 64) || ksplit < 1 ||
         ksplit > K / kBlockK || row_offset < 0 || row_offset + rows > total_rows ||
         weight_type < 0 || weight_type > 2 || (weight_type == 0 && absmax == nullptr))
@@ -810,6 +903,18 @@ cudaError_t batch_gemm(int weight_type, const void* weight, const float* absmax,
     a.row_offset = row_offset;
     a.total_rows = total_rows;
     a.err = err;
+    memset(&a.e, 0, sizeof(a.e));
+    if (epi != nullptr && epi->mode != 0) {
+        // fused epilogues: NF4 weights, the whole matrix in the partials, the tile shapes they need
+        if (weight_type == 1 || epi->tickets == nullptr || epi->batch < 1 || epi->batch > n_pad || row_offset != 0 ||
+            total_rows != rows || n_pad > 64 || epi->mode > 3 || (epi->mode == 1 && epi->resid == nullptr) ||
+            (epi->mode == 2 && (epi->hout == nullptr || rows % kTcM != 0)) ||
+            (epi->mode == 3 && (rows != (epi->q_heads + 2 * epi->kv_heads) * kTcM || epi->pos == nullptr ||
+                                epi->q_out == nullptr || epi->kcache == nullptr || epi->vcache == nullptr ||
+                                epi->rope_cos == nullptr || epi->rope_sin == nullptr)))
+            return cudaErrorInvalidValue;
+        a.e = *epi;
+    }
     if (weight_type == 2) return launch_gemm<2>(a, ksplit, s);
     return weight_type == 0 ? launch_gemm<0>(a, ksplit, s) : launch_gemm<1>(a, ksplit, s);
 }

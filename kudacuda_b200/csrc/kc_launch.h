@@ -189,13 +189,35 @@ struct PersistLaunch {
 // [n_pad][K] (rows >= batch zero) on the tcgen05 tensor cores: fp32 split-K
 // partials[(split * total_rows + row_offset + r) * n_pad + b].
 int batch_gemm_ksplit(int rows, int K);
+// Fused epilogue of the GEMM (NF4 forms), run by the last CTA of each 128-row
+// tile's splits (per-tile int32 tickets, zero before the first launch, reset
+// by the kernel): 1 residual (resid[b][r] = bf16(resid + bf16(sum))), 2 SwiGLU
+// (each tile = 64 gate rows then the same 64 up rows; hout[b][j]), 3 q/k/v
+// (each tile = one 128-dim head of q | k | v: bias, RoPE, K/V append).
+struct BatchEpilogue {
+    int mode;
+    int batch;
+    int* tickets;
+    uint16_t* resid;
+    uint16_t* hout;
+    int q_heads, kv_heads, cap, max_pos, shared_cache;
+    const uint16_t* q_bias;
+    const uint16_t* k_bias;
+    const uint16_t* v_bias;
+    const uint16_t* rope_cos;
+    const uint16_t* rope_sin;
+    const int32_t* pos;
+    uint16_t* q_out;
+    uint16_t* kcache;
+    uint16_t* vcache;
+};
 // NF4 re-tiled for the GEMM (weight_type 2): per 128-row tile and 64-element
 // K block one 4,608-byte record (codes [128][32 B], absmax [128] fp32)
 int64_t batch_retile_bytes(int rows, int K);
 cudaError_t batch_retile(const uint8_t* packed, const float* absmax, int rows, int K, uint8_t* out, cudaStream_t s);
 cudaError_t batch_gemm(int weight_type, const void* weight, const float* absmax, int rows, int K, const uint16_t* x,
                        int n_pad, int ksplit, float* partials, int row_offset, int total_rows, int* err,
-                       cudaStream_t s);
+                       cudaStream_t s, const BatchEpilogue* epi = nullptr);
 cudaError_t batch_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* out, int batch, int H, float eps,
                           cudaStream_t s);
 struct BatchQkv {

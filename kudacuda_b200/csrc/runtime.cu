@@ -1085,6 +1085,122 @@ int kudacuda_sm100_batch_retile(void* raw, uint64_t packed, uint64_t absmax, int
                                    static_cast<int>(k), P<uint8_t>(out), S(stream)));
 }
 
+namespace {
+// shared checks of the fused-epilogue GEMM entries
+bool fused_gemm_ok(Handle* h, const char* op, int weight_type, uint64_t weight, uint64_t absmax, int64_t rows,
+                   int64_t k, uint64_t x, int64_t n_pad, int64_t ksplit, int64_t batch, uint64_t partials,
+                   int64_t partials_bytes, uint64_t tickets) {
+    if (weight == 0 || x == 0 || partials == 0 || tickets == 0 || (weight_type != 0 && weight_type != 2) ||
+        (weight_type == 0 && absmax == 0) || rows < 1 || rows > (1 << 24) || k < 64 || k % 64 != 0 ||
+        k > (1 << 20) || !npad_ok(n_pad) || ksplit < 1 || ksplit > k / 64 || batch < 1 || batch > n_pad ||
+        partials_bytes < ksplit * rows * n_pad * 4) {
+        std::string m(op);
+        m += " requires NF4 weights (weight_type 0 with absmax, or 2 re-tiled), K % 64 == 0, n_pad in {16, 32, 64}, "
+             "1 <= batch <= n_pad, 1 <= ksplit <= K/64, partials of ksplit * rows * n_pad floats, tickets";
+        h->set_error(m.c_str());
+        return false;
+    }
+    return true;
+}
+kc::BatchEpilogue fused_epi(int mode, int64_t batch, uint64_t tickets) {
+    kc::BatchEpilogue e;
+    memset(&e, 0, sizeof(e));
+    e.mode = mode;
+    e.batch = static_cast<int>(batch);
+    e.tickets = P<int>(tickets);
+    return e;
+}
+}  // namespace
+
+int kudacuda_sm100_batch_gemm_residual(void* raw, int weight_type, uint64_t weight, uint64_t absmax, int64_t rows,
+                                       int64_t k, uint64_t x, int64_t n_pad, int64_t ksplit, int64_t batch,
+                                       uint64_t partials, int64_t partials_bytes, uint64_t tickets, uint64_t resid,
+                                       uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_gemm_residual")) return 1;
+    if (!fused_gemm_ok(h, "sm100_batch_gemm_residual", weight_type, weight, absmax, rows, k, x, n_pad, ksplit, batch,
+                       partials, partials_bytes, tickets))
+        return 1;
+    if (resid == 0) {
+        h->set_error("sm100_batch_gemm_residual requires the residual stream [batch][rows] bf16");
+        return 1;
+    }
+    kc::BatchEpilogue e = fused_epi(1, batch, tickets);
+    e.resid = P<uint16_t>(resid);
+    return finish(h, "gemm_tc_kernel (residual)",
+                  kc::batch_gemm(weight_type, P<const void>(weight), P<const float>(absmax), static_cast<int>(rows),
+                                 static_cast<int>(k), P<const uint16_t>(x), static_cast<int>(n_pad),
+                                 static_cast<int>(ksplit), P<float>(partials), 0, static_cast<int>(rows), h->err_word,
+                                 S(stream), &e));
+}
+
+int kudacuda_sm100_batch_gemm_swiglu(void* raw, int weight_type, uint64_t weight, uint64_t absmax,
+                                     int64_t intermediate, int64_t k, uint64_t x, int64_t n_pad, int64_t ksplit,
+                                     int64_t batch, uint64_t partials, int64_t partials_bytes, uint64_t tickets,
+                                     uint64_t out, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_gemm_swiglu")) return 1;
+    if (!fused_gemm_ok(h, "sm100_batch_gemm_swiglu", weight_type, weight, absmax, 2 * intermediate, k, x, n_pad,
+                       ksplit, batch, partials, partials_bytes, tickets))
+        return 1;
+    if (out == 0 || intermediate % 64 != 0) {
+        h->set_error("sm100_batch_gemm_swiglu requires intermediate % 64 == 0 (weights in 64-row gate | up tiles) "
+                     "and the output [batch][intermediate] bf16");
+        return 1;
+    }
+    kc::BatchEpilogue e = fused_epi(2, batch, tickets);
+    e.hout = P<uint16_t>(out);
+    return finish(h, "gemm_tc_kernel (swiglu)",
+                  kc::batch_gemm(weight_type, P<const void>(weight), P<const float>(absmax),
+                                 static_cast<int>(2 * intermediate), static_cast<int>(k), P<const uint16_t>(x),
+                                 static_cast<int>(n_pad), static_cast<int>(ksplit), P<float>(partials), 0,
+                                 static_cast<int>(2 * intermediate), h->err_word, S(stream), &e));
+}
+
+int kudacuda_sm100_batch_gemm_qkv_rope(void* raw, int weight_type, uint64_t weight, uint64_t absmax, int64_t k,
+                                       uint64_t x, int64_t n_pad, int64_t ksplit, int64_t batch, uint64_t partials,
+                                       int64_t partials_bytes, uint64_t tickets, int64_t q_heads, int64_t kv_heads,
+                                       int64_t head_dim, uint64_t q_bias, uint64_t k_bias, uint64_t v_bias,
+                                       uint64_t rope_cos, uint64_t rope_sin, int64_t max_pos, uint64_t pos,
+                                       uint64_t q_out, uint64_t key_cache, uint64_t value_cache, int64_t kv_capacity,
+                                       int shared_cache, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_batch_gemm_qkv_rope")) return 1;
+    const int64_t rows = (q_heads + 2 * kv_heads) * 128;
+    if (head_dim != 128 || q_heads < 1 || kv_heads < 1 || q_heads > 256 || kv_heads > 256) {
+        h->set_error("sm100_batch_gemm_qkv_rope requires head_dim 128 (one tile per head)");
+        return 1;
+    }
+    if (!fused_gemm_ok(h, "sm100_batch_gemm_qkv_rope", weight_type, weight, absmax, rows, k, x, n_pad, ksplit, batch,
+                       partials, partials_bytes, tickets))
+        return 1;
+    if (rope_cos == 0 || rope_sin == 0 || pos == 0 || q_out == 0 || key_cache == 0 || value_cache == 0 ||
+        max_pos < 1 || kv_capacity < 1) {
+        h->set_error("sm100_batch_gemm_qkv_rope requires rope tables, positions, q output and caches");
+        return 1;
+    }
+    kc::BatchEpilogue e = fused_epi(3, batch, tickets);
+    e.q_heads = static_cast<int>(q_heads);
+    e.kv_heads = static_cast<int>(kv_heads);
+    e.cap = static_cast<int>(kv_capacity);
+    e.max_pos = static_cast<int>(max_pos);
+    e.shared_cache = shared_cache != 0 ? 1 : 0;
+    e.q_bias = P<const uint16_t>(q_bias);
+    e.k_bias = P<const uint16_t>(k_bias);
+    e.v_bias = P<const uint16_t>(v_bias);
+    e.rope_cos = P<const uint16_t>(rope_cos);
+    e.rope_sin = P<const uint16_t>(rope_sin);
+    e.pos = P<const int32_t>(pos);
+    e.q_out = P<uint16_t>(q_out);
+    e.kcache = P<uint16_t>(key_cache);
+    e.vcache = P<uint16_t>(value_cache);
+    return finish(h, "gemm_tc_kernel (q/k/v + RoPE)",
+                  kc::batch_gemm(weight_type, P<const void>(weight), P<const float>(absmax), static_cast<int>(rows),
+                                 static_cast<int>(k), P<const uint16_t>(x), static_cast<int>(n_pad),
+                                 static_cast<int>(ksplit), P<float>(partials), 0, static_cast<int>(rows), h->err_word,
+                                 S(stream), &e));
+}
+
 int kudacuda_sm100_batch_rmsnorm(void* raw, uint64_t x, uint64_t weight, uint64_t out, int64_t batch, int64_t hidden,
                                  float eps, uint64_t stream) {
     Handle* h = as_handle(raw);

@@ -1169,6 +1169,50 @@ class KudaCudaBridge:
                    int(n_pad), int(ksplit), self._tensor_pointer(partials, "partials"), int(row_offset), total,
                    _normalize_cuda_handle(stream_ptr))
 
+    def _fused_gemm_common(self, weight: Any, absmax: Any, x: Any, partials: Any, tickets: Any) -> list:
+        return [self._tensor_pointer(weight, "weight"), self._optional_pointer(absmax, "absmax")], \
+            [self._tensor_pointer(x, "x")], [self._tensor_pointer(partials, "partials"),
+                                             int(partials.numel()) * int(partials.element_size()),
+                                             self._tensor_pointer(tickets, "tickets")]
+
+    def dispatch_batch_gemm_residual(self, weight: Any, absmax: Any, x: Any, partials: Any, tickets: Any, resid: Any, *,
+                                     weight_type: int, rows: int, k: int, n_pad: int, ksplit: int, batch: int,
+                                     stream_ptr: int) -> None:
+        """GEMM + fused residual epilogue: resid[b][r] = bf16(resid + bf16(W . x[b]))."""
+
+        w, xx, pt = self._fused_gemm_common(weight, absmax, x, partials, tickets)
+        self._call("kudacuda_sm100_batch_gemm_residual", int(weight_type), *w, int(rows), int(k), *xx, int(n_pad),
+                   int(ksplit), int(batch), *pt, self._tensor_pointer(resid, "resid"),
+                   _normalize_cuda_handle(stream_ptr))
+
+    def dispatch_batch_gemm_swiglu(self, weight: Any, absmax: Any, x: Any, partials: Any, tickets: Any, out: Any, *,
+                                   weight_type: int, intermediate: int, k: int, n_pad: int, ksplit: int, batch: int,
+                                   stream_ptr: int) -> None:
+        """GEMM over gate|up weights in 64-row gate/up tiles + fused SwiGLU."""
+
+        w, xx, pt = self._fused_gemm_common(weight, absmax, x, partials, tickets)
+        self._call("kudacuda_sm100_batch_gemm_swiglu", int(weight_type), *w, int(intermediate), int(k), *xx,
+                   int(n_pad), int(ksplit), int(batch), *pt, self._tensor_pointer(out, "out"),
+                   _normalize_cuda_handle(stream_ptr))
+
+    def dispatch_batch_gemm_qkv_rope(self, weight: Any, absmax: Any, x: Any, partials: Any, tickets: Any,
+                                     q_bias: Any, k_bias: Any, v_bias: Any, rope_cos: Any, rope_sin: Any, pos: Any,
+                                     q_out: Any, key_cache: Any, value_cache: Any, *, weight_type: int, k: int,
+                                     n_pad: int, ksplit: int, batch: int, q_heads: int, kv_heads: int, head_dim: int,
+                                     max_pos: int, kv_capacity: int, shared_cache: bool = False,
+                                     stream_ptr: int) -> None:
+        """GEMM over q|k|v weights + fused bias, RoPE and K/V append per head."""
+
+        w, xx, pt = self._fused_gemm_common(weight, absmax, x, partials, tickets)
+        self._call("kudacuda_sm100_batch_gemm_qkv_rope", int(weight_type), *w, int(k), *xx, int(n_pad), int(ksplit),
+                   int(batch), *pt, int(q_heads), int(kv_heads), int(head_dim),
+                   self._optional_pointer(q_bias, "q_bias"), self._optional_pointer(k_bias, "k_bias"),
+                   self._optional_pointer(v_bias, "v_bias"), self._tensor_pointer(rope_cos, "rope_cos"),
+                   self._tensor_pointer(rope_sin, "rope_sin"), int(max_pos), self._tensor_pointer(pos, "pos"),
+                   self._tensor_pointer(q_out, "q_out"), self._tensor_pointer(key_cache, "key_cache"),
+                   self._tensor_pointer(value_cache, "value_cache"), int(kv_capacity), 1 if shared_cache else 0,
+                   _normalize_cuda_handle(stream_ptr))
+
     def dispatch_batch_rmsnorm(self, x: Any, weight: Any, out: Any, *, batch: int, hidden: int, epsilon: float,
                                stream_ptr: int) -> None:
         self._call("kudacuda_sm100_batch_rmsnorm", self._tensor_pointer(x, "x"), self._tensor_pointer(weight, "weight"),

@@ -77,6 +77,17 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "kudacuda_sm100_batch_gemm": (_i32, [_p, _i32, _u64, _u64, _i64, _i64, _u64, _i64, _i64, _u64, _i64, _i64, _u64]),
     "kudacuda_sm100_batch_retile_bytes": (_i64, [_i64, _i64]),
     "kudacuda_sm100_batch_retile": (_i32, [_p, _u64, _u64, _i64, _i64, _u64, _i64, _u64]),
+    "kudacuda_sm100_batch_gemm_residual": (
+        _i32, [_p, _i32, _u64, _u64, _i64, _i64, _u64, _i64, _i64, _i64, _u64, _i64, _u64, _u64, _u64]
+    ),
+    "kudacuda_sm100_batch_gemm_swiglu": (
+        _i32, [_p, _i32, _u64, _u64, _i64, _i64, _u64, _i64, _i64, _i64, _u64, _i64, _u64, _u64, _u64]
+    ),
+    "kudacuda_sm100_batch_gemm_qkv_rope": (
+        _i32,
+        [_p, _i32, _u64, _u64, _i64, _u64, _i64, _i64, _i64, _u64, _i64, _u64, _i64, _i64, _i64] + [_u64] * 5
+        + [_i64, _u64, _u64, _u64, _u64, _i64, _i32, _u64],
+    ),
     "kudacuda_sm100_batch_rmsnorm": (_i32, [_p, _u64, _u64, _u64, _i64, _i64, _f32, _u64]),
     "kudacuda_sm100_batch_qkv_rope": (
         _i32, [_p, _u64, _i64, _i64, _i64, _i64, _i64, _i64] + [_u64] * 5 + [_i64] + [_u64] * 4 + [_i64, _i32, _u64]

@@ -387,3 +387,43 @@ def test_batched_prefill_then_persistent_decode_teacher_forced():
     pre.bridge.shutdown()
     br.reset_graph()
     br.shutdown()
+
+
+@pytest.mark.parametrize("batch", [5, 40])
+def test_fused_epilogues_bit_identical_to_separate(bridge, batch):
+    """The GEMMs with fused epilogues (last split CTA of each tile finishes the
+    op) against the GEMMs + separate epilogue kernels: the same split order,
+    so every output bit is the same -- residual stream, caches, next tokens."""
+
+    import torch
+
+    from kudacuda_b200.decode_engine import BatchedDecodePlan, random_weights, tiny_config
+
+    cfg = tiny_config(layers=2, vocab=4096)
+    w = random_weights(bridge, cfg, seed=5, device="cuda:0")
+    plans = [BatchedDecodePlan(bridge, w, batch=batch, kv_bucket=128, max_tokens=128, device="cuda:0", fused=f)
+             for f in (True, False)]
+    plans[0].FUSE_MAX_SPLITS = 64  # every projection through its fused epilogue
+    rng = np.random.default_rng(batch)
+    shape = tuple(plans[0].buffers.kcache.shape)
+    kc0 = torch.from_numpy(O.bf16_bits(rng.normal(0, 1, shape).astype(np.float32)).view(np.int16))
+    vc0 = torch.from_numpy(O.bf16_bits(rng.normal(0, 1, shape).astype(np.float32)).view(np.int16))
+    tokens = [int(t) for t in rng.integers(0, cfg.vocab, batch)]
+    positions = [int(p) for p in rng.integers(0, 120, batch)]
+    stream = torch.cuda.Stream()
+    outs = []
+    for plan in plans:
+        plan.buffers.kcache.copy_(kc0.view(torch.bfloat16).to("cuda:0"))
+        plan.buffers.vcache.copy_(vc0.view(torch.bfloat16).to("cuda:0"))
+        for step in range(2):  # two steps: the tickets reset themselves between launches
+            plan.set_state(tokens, [p + step for p in positions], stream)
+            with torch.cuda.stream(stream):
+                plan.record(int(stream.cuda_stream))
+            stream.synchronize()
+        outs.append((_b16(plan.buffers.x).copy(), _b16(plan.buffers.kcache).copy(), _b16(plan.buffers.vcache).copy(),
+                     plan.buffers.state.cpu().numpy().copy()))
+    assert bridge.error_word(clear=True) == 0
+    for a, b in zip(*outs):
+        np.testing.assert_array_equal(a, b)
+    assert int(plans[0].tickets.abs().sum().item()) == 0
+    assert plans[0].launches_per_step < plans[1].launches_per_step
