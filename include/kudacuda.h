@@ -454,6 +454,8 @@ KUDACUDA_API int kudacuda_sm100_batch_argmax_pairs(void* handle, uint64_t partia
 KUDACUDA_API int kudacuda_sm100_batch_select_advance(void* handle, uint64_t gathered, int64_t world, int64_t batch,
                                                      uint64_t state, uint64_t history, int64_t history_len,
                                                      uint64_t stream);
+KUDACUDA_API int64_t kudacuda_sm100_gqa_batch_workspace_bytes(int64_t batch_size, int64_t query_heads,
+                                                              int64_t kv_heads, int64_t kv_stride);
 KUDACUDA_API int kudacuda_sm100_gqa_decode_batch(void* handle, uint64_t query, uint64_t key_cache,
                                                  uint64_t value_cache, uint64_t output, uint64_t workspace,
                                                  int64_t workspace_bytes, uint64_t tickets, uint64_t kv_len_array,

@@ -1388,6 +1388,32 @@ int kudacuda_sm100_batch_state_views(void* raw, uint64_t state, int64_t batch, u
                                         P<int32_t>(kv_len), S(stream)));
 }
 
+namespace {
+// Split plan of the per-sequence-length attention: with many (sequence, KV
+// head) pairs the split-KV kernel over 64-token chunks (a sequence of L
+// tokens keeps ceil(L / 64) CTAs busy, the rest exit at once); with few, the
+// cluster kernel (its own plan) and the default split plan as its fallback.
+bool batch_gqa_split(int64_t batch, int64_t kv_heads) { return batch * kv_heads >= 64; }
+void batch_gqa_plan(int64_t batch, int64_t kv_heads, int64_t stride, int* chunk, int* nsplit) {
+    if (batch_gqa_split(batch, kv_heads)) {
+        *chunk = 64;
+        *nsplit = static_cast<int>((stride + 63) / 64);
+    } else {
+        kc::gqa_plan_splits(static_cast<int>(stride), static_cast<int>(batch), static_cast<int>(kv_heads), 0, chunk,
+                            nsplit);
+    }
+}
+}  // namespace
+
+int64_t kudacuda_sm100_gqa_batch_workspace_bytes(int64_t batch_size, int64_t query_heads, int64_t kv_heads,
+                                                 int64_t kv_stride) {
+    if (batch_size < 1 || query_heads < 1 || kv_heads < 1 || kv_stride < 1 || kv_stride > (1 << 20)) return -1;
+    int chunk = 0, nsplit = 0;
+    batch_gqa_plan(batch_size, kv_heads, kv_stride, &chunk, &nsplit);
+    return static_cast<int64_t>(kc::gqa_partials_floats(static_cast<int>(batch_size), static_cast<int>(query_heads),
+                                                        nsplit, 128) * sizeof(float));
+}
+
 int kudacuda_sm100_gqa_decode_batch(void* raw, uint64_t query, uint64_t key_cache, uint64_t value_cache,
                                     uint64_t output, uint64_t workspace, int64_t workspace_bytes, uint64_t tickets,
                                     uint64_t kv_len_array, int64_t batch_size, int64_t kv_stride, int64_t query_heads,
@@ -1423,7 +1449,7 @@ int kudacuda_sm100_gqa_decode_batch(void* raw, uint64_t query, uint64_t key_cach
     // take part in its barriers (batch 64, 2048-token caches, lengths 63-510:
     // 5.55 vs 6.35 ms per step); few pairs: the cluster kernel (batch 16:
     // 3.90 vs 4.08 ms per step)
-    a.split_only = batch_size * kv_heads >= 64 ? 1 : 0;
+    a.split_only = batch_gqa_split(batch_size, kv_heads) ? 1 : 0;
     a.kv_len = static_cast<int>(kv_stride);
     a.stride = static_cast<int>(kv_stride);
     a.batch = static_cast<int>(batch_size);
@@ -1432,10 +1458,10 @@ int kudacuda_sm100_gqa_decode_batch(void* raw, uint64_t query, uint64_t key_cach
     a.head_dim = 128;
     a.scale = scale;
     a.err = h->err_word;
-    kc::gqa_plan_splits(static_cast<int>(kv_stride), a.batch, a.kv_heads, 0, &a.chunk, &a.nsplit);
+    batch_gqa_plan(batch_size, kv_heads, kv_stride, &a.chunk, &a.nsplit);
     const size_t need = kc::gqa_partials_floats(a.batch, a.q_heads, a.nsplit, 128) * sizeof(float);
     if (workspace_bytes < static_cast<int64_t>(need)) {
-        h->set_error("sm100_gqa_decode_batch workspace is smaller than kudacuda_sm100_gqa_workspace_bytes()");
+        h->set_error("sm100_gqa_decode_batch workspace is smaller than kudacuda_sm100_gqa_batch_workspace_bytes()");
         return 1;
     }
     return finish(h, "gqa decode (per-sequence lengths)", kc::gqa_decode(a, kc::kBF16, S(stream)));

@@ -854,8 +854,8 @@ class BatchedDecodePlan:
         self.ks_lm = ks(lm_rows, c.hidden)
         part = max(self.ks_qkv * self.qkv_rows, self.ks_o * c.hidden, self.ks_gu * 2 * self.inter,
                    self.ks_dn * c.hidden, self.ks_lm * lm_rows) * self.n_pad
-        ws, tickets, _ = bridge.gqa_workspace(batch=B, query_heads=self.q_heads, kv_heads=self.kv_heads,
-                                              kv_extent=cap, device=device, torch_module=torch)
+        ws, tickets = bridge.gqa_batch_workspace(batch=B, query_heads=self.q_heads, kv_heads=self.kv_heads,
+                                                 kv_stride=cap, device=device, torch_module=torch)
         cos, sin = rope_tables(torch, max(cap, max_tokens) + 1, d, c.rope_theta, device)
         ntiles = max((self.qkv_rows + 127) // 128, (c.hidden + 127) // 128, (2 * self.inter + 127) // 128)
         self.tickets = torch.zeros(ntiles, dtype=torch.int32, device=device)  # fused epilogues (self-resetting)

@@ -1288,6 +1288,21 @@ class KudaCudaBridge:
                    int(batch), self._tensor_pointer(state, "state"), self._optional_pointer(history, "history"),
                    hist_len, _normalize_cuda_handle(stream_ptr))
 
+    def gqa_batch_workspace(self, *, batch: int, query_heads: int, kv_heads: int, kv_stride: int, device: Any,
+                            torch_module: Any = None) -> tuple[Any, Any]:
+        """(workspace, tickets) for dispatch_gqa_decode_batch, allocated once
+        through torch (tickets zero; the kernels leave them zero)."""
+
+        if torch_module is None:
+            import torch as torch_module
+        n = int(self.lib.kudacuda_sm100_gqa_batch_workspace_bytes(int(batch), int(query_heads), int(kv_heads),
+                                                                   int(kv_stride)))
+        if n <= 0:
+            raise NativeCudaError("kudacuda_sm100_gqa_batch_workspace_bytes rejected the shape")
+        ws = torch_module.empty((n // 4,), dtype=torch_module.float32, device=device)
+        tickets = torch_module.zeros((int(batch) * int(kv_heads),), dtype=torch_module.int32, device=device)
+        return ws, tickets
+
     def dispatch_gqa_decode_batch(self, query: Any, key_cache: Any, value_cache: Any, output: Any, workspace: Any,
                                   tickets: Any, kv_len: Any, *, batch: int, kv_stride: int, query_heads: int,
                                   kv_heads: int, head_dim: int = 128, scale: float | None = None,

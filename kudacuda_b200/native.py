@@ -103,6 +103,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "kudacuda_sm100_batch_split_sum": (_i32, [_p, _u64, _i64, _i64, _i64, _u64, _u64]),
     "kudacuda_sm100_batch_argmax_pairs": (_i32, [_p, _u64, _i64, _i64, _i64, _i64, _u64, _i64, _i64, _u64, _u64]),
     "kudacuda_sm100_batch_select_advance": (_i32, [_p, _u64, _i64, _i64, _u64, _u64, _i64, _u64]),
+    "kudacuda_sm100_gqa_batch_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "kudacuda_sm100_gqa_decode_batch": (
         _i32, [_p, _u64, _u64, _u64, _u64, _u64, _i64, _u64, _u64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _u64]
     ),
