@@ -15,10 +15,11 @@
 // (16, 32 or 64) for a range of 64-element K blocks (split-K, so every op has
 // enough CTAs).  A producer warp brings each block's weights and the
 // activations' block (2D TMA, 128-byte swizzle) into a shared ring; for NF4,
-// eight warps dequantise the 128 x 64 tile into a 128-byte-swizzled K-major
-// bf16 tile (two in flight); one thread issues four tcgen05.mma (K = 16
-// each) into a 128 x N fp32 TMEM accumulator and commits to mbarriers that
-// free the ring stage and the tile.  bf16 weights (the tied lm_head) skip the
+// eight warps dequantise the 128 x 64 tile into tensor memory (tcgen05.st,
+// one row per lane, four tiles in flight beside the accumulator); one thread
+// issues four tcgen05.mma (K = 16 each, A from tensor memory or shared
+// memory, B from shared memory) into a 128 x N fp32 TMEM accumulator and
+// commits to an mbarrier that frees the ring stage and the tile.  bf16 weights (the tied lm_head) skip the
 // dequant: TMA places them in the swizzled layout the tensor core reads.  NF4
 // comes either in the bitsandbytes layout or re-tiled at load into one
 // contiguous record per tile and block (one bulk copy).  The accumulator is
@@ -62,6 +63,22 @@ __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+// A operand from tensor memory (one row per lane, two bf16 per 32-bit column)
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                             uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+          "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -133,8 +150,9 @@ __device__ __forceinline__ uint32_t sw128_chunk(int r, int c) {
 //   warps 2-9 (NF4) dequantise: thread (row r, half h) reads its 16 code
 //            bytes, looks up byte -> (level[hi], level[lo]) in a pair table
 //            (16 lane-indexed copies: conflict-free 64-bit lookups), scales by
-//            the block's absmax in fp32, rounds to bf16 and writes the
-//            swizzled A tile; then they read the accumulator out.
+//            the block's absmax in fp32, rounds to bf16 and stores the 32
+//            weights to its TMEM lane (warp w owns lanes 32 (w % 4) ..); then
+//            they read the accumulator out.
 // Barriers: raw_full (TMA bytes landed), raw_empty (the MMAs of that stage's
 // block are done: frees the stage for the producer and, for the dequant warps,
 // the A tile that block read), a_full (256 dequant arrivals), done; one
@@ -142,8 +160,10 @@ __device__ __forceinline__ uint32_t sw128_chunk(int r, int c) {
 constexpr int kGThreads = 320;
 constexpr int kPairCopies = 16;
 constexpr int kPairTableBytes = 256 * kPairCopies * 8;  // 32 KB
-constexpr int kMaxA = 2;
-constexpr int kMaxRaw = 4;
+constexpr int kMaxA = 4;
+constexpr int kTmemAcc = 64;    // accumulator columns (N <= 64)
+constexpr int kTmemATile = 32;  // one dequantised A tile: 128 lanes x 64 bf16 = 32 columns
+constexpr int kMaxRaw = 6;  // ring stages: bounds the barrier arrays (raw_stages() <= this, checked on launch)
 
 // Weight forms: WT 0 NF4 in the bitsandbytes layout (codes by 2D TMA, absmax
 // by the dequant threads from global memory), WT 1 bf16, WT 2 NF4 re-tiled at
@@ -154,17 +174,21 @@ constexpr int kRetileRecord = kTcM * 32 + kTcM * 4;  // 4608
 template <int WT>
 struct GemmSmem {
     static constexpr bool kNf4 = WT != 1;
-    static __host__ __device__ int raw_stages(int n) { return (kNf4 && n == 64) ? 3 : 4; }
-    // two dequantised A tiles (within two CTAs per SM; deeper measured slower)
-    static __host__ __device__ int a_stages(int n) { return kNf4 ? 2 : 0; }
+    static __host__ __device__ int raw_stages(int n) { return kNf4 ? (n == 64 ? 5 : 6) : 4; }
+    // NF4: four dequantised A tiles in tensor memory (after the accumulator)
+    static __host__ __device__ int a_stages(int n) { return kNf4 ? kMaxA : 0; }
     static __host__ __device__ int w_bytes() { return WT == 0 ? kTcM * 32 : WT == 1 ? kATileBytes : kRetileRecord; }
     // stage = [weights][activations] (WT 0, 1) or [activations][record] (WT 2); the swizzled tiles start
     // on 1024-byte boundaries
     static __host__ __device__ int b_off(int n) { return WT == 2 ? 0 : w_bytes(); }
     static __host__ __device__ int w_off(int n) { return WT == 2 ? n * kBlockK * 2 : 0; }
     static __host__ __device__ int raw_bytes(int n) { return (w_bytes() + n * kBlockK * 2 + 1023) / 1024 * 1024; }
-    static __host__ __device__ int fixed_bytes(int n) { return kNf4 ? kPairTableBytes + a_stages(n) * kATileBytes : 0; }
-    static __host__ __device__ int bytes(int n) { return 1024 + fixed_bytes(n) + raw_stages(n) * raw_bytes(n); }
+    static __host__ __device__ int fixed_bytes(int n) { return kNf4 ? kPairTableBytes : 0; }
+    // NF4 CTAs take 256 TMEM columns, so at most two may share an SM: at least 80 KB keeps a third off
+    static __host__ __device__ int bytes(int n) {
+        const int b = 1024 + fixed_bytes(n) + raw_stages(n) * raw_bytes(n);
+        return kNf4 && b < 80 * 1024 ? 80 * 1024 : b;
+    }
 };
 
 // Fused epilogue, run by the last CTA of a tile to finish its split (ticket):
@@ -261,9 +285,9 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
     // 1024-byte aligned base (the swizzled tiles need it)
     uint8_t* const base = smem_raw + (((smem_u32(smem_raw) + 1023u) & ~1023u) - smem_u32(smem_raw));
     uint8_t* const table = base;                          // NF4: pair table
-    uint8_t* const atile = base + kPairTableBytes;        // NF4: SA dequantised A tiles
     uint8_t* const raw = base + G::fixed_bytes(n);        // ring of R stages
-    const int ncols = n <= 32 ? 32 : 64;
+    // TMEM: the 128 x N fp32 accumulator at column 0; NF4 adds SA bf16 A tiles from column 64
+    const int ncols = G::kNf4 ? 256 : (n <= 32 ? 32 : 64);
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
@@ -332,12 +356,20 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
                 if (G::kNf4) bar_wait(&a_full[s], (it / SA) & 1, abort_p);
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 uint8_t* const stg = raw + j * rb;
-                const uint32_t sa = smem_u32(G::kNf4 ? atile + s * kATileBytes : stg);
                 const uint32_t sb = smem_u32(stg + G::b_off(n));
+                if (G::kNf4) {  // K step k = columns 8k .. 8k + 7 of the A tile
+                    const uint32_t ta = tmem + static_cast<uint32_t>(kTmemAcc + s * kTmemATile);
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    umma_bf16(tmem, umma_desc_sw128(sa + 32 * k), umma_desc_sw128(sb + 32 * k), idesc,
-                              (it > 0 || k > 0) ? 1u : 0u);
+                    for (int k = 0; k < 4; ++k)
+                        umma_bf16_ts(tmem, ta + 8 * k, umma_desc_sw128(sb + 32 * k), idesc,
+                                     (it > 0 || k > 0) ? 1u : 0u);
+                } else {
+                    const uint32_t sa = smem_u32(stg);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        umma_bf16(tmem, umma_desc_sw128(sa + 32 * k), umma_desc_sw128(sb + 32 * k), idesc,
+                                  (it > 0 || k > 0) ? 1u : 0u);
+                }
                 // raw_empty[j] frees the ring stage and, for the dequant warps,
                 // the A tile this block read
                 umma_commit(&raw_empty[j]);
@@ -345,14 +377,16 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
             umma_commit(&done_bar);
         }
     } else if (G::kNf4) {
-        // ---- dequantise: thread (r, h) owns 32 weights of row r per block
-        const int dq = tid - 64, r = dq >> 1, h = dq & 1;
+        // ---- dequantise: warp w owns TMEM lanes 32 (w % 4) .. + 31 (tile rows) and
+        // half (w - 2) / 4 of each block's 64 elements; thread = one row
+        const int dq = tid - 64, h = dq >> 7, r = 32 * (warp & 3) + lane;
         const int grow = tile * kTcM + r;
         const bool row_ok = grow < a.rows;
         const float* arow = WT == 0 ? a.absmax + static_cast<int64_t>(row_ok ? grow : 0) * nblk : nullptr;
         const bool vec4 = WT == 0 && (nblk & 3) == 0;
         const uint32_t tl_u32 = smem_u32(table) + static_cast<uint32_t>((lane & (kPairCopies - 1)) * 8);
-        const uint32_t raw_u32 = smem_u32(raw), atile_u32 = smem_u32(atile);
+        const uint32_t raw_u32 = smem_u32(raw);
+        const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
         float4 cur4 = make_float4(0.F, 0.F, 0.F, 0.F), nxt4 = cur4;
         int cur_g = -1;
         for (int it = 0; it < nit; ++it) {
@@ -388,11 +422,11 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
                 const int ib = it - SA;
                 bar_wait(&raw_empty[ib % R], (ib / R) & 1, abort_p);
             }
-            const uint32_t as = atile_u32 + static_cast<uint32_t>(s * kATileBytes);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint64_t ss = (static_cast<uint64_t>(__float_as_uint(sc)) << 32) | __float_as_uint(sc);
+            uint32_t o[16];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                uint32_t o[4];
                 const uint32_t w = cw[q];
                 // byte bb of w -> table offset byte * 128 (+ this lane's copy)
                 const uint32_t off[4] = {(w << 7) & 0x7F80u, (w >> 1) & 0x7F80u, (w >> 9) & 0x7F80u,
@@ -405,14 +439,13 @@ __global__ void __launch_bounds__(kGThreads, 2) gemm_tc_kernel(const __grid_cons
                         "mul.rn.f32x2 t, t, %2;\n\t"
                         "mov.b64 {lo, hi}, t;\n\t"
                         "cvt.rn.bf16x2.f32 %0, hi, lo;\n\t}"
-                        : "=r"(o[bb])
+                        : "=r"(o[4 * q + bb])
                         : "r"(tl_u32 + off[bb]), "l"(ss));
                 }
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(as + sw128_chunk(r, 4 * h + q)),
-                             "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3])
-                             : "memory");
             }
-            fence_proxy_async_smem();  // generic stores -> visible to the tensor core
+            // columns 16 h .. 16 h + 15 of A tile s, this warp's 32 lanes
+            tmem_st16(t_row + static_cast<uint32_t>(kTmemAcc + s * kTmemATile + 16 * h), o);
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             bar_arrive(&a_full[s]);
         }
     }
@@ -847,6 +880,9 @@ int batch_gemm_ksplit(int rows, int K) {
 namespace {
 template <int WT>
 cudaError_t launch_gemm(const TcArgs& a, int ksplit, cudaStream_t s) {
+    if (GemmSmem<WT>::raw_stages(a.n_pad) > kMaxRaw || GemmSmem<WT>::a_stages(a.n_pad) > kMaxA ||
+        GemmSmem<WT>::a_stages(a.n_pad) > GemmSmem<WT>::raw_stages(a.n_pad))
+        return cudaErrorInvalidConfiguration;  // barrier arrays, and the A-tile release rule needs R >= SA
     CUtensorMap mw, mx;
     cudaError_t st;
     if (WT == 2)

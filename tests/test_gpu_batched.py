@@ -144,7 +144,12 @@ def test_batched_step_against_oracle_per_sequence(bridge, batched_one_layer):
         x = emb[tok].copy()
         kc, vc = kc0[0, b].copy(), vc0[0, b].copy()
         O.layer_step_hf(layer, ocfg, x, kc, vc, plan.kv_bucket, pos, cos[pos], sin[pos])
-        norm_close(O.bf16_to_f32(xs[b]), O.bf16_to_f32(x))
+        # the batched path rounds every dequantised weight to bf16 (the
+        # Transformers + bitsandbytes arithmetic) where the oracle's layer keeps
+        # them fp32 (the reference kernels'): a few elements of the composed
+        # layer output differ by ~3 bf16 ulps, so the element bound is 2e-2
+        # of the largest value; the norm-wise bound stays 1e-2
+        norm_close(O.bf16_to_f32(xs[b]), O.bf16_to_f32(x), elem_rel=2e-2)
         norm_close(O.bf16_to_f32(kc_gpu[0, b][:, pos]), O.bf16_to_f32(kc[:, pos]))
         norm_close(O.bf16_to_f32(vc_gpu[0, b][:, pos]), O.bf16_to_f32(vc[:, pos]))
         np.testing.assert_array_equal(kc_gpu[0, b][:, :pos], kc0[0, b][:, :pos])
