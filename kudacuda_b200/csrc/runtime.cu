@@ -1397,6 +1397,13 @@ bool batch_gqa_split(int64_t batch, int64_t kv_heads) { return batch * kv_heads 
 void batch_gqa_plan(int64_t batch, int64_t kv_heads, int64_t stride, int* chunk, int* nsplit) {
     kc::gqa_plan_splits(static_cast<int>(stride), static_cast<int>(batch), static_cast<int>(kv_heads), 0, chunk,
                         nsplit);
+    // With 128 or more (sequence, kv head) pairs, 128-token chunks balance the
+    // split-KV grid better (B200: batch 64 x 2 kv heads 3.6% faster per step);
+    // at 64 pairs the default chunking is faster (batch 32: 5%).
+    if (batch * kv_heads >= 128 && *chunk > 128) {
+        *chunk = 128;
+        *nsplit = static_cast<int>((stride + 127) / 128);
+    }
 }
 }  // namespace
 
