@@ -973,7 +973,7 @@ def batched_gemm_roofline(torch, bridge, plan, stream) -> dict:
     tf = _peak_tflops()
     plan.capture(stream)  # the handle holds one graph: recapture the step
     return {
-        "kernel": "gemm_tc_kernel<2> (re-tiled NF4 by bulk copy, bf16 dequant in shared memory, tcgen05.mma M=128 x N=n_pad, TMEM)",
+        "kernel": "gemm_tc_kernel<2> (re-tiled NF4 by bulk copy, bf16 dequant into tensor memory, tcgen05.mma with A from TMEM, M=128 x N=n_pad)",
         "bound": "hbm",
         "achieved": round(achieved, 1),
         "peak": peak,

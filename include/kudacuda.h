@@ -350,7 +350,8 @@ KUDACUDA_API int kudacuda_sm100_decode_layers_persistent(void* handle, uint64_t 
  *   batch_retile (absmax unused, the fastest NF4 form).  ksplit in [1, k/64];
  *   batch_gemm_ksplit suggests one.  Several matrices may share one partials
  *   buffer through row_offset.
- * The epilogues sum the splits in split order (deterministic):
+ * The epilogues sum the splits in split order (deterministic); their
+ * partials pointer is 16-byte aligned, as batch_gemm requires of its own:
  *   batch_qkv_rope: partials rows q | k | v; bias, RoPE at pos[b] (int32 [B]),
  *     q -> q_out [B][qh][hd], k/v appended to caches [B][kvh][kv_capacity][hd]
  *     at pos[b];
@@ -361,6 +362,8 @@ KUDACUDA_API int kudacuda_sm100_decode_layers_persistent(void* handle, uint64_t 
  *     bf16-rounded logits; state is int32 [B][4] = {token, pos, kv_len, pad}
  *     and becomes {argmax, pos + 1, pos + 2, pad}; history [B][history_len]
  *     (optional) records the token at its new position.
+ * batch_rmsnorm: per sequence, Transformers' RMSNorm in bf16 (hidden % 8 == 0,
+ *   hidden <= 8192, x / weight / out 16-byte aligned).
  * batch_embedding: x[b] = embedding[state[b].token]; batch_state_views copies
  * state's pos and kv_len columns to pos[B] and kv_len[B] for the RoPE
  * epilogue and gqa_decode_batch (kudacuda_sm100_gqa_decode, bf16, with a

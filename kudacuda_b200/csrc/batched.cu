@@ -496,18 +496,37 @@ __device__ __forceinline__ float split_sum(const float* partials, int ksplit, in
     return v;
 }
 
-// out[b][:] = bf16(w * bf16(x[b] * rsqrt(mean(x[b]^2) + eps)))  (one CTA per sequence)
+// out[b][:] = bf16(w * bf16(x[b] * rsqrt(mean(x[b]^2) + eps)))  (one CTA per sequence).
+// hidden % 8 == 0: each thread holds up to kNormVec uint4 of x (8 bf16 each) and
+// the matching weights in registers, so the row is read once.
+constexpr int kNormVec = 4;  // hidden <= 256 * 8 * kNormVec in one pass
 __global__ void __launch_bounds__(256) batch_rmsnorm_kernel(const uint16_t* x, const uint16_t* w, uint16_t* out,
                                                             int H, float eps) {
     __shared__ float red[8];
     pdl_launch_dependents();
     pdl_wait_on_producer();
     const int b = blockIdx.x, tid = threadIdx.x;
-    const uint16_t* xb = x + static_cast<int64_t>(b) * H;
+    const uint4* xb = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(b) * H);
+    const uint4* wb = reinterpret_cast<const uint4*>(w);
+    const int nv = H >> 3;
+    uint4 xv[kNormVec], wv[kNormVec];
+#pragma unroll
+    for (int u = 0; u < kNormVec; ++u) {
+        const int i = tid + 256 * u;
+        xv[u] = i < nv ? xb[i] : make_uint4(0, 0, 0, 0);
+        wv[u] = i < nv ? __ldg(wb + i) : make_uint4(0, 0, 0, 0);
+    }
     float ss = 0.F;
-    for (int i = tid; i < H; i += 256) {
-        const float v = bf16_bits_to_f32(xb[i]);
-        ss += v * v;
+#pragma unroll
+    for (int u = 0; u < kNormVec; ++u) {
+        const uint32_t* e = reinterpret_cast<const uint32_t*>(&xv[u]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float lo = bf16_bits_to_f32(static_cast<uint16_t>(e[j] & 0xFFFFu));
+            const float hi = bf16_bits_to_f32(static_cast<uint16_t>(e[j] >> 16));
+            ss += lo * lo;
+            ss += hi * hi;
+        }
     }
     ss = warp_sum(ss);
     if ((tid & 31) == 0) red[tid >> 5] = ss;
@@ -516,43 +535,106 @@ __global__ void __launch_bounds__(256) batch_rmsnorm_kernel(const uint16_t* x, c
 #pragma unroll
     for (int i = 0; i < 8; ++i) tot += red[i];
     const float inv = 1.0F / sqrtf(tot / static_cast<float>(H) + eps);
-    for (int i = tid; i < H; i += 256)
-        out[static_cast<int64_t>(b) * H + i] =
-            f32_to_bf16_bits(round_bf16(bf16_bits_to_f32(w[i]) * round_bf16(bf16_bits_to_f32(xb[i]) * inv)));
+    uint4* ob = reinterpret_cast<uint4*>(out + static_cast<int64_t>(b) * H);
+#pragma unroll
+    for (int u = 0; u < kNormVec; ++u) {
+        const int i = tid + 256 * u;
+        if (i < nv) {
+            const uint32_t* e = reinterpret_cast<const uint32_t*>(&xv[u]);
+            const uint32_t* g = reinterpret_cast<const uint32_t*>(&wv[u]);
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float lo = round_bf16(bf16_bits_to_f32(static_cast<uint16_t>(g[j] & 0xFFFFu)) *
+                                            round_bf16(bf16_bits_to_f32(static_cast<uint16_t>(e[j] & 0xFFFFu)) * inv));
+                const float hi = round_bf16(bf16_bits_to_f32(static_cast<uint16_t>(g[j] >> 16)) *
+                                            round_bf16(bf16_bits_to_f32(static_cast<uint16_t>(e[j] >> 16)) * inv));
+                o[j] = static_cast<uint32_t>(f32_to_bf16_bits(lo)) | (static_cast<uint32_t>(f32_to_bf16_bits(hi)) << 16);
+            }
+            ob[i] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    }
 }
 
 // The epilogues work on tiles of consecutive rows x the padded batch: the
-// split-K partial sums [split][row][n_pad] are read row-contiguous (coalesced),
-// summed in split order (deterministic), staged in shared memory, and written
-// per sequence along the row (coalesced).
-constexpr int kEpiRows = 32;
+// split-K partial sums [split][row][n_pad] (16-byte aligned, as the GEMM
+// writes them) are read row-contiguous as float4 (coalesced), summed in split
+// order (deterministic), staged in shared memory, and written per sequence
+// along the row.  A tile is epi_rows(n_pad) rows = 1,024 floats, one float4 per
+// thread, so every load a thread needs can be in flight at once.
+constexpr int kEpiFloats = 1024;
+__host__ __device__ __forceinline__ int epi_rows(int n_pad) { return kEpiFloats / n_pad; }
 
-// sums of `nrows` rows starting at `row0` into t[row][b] (padded stride n_pad + 1);
-// the split loads of an element are independent (issued together), the adds
-// run in split order
-__device__ __forceinline__ void sum_tile(const float* partials, int ksplit, int rows, int n_pad, int row0, int nrows,
-                                         float* t) {
-    const int total = nrows * n_pad;
-    const int64_t kstride = static_cast<int64_t>(rows) * n_pad;
-    for (int e = threadIdx.x; e < total; e += blockDim.x) {
-        const int i = e / n_pad, b = e - i * n_pad;
-        const float* p = partials + static_cast<int64_t>(row0 + i) * n_pad + b;
-        float v = 0.F;
-        int k = 0;
-        for (; k + 4 <= ksplit; k += 4) {
-            const float a0 = __ldg(p + k * kstride), a1 = __ldg(p + (k + 1) * kstride);
-            const float a2 = __ldg(p + (k + 2) * kstride), a3 = __ldg(p + (k + 3) * kstride);
-            v += a0;
-            v += a1;
-            v += a2;
-            v += a3;
+// Sums of rows row0[u] .. row0[u] + nrows - 1 (nrows <= PER * kEpiFloats / n_pad)
+// of NT tiles into t[u][row * (n_pad + 1) + b]; each thread owns PER float4s
+// of a tile.  The loads of up to 16 (one float4 a thread) or 8 / (NT * PER)
+// splits are issued together (at most 64 registers of loads in flight);
+// the adds run in split order from +0, the order of every other reader of the
+// partials (the fused epilogue, split_sum).
+template <int NT, int PER>
+__device__ __forceinline__ void sum_tiles(const float* partials, int ksplit, int rows, int n_pad, const int (&row0)[NT],
+                                          int nrows, float* const (&t)[NT]) {
+    constexpr int kB = NT * PER == 1 ? 16 : 8 / (NT * PER) > 0 ? 8 / (NT * PER) : 1;
+    const int q = n_pad >> 2;  // float4s per row
+    const int total = nrows * q;
+    const int64_t kstride4 = static_cast<int64_t>(rows) * q;
+    const float4* p[NT][PER];
+    bool active[PER];
+#pragma unroll
+    for (int v = 0; v < PER; ++v) {
+        const int f = threadIdx.x + 256 * v;
+        active[v] = f < total;
+#pragma unroll
+        for (int u = 0; u < NT; ++u)
+            p[u][v] = reinterpret_cast<const float4*>(partials) + static_cast<int64_t>(row0[u]) * q + (active[v] ? f : 0);
+    }
+    float4 acc[NT][PER];
+#pragma unroll
+    for (int u = 0; u < NT; ++u)
+#pragma unroll
+        for (int v = 0; v < PER; ++v) acc[u][v] = make_float4(0.F, 0.F, 0.F, 0.F);
+    for (int k0 = 0; k0 < ksplit; k0 += kB) {
+        float4 r[NT][PER][kB];
+#pragma unroll
+        for (int j = 0; j < kB; ++j)
+#pragma unroll
+            for (int v = 0; v < PER; ++v) {
+                const bool ok = active[v] && k0 + j < ksplit;
+#pragma unroll
+                for (int u = 0; u < NT; ++u)
+                    r[u][v][j] = ok ? __ldg(p[u][v] + static_cast<int64_t>(k0 + j) * kstride4)
+                                    : make_float4(0.F, 0.F, 0.F, 0.F);
+            }
+#pragma unroll
+        for (int j = 0; j < kB; ++j) {
+            if (k0 + j < ksplit) {
+#pragma unroll
+                for (int u = 0; u < NT; ++u)
+#pragma unroll
+                    for (int v = 0; v < PER; ++v) {
+                        acc[u][v].x += r[u][v][j].x;
+                        acc[u][v].y += r[u][v][j].y;
+                        acc[u][v].z += r[u][v][j].z;
+                        acc[u][v].w += r[u][v][j].w;
+                    }
+            }
         }
-        for (; k < ksplit; ++k) v += __ldg(p + k * kstride);
-        t[i * (n_pad + 1) + b] = v;
+    }
+#pragma unroll
+    for (int v = 0; v < PER; ++v) {
+        if (active[v]) {
+            const int f = threadIdx.x + 256 * v, i = f / q, c = 4 * (f - i * q);
+#pragma unroll
+            for (int u = 0; u < NT; ++u) {
+                float* d = t[u] + i * (n_pad + 1) + c;
+                d[0] = acc[u][v].x;
+                d[1] = acc[u][v].y;
+                d[2] = acc[u][v].z;
+                d[3] = acc[u][v].w;
+            }
+        }
     }
 }
-// rows per epilogue CTA: about 512 (row, sequence) elements
-__host__ __device__ __forceinline__ int epi_rows(int n_pad) { return n_pad >= 64 ? 8 : n_pad >= 32 ? 16 : 32; }
 
 // bias + RoPE (Transformers' rotate_half with bf16 rounding) + K/V append at
 // pos[b]; one CTA per (head of q | k | v, group of kQkvPairs dimension pairs
@@ -567,8 +649,11 @@ __global__ void __launch_bounds__(256) batch_qkv_epilogue_kernel(const BatchQkv 
     const int groups = half / kQkvPairs;
     const int head = blockIdx.x / groups;  // 0 .. q_heads + 2 kv_heads - 1
     const int i0 = (blockIdx.x - head * groups) * kQkvPairs;
-    sum_tile(a.partials, a.ksplit, rows, a.n_pad, head * hd + i0, kQkvPairs, tq);
-    sum_tile(a.partials, a.ksplit, rows, a.n_pad, head * hd + half + i0, kQkvPairs, tq + kQkvPairs * np1);
+    {
+        const int r0[2] = {head * hd + i0, head * hd + half + i0};
+        float* const tt[2] = {tq, tq + kQkvPairs * np1};
+        sum_tiles<2, 1>(a.partials, a.ksplit, rows, a.n_pad, r0, kQkvPairs, tt);
+    }
     __syncthreads();
     const bool isq = head < a.q_heads, isk = !isq && head < a.q_heads + a.kv_heads;
     if (isq || isk) {
@@ -613,37 +698,55 @@ __global__ void __launch_bounds__(256) batch_qkv_epilogue_kernel(const BatchQkv 
     }
 }
 
-// x[b][r] = bf16(x[b][r] + bf16(sum))   (o_proj, down); 32 rows per CTA
+// x[b][r] = bf16(x[b][r] + bf16(sum))   (o_proj, down); epi_rows(n_pad) rows per CTA.
+// Each thread reads its (at most four) residual elements before any store.
 __global__ void __launch_bounds__(256) batch_residual_kernel(const float* partials, int ksplit, int rows, int n_pad,
                                                              int batch, uint16_t* x) {
-    __shared__ float t[kEpiRows * 65];
+    __shared__ float t[kEpiFloats + 64];  // [er][n_pad + 1]
     pdl_launch_dependents();
     pdl_wait_on_producer();
     const int er = epi_rows(n_pad);
     const int row0 = blockIdx.x * er;
     const int nr = min(er, rows - row0);
-    sum_tile(partials, ksplit, rows, n_pad, row0, nr, t);
+    {
+        const int r0[1] = {row0};
+        float* const tt[1] = {t};
+        sum_tiles<1, 1>(partials, ksplit, rows, n_pad, r0, nr, tt);
+    }
     __syncthreads();
-    for (int e = threadIdx.x; e < batch * er; e += blockDim.x) {
-        const int b = e / er, i = e - b * er;
-        if (i < nr) {
-            uint16_t* xp = x + static_cast<int64_t>(b) * rows + row0 + i;
-            *xp = f32_to_bf16_bits(bf16_bits_to_f32(*xp) + round_bf16(t[i * (n_pad + 1) + b]));
-        }
+    constexpr int kPer = kEpiFloats / 256;  // batch * er <= n_pad * er = 1,024 elements
+    uint16_t* xp[kPer];
+    uint16_t xv[kPer];
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+        const int e = threadIdx.x + 256 * u, b = e / er, i = e - b * er;
+        xp[u] = (b < batch && i < nr) ? x + static_cast<int64_t>(b) * rows + row0 + i : nullptr;
+        xv[u] = xp[u] != nullptr ? *xp[u] : static_cast<uint16_t>(0);
+    }
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+        const int e = threadIdx.x + 256 * u, b = e / er, i = e - b * er;
+        if (xp[u] != nullptr) *xp[u] = f32_to_bf16_bits(bf16_bits_to_f32(xv[u]) + round_bf16(t[i * (n_pad + 1) + b]));
     }
 }
 
-// h[b][j] = bf16(bf16(silu(bf16 gate_j)) * bf16 up_j); rows = gate (inter) | up (inter); 32 j per CTA
+// h[b][j] = bf16(bf16(silu(bf16 gate_j)) * bf16 up_j); rows = gate (inter) | up (inter);
+// 2 * epi_rows(n_pad) j per CTA (grid within one wave at n_pad 64), gate and up
+// tiles summed in one pass
+constexpr int kSwigluPer = 2;
 __global__ void __launch_bounds__(256) batch_swiglu_kernel(const float* partials, int ksplit, int inter, int n_pad,
                                                            int batch, uint16_t* h) {
-    __shared__ float tg[kEpiRows * 65], tu[kEpiRows * 65];
+    __shared__ float tg[kSwigluPer * kEpiFloats + 128], tu[kSwigluPer * kEpiFloats + 128];
     pdl_launch_dependents();
     pdl_wait_on_producer();
-    const int er = epi_rows(n_pad);
+    const int er = kSwigluPer * epi_rows(n_pad);
     const int j0 = blockIdx.x * er;
     const int nr = min(er, inter - j0);
-    sum_tile(partials, ksplit, 2 * inter, n_pad, j0, nr, tg);
-    sum_tile(partials, ksplit, 2 * inter, n_pad, inter + j0, nr, tu);
+    {
+        const int r0[2] = {j0, inter + j0};
+        float* const tt[2] = {tg, tu};
+        sum_tiles<2, kSwigluPer>(partials, ksplit, 2 * inter, n_pad, r0, nr, tt);
+    }
     __syncthreads();
     for (int e = threadIdx.x; e < batch * er; e += blockDim.x) {
         const int b = e / er, i = e - b * er;
@@ -864,17 +967,35 @@ cudaError_t batch_retile(const uint8_t* packed, const float* absmax, int rows, i
 }
 
 int batch_gemm_ksplit(int rows, int K) {
-    // about two CTAs per SM, but at least 8 K blocks per CTA where K allows:
-    // a CTA streams its blocks through the cp.async ring, so fatter CTAs keep
-    // more bytes in flight and write fewer fp32 partials
+    // A CTA's time is set by its K blocks (a per-block load -> dequant -> MMA
+    // chain) plus a fixed start-up and drain, and two CTAs share an SM, so
+    // what counts is how full the last wave of CTAs is.  The smallest split
+    // whose last wave is at least 85% full wins, else the fullest; every CTA
+    // keeps at least 4 K blocks, and a matrix with a wave of tiles already is
+    // not split (its partials would grow for nothing).  Measured on B200
+    // (n_pad 64, us per launch): gate|up 22016 x 2048 split 2 / 3 / 4: 31.7 /
+    // 25.8 / 32.4; q|k|v 2560 x 2048 split 4 / 8: 9.4 / 7.7; down 2048 x
+    // 11008 split 16 / 21 (a second wave of 40 CTAs): 13.2 / 20.0.
     const int mtiles = (rows + kTcM - 1) / kTcM;
     const int nblk = K / kBlockK;
-    const int target = 2 * device_sm_count();
-    int ks = (target + mtiles - 1) / mtiles;
-    const int cap = nblk / 8 > 1 ? nblk / 8 : 1;
-    if (ks > cap) ks = cap;
-    if (ks > 16) ks = 16;
-    return ks < 1 ? 1 : ks;
+    const int slots = 2 * device_sm_count();
+    if (mtiles >= slots) return 1;
+    int cap = nblk / 4;
+    if (cap > 32) cap = 32;
+    if (cap < 1) cap = 1;
+    int best = 1;
+    double best_fill = 0.0;
+    for (int ks = 1; ks <= cap; ++ks) {
+        const int ctas = mtiles * ks;
+        const int waves = (ctas + slots - 1) / slots;
+        const double fill = static_cast<double>(ctas) / (static_cast<double>(waves) * slots);
+        if (fill >= 0.85) return ks;
+        if (fill > best_fill + 1e-9) {
+            best_fill = fill;
+            best = ks;
+        }
+    }
+    return best;
 }
 
 namespace {
@@ -957,11 +1078,15 @@ cudaError_t batch_gemm(int weight_type, const void* weight, const float* absmax,
 
 cudaError_t batch_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* out, int batch, int H, float eps,
                           cudaStream_t s) {
+    if (H % 8 != 0 || H > 256 * 8 * kNormVec) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) & 15u)
+        return cudaErrorMisalignedAddress;
     return launch_pdl(batch_rmsnorm_kernel, dim3(batch), dim3(256), 0, s, x, w, out, H, eps);
 }
 
 cudaError_t batch_qkv_epilogue(const BatchQkv& q, cudaStream_t s) {
     if (q.n_pad > 64 || q.head_dim % (2 * kQkvPairs) != 0) return cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(q.partials) & 15u) return cudaErrorMisalignedAddress;
     const int groups = q.head_dim / 2 / kQkvPairs;
     return launch_pdl(batch_qkv_epilogue_kernel, dim3((q.q_heads + 2 * q.kv_heads) * groups), dim3(256), 0, s, q);
 }
@@ -969,6 +1094,7 @@ cudaError_t batch_qkv_epilogue(const BatchQkv& q, cudaStream_t s) {
 cudaError_t batch_residual(const float* partials, int ksplit, int rows, int n_pad, int batch, uint16_t* x,
                            cudaStream_t s) {
     if (n_pad > 64) return cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(partials) & 15u) return cudaErrorMisalignedAddress;
     const int er = epi_rows(n_pad);
     return launch_pdl(batch_residual_kernel, dim3((rows + er - 1) / er), dim3(256), 0, s, partials, ksplit,
                       rows, n_pad, batch, x);
@@ -977,7 +1103,8 @@ cudaError_t batch_residual(const float* partials, int ksplit, int rows, int n_pa
 cudaError_t batch_swiglu(const float* partials, int ksplit, int inter, int n_pad, int batch, uint16_t* h,
                          cudaStream_t s) {
     if (n_pad > 64) return cudaErrorInvalidValue;
-    const int er = epi_rows(n_pad);
+    if (reinterpret_cast<uintptr_t>(partials) & 15u) return cudaErrorMisalignedAddress;
+    const int er = kSwigluPer * epi_rows(n_pad);
     return launch_pdl(batch_swiglu_kernel, dim3((inter + er - 1) / er), dim3(256), 0, s, partials, ksplit,
                       inter, n_pad, batch, h);
 }

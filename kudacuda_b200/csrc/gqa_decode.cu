@@ -73,7 +73,21 @@ __device__ __forceinline__ void load_vec4(const void* base, int64_t elem, float*
     }
 }
 
-// Combine the nsplit partials of the G heads of one (batch, kv head).  Lane
+// The KV length of sequence b (one length for all, or one per sequence),
+// clamped to [0, stride]; the split kernel flags a length out of range.
+__device__ __forceinline__ int gqa_kv_len(const GqaArgs& a, int b) {
+    const int kv_len = a.kv_len_dev != nullptr ? a.kv_len_dev[a.kv_len_per_batch ? b : 0] : a.kv_len;
+    return kv_len < 1 ? 0 : kv_len > a.stride ? a.stride : kv_len;
+}
+// Splits that hold tokens of a sequence of kv_len tokens: ceil(kv_len / chunk),
+// at least 1 (an empty length still has split 0 write an empty partial).  Only
+// these run past their first lines, write partials and take a ticket.
+__device__ __forceinline__ int gqa_live_splits(const GqaArgs& a, int kv_len) {
+    const int s = (kv_len + a.chunk - 1) / a.chunk;
+    return s < 1 ? 1 : s > a.nsplit ? a.nsplit : s;
+}
+
+// Combine the live partials of the G heads of one (batch, kv head).  Lane
 // s of a warp owns split s (mod 32) for the max and the softmax weights; the
 // weights are then broadcast so every lane accumulates its 4 dims over all
 // splits with independent (batched) loads.
@@ -81,25 +95,26 @@ template <int DT, int G>
 __device__ void gqa_combine_group(const GqaArgs& a, int b, int kvh) {
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
+    const int live = gqa_live_splits(a, gqa_kv_len(a, b));
     for (int h = warp; h < G; h += kGqaThreads / 32) {
         const int qh = kvh * G + h;
         const float* base = a.partials + (static_cast<int64_t>(b) * a.q_heads + qh) * a.nsplit * kPartialStride;
         float m = -INFINITY;
-        for (int s = lane; s < a.nsplit; s += 32) m = fmaxf(m, __ldcg(base + s * kPartialStride));
+        for (int s = lane; s < live; s += 32) m = fmaxf(m, __ldcg(base + s * kPartialStride));
         m = warp_max(m);
         float l = 0.0F;
         float acc[4] = {0.0F, 0.0F, 0.0F, 0.0F};
-        for (int s0 = 0; s0 < a.nsplit; s0 += 32) {
+        for (int s0 = 0; s0 < live; s0 += 32) {
             const int s = s0 + lane;
             float w = 0.0F;
-            if (s < a.nsplit) {
+            if (s < live) {
                 const float ms = __ldcg(base + s * kPartialStride);
                 if (ms != -INFINITY) {
                     w = exp2f(ms - m);
                     l += w * __ldcg(base + s * kPartialStride + 1);
                 }
             }
-            const int cnt = min(32, a.nsplit - s0);
+            const int cnt = min(32, live - s0);
 #pragma unroll 4
             for (int i = 0; i < cnt; ++i) {
                 const float wi = __shfl_sync(0xffffffffu, w, i);
@@ -138,12 +153,6 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a)
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
-    if (tid == 0) {
-        mbar_init(&kv_bar[0], 1);
-        mbar_init(&kv_bar[1], 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
     pdl_launch_dependents();
     pdl_wait_on_producer();
 
@@ -151,11 +160,19 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a)
     const int kvh = blockIdx.x - b * a.kv_heads;
     const int split = blockIdx.y;
 
-    int kv_len = a.kv_len_dev != nullptr ? a.kv_len_dev[a.kv_len_per_batch ? b : 0] : a.kv_len;
-    if (kv_len < 1 || kv_len > a.stride) {
-        if (a.err != nullptr && tid == 0) atomicOr(a.err, 4);
-        kv_len = kv_len < 1 ? 0 : a.stride;
+    const int kv_raw = a.kv_len_dev != nullptr ? a.kv_len_dev[a.kv_len_per_batch ? b : 0] : a.kv_len;
+    if ((kv_raw < 1 || kv_raw > a.stride) && a.err != nullptr && tid == 0 && split == 0) atomicOr(a.err, 4);
+    const int kv_len = gqa_kv_len(a, b);
+    // splits past the sequence's last token leave at once (a whole CTA: the
+    // length is the same for every thread); the combine reads live ones only
+    const int live = gqa_live_splits(a, kv_len);
+    if (split >= live) return;
+    if (tid == 0) {
+        mbar_init(&kv_bar[0], 1);
+        mbar_init(&kv_bar[1], 1);
+        fence_mbar_init();
     }
+    __syncthreads();
     const int t0 = split * a.chunk;
     int n = kv_len - t0;
     n = n < 0 ? 0 : (n > a.chunk ? a.chunk : n);
@@ -270,7 +287,7 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a)
     if (tid == 0) {
         int* ctr = a.counters + blockIdx.x;
         const int ticket = atomicAdd(ctr, 1);
-        const int last = ticket == a.nsplit - 1;
+        const int last = ticket == live - 1;
         if (last) atomicExch(ctr, 0);  // self-reset for the next launch / graph replay
         last_s = last;
     }

@@ -1206,8 +1206,9 @@ int kudacuda_sm100_batch_rmsnorm(void* raw, uint64_t x, uint64_t weight, uint64_
     Handle* h = as_handle(raw);
     if (!ready(h, "kudacuda_sm100_batch_rmsnorm")) return 1;
     if (x == 0 || weight == 0 || out == 0 || batch < 1 || batch > 64 || hidden < 8 || hidden % 8 != 0 ||
-        hidden > (1 << 20) || !(eps > 0.0F)) {
-        h->set_error("sm100_batch_rmsnorm requires non-null pointers, 1 <= batch <= 64, hidden % 8 == 0, eps > 0");
+        hidden > 8192 || !(eps > 0.0F)) {
+        h->set_error("sm100_batch_rmsnorm requires non-null pointers, 1 <= batch <= 64, hidden % 8 == 0, "
+                     "hidden <= 8192, eps > 0");
         return 1;
     }
     return finish(h, "batch_rmsnorm_kernel",

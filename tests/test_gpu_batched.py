@@ -287,6 +287,87 @@ def test_batch_tp_pieces_exact(bridge):
     assert bridge.error_word(clear=True) == 0
 
 
+def _split_sum_np(p):
+    s = np.zeros(p.shape[1:], dtype=np.float32)
+    for k in range(p.shape[0]):  # split order, from +0, in fp32
+        s = s + p[k]
+    return s
+
+
+@pytest.mark.parametrize(
+    "n_pad,batch,ksplit,rows",
+    [
+        (16, 5, 1, 300),     # ragged last tile, one split
+        (32, 20, 3, 300),
+        (64, 64, 17, 2048),  # more splits than one round of loads
+        (64, 33, 2, 200),
+    ],
+)
+def test_batch_epilogues_against_numpy(bridge, n_pad, batch, ksplit, rows):
+    """The residual and SwiGLU epilogues against a numpy restatement: split
+    sums in split order, bf16 rounding points as Transformers; the residual is
+    bit-exact, SwiGLU within one bf16 step (CUDA expf vs numpy exp) on at most
+    0.1% of elements; sequences from `batch` up are not written.  The batched
+    RMSNorm (a tree sum of squares) against the same arithmetic with an exact
+    sum of squares: the fp32 scale may differ in its last bits and, through the
+    two bf16 roundings (x * scale, then * weight), an element by up to two bf16
+    steps on at most 1% of elements.  Against the oracle, whose sequential fp32
+    sum over 2,048 squares is itself off by ~1e-5 relative (26 flips in a row
+    against the exact sum on these inputs), at most 3%."""
+
+    import torch
+
+    from kudacuda_b200.kudacuda_sidecar import NativeCudaError
+
+    dev = "cuda:0"
+    rng = np.random.default_rng(11 + n_pad + ksplit)
+    part_np = rng.normal(0, 1, (ksplit, rows, n_pad)).astype(np.float32)
+    part = torch.from_numpy(part_np).to(dev)
+    s = _split_sum_np(part_np)  # [rows][n_pad]
+    # residual
+    x0 = O.bf16_bits(rng.normal(0, 1, (n_pad, rows)).astype(np.float32))
+    x = torch.from_numpy(x0.view(np.int16)).to(dev)
+    bridge.dispatch_batch_residual(part, x, ksplit=ksplit, rows=rows, n_pad=n_pad, batch=batch, stream_ptr=0)
+    ref = x0.copy()
+    ref[:batch] = O.bf16_bits(O.bf16_to_f32(x0[:batch]) + O.bf16_to_f32(O.bf16_bits(s.T[:batch].copy())))
+    np.testing.assert_array_equal(x.cpu().numpy().view(np.uint16), ref)
+    # SwiGLU over gate | up halves
+    inter = rows // 2
+    h = torch.zeros((n_pad, inter), dtype=torch.int16, device=dev)
+    bridge.dispatch_batch_swiglu(part, h, ksplit=ksplit, intermediate=inter, n_pad=n_pad, batch=batch, stream_ptr=0)
+    g = O.bf16_to_f32(O.bf16_bits(s[:inter].T[:batch].copy()))
+    u = O.bf16_to_f32(O.bf16_bits(s[inter:2 * inter].T[:batch].copy()))
+    act = O.bf16_to_f32(O.bf16_bits((g / (np.float32(1) + np.exp(-g))).astype(np.float32)))
+    href = O.bf16_bits((act * u).astype(np.float32))
+    got = h.cpu().numpy().view(np.uint16)
+    diff = np.abs(got[:batch].astype(np.int32) - href.astype(np.int32))
+    assert diff.max() <= 1 and np.count_nonzero(diff) <= max(1, diff.size // 1000)
+    assert not got[batch:].any()
+    # RMSNorm, one CTA per sequence
+    hidden = 2048 if rows >= 2048 else 256
+    xr = O.bf16_bits(rng.normal(0, 1, (batch, hidden)).astype(np.float32))
+    wr = O.bf16_bits(rng.normal(1, 0.1, hidden).astype(np.float32))
+    out = torch.zeros((batch, hidden), dtype=torch.int16, device=dev)
+    bridge.dispatch_batch_rmsnorm(torch.from_numpy(xr.view(np.int16)).to(dev), torch.from_numpy(wr.view(np.int16)).to(dev),
+                                  out, batch=batch, hidden=hidden, epsilon=1e-6, stream_ptr=0)
+    got = out.cpu().numpy().view(np.uint16)
+    for b in range(batch):
+        xf = O.bf16_to_f32(xr[b])
+        ss = np.float32((xf.astype(np.float64) ** 2).sum())
+        inv = np.float32(1) / np.sqrt(ss / np.float32(hidden) + np.float32(1e-6))
+        hn = O.bf16_to_f32(O.bf16_bits((xf * inv).astype(np.float32)))
+        exact = O.bf16_bits((O.bf16_to_f32(wr) * hn).astype(np.float32))
+        d = np.abs(got[b].astype(np.int32) - exact.astype(np.int32))
+        assert d.max() <= 2 and np.count_nonzero(d) <= hidden // 100
+        d = np.abs(got[b].astype(np.int32) - O.rmsnorm_hf_bf16(xr[b].copy(), wr, 1e-6).astype(np.int32))
+        assert d.max() <= 2 and np.count_nonzero(d) <= 3 * hidden // 100
+    # partials off a 16-byte boundary are refused, not read
+    with pytest.raises(NativeCudaError):
+        bridge.dispatch_batch_residual(part.view(-1)[1:], x, ksplit=1, rows=rows, n_pad=n_pad, batch=batch,
+                                       stream_ptr=0)
+    assert bridge.error_word(clear=True) == 0
+
+
 def test_batched_untied_nf4_lm_head_against_oracle(bridge):
     """An untied NF4 lm_head (the Llama form) goes through the vocabulary-
     parallel pieces (argmax pairs + select) even on one rank; each sequence's
