@@ -136,10 +136,6 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
     return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
            (2ull << 61);
 }
-// byte offset of 16-byte chunk c (0..7) of row r in a 128-byte-swizzled K-major tile
-__device__ __forceinline__ uint32_t sw128_chunk(int r, int c) {
-    return static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
-}
 // ---- the tensor-core GEMM
 // One CTA = one 128-row tile x one split of K, ten warps:
 //   warp 0   TMA producer: per 64-element K block, the weight tile (NF4 codes
