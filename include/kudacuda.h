@@ -348,7 +348,9 @@ KUDACUDA_API int kudacuda_sm100_decode_layers_persistent(void* handle, uint64_t 
  *   accumulator in TMEM).  weight_type 0: NF4 packed [rows][k/2] + fp32 absmax
  *   [rows][k/64]; 1: bf16 [rows][k] (absmax unused); 2: NF4 re-tiled by
  *   batch_retile (absmax unused, the fastest NF4 form).  ksplit in [1, k/64];
- *   batch_gemm_ksplit suggests one.  Several matrices may share one partials
+ *   batch_gemm_ksplit suggests one (the smallest split whose last wave of CTAs,
+ *   two per SM, is well filled; at least 4 K blocks per CTA).  Several
+ *   matrices may share one partials
  *   buffer through row_offset.
  * The epilogues sum the splits in split order (deterministic); their
  * partials pointer is 16-byte aligned, as batch_gemm requires of its own:
