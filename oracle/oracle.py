@@ -84,7 +84,10 @@ def bf16_to_f32(b: np.ndarray) -> np.ndarray:
 
 
 def f16_bits(x: np.ndarray) -> np.ndarray:
-    return np.asarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
+    """fp32 -> f16 bit patterns, round to nearest even; beyond the f16 range -> inf (IEEE, as torch)."""
+
+    with np.errstate(over="ignore"):
+        return np.asarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
 
 
 def f16_to_f32(b: np.ndarray) -> np.ndarray:
