@@ -46,6 +46,9 @@ KV_BUCKET = 512
 SEED = 20260824
 METRIC = "batch-1 decode tok/s"
 UNIT = "tok/s"
+# arithmetic of the batch-1 GEMVs: NF4 levels and the bf16-valued activations
+# are staged as f16 for the mma (exact products into f32), absmax applied in f32
+DTYPE_BATCH1 = "nf4-weights(f16 levels)/bf16-activations staged as f16/f32-accumulate"
 
 
 def _peaks() -> tuple[float, str]:
@@ -227,7 +230,7 @@ def run_gpu(args) -> dict | None:
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "nf4-weights/bf16-activations/f32-accumulate",
+            "dtype": DTYPE_BATCH1,
             "data": "synthetic (random-init weights N(0,0.02) NF4-quantised on device; uniform-random prompt)",
             "config": {
                 "workload": "config3: Qwen2.5-3B-architecture NF4 decode, batch 1, static CUDA graph, KV bucket 512",
@@ -501,7 +504,7 @@ def run_reference(args) -> dict | None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "nf4-weights/bf16-activations/f32-accumulate",
+        "dtype": DTYPE_BATCH1,
         "data": "synthetic",
         "config": {"workload": "config3: Qwen2.5-3B-architecture NF4 decode, batch 1", "global_batch": 1},
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": O.num_threads(), "kind": "port",
@@ -601,7 +604,7 @@ def run_tp(args) -> dict | None:
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
-            "dtype": "nf4-weights/bf16-activations/f32-accumulate",
+            "dtype": DTYPE_BATCH1,
             "data": "synthetic (random-init weights N(0,0.02) NF4-quantised on device; uniform-random prompt)",
             "config": {
                 "workload": "config5: Llama-3-8B-architecture NF4 decode, batch 1, tensor-parallel, static CUDA graph",

@@ -276,8 +276,10 @@ KUDACUDA_API int kudacuda_sm100_select_token(void* handle, uint64_t pairs, int64
  * batch * kv_heads <= 1024; larger requests fail with a message).  The first
  * call on each device looks the array up and zeroes its tickets, so it must
  * come before any stream capture on that device.  Calls that overlap in time
- * share the array and race: serialise them.  It allocates nothing and does
- * not synchronise. */
+ * share the array and race: serialise them.  An overlap can also leave the
+ * shared tickets nonzero, and then every later call on that device combines
+ * at the wrong time (wrong results) until the library is unloaded.  It
+ * allocates nothing and does not synchronise. */
 KUDACUDA_API int kudacuda_sm100_gqa_decode_static(void* handle, uint64_t query, uint64_t key_cache,
                                                   uint64_t value_cache, uint64_t output, uint64_t kv_len_device,
                                                   int dtype, int64_t batch_size, int64_t kv_len, int64_t kv_stride,

@@ -279,6 +279,21 @@ struct ConsumerState {
     bool failed;  // a ring wait ran out: no further waits or refills this step
 };
 
+// After a ring wait ran out: every slot of this warp's ring may still have a
+// bulk copy in flight (one each, issued before the failure; none is issued
+// after it).  Lane 0 waits for them, bounded, in ring order from the slot that
+// failed, so no copy still writes into shared memory once the CTA has exited.
+__device__ __noinline__ void ring_drain(uint64_t* bars, int ring_slots, int slot, uint32_t parity) {
+    for (int i = 0; i < ring_slots; ++i) {
+        for (int retry = 0; retry < 4 && !mbar_wait_bounded(&bars[slot], parity); ++retry) {
+        }
+        if (++slot == ring_slots) {
+            slot = 0;
+            parity ^= 1u;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ one GEMV op of one layer
 // xs holds the f16 input vector.  Every warp consumes its chunk range from its
 // ring, refilling each slot from the producer cursor as soon as it is read;
@@ -304,7 +319,9 @@ __device__ void gemv_op(const PersistArgs& a, int layer, const uint8_t* lut, uin
             if (lane == 0) {
                 atomicExch(a.misc, 1u);
                 atomicOr(a.err, 16);
+                ring_drain(bars, a.ring_slots, cs.slot, cs.parity);
             }
+            __syncwarp();
         }
         const uint8_t* st = ring + cs.slot * kChunkBytes;
         if (g == 0) {  // only batch column 0 of B matters: lanes 0..3 carry x

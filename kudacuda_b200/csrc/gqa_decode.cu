@@ -188,12 +188,15 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a)
         mbar_arrive_expect_tx(&kv_bar[1], bytes);
         bulk_g2s(const_cast<uint16_t*>(vs), static_cast<const uint16_t*>(a.vcache) + row0, bytes, &kv_bar[1]);
     }
-    // A wait that runs out records bit 16, waits once more (bounded) for the
-    // copy still in flight, and leaves the chunk empty.
+    // A wait that runs out records bit 16, waits again (bounded, a few times)
+    // for the copy still in flight, and leaves the chunk empty.
+    // The retries give a late copy time to land before the CTA can exit, so
+    // no bulk copy still writes into this CTA's shared memory after it ends.
     auto wait_rows = [&](uint64_t* bar) {
         if (n == 0 || mbar_wait_bounded(bar, 0)) return;
         if (a.err != nullptr) atomicOr(a.err, 16);
-        mbar_wait_bounded(bar, 0);
+        for (int retry = 0; retry < 8 && !mbar_wait_bounded(bar, 0); ++retry) {
+        }
         n = 0;
     };
 
@@ -310,9 +313,13 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_split_kernel(const GqaArgs a)
 //     level accuracy while V stays in its storage type; V fragments come from
 //     ldmatrix.trans of the padded rows;
 //   * each CTA writes (max, sum, acc) into the cluster leader's (rank 0)
-//     shared memory and arrives on the leader's mbarrier; the leader combines
-//     and stores.  Only the leader's shared memory is read remotely, and it
-//     leaves last.
+//     shared memory, then every CTA of the cluster meets at a closing cluster
+//     barrier (arrive.release / wait.acquire); after it the leader combines
+//     and stores.  Only the leader's shared memory is written remotely, and
+//     no CTA leaves before every remote store into it has completed: the
+//     leader cannot exit while a peer still writes into its shared memory.
+//     Every CTA reaches the closing barrier (no data-dependent wait precedes
+//     it), so it needs no time limit.
 constexpr int kGqaClusterThreads = 512;
 constexpr int kGqaClusterWarps = kGqaClusterThreads / 32;
 constexpr int kGqaMaxCluster = 8;
@@ -361,30 +368,11 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
     return r;
 }
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
 template <int DT, int G>
 __global__ void __launch_bounds__(kGqaClusterThreads) gqa_cluster_kernel(const GqaArgs a) {
     __shared__ __align__(16) float s_s[2][8][kGqaMaxChunk];  // score halves (dims 0-63, 64-127); then P in [0]
     __shared__ __align__(8) float gat_ml[kGqaMaxCluster][G][2];  // leader: gathered (max, sum)
     __shared__ float ml_s[G][2];
-    __shared__ __align__(8) uint64_t gat_bar;  // leader: one arrival per CTA of the cluster
     extern __shared__ __align__(16) uint8_t kv_rows[];
 
     const int tid = threadIdx.x;
@@ -393,12 +381,8 @@ __global__ void __launch_bounds__(kGqaClusterThreads) gqa_cluster_kernel(const G
     const int g = lane >> 2, t = lane & 3;
     const int S = a.nsplit;
     const int split = blockIdx.y;  // == rank in the cluster
-    if (tid == 0) {
-        mbar_init(&gat_bar, S);
-        fence_mbar_init();
-    }
-    // announce this CTA (its barrier is initialised) to the cluster; the
-    // matching wait comes right before the first remote access
+    // announce this CTA (it has started, so its shared memory exists) to the
+    // cluster; the matching wait comes right before the first remote access
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     pdl_launch_dependents();
     pdl_wait_on_producer();
@@ -564,20 +548,13 @@ __global__ void __launch_bounds__(kGqaClusterThreads) gqa_cluster_kernel(const G
         asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(dst), "f"(ml_s[tid][0]), "f"(ml_s[tid][1])
                      : "memory");
     }
-    __syncthreads();
-    if (tid == 0) mbar_arrive_remote(mapa_shared(smem_u32(&gat_bar), 0));
-    if (split != 0) return;  // only the leader's shared memory is read remotely
+    // closing rendezvous: the release orders this CTA's remote stores before
+    // its arrival, the acquire makes every peer's stores visible to the leader
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (split != 0) return;
 
     // ---- leader: combine the S partials (loops unrolled over the cluster bound)
-    bool ok = true;
-    {
-        uint32_t i = 0;
-        for (; i < kMbarPollLimit; ++i)
-            if (mbar_try_wait_cluster(&gat_bar, 0)) break;
-        ok = i < kMbarPollLimit;
-        if (!ok && tid == 0 && a.err != nullptr) atomicOr(a.err, 16);
-    }
-    if (!ok) return;
     for (int u = tid; u < G * kHeadDim; u += kGqaClusterThreads) {
         const int h = u / kHeadDim, d = u - h * kHeadDim;
         float mr[kGqaMaxCluster], lr[kGqaMaxCluster], ar[kGqaMaxCluster];
@@ -744,7 +721,9 @@ namespace {
 // capture on it).
 cudaError_t static_gqa_scratch(cudaStream_t s, float** partials, int** tickets) {
     static std::atomic<float*> cached[64];
-    const int dev = current_device_index();
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;  // one cached address per device ordinal 0..63
     float* base = cached[dev].load(std::memory_order_acquire);
     if (base == nullptr) {
         void* p = nullptr;
@@ -761,13 +740,19 @@ cudaError_t static_gqa_scratch(cudaStream_t s, float** partials, int** tickets) 
 }
 }  // namespace
 
+bool gqa_static_fits(int batch, int q_heads, int kv_heads, int extent) {
+    if (batch <= 0 || kv_heads <= 0 || q_heads <= 0 || extent <= 0) return false;
+    if (static_cast<int64_t>(batch) * kv_heads > kStaticGqaTickets) return false;
+    int chunk = 0, nsplit = 0;
+    gqa_plan_splits(extent, batch, kv_heads, 0, &chunk, &nsplit);
+    return gqa_partials_floats(batch, q_heads, nsplit, kHeadDim) <= kStaticGqaPartialFloats;
+}
+
 cudaError_t gqa_decode_static_scratch(GqaArgs a, int dt, cudaStream_t s) {
     if (a.batch <= 0 || a.kv_heads <= 0 || a.q_heads <= 0 || a.stride <= 0) return cudaErrorInvalidValue;
     const int extent = a.kv_len_dev != nullptr ? a.stride : a.kv_len;
+    if (!gqa_static_fits(a.batch, a.q_heads, a.kv_heads, extent)) return cudaErrorInvalidValue;
     gqa_plan_splits(extent, a.batch, a.kv_heads, 0, &a.chunk, &a.nsplit);
-    if (gqa_partials_floats(a.batch, a.q_heads, a.nsplit, kHeadDim) > kStaticGqaPartialFloats ||
-        static_cast<int64_t>(a.batch) * a.kv_heads > kStaticGqaTickets)
-        return cudaErrorInvalidValue;
     cudaError_t st = static_gqa_scratch(s, &a.partials, &a.counters);
     if (st != cudaSuccess) return st;
     a.split_only = 1;

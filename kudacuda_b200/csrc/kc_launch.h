@@ -115,6 +115,8 @@ cudaError_t gqa_decode(GqaArgs a, int dt, cudaStream_t s);
 // ignored.  Plans its own splits; fails with cudaErrorInvalidValue when the
 // partials or tickets would not fit.
 cudaError_t gqa_decode_static_scratch(GqaArgs a, int dt, cudaStream_t s);
+// true when a static-scratch call of these sizes fits the fixed array
+bool gqa_static_fits(int batch, int q_heads, int kv_heads, int extent);
 size_t gqa_partials_floats(int batch, int q_heads, int nsplit, int head_dim);
 
 // ---- tensor-parallel step ops (tp_ops.cu) ---------------------------------------

@@ -24,6 +24,10 @@ namespace {
 // at most 128 splits (chunks of 64..256 tokens cover up to 32768 tokens).
 constexpr int kRefGqaMaxSplits = 128;
 constexpr int kRefGqaHeads = 16;
+// size bounds of the sm100 GQA entries, checked before any int arithmetic:
+// batch * heads products stay far inside int
+constexpr int64_t kMaxGqaBatch = 65536;
+constexpr int64_t kMaxGqaHeads = 1024;
 
 struct Handle {
     explicit Handle(int dev) : device_id(dev) {}
@@ -657,7 +661,9 @@ int kudacuda_sm100_swiglu_nf4_bf16(void* raw, uint64_t input, uint64_t norm_weig
 
 int64_t kudacuda_sm100_gqa_workspace_bytes(int64_t batch_size, int64_t query_heads, int64_t kv_heads,
                                            int64_t kv_extent, int64_t head_dim) {
-    if (batch_size < 1 || query_heads < 1 || kv_heads < 1 || kv_extent < 1 || head_dim < 1) return -1;
+    if (batch_size < 1 || batch_size > kc::kMaxGqaBatch || query_heads < 1 || query_heads > kc::kMaxGqaHeads || kv_heads < 1 ||
+        kv_heads > query_heads || kv_extent < 1 || kv_extent > (1 << 20) || head_dim < 1 || head_dim > 1024)
+        return -1;
     int chunk = 0, nsplit = 0;
     kc::gqa_plan_splits(static_cast<int>(kv_extent), static_cast<int>(batch_size), static_cast<int>(kv_heads), 0,
                         &chunk, &nsplit);
@@ -676,12 +682,13 @@ int kudacuda_sm100_gqa_decode(void* raw, uint64_t query, uint64_t key_cache, uin
         return 1;
     }
     const int64_t group = kv_heads > 0 ? query_heads / kv_heads : 0;
-    if (batch_size < 1 || kv_heads < 1 || query_heads % kv_heads != 0 ||
+    if (batch_size < 1 || batch_size > kc::kMaxGqaBatch || kv_heads < 1 || query_heads > kc::kMaxGqaHeads ||
+        query_heads % kv_heads != 0 ||
         !(group == 1 || group == 2 || group == 4 || group == 8) || head_dim != 128 || kv_stride < 1 ||
         kv_stride > (1 << 20) || (kv_len_device == 0 && (kv_len < 1 || kv_len > kv_stride)) || !(scale > 0.0F) ||
         (dtype != kc::kF16 && dtype != kc::kBF16)) {
         h->set_error("sm100_gqa_decode requires head_dim=128, query_heads/kv_heads in {1,2,4,8}, 1<=kv_len<=kv_stride, "
-                     "positive scale, dtype f16 or bf16");
+                     "positive scale, dtype f16 or bf16, batch_size<=65536, query_heads<=1024");
         return 1;
     }
     kc::GqaArgs a;
@@ -722,12 +729,13 @@ int kudacuda_sm100_gqa_decode_static(void* raw, uint64_t query, uint64_t key_cac
         return 1;
     }
     const int64_t group = kv_heads > 0 ? query_heads / kv_heads : 0;
-    if (batch_size < 1 || kv_heads < 1 || query_heads % kv_heads != 0 ||
+    if (batch_size < 1 || batch_size > kc::kMaxGqaBatch || kv_heads < 1 || query_heads > kc::kMaxGqaHeads ||
+        query_heads % kv_heads != 0 ||
         !(group == 1 || group == 2 || group == 4 || group == 8) || head_dim != 128 || kv_stride < 1 ||
         kv_stride > (1 << 20) || (kv_len_device == 0 && (kv_len < 1 || kv_len > kv_stride)) || !(scale > 0.0F) ||
         (dtype != kc::kF16 && dtype != kc::kBF16)) {
         h->set_error("sm100_gqa_decode_static requires head_dim=128, query_heads/kv_heads in {1,2,4,8}, "
-                     "1<=kv_len<=kv_stride, positive scale, dtype f16 or bf16");
+                     "1<=kv_len<=kv_stride, positive scale, dtype f16 or bf16, batch_size<=65536, query_heads<=1024");
         return 1;
     }
     kc::GqaArgs a;
@@ -745,13 +753,12 @@ int kudacuda_sm100_gqa_decode_static(void* raw, uint64_t query, uint64_t key_cac
     a.head_dim = 128;
     a.scale = scale;
     a.err = h->err_word;
-    const cudaError_t st = kc::gqa_decode_static_scratch(a, dtype, S(stream));
-    if (st == cudaErrorInvalidValue) {
+    if (!kc::gqa_static_fits(a.batch, a.q_heads, a.kv_heads, a.kv_len_dev != nullptr ? a.stride : a.kv_len)) {
         h->set_error("sm100_gqa_decode_static: partials or tickets exceed the fixed scratch (1 MiB of partials, "
                      "1024 tickets); use kudacuda_sm100_gqa_decode with a caller workspace");
         return 1;
     }
-    return finish(h, "gqa_split_kernel (static scratch)", st);
+    return finish(h, "gqa_split_kernel (static scratch)", kc::gqa_decode_static_scratch(a, dtype, S(stream)));
 }
 
 int kudacuda_sm100_rmsnorm_nf4_gemv(void* raw, uint64_t input, uint64_t norm_weight, uint64_t weight_packed,
@@ -1410,7 +1417,9 @@ void batch_gqa_plan(int64_t batch, int64_t kv_heads, int64_t stride, int* chunk,
 
 int64_t kudacuda_sm100_gqa_batch_workspace_bytes(int64_t batch_size, int64_t query_heads, int64_t kv_heads,
                                                  int64_t kv_stride) {
-    if (batch_size < 1 || query_heads < 1 || kv_heads < 1 || kv_stride < 1 || kv_stride > (1 << 20)) return -1;
+    if (batch_size < 1 || batch_size > 4096 || query_heads < 1 || query_heads > kc::kMaxGqaHeads || kv_heads < 1 ||
+        kv_heads > query_heads || kv_stride < 1 || kv_stride > (1 << 20))
+        return -1;
     int chunk = 0, nsplit = 0;
     batch_gqa_plan(batch_size, kv_heads, kv_stride, &chunk, &nsplit);
     return static_cast<int64_t>(kc::gqa_partials_floats(static_cast<int>(batch_size), static_cast<int>(query_heads),
@@ -1430,7 +1439,8 @@ int kudacuda_sm100_gqa_decode_batch(void* raw, uint64_t query, uint64_t key_cach
         return 1;
     }
     const int64_t group = kv_heads > 0 ? query_heads / kv_heads : 0;
-    if (batch_size < 1 || batch_size > 4096 || kv_heads < 1 || query_heads % kv_heads != 0 ||
+    if (batch_size < 1 || batch_size > 4096 || kv_heads < 1 || query_heads > kc::kMaxGqaHeads ||
+        query_heads % kv_heads != 0 ||
         !(group == 1 || group == 2 || group == 4 || group == 8) || head_dim != 128 || kv_stride < 1 ||
         kv_stride > (1 << 20) || !(scale > 0.0F)) {
         h->set_error("sm100_gqa_decode_batch requires head_dim=128, query_heads/kv_heads in {1,2,4,8}, positive scale");

@@ -2,7 +2,7 @@
 Python code (run in a container that has the reference checkout; the GPU box
 does not, so the outputs are committed).
 
-    python tests/golden/make_golden.py [--reference /path/to/KudaCuda]
+    python tests/golden/make_golden.py --reference /path/to/KudaCuda   (or KUDACUDA_REFERENCE=...)
 
 Sources imported from the reference:
   harness/reference.py:9-31                        rmsnorm_reference (float64)
@@ -39,9 +39,12 @@ def import_reference(ref: Path):
 
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference", type=Path, default=Path(os.environ.get("KUDACUDA_REFERENCE", "/root/reference")))
+    parser.add_argument("--reference", type=Path, default=os.environ.get("KUDACUDA_REFERENCE"),
+                        help="path of the reference checkout (or set KUDACUDA_REFERENCE)")
     args = parser.parse_args()
-    rmsnorm_reference, compare_values, reference_qwen2_gqa = import_reference(args.reference)
+    if args.reference is None:
+        parser.error("give --reference PATH or set KUDACUDA_REFERENCE")
+    rmsnorm_reference, compare_values, reference_qwen2_gqa = import_reference(Path(args.reference))
     import torch
 
     g = np.random.default_rng(SEED)

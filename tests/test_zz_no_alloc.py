@@ -80,6 +80,49 @@ def test_static_scratch_gqa_matches_workspace_entry(kc_lib, kc_handle, oracle_mo
     assert int(_host(tickets).sum()) == 0
 
 
+def test_static_scratch_gqa_device_length_and_batch(kc_lib, kc_handle, oracle_mod):
+    """kv_len_device given (the extent is the stride) and batch 2 (one ticket
+    per (sequence, KV head)): two calls in a row, each against the workspace
+    entry (same split plan: bit-identical) and the oracle per sequence."""
+
+    import torch
+
+    O = oracle_mod
+    g = F.rng(4242)
+    q_heads, kv_heads, d, batch, stride = 16, 2, 128, 2, 2304
+    kc = F.bf16_normal(g, batch * kv_heads * stride * d)
+    vc = F.bf16_normal(g, batch * kv_heads * stride * d)
+    dk, dv = _dev(kc), _dev(vc)
+    scale = 1.0 / math.sqrt(d)
+    nbytes = kc_lib.kudacuda_sm100_gqa_workspace_bytes(batch, q_heads, kv_heads, stride, d)
+    ws = _dev(np.zeros(nbytes // 4, dtype=np.float32))
+    tickets = _dev(np.zeros(batch * kv_heads, dtype=np.int32))
+    for call, kv_len in enumerate((2200, 1501)):
+        dlen = _dev(np.array([kv_len], dtype=np.int32))
+        q = F.bf16_normal(g, batch * q_heads * d)
+        dq = _dev(q)
+        out_static = _dev(np.zeros(batch * q_heads * d, dtype=np.uint16))
+        out_ws = _dev(np.zeros(batch * q_heads * d, dtype=np.uint16))
+        _ok(kc_lib, kc_handle, kc_lib.kudacuda_sm100_gqa_decode_static(
+            kc_handle, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), out_static.data_ptr(), dlen.data_ptr(), O.BF16,
+            batch, 0, stride, q_heads, kv_heads, d, scale, _stream()))
+        # the workspace entry with split-KV forced: the same plan over the stride
+        _ok(kc_lib, kc_handle, kc_lib.kudacuda_sm100_gqa_decode(
+            kc_handle, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), out_ws.data_ptr(), ws.data_ptr(), nbytes,
+            tickets.data_ptr(), dlen.data_ptr(), O.BF16, batch, 0, stride, q_heads, kv_heads, d, scale, _stream()))
+        got_static, got_ws = _host(out_static), _host(out_ws)
+        assert np.array_equal(got_static, got_ws), f"call {call}: static scratch differs from workspace entry"
+        qs = q.reshape(batch, q_heads * d)
+        kcs = kc.reshape(batch, kv_heads * stride * d)
+        vcs = vc.reshape(batch, kv_heads * stride * d)
+        for b in range(batch):
+            ref = O.gqa_decode(qs[b], kcs[b], vcs[b], O.BF16, q_heads, kv_heads, d, kv_len, stride, scale)
+            got = O.bf16_to_f32(got_static.reshape(batch, -1)[b])
+            np.testing.assert_allclose(got, O.bf16_to_f32(ref), atol=GQA_TOL, rtol=GQA_TOL)
+    torch.cuda.synchronize()
+    assert int(_host(tickets).sum()) == 0
+
+
 def test_static_scratch_gqa_rejects_oversized_requests(kc_lib, kc_handle, oracle_mod):
     # 64 query heads x 8 kv heads x batch 8 needs more partials than the fixed 1 MiB array holds
     O = oracle_mod
