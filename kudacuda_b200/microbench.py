@@ -15,6 +15,10 @@ KV rows for attention).
       the persistent all-layers kernel alone (Qwen2.5-3B layer shapes, random
       NF4 weights), launched directly on its stream at position kv - 1
 
+    python -m kudacuda_b200.microbench --op refcompare [--launches 36 --reps 20]
+      the reference's own kernels (oracle/_ref, built for sm_100a from its
+      sources) against this library's through the same reference ABI entries
+
     python -m kudacuda_b200.microbench --op prefill --prompt 512
       time to first token: batched prefill (64-token chunks on the tensor
       cores) against the decode-loop prefill, full Qwen2.5-3B architecture
@@ -280,6 +284,143 @@ def time_prefill(torch, prompt_len: int, device: str) -> dict:
     return out
 
 
+def time_refcompare(torch, device: str, launches: int, reps: int) -> list[dict]:
+    """The reference's own kernels (oracle/_ref/libkudacuda_ref.so, compiled
+    for sm_100a from its sources) against this library's, through the same
+    reference ABI entries on the same inputs: fused RMSNorm + NF4 QKV (v1,
+    v3), NF4 SwiGLU (f16, bf16), GQA decode (direct at kv 512 / 1024 / 2048,
+    graph and workspace_v3 at capacity 512).  Each library's calls are
+    captured ``launches`` times into one torch CUDA graph, cycling over enough
+    input copies that a replay reads more than the 126 MB L2; device time per
+    call from CUDA events around ``reps`` replays."""
+
+    import ctypes
+    from pathlib import Path
+
+    from . import native
+
+    ref_path = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libkudacuda_ref.so"
+    if not ref_path.exists():
+        raise FileNotFoundError(f"{ref_path} not built (make -C oracle ref REFERENCE=...)")
+    libs = {"reference": native.configure(ctypes.CDLL(str(ref_path))), "b200": native.load_library()}
+    handles = {}
+    for name, lib in libs.items():
+        h = lib.kudacuda_create(torch.device(device).index or 0)
+        assert h and lib.kudacuda_freeze(h) == 0, lib.kudacuda_last_error(h)
+        handles[name] = h
+    f16 = torch.float16
+    l2 = 160 << 20
+
+    def copies_for(nbytes: int) -> int:
+        return max(2, min(64, -(-l2 // max(nbytes, 1))))
+
+    def nf4(rows, k, n):
+        return [(torch.randint(0, 256, (rows * k // 2,), dtype=torch.uint8, device=device),
+                 torch.rand(rows * k // 64, device=device) * 0.05 + 0.01) for _ in range(n)]
+
+    cases = []
+    # fused RMSNorm + NF4 QKV (hidden 2048, q 2048, k/v 256)
+    qkv_bytes = (2560 * 2048) // 2 + (2560 * 2048) // 16 + 2 * 2048 * 2 + 2 * 2560 * 2
+    nq = copies_for(qkv_bytes)
+    Q, K, V = nf4(2048, 2048, nq), nf4(256, 2048, nq), nf4(256, 2048, nq)
+    x = torch.randn(2048, device=device).to(f16)
+    nw = (1 + 0.02 * torch.randn(2048, device=device)).to(f16)
+    bq, bk, bv = (torch.randn(n, device=device).mul(0.02).to(f16) for n in (2048, 256, 256))
+    qo, ko, vo = (torch.empty(n, dtype=f16, device=device) for n in (2048, 256, 256))
+    ws_norm = torch.empty(2048, dtype=torch.float32, device=device)
+    for variant in ("", "_v3"):
+        def f(lib, h, i, sp, variant=variant):
+            j = i % nq
+            args = [h, x.data_ptr(), nw.data_ptr(), Q[j][0].data_ptr(), Q[j][1].data_ptr(), bq.data_ptr(),
+                    K[j][0].data_ptr(), K[j][1].data_ptr(), bk.data_ptr(), V[j][0].data_ptr(), V[j][1].data_ptr(),
+                    bv.data_ptr()]
+            if variant:
+                args.append(ws_norm.data_ptr())
+            args += [qo.data_ptr(), ko.data_ptr(), vo.data_ptr(), 1, 2048, 2048, 256, 64, 1e-6, sp]
+            return getattr(lib, "kudacuda_qwen2_fused_rmsnorm_qkv_nf4" + variant)(*args)
+        cases.append((f"qkv_nf4{variant or '_v1'}", qkv_bytes, f))
+    # NF4 SwiGLU (hidden 2048, intermediate 11008)
+    sw_bytes = 2 * ((11008 * 2048) // 2 + (11008 * 2048) // 16) + 2 * 2048 * 2 + 11008 * 2
+    ns = copies_for(sw_bytes)
+    G, U = nf4(11008, 2048, ns), nf4(11008, 2048, ns)
+    h_out = torch.empty(11008, dtype=f16, device=device)
+    xb, nwb = x.to(torch.bfloat16), nw.to(torch.bfloat16)
+    for dt, sym, xi, ni in (("f16", "kudacuda_qwen2_swiglu_nf4", x, nw),
+                            ("bf16", "kudacuda_qwen2_swiglu_nf4_bf16", xb, nwb)):
+        def f(lib, h, i, sp, sym=sym, xi=xi, ni=ni):
+            j = i % ns
+            return getattr(lib, sym)(h, xi.data_ptr(), ni.data_ptr(), G[j][0].data_ptr(), G[j][1].data_ptr(),
+                                     U[j][0].data_ptr(), U[j][1].data_ptr(), h_out.data_ptr(), 1, 2048, 11008, 64,
+                                     1e-6, sp)
+        cases.append((f"swiglu_nf4_{dt}", sw_bytes, f))
+    # GQA decode (16 / 2 / 128 heads)
+    q = torch.randn(16 * 128, device=device).to(f16)
+    o = torch.empty(16 * 128, dtype=f16, device=device)
+    scale = 1.0 / math.sqrt(128)
+    for kv in (512, 1024, 2048):
+        nbytes = 2 * 2 * kv * 128 * 2 + 2 * 16 * 128 * 2
+        nk = copies_for(nbytes)
+        KC = [torch.randn(2 * kv * 128, device=device).to(f16) for _ in range(nk)]
+        VC = [torch.randn(2 * kv * 128, device=device).to(f16) for _ in range(nk)]
+
+        def f(lib, h, i, sp, KC=KC, VC=VC, kv=kv, nk=nk):
+            j = i % nk
+            return lib.kudacuda_qwen2_gqa_decode(h, q.data_ptr(), KC[j].data_ptr(), VC[j].data_ptr(), o.data_ptr(),
+                                                 1, 1, kv, 16, 2, 128, scale, sp)
+        cases.append((f"gqa_direct_kv{kv}", nbytes, f))
+        if kv == 512:
+            kvl = torch.tensor([kv], dtype=torch.int32, device=device)
+            wsg = torch.empty(16 * 8 * 130, dtype=torch.float32, device=device)
+
+            def fg(lib, h, i, sp, KC=KC, VC=VC, nk=nk, kvl=kvl):
+                j = i % nk
+                return lib.kudacuda_qwen2_gqa_decode_graph(h, q.data_ptr(), KC[j].data_ptr(), VC[j].data_ptr(),
+                                                           o.data_ptr(), 1, 1, 512, 16, 2, 128, scale,
+                                                           kvl.data_ptr(), sp)
+
+            def fw(lib, h, i, sp, KC=KC, VC=VC, nk=nk, kvl=kvl, wsg=wsg):
+                j = i % nk
+                return lib.kudacuda_qwen2_gqa_decode_workspace_v3(h, q.data_ptr(), KC[j].data_ptr(),
+                                                                  VC[j].data_ptr(), o.data_ptr(), wsg.data_ptr(),
+                                                                  kvl.data_ptr(), 1, 1, 512, 16, 2, 128, scale, sp)
+            cases.append(("gqa_graph_cap512", nbytes, fg))
+            cases.append(("gqa_workspace_v3_cap512", nbytes, fw))
+
+    results = []
+    stream = torch.cuda.Stream()
+    sp = int(stream.cuda_stream)
+    for name, nbytes, fn in cases:
+        row = {"op": name, "bytes": nbytes}
+        for lname, lib in libs.items():
+            h = handles[lname]
+            with torch.cuda.stream(stream):
+                for i in range(launches):
+                    assert fn(lib, h, i, sp) == 0, lib.kudacuda_last_error(h)
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for i in range(launches):
+                    fn(lib, h, i, sp)
+            graph.replay()
+            stream.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e.record(stream)
+            e.synchronize()
+            us = s.elapsed_time(e) * 1e3 / (reps * launches)
+            row[f"{lname}_us"] = round(us, 3)
+            row[f"{lname}_gbs"] = round(nbytes / (us * 1e-6) / 1e9, 1)
+            del graph
+        row["speedup"] = round(row["reference_us"] / row["b200_us"], 2)
+        results.append(row)
+    torch.cuda.synchronize()
+    for lname, lib in libs.items():
+        lib.kudacuda_destroy(handles[lname])
+    return results
+
+
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--op", default="all")
@@ -294,6 +435,10 @@ def main(argv=None) -> int:
     import torch
 
     torch.cuda.set_device(torch.device(args.device))
+    if args.op == "refcompare":
+        for r in time_refcompare(torch, args.device, args.launches, args.reps):
+            print(json.dumps(r), flush=True)
+        return 0
     if args.op == "prefill":
         r = time_prefill(torch, args.prompt, args.device)
         print(json.dumps(r), flush=True)
