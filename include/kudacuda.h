@@ -334,6 +334,30 @@ KUDACUDA_API int kudacuda_sm100_decode_layers_persistent(void* handle, uint64_t 
                                                          int64_t head_dim, int64_t intermediate,
                                                          int64_t kv_capacity, float eps, float scale,
                                                          uint64_t stream);
+/* Test hooks of the same kernel (no reference counterpart).  taps (0: off) is
+ * a device bf16 buffer of layers * decode_persistent_tap_elements(...) / layers
+ * elements per layer, taps_bytes its size; each layer's record receives
+ * xn = RMSNorm(x) [hidden], q, k, v after bias and RoPE [q_heads * head_dim,
+ * 2 x kv_heads * head_dim], the attention output [q_heads * head_dim],
+ * x1 = x + o_proj [hidden], RMSNorm(x1) [hidden], h = SwiGLU [intermediate]
+ * and x2 = x1 + down [hidden], in that order.  spin_limit (0: default)
+ * bounds the polls of every dependency wait; stall_counter (-1: off) makes
+ * the wait on one counter of layer 0 (0 qkv, 1 attention, 2 o_proj,
+ * 3 gate/up, 4 down) unreachable, so that wait runs out, sets bit 4 of the
+ * error word and ends the step early -- the bounded-wait path, exercised
+ * without a fault.  Everything else is decode_layers_persistent. */
+KUDACUDA_API int64_t kudacuda_sm100_decode_persistent_tap_elements(int64_t layers, int64_t hidden, int64_t q_heads,
+                                                                  int64_t kv_heads, int64_t head_dim,
+                                                                  int64_t intermediate);
+KUDACUDA_API int kudacuda_sm100_decode_layers_persistent_debug(void* handle, uint64_t layer_table, int64_t layers,
+                                                               uint64_t x, uint64_t state, uint64_t rope_cos,
+                                                               uint64_t rope_sin, int64_t max_pos, uint64_t scratch,
+                                                               int64_t scratch_bytes, int64_t hidden, int64_t q_heads,
+                                                               int64_t kv_heads, int64_t head_dim,
+                                                               int64_t intermediate, int64_t kv_capacity, float eps,
+                                                               float scale, uint64_t taps, int64_t taps_bytes,
+                                                               int64_t spin_limit, int64_t stall_counter,
+                                                               uint64_t stream);
 
 /* Batched decode: B independent sequences advance one token per step.  No
  * reference counterpart (the reference's projections and its GQA contract,

@@ -85,7 +85,40 @@ struct PersistArgs {
     int gslots, ring_slots;
     int groups[4], nbpt[4];
     int work_bytes, xs_bytes, bias_rows;
+    // debug / test hooks (all off in the production launch):
+    uint16_t* taps;       // nullptr, or bf16 [nlayers][tap_stride] intermediates (layout in tap_offsets)
+    int tap_stride;
+    uint32_t spin_limit;  // polls of one dependency wait before it gives up
+    int stall_counter;    // -1, or the counter (layer 0) whose wait target is made unreachable
 };
+
+// Offsets of the intermediates inside one layer's tap record (bf16 values):
+// xn = RMSNorm(x) [hidden], q, k, v after bias + RoPE [q_heads*hd, 2 x kv_heads*hd],
+// attention output [q_heads*hd], x1 = x + o_proj [hidden], xn2 [hidden],
+// h = SwiGLU [inter], x2 = x1 + down [hidden].
+struct TapOffsets {
+    int xn, q, k, v, att, x1, xn2, h, x2, stride;
+};
+__host__ __device__ inline TapOffsets tap_offsets(int hidden, int qh, int kvh, int hd, int inter) {
+    TapOffsets t;
+    t.xn = 0;
+    t.q = t.xn + hidden;
+    t.k = t.q + qh * hd;
+    t.v = t.k + kvh * hd;
+    t.att = t.v + kvh * hd;
+    t.x1 = t.att + qh * hd;
+    t.xn2 = t.x1 + hidden;
+    t.h = t.xn2 + hidden;
+    t.x2 = t.h + inter;
+    t.stride = t.x2 + hidden;
+    return t;
+}
+__device__ __forceinline__ uint16_t* layer_taps(const PersistArgs& a, int layer) {
+    return a.taps == nullptr ? nullptr : a.taps + static_cast<int64_t>(layer) * a.tap_stride;
+}
+__device__ __forceinline__ TapOffsets tap_offsets(const PersistArgs& a) {
+    return tap_offsets(a.hidden, a.qh, a.kvh, a.hd, a.inter);
+}
 
 // ------------------------------------------------------------------ small helpers
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
@@ -134,10 +167,11 @@ __device__ __forceinline__ uint4 ldcg_u4(const void* p) { return __ldcg(reinterp
 // the acquire).  A wait that runs out raises the abort flag and error bit 4.
 __device__ void cta_wait(const PersistArgs& a, const unsigned* ctr, unsigned target) {
     if (threadIdx.x == 0) {
+        if (a.stall_counter >= 0 && ctr == a.counters + a.stall_counter) ++target;  // test hook: never reached
         uint32_t n = 0;
         while (ld_acquire(ctr) < target) {
             if (ld_acquire(a.misc) != 0u) break;
-            if (++n > kSpinLimit) {
+            if (++n > a.spin_limit) {
                 atomicExch(a.misc, 1u);
                 atomicOr(a.err, 16);
                 break;
@@ -413,7 +447,8 @@ __device__ __forceinline__ void norm_prefetch(const PersistArgs& a, const uint16
         if (o < a.hidden / 8) wv[i] = __ldg(reinterpret_cast<const uint4*>(w + 8 * o));
     }
 }
-__device__ void stage_norm(const PersistArgs& a, const uint16_t* xres, const uint4* wv, uint16_t* xs, float* red) {
+__device__ void stage_norm(const PersistArgs& a, const uint16_t* xres, const uint4* wv, uint16_t* xs, float* red,
+                           uint16_t* tap) {
     const int tid = threadIdx.x;
     const int n8 = a.hidden / 8;
     float ss = 0.F;
@@ -446,6 +481,7 @@ __device__ void stage_norm(const PersistArgs& a, const uint16_t* xres, const uin
                     const float we = bf16_bits_to_f32(static_cast<uint16_t>(ww[j] >> (16 * hh)));
                     v[hh] = round_bf16(we * round_bf16(xe * inv));
                     overflow |= !(fabsf(v[hh]) <= 65504.F);
+                    if (tap != nullptr) tap[8 * o + 2 * j + hh] = f32_to_bf16_bits(v[hh]);
                 }
                 out[j] = static_cast<uint32_t>(f32_to_f16_bits(v[0])) |
                          (static_cast<uint32_t>(f32_to_f16_bits(v[1])) << 16);
@@ -458,7 +494,7 @@ __device__ void stage_norm(const PersistArgs& a, const uint16_t* xres, const uin
 
 // xs[j] = f16(h_j), h_j = bf16(bf16(silu(bf16 gate_j)) * bf16 up_j), from the
 // gate/up slots, for the h blocks this CTA's share of down reads
-__device__ void stage_swiglu(const PersistArgs& a, const int* rng, const uint8_t* nsl, uint16_t* xs) {
+__device__ void stage_swiglu(const PersistArgs& a, const int* rng, const uint8_t* nsl, uint16_t* xs, uint16_t* tap) {
     const BlockSet bs = op_blocks(a, rng, kPDn);
     bool overflow = false;
 #pragma unroll 2
@@ -478,6 +514,7 @@ __device__ void stage_swiglu(const PersistArgs& a, const int* rng, const uint8_t
             const float hv = round_bf16(act * u);
             overflow |= !(fabsf(hv) <= 65504.F);
             hb[k] = f32_to_f16_bits(hv);
+            if (tap != nullptr) tap[j + k] = f32_to_bf16_bits(hv);
         }
         *reinterpret_cast<uint2*>(xs + j) = make_uint2(hb[0] | (static_cast<uint32_t>(hb[1]) << 16),
                                                        hb[2] | (static_cast<uint32_t>(hb[3]) << 16));
@@ -544,6 +581,8 @@ __device__ void attention_split(const PersistArgs& a, int layer, const uint64_t*
     const AttSmem sm = att_smem(a, work);
     const int qg = a.qh * (hd / 64), kg = a.kvh * (hd / 64);
     const bool bias = a.bias_rows > 0;
+    uint16_t* tap = s == 0 ? layer_taps(a, layer) : nullptr;
+    const TapOffsets to = tap_offsets(a);
 
     // q (gq heads) and k_new: four RoPE pairs (i .. i+3, i+half .. i+half+3) per thread;
     // v_new: four plain rows per thread
@@ -578,6 +617,11 @@ __device__ void attention_split(const PersistArgs& a, int layer, const uint64_t*
                     sm.knew[i + k] = lo;
                     sm.knew[i + k + half] = hi;
                 }
+                if (tap != nullptr) {
+                    uint16_t* t = tap + (isq ? to.q : to.k) + head * hd + i + k;
+                    t[0] = f32_to_bf16_bits(lo);
+                    t[half] = f32_to_bf16_bits(hi);
+                }
             }
         } else {
             const int d = 4 * (idx - nq4), v0 = hk * hd + d;  // row within the v matrix
@@ -588,6 +632,7 @@ __device__ void attention_split(const PersistArgs& a, int layer, const uint64_t*
                 float y = round_bf16(ys[k]);
                 if (bias) y = round_bf16(y + bf16_bits_to_f32(bias_s[(a.qh + a.kvh) * hd + v0 + k]));
                 sm.vnew[d + k] = y;
+                if (tap != nullptr) tap[to.v + v0 + k] = f32_to_bf16_bits(y);
             }
         }
     }
@@ -726,7 +771,7 @@ __device__ __forceinline__ void merge_att(float& M, float& den, float4& num, flo
     num.w = num.w * c1 + n2.w * c2;
     M = Mn;
 }
-__device__ void stage_attention(const PersistArgs& a, const int* rng, const AttPlan& ap, uint16_t* xs) {
+__device__ void stage_attention(const PersistArgs& a, const int* rng, const AttPlan& ap, uint16_t* xs, uint16_t* tap) {
     const BlockSet bs = op_blocks(a, rng, kPO);
     const int gq = a.qh / a.kvh, hd = a.hd, rec = hd + 4;
     bool overflow = false;
@@ -784,6 +829,7 @@ __device__ void stage_attention(const PersistArgs& a, const int* rng, const AttP
             for (int k = 0; k < 4; ++k) {
                 overflow |= !(fabsf(o4[k]) <= 65504.F);
                 hb[k] = f32_to_f16_bits(o4[k]);
+                if (tap != nullptr) tap[i + k] = f32_to_bf16_bits(o4[k]);
             }
             *reinterpret_cast<uint2*>(xs + i) = make_uint2(hb[0] | (static_cast<uint32_t>(hb[1]) << 16),
                                                            hb[2] | (static_cast<uint32_t>(hb[3]) << 16));
@@ -885,12 +931,17 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_layers_kernel(const Persi
             }
         }
         for (int i = tid; i < kPartGroups * kPWarps * 64; i += kPThreads) part[i] = 0.F;
+        uint16_t* tap = layer_taps(a, l);
+        const TapOffsets to = tap_offsets(a);
+        const bool tap0 = tap != nullptr && blockIdx.x == 0;
         if (l > 0) {
             cta_wait(a, a.counters + (l - 1) * kCounterStride + kCDn, G);
             residual_from_slots(a, nsl, kPDn, xres);
         }
         __syncthreads();
-        stage_norm(a, xres, wv, xs, red);
+        if (l > 0 && tap0)
+            for (int i = tid; i < a.hidden; i += kPThreads) layer_taps(a, l - 1)[to.x2 + i] = xres[i];
+        stage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn : nullptr);
         __syncthreads();
         gemv_op<kPQkv>(a, l, lut, ring, bars, ps, cs, xs, part);
         // ---- attention
@@ -919,7 +970,7 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_layers_kernel(const Persi
         // ---- o_proj (its input: every split of every head)
         norm_prefetch(a, reinterpret_cast<const uint16_t*>(L[kLPostNorm]), wv);
         cta_wait(a, ctr + kCAtt, static_cast<unsigned>(a.kvh * ap.ns));
-        stage_attention(a, rng, ap, xs);
+        stage_attention(a, rng, ap, xs, tap != nullptr ? tap + to.att : nullptr);
         __syncthreads();
         for (int i = tid; i < kPartGroups * kPWarps * 64; i += kPThreads) part[i] = 0.F;
         __syncthreads();
@@ -929,13 +980,15 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_layers_kernel(const Persi
         cta_wait(a, ctr + kCO, G);
         residual_from_slots(a, nsl, kPO, xres);
         __syncthreads();
-        stage_norm(a, xres, wv, xs, red);
+        if (tap0)
+            for (int i = tid; i < a.hidden; i += kPThreads) tap[to.x1 + i] = xres[i];
+        stage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn2 : nullptr);
         __syncthreads();
         gemv_op<kPGu>(a, l, lut, ring, bars, ps, cs, xs, part);
         // ---- SwiGLU + down
         for (int i = tid; i < kPartGroups * kPWarps * 64; i += kPThreads) part[i] = 0.F;
         cta_wait(a, ctr + kCGu, G);
-        stage_swiglu(a, rng, nsl, xs);
+        stage_swiglu(a, rng, nsl, xs, tap != nullptr ? tap + to.h : nullptr);
         __syncthreads();
         gemv_op<kPDn>(a, l, lut, ring, bars, ps, cs, xs, part);
     }
@@ -946,7 +999,12 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_layers_kernel(const Persi
         cta_wait(a, a.counters + (a.nlayers - 1) * kCounterStride + kCDn, gridDim.x);
         residual_from_slots(a, nsl, kPDn, xres);
         __syncthreads();
-        for (int i = tid; i < a.hidden; i += kPThreads) a.x[i] = xres[i];
+        uint16_t* last = layer_taps(a, a.nlayers - 1);
+        const int x2 = tap_offsets(a).x2;
+        for (int i = tid; i < a.hidden; i += kPThreads) {
+            a.x[i] = xres[i];
+            if (last != nullptr) last[x2 + i] = xres[i];
+        }
     }
     __syncthreads();
     if (tid == 0) {
@@ -1126,6 +1184,10 @@ PersistGeom persist_geom(const PersistDims& d, int sms) {
 
 int64_t decode_persistent_scratch_bytes(const PersistDims& d, int sms) { return persist_geom(d, sms).total; }
 
+int64_t decode_persistent_tap_stride(const PersistDims& d) {
+    return tap_offsets(d.hidden, d.q_heads, d.kv_heads, d.head_dim, d.intermediate).stride;
+}
+
 const char* decode_persistent_check(const PersistDims& d, int sms) {
     if (d.layers < 1 || d.hidden < 64 || d.hidden % 64 != 0 || d.head_dim != 128 || d.q_heads < 1 || d.kv_heads < 1 ||
         d.q_heads % d.kv_heads != 0 || d.q_heads / d.kv_heads > 8 || d.intermediate % 64 != 0 ||
@@ -1180,6 +1242,10 @@ cudaError_t decode_layers_persistent(const PersistLaunch& p, cudaStream_t stream
     a.work_bytes = g.work_bytes;
     a.xs_bytes = g.xs_bytes;
     a.bias_rows = g.bias_rows;
+    a.taps = p.taps;
+    a.tap_stride = tap_offsets(p.dims.hidden, p.dims.q_heads, p.dims.kv_heads, p.dims.head_dim, p.dims.intermediate).stride;
+    a.spin_limit = p.spin_limit > 0 ? p.spin_limit : kSpinLimit;
+    a.stall_counter = p.stall_counter;
     cudaError_t st = cudaFuncSetAttribute(decode_layers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, g.smem);
     if (st != cudaSuccess) return st;
     cudaLaunchConfig_t cfg = {};

@@ -185,7 +185,14 @@ struct PersistLaunch {
     const uint16_t* rope_sin;
     void* scratch;
     int* err;
+    // test hooks (off: nullptr / 0 / -1): per-layer bf16 intermediates, the
+    // poll limit of a dependency wait, a counter whose wait never completes
+    uint16_t* taps = nullptr;
+    uint32_t spin_limit = 0;
+    int stall_counter = -1;
 };
+// elements of one layer's tap record of the persistent kernel
+int64_t decode_persistent_tap_stride(const PersistDims& d);
 // ---- batched decode (batched.cu) ----------------------------------------------
 // NF4 (weight_type 0), bf16 (1) or re-tiled NF4 (2) weights [rows][K] times bf16 activations
 // [n_pad][K] (rows >= batch zero) on the tcgen05 tensor cores: fp32 split-K

@@ -1005,6 +1005,26 @@ int kudacuda_sm100_decode_layers_persistent(void* raw, uint64_t layer_table, int
                                             int64_t scratch_bytes, int64_t hidden, int64_t q_heads, int64_t kv_heads,
                                             int64_t head_dim, int64_t intermediate, int64_t kv_capacity, float eps,
                                             float scale, uint64_t stream) {
+    return kudacuda_sm100_decode_layers_persistent_debug(raw, layer_table, layers, x, state, rope_cos, rope_sin,
+                                                         max_pos, scratch, scratch_bytes, hidden, q_heads, kv_heads,
+                                                         head_dim, intermediate, kv_capacity, eps, scale, 0, 0, 0, -1,
+                                                         stream);
+}
+
+int64_t kudacuda_sm100_decode_persistent_tap_elements(int64_t layers, int64_t hidden, int64_t q_heads,
+                                                      int64_t kv_heads, int64_t head_dim, int64_t intermediate) {
+    kc::PersistDims d;
+    if (!persist_dims(layers, hidden, q_heads, kv_heads, head_dim, intermediate, 1, d)) return -1;
+    return layers * kc::decode_persistent_tap_stride(d);
+}
+
+int kudacuda_sm100_decode_layers_persistent_debug(void* raw, uint64_t layer_table, int64_t layers, uint64_t x,
+                                                  uint64_t state, uint64_t rope_cos, uint64_t rope_sin,
+                                                  int64_t max_pos, uint64_t scratch, int64_t scratch_bytes,
+                                                  int64_t hidden, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                                  int64_t intermediate, int64_t kv_capacity, float eps, float scale,
+                                                  uint64_t taps, int64_t taps_bytes, int64_t spin_limit,
+                                                  int64_t stall_counter, uint64_t stream) {
     Handle* h = as_handle(raw);
     if (!ready(h, "kudacuda_sm100_decode_layers_persistent")) return 1;
     kc::PersistDims d;
@@ -1039,6 +1059,20 @@ int kudacuda_sm100_decode_layers_persistent(void* raw, uint64_t layer_table, int
     p.rope_sin = P<const uint16_t>(rope_sin);
     p.scratch = P<void>(scratch);
     p.err = h->err_word;
+    if (taps != 0 && taps_bytes < 2 * layers * kc::decode_persistent_tap_stride(d)) {
+        h->set_error("sm100_decode_layers_persistent_debug: taps buffer is smaller than "
+                     "2 * kudacuda_sm100_decode_persistent_tap_elements() bytes");
+        return 1;
+    }
+    if (spin_limit < 0 || spin_limit > (int64_t{1} << 30) || stall_counter < -1 ||
+        stall_counter >= static_cast<int64_t>(layers) * 8) {
+        h->set_error("sm100_decode_layers_persistent_debug: spin_limit must be 0..2^30 (0: default) and "
+                     "stall_counter -1 or a counter index below layers * 8");
+        return 1;
+    }
+    p.taps = P<uint16_t>(taps);
+    p.spin_limit = static_cast<uint32_t>(spin_limit);
+    p.stall_counter = static_cast<int>(stall_counter);
     return finish(h, "decode_layers_kernel", kc::decode_layers_persistent(p, S(stream)));
 }
 

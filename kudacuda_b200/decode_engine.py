@@ -399,14 +399,39 @@ class PersistentLayers:
             out += [int(codes.data_ptr()), int(absm.data_ptr())]
         return out
 
-    def record(self, stream_ptr: int) -> int:
+    def record(self, stream_ptr: int, *, taps: Any = None, spin_limit: int = 0, stall_counter: int = -1) -> int:
+        """Launch the kernel (one launch).  ``taps``/``spin_limit``/``stall_counter``
+        are the test hooks of kudacuda_sm100_decode_layers_persistent_debug."""
+
         p, b, c = self.plan, self.plan.buffers, self.plan.config
         p.bridge.dispatch_decode_layers_persistent(
             self.table, b.x, b.state, b.rope_cos, b.rope_sin, self.scratch, layers=c.layers,
             max_pos=int(b.rope_cos.shape[0]), hidden=c.hidden, q_heads=p.q_heads, kv_heads=p.kv_heads,
             head_dim=c.head_dim, intermediate=p.inter, kv_capacity=p.kv_bucket, epsilon=c.eps,
-            scale=1.0 / math.sqrt(c.head_dim), stream_ptr=stream_ptr)
+            scale=1.0 / math.sqrt(c.head_dim), stream_ptr=stream_ptr, taps=taps, spin_limit=spin_limit,
+            stall_counter=stall_counter)
         return 1
+
+    def tap_layout(self) -> dict[str, tuple[int, int]]:
+        """(offset, length) of each intermediate in one layer's tap record."""
+
+        p, c = self.plan, self.plan.config
+        names = (("xn", c.hidden), ("q", p.q_heads * c.head_dim), ("k", p.kv_heads * c.head_dim),
+                 ("v", p.kv_heads * c.head_dim), ("att", p.q_heads * c.head_dim), ("x1", c.hidden),
+                 ("xn2", c.hidden), ("h", p.inter), ("x2", c.hidden))
+        out, off = {}, 0
+        for n, ln in names:
+            out[n] = (off, ln)
+            off += ln
+        out["stride"] = (off, 0)
+        return out
+
+    def new_taps(self) -> Any:
+        p, c = self.plan, self.plan.config
+        n = p.bridge.persistent_tap_elements(layers=c.layers, hidden=c.hidden, q_heads=p.q_heads,
+                                             kv_heads=p.kv_heads, head_dim=c.head_dim, intermediate=p.inter)
+        assert n == c.layers * self.tap_layout()["stride"][0]
+        return p.torch.zeros(n, dtype=p.torch.bfloat16, device=p.device)
 
 
 

@@ -1125,13 +1125,29 @@ class KudaCudaBridge:
     def dispatch_decode_layers_persistent(self, layer_table: Any, x: Any, state: Any, rope_cos: Any, rope_sin: Any,
                                           scratch: Any, *, layers: int, max_pos: int,
                                           hidden: int, q_heads: int, kv_heads: int, head_dim: int, intermediate: int,
-                                          kv_capacity: int, epsilon: float, scale: float, stream_ptr: int) -> None:
-        self._call("kudacuda_sm100_decode_layers_persistent", self._tensor_pointer(layer_table, "layer_table"),
-                   int(layers), self._tensor_pointer(x, "x"), self._tensor_pointer(state, "state"), self._tensor_pointer(rope_cos, "rope_cos"),
-                   self._tensor_pointer(rope_sin, "rope_sin"), int(max_pos), self._tensor_pointer(scratch, "scratch"),
-                   int(scratch.numel()) * int(scratch.element_size()), int(hidden), int(q_heads), int(kv_heads),
-                   int(head_dim), int(intermediate), int(kv_capacity), float(epsilon), float(scale),
-                   _normalize_cuda_handle(stream_ptr))
+                                          kv_capacity: int, epsilon: float, scale: float, stream_ptr: int,
+                                          taps: Any = None, spin_limit: int = 0, stall_counter: int = -1) -> None:
+        args = [self._tensor_pointer(layer_table, "layer_table"), int(layers), self._tensor_pointer(x, "x"),
+                self._tensor_pointer(state, "state"), self._tensor_pointer(rope_cos, "rope_cos"),
+                self._tensor_pointer(rope_sin, "rope_sin"), int(max_pos), self._tensor_pointer(scratch, "scratch"),
+                int(scratch.numel()) * int(scratch.element_size()), int(hidden), int(q_heads), int(kv_heads),
+                int(head_dim), int(intermediate), int(kv_capacity), float(epsilon), float(scale)]
+        if taps is None and not spin_limit and stall_counter < 0:
+            self._call("kudacuda_sm100_decode_layers_persistent", *args, _normalize_cuda_handle(stream_ptr))
+            return
+        tp = 0 if taps is None else self._tensor_pointer(taps, "taps")
+        tb = 0 if taps is None else int(taps.numel()) * int(taps.element_size())
+        self._call("kudacuda_sm100_decode_layers_persistent_debug", *args, tp, tb, int(spin_limit),
+                   int(stall_counter), _normalize_cuda_handle(stream_ptr))
+
+    def persistent_tap_elements(self, *, layers: int, hidden: int, q_heads: int, kv_heads: int, head_dim: int,
+                                intermediate: int) -> int:
+        n = int(self.lib.kudacuda_sm100_decode_persistent_tap_elements(int(layers), int(hidden), int(q_heads),
+                                                                         int(kv_heads), int(head_dim),
+                                                                         int(intermediate)))
+        if n < 0:
+            raise NativeCudaError("kudacuda_sm100_decode_persistent_tap_elements: unsupported shapes")
+        return n
 
     # ---------------------------------------------------------------- batched decode (B sequences per step)
     def batch_gemm_ksplit(self, rows: int, k: int) -> int:

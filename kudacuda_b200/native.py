@@ -73,6 +73,12 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         [_p, _u64, _i64, _u64, _u64, _u64, _u64, _i64, _u64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _f32,
          _u64],
     ),
+    "kudacuda_sm100_decode_persistent_tap_elements": (_i64, [_i64] * 6),
+    "kudacuda_sm100_decode_layers_persistent_debug": (
+        _i32,
+        [_p, _u64, _i64, _u64, _u64, _u64, _u64, _i64, _u64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _f32,
+         _u64, _i64, _i64, _i64, _u64],
+    ),
     "kudacuda_sm100_batch_gemm_ksplit": (_i64, [_i64, _i64]),
     "kudacuda_sm100_batch_gemm": (_i32, [_p, _i32, _u64, _u64, _i64, _i64, _u64, _i64, _i64, _u64, _i64, _i64, _u64]),
     "kudacuda_sm100_batch_retile_bytes": (_i64, [_i64, _i64]),
