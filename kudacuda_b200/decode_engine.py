@@ -344,6 +344,38 @@ class DecodeBuffers:
     lm_scratch: Any = None  # f32 logits for an NF4 lm_head
 
 
+class LayerCaches:
+    """Caller-owned per-layer K (or V) caches as one indexable object: item
+    ``li`` is layer li's [kv_heads, cap, head_dim] bf16 view (the tensors may
+    be [1, kv_heads, cap, head_dim], as Transformers' caches are);
+    ``zero_()`` clears every layer."""
+
+    def __init__(self, tensors: list) -> None:
+        self.layers = [t.view(t.shape[-3], t.shape[-2], t.shape[-1]) for t in tensors]
+
+    def __getitem__(self, i: int) -> Any:
+        return self.layers[i]
+
+    def __len__(self) -> int:
+        return len(self.layers)
+
+    @property
+    def shape(self) -> tuple:
+        return (len(self.layers), *tuple(self.layers[0].shape))
+
+    def zero_(self) -> "LayerCaches":
+        for t in self.layers:
+            t.zero_()
+        return self
+
+    def data_ptrs(self) -> list[int]:
+        return [int(t.data_ptr()) for t in self.layers]
+
+
+def _buffer_ptrs(t: Any) -> list[int]:
+    return t.data_ptrs() if isinstance(t, LayerCaches) else [int(t.data_ptr())]
+
+
 class PersistentLayers:
     """Device data of the persistent decode path for one plan: every layer's
     q/k/v, o, gate/up and down weights copied once into the stream layout of
@@ -442,7 +474,11 @@ class StaticDecodePlan:
 
     def __init__(self, bridge: KudaCudaBridge, weights: ModelWeights, *, kv_bucket: int = 512,
                  max_tokens: Optional[int] = None, device: Any = "cuda:0", torch_module: Any = None,
-                 allreduce: Any = None, keep_logits: bool = True, persistent: bool = False) -> None:
+                 allreduce: Any = None, keep_logits: bool = True, persistent: bool = False,
+                 kv_cache: Optional[tuple[list, list]] = None) -> None:
+        """``kv_cache=(keys, values)``: caller-owned per-layer caches (bf16,
+        contiguous, [1 or absent, kv_heads, kv_bucket, head_dim]) used in
+        place of the plan's own -- e.g. a Transformers prefill cache."""
         if torch_module is None:
             import torch as torch_module
         self.torch = torch_module
@@ -466,14 +502,29 @@ class StaticDecodePlan:
                                                    kv_extent=cap, device=device, torch_module=torch)
         lm_bytes = bridge.lm_head_workspace_bytes()
         cos, sin = rope_tables(torch, max(cap, max_tokens) + 1, c.head_dim, c.rope_theta, device)
+        if kv_cache is None:
+            kcache = torch.zeros((c.layers, self.kv_heads, cap, c.head_dim), dtype=bf16, device=device)
+            vcache = torch.zeros((c.layers, self.kv_heads, cap, c.head_dim), dtype=bf16, device=device)
+        else:
+            keys, values = (list(t) for t in kv_cache)
+            want = (self.kv_heads, cap, c.head_dim)
+            if len(keys) != c.layers or len(values) != c.layers:
+                raise NativeCudaError(f"kv_cache needs {c.layers} key and value tensors")
+            for t in keys + values:
+                if (t.dtype != bf16 or not t.is_contiguous() or tuple(t.shape[-3:]) != want or
+                        (t.dim() == 4 and int(t.shape[0]) != 1) or t.dim() not in (3, 4) or
+                        t.device != torch.device(device)):
+                    raise NativeCudaError(f"kv_cache tensors must be contiguous bf16 [1, {want[0]}, {want[1]}, "
+                                          f"{want[2]}] on {device}; got {tuple(t.shape)} {t.dtype} {t.device}")
+            kcache, vcache = LayerCaches(keys), LayerCaches(values)
         self.buffers = DecodeBuffers(
             state=torch.zeros(4, dtype=torch.int32, device=device),
             x=torch.zeros(c.hidden, dtype=bf16, device=device),
             q=torch.zeros(self.q_heads * c.head_dim, dtype=bf16, device=device),
             attn=torch.zeros(self.q_heads * c.head_dim, dtype=bf16, device=device),
             h=torch.zeros(self.inter, dtype=bf16, device=device),
-            kcache=torch.zeros((c.layers, self.kv_heads, cap, c.head_dim), dtype=bf16, device=device),
-            vcache=torch.zeros((c.layers, self.kv_heads, cap, c.head_dim), dtype=bf16, device=device),
+            kcache=kcache,
+            vcache=vcache,
             gqa_ws=ws,
             gqa_tickets=tickets,
             gqa_ws_bytes=nbytes,
@@ -515,9 +566,9 @@ class StaticDecodePlan:
         device pointer the graph bakes in (buffers, caches, weights)."""
 
         b, w, c = self.buffers, self.weights, self.config
-        ptrs = [t.data_ptr() for t in (b.state, b.x, b.q, b.attn, b.h, b.kcache, b.vcache, b.gqa_ws, b.gqa_tickets,
-                                       b.lm_ws, b.lm_ticket, b.logits, b.next_token, b.history, b.rope_cos, b.rope_sin,
-                                       w.embedding, w.final_norm)]
+        ptrs = [p for t in (b.state, b.x, b.q, b.attn, b.h, b.kcache, b.vcache, b.gqa_ws, b.gqa_tickets,
+                            b.lm_ws, b.lm_ticket, b.logits, b.next_token, b.history, b.rope_cos, b.rope_sin,
+                            w.embedding, w.final_norm) for p in _buffer_ptrs(t)]
         if self.persistent is not None:
             ptrs += self.persistent.pointers()
         for L in w.layers:
@@ -618,16 +669,21 @@ class StaticDecodePlan:
         self.torch.cuda.synchronize(self.device)
 
     # ------------------------------------------------------------------ graph
-    def capture(self, stream: Any) -> None:
+    def capture(self, stream: Any, *, warm_position: int = 0) -> None:
         """Warm every kernel once eagerly (lazy attribute set-up), restore the
-        state, then capture one step into the handle's graph."""
+        state, then capture one step into the handle's graph.  The warm-up
+        step runs token 0 at ``warm_position`` and writes that cache row, so
+        a caller whose cache already holds rows passes the first row it will
+        decode (the first replay rewrites it)."""
 
         torch = self.torch
         sp = int(stream.cuda_stream)
         saved_state = self.buffers.state.clone()
         saved_hist = self.buffers.history.clone()
-        # the warm-up step runs on a valid state (token 0 at position 0)
-        self.buffers.state.copy_(torch.tensor([0, 0, 1, 0], dtype=torch.int32))
+        wp = int(warm_position)
+        if not 0 <= wp < self.kv_bucket:
+            raise NativeCudaError(f"warm_position {wp} outside the KV bucket {self.kv_bucket}")
+        self.buffers.state.copy_(torch.tensor([0, wp, wp + 1, 0], dtype=torch.int32))
         torch.cuda.synchronize(self.device)
         with torch.cuda.stream(stream):
             self.record(sp)
@@ -1161,6 +1217,8 @@ class BatchedPrefill:
         self.decode = decode_plan
         self.chunk = int(chunk)
         b = decode_plan.buffers
+        if isinstance(b.kcache, LayerCaches):
+            raise NativeCudaError("batched prefill needs the plan's own [layers, kv_heads, cap, d] caches")
         # a handle of its own: a handle holds one graph, the decode plan's
         br = decode_plan.bridge
         self.bridge = KudaCudaBridge(device_id=br.device_id, lib_path=br.library_path, native_lib=br.lib)

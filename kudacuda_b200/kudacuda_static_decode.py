@@ -1,25 +1,28 @@
 """Fixed-shape decode for a Transformers Qwen2/Llama model, B200 edition.
 
-Mirrors the reference's static-decode interface
-(python/kudacuda_static_decode.py:80-447: ``GraphStaticCache``,
-``StaticDecodeContract``, ``StaticDecodeGraphRunner`` with ``capture`` /
-``replay`` / ``invalidate`` / ``captured`` / ``model_fingerprint``), but the
-captured graph is not a Transformers forward with patched attention: the
-runner converts the model's linears to NF4 (blocksize 64, fp32 absmax, on the
-device with the library's quantiser, or takes bitsandbytes-packed tensors as
-they are), and captures this library's whole decode step -- embedding, 36
-fused layer blocks, lm_head + argmax, state advance -- as one CUDA graph
-guarded by a ``DecodeGraphKey``.  Replay writes {token, position} on the
-device through the C ABI; nothing is recomputed on the host.
+A drop-in for the reference's static-decode module
+(python/kudacuda_static_decode.py:80-447): ``GraphStaticCache`` (with
+``from_dynamic_cache``), ``StaticDecodeContract`` and
+``StaticDecodeGraphRunner`` take the same calls -- ``capture(*, input_ids,
+position_ids, attention_mask, cache_position, past_key_values,
+logical_kv_len, kv_bucket, tactic_name, stream_ptr, stream, device_id,
+model_kwargs, workspace)`` and ``replay(*, next_token, position_ids,
+cache_position, logical_kv_len, stream_ptr)``, both returning the logits
+[1, 1, vocab] of the step -- so tools/benchmark/benchmark_gemma.py:292-350
+drives it unchanged.
 
-``GraphStaticCache`` exposes the fixed-capacity KV buffers of a plan with the
-cache methods Transformers code calls (``update``, ``get_seq_length``,
-``get_max_length``, ``get_max_cache_shape``, ``len``).
+What is captured differs: not a Transformers forward with patched attention
+but this library's whole decode step (embedding, every decoder layer in one
+persistent launch, final RMSNorm + tied lm_head, state advance), over NF4
+weights converted once from the model (bitsandbytes-packed tensors are taken
+as they are; dense linears are quantised on the device) and over the
+caller's GraphStaticCache tensors, which the step reads and appends to in
+place.  Replay writes the token (a device copy), position and KV length, then
+replays the graph; nothing of the model runs on the host.
 """
 
 from __future__ import annotations
 
-import hashlib
 from dataclasses import dataclass
 from typing import Any, Optional
 
@@ -31,7 +34,7 @@ from .decode_engine import (
     StaticDecodePlan,
     quantize_nf4,
 )
-from .kudacuda_graph_plan import GraphContractError
+from .kudacuda_graph_plan import DecodeGraphKey, GraphContractError
 from .kudacuda_sidecar import KudaCudaBridge, NativeCudaError
 
 
@@ -136,40 +139,90 @@ def weights_from_transformers(bridge: KudaCudaBridge, model: Any, *, device: Any
     return ModelWeights(cfg, layers, embedding, bf16(base.norm.weight), lm_head)
 
 
-# ------------------------------------------------------------------ static cache view
-class GraphStaticCache:
-    """Fixed-capacity KV view of a plan's caches ([layers][kv_heads][cap][d])."""
+# ------------------------------------------------------------------ static cache
+def _cache_layers(cache: Any) -> list:
+    """Per-layer entries of a Transformers cache: ``cache.layers`` (objects
+    with keys/values) or parallel key_cache / value_cache lists."""
 
-    def __init__(self, key_cache: Any, value_cache: Any, *, seq_length: int = 0) -> None:
-        self.key_cache = key_cache
-        self.value_cache = value_cache
-        self.max_cache_len = int(key_cache.shape[2])
-        self._seq = int(seq_length)
+    layers = getattr(cache, "layers", None)
+    if layers is not None:
+        return list(layers)
+    keys, values = getattr(cache, "key_cache", None), getattr(cache, "value_cache", None)
+    if keys is not None and values is not None:
+        return list(zip(keys, values))
+    return []
+
+
+def _layer_kv(entry: Any, index: int) -> tuple[Any, Any]:
+    if isinstance(entry, tuple) and len(entry) == 2:
+        return entry
+    for kname, vname in (("keys", "values"), ("key_cache", "value_cache")):
+        k, v = getattr(entry, kname, None), getattr(entry, vname, None)
+        if k is not None and v is not None:
+            return k, v
+    raise GraphContractError(f"cache layer {index} has no key/value tensors")
+
+
+def _shape(value: Any) -> tuple[int, ...]:
+    return tuple(int(v) for v in getattr(value, "shape", ()))
+
+
+class GraphStaticCache:
+    """Fixed-capacity KV cache for graph replay: per-layer K and V tensors
+    [batch, kv_heads, max_cache_len, head_dim] and a device-resident
+    ``cache_position`` (the reference's GraphStaticCache,
+    python/kudacuda_static_decode.py:80-172)."""
+
+    def __init__(self, *, key_cache: list, value_cache: list, cache_position: Any, sequence_length: int,
+                 max_cache_len: int) -> None:
+        self.key_cache = list(key_cache)
+        self.value_cache = list(value_cache)
+        self.cache_position = cache_position
+        self._sequence_length = int(sequence_length)
+        self.max_cache_len = int(max_cache_len)
+        self.layers = list(zip(self.key_cache, self.value_cache))
 
     @classmethod
-    def from_plan(cls, plan: StaticDecodePlan, *, seq_length: int = 0) -> "GraphStaticCache":
-        return cls(plan.buffers.kcache, plan.buffers.vcache, seq_length=seq_length)
+    def from_dynamic_cache(cls, torch_module: Any, dynamic_cache: Any, *, max_cache_len: int) -> "GraphStaticCache":
+        """Copy a prefilled Transformers cache into fixed-capacity tensors
+        (rows past the prefix are zero)."""
 
-    def update(self, key_states: Any, value_states: Any, layer_idx: int, cache_kwargs: Optional[dict] = None,
-               *args: Any, **kwargs: Any) -> tuple[Any, Any]:
-        """Write [1, kv_heads, n, d] rows at ``cache_position`` (index_copy on
-        the token axis) and return the layer's full fixed-size K/V."""
+        torch = torch_module
+        entries = _cache_layers(dynamic_cache)
+        if not entries:
+            raise GraphContractError("dynamic cache does not expose cache layers")
+        cap = int(max_cache_len)
+        keys, values = [], []
+        for i, entry in enumerate(entries):
+            k, v = _layer_kv(entry, i)
+            if k.dim() != 4 or _shape(v) != _shape(k):
+                raise GraphContractError(f"cache layer {i} is not a rank-4 KV pair")
+            n = int(k.shape[-2])
+            if n > cap:
+                raise GraphContractError("max_cache_len is smaller than the prefetched cache")
+            shape = (int(k.shape[0]), int(k.shape[1]), cap, int(k.shape[3]))
+            kt = torch.zeros(shape, dtype=k.dtype, device=k.device)
+            vt = torch.zeros(shape, dtype=v.dtype, device=v.device)
+            kt[..., :n, :].copy_(k)
+            vt[..., :n, :].copy_(v)
+            keys.append(kt)
+            values.append(vt)
+        seq = int(dynamic_cache.get_seq_length())
+        pos = torch.tensor([seq], dtype=torch.long, device=keys[0].device)
+        return cls(key_cache=keys, value_cache=values, cache_position=pos, sequence_length=seq, max_cache_len=cap)
 
-        kwargs = dict(cache_kwargs or {}, **kwargs)
-        pos = kwargs.get("cache_position")
-        k_layer, v_layer = self.key_cache[layer_idx], self.value_cache[layer_idx]
-        if pos is None:
-            raise GraphContractError("GraphStaticCache.update needs cache_position")
-        if int(pos.max()) >= self.max_cache_len:
-            raise GraphContractError("cache_position exceeds the static KV capacity")
-        k_layer.index_copy_(1, pos, key_states[0].to(k_layer.dtype))
-        v_layer.index_copy_(1, pos, value_states[0].to(v_layer.dtype))
-        if layer_idx == 0:
-            self._seq = max(self._seq, int(pos.max()) + 1)
-        return k_layer.unsqueeze(0), v_layer.unsqueeze(0)
+    def update(self, key_states: Any, value_states: Any, layer_idx: int, *args: Any, **kwargs: Any) -> tuple[Any, Any]:
+        """Write the step's rows at ``cache_position`` (token axis) and return
+        the layer's full fixed-size K/V (what Transformers attention reads)."""
+
+        if int(key_states.shape[-2]) != int(self.cache_position.numel()):
+            raise GraphContractError("graph cache position count does not match key update length")
+        self.key_cache[layer_idx].index_copy_(2, self.cache_position, key_states)
+        self.value_cache[layer_idx].index_copy_(2, self.cache_position, value_states)
+        return self.key_cache[layer_idx], self.value_cache[layer_idx]
 
     def get_seq_length(self, layer_idx: int = 0) -> int:
-        return self._seq
+        return self._sequence_length
 
     def get_max_length(self, layer_idx: int = 0) -> int:
         return self.max_cache_len
@@ -178,112 +231,232 @@ class GraphStaticCache:
         return self.max_cache_len
 
     def __len__(self) -> int:
-        return int(self.key_cache.shape[0])
+        return len(self.key_cache)
 
 
 # ------------------------------------------------------------------ runner
 @dataclass(frozen=True)
 class StaticDecodeContract:
-    tactic_name: str = "decode_step_sm100_v1"
-    kv_bucket: int = 512
-    batch_size: int = 1
-    query_len: int = 1
+    key: DecodeGraphKey
+    stream_ptr: int
+    logical_kv_len: int
 
 
 class StaticDecodeGraphRunner:
-    """Capture one decode step of a Transformers decoder as this library's
-    CUDA graph; replay it per token."""
+    """Capture one complete decode step and replay it by pointer identity
+    (the reference's StaticDecodeGraphRunner, with its capture / replay /
+    invalidate signatures and status fields)."""
 
-    def __init__(self, bridge: KudaCudaBridge, model: Any, torch_module: Any = None, *,
-                 device: Any = "cuda:0") -> None:
+    def __init__(self, bridge: KudaCudaBridge, model: Any, torch_module: Any = None) -> None:
         if torch_module is None:
             import torch as torch_module
         self.bridge = bridge
         self.model = model
         self.torch = torch_module
-        self.device = device
-        self.plan: Optional[StaticDecodePlan] = None
-        self.cache: Optional[GraphStaticCache] = None
         self.contract: Optional[StaticDecodeContract] = None
-        self.stream: Any = None
-        self.fallback_reason: Optional[str] = None
+        self.static_inputs: dict[str, Any] = {}
+        self.cache: Any = None
+        self.kv_len_device: Any = None
+        self.logits: Any = None
+        self.status = "not-requested"
+        self.reason: Optional[str] = None
+        self.capture_ms: Optional[float] = None
+        self.replay_count = 0
+        self.backend = "native"
+        self.cuda_graph: Any = None
+        self.workspace: Any = None
+        self.plan: Optional[StaticDecodePlan] = None
         self._weights: Optional[ModelWeights] = None
-        self._host_in = None
-        self._host_out = None
+        self._stream: Any = None
+        self._host: Any = None
+        self._host_next = 0
 
     @property
     def captured(self) -> bool:
-        return self.plan is not None and self.plan.captured
+        return self.contract is not None and self.status == "captured"
 
     @staticmethod
     def model_fingerprint(model: Any) -> str:
-        """Architecture identity of the model (config fields that shape the graph)."""
+        """Identity of the model the graph was built for: class, model type,
+        layer count, hidden size, vocabulary and dtype."""
 
-        cfg = decoder_config_from_transformers(model)
-        return hashlib.sha256(repr(cfg).encode()).hexdigest()[:16]
+        config = getattr(model, "config", None)
+        fields = (type(model).__name__, getattr(config, "model_type", ""), getattr(config, "num_hidden_layers", ""),
+                  getattr(config, "hidden_size", ""), getattr(config, "vocab_size", ""),
+                  str(getattr(config, "torch_dtype", "")))
+        return "|".join(str(f) for f in fields)
 
-    def capture(self, *, kv_bucket: int = 512, stream: Any = None,
-                tactic_name: str = "decode_step_sm100_v1") -> None:
+    def prepare_weights(self, device: Any = None) -> ModelWeights:
+        """The model's decode weights (NF4), converted once and reused by every
+        capture; callable before capture (e.g. to build an eager model on the
+        same NF4 values)."""
+
+        if device is None:
+            device = next(self.model.parameters()).device
+        if self._weights is None:
+            self._weights = weights_from_transformers(self.bridge, self.model, device=device, torch_module=self.torch)
+        return self._weights
+
+    def capture(self, *, input_ids: Any, position_ids: Any, attention_mask: Any, cache_position: Any,
+                past_key_values: GraphStaticCache, logical_kv_len: int, kv_bucket: int, tactic_name: str,
+                stream_ptr: int, stream: Any = None, device_id: int = 0, model_kwargs: Any = None,
+                workspace: Any = None) -> Any:
+        """Build the plan over ``past_key_values``' tensors, capture one step,
+        replay it once for ``input_ids`` at position ``logical_kv_len`` and
+        return its logits [1, 1, vocab].  ``attention_mask`` and
+        ``model_kwargs`` are accepted for signature parity and not read: the
+        step attends over exactly ``logical_kv_len + 1`` cached rows."""
+
+        import time
+
         torch = self.torch
         if self.captured:
-            raise GraphContractError("runner already holds a captured graph; invalidate it first")
+            raise GraphContractError("graph runner already has a captured forward")
+        if _shape(input_ids) != (1, 1):
+            raise GraphContractError("static decode captures batch 1, query length 1")
+        cache = past_key_values
+        if int(kv_bucket) != int(cache.max_cache_len):
+            raise GraphContractError("kv_bucket differs from the graph cache's max_cache_len")
+        if not 0 <= int(logical_kv_len) < int(kv_bucket):
+            raise GraphContractError("logical_kv_len + 1 exceeds the KV bucket")
+        t0 = time.perf_counter()
+        device = input_ids.device
         try:
-            if self._weights is None:
-                self._weights = weights_from_transformers(self.bridge, self.model, device=self.device,
-                                                          torch_module=torch)
-            self.stream = stream or torch.cuda.Stream(device=self.device)
-            self.plan = StaticDecodePlan(self.bridge, self._weights, kv_bucket=kv_bucket, device=self.device,
-                                         torch_module=torch)
-            self.plan.capture(self.stream)
-        except Exception as exc:
-            self.invalidate(f"capture failed: {exc}")
-            raise
-        self.cache = GraphStaticCache.from_plan(self.plan)
-        self.contract = StaticDecodeContract(tactic_name=tactic_name, kv_bucket=int(kv_bucket))
-        self._host_in = torch.zeros(4, dtype=torch.int32).pin_memory()
-        self._host_out = torch.zeros(1, dtype=torch.int32).pin_memory()
+            weights = self.prepare_weights(device)
+            kv = (cache.key_cache, cache.value_cache)
+            try:
+                plan = StaticDecodePlan(self.bridge, weights, kv_bucket=int(kv_bucket), device=device,
+                                        torch_module=torch, persistent=True, kv_cache=kv)
+            except NativeCudaError:  # shapes outside the persistent kernel: the per-op step
+                plan = StaticDecodePlan(self.bridge, weights, kv_bucket=int(kv_bucket), device=device,
+                                        torch_module=torch, kv_cache=kv)
+            self.plan = plan
+            self._stream = stream if stream is not None else torch.cuda.ExternalStream(int(stream_ptr))
+            if int(self._stream.cuda_stream) != int(stream_ptr):
+                raise GraphContractError("stream and stream_ptr name different streams")
+            self.bridge.reset_graph()
+            plan.capture(self._stream, warm_position=int(logical_kv_len))
+        except Exception as error:
+            self.plan = None
+            try:
+                self.bridge.reset_graph()
+            except NativeCudaError:
+                pass
+            self.status = "fallback"
+            self.reason = f"capture_failed:{type(error).__name__}:{error}"
+            raise GraphContractError(self.reason) from error
+        self.static_inputs = {"input_ids": input_ids.clone(), "position_ids": position_ids.clone(),
+                              "attention_mask": attention_mask, "cache_position": cache_position}
+        self.cache = cache
+        self.workspace = workspace
+        self.kv_len_device = plan.buffers.state[2:3]
+        self.logits = plan.buffers.logits.view(1, 1, -1)
+        # pinned host slots for the per-step state copies; a slot is reused
+        # only after the copies that read it have run (its event)
+        self._host = [(torch.zeros(4, dtype=torch.int32).pin_memory(), torch.zeros(1, dtype=torch.long).pin_memory(),
+                       torch.cuda.Event()) for _ in range(4)]
+        self._host_next = 0
+        self.contract = StaticDecodeContract(key=plan.graph_key, stream_ptr=int(stream_ptr),
+                                             logical_kv_len=int(logical_kv_len) + 1)
+        self.status = "captured"
+        self.reason = None
+        self._step(input_ids, int(logical_kv_len))
+        self.replay_count = 1
+        self.capture_ms = (time.perf_counter() - t0) * 1e3
+        return self.logits
 
-    def replay(self, token_id: int, position: int, *, stream: Any = None) -> int:
-        """One decode step for ``token_id`` at ``position``; returns the greedy
-        next token (host-synchronous, through kudacuda_sm100_graph_step_host)."""
+    def _step(self, token: Any, logical_kv_len: int) -> None:
+        """state <- {token (device copy), position, kv_len}; cache_position <-
+        position; replay -- all ordered on the capture stream."""
 
-        if not self.captured or self.plan is None:
-            raise GraphContractError("runner has no captured graph")
-        if stream is not None and stream is not self.stream:
-            raise GraphContractError("replay stream differs from the capture stream")
-        if not 0 <= int(position) < self.plan.kv_bucket:
-            raise GraphContractError(f"position {position} outside the KV bucket {self.plan.kv_bucket}")
+        torch = self.torch
         b = self.plan.buffers
-        self._host_in[0], self._host_in[1], self._host_in[2] = int(token_id), int(position), int(position) + 1
-        self.bridge.graph_step_host(self._host_in, b.state, self._host_out, b.next_token,
-                                    stream_ptr=int(self.stream.cuda_stream))
-        if self.cache is not None:
-            self.cache._seq = max(self.cache._seq, int(position) + 1)
-        return int(self._host_out[0])
+        pos = int(logical_kv_len)
+        state_h, pos_h, done = self._host[self._host_next]
+        self._host_next = (self._host_next + 1) % len(self._host)
+        done.synchronize()  # the copies that last read this slot have run
+        state_h[0], state_h[1], state_h[2], state_h[3] = 0, pos, pos + 1, 0
+        pos_h[0] = pos
+        with torch.cuda.stream(self._stream):
+            b.state.copy_(state_h, non_blocking=True)
+            b.state[0:1].copy_(token.reshape(-1)[:1], non_blocking=True)
+            self.cache.cache_position.copy_(pos_h, non_blocking=True)
+            done.record(self._stream)
+        self.plan.replay(self._stream)
 
-    def generate(self, prompt: list[int], new_tokens: int) -> list[int]:
-        """Greedy continuation of ``prompt`` (prompt tokens through decode steps)."""
+    def replay(self, *, next_token: Any, position_ids: Any, cache_position: int, logical_kv_len: int,
+               stream_ptr: int) -> Any:
+        """One decode step for ``next_token`` with ``logical_kv_len`` rows
+        already cached; returns the logits [1, 1, vocab] (device buffer,
+        overwritten by the next replay).  The step's RoPE position and cache
+        row are ``cache_position`` (equal to ``position_ids`` in every caller
+        of the reference)."""
 
-        if self.plan is None:
-            raise GraphContractError("runner has no captured graph")
-        self.plan.reset_cache()
-        if self.cache is not None:
-            self.cache._seq = 0
-        nxt = 0
-        for i, tok in enumerate(prompt):
-            nxt = self.replay(tok, i)
-        out = [nxt]
-        for j in range(1, int(new_tokens)):
-            out.append(self.replay(out[-1], len(prompt) + j - 1))
+        if not self.captured or self.contract is None or self.plan is None:
+            raise GraphContractError("graph runner has no captured forward")
+        if int(stream_ptr) != self.contract.stream_ptr:
+            raise GraphContractError("graph replay stream changed")
+        if int(logical_kv_len) + 1 > self.contract.key.kv_bucket:
+            raise GraphContractError("graph replay KV length exceeds the captured bucket")
+        if _shape(next_token) != _shape(self.static_inputs["input_ids"]):
+            raise GraphContractError("graph replay token shape changed")
+        if _shape(position_ids) != _shape(self.static_inputs["position_ids"]):
+            raise GraphContractError("graph replay position shape changed")
+        if int(cache_position) != int(logical_kv_len):
+            raise GraphContractError("cache_position must equal logical_kv_len (one new row per step)")
+        self.plan.verify_key()
+        self._step(next_token, int(logical_kv_len))
+        self.replay_count += 1
+        return self.logits
+
+    def generate(self, prompt: list[int], new_tokens: int, *, kv_bucket: int = 512) -> list[int]:
+        """Greedy continuation of ``prompt`` with the prompt fed through decode
+        steps (no Transformers prefill); captures on first use."""
+
+        torch = self.torch
+        device = next(self.model.parameters()).device
+        first = torch.tensor([[int(prompt[0])]], dtype=torch.long, device=device)
+        if not self.captured:
+            cfg = decoder_config_from_transformers(self.model)
+            shape = (1, cfg.kv_heads, int(kv_bucket), cfg.head_dim)
+            keys = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(cfg.layers)]
+            values = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(cfg.layers)]
+            cache = GraphStaticCache(key_cache=keys, value_cache=values,
+                                     cache_position=torch.zeros(1, dtype=torch.long, device=device),
+                                     sequence_length=0, max_cache_len=int(kv_bucket))
+            stream = torch.cuda.Stream(device=device)
+            logits = self.capture(input_ids=first, position_ids=first * 0, attention_mask=None,
+                                  cache_position=cache.cache_position, past_key_values=cache, logical_kv_len=0,
+                                  kv_bucket=int(kv_bucket), tactic_name="decode_step_sm100_persistent_v1",
+                                  stream_ptr=int(stream.cuda_stream), stream=stream)
+        else:
+            self.plan.reset_cache()
+            logits = self.replay(next_token=first, position_ids=first * 0, cache_position=0, logical_kv_len=0,
+                                 stream_ptr=self.contract.stream_ptr)
+        sp = self.contract.stream_ptr
+        out: list[int] = []
+        i = 1
+        while len(out) < int(new_tokens):
+            if i < len(prompt):
+                tok = torch.tensor([[int(prompt[i])]], dtype=torch.long, device=device)
+            else:
+                tok = torch.argmax(logits[:, -1, :], dim=-1, keepdim=True)
+                out.append(int(tok.item()))
+                if len(out) == int(new_tokens):
+                    break
+            pos = torch.tensor([[i]], dtype=torch.long, device=device)
+            logits = self.replay(next_token=tok, position_ids=pos, cache_position=i, logical_kv_len=i, stream_ptr=sp)
+            i += 1
         return out
 
     def invalidate(self, reason: str) -> None:
-        self.fallback_reason = str(reason)
-        if self.plan is not None:
-            self.plan.graph_plan.invalidate()
         try:
             self.bridge.reset_graph()
         except NativeCudaError:
             pass
+        if self.plan is not None:
+            self.plan.graph_plan.invalidate()
         self.plan = None
-        self.cache = None
+        self.contract = None
+        self.status = "fallback"
+        self.reason = str(reason)

@@ -304,3 +304,47 @@ def test_shutdown_destroys_the_handle_once():
 
 def test_platform_library_name():
     assert select_library_name("Linux").endswith(".so")
+
+
+# ------------------------------------------------------------------ the reference's own bridge on this library
+def _reference_checkout():
+    import os
+
+    env = os.environ.get("KUDACUDA_REFERENCE")
+    for cand in ([Path(env)] if env else []) + [Path(__file__).resolve().parents[2] / "reference"]:
+        if (cand / "python" / "kudacuda_sidecar.py").is_file():
+            return cand
+    return None
+
+
+def test_reference_bridge_binds_this_library_and_manifest():
+    """The reference's unmodified KudaCudaBridge (python/kudacuda_sidecar.py:
+    185-431) loads this repository's manifest with its own loader and contract
+    parsers, binds this library with its own ctypes argtypes (every symbol it
+    binds resolves), gets a handle from kudacuda_create, and -- in a container
+    without a GPU -- fails only at kudacuda_freeze, with this library's error
+    message through its own error path."""
+
+    import importlib.util
+    import sys
+
+    ref = _reference_checkout()
+    if ref is None:
+        pytest.skip("no reference checkout at hand (KUDACUDA_REFERENCE)")
+    spec = importlib.util.spec_from_file_location("reference_kudacuda_sidecar", ref / "python" / "kudacuda_sidecar.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod  # its dataclasses look their module up
+    try:
+        spec.loader.exec_module(mod)
+    finally:
+        sys.modules.pop(spec.name, None)
+    manifest = Path(native.PACKAGE_DIR) / "manifests" / "b200-sm100.json"
+    lib = ctypes.CDLL(str(native.DEFAULT_LIBRARY))
+    assert mod.load_manifest(manifest)["target_arch"] == "sm_100a"
+    try:
+        bridge = mod.KudaCudaBridge(manifest=manifest, native_lib=lib, device_id=0)
+    except mod.NativeCudaError as exc:  # no GPU here: the handle exists, freeze reports the device
+        assert "kudacuda_freeze" in str(exc) and "cudaSetDevice" in str(exc), str(exc)
+        return
+    assert bridge.engine_handle  # on a machine with a GPU the bridge is fully usable
+    bridge.shutdown()

@@ -1,127 +1,155 @@
-"""GPU test of the Transformers-model runner (kudacuda_static_decode): a
-2-layer Qwen2 model with the config-1 layer shapes is converted to NF4 and
-decoded through one captured graph per token; greedy top-1 agreement is
-measured teacher-forced against Transformers' eager bf16 forward on the same
-dequantised NF4 weights -- the restatement of the reference's eager NF4 path
-(Transformers + bitsandbytes Linear4bit, which computes with weights
-dequantised to bf16; bitsandbytes itself is absent here).  Both sides see the
-same token history at every position, so a disagreement is a per-step
-numerical near-tie, not compounding drift."""
+"""The drop-in static-decode runner (kudacuda_static_decode), driven exactly as
+the reference's benchmark drives its own (tools/benchmark/benchmark_gemma.py:
+267-350): a Transformers prefill into a DynamicCache,
+``GraphStaticCache.from_dynamic_cache``, ``runner.capture(...)`` returning the
+first decode logits, then ``runner.replay(...)`` per token with the argmax
+taken from the returned logits.
+
+The eager side is the restatement of the reference's eager NF4 path
+(Transformers + bitsandbytes Linear4bit, which computes with each weight
+dequantised to bf16; bitsandbytes is absent here): the same Transformers model
+with every linear set to the runner's own NF4 weights dequantised, in bf16,
+and the same model in fp32 for the precision floor.  Agreement is
+teacher-forced over 128 greedy tokens: every side predicts the next token
+after the same history (the bf16 eager greedy sequence), so a disagreement is
+a per-step near-tie, not compounding drift.  Reported beside it: the fp32
+eager path's agreement with the bf16 eager path on the same positions -- how
+much the eager path itself depends on the rounding of its arithmetic.
+
+* a 2-layer model with the config-1 layer shapes and a 4096-token vocabulary;
+* the full config-3 model: Qwen2.5-3B architecture (36 layers, vocabulary
+  151936, tied embedding), random init N(0, 0.02), 64-token random prompt,
+  KV bucket 512 -- the bench's workload.
+"""
+
+import copy
 
 import pytest
 
 pytestmark = pytest.mark.gpu
 
-PROMPT_LEN, NEW_TOKENS = 16, 128
-# A random-init model has many near-tied logits: Transformers' own bf16 eager
-# forward agrees with its fp32 eager forward on only ~97.7% of positions here,
-# so the bar is relative to that floor (at most 4 of 128 more disagreements)
-# plus an absolute minimum.
-AGREEMENT = 0.94
-FLOOR_MARGIN = 4 / 128
+NEW_TOKENS = 128
 
 
-def _tiny_qwen2(torch):
+def _qwen2(torch, layers, vocab):
     from transformers import Qwen2Config, Qwen2ForCausalLM
 
-    cfg = Qwen2Config(hidden_size=2048, intermediate_size=11008, num_hidden_layers=2, num_attention_heads=16,
-                      num_key_value_heads=2, vocab_size=4096, max_position_embeddings=1024, rope_theta=1.0e6,
-                      rms_norm_eps=1.0e-6, tie_word_embeddings=True)
+    cfg = Qwen2Config(hidden_size=2048, intermediate_size=11008, num_hidden_layers=layers, num_attention_heads=16,
+                      num_key_value_heads=2, vocab_size=vocab, max_position_embeddings=1024, rope_theta=1.0e6,
+                      rms_norm_eps=1.0e-6, tie_word_embeddings=True, initializer_range=0.02)
     torch.manual_seed(20260824)
-    model = Qwen2ForCausalLM(cfg)
-    return model.to(device="cuda:0", dtype=torch.bfloat16).eval()
+    with torch.device("cuda:0"):
+        model = Qwen2ForCausalLM(cfg)
+    model = model.to(dtype=torch.bfloat16).eval()
+    model.config._attn_implementation = "eager"
+    return model
 
 
-def test_runner_matches_transformers_eager_on_the_same_nf4_weights():
-    import copy
+def _set_linears(torch, model, weights, deq, dtype):
+    with torch.no_grad():
+        for layer, L in zip(model.model.layers, weights.layers):
+            a, m = layer.self_attn, layer.mlp
+            for mod, lin in ((a.q_proj, L.q), (a.k_proj, L.k), (a.v_proj, L.v), (a.o_proj, L.o),
+                             (m.gate_proj, L.gate), (m.up_proj, L.up), (m.down_proj, L.down)):
+                mod.weight.copy_(deq(lin, dtype))
 
+
+def _run(layers, vocab, prompt_len, kv_bucket):
     import torch
+    from transformers import DynamicCache
 
     from kudacuda_b200.kudacuda_sidecar import KudaCudaBridge
-    from kudacuda_b200.kudacuda_static_decode import StaticDecodeGraphRunner
+    from kudacuda_b200.kudacuda_static_decode import GraphStaticCache, StaticDecodeGraphRunner
 
-    model = _tiny_qwen2(torch)
+    torch.cuda.set_device(0)
+    device = torch.device("cuda:0")
+    model = _qwen2(torch, layers, vocab)
     bridge = KudaCudaBridge(device_id=0)
     runner = StaticDecodeGraphRunner(bridge, model, torch)
-    runner.capture(kv_bucket=256)
-    assert runner.captured
-
-    # eager models computing with the runner's NF4 weights: fp32 with the exact
-    # dequantised values, and bf16 with them rounded to bf16 (the reference's
-    # eager NF4 path: bitsandbytes dequantises to the compute dtype)
-    w = runner._weights
+    w = runner.prepare_weights(device)
     sp = int(torch.cuda.current_stream().cuda_stream)
 
     def deq(lin, dtype):
-        out = torch.empty((lin.rows, lin.k), dtype=dtype, device="cuda:0")
+        out = torch.empty((lin.rows, lin.k), dtype=dtype, device=device)
         bridge.dispatch_nf4_dequantize(lin.packed, lin.absmax, out, n=lin.rows * lin.k, stream_ptr=sp)
         return out
 
+    # the eager models compute with the runner's NF4 weights: bf16-rounded
+    # (the reference's eager path) and exact in fp32 (the precision floor)
+    _set_linears(torch, model, w, deq, torch.bfloat16)
     m32 = copy.deepcopy(model).float()
-    with torch.no_grad():
-        for mdl, dt in ((model, torch.bfloat16), (m32, torch.float32)):
-            for layer, L in zip(mdl.model.layers, w.layers):
-                a, m = layer.self_attn, layer.mlp
-                for mod, lin in ((a.q_proj, L.q), (a.k_proj, L.k), (a.v_proj, L.v), (a.o_proj, L.o),
-                                 (m.gate_proj, L.gate), (m.up_proj, L.up), (m.down_proj, L.down)):
-                    mod.weight.copy_(deq(lin, dt))
-            mdl.config._attn_implementation = "eager"
+    _set_linears(torch, m32, w, deq, torch.float32)
+    m32.config._attn_implementation = "eager"
     torch.cuda.synchronize()
 
-    g = torch.Generator().manual_seed(7)
-    prompt = torch.randint(0, 4096, (PROMPT_LEN,), generator=g).tolist()
+    g = torch.Generator().manual_seed(64)
+    prompt = torch.randint(0, vocab, (prompt_len,), generator=g).tolist()
+    ids = torch.tensor([prompt], device=device)
     with torch.no_grad():
-        ids = torch.tensor([prompt], device="cuda:0")
-        seq = m32.generate(ids, max_new_tokens=NEW_TOKENS, do_sample=False, min_new_tokens=NEW_TOKENS,
-                           pad_token_id=0, eos_token_id=None)[0].tolist()
-        full = torch.tensor([seq[:-1]], device="cuda:0")
-        p32 = m32(full).logits[0].float().argmax(-1).tolist()[PROMPT_LEN - 1:]
-        p16 = model(full).logits[0].float().argmax(-1).tolist()[PROMPT_LEN - 1:]
-    # teacher-forced: our next-token prediction at every generated position
-    runner.plan.reset_cache()
+        seq = model.generate(ids, max_new_tokens=NEW_TOKENS, min_new_tokens=NEW_TOKENS, do_sample=False,
+                             pad_token_id=0, eos_token_id=None)[0].tolist()
+        full = torch.tensor([seq[:-1]], device=device)
+        p32 = m32(full).logits[0].float().argmax(-1).tolist()[prompt_len - 1:]
+    del m32
+    torch.cuda.empty_cache()
+    ref = seq[prompt_len:]  # the bf16 eager greedy tokens
+
+    # ---- the reference benchmark's flow, teacher-forced on the eager tokens
+    with torch.no_grad():
+        dynamic_cache = DynamicCache(config=model.config)
+        prefill = model(input_ids=ids, past_key_values=dynamic_cache, use_cache=True)
+    graph_cache = GraphStaticCache.from_dynamic_cache(torch, dynamic_cache, max_cache_len=kv_bucket)
+    assert graph_cache.get_seq_length() == prompt_len and len(graph_cache) == layers
+    mask = {"full_attention": torch.zeros((1, 1, 1, kv_bucket), dtype=torch.bfloat16, device=device)}
+    first = torch.argmax(prefill.logits[:, -1, :], dim=-1, keepdim=True)
     ours = []
-    for pos in range(len(seq) - 1):
-        nxt = runner.replay(seq[pos], pos)
-        if pos >= PROMPT_LEN - 1:
-            ours.append(nxt)
+    stream = torch.cuda.Stream(device=device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        stream_ptr = int(stream.cuda_stream)
+        position_ids = torch.tensor([[prompt_len]], dtype=torch.long, device=device)
+        logits = runner.capture(input_ids=first, position_ids=position_ids, attention_mask=mask,
+                                cache_position=graph_cache.cache_position, past_key_values=graph_cache,
+                                logical_kv_len=prompt_len, kv_bucket=kv_bucket,
+                                tactic_name="decode_step_sm100_persistent_v1", stream_ptr=stream_ptr, stream=stream)
+        assert runner.captured and runner.replay_count == 1
+        assert tuple(logits.shape) == (1, 1, vocab)
+        ours.append(int(torch.argmax(logits[:, -1, :], dim=-1).item()))
+        logical_kv_len = prompt_len + 1
+        for i in range(1, NEW_TOKENS):
+            next_token = torch.tensor([[ref[i - 1]]], dtype=torch.long, device=device)  # teacher forcing
+            position_ids = torch.tensor([[logical_kv_len]], dtype=torch.long, device=device)
+            replayed = runner.replay(next_token=next_token, position_ids=position_ids, cache_position=logical_kv_len,
+                                     logical_kv_len=logical_kv_len, stream_ptr=stream_ptr)
+            ours.append(int(torch.argmax(replayed[:, -1, :], dim=-1).item()))
+            logical_kv_len += 1
+        stream.synchronize()
+    assert bridge.error_word(clear=True) == 0
+    assert int(graph_cache.cache_position.item()) == prompt_len + NEW_TOKENS - 1
+    first_eager = int(first.item())
+    runner.invalidate("test done")
+    assert not runner.captured and runner.status == "fallback"
+    bridge.shutdown()
 
     def agree(a, b):
         return sum(int(x == y) for x, y in zip(a, b)) / len(a)
 
-    a32, a16, ref_noise = agree(ours, p32), agree(ours, p16), agree(p16, p32)
-    print(f"teacher-forced top-1 agreement over {len(ours)} tokens: ours vs fp32-eager {a32:.4f}, "
-          f"ours vs bf16-eager {a16:.4f}, bf16-eager vs fp32-eager {ref_noise:.4f}")
-    assert bridge.error_word(clear=True) == 0
-    msg = f"ours/fp32 {a32:.4f} ours/bf16 {a16:.4f} bf16/fp32 {ref_noise:.4f}"
-    assert a32 >= AGREEMENT and a16 >= AGREEMENT, msg
-    assert a32 >= ref_noise - FLOOR_MARGIN, msg
-    # free-running greedy generation through the runner also starts with the same token
-    gen = runner.generate(prompt, 8)
-    assert gen[0] == seq[PROMPT_LEN] or gen[0] == p16[0]
+    return dict(ours_vs_bf16=agree(ours, ref), ours_vs_fp32=agree(ours, p32), fp32_vs_bf16=agree(p32, ref),
+                first=(ours[0], first_eager, ref[0]))
 
-    # the batched tensor-core path on the same weights (one sequence): its
-    # arithmetic is the bf16 eager path's (weights dequantised to bf16, bf16
-    # matmul with fp32 accumulation), so it tracks the bf16 forward closely
-    from kudacuda_b200.decode_engine import BatchedDecodePlan
 
-    bbridge = KudaCudaBridge(device_id=0)
-    bplan = BatchedDecodePlan(bbridge, w, batch=1, kv_bucket=256, max_tokens=256, device="cuda:0")
-    bstream = torch.cuda.Stream()
-    bplan.capture(bstream)
-    bplan.reset_cache()
-    batched = []
-    for pos in range(len(seq) - 1):
-        nxt = bplan.step_tokens([seq[pos]], [pos], bstream)[0]
-        if pos >= PROMPT_LEN - 1:
-            batched.append(nxt)
-    b32, b16 = agree(batched, p32), agree(batched, p16)
-    print(f"batched path: vs fp32-eager {b32:.4f}, vs bf16-eager {b16:.4f}")
-    assert bbridge.error_word(clear=True) == 0
-    bmsg = f"batched/fp32 {b32:.4f} batched/bf16 {b16:.4f} bf16/fp32 {ref_noise:.4f}"
-    assert b32 >= AGREEMENT and b16 >= AGREEMENT, bmsg
-    assert b32 >= ref_noise - FLOOR_MARGIN, bmsg
-    bplan.release()
-    bbridge.reset_graph()
-    bbridge.shutdown()
-    runner.invalidate("test done")
-    assert not runner.captured
+def test_runner_two_layer_model_benchmark_flow():
+    r = _run(layers=2, vocab=4096, prompt_len=16, kv_bucket=256)
+    print(f"2-layer: {r}")
+    assert r["first"][1] == r["first"][2]
+    assert r["ours_vs_bf16"] >= 0.94 and r["ours_vs_fp32"] >= 0.94, r
+
+
+def test_runner_config3_qwen25_3b_128_greedy_tokens():
+    """The north-star agreement check on the bench's model: 36 layers,
+    vocabulary 151936, 64-token prompt, KV bucket 512, 128 tokens."""
+
+    r = _run(layers=36, vocab=151936, prompt_len=64, kv_bucket=512)
+    print(f"config-3 (Qwen2.5-3B architecture): {r}")
+    assert r["ours_vs_bf16"] >= r["fp32_vs_bf16"] - 4 / NEW_TOKENS, r
+    assert r["ours_vs_bf16"] >= 0.90, r
