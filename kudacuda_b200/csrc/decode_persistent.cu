@@ -45,6 +45,32 @@
 #include "kc_common.cuh"
 #include "kc_launch.h"
 
+// Phase timestamps for profiling builds only (-DKC_PERSIST_STAMPS; off in the
+// library): thread 0 of every CTA records %globaltimer at fixed points of one
+// layer (KC_STAMP_LAYER) into g_persist_stamps[cta][32], read back with
+// kc_persist_read_stamps.  No work is skipped or added to the product build.
+#ifdef KC_PERSIST_STAMPS
+#ifndef KC_STAMP_LAYER
+#define KC_STAMP_LAYER 18
+#endif
+__device__ unsigned long long g_persist_stamps[1024 * 32];
+#define KC_STAMP(l, i)                                                          \
+    do {                                                                        \
+        if ((l) == KC_STAMP_LAYER && threadIdx.x == 0) {                        \
+            unsigned long long t_;                                              \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)::"memory");    \
+            g_persist_stamps[blockIdx.x * 32 + (i)] = t_;                       \
+        }                                                                       \
+    } while (0)
+extern "C" __attribute__((visibility("default"))) int kc_persist_read_stamps(unsigned long long* out, int n) {
+    return static_cast<int>(cudaMemcpyFromSymbol(out, g_persist_stamps, sizeof(unsigned long long) * n));
+}
+#else
+#define KC_STAMP(l, i) \
+    do {               \
+    } while (0)
+#endif
+
 namespace kc {
 namespace {
 
@@ -401,6 +427,8 @@ __device__ void gemv_op(const PersistArgs& a, int layer, const uint8_t* lut, uin
             ++cgrp;
         }
     }
+    constexpr int kStampBase = OP == kPQkv ? 3 : OP == kPO ? 10 : OP == kPGu ? 15 : 20;
+    KC_STAMP(layer, kStampBase);  // warp 0's chunks done
     if (r.w1 > r.w0 && cblk != 0 && t == 0) {
         float* pp = part + ((cgrp - first_grp) * kPWarps + warp) * 64;
 #pragma unroll
@@ -410,6 +438,7 @@ __device__ void gemv_op(const PersistArgs& a, int layer, const uint8_t* lut, uin
         }
     }
     __syncthreads();
+    KC_STAMP(layer, kStampBase + 1);  // every warp's chunks done
     // fixed-order reduction over the 16 warps -> one slot per touched group
     const int T = r.groups * nbpt;
     for (int idx = tid; idx < nlg * 64; idx += kPThreads) {
@@ -421,6 +450,7 @@ __device__ void gemv_op(const PersistArgs& a, int layer, const uint8_t* lut, uin
         a.gslot[OP][(static_cast<size_t>(grp) * a.gslots + j) * 64 + rr] = v;
     }
     cta_signal(a.counters + layer * kCounterStride + (OP == kPQkv ? kCQkv : OP == kPO ? kCO : OP == kPGu ? kCGu : kCDn));
+    KC_STAMP(layer, kStampBase + 2);  // partials published
 }
 
 // ------------------------------------------------------------------ staging
@@ -919,6 +949,7 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_layers_kernel(const Persi
         const uint64_t* L = a.layers + static_cast<int64_t>(l) * kLayerSlots;
         unsigned* ctr = a.counters + l * kCounterStride;
         const unsigned G = gridDim.x;
+        KC_STAMP(l, 0);
         // ---- RMSNorm + QKV
         norm_prefetch(a, reinterpret_cast<const uint16_t*>(L[kLInNorm]), wv);
         if (a.bias_rows > 0) {  // q, k, v biases of this layer, for the attention CTAs
@@ -939,10 +970,12 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_layers_kernel(const Persi
             residual_from_slots(a, nsl, kPDn, xres);
         }
         __syncthreads();
+        KC_STAMP(l, 1);
         if (l > 0 && tap0)
             for (int i = tid; i < a.hidden; i += kPThreads) layer_taps(a, l - 1)[to.x2 + i] = xres[i];
         stage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn : nullptr);
         __syncthreads();
+        KC_STAMP(l, 2);
         gemv_op<kPQkv>(a, l, lut, ring, bars, ps, cs, xs, part);
         // ---- attention
         if (att_cta) {
@@ -965,31 +998,39 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_layers_kernel(const Persi
                 }
             }
             cta_wait(a, ctr + kCQkv, G);
+            KC_STAMP(l, 6);
             attention_split(a, l, L, nsl, pos_c, kv_len, ap, bias_s, rope_s, work, kvp, kPref);
+            KC_STAMP(l, 7);
         }
         // ---- o_proj (its input: every split of every head)
         norm_prefetch(a, reinterpret_cast<const uint16_t*>(L[kLPostNorm]), wv);
         cta_wait(a, ctr + kCAtt, static_cast<unsigned>(a.kvh * ap.ns));
+        KC_STAMP(l, 8);
         stage_attention(a, rng, ap, xs, tap != nullptr ? tap + to.att : nullptr);
         __syncthreads();
+        KC_STAMP(l, 9);
         for (int i = tid; i < kPartGroups * kPWarps * 64; i += kPThreads) part[i] = 0.F;
         __syncthreads();
         gemv_op<kPO>(a, l, lut, ring, bars, ps, cs, xs, part);
         // ---- residual + RMSNorm + gate/up
         for (int i = tid; i < kPartGroups * kPWarps * 64; i += kPThreads) part[i] = 0.F;
         cta_wait(a, ctr + kCO, G);
+        KC_STAMP(l, 13);
         residual_from_slots(a, nsl, kPO, xres);
         __syncthreads();
         if (tap0)
             for (int i = tid; i < a.hidden; i += kPThreads) tap[to.x1 + i] = xres[i];
         stage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn2 : nullptr);
         __syncthreads();
+        KC_STAMP(l, 14);
         gemv_op<kPGu>(a, l, lut, ring, bars, ps, cs, xs, part);
         // ---- SwiGLU + down
         for (int i = tid; i < kPartGroups * kPWarps * 64; i += kPThreads) part[i] = 0.F;
         cta_wait(a, ctr + kCGu, G);
+        KC_STAMP(l, 18);
         stage_swiglu(a, rng, nsl, xs, tap != nullptr ? tap + to.h : nullptr);
         __syncthreads();
+        KC_STAMP(l, 19);
         gemv_op<kPDn>(a, l, lut, ring, bars, ps, cs, xs, part);
     }
     // ---- the last residual add, written out by CTA 0; then the last CTA to
