@@ -76,7 +76,10 @@ namespace {
 
 constexpr int kPWarps = 16;
 constexpr int kPThreads = kPWarps * 32;
-constexpr int kPMaxSlots = 4;
+#ifndef KC_PERSIST_RING_MAX
+#define KC_PERSIST_RING_MAX 4
+#endif
+constexpr int kPMaxSlots = KC_PERSIST_RING_MAX;  // bulk-copy slots per warp (fewer when shared memory is short)
 constexpr int kChunkCodes = 2048;
 constexpr int kChunkAbs = 256;
 constexpr int kChunkBytes = kChunkCodes + kChunkAbs;
@@ -330,6 +333,15 @@ __device__ __forceinline__ void stream_issue(const PersistArgs& a, Stream& s, in
     mbar_arrive_expect_tx(&bars[slot], kChunkBytes);
     bulk_g2s(dst, codes, kChunkCodes, &bars[slot]);
     bulk_g2s(dst + kChunkCodes, absm, kChunkAbs, &bars[slot]);
+#ifdef KC_PERSIST_L2PF
+    if (s.layer + 1 < a.nlayers) {  // the same chunk of the next layer into L2 (no data returns to the SM)
+        const uint64_t* Ln = L + kLayerSlots;
+        const uint8_t* cn = reinterpret_cast<const uint8_t*>(Ln[2 * s.op]) + static_cast<size_t>(s.c) * kChunkCodes;
+        const uint8_t* an = reinterpret_cast<const uint8_t*>(Ln[2 * s.op + 1]) + static_cast<size_t>(s.c) * kChunkAbs;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(cn), "r"(kChunkCodes) : "memory");
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(an), "r"(kChunkAbs) : "memory");
+    }
+#endif
     ++s.c;
 }
 
@@ -449,6 +461,7 @@ __device__ void gemv_op(const PersistArgs& a, int layer, const uint8_t* lut, uin
         const int j = static_cast<int>(blockIdx.x) - chunk_owner(grp * nbpt, T);
         a.gslot[OP][(static_cast<size_t>(grp) * a.gslots + j) * 64 + rr] = v;
     }
+    KC_STAMP(layer, 23 + OP);  // partial slots written
     cta_signal(a.counters + layer * kCounterStride + (OP == kPQkv ? kCQkv : OP == kPO ? kCO : OP == kPGu ? kCGu : kCDn));
     KC_STAMP(layer, kStampBase + 2);  // partials published
 }
@@ -1205,7 +1218,7 @@ PersistGeom persist_geom(const PersistDims& d, int sms) {
     const int tail = ((d.hidden + 63) & ~63) * 2 + ((g.bias_rows + 63) & ~63) * 2 + d.head_dim * 4;
     const int limit = 232448 - kStaticSmemBudget;
     g.ring_slots = kPMaxSlots;
-    while (g.ring_slots > 2 && kPLutBytes + kPWarps * g.ring_slots * kChunkBytes + g.work_bytes + tail > limit)
+    while (g.ring_slots > 1 && kPLutBytes + kPWarps * g.ring_slots * kChunkBytes + g.work_bytes + tail > limit)
         --g.ring_slots;
     g.smem = kPLutBytes + kPWarps * g.ring_slots * kChunkBytes + g.work_bytes + tail;
     auto up = [](int64_t v) { return (v + 255) & ~static_cast<int64_t>(255); };
