@@ -143,6 +143,47 @@ def quantize_nf4(bridge: KudaCudaBridge, torch: Any, w_bf16: Any, stream_ptr: in
     return NF4Linear(packed, absmax, rows, k)
 
 
+@dataclass(frozen=True)
+class TPShard:
+    """This rank's (start, count) along each tensor-parallel dimension
+    (Megatron-style): ``q`` -- q_proj rows and o_proj K (heads x head_dim);
+    ``kv`` -- k/v rows; ``inter`` -- gate/up rows and down K; ``vocab`` --
+    lm_head rows (vocab-parallel)."""
+
+    q: tuple[int, int]
+    kv: tuple[int, int]
+    inter: tuple[int, int]
+    vocab: tuple[int, int]
+
+
+def tp_shard(config: DecoderConfig, rank: int, world: int) -> TPShard:
+    """The slices rank ``rank`` of ``world`` holds.  Row-parallel K slices
+    (o_proj, down) fall on 64-element NF4 block boundaries, so a shard's codes
+    and absmax are exactly the full matrix's."""
+
+    c = config
+    if not 0 <= rank < world or c.q_heads % world or c.kv_heads % world or c.intermediate % world or c.vocab % world:
+        raise ValueError(f"tensor parallelism over {world} ranks needs q_heads, kv_heads, intermediate and vocab "
+                         f"divisible by {world}")
+    qn, kvn, il, vl = (c.q_heads // world) * c.head_dim, (c.kv_heads // world) * c.head_dim, c.intermediate // world, \
+        c.vocab // world
+    if qn % 64 or il % 64:
+        raise ValueError("row-parallel K slices must be multiples of the NF4 block (64)")
+    return TPShard(q=(rank * qn, qn), kv=(rank * kvn, kvn), inter=(rank * il, il), vocab=(rank * vl, vl))
+
+
+def shard_rows(w: Any, sl: tuple[int, int]) -> Any:
+    """Column-parallel slice: rows [start, start + count) (torch or numpy)."""
+
+    return w[sl[0]:sl[0] + sl[1]]
+
+
+def shard_cols(w: Any, sl: tuple[int, int]) -> Any:
+    """Row-parallel slice: K columns [start, start + count) (torch or numpy)."""
+
+    return w[:, sl[0]:sl[0] + sl[1]]
+
+
 def random_weights(bridge: KudaCudaBridge, config: DecoderConfig, *, seed: int = 20260824, device: Any = "cuda:0",
                    torch_module: Any = None, shard: tuple[int, int] = (0, 1)) -> ModelWeights:
     """Synthetic weights of the BASELINE distribution: linears N(0, 0.02) in
@@ -160,14 +201,13 @@ def random_weights(bridge: KudaCudaBridge, config: DecoderConfig, *, seed: int =
     gen.manual_seed(int(seed))
     stream_ptr = int(torch.cuda.current_stream(device).cuda_stream)
     c = config
-    qh, kvh = c.q_heads // world, c.kv_heads // world
-    i_loc = c.intermediate // world
+    sh = tp_shard(c, rank, world)
 
-    def cols(w: Any, start: int, count: int) -> Any:  # row-parallel: slice K
-        return w[:, start:start + count].contiguous()
+    def cols(w: Any, sl: tuple[int, int]) -> Any:
+        return shard_cols(w, sl).contiguous()
 
-    def rows(w: Any, start: int, count: int) -> Any:  # column-parallel: slice N
-        return w[start:start + count].contiguous()
+    def rows(w: Any, sl: tuple[int, int]) -> Any:
+        return shard_rows(w, sl).contiguous()
 
     layers = []
     for _ in range(c.layers):
@@ -183,22 +223,20 @@ def random_weights(bridge: KudaCudaBridge, config: DecoderConfig, *, seed: int =
         biases = [None, None, None]
         if c.qkv_bias:
             biases = [_randn_bf16(torch, (n,), 0.02, gen, device) for n in (c.q_out, c.kv_out, c.kv_out)]
-        d = c.head_dim
-        q_sl, kv_sl, i_sl = (rank * qh * d, qh * d), (rank * kvh * d, kvh * d), (rank * i_loc, i_loc)
         layers.append(
             LayerWeights(
                 in_norm=in_norm,
                 post_norm=post_norm,
-                q=quantize_nf4(bridge, torch, rows(wq, *q_sl), stream_ptr),
-                k=quantize_nf4(bridge, torch, rows(wk, *kv_sl), stream_ptr),
-                v=quantize_nf4(bridge, torch, rows(wv, *kv_sl), stream_ptr),
-                o=quantize_nf4(bridge, torch, cols(wo, *q_sl), stream_ptr),
-                gate=quantize_nf4(bridge, torch, rows(wg, *i_sl), stream_ptr),
-                up=quantize_nf4(bridge, torch, rows(wu, *i_sl), stream_ptr),
-                down=quantize_nf4(bridge, torch, cols(wd, *i_sl), stream_ptr),
-                q_bias=None if biases[0] is None else rows(biases[0], *q_sl),
-                k_bias=None if biases[1] is None else rows(biases[1], *kv_sl),
-                v_bias=None if biases[2] is None else rows(biases[2], *kv_sl),
+                q=quantize_nf4(bridge, torch, rows(wq, sh.q), stream_ptr),
+                k=quantize_nf4(bridge, torch, rows(wk, sh.kv), stream_ptr),
+                v=quantize_nf4(bridge, torch, rows(wv, sh.kv), stream_ptr),
+                o=quantize_nf4(bridge, torch, cols(wo, sh.q), stream_ptr),
+                gate=quantize_nf4(bridge, torch, rows(wg, sh.inter), stream_ptr),
+                up=quantize_nf4(bridge, torch, rows(wu, sh.inter), stream_ptr),
+                down=quantize_nf4(bridge, torch, cols(wd, sh.inter), stream_ptr),
+                q_bias=None if biases[0] is None else rows(biases[0], sh.q),
+                k_bias=None if biases[1] is None else rows(biases[1], sh.kv),
+                v_bias=None if biases[2] is None else rows(biases[2], sh.kv),
             )
         )
         del wq, wk, wv, wo, wg, wu, wd
@@ -207,8 +245,7 @@ def random_weights(bridge: KudaCudaBridge, config: DecoderConfig, *, seed: int =
     lm_head = None
     if not c.tie_embeddings:  # vocab-parallel: this rank's rows of the NF4 lm_head
         w_lm = _randn_bf16(torch, (c.vocab, c.hidden), 0.02, gen, device)
-        v_loc = c.vocab // world
-        lm_head = quantize_nf4(bridge, torch, rows(w_lm, rank * v_loc, v_loc), stream_ptr)
+        lm_head = quantize_nf4(bridge, torch, rows(w_lm, sh.vocab), stream_ptr)
         del w_lm
     torch.cuda.synchronize(device)
     return ModelWeights(c, layers, embedding, final_norm, lm_head)
