@@ -400,14 +400,15 @@ def time_refcompare(torch, device: str, launches: int, reps: int) -> list[dict]:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
                 for i in range(launches):
-                    fn(lib, h, i, sp)
-            graph.replay()
-            stream.synchronize()
+                    assert fn(lib, h, i, sp) == 0, lib.kudacuda_last_error(h)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record(stream)
-            for _ in range(reps):
+            with torch.cuda.stream(stream):  # replay launches on the current stream: the timed one
                 graph.replay()
-            e.record(stream)
+                stream.synchronize()
+                s.record(stream)
+                for _ in range(reps):
+                    graph.replay()
+                e.record(stream)
             e.synchronize()
             us = s.elapsed_time(e) * 1e3 / (reps * launches)
             row[f"{lname}_us"] = round(us, 3)

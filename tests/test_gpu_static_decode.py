@@ -55,7 +55,7 @@ def _set_linears(torch, model, weights, deq, dtype):
                 mod.weight.copy_(deq(lin, dtype))
 
 
-def _run(layers, vocab, prompt_len, kv_bucket):
+def _run(layers, vocab, prompt_len, kv_bucket, batched=False):
     import torch
     from transformers import DynamicCache
 
@@ -131,14 +131,36 @@ def _run(layers, vocab, prompt_len, kv_bucket):
     first_eager = int(first.item())
     runner.invalidate("test done")
     assert not runner.captured and runner.status == "fallback"
-    bridge.shutdown()
 
     def agree(a, b):
         return sum(int(x == y) for x, y in zip(a, b)) / len(a)
 
     # ours[j] and p32[j + 1] both predict ref[j + 1] (127 positions after the same history)
-    return dict(ours_vs_bf16=agree(ours, ref[1:]), ours_vs_fp32=agree(ours, p32[1:]),
-                fp32_vs_bf16=agree(p32[1:], ref[1:]), first_eager=(first_eager, ref[0]), n=len(ours))
+    out = dict(ours_vs_bf16=agree(ours, ref[1:]), ours_vs_fp32=agree(ours, p32[1:]),
+               fp32_vs_bf16=agree(p32[1:], ref[1:]), first_eager=(first_eager, ref[0]), n=len(ours))
+    if batched:
+        # the batched tensor-core path on the same weights (one sequence): it
+        # rounds every dequantised weight to bf16 and multiplies in bf16 with
+        # fp32 accumulation -- the eager path's arithmetic up to summation order
+        from kudacuda_b200.decode_engine import BatchedDecodePlan
+
+        bbridge = KudaCudaBridge(device_id=0)
+        bplan = BatchedDecodePlan(bbridge, w, batch=1, kv_bucket=kv_bucket, max_tokens=kv_bucket, device="cuda:0")
+        bstream = torch.cuda.Stream()
+        bplan.capture(bstream)
+        bplan.reset_cache()
+        bat = []
+        for pos in range(len(seq) - 1):
+            nxt = bplan.step_tokens([seq[pos]], [pos], bstream)[0]
+            if pos >= prompt_len:  # after ref[pos - prompt_len]: predicts ref[pos - prompt_len + 1]
+                bat.append(nxt)
+        assert bbridge.error_word(clear=True) == 0
+        out.update(batched_vs_bf16=agree(bat, ref[1:]), batched_vs_fp32=agree(bat, p32[1:]))
+        bplan.release()
+        bbridge.reset_graph()
+        bbridge.shutdown()
+    bridge.shutdown()
+    return out
 
 
 def test_runner_two_layer_model_benchmark_flow():
@@ -152,9 +174,13 @@ def test_runner_config3_qwen25_3b_128_greedy_tokens():
     """The north-star agreement check on the bench's model: 36 layers,
     vocabulary 151936, 64-token prompt, KV bucket 512, 128 tokens."""
 
-    r = _run(layers=36, vocab=151936, prompt_len=64, kv_bucket=512)
+    r = _run(layers=36, vocab=151936, prompt_len=64, kv_bucket=512, batched=True)
     print(f"config-3 (Qwen2.5-3B architecture): {r}")
     assert r["first_eager"][0] == r["first_eager"][1] and r["n"] == NEW_TOKENS - 1
-    # on this random-init model the eager path's own fp32-vs-bf16 agreement is
-    # the floor any other arithmetic can be held to
-    assert r["ours_vs_bf16"] >= r["fp32_vs_bf16"] - 0.05, r
+    # On this random-init model the eager path's own fp32-vs-bf16 agreement
+    # (measured: 0.85) is the floor any other arithmetic can be held to; 127
+    # positions give a standard error of ~0.035, so the bar is the floor
+    # minus 0.08 (about two standard errors).
+    floor = r["fp32_vs_bf16"]
+    for key in ("ours_vs_bf16", "ours_vs_fp32", "batched_vs_bf16", "batched_vs_fp32"):
+        assert r[key] >= floor - 0.08, (key, r)
