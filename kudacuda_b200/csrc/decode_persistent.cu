@@ -46,20 +46,23 @@
 #include "kc_launch.h"
 
 // Phase timestamps for profiling builds only (-DKC_PERSIST_STAMPS; off in the
-// library): thread 0 of every CTA records %globaltimer at fixed points of one
-// layer (KC_STAMP_LAYER) into g_persist_stamps[cta][32], read back with
-// kc_persist_read_stamps.  No work is skipped or added to the product build.
+// library): thread 0 of every CTA records %globaltimer (comparable across
+// SMs) and clock64 (this SM's cycle counter) at fixed points of one layer
+// (KC_STAMP_LAYER) into g_persist_stamps[cta][64] (timer in [0, 32), cycles
+// in [32, 64)), read back with kc_persist_read_stamps.  No work is skipped or
+// added to the product build.
 #ifdef KC_PERSIST_STAMPS
 #ifndef KC_STAMP_LAYER
 #define KC_STAMP_LAYER 18
 #endif
-__device__ unsigned long long g_persist_stamps[1024 * 32];
+__device__ unsigned long long g_persist_stamps[1024 * 64];
 #define KC_STAMP(l, i)                                                          \
     do {                                                                        \
         if ((l) == KC_STAMP_LAYER && threadIdx.x == 0) {                        \
             unsigned long long t_;                                              \
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)::"memory");    \
-            g_persist_stamps[blockIdx.x * 32 + (i)] = t_;                       \
+            g_persist_stamps[blockIdx.x * 64 + (i)] = t_;                       \
+            g_persist_stamps[blockIdx.x * 64 + 32 + (i)] = clock64();           \
         }                                                                       \
     } while (0)
 extern "C" __attribute__((visibility("default"))) int kc_persist_read_stamps(unsigned long long* out, int n) {
