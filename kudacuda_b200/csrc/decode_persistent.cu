@@ -88,7 +88,7 @@ constexpr int kChunkAbs = 256;
 constexpr int kChunkBytes = kChunkCodes + kChunkAbs;
 constexpr int kPLutBytes = 65536;  // 256 entry rows x 256 B, lane replicas in the first 128 B of a row
 constexpr int kPartGroups = 5;     // row groups one CTA may touch in one op (checked on the host)
-constexpr int kAttTile = 16;       // tokens per attention tile (and per split, up to kAttMaxSplits splits)
+constexpr int kAttTile = 64;       // tokens per attention tile (a split covers one or more tiles)
 constexpr int kAttMaxSplits = 32;  // splits per KV head
 constexpr int kMaxGroups = 512;    // row groups per op (checked on the host)
 constexpr int kCounterStride = 8;  // per layer: 0 qkv, 1 attention, 2 o_proj, 3 gate/up, 4 down
@@ -192,7 +192,6 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
     asm volatile("fence.acq_rel.gpu;\n\tred.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint4 ldcg_u4(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
 
 // Thread 0 waits until *ctr >= target (or the step was aborted); then the
 // whole CTA continues (the barrier orders every thread's later reads after
@@ -442,7 +441,7 @@ __device__ void gemv_op(const PersistArgs& a, int layer, const uint8_t* lut, uin
             ++cgrp;
         }
     }
-    constexpr int kStampBase = OP == kPQkv ? 3 : OP == kPO ? 10 : OP == kPGu ? 15 : 20;
+    [[maybe_unused]] constexpr int kStampBase = OP == kPQkv ? 3 : OP == kPO ? 10 : OP == kPGu ? 15 : 20;
     KC_STAMP(layer, kStampBase);  // warp 0's chunks done
     if (r.w1 > r.w0 && cblk != 0 && t == 0) {
         float* pp = part + ((cgrp - first_grp) * kPWarps + warp) * 64;
@@ -569,6 +568,14 @@ __device__ void stage_swiglu(const PersistArgs& a, const int* rng, const uint8_t
 }
 
 // ------------------------------------------------------------------ attention
+// A split of one KV head covers ts tokens (a multiple of kAttTile) in tiles of
+// kAttTile tokens.  The tile's K and V rows land in padded shared rows by
+// per-row bulk copies (the first tile's are issued before the split waits for
+// q), then scores and P.V run on the tensor core, as in the cluster GQA
+// kernel (gqa_decode.cu): mma.m16n8k16 bf16 with the group's query heads in
+// A rows 0..gq-1 and 8 tokens per n-tile, q and K exact in bf16 with fp32
+// accumulation; P split into bf16 hi + lo halves (P = hi + lo to ~16
+// significant bits) against ldmatrix.trans V fragments.
 struct AttPlan {
     int ns, ts;  // splits per KV head, tokens per split (a multiple of kAttTile)
 };
@@ -582,28 +589,59 @@ __device__ __forceinline__ AttPlan att_plan(const PersistArgs& a, int kv_len) {
     return p;
 }
 
-constexpr int kKRow = 136;  // padded K row in shared memory (bf16): 272 bytes, so 16-byte row reads do not conflict
+constexpr int kKRow = 136;  // padded K/V/q row in shared memory (bf16): 272 bytes, conflict-free fragment loads
 
 struct AttSmem {
-    float* qf;    // [gq][hd], scaled by scale * log2(e)
-    float* sc;    // [gq][kAttTile]: scores, then probabilities
-    float* ml;    // [gq][4]: running max, sum, correction
-    float* knew;  // [hd]
-    float* vnew;  // [hd]
-    uint16_t* kt; // [kAttTile][kKRow]
-    uint16_t* vt; // [kAttTile][hd]
+    uint16_t* kt;  // [kAttTile][kKRow]
+    uint16_t* vt;  // [kAttTile][kKRow]
+    uint16_t* qb;  // [8][kKRow]: the group's q rows (bf16, unscaled), rows >= gq zero
+    float* ss;     // [2][8][kAttTile]: score halves (dims 0-63, 64-127), then probabilities in [0]
+    float* ml;     // [8][4]: running max, sum, correction
+    float* knew;   // [hd]
+    float* vnew;   // [hd]
 };
-__device__ __forceinline__ AttSmem att_smem(const PersistArgs& a, uint8_t* work) {
-    const int gq = a.qh / a.kvh, hd = a.hd;
+constexpr int kAttSmemBytes = 2 * kAttTile * kKRow * 2 + 8 * kKRow * 2 + 2 * 8 * kAttTile * 4 + 8 * 4 * 4 + 2 * 128 * 4;
+__device__ __forceinline__ AttSmem att_smem(uint8_t* work) {
     AttSmem s;
-    s.qf = reinterpret_cast<float*>(work);
-    s.sc = s.qf + gq * hd;
-    s.ml = s.sc + gq * kAttTile;
-    s.knew = s.ml + gq * 4;
-    s.vnew = s.knew + hd;
-    s.kt = reinterpret_cast<uint16_t*>(s.vnew + hd);
+    s.kt = reinterpret_cast<uint16_t*>(work);
     s.vt = s.kt + kAttTile * kKRow;
+    s.qb = s.vt + kAttTile * kKRow;
+    s.ss = reinterpret_cast<float*>(s.qb + 8 * kKRow);
+    s.ml = s.ss + 2 * 8 * kAttTile;
+    s.knew = s.ml + 8 * 4;
+    s.vnew = s.knew + 128;
     return s;
+}
+
+// Warp 0 (all lanes) issues the bulk copies of K and V rows [t0, t0 + nt) of
+// one KV head into the padded tile rows, completing on `bar`.  The caller
+// has ordered every earlier access to the tile rows before this (a CTA
+// barrier after a proxy fence).
+__device__ __forceinline__ void att_issue_tile(const uint16_t* kc, const uint16_t* vc, int t0, int nt,
+                                               const AttSmem& sm, uint64_t* bar) {
+    const int lane = threadIdx.x & 31;
+    if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nt) * 512u);
+    __syncwarp();
+    for (int r = lane; r < nt; r += 32) {
+        bulk_g2s(sm.kt + r * kKRow, kc + static_cast<int64_t>(t0 + r) * 128, 256u, bar);
+        bulk_g2s(sm.vt + r * kKRow, vc + static_cast<int64_t>(t0 + r) * 128, 256u, bar);
+    }
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t& r0, uint32_t& r1, uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+// P pair -> bf16 hi pair and lo pair with p = hi + lo
+__device__ __forceinline__ void split_bf16_pair(float p0, float p1, uint32_t& hi, uint32_t& lo) {
+    const float h0 = round_bf16(p0), h1 = round_bf16(p1);
+    hi = static_cast<uint32_t>(f32_to_bf16_bits(h0)) | (static_cast<uint32_t>(f32_to_bf16_bits(h1)) << 16);
+    lo = static_cast<uint32_t>(f32_to_bf16_bits(p0 - h0)) | (static_cast<uint32_t>(f32_to_bf16_bits(p1 - h1)) << 16);
 }
 
 // QKV group row of q/k element (head, i) for i < hd/2; its RoPE partner is 32 rows on
@@ -612,25 +650,26 @@ __device__ __forceinline__ void rope_group_row(int hd, int head, int i, int base
     rr = i & 31;
 }
 
-// One split (KV head hk, tokens [tok0, tok1)) of one layer: q and the new
-// k/v row from the QKV slots (bias, RoPE, Transformers' rounding), then per
-// 64-token tile: one thread per (head, token) score, one warp per head for the
-// online softmax (log2 domain), one thread per (head, dim pair) for P.V with
-// the accumulator in registers; partial (max, sum, acc) out.
+// One split (KV head hk, tokens [tok0, tok1)) of one layer: q and the new k/v
+// row from the QKV slots (bias, RoPE, Transformers' rounding), the tiles'
+// scores, a chunk softmax per head (log2 domain, online across tiles) and
+// P.V; then the partial (max, sum, acc) per query head.  The first tile's
+// copies were issued by the caller on `bar` (parity `phase`).
 __device__ void attention_split(const PersistArgs& a, int layer, const uint64_t* L, const uint8_t* nsl, int pos,
                                 int kv_len, const AttPlan& ap, const uint16_t* bias_s, const float* rope_s,
-                                uint8_t* work, const uint4* kv_pref, int npref) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+                                const AttSmem& sm, uint64_t* bar, uint32_t& phase) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int gq = a.qh / a.kvh, hd = a.hd, half = hd / 2;
     const int hk = static_cast<int>(blockIdx.x) / ap.ns, s = static_cast<int>(blockIdx.x) - hk * ap.ns;
     const int tok0 = s * ap.ts, tok1 = min(kv_len, tok0 + ap.ts);
-    const AttSmem sm = att_smem(a, work);
     const int qg = a.qh * (hd / 64), kg = a.kvh * (hd / 64);
     const bool bias = a.bias_rows > 0;
     uint16_t* tap = s == 0 ? layer_taps(a, layer) : nullptr;
     const TapOffsets to = tap_offsets(a);
+    uint16_t* kc = reinterpret_cast<uint16_t*>(L[kLKCache]) + static_cast<int64_t>(hk) * a.cap * hd;
+    uint16_t* vc = reinterpret_cast<uint16_t*>(L[kLVCache]) + static_cast<int64_t>(hk) * a.cap * hd;
 
-    // q (gq heads) and k_new: four RoPE pairs (i .. i+3, i+half .. i+half+3) per thread;
+    // q (gq heads, bf16 into qb) and k_new: four RoPE pairs (i .. i+3, i+half .. i+half+3) per thread;
     // v_new: four plain rows per thread
     const int nq4 = (gq + 1) * (half / 4), nv4 = hd / 4;
     for (int idx = tid; idx < nq4 + nv4; idx += kPThreads) {
@@ -657,16 +696,16 @@ __device__ void attention_split(const PersistArgs& a, int layer, const uint64_t*
                 const float hi = round_bf16(round_bf16(y1 * c) + round_bf16(y0 * sn));
                 if (isq) {
                     const int hq = head - hk * gq;
-                    sm.qf[hq * hd + i + k] = lo * a.scale_log2;
-                    sm.qf[hq * hd + i + k + half] = hi * a.scale_log2;
+                    sm.qb[hq * kKRow + i + k] = f32_to_bf16_bits(lo);
+                    sm.qb[hq * kKRow + i + k + half] = f32_to_bf16_bits(hi);
                 } else {
                     sm.knew[i + k] = lo;
                     sm.knew[i + k + half] = hi;
                 }
                 if (tap != nullptr) {
-                    uint16_t* t = tap + (isq ? to.q : to.k) + head * hd + i + k;
-                    t[0] = f32_to_bf16_bits(lo);
-                    t[half] = f32_to_bf16_bits(hi);
+                    uint16_t* tp = tap + (isq ? to.q : to.k) + head * hd + i + k;
+                    tp[0] = f32_to_bf16_bits(lo);
+                    tp[half] = f32_to_bf16_bits(hi);
                 }
             }
         } else {
@@ -682,194 +721,207 @@ __device__ void attention_split(const PersistArgs& a, int layer, const uint64_t*
             }
         }
     }
-    if (tid < gq) {
+    for (int i = gq * hd + tid; i < 8 * hd; i += kPThreads) sm.qb[(i / hd) * kKRow + i % hd] = 0;  // A rows >= gq
+    if (tid < 8) {
         sm.ml[tid * 4 + 0] = -INFINITY;
         sm.ml[tid * 4 + 1] = 0.F;
+        sm.ml[tid * 4 + 2] = 1.F;
     }
-    const uint16_t* kc = reinterpret_cast<const uint16_t*>(L[kLKCache]) + static_cast<int64_t>(hk) * a.cap * hd;
-    const uint16_t* vc = reinterpret_cast<const uint16_t*>(L[kLVCache]) + static_cast<int64_t>(hk) * a.cap * hd;
-    const int per_row = hd / 8;  // uint4 per row
-    const bool pv_thread = tid < gq * (hd / 2);
-    const int phq = tid / (hd / 2), pdp = tid % (hd / 2);  // P.V: head, dim pair
-    float acc0 = 0.F, acc1 = 0.F;
+    __syncthreads();
+    // q A fragments (rows 8..15 of A are zero): k-step s8 covers dims 16*s8 .. 16*s8+15
+    uint32_t qa[8][2];
+    {
+        const uint32_t* qw = reinterpret_cast<const uint32_t*>(sm.qb + g * kKRow);
+#pragma unroll
+        for (int s8 = 0; s8 < 8; ++s8) {
+            qa[s8][0] = qw[8 * s8 + t];
+            qa[s8][1] = qw[8 * s8 + t + 4];
+        }
+    }
+    float o0[4] = {0.F, 0.F, 0.F, 0.F}, o1[4] = {0.F, 0.F, 0.F, 0.F};  // warp w: dims 8w .. 8w+7 of head g
+    const uint32_t vbase = smem_u32(sm.vt) + static_cast<uint32_t>((lane & 15) * kKRow * 2 + 16 * warp);
     for (int t0 = tok0; t0 < tok1; t0 += kAttTile) {
         const int nt = min(kAttTile, tok1 - t0);
-        auto put = [&](int o, uint4 v) {
-            if (o < nt * per_row) {
-                *reinterpret_cast<uint4*>(sm.kt + (o / per_row) * kKRow + 8 * (o % per_row)) = v;
-            } else {
-                reinterpret_cast<uint4*>(sm.vt)[o - nt * per_row] = v;
+        if (t0 != tok0) {  // every thread is done with the previous tile's rows
+            fence_proxy_async_smem();
+            __syncthreads();
+            if (warp == 0) att_issue_tile(kc, vc, t0, nt, sm, bar);
+        }
+        if (!mbar_wait_bounded(bar, phase)) {
+            if (tid == 0) {
+                atomicExch(a.misc, 1u);
+                atomicOr(a.err, 16);
             }
-        };
-        if (t0 == tok0) {  // the first tile was fetched before the dependency wait
-            for (int j = 0; j < npref; ++j) {
-                const int o = tid + j * kPThreads;
-                if (o < 2 * nt * per_row) put(o, kv_pref[j]);
-            }
-        } else {
-            for (int o = tid; o < 2 * nt * per_row; o += kPThreads) {
-                const bool isk = o < nt * per_row;
-                const int oo = isk ? o : o - nt * per_row;
-                put(o, ldcg_u4((isk ? kc : vc) + static_cast<int64_t>(t0) * hd + 8 * oo));
+            for (int retry = 0; retry < 8 && !mbar_wait_bounded(bar, phase); ++retry) {
             }
         }
-        __syncthreads();
+        phase ^= 1u;
+        const int n16 = (nt + 15) & ~15;
         if (pos >= t0 && pos < t0 + nt) {  // this step's row: computed above, also appended to the caches
             for (int d = tid; d < hd; d += kPThreads) {
                 const uint16_t kb = f32_to_bf16_bits(sm.knew[d]), vb = f32_to_bf16_bits(sm.vnew[d]);
                 sm.kt[(pos - t0) * kKRow + d] = kb;
-                sm.vt[(pos - t0) * hd + d] = vb;
-                reinterpret_cast<uint16_t*>(L[kLKCache])[(static_cast<int64_t>(hk) * a.cap + pos) * hd + d] = kb;
-                reinterpret_cast<uint16_t*>(L[kLVCache])[(static_cast<int64_t>(hk) * a.cap + pos) * hd + d] = vb;
+                sm.vt[(pos - t0) * kKRow + d] = vb;
+                kc[static_cast<int64_t>(pos) * hd + d] = kb;
+                vc[static_cast<int64_t>(pos) * hd + d] = vb;
             }
-            __syncthreads();
         }
-        // scores: thread (head, token) -- a 128-long dot with four partial sums (hd == 128)
-        if (tid < gq * kAttTile) {
-            const int hq = tid / kAttTile, tk = tid % kAttTile;
-            float sv = -INFINITY;
-            if (tk < nt) {
-                const float4* qv = reinterpret_cast<const float4*>(sm.qf + hq * hd);
-                const uint4* kv = reinterpret_cast<const uint4*>(sm.kt + tk * kKRow);
-                float p0 = 0.F, p1 = 0.F, p2 = 0.F, p3 = 0.F;
-#pragma unroll 4
-                for (int c = 0; c < hd / 8; ++c) {
-                    const uint4 k8 = kv[c];
-                    const float4 qa = qv[2 * c], qb = qv[2 * c + 1];
-                    p0 = fmaf(qa.x, bf16_bits_to_f32(static_cast<uint16_t>(k8.x & 0xffffu)), p0);
-                    p1 = fmaf(qa.y, bf16_bits_to_f32(static_cast<uint16_t>(k8.x >> 16)), p1);
-                    p2 = fmaf(qa.z, bf16_bits_to_f32(static_cast<uint16_t>(k8.y & 0xffffu)), p2);
-                    p3 = fmaf(qa.w, bf16_bits_to_f32(static_cast<uint16_t>(k8.y >> 16)), p3);
-                    p0 = fmaf(qb.x, bf16_bits_to_f32(static_cast<uint16_t>(k8.z & 0xffffu)), p0);
-                    p1 = fmaf(qb.y, bf16_bits_to_f32(static_cast<uint16_t>(k8.z >> 16)), p1);
-                    p2 = fmaf(qb.z, bf16_bits_to_f32(static_cast<uint16_t>(k8.w & 0xffffu)), p2);
-                    p3 = fmaf(qb.w, bf16_bits_to_f32(static_cast<uint16_t>(k8.w >> 16)), p3);
-                }
-                sv = (p0 + p1) + (p2 + p3);
+        // V rows nt .. n16-1 take part in the last P.V k-step with P = 0: make them finite
+        for (int i = tid; i < (n16 - nt) * (hd / 2); i += kPThreads)
+            reinterpret_cast<uint32_t*>(sm.vt + (nt + i / (hd / 2)) * kKRow)[i % (hd / 2)] = 0u;
+        __syncthreads();
+        // scores: unit (n-tile of 8 tokens, dim half) per warp, two accumulators over the half's four k-steps
+        if (warp < (n16 >> 3) * 2) {
+            const int ntl = warp >> 1, hf = warp & 1;
+            float c0[4] = {0.F, 0.F, 0.F, 0.F}, c1[4] = {0.F, 0.F, 0.F, 0.F};
+            const uint8_t* krow = reinterpret_cast<const uint8_t*>(sm.kt) + (ntl * 8 + g) * kKRow * 2 + 4 * t + 128 * hf;
+#pragma unroll
+            for (int s4 = 0; s4 < 4; s4 += 2) {
+                const uint32_t qA0 = hf ? qa[4 + s4][0] : qa[s4][0], qA1 = hf ? qa[4 + s4][1] : qa[s4][1];
+                const uint32_t qB0 = hf ? qa[5 + s4][0] : qa[s4 + 1][0], qB1 = hf ? qa[5 + s4][1] : qa[s4 + 1][1];
+                mma_bf16_16816(c0, qA0, 0u, qA1, 0u, *reinterpret_cast<const uint32_t*>(krow + 32 * s4),
+                               *reinterpret_cast<const uint32_t*>(krow + 32 * s4 + 16));
+                mma_bf16_16816(c1, qB0, 0u, qB1, 0u, *reinterpret_cast<const uint32_t*>(krow + 32 * s4 + 32),
+                               *reinterpret_cast<const uint32_t*>(krow + 32 * s4 + 48));
             }
-            sm.sc[hq * kAttTile + tk] = sv;
+            if (g < gq) {
+                *reinterpret_cast<float2*>(sm.ss + (hf * 8 + g) * kAttTile + ntl * 8 + 2 * t) =
+                    make_float2((c0[0] + c1[0]) * a.scale_log2, (c0[1] + c1[1]) * a.scale_log2);
+            }
         }
         __syncthreads();
-        if (warp < gq) {  // online softmax over the tile, one warp per query head (one token per lane)
-            const float v0 = lane < kAttTile ? sm.sc[warp * kAttTile + lane] : -INFINITY;
-            const float mx = warp_max(v0);
+        // online softmax per head over the tile (log2 domain); probabilities zero past nt
+        if (warp < gq) {
+            float v[2];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int j = lane + 32 * k;
+                v[k] = j < nt ? sm.ss[warp * kAttTile + j] + sm.ss[(8 + warp) * kAttTile + j] : -INFINITY;
+                mx = fmaxf(mx, v[k]);
+            }
+            mx = warp_max(mx);
             const float m_old = sm.ml[warp * 4 + 0];
             const float m_new = fmaxf(m_old, mx);
-            const float e0 = lane < nt ? exp2f(v0 - m_new) : 0.F;
-            const float ls = warp_sum(e0);
-            if (lane < kAttTile) sm.sc[warp * kAttTile + lane] = e0;
+            float ls = 0.F;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int j = lane + 32 * k;
+                const float p = j < nt ? exp2f(v[k] - m_new) : 0.F;
+                if (j < n16) sm.ss[warp * kAttTile + j] = p;
+                ls += p;
+            }
+            ls = warp_sum(ls);
             if (lane == 0) {
-                const float corr = exp2f(m_old - m_new);
+                const float corr = m_old == -INFINITY ? 0.F : exp2f(m_old - m_new);
                 sm.ml[warp * 4 + 0] = m_new;
                 sm.ml[warp * 4 + 1] = sm.ml[warp * 4 + 1] * corr + ls;
                 sm.ml[warp * 4 + 2] = corr;
             }
         }
         __syncthreads();
-        if (pv_thread) {  // P.V for one (head, dim pair), four interleaved chains
-            const float corr = sm.ml[phq * 4 + 2];
-            const float* pr = sm.sc + phq * kAttTile;
-            const uint32_t* vr = reinterpret_cast<const uint32_t*>(sm.vt) + pdp;
-            float a0[2] = {0.F, 0.F}, a1[2] = {0.F, 0.F};
-            int tk = 0;
-            for (; tk + 1 < nt; tk += 2) {
-                const uint32_t va = vr[tk * (hd / 2)], vb = vr[(tk + 1) * (hd / 2)];
-                a0[0] = fmaf(pr[tk], bf16_bits_to_f32(static_cast<uint16_t>(va & 0xffffu)), a0[0]);
-                a1[0] = fmaf(pr[tk], bf16_bits_to_f32(static_cast<uint16_t>(va >> 16)), a1[0]);
-                a0[1] = fmaf(pr[tk + 1], bf16_bits_to_f32(static_cast<uint16_t>(vb & 0xffffu)), a0[1]);
-                a1[1] = fmaf(pr[tk + 1], bf16_bits_to_f32(static_cast<uint16_t>(vb >> 16)), a1[1]);
+        // P.V: warp w owns dims 8w .. 8w+7; k-steps of 16 tokens alternate between two accumulators
+        if (warp < hd / 8) {
+            const float corr = g < gq ? sm.ml[g * 4 + 2] : 1.F;
+            o0[0] *= corr;
+            o0[1] *= corr;
+            o1[0] *= corr;
+            o1[1] *= corr;
+            const float* prow = sm.ss + (g < gq ? g : 0) * kAttTile + 2 * t;
+            const int nk = n16 >> 4;
+            for (int kk = 0; kk < nk; kk += 2) {
+                const bool two = kk + 1 < nk;
+                uint32_t b0, b1, b2 = 0u, b3 = 0u;
+                ldsm_x2_trans(b0, b1, vbase + static_cast<uint32_t>(kk * 16 * kKRow * 2));
+                if (two) ldsm_x2_trans(b2, b3, vbase + static_cast<uint32_t>((kk + 1) * 16 * kKRow * 2));
+                float2 pa = make_float2(0.F, 0.F), pb = pa, pc = pa, pd = pa;
+                if (g < gq) {
+                    pa = *reinterpret_cast<const float2*>(prow + kk * 16);
+                    pb = *reinterpret_cast<const float2*>(prow + kk * 16 + 8);
+                    if (two) {
+                        pc = *reinterpret_cast<const float2*>(prow + kk * 16 + 16);
+                        pd = *reinterpret_cast<const float2*>(prow + kk * 16 + 24);
+                    }
+                }
+                uint32_t ah0, al0, ah2, al2, ch0, cl0, ch2, cl2;
+                split_bf16_pair(pa.x, pa.y, ah0, al0);
+                split_bf16_pair(pb.x, pb.y, ah2, al2);
+                split_bf16_pair(pc.x, pc.y, ch0, cl0);
+                split_bf16_pair(pd.x, pd.y, ch2, cl2);
+                mma_bf16_16816(o0, ah0, 0u, ah2, 0u, b0, b1);
+                if (two) mma_bf16_16816(o1, ch0, 0u, ch2, 0u, b2, b3);
+                mma_bf16_16816(o0, al0, 0u, al2, 0u, b0, b1);
+                if (two) mma_bf16_16816(o1, cl0, 0u, cl2, 0u, b2, b3);
             }
-            if (tk < nt) {
-                const uint32_t va = vr[tk * (hd / 2)];
-                a0[0] = fmaf(pr[tk], bf16_bits_to_f32(static_cast<uint16_t>(va & 0xffffu)), a0[0]);
-                a1[0] = fmaf(pr[tk], bf16_bits_to_f32(static_cast<uint16_t>(va >> 16)), a1[0]);
-            }
-            acc0 = acc0 * corr + (a0[0] + a0[1]);
-            acc1 = acc1 * corr + (a1[0] + a1[1]);
         }
-        __syncthreads();
     }
     const int rec = hd + 4;
     float* mine = a.apart + ((static_cast<size_t>(hk) * kAttMaxSplits + s) * gq) * rec;
-    if (pv_thread) {
-        mine[phq * rec + 4 + 2 * pdp] = acc0;
-        mine[phq * rec + 4 + 2 * pdp + 1] = acc1;
-        if (pdp == 0) {
-            mine[phq * rec + 0] = sm.ml[phq * 4 + 0];
-            mine[phq * rec + 1] = sm.ml[phq * 4 + 1];
-        }
+    if (warp < hd / 8 && g < gq)
+        *reinterpret_cast<float2*>(mine + g * rec + 4 + 8 * warp + 2 * t) = make_float2(o0[0] + o1[0], o0[1] + o1[1]);
+    if (tid < gq) {
+        mine[tid * rec + 0] = sm.ml[tid * 4 + 0];
+        mine[tid * rec + 1] = sm.ml[tid * 4 + 1];
     }
     cta_signal(a.counters + layer * kCounterStride + kCAtt);
 }
 
 // xs = f16(attention output) for the input blocks this CTA's share of o_proj
-// reads.  Four lanes per four outputs, each merging up to 8 splits' (max, sum,
-// acc) with its loads all in flight, then a shuffle merge -- the order of the
-// merge is fixed, so the result is deterministic.
-__device__ __forceinline__ void merge_att(float& M, float& den, float4& num, float m2, float d2, float4 n2) {
-    const float Mn = fmaxf(M, m2);
-    const float c1 = M == -INFINITY ? 0.F : exp2f(M - Mn);
-    const float c2 = m2 == -INFINITY ? 0.F : exp2f(m2 - Mn);
-    den = den * c1 + d2 * c2;
-    num.x = num.x * c1 + n2.x * c2;
-    num.y = num.y * c1 + n2.y * c2;
-    num.z = num.z * c1 + n2.z * c2;
-    num.w = num.w * c1 + n2.w * c2;
-    M = Mn;
-}
-__device__ void stage_attention(const PersistArgs& a, const int* rng, const AttPlan& ap, uint16_t* xs, uint16_t* tap) {
-    const BlockSet bs = op_blocks(a, rng, kPO);
+// reads.  First every (query head, split) pair's softmax weight w = 2^(m -
+// M) / sum_s 2^(m_s - M) l_s is formed once (one warp per head, one lane per
+// split, at most 32 splits) into shared memory; then four lanes per output
+// quad sum w x acc over disjoint split subsets with float4 loads of the
+// accumulators and a fixed shuffle order -- every CTA forms the same bits.
+__device__ void stage_attention(const PersistArgs& a, const int* rng, const AttPlan& ap, uint16_t* xs, float* wn,
+                                uint16_t* tap) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int gq = a.qh / a.kvh, hd = a.hd, rec = hd + 4;
+    for (int head = warp; head < a.qh; head += kPWarps) {
+        const int hk = head / gq, hq = head - hk * gq;
+        const float* p = a.apart + ((static_cast<size_t>(hk) * kAttMaxSplits + lane) * gq + hq) * rec;
+        const bool live = lane < ap.ns;
+        const float m = live ? __ldcg(p) : -INFINITY;
+        const float l = live ? __ldcg(p + 1) : 0.F;
+        const float M = warp_max(m);
+        const float e = live && m != -INFINITY ? exp2f(m - M) : 0.F;
+        const float den = warp_sum(e * l);
+        wn[head * kAttMaxSplits + lane] = den > 0.F ? e / den : 0.F;
+    }
+    __syncthreads();
+    const BlockSet bs = op_blocks(a, rng, kPO);
     bool overflow = false;
     const int nq = bs.n * 16;  // output quads
     // every lane of a warp runs the same trip count (the shuffles need all 32)
     for (int base = 0; base < nq * 4; base += kPThreads) {
-        const int idx = base + static_cast<int>(threadIdx.x);
+        const int idx = base + tid;
         const bool live = idx < nq * 4;
         const int quad = live ? idx >> 2 : 0, part = idx & 3;
         const int b = (bs.lo + (quad >> 4)) % bs.nbpt;
         const int i = 64 * b + 4 * (quad & 15);  // four consecutive outputs of one head
         const int head = i / hd, d = i - head * hd, hk = head / gq, hq = head - hk * gq;
-        const float* base_p = a.apart + (static_cast<size_t>(hk) * kAttMaxSplits * gq + hq) * rec;
-        float ms[8], ls[8];
-        float4 av[8];
+        const float* base_p = a.apart + (static_cast<size_t>(hk) * kAttMaxSplits * gq + hq) * rec + 4 + d;
+        float4 acc = make_float4(0.F, 0.F, 0.F, 0.F);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int sidx = 8 * part + k;
-            const bool ok = live && sidx < ap.ns;
-            const float* rj = base_p + static_cast<size_t>(sidx) * gq * rec;
-            ms[k] = ok ? __ldcg(rj) : -INFINITY;
-            ls[k] = ok ? __ldcg(rj + 1) : 0.F;
-            av[k] = ok ? __ldcg(reinterpret_cast<const float4*>(rj + 4 + d)) : make_float4(0.F, 0.F, 0.F, 0.F);
-        }
-        float M = -INFINITY, den = 0.F;
-        float4 num = make_float4(0.F, 0.F, 0.F, 0.F);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) merge_att(M, den, num, ms[k], ls[k], av[k]);
-#pragma unroll
-        for (int o = 1; o <= 2; o <<= 1) {
-            const float m2 = __shfl_xor_sync(0xffffffffu, M, o), d2 = __shfl_xor_sync(0xffffffffu, den, o);
-            float4 n2;
-            n2.x = __shfl_xor_sync(0xffffffffu, num.x, o);
-            n2.y = __shfl_xor_sync(0xffffffffu, num.y, o);
-            n2.z = __shfl_xor_sync(0xffffffffu, num.z, o);
-            n2.w = __shfl_xor_sync(0xffffffffu, num.w, o);
-            // the lower part index always merges first, so every lane of the four gets the same bits
-            if ((part & o) == 0) {
-                merge_att(M, den, num, m2, d2, n2);
-            } else {
-                float Mo = m2, dno = d2;
-                float4 nmo = n2;
-                merge_att(Mo, dno, nmo, M, den, num);
-                M = Mo;
-                den = dno;
-                num = nmo;
+        for (int k = 0; k < kAttMaxSplits / 4; ++k) {
+            const int sidx = part + 4 * k;
+            if (live && sidx < ap.ns) {
+                const float w = wn[head * kAttMaxSplits + sidx];
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(base_p + static_cast<size_t>(sidx) * gq * rec));
+                acc.x = fmaf(w, v.x, acc.x);
+                acc.y = fmaf(w, v.y, acc.y);
+                acc.z = fmaf(w, v.z, acc.z);
+                acc.w = fmaf(w, v.w, acc.w);
             }
         }
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {  // (p0 + p1) + (p2 + p3), the same order on every lane
+            acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+            acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+            acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
+            acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
+        }
         if (live && part == 0) {
-            const float inv = 1.0F / den;
-            const float o4[4] = {round_bf16(num.x * inv), round_bf16(num.y * inv), round_bf16(num.z * inv),
-                                 round_bf16(num.w * inv)};
+            const float o4[4] = {round_bf16(acc.x), round_bf16(acc.y), round_bf16(acc.z), round_bf16(acc.w)};
             uint16_t hb[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -887,6 +939,7 @@ __device__ void stage_attention(const PersistArgs& a, const int* rng, const AttP
 __global__ void __launch_bounds__(kPThreads, 1) decode_layers_kernel(const PersistArgs a) {
     extern __shared__ __align__(128) uint8_t dsm[];
     __shared__ __align__(8) uint64_t bars_all[kPWarps * kPMaxSlots];
+    __shared__ __align__(8) uint64_t att_bar;  // attention tile copies
     __shared__ float red[kPWarps];
     __shared__ uint8_t nsl[4 * kMaxGroups];  // slots per row group, per op
     __shared__ int rng[4 * kRangeStride];    // chunk ranges of this CTA and its warps, per op
@@ -918,6 +971,7 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_layers_kernel(const Persi
     ps.done = a.nlayers < 1;
     if (lane == 0) {
         for (int s = 0; s < a.ring_slots; ++s) mbar_init(&bars[s], 1);
+        if (warp == 0) mbar_init(&att_bar, 1);
         fence_mbar_init();
         for (int s = 0; s < a.ring_slots; ++s) stream_issue(a, ps, warp, ring, bars, s);
     }
@@ -955,6 +1009,7 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_layers_kernel(const Persi
     __syncthreads();
     const AttPlan ap = att_plan(a, kv_len);
     const bool att_cta = static_cast<int>(blockIdx.x) < a.kvh * ap.ns;
+    uint32_t att_phase = 0;
 
     ConsumerState cs;
     cs.slot = 0;
@@ -995,34 +1050,25 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_layers_kernel(const Persi
         gemv_op<kPQkv>(a, l, lut, ring, bars, ps, cs, xs, part);
         // ---- attention
         if (att_cta) {
-            // fetch this split's first K/V tile before waiting (rows of earlier steps are final)
-            constexpr int kPref = 1;  // 2 * kAttTile rows of hd bf16 = one uint4 per thread
-            uint4 kvp[kPref];
-            const int hk = static_cast<int>(blockIdx.x) / ap.ns, s = static_cast<int>(blockIdx.x) - hk * ap.ns;
-            const int tok0 = s * ap.ts, nt = min(kAttTile, kv_len - tok0);
-            const int per_row = a.hd / 8;
+            // issue this split's first K/V tile before waiting for q (rows of earlier steps are final)
+            const AttSmem att_sm = att_smem(work);
+            const int hk = static_cast<int>(blockIdx.x) / ap.ns, sp = static_cast<int>(blockIdx.x) - hk * ap.ns;
+            const int tok0 = sp * ap.ts;
             const uint16_t* kc = reinterpret_cast<const uint16_t*>(L[kLKCache]) + static_cast<int64_t>(hk) * a.cap * a.hd;
             const uint16_t* vc = reinterpret_cast<const uint16_t*>(L[kLVCache]) + static_cast<int64_t>(hk) * a.cap * a.hd;
-#pragma unroll
-            for (int j = 0; j < kPref; ++j) {
-                const int o = tid + j * kPThreads;
-                kvp[j] = make_uint4(0, 0, 0, 0);
-                if (o < 2 * nt * per_row) {
-                    const bool isk = o < nt * per_row;
-                    const int oo = isk ? o : o - nt * per_row;
-                    kvp[j] = ldcg_u4((isk ? kc : vc) + static_cast<int64_t>(tok0) * a.hd + 8 * oo);
-                }
-            }
+            fence_proxy_async_smem();  // the tile rows' earlier generic accesses (xs, partials) before the copies
+            __syncthreads();
+            if (warp == 0) att_issue_tile(kc, vc, tok0, min(kAttTile, kv_len - tok0), att_sm, &att_bar);
             cta_wait(a, ctr + kCQkv, G);
             KC_STAMP(l, 6);
-            attention_split(a, l, L, nsl, pos_c, kv_len, ap, bias_s, rope_s, work, kvp, kPref);
+            attention_split(a, l, L, nsl, pos_c, kv_len, ap, bias_s, rope_s, att_sm, &att_bar, att_phase);
             KC_STAMP(l, 7);
         }
         // ---- o_proj (its input: every split of every head)
         norm_prefetch(a, reinterpret_cast<const uint16_t*>(L[kLPostNorm]), wv);
         cta_wait(a, ctr + kCAtt, static_cast<unsigned>(a.kvh * ap.ns));
         KC_STAMP(l, 8);
-        stage_attention(a, rng, ap, xs, tap != nullptr ? tap + to.att : nullptr);
+        stage_attention(a, rng, ap, xs, part, tap != nullptr ? tap + to.att : nullptr);
         __syncthreads();
         KC_STAMP(l, 9);
         for (int i = tid; i < kPartGroups * kPWarps * 64; i += kPThreads) part[i] = 0.F;
@@ -1215,7 +1261,7 @@ PersistGeom persist_geom(const PersistDims& d, int sms) {
     g.xs_bytes = (kmax * 2 + 127) & ~127;
     const int gq = d.kv_heads > 0 ? d.q_heads / d.kv_heads : 1;
     const int work = g.xs_bytes + kPartGroups * kPWarps * 64 * 4;
-    const int att = (gq * d.head_dim + gq * kAttTile + gq * 4 + 2 * d.head_dim) * 4 + kAttTile * (kKRow + d.head_dim) * 2;
+    const int att = kAttSmemBytes;
     g.work_bytes = ((work > att ? work : att) + 127) & ~127;
     g.bias_rows = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
     const int tail = ((d.hidden + 63) & ~63) * 2 + ((g.bias_rows + 63) & ~63) * 2 + d.head_dim * 4;
