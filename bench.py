@@ -269,6 +269,8 @@ def run_gpu(args) -> dict | None:
             "launches_per_step": plan.launches_per_step,
             "clocks": clocks.summary(),
         }
+        if args.path == "persistent":
+            out["direct_decode_profile"] = direct_decode_profile(torch, weights, device, local)
         if not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline_sample(weights_to_host=(weights, plan), seconds=args.cpu_seconds)
     if dist is not None:
@@ -276,6 +278,48 @@ def run_gpu(args) -> dict | None:
         dist.destroy_process_group()
     bridge.reset_graph()
     return out
+
+
+def direct_decode_profile(torch, weights, device: str, local: int, lengths=(512, 1024, 2048), steps: int = 16) -> dict:
+    """Config 3's "direct-decode profile to 2048": the same weights in a plan
+    with a 2048-token KV bucket (its own handle and graph), random N(0,1)
+    cache rows, `steps` timed graph replays ending at each kv_len in
+    `lengths` (CUDA events on the replay stream)."""
+
+    from kudacuda_b200.decode_engine import QWEN25_3B, StaticDecodePlan
+    from kudacuda_b200.kudacuda_sidecar import KudaCudaBridge
+
+    cap = max(lengths)
+    br = KudaCudaBridge(device_id=local)
+    plan = StaticDecodePlan(br, weights, kv_bucket=cap, max_tokens=cap, device=device, persistent=True)
+    stream = torch.cuda.Stream(device=device)
+    plan.capture(stream)
+    gd = torch.Generator(device=device).manual_seed(SEED + 7)
+    for li in range(QWEN25_3B.layers):
+        plan.buffers.kcache[li].normal_(generator=gd)
+        plan.buffers.vcache[li].normal_(generator=gd)
+    peak, _ = _peaks()
+    wb = QWEN25_3B.weight_bytes_per_token()
+    points = []
+    for L in lengths:
+        plan.set_state(1, L - steps - 1, stream)
+        for _ in range(3):
+            plan.replay(stream)
+        plan.set_state(1, L - steps - 1, stream)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(steps):
+            plan.replay(stream)
+        e.record(stream)
+        e.synchronize()
+        ms = s.elapsed_time(e) / steps
+        nbytes = sum(wb.values()) + QWEN25_3B.kv_bytes_per_token(L - steps // 2)
+        points.append({"kv_len": [L - steps, L], "tok_s": round(1e3 / ms, 2), "ms_per_step": round(ms, 4),
+                       "bytes_per_token": nbytes, "frac_of_measured_hbm": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4)})
+    err = br.error_word(clear=True)
+    br.reset_graph()
+    br.shutdown()
+    return {"kv_bucket": cap, "path": "persistent", "points": points, "device_error_word": err}
 
 
 def persistent_kernel_roofline(torch, bridge, plan, stream, pos: int) -> dict:
