@@ -359,6 +359,41 @@ KUDACUDA_API int kudacuda_sm100_decode_layers_persistent_debug(void* handle, uin
                                                                int64_t spin_limit, int64_t stall_counter,
                                                                uint64_t stream);
 
+/* Row-split persistent decode (no reference counterpart): the same step as
+ * decode_layers_persistent with a different work split -- every op's output
+ * rows come in 16-row tiles, each owned by one CTA that streams all of its K
+ * and finishes the rows itself (q/k after bias and RoPE with k and v written
+ * into the cache row, x + o_proj, SwiGLU, x + down), so consumers read
+ * finished vectors instead of partial sums.  nf4_retile16 copies
+ * bitsandbytes NF4 tensors into its units (tile, 64-element block): 512 code
+ * bytes in m16n8k16 lane order then the tile rows' 16 fp32 absmax, 576 bytes,
+ * tile-major; modes as nf4_retile (0 plain, rows % 16 == 0; 1 gate/up in
+ * tiles of 8 pairs; 2 q/k/v with q/k heads in tiles of 8 RoPE pairs, then
+ * 16-row v tiles); nf4_retile16_tiles returns the tile count (-1 when
+ * unsupported).  layer_table is a device int64 [layers][16]: qkv units, o
+ * units, gate/up units, down units, input norm, post norm, q bias, k bias,
+ * v bias (0 when absent), K cache, V cache, then zeros.  taps / spin_limit /
+ * stall_counter are the test hooks of decode_layers_persistent_debug (the
+ * same tap layout; counter index = layer * 16 + {0 qkv, 1 attention,
+ * 2 o_proj, 3 gate/up, 4 down}).  Deterministic (fixed summation order);
+ * every device wait is bounded and reports bit 4 of the error word. */
+KUDACUDA_API int64_t kudacuda_sm100_nf4_retile16_tiles(int mode, int64_t rows0, int64_t rows1, int64_t rows2,
+                                                       int64_t head_dim);
+KUDACUDA_API int kudacuda_sm100_nf4_retile16(void* handle, int mode, uint64_t packed0, uint64_t absmax0, int64_t rows0,
+                                             uint64_t packed1, uint64_t absmax1, int64_t rows1, uint64_t packed2,
+                                             uint64_t absmax2, int64_t rows2, int64_t k, int64_t head_dim,
+                                             uint64_t out_units, int64_t out_bytes, uint64_t stream);
+KUDACUDA_API int64_t kudacuda_sm100_decode_rows_scratch_bytes(void* handle, int64_t layers, int64_t hidden,
+                                                             int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                                             int64_t intermediate, int64_t kv_capacity);
+KUDACUDA_API int kudacuda_sm100_decode_layers_rows(void* handle, uint64_t layer_table, int64_t layers, uint64_t x,
+                                                   uint64_t state, uint64_t rope_cos, uint64_t rope_sin,
+                                                   int64_t max_pos, uint64_t scratch, int64_t scratch_bytes,
+                                                   int64_t hidden, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                                   int64_t intermediate, int64_t kv_capacity, float eps, float scale,
+                                                   uint64_t taps, int64_t taps_bytes, int64_t spin_limit,
+                                                   int64_t stall_counter, uint64_t stream);
+
 /* Batched decode: B independent sequences advance one token per step.  No
  * reference counterpart (the reference's projections and its GQA contract,
  * python/kudacuda_sidecar.py:145-153, are batch 1); the arithmetic is what

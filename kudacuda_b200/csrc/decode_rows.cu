@@ -1,0 +1,1157 @@
+// decode_rows.cu -- all decoder layers of one batch-1 decode step in one
+// persistent cooperative launch on sm_100a, with a row-complete work split.
+//
+// Replaces, for the static decode plan, the per-layer launch sequence
+// (RMSNorm+QKV+RoPE+append, GQA decode, o_proj+residual, RMSNorm+SwiGLU,
+// down+residual) that stands in for the reference's per-op kernels
+// (kernels/common/nf4_tiled_gemv.cuh:61-278, nf4_swiglu_bf16.cuh:65-209,
+// qwen2_gqa_decode.cuh:17-203) and the bitsandbytes o_proj/down matmuls
+// (python/kudacuda_sidecar.py:947, :1746).  Arithmetic and rounding points are
+// Transformers' (those of the per-op HF-semantics kernels in nf4_gemv.cuh).
+//
+// Work split: every op's output rows come in 16-row tiles, and each tile is
+// owned by ONE CTA that streams all of its K -- so each output value is
+// finished exactly once, by its owner, with the op's epilogue: q/k after bias
+// and RoPE (k and v go straight into the cache row of this step), x + o_proj,
+// SwiGLU, x + down.  Consumers then read the few KB of finished values they
+// need (the residual stream, q, the attention output, h) instead of summing
+// partial slots.  Each warp of a CTA streams a contiguous range of the CTA's
+// (tile, K-block) units through its own ring of bulk copies, and the 16
+// warps' per-tile sums meet in shared memory in a fixed order (the result is
+// deterministic).
+//
+// Unit (tile, block b): 512 code bytes -- lane 4g + t holds bytes
+// [32b + 8t, +8) of tile rows g and g + 8, exactly its m16n8k16 A fragments --
+// then the 16 rows' fp32 absmax of block b (576 bytes; nf4_retile16_kernel
+// writes them tile-major from the bitsandbytes layout).  Tile rows: q/k heads
+// in tiles of 8 RoPE pairs (row r and its partner r + 8), gate/up pairs, or
+// 16 consecutive rows.
+//
+// Dependencies (each a counter per layer: release increments by the
+// producers, one acquiring thread per consumer CTA, bounded spins that abort
+// the step and set bit 4 of the error word): x ready -> q/k/v (all CTAs) ->
+// attention splits (a ticket per KV head picks the split that merges them)
+// -> o_proj owners -> x1 ready -> gate/up (all CTAs) -> down owners -> next
+// layer.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kc_common.cuh"
+#include "kc_launch.h"
+
+// Phase timestamps for profiling builds only (-DKC_PERSIST_STAMPS; off in the
+// library): thread 0 of every CTA records %globaltimer and clock64 at fixed
+// points of one layer (KC_STAMP_LAYER) into g_rows_stamps[cta][64], read back
+// with kc_rows_read_stamps.  No work is skipped or added to the product build.
+#ifdef KC_PERSIST_STAMPS
+#ifndef KC_STAMP_LAYER
+#define KC_STAMP_LAYER 18
+#endif
+__device__ unsigned long long g_rows_stamps[1024 * 64];
+#define KR_STAMP(l, i)                                                          \
+    do {                                                                        \
+        if ((l) == KC_STAMP_LAYER && threadIdx.x == 0) {                        \
+            unsigned long long t_;                                              \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)::"memory");    \
+            g_rows_stamps[blockIdx.x * 64 + (i)] = t_;                          \
+            g_rows_stamps[blockIdx.x * 64 + 32 + (i)] = clock64();              \
+        }                                                                       \
+    } while (0)
+extern "C" __attribute__((visibility("default"))) int kc_rows_read_stamps(unsigned long long* out, int n) {
+    return static_cast<int>(cudaMemcpyFromSymbol(out, g_rows_stamps, sizeof(unsigned long long) * n));
+}
+#else
+#define KR_STAMP(l, i) \
+    do {               \
+    } while (0)
+#endif
+
+namespace kc {
+namespace {
+
+constexpr int kRW = 16;  // warps per CTA
+constexpr int kRT = kRW * 32;
+constexpr int kRMaxSlots = 3;
+constexpr int kUnitCodes = 512;
+constexpr int kUnitBytes = 576;
+constexpr int kSlotUnits = 4;
+constexpr int kSlotBytes = kSlotUnits * kUnitBytes;
+constexpr int kRLutBytes = 65536;  // 256 entry rows x 256 B, lane replicas in the first 128 B of a row
+constexpr int kMaxCtaTiles = 16;   // tiles of one op one CTA may own (checked on the host)
+constexpr int kRStride = 16;       // counters per layer: 0 qkv, 1 attention, 2 o_proj, 3 gate/up, 4 down, 5.. tickets
+constexpr uint32_t kRSpinLimit = 1u << 21;
+constexpr int kATile = 64;         // tokens per attention tile
+constexpr int kAMaxSplits = 32;    // splits per KV head
+constexpr int kKRow = 136;         // padded K/V/q row in shared memory (bf16): 272 bytes
+constexpr int kRngStride = kRW + 3;  // per op: t0, t1, warp unit bounds 0..16
+
+enum RowOp { kOQkv = 0, kOO = 1, kOGu = 2, kODn = 3 };
+enum RowCtr { kCQkv = 0, kCAtt = 1, kCO = 2, kCGu = 3, kCDn = 4, kCTicket = 5 };
+enum RowSlot { kTUnits0 = 0, kTInNorm = 4, kTPostNorm, kTQBias, kTKBias, kTVBias, kTKCache, kTVCache, kTSlots = 16 };
+
+struct RowArgs {
+    const uint64_t* layers;  // [nlayers][kTSlots] device pointers
+    int nlayers, hidden, qh, kvh, hd, inter, cap, max_pos;
+    float eps, scale_log2;
+    const int32_t* state;  // {token, pos, kv_len, pad}
+    uint16_t* x;           // bf16 [hidden]: the step's input, then every layer's x2 (the last is the output)
+    const uint16_t* rope_cos;
+    const uint16_t* rope_sin;
+    unsigned* counters;  // [nlayers * kRStride]
+    unsigned* misc;      // [0] abort flag, [1] final ticket
+    uint16_t* qg;        // bf16 [qh * hd]: this layer's q after bias and RoPE
+    uint16_t* attg;      // bf16 [qh * hd]: attention output
+    uint16_t* x1g;       // bf16 [hidden]: x + o_proj
+    uint16_t* hg;        // bf16 [inter]: SwiGLU output
+    float* apart;        // [kvh][kAMaxSplits][gq][hd + 4] attention partials
+    int* err;
+    int ring_slots;
+    int tiles[4], nbpt[4], ctas[4];
+    int xs_bytes, work_bytes, bias_rows;
+    uint16_t* taps;  // test hooks, as decode_persistent.cu
+    int tap_stride;
+    uint32_t spin_limit;
+    int stall_counter;
+};
+
+// tap record offsets (the same layout as the other persistent kernel)
+struct RTaps {
+    int xn, q, k, v, att, x1, xn2, h, x2, stride;
+};
+__host__ __device__ inline RTaps rtaps(int hidden, int qh, int kvh, int hd, int inter) {
+    RTaps t;
+    t.xn = 0;
+    t.q = hidden;
+    t.k = t.q + qh * hd;
+    t.v = t.k + kvh * hd;
+    t.att = t.v + kvh * hd;
+    t.x1 = t.att + qh * hd;
+    t.xn2 = t.x1 + hidden;
+    t.h = t.xn2 + hidden;
+    t.x2 = t.h + inter;
+    t.stride = t.x2 + hidden;
+    return t;
+}
+__device__ __forceinline__ uint16_t* rtap(const RowArgs& a, int layer) {
+    return a.taps == nullptr ? nullptr : a.taps + static_cast<int64_t>(layer) * a.tap_stride;
+}
+
+// ------------------------------------------------------------------ small helpers
+__device__ __forceinline__ uint32_t prmt_r(uint32_t a, uint32_t b, uint32_t s) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s));
+    return d;
+}
+__device__ __forceinline__ void mma_f16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Pair-table lookup of byte j of w (selector 0x55j4): entry row byte << 8, lane replica lane << 2.
+__device__ __forceinline__ uint32_t lut_pair_r(const uint8_t* lut, uint32_t w, uint32_t sel, uint32_t lane4) {
+    return *reinterpret_cast<const uint32_t*>(lut + prmt_r(w, lane4, sel));
+}
+// One unit: rows g and g + 8 of a 16-row tile over one 64-element block
+// (w.x, w.y: 8 bytes of row g; w.z, w.w: 8 bytes of row g + 8); returns the
+// batch-column-0 sums (row g, row g + 8), valid in lanes with t == 0.
+__device__ __forceinline__ float2 unit_dot_r(const uint8_t* lut, uint32_t lane4, uint4 w, uint4 x0, uint4 x1) {
+    float c[4] = {0.F, 0.F, 0.F, 0.F};
+    mma_f16(c, lut_pair_r(lut, w.x, 0x5504u, lane4), lut_pair_r(lut, w.z, 0x5504u, lane4),
+            lut_pair_r(lut, w.x, 0x5514u, lane4), lut_pair_r(lut, w.z, 0x5514u, lane4), x0.x, x0.y);
+    mma_f16(c, lut_pair_r(lut, w.x, 0x5524u, lane4), lut_pair_r(lut, w.z, 0x5524u, lane4),
+            lut_pair_r(lut, w.x, 0x5534u, lane4), lut_pair_r(lut, w.z, 0x5534u, lane4), x0.z, x0.w);
+    mma_f16(c, lut_pair_r(lut, w.y, 0x5504u, lane4), lut_pair_r(lut, w.w, 0x5504u, lane4),
+            lut_pair_r(lut, w.y, 0x5514u, lane4), lut_pair_r(lut, w.w, 0x5514u, lane4), x1.x, x1.y);
+    mma_f16(c, lut_pair_r(lut, w.y, 0x5524u, lane4), lut_pair_r(lut, w.w, 0x5524u, lane4),
+            lut_pair_r(lut, w.y, 0x5534u, lane4), lut_pair_r(lut, w.w, 0x5534u, lane4), x1.z, x1.w);
+    return make_float2(c[0], c[2]);
+}
+__device__ __forceinline__ unsigned ld_acquire_r(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned ld_relaxed_r(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Thread 0 waits until *ctr >= target (or the step was aborted), polling with
+// relaxed loads (the abort flag every 32 polls) and acquiring once at the
+// end; then the whole CTA continues.  A wait that runs out raises the abort
+// flag and error bit 4.
+__device__ void rwait(const RowArgs& a, const unsigned* ctr, unsigned target) {
+    if (threadIdx.x == 0) {
+        if (a.stall_counter >= 0 && ctr == a.counters + a.stall_counter) ++target;  // test hook: never reached
+        uint32_t n = 0;
+        while (ld_relaxed_r(ctr) < target) {
+            if ((++n & 31u) == 0u) {
+                if (ld_relaxed_r(a.misc) != 0u) break;
+                if (n > a.spin_limit) {
+                    atomicExch(a.misc, 1u);
+                    atomicOr(a.err, 16);
+                    break;
+                }
+            }
+        }
+        (void)ld_acquire_r(ctr);
+    }
+    __syncthreads();
+}
+// After every thread of the CTA wrote its results: one release increment.
+__device__ __forceinline__ void rsignal(unsigned* ctr) {
+    __syncthreads();
+    if (threadIdx.x == 0)
+        asm volatile("fence.acq_rel.gpu;\n\tred.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+}
+
+// ------------------------------------------------------------------ ownership
+// rng[op * kRngStride]: [0] = first owned tile, [1] = one past the last,
+// [2 + w] = warp w's first unit (relative to the CTA's first unit), [2 + 16] = unit count.
+__device__ __forceinline__ void fill_rng(const RowArgs& a, int* rng) {
+    const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
+    for (int i = threadIdx.x; i < 4 * kRngStride; i += kRT) {
+        const int op = i / kRngStride, k = i - op * kRngStride;
+        const int T = a.tiles[op];
+        const int t0 = static_cast<int>(static_cast<int64_t>(c) * T / G);
+        const int t1 = static_cast<int>(static_cast<int64_t>(c + 1) * T / G);
+        const int U = (t1 - t0) * a.nbpt[op];
+        rng[i] = k == 0 ? t0 : k == 1 ? t1 : (k - 2) * U / kRW;
+    }
+}
+
+// ------------------------------------------------------------------ per-warp unit stream
+struct RStream {  // producer cursor (lane 0)
+    int layer, op, u, end;
+    bool done;
+};
+__device__ __forceinline__ void rstream_normalise(const RowArgs& a, const int* rng, RStream& s, int warp) {
+    while (!s.done && s.u >= s.end) {
+        if (++s.op == 4) {
+            s.op = 0;
+            if (++s.layer == a.nlayers) {
+                s.done = true;
+                break;
+            }
+        }
+        s.u = rng[s.op * kRngStride + 2 + warp];
+        s.end = rng[s.op * kRngStride + 3 + warp];
+    }
+}
+__device__ __forceinline__ void rstream_issue(const RowArgs& a, const int* rng, RStream& s, int warp, uint8_t* ring,
+                                              uint64_t* bars, int slot) {
+    rstream_normalise(a, rng, s, warp);
+    if (s.done) return;
+    const int n = min(kSlotUnits, s.end - s.u);
+    const int64_t unit = static_cast<int64_t>(rng[s.op * kRngStride]) * a.nbpt[s.op] + s.u;
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(a.layers[static_cast<int64_t>(s.layer) * kTSlots + s.op]) +
+                         unit * kUnitBytes;
+    const uint32_t bytes = static_cast<uint32_t>(n) * kUnitBytes;
+    mbar_arrive_expect_tx(&bars[slot], bytes);
+    bulk_g2s(ring + slot * kSlotBytes, src, bytes, &bars[slot]);
+    s.u += n;
+}
+struct RCons {
+    int slot;
+    uint32_t parity;
+    bool failed;
+};
+// After a ring wait ran out: every slot may still have a copy in flight (one
+// each, none issued after the failure); lane 0 waits for them, bounded, so no
+// copy writes into shared memory after the CTA has exited.
+__device__ __noinline__ void rring_drain(uint64_t* bars, int ring_slots, int slot, uint32_t parity) {
+    for (int i = 0; i < ring_slots; ++i) {
+        for (int retry = 0; retry < 4 && !mbar_wait_bounded(&bars[slot], parity); ++retry) {
+        }
+        if (++slot == ring_slots) {
+            slot = 0;
+            parity ^= 1u;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ one GEMV op: this CTA's tiles
+// xs holds the f16 input vector.  Each warp consumes its unit range slot by
+// slot, refilling each slot from the stream as soon as it is read; per-tile
+// sums of the warp go to part[tile][warp][16]; then the CTA sums the warps in
+// fixed order and hands every (tile, row pair) to `epi` (rows r and r + 8).
+template <int OP, class Epi>
+__device__ void rgemv(const RowArgs& a, const int* rng, const uint8_t* lut, uint8_t* ring, uint64_t* bars, RStream& ps,
+                      RCons& cs, const uint16_t* xs, float* part, Epi epi) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+    const int* rr = rng + OP * kRngStride;
+    const int t0 = rr[0], ntiles = rr[1] - rr[0];
+    const int nbpt = a.nbpt[OP];
+    const int uw0 = rr[2 + warp], uw1 = rr[3 + warp];
+    for (int i = tid; i < kMaxCtaTiles * kRW * 16; i += kRT) part[i] = 0.F;
+    __syncthreads();
+    const uint32_t lane4 = static_cast<uint32_t>(lane) << 2;
+    int tile = uw0 / nbpt, blk = uw0 - (uw0 / nbpt) * nbpt;
+    float acc_lo = 0.F, acc_hi = 0.F;
+    uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0;
+    for (int u = uw0; u < uw1;) {
+        if (!cs.failed && !mbar_wait_bounded(&bars[cs.slot], cs.parity)) {
+            cs.failed = true;
+            if (lane == 0) {
+                atomicExch(a.misc, 1u);
+                atomicOr(a.err, 16);
+                rring_drain(bars, a.ring_slots, cs.slot, cs.parity);
+            }
+            __syncwarp();
+        }
+        const uint8_t* st = ring + cs.slot * kSlotBytes;
+        const int n = min(kSlotUnits, uw1 - u);
+        for (int k = 0; k < n; ++k) {
+            if (g == 0) {  // only batch column 0 of B matters: lanes 0..3 carry x
+                const uint4* xp = reinterpret_cast<const uint4*>(xs + blk * 64 + 16 * t);
+                x0 = xp[0];
+                x1 = xp[1];
+            }
+            float aA = 0.F, aB = 0.F;
+            if (t == 0) {
+                const float* am = reinterpret_cast<const float*>(st + k * kUnitBytes + kUnitCodes);
+                aA = am[g];
+                aB = am[8 + g];
+            }
+            const uint4 w = reinterpret_cast<const uint4*>(st + k * kUnitBytes)[lane];
+            const float2 pr = unit_dot_r(lut, lane4, w, x0, x1);
+            acc_lo = fmaf(pr.x, aA, acc_lo);
+            acc_hi = fmaf(pr.y, aB, acc_hi);
+            if (++blk == nbpt) {  // tile done for this warp
+                if (t == 0) {
+                    float* pp = part + (tile * kRW + warp) * 16;
+                    pp[g] = acc_lo;
+                    pp[8 + g] = acc_hi;
+                }
+                acc_lo = acc_hi = 0.F;
+                blk = 0;
+                ++tile;
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && !cs.failed) {
+            fence_proxy_async_smem();  // this slot's generic reads before the async-proxy refill
+            rstream_issue(a, rng, ps, warp, ring, bars, cs.slot);
+        }
+        if (++cs.slot == a.ring_slots) {
+            cs.slot = 0;
+            cs.parity ^= 1u;
+        }
+        u += n;
+    }
+    if (uw1 > uw0 && blk != 0 && t == 0) {
+        float* pp = part + (tile * kRW + warp) * 16;
+        pp[g] = acc_lo;
+        pp[8 + g] = acc_hi;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < ntiles * 8; idx += kRT) {
+        const int tl = idx >> 3, r = idx & 7;
+        float lo = 0.F, hi = 0.F;
+#pragma unroll 4
+        for (int w = 0; w < kRW; ++w) {
+            lo += part[(tl * kRW + w) * 16 + r];
+            hi += part[(tl * kRW + w) * 16 + 8 + r];
+        }
+        epi(t0 + tl, r, lo, hi);
+    }
+}
+
+// ------------------------------------------------------------------ staging
+// xs = f16(RMSNorm_HF(x) * w): x_norm = bf16(w * bf16(x * rsqrt(mean(x^2) + eps)));
+// w was loaded into registers before the dependency wait.
+constexpr int kNormPer = 4;  // hidden <= 8 * 512 * 4
+__device__ __forceinline__ void rnorm_prefetch(const RowArgs& a, const uint16_t* w, uint4* wv) {
+#pragma unroll
+    for (int i = 0; i < kNormPer; ++i) {
+        const int o = threadIdx.x + i * kRT;
+        if (o < a.hidden / 8) wv[i] = __ldg(reinterpret_cast<const uint4*>(w + 8 * o));
+    }
+}
+__device__ void rstage_norm(const RowArgs& a, const uint16_t* xres, const uint4* wv, uint16_t* xs, float* red,
+                            uint16_t* tap) {
+    const int tid = threadIdx.x;
+    const int n8 = a.hidden / 8;
+    float ss = 0.F;
+    for (int i = tid; i < a.hidden; i += kRT) {
+        const float v = bf16_bits_to_f32(xres[i]);
+        ss += v * v;
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.F;
+#pragma unroll
+    for (int i = 0; i < kRW; ++i) tot += red[i];
+    const float inv = 1.0F / sqrtf(tot / static_cast<float>(a.hidden) + a.eps);
+    bool overflow = false;
+#pragma unroll
+    for (int i = 0; i < kNormPer; ++i) {
+        const int o = tid + i * kRT;
+        if (o < n8) {
+            const uint4 xv = reinterpret_cast<const uint4*>(xres)[o];
+            const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+            const uint32_t ww[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+            uint32_t out[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float v[2];
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const float xe = bf16_bits_to_f32(static_cast<uint16_t>(xx[j] >> (16 * hh)));
+                    const float we = bf16_bits_to_f32(static_cast<uint16_t>(ww[j] >> (16 * hh)));
+                    v[hh] = round_bf16(we * round_bf16(xe * inv));
+                    overflow |= !(fabsf(v[hh]) <= 65504.F);
+                    if (tap != nullptr) tap[8 * o + 2 * j + hh] = f32_to_bf16_bits(v[hh]);
+                }
+                out[j] = static_cast<uint32_t>(f32_to_f16_bits(v[0])) |
+                         (static_cast<uint32_t>(f32_to_f16_bits(v[1])) << 16);
+            }
+            reinterpret_cast<uint4*>(xs)[o] = make_uint4(out[0], out[1], out[2], out[3]);
+        }
+    }
+    if (overflow) atomicOr(a.err, 1);
+    __syncthreads();
+}
+// dst (shared, n bf16) = src (global, written by other CTAs before the acquire)
+__device__ __forceinline__ void rload_bf16(uint16_t* dst, const uint16_t* src, int n) {
+    for (int i = threadIdx.x; i < n / 8; i += kRT)
+        reinterpret_cast<uint4*>(dst)[i] = __ldcg(reinterpret_cast<const uint4*>(src) + i);
+}
+// xs (shared, n f16) = f16(src (global bf16)); values beyond f16 range flag bit 1
+__device__ void rstage_f16(const RowArgs& a, uint16_t* xs, const uint16_t* src, int n) {
+    bool overflow = false;
+    for (int i = threadIdx.x; i < n / 8; i += kRT) {
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src) + i);
+        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+        uint32_t out[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float f0 = __uint_as_float(vv[j] << 16), f1 = __uint_as_float(vv[j] & 0xffff0000u);
+            overflow |= !(fabsf(f0) <= 65504.F) || !(fabsf(f1) <= 65504.F);
+            out[j] = static_cast<uint32_t>(f32_to_f16_bits(f0)) | (static_cast<uint32_t>(f32_to_f16_bits(f1)) << 16);
+        }
+        reinterpret_cast<uint4*>(xs)[i] = make_uint4(out[0], out[1], out[2], out[3]);
+    }
+    if (overflow) atomicOr(a.err, 1);
+    __syncthreads();
+}
+
+// ------------------------------------------------------------------ attention
+// A split of one KV head covers ts tokens (a multiple of kATile) in tiles of
+// kATile tokens.  The tile's K and V rows land in padded shared rows by
+// per-row bulk copies (the first tile's are issued before the split waits for
+// q); scores and P.V run on the tensor core as in the cluster GQA kernel
+// (gqa_decode.cu): mma.m16n8k16 bf16 with the group's query heads in A rows
+// 0..gq-1 and 8 tokens per n-tile, fp32 accumulation; P split into bf16 hi +
+// lo halves against ldmatrix.trans V fragments.
+struct RAttPlan {
+    int ns, ts;
+};
+__device__ __forceinline__ RAttPlan ratt_plan(const RowArgs& a, int kv_len) {
+    RAttPlan p;
+    const int per_head = max(1, min(kAMaxSplits, static_cast<int>(gridDim.x) / a.kvh));
+    const int tiles = (kv_len + kATile - 1) / kATile;
+    const int ns = min(per_head, tiles);
+    p.ts = kATile * ((tiles + ns - 1) / ns);
+    p.ns = (kv_len + p.ts - 1) / p.ts;
+    return p;
+}
+struct RAttSmem {
+    uint16_t* kt;  // [kATile][kKRow]
+    uint16_t* vt;  // [kATile][kKRow]
+    uint16_t* qb;  // [8][kKRow]: the group's q rows (bf16), rows >= gq zero
+    float* ss;     // [2][8][kATile]: score halves, then probabilities in [0]; the merge's weights
+    float* ml;     // [8][4]: running max, sum, correction
+};
+constexpr int kRAttSmemBytes = 2 * kATile * kKRow * 2 + 8 * kKRow * 2 + 2 * 8 * kATile * 4 + 8 * 4 * 4;
+__device__ __forceinline__ RAttSmem ratt_smem(uint8_t* work) {
+    RAttSmem s;
+    s.kt = reinterpret_cast<uint16_t*>(work);
+    s.vt = s.kt + kATile * kKRow;
+    s.qb = s.vt + kATile * kKRow;
+    s.ss = reinterpret_cast<float*>(s.qb + 8 * kKRow);
+    s.ml = s.ss + 2 * 8 * kATile;
+    return s;
+}
+// Warp 0 (all lanes) issues the bulk copies of K and V rows [t0, t0 + nt) of
+// one KV head into the padded tile rows, completing on `bar`.
+__device__ __forceinline__ void ratt_issue(const uint16_t* kc, const uint16_t* vc, int t0, int nt, const RAttSmem& sm,
+                                           uint64_t* bar) {
+    const int lane = threadIdx.x & 31;
+    if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nt) * 512u);
+    __syncwarp();
+    for (int r = lane; r < nt; r += 32) {
+        bulk_g2s(sm.kt + r * kKRow, kc + static_cast<int64_t>(t0 + r) * 128, 256u, bar);
+        bulk_g2s(sm.vt + r * kKRow, vc + static_cast<int64_t>(t0 + r) * 128, 256u, bar);
+    }
+}
+__device__ __forceinline__ void rldsm_x2_trans(uint32_t& r0, uint32_t& r1, uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void rsplit_pair(float p0, float p1, uint32_t& hi, uint32_t& lo) {
+    const float h0 = round_bf16(p0), h1 = round_bf16(p1);
+    hi = static_cast<uint32_t>(f32_to_bf16_bits(h0)) | (static_cast<uint32_t>(f32_to_bf16_bits(h1)) << 16);
+    lo = static_cast<uint32_t>(f32_to_bf16_bits(p0 - h0)) | (static_cast<uint32_t>(f32_to_bf16_bits(p1 - h1)) << 16);
+}
+
+// One split (KV head hk, tokens [tok0, tok1)) of one layer; then the split
+// that arrives last for its KV head (a ticket) merges every split of the head
+// into the attention output, written once for all o_proj owners.
+__device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int pos, int kv_len, const RAttPlan& ap,
+                           const RAttSmem& sm, uint64_t* bar, uint32_t& phase, int* flag) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+    const int gq = a.qh / a.kvh, hd = a.hd;
+    const int hk = static_cast<int>(blockIdx.x) / ap.ns, s = static_cast<int>(blockIdx.x) - hk * ap.ns;
+    const int tok0 = s * ap.ts, tok1 = min(kv_len, tok0 + ap.ts);
+    const uint16_t* kc = reinterpret_cast<const uint16_t*>(L[kTKCache]) + static_cast<int64_t>(hk) * a.cap * hd;
+    const uint16_t* vc = reinterpret_cast<const uint16_t*>(L[kTVCache]) + static_cast<int64_t>(hk) * a.cap * hd;
+    // the group's q rows (bf16 pairs) from the QKV owners; rows >= gq zero
+    for (int i = tid; i < 8 * hd / 2; i += kRT) {
+        const int row = i / (hd / 2), c = i - row * (hd / 2);
+        const uint32_t v = row < gq ? __ldcg(reinterpret_cast<const uint32_t*>(a.qg) + ((hk * gq + row) * hd) / 2 + c) : 0u;
+        reinterpret_cast<uint32_t*>(sm.qb + row * kKRow)[c] = v;
+    }
+    if (tid < 8) {
+        sm.ml[tid * 4 + 0] = -INFINITY;
+        sm.ml[tid * 4 + 1] = 0.F;
+        sm.ml[tid * 4 + 2] = 1.F;
+    }
+    __syncthreads();
+    uint32_t qa[8][2];
+    {
+        const uint32_t* qw = reinterpret_cast<const uint32_t*>(sm.qb + g * kKRow);
+#pragma unroll
+        for (int s8 = 0; s8 < 8; ++s8) {
+            qa[s8][0] = qw[8 * s8 + t];
+            qa[s8][1] = qw[8 * s8 + t + 4];
+        }
+    }
+    float o0[4] = {0.F, 0.F, 0.F, 0.F}, o1[4] = {0.F, 0.F, 0.F, 0.F};  // warp w: dims 8w .. 8w+7 of head g
+    const uint32_t vbase = smem_u32(sm.vt) + static_cast<uint32_t>((lane & 15) * kKRow * 2 + 16 * warp);
+    for (int t0 = tok0; t0 < tok1; t0 += kATile) {
+        const int nt = min(kATile, tok1 - t0);
+        if (t0 != tok0) {  // every thread is done with the previous tile's rows
+            fence_proxy_async_smem();
+            __syncthreads();
+            if (warp == 0) ratt_issue(kc, vc, t0, nt, sm, bar);
+        }
+        if (!mbar_wait_bounded(bar, phase)) {
+            if (tid == 0) {
+                atomicExch(a.misc, 1u);
+                atomicOr(a.err, 16);
+            }
+            for (int retry = 0; retry < 8 && !mbar_wait_bounded(bar, phase); ++retry) {
+            }
+        }
+        phase ^= 1u;
+        const int n16 = (nt + 15) & ~15;
+        if (pos >= t0 && pos < t0 + nt) {  // this step's row, written by the k/v owners after the copy may have run
+            for (int i = tid; i < hd / 8; i += kRT) {
+                reinterpret_cast<uint4*>(sm.kt + (pos - t0) * kKRow)[i] =
+                    __ldcg(reinterpret_cast<const uint4*>(kc + static_cast<int64_t>(pos) * hd) + i);
+                reinterpret_cast<uint4*>(sm.vt + (pos - t0) * kKRow)[i] =
+                    __ldcg(reinterpret_cast<const uint4*>(vc + static_cast<int64_t>(pos) * hd) + i);
+            }
+        }
+        // V rows nt .. n16-1 take part in the last P.V k-step with P = 0: make them finite
+        for (int i = tid; i < (n16 - nt) * (hd / 2); i += kRT)
+            reinterpret_cast<uint32_t*>(sm.vt + (nt + i / (hd / 2)) * kKRow)[i % (hd / 2)] = 0u;
+        __syncthreads();
+        if (warp < (n16 >> 3) * 2) {  // scores: unit (n-tile of 8 tokens, dim half) per warp
+            const int ntl = warp >> 1, hf = warp & 1;
+            float c0[4] = {0.F, 0.F, 0.F, 0.F}, c1[4] = {0.F, 0.F, 0.F, 0.F};
+            const uint8_t* krow = reinterpret_cast<const uint8_t*>(sm.kt) + (ntl * 8 + g) * kKRow * 2 + 4 * t + 128 * hf;
+#pragma unroll
+            for (int s4 = 0; s4 < 4; s4 += 2) {
+                const uint32_t qA0 = hf ? qa[4 + s4][0] : qa[s4][0], qA1 = hf ? qa[4 + s4][1] : qa[s4][1];
+                const uint32_t qB0 = hf ? qa[5 + s4][0] : qa[s4 + 1][0], qB1 = hf ? qa[5 + s4][1] : qa[s4 + 1][1];
+                mma_bf16(c0, qA0, 0u, qA1, 0u, *reinterpret_cast<const uint32_t*>(krow + 32 * s4),
+                         *reinterpret_cast<const uint32_t*>(krow + 32 * s4 + 16));
+                mma_bf16(c1, qB0, 0u, qB1, 0u, *reinterpret_cast<const uint32_t*>(krow + 32 * s4 + 32),
+                         *reinterpret_cast<const uint32_t*>(krow + 32 * s4 + 48));
+            }
+            if (g < gq)
+                *reinterpret_cast<float2*>(sm.ss + (hf * 8 + g) * kATile + ntl * 8 + 2 * t) =
+                    make_float2((c0[0] + c1[0]) * a.scale_log2, (c0[1] + c1[1]) * a.scale_log2);
+        }
+        __syncthreads();
+        if (warp < gq) {  // online softmax per head over the tile (log2 domain); probabilities zero past nt
+            float v[2];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int j = lane + 32 * k;
+                v[k] = j < nt ? sm.ss[warp * kATile + j] + sm.ss[(8 + warp) * kATile + j] : -INFINITY;
+                mx = fmaxf(mx, v[k]);
+            }
+            mx = warp_max(mx);
+            const float m_old = sm.ml[warp * 4 + 0];
+            const float m_new = fmaxf(m_old, mx);
+            float ls = 0.F;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int j = lane + 32 * k;
+                const float p = j < nt ? exp2f(v[k] - m_new) : 0.F;
+                if (j < n16) sm.ss[warp * kATile + j] = p;
+                ls += p;
+            }
+            ls = warp_sum(ls);
+            if (lane == 0) {
+                const float corr = m_old == -INFINITY ? 0.F : exp2f(m_old - m_new);
+                sm.ml[warp * 4 + 0] = m_new;
+                sm.ml[warp * 4 + 1] = sm.ml[warp * 4 + 1] * corr + ls;
+                sm.ml[warp * 4 + 2] = corr;
+            }
+        }
+        __syncthreads();
+        if (warp < hd / 8) {  // P.V: warp w owns dims 8w .. 8w+7
+            const float corr = g < gq ? sm.ml[g * 4 + 2] : 1.F;
+            o0[0] *= corr;
+            o0[1] *= corr;
+            o1[0] *= corr;
+            o1[1] *= corr;
+            const float* prow = sm.ss + (g < gq ? g : 0) * kATile + 2 * t;
+            const int nk = n16 >> 4;
+            for (int kk = 0; kk < nk; kk += 2) {
+                const bool two = kk + 1 < nk;
+                uint32_t b0, b1, b2 = 0u, b3 = 0u;
+                rldsm_x2_trans(b0, b1, vbase + static_cast<uint32_t>(kk * 16 * kKRow * 2));
+                if (two) rldsm_x2_trans(b2, b3, vbase + static_cast<uint32_t>((kk + 1) * 16 * kKRow * 2));
+                float2 pa = make_float2(0.F, 0.F), pb = pa, pc = pa, pd = pa;
+                if (g < gq) {
+                    pa = *reinterpret_cast<const float2*>(prow + kk * 16);
+                    pb = *reinterpret_cast<const float2*>(prow + kk * 16 + 8);
+                    if (two) {
+                        pc = *reinterpret_cast<const float2*>(prow + kk * 16 + 16);
+                        pd = *reinterpret_cast<const float2*>(prow + kk * 16 + 24);
+                    }
+                }
+                uint32_t ah0, al0, ah2, al2, ch0, cl0, ch2, cl2;
+                rsplit_pair(pa.x, pa.y, ah0, al0);
+                rsplit_pair(pb.x, pb.y, ah2, al2);
+                rsplit_pair(pc.x, pc.y, ch0, cl0);
+                rsplit_pair(pd.x, pd.y, ch2, cl2);
+                mma_bf16(o0, ah0, 0u, ah2, 0u, b0, b1);
+                if (two) mma_bf16(o1, ch0, 0u, ch2, 0u, b2, b3);
+                mma_bf16(o0, al0, 0u, al2, 0u, b0, b1);
+                if (two) mma_bf16(o1, cl0, 0u, cl2, 0u, b2, b3);
+            }
+        }
+    }
+    const int rec = hd + 4;
+    float* mine = a.apart + ((static_cast<size_t>(hk) * kAMaxSplits + s) * gq) * rec;
+    if (warp < hd / 8 && g < gq)
+        *reinterpret_cast<float2*>(mine + g * rec + 4 + 8 * warp + 2 * t) = make_float2(o0[0] + o1[0], o0[1] + o1[1]);
+    if (tid < gq) {
+        mine[tid * rec + 0] = sm.ml[tid * 4 + 0];
+        mine[tid * rec + 1] = sm.ml[tid * 4 + 1];
+    }
+    // ---- the last split of this KV head to arrive merges all of them
+    unsigned* ctr = a.counters + layer * kRStride;
+    __syncthreads();
+    if (tid == 0) {
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        const unsigned old = atomicAdd(ctr + kCTicket + hk, 1u);
+        const int last = old + 1u == static_cast<unsigned>(ap.ns);
+        if (last) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        *flag = last;
+    }
+    __syncthreads();
+    if (!*flag) return;
+    float* wn = sm.ss;  // [gq][kAMaxSplits] normalised split weights
+    if (warp < gq) {
+        const float* p = a.apart + ((static_cast<size_t>(hk) * kAMaxSplits + lane) * gq + warp) * rec;
+        const bool live = lane < ap.ns;
+        const float m = live ? __ldcg(p) : -INFINITY;
+        const float l = live ? __ldcg(p + 1) : 0.F;
+        const float M = warp_max(m);
+        const float e = live && m != -INFINITY ? exp2f(m - M) : 0.F;
+        const float den = warp_sum(e * l);
+        wn[warp * kAMaxSplits + lane] = den > 0.F ? e / den : 0.F;
+    }
+    __syncthreads();
+    uint16_t* tap = rtap(a, layer);
+    const int att_off = tap != nullptr ? rtaps(a.hidden, a.qh, a.kvh, hd, a.inter).att : 0;
+    bool overflow = false;
+    for (int idx = tid; idx < gq * hd / 2; idx += kRT) {  // two dims per thread
+        const int hq = idx / (hd / 2), d = 2 * (idx - hq * (hd / 2));
+        const float* base = a.apart + (static_cast<size_t>(hk) * kAMaxSplits * gq + hq) * rec + 4 + d;
+        float acc0 = 0.F, acc1 = 0.F;
+        for (int sp = 0; sp < ap.ns; ++sp) {
+            const float w = wn[hq * kAMaxSplits + sp];
+            const float2 v = __ldcg(reinterpret_cast<const float2*>(base + static_cast<size_t>(sp) * gq * rec));
+            acc0 = fmaf(w, v.x, acc0);
+            acc1 = fmaf(w, v.y, acc1);
+        }
+        const uint16_t b0 = f32_to_bf16_bits(acc0), b1 = f32_to_bf16_bits(acc1);
+        const int o = (hk * gq + hq) * hd + d;
+        reinterpret_cast<uint32_t*>(a.attg)[o / 2] = static_cast<uint32_t>(b0) | (static_cast<uint32_t>(b1) << 16);
+        overflow |= !(fabsf(bf16_bits_to_f32(b0)) <= 65504.F) || !(fabsf(bf16_bits_to_f32(b1)) <= 65504.F);
+        if (tap != nullptr) {
+            tap[att_off + o] = b0;
+            tap[att_off + o + 1] = b1;
+        }
+    }
+    if (overflow) atomicOr(a.err, 1);
+    rsignal(ctr + kCAtt);
+}
+
+// ------------------------------------------------------------------ the kernel
+__global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
+    extern __shared__ __align__(128) uint8_t dsm[];
+    __shared__ __align__(8) uint64_t bars_all[kRW * kRMaxSlots];
+    __shared__ __align__(8) uint64_t att_bar;
+    __shared__ float red[kRW];
+    __shared__ int rng[4 * kRngStride];
+    __shared__ int flag;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint8_t* lut = dsm;
+    uint8_t* rings = dsm + kRLutBytes;
+    uint8_t* work = rings + kRW * a.ring_slots * kSlotBytes;
+    uint16_t* xs = reinterpret_cast<uint16_t*>(work);
+    float* part = reinterpret_cast<float*>(work + a.xs_bytes);
+    uint16_t* xres = reinterpret_cast<uint16_t*>(work + a.work_bytes);
+    uint16_t* bias_s = xres + ((a.hidden + 63) & ~63);
+    float* rope_s = reinterpret_cast<float*>(bias_s + ((a.bias_rows + 63) & ~63));
+    uint8_t* ring = rings + warp * a.ring_slots * kSlotBytes;
+    uint64_t* bars = bars_all + warp * kRMaxSlots;
+
+    // ---- per-warp stream: start every ring before anything else (weights are static)
+    fill_rng(a, rng);
+    __syncthreads();
+    RStream ps;
+    ps.layer = 0;
+    ps.op = 0;
+    ps.u = rng[2 + warp];
+    ps.end = rng[3 + warp];
+    ps.done = a.nlayers < 1;
+    if (lane == 0) {
+        for (int s = 0; s < a.ring_slots; ++s) mbar_init(&bars[s], 1);
+        if (warp == 0) mbar_init(&att_bar, 1);
+        fence_mbar_init();
+        for (int s = 0; s < a.ring_slots; ++s) rstream_issue(a, rng, ps, warp, ring, bars, s);
+    }
+    // pair table: entry e -> half2(level[e >> 4], level[e & 15]) at row e, lane replica l
+    for (int i = tid; i < 256 * 8; i += kRT) {
+        const int e = i >> 3;
+        const uint32_t v = static_cast<uint32_t>(f32_to_f16_bits(kNf4Levels[e >> 4])) |
+                           (static_cast<uint32_t>(f32_to_f16_bits(kNf4Levels[e & 15])) << 16);
+        reinterpret_cast<uint4*>(lut + e * 256)[i & 7] = make_uint4(v, v, v, v);
+    }
+    const int pos = __ldcg(a.state + 1);
+    int kv_len = __ldcg(a.state + 2);
+    if (kv_len < 1 || kv_len > a.cap || pos < 0 || pos >= a.cap || pos >= a.max_pos || pos != kv_len - 1) {
+        if (tid == 0) atomicOr(a.err, 2);
+        kv_len = max(1, min(kv_len, a.cap));
+    }
+    const int pos_c = max(0, min(pos, min(a.cap, a.max_pos) - 1));
+    {
+        const int half = a.hd / 2;
+        for (int i = tid; i < half; i += kRT) {
+            rope_s[i] = bf16_bits_to_f32(a.rope_cos[static_cast<int64_t>(pos_c) * half + i]);
+            rope_s[half + i] = bf16_bits_to_f32(a.rope_sin[static_cast<int64_t>(pos_c) * half + i]);
+        }
+    }
+    __syncthreads();
+    const RAttPlan ap = ratt_plan(a, kv_len);
+    const bool att_cta = static_cast<int>(blockIdx.x) < a.kvh * ap.ns;
+    uint32_t att_phase = 0;
+    const bool own_o = rng[kOO * kRngStride + 1] > rng[kOO * kRngStride];
+    const bool own_dn = rng[kODn * kRngStride + 1] > rng[kODn * kRngStride];
+    const bool own_qkv = rng[kOQkv * kRngStride + 1] > rng[kOQkv * kRngStride];
+    const bool own_gu = rng[kOGu * kRngStride + 1] > rng[kOGu * kRngStride];
+    const RTaps to = rtaps(a.hidden, a.qh, a.kvh, a.hd, a.inter);
+    const int hd = a.hd, half = hd / 2;
+
+    RCons cs;
+    cs.slot = 0;
+    cs.parity = 0;
+    cs.failed = false;
+    uint4 wv[kNormPer];
+    for (int l = 0; l < a.nlayers; ++l) {
+        const uint64_t* L = a.layers + static_cast<int64_t>(l) * kTSlots;
+        unsigned* ctr = a.counters + l * kRStride;
+        uint16_t* tap = rtap(a, l);
+        const bool tap0 = tap != nullptr && blockIdx.x == 0;
+        KR_STAMP(l, 0);
+        // ---- x ready -> RMSNorm -> q/k/v owners (bias, RoPE, k/v into the cache row)
+        rnorm_prefetch(a, reinterpret_cast<const uint16_t*>(L[kTInNorm]), wv);
+        if (a.bias_rows > 0) {
+            const int nq = a.qh * hd, nk = a.kvh * hd;
+            for (int i = tid; i < a.bias_rows; i += kRT) {
+                const uint16_t* b =
+                    reinterpret_cast<const uint16_t*>(L[i < nq ? kTQBias : i < nq + nk ? kTKBias : kTVBias]);
+                const int j = i < nq ? i : i < nq + nk ? i - nq : i - nq - nk;
+                bias_s[i] = b != nullptr ? b[j] : static_cast<uint16_t>(0);
+            }
+        }
+        if (l > 0) rwait(a, a.counters + (l - 1) * kRStride + kCDn, static_cast<unsigned>(a.ctas[kODn]));
+        rload_bf16(xres, a.x, a.hidden);
+        __syncthreads();
+        KR_STAMP(l, 1);
+        rstage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn : nullptr);
+        KR_STAMP(l, 2);
+        {
+            uint16_t* kcl = reinterpret_cast<uint16_t*>(L[kTKCache]);
+            uint16_t* vcl = reinterpret_cast<uint16_t*>(L[kTVCache]);
+            const int qt = a.qh * hd / 16, kt = a.kvh * hd / 16, per = hd / 16;
+            const bool bias = a.bias_rows > 0;
+            rgemv<kOQkv>(a, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
+                if (T < qt + kt) {  // q or k: RoPE pair (i, i + half)
+                    const bool isq = T < qt;
+                    const int u = isq ? T : T - qt, head = u / per, i = 8 * (u - head * per) + r;
+                    const int row0 = (isq ? 0 : a.qh * hd) + head * hd + i;
+                    float y0 = round_bf16(ylo), y1 = round_bf16(yhi);
+                    if (bias) {
+                        y0 = round_bf16(y0 + bf16_bits_to_f32(bias_s[row0]));
+                        y1 = round_bf16(y1 + bf16_bits_to_f32(bias_s[row0 + half]));
+                    }
+                    const float c = rope_s[i], sn = rope_s[half + i];
+                    const uint16_t lo = f32_to_bf16_bits(round_bf16(round_bf16(y0 * c) + round_bf16(-y1 * sn)));
+                    const uint16_t hi = f32_to_bf16_bits(round_bf16(round_bf16(y1 * c) + round_bf16(y0 * sn)));
+                    if (isq) {
+                        a.qg[head * hd + i] = lo;
+                        a.qg[head * hd + i + half] = hi;
+                    } else {
+                        kcl[(static_cast<int64_t>(head) * a.cap + pos_c) * hd + i] = lo;
+                        kcl[(static_cast<int64_t>(head) * a.cap + pos_c) * hd + i + half] = hi;
+                    }
+                    if (tap != nullptr) {
+                        uint16_t* tp = tap + (isq ? to.q : to.k) + head * hd + i;
+                        tp[0] = lo;
+                        tp[half] = hi;
+                    }
+                } else {  // v: rows d and d + 8 of a 16-row tile
+                    const int d0 = 16 * (T - qt - kt) + r;
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        const int d = d0 + 8 * k;
+                        float y = round_bf16(k == 0 ? ylo : yhi);
+                        if (bias) y = round_bf16(y + bf16_bits_to_f32(bias_s[(a.qh + a.kvh) * hd + d]));
+                        const uint16_t vb = f32_to_bf16_bits(y);
+                        const int hv = d / hd;
+                        vcl[(static_cast<int64_t>(hv) * a.cap + pos_c) * hd + (d - hv * hd)] = vb;
+                        if (tap != nullptr) tap[to.v + d] = vb;
+                    }
+                }
+            });
+            if (own_qkv) rsignal(ctr + kCQkv);
+        }
+        KR_STAMP(l, 3);
+        // ---- attention splits, merged once per KV head
+        if (att_cta) {
+            const RAttSmem sm = ratt_smem(work);
+            const int hk = static_cast<int>(blockIdx.x) / ap.ns, sp = static_cast<int>(blockIdx.x) - hk * ap.ns;
+            const int tok0 = sp * ap.ts;
+            const uint16_t* kc = reinterpret_cast<const uint16_t*>(L[kTKCache]) + static_cast<int64_t>(hk) * a.cap * hd;
+            const uint16_t* vc = reinterpret_cast<const uint16_t*>(L[kTVCache]) + static_cast<int64_t>(hk) * a.cap * hd;
+            fence_proxy_async_smem();  // the tile rows' earlier generic accesses (xs, partials) before the copies
+            __syncthreads();
+            if (warp == 0) ratt_issue(kc, vc, tok0, min(kATile, kv_len - tok0), sm, &att_bar);
+            rwait(a, ctr + kCQkv, static_cast<unsigned>(a.ctas[kOQkv]));
+            KR_STAMP(l, 4);
+            rattention(a, l, L, pos_c, kv_len, ap, sm, &att_bar, att_phase, &flag);
+            KR_STAMP(l, 5);
+        }
+        // ---- o_proj owners: x1 = x + o_proj(attention)
+        rnorm_prefetch(a, reinterpret_cast<const uint16_t*>(L[kTPostNorm]), wv);
+        if (own_o) {
+            rwait(a, ctr + kCAtt, static_cast<unsigned>(a.kvh));
+            KR_STAMP(l, 6);
+            rstage_f16(a, xs, a.attg, a.qh * hd);
+            KR_STAMP(l, 7);
+            rgemv<kOO>(a, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    const int row = 16 * T + r + 8 * k;
+                    const float o = round_bf16(k == 0 ? ylo : yhi);
+                    const uint16_t x1 = f32_to_bf16_bits(bf16_bits_to_f32(xres[row]) + o);
+                    a.x1g[row] = x1;
+                    if (tap != nullptr) tap[to.x1 + row] = x1;
+                }
+            });
+            rsignal(ctr + kCO);
+            KR_STAMP(l, 8);
+        }
+        // ---- x1 ready -> RMSNorm -> gate/up owners (SwiGLU)
+        rwait(a, ctr + kCO, static_cast<unsigned>(a.ctas[kOO]));
+        KR_STAMP(l, 9);
+        rload_bf16(xres, a.x1g, a.hidden);
+        __syncthreads();
+        rstage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn2 : nullptr);
+        KR_STAMP(l, 10);
+        {
+            bool overflow = false;
+            rgemv<kOGu>(a, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
+                const int j = 8 * T + r;
+                const float gv = round_bf16(ylo), uv = round_bf16(yhi);
+                const float act = round_bf16(gv / (1.0F + expf(-gv)));
+                const uint16_t h = f32_to_bf16_bits(act * uv);
+                a.hg[j] = h;
+                overflow |= !(fabsf(bf16_bits_to_f32(h)) <= 65504.F);
+                if (tap != nullptr) tap[to.h + j] = h;
+            });
+            if (overflow) atomicOr(a.err, 1);
+            if (own_gu) rsignal(ctr + kCGu);
+        }
+        KR_STAMP(l, 11);
+        // ---- down owners: x2 = x1 + down(h), the next layer's input
+        if (own_dn) {
+            rwait(a, ctr + kCGu, static_cast<unsigned>(a.ctas[kOGu]));
+            KR_STAMP(l, 12);
+            rstage_f16(a, xs, a.hg, a.inter);
+            KR_STAMP(l, 13);
+            rgemv<kODn>(a, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    const int row = 16 * T + r + 8 * k;
+                    const float d = round_bf16(k == 0 ? ylo : yhi);
+                    const uint16_t x2 = f32_to_bf16_bits(bf16_bits_to_f32(xres[row]) + d);
+                    a.x[row] = x2;
+                    if (tap != nullptr) tap[to.x2 + row] = x2;
+                }
+            });
+            rsignal(ctr + kCDn);
+            KR_STAMP(l, 14);
+        }
+    }
+    // ---- the last CTA to finish resets the counters for the next step
+    // (every issued copy has been consumed: the stream and the consumers walk
+    // the same unit sequence); the kernel's end makes x final for the lm_head
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(a.misc + 1, 1u);
+        if (old == gridDim.x - 1) {
+            for (int i = 0; i < a.nlayers * kRStride; ++i) a.counters[i] = 0u;
+            a.misc[0] = 0u;
+            a.misc[1] = 0u;
+            __threadfence();
+        }
+    }
+}
+
+// ------------------------------------------------------------------ re-tiling into 16-row tiles
+struct Retile16Args {
+    const uint8_t* packed[3];
+    const float* absmax[3];
+    int rows[3];
+    int mode, K, hd, tiles;
+    uint8_t* out;
+};
+__device__ __forceinline__ void tile16_row(const Retile16Args& r, int tile, int rr, int& m, int& row) {
+    if (r.mode == kRetilePlain) {
+        m = 0;
+        row = 16 * tile + rr;
+    } else if (r.mode == kRetileSwiGlu) {
+        m = rr < 8 ? 0 : 1;
+        row = 8 * tile + (rr & 7);
+    } else {  // q / k heads in tiles of 8 RoPE pairs, then 16-row v tiles
+        const int per = r.hd / 16;
+        const int qt = r.rows[0] / r.hd * per, kt = r.rows[1] / r.hd * per;
+        if (tile < qt + kt) {
+            m = tile < qt ? 0 : 1;
+            const int u = tile < qt ? tile : tile - qt;
+            const int head = u / per, mm = u - head * per;
+            row = head * r.hd + 8 * mm + (rr & 7) + (rr >= 8 ? r.hd / 2 : 0);
+        } else {
+            m = 2;
+            row = 16 * (tile - qt - kt) + rr;
+        }
+    }
+}
+__global__ void nf4_retile16_kernel(const Retile16Args r) {
+    const int nbpt = r.K / 64;
+    const int64_t total = static_cast<int64_t>(r.tiles) * nbpt * 32;  // 32 lanes x 16 code bytes per unit
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t unit = i >> 5;
+        const int l = static_cast<int>(i & 31);
+        const int tile = static_cast<int>(unit / nbpt), b = static_cast<int>(unit - static_cast<int64_t>(tile) * nbpt);
+        const int g = l >> 2, t = l & 3;
+        int mA, rowA, mB, rowB;
+        tile16_row(r, tile, g, mA, rowA);
+        tile16_row(r, tile, g + 8, mB, rowB);
+        const uint2 pa = *reinterpret_cast<const uint2*>(r.packed[mA] + static_cast<int64_t>(rowA) * (r.K / 2) + 32 * b + 8 * t);
+        const uint2 pb = *reinterpret_cast<const uint2*>(r.packed[mB] + static_cast<int64_t>(rowB) * (r.K / 2) + 32 * b + 8 * t);
+        uint8_t* u = r.out + unit * kUnitBytes;
+        reinterpret_cast<uint4*>(u)[l] = make_uint4(pa.x, pa.y, pb.x, pb.y);
+        if (l < 16) {
+            int m, row;
+            tile16_row(r, tile, l, m, row);
+            reinterpret_cast<float*>(u + kUnitCodes)[l] = r.absmax[m][static_cast<int64_t>(row) * nbpt + b];
+        }
+    }
+}
+
+// ------------------------------------------------------------------ launch geometry
+struct RowGeom {
+    int tiles[4], nbpt[4], ctas[4];
+    int xs_bytes, work_bytes, bias_rows, ring_slots, smem;
+    int64_t off_misc, off_qg, off_attg, off_x1g, off_hg, off_apart, total;
+};
+constexpr int kRStaticSmemBudget = 3072;
+
+RowGeom row_geom(const PersistDims& d, int sms) {
+    RowGeom g;
+    g.tiles[kOQkv] = (d.q_heads + 2 * d.kv_heads) * d.head_dim / 16;
+    g.nbpt[kOQkv] = d.hidden / 64;
+    g.tiles[kOO] = d.hidden / 16;
+    g.nbpt[kOO] = d.q_heads * d.head_dim / 64;
+    g.tiles[kOGu] = d.intermediate / 8;
+    g.nbpt[kOGu] = d.hidden / 64;
+    g.tiles[kODn] = d.hidden / 16;
+    g.nbpt[kODn] = d.intermediate / 64;
+    for (int i = 0; i < 4; ++i) g.ctas[i] = g.tiles[i] < sms ? g.tiles[i] : sms;
+    int kmax = d.hidden > d.intermediate ? d.hidden : d.intermediate;
+    kmax = kmax > d.q_heads * d.head_dim ? kmax : d.q_heads * d.head_dim;
+    g.xs_bytes = (kmax * 2 + 127) & ~127;
+    const int work = g.xs_bytes + kMaxCtaTiles * kRW * 16 * 4;
+    g.work_bytes = ((work > kRAttSmemBytes ? work : kRAttSmemBytes) + 127) & ~127;
+    g.bias_rows = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
+    const int tail = ((d.hidden + 63) & ~63) * 2 + ((g.bias_rows + 63) & ~63) * 2 + d.head_dim * 4;
+    const int limit = 232448 - kRStaticSmemBudget;
+    g.ring_slots = kRMaxSlots;
+    while (g.ring_slots > 1 && kRLutBytes + kRW * g.ring_slots * kSlotBytes + g.work_bytes + tail > limit) --g.ring_slots;
+    g.smem = kRLutBytes + kRW * g.ring_slots * kSlotBytes + g.work_bytes + tail;
+    auto up = [](int64_t v) { return (v + 255) & ~static_cast<int64_t>(255); };
+    const int gq = d.kv_heads > 0 ? d.q_heads / d.kv_heads : 1;
+    int64_t off = up(static_cast<int64_t>(d.layers) * kRStride * 4);
+    g.off_misc = off;
+    off = up(off + 64);
+    g.off_qg = off;
+    off = up(off + static_cast<int64_t>(d.q_heads) * d.head_dim * 2);
+    g.off_attg = off;
+    off = up(off + static_cast<int64_t>(d.q_heads) * d.head_dim * 2);
+    g.off_x1g = off;
+    off = up(off + static_cast<int64_t>(d.hidden) * 2);
+    g.off_hg = off;
+    off = up(off + static_cast<int64_t>(d.intermediate) * 2);
+    g.off_apart = off;
+    off = up(off + static_cast<int64_t>(d.kv_heads) * kAMaxSplits * gq * (d.head_dim + 4) * 4);
+    g.total = off;
+    return g;
+}
+}  // namespace
+
+int retile16_tiles(int mode, int rows0, int rows1, int rows2, int head_dim) {
+    if (mode == kRetilePlain) return rows0 % 16 == 0 && rows0 > 0 ? rows0 / 16 : -1;
+    if (mode == kRetileSwiGlu) return rows0 == rows1 && rows0 % 8 == 0 && rows0 > 0 ? rows0 / 8 : -1;
+    if (mode == kRetileQkvRope) {
+        if (head_dim < 16 || head_dim % 16 != 0 || rows0 % head_dim != 0 || rows1 % head_dim != 0 || rows1 != rows2 ||
+            rows0 <= 0 || rows1 <= 0 || rows2 % 16 != 0)
+            return -1;
+        return rows0 / head_dim * (head_dim / 16) + rows1 / head_dim * (head_dim / 16) + rows2 / 16;
+    }
+    return -1;
+}
+
+cudaError_t nf4_retile16(int mode, const uint8_t* const* packed, const float* const* absmax, const int* rows, int K,
+                         int head_dim, uint8_t* out, cudaStream_t stream) {
+    Retile16Args r;
+    for (int i = 0; i < 3; ++i) {
+        r.packed[i] = packed[i];
+        r.absmax[i] = absmax[i];
+        r.rows[i] = rows[i];
+    }
+    r.mode = mode;
+    r.K = K;
+    r.hd = head_dim;
+    r.tiles = retile16_tiles(mode, rows[0], rows[1], rows[2], head_dim);
+    if (r.tiles < 1 || K < 64 || K % 64 != 0) return cudaErrorInvalidValue;
+    r.out = out;
+    const int64_t total = static_cast<int64_t>(r.tiles) * (K / 64) * 32;
+    const int threads = 256;
+    const int64_t blocks = (total + threads - 1) / threads;
+    nf4_retile16_kernel<<<static_cast<unsigned>(blocks < 65535 * 16 ? blocks : 65535 * 16), threads, 0, stream>>>(r);
+    return cudaGetLastError();
+}
+
+int64_t decode_rows_scratch_bytes(const PersistDims& d, int sms) { return row_geom(d, sms).total; }
+
+const char* decode_rows_check(const PersistDims& d, int sms) {
+    if (d.layers < 1 || d.hidden < 64 || d.hidden % 64 != 0 || d.head_dim != 128 || d.q_heads < 1 || d.kv_heads < 1 ||
+        d.q_heads % d.kv_heads != 0 || d.q_heads / d.kv_heads > 8 || d.intermediate % 64 != 0 ||
+        d.hidden > 8 * kRT * kNormPer || d.kv_capacity < 1 || d.kv_heads > sms || d.kv_heads + kCTicket > kRStride)
+        return "row-split persistent decode requires hidden % 64 == 0 (<= 16384), head_dim 128, q_heads/kv_heads <= 8, "
+               "kv_heads <= 11, intermediate % 64 == 0";
+    const RowGeom g = row_geom(d, sms);
+    if (g.smem > 232448 - kRStaticSmemBudget) return "row-split persistent decode: shapes need more shared memory than one SM has";
+    for (int i = 0; i < 4; ++i) {
+        if ((g.tiles[i] + sms - 1) / sms > kMaxCtaTiles) return "row-split persistent decode: an op has more than 16 tiles per SM";
+        if (static_cast<int64_t>(g.tiles[i]) * g.nbpt[i] >= (int64_t{1} << 30)) return "row-split persistent decode: an op is too large";
+    }
+    return nullptr;
+}
+
+int64_t decode_rows_tap_stride(const PersistDims& d) {
+    return rtaps(d.hidden, d.q_heads, d.kv_heads, d.head_dim, d.intermediate).stride;
+}
+
+cudaError_t decode_layers_rows(const PersistLaunch& p, cudaStream_t stream) {
+    const int sms = device_sm_count();
+    const RowGeom g = row_geom(p.dims, sms);
+    RowArgs a;
+    a.layers = p.layer_table;
+    a.nlayers = p.dims.layers;
+    a.hidden = p.dims.hidden;
+    a.qh = p.dims.q_heads;
+    a.kvh = p.dims.kv_heads;
+    a.hd = p.dims.head_dim;
+    a.inter = p.dims.intermediate;
+    a.cap = p.dims.kv_capacity;
+    a.max_pos = p.max_pos;
+    a.eps = p.eps;
+    a.scale_log2 = p.scale * 1.4426950408889634F;
+    a.state = p.state;
+    a.x = p.x;
+    a.rope_cos = p.rope_cos;
+    a.rope_sin = p.rope_sin;
+    char* s = static_cast<char*>(p.scratch);
+    a.counters = reinterpret_cast<unsigned*>(s);
+    a.misc = reinterpret_cast<unsigned*>(s + g.off_misc);
+    a.qg = reinterpret_cast<uint16_t*>(s + g.off_qg);
+    a.attg = reinterpret_cast<uint16_t*>(s + g.off_attg);
+    a.x1g = reinterpret_cast<uint16_t*>(s + g.off_x1g);
+    a.hg = reinterpret_cast<uint16_t*>(s + g.off_hg);
+    a.apart = reinterpret_cast<float*>(s + g.off_apart);
+    a.err = p.err;
+    a.ring_slots = g.ring_slots;
+    for (int i = 0; i < 4; ++i) {
+        a.tiles[i] = g.tiles[i];
+        a.nbpt[i] = g.nbpt[i];
+        a.ctas[i] = g.ctas[i];
+    }
+    a.xs_bytes = g.xs_bytes;
+    a.work_bytes = g.work_bytes;
+    a.bias_rows = g.bias_rows;
+    a.taps = p.taps;
+    a.tap_stride = rtaps(p.dims.hidden, p.dims.q_heads, p.dims.kv_heads, p.dims.head_dim, p.dims.intermediate).stride;
+    a.spin_limit = p.spin_limit > 0 ? p.spin_limit : kRSpinLimit;
+    a.stall_counter = p.stall_counter;
+    cudaError_t st = cudaFuncSetAttribute(decode_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, g.smem);
+    if (st != cudaSuccess) return st;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(sms));
+    cfg.blockDim = dim3(kRT);
+    cfg.dynamicSmemBytes = static_cast<size_t>(g.smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;  // every CTA resident at once: they wait on each other
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, decode_rows_kernel, a);
+}
+
+}  // namespace kc

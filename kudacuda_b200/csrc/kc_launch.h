@@ -193,6 +193,14 @@ struct PersistLaunch {
 };
 // elements of one layer's tap record of the persistent kernel
 int64_t decode_persistent_tap_stride(const PersistDims& d);
+// ---- row-split persistent decode (decode_rows.cu): 16-row tiles, each owned by one CTA
+int retile16_tiles(int mode, int rows0, int rows1, int rows2, int head_dim);
+cudaError_t nf4_retile16(int mode, const uint8_t* const* packed, const float* const* absmax, const int* rows, int K,
+                         int head_dim, uint8_t* out, cudaStream_t stream);
+int64_t decode_rows_scratch_bytes(const PersistDims& d, int sms);
+const char* decode_rows_check(const PersistDims& d, int sms);
+int64_t decode_rows_tap_stride(const PersistDims& d);
+cudaError_t decode_layers_rows(const PersistLaunch& p, cudaStream_t stream);
 // ---- batched decode (batched.cu) ----------------------------------------------
 // NF4 (weight_type 0), bf16 (1) or re-tiled NF4 (2) weights [rows][K] times bf16 activations
 // [n_pad][K] (rows >= batch zero) on the tcgen05 tensor cores: fp32 split-K

@@ -1076,6 +1076,110 @@ int kudacuda_sm100_decode_layers_persistent_debug(void* raw, uint64_t layer_tabl
     return finish(h, "decode_layers_kernel", kc::decode_layers_persistent(p, S(stream)));
 }
 
+// ---------------------------------------------------------------- row-split persistent decode
+int64_t kudacuda_sm100_nf4_retile16_tiles(int mode, int64_t rows0, int64_t rows1, int64_t rows2, int64_t head_dim) {
+    if (rows0 < 0 || rows1 < 0 || rows2 < 0 || head_dim < 0 || rows0 > (1 << 24) || rows1 > (1 << 24) ||
+        rows2 > (1 << 24) || head_dim > 4096)
+        return -1;
+    return kc::retile16_tiles(mode, static_cast<int>(rows0), static_cast<int>(rows1), static_cast<int>(rows2),
+                              static_cast<int>(head_dim));
+}
+
+int kudacuda_sm100_nf4_retile16(void* raw, int mode, uint64_t packed0, uint64_t absmax0, int64_t rows0,
+                                uint64_t packed1, uint64_t absmax1, int64_t rows1, uint64_t packed2, uint64_t absmax2,
+                                int64_t rows2, int64_t k, int64_t head_dim, uint64_t out_units, int64_t out_bytes,
+                                uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_nf4_retile16")) return 1;
+    const int64_t tiles = kudacuda_sm100_nf4_retile16_tiles(mode, rows0, rows1, rows2, head_dim);
+    const bool need1 = mode != kc::kRetilePlain, need2 = mode == kc::kRetileQkvRope;
+    if (tiles < 1 || k < 64 || k % 64 != 0 || k > (1 << 20) || packed0 == 0 || absmax0 == 0 || out_units == 0 ||
+        (need1 && (packed1 == 0 || absmax1 == 0)) || (need2 && (packed2 == 0 || absmax2 == 0))) {
+        h->set_error("sm100_nf4_retile16 requires mode 0 (plain, rows % 16 == 0), 1 (SwiGLU, gate rows == up rows, "
+                     "% 8 == 0) or 2 (q/k/v, head_dim % 16 == 0), K % 64 == 0 and non-null pointers");
+        return 1;
+    }
+    if (out_bytes < tiles * (k / 64) * 576) {
+        h->set_error("sm100_nf4_retile16: output is smaller than tiles * (k / 64) * 576 bytes");
+        return 1;
+    }
+    const uint8_t* packed[3] = {P<const uint8_t>(packed0), P<const uint8_t>(packed1), P<const uint8_t>(packed2)};
+    const float* absmax[3] = {P<const float>(absmax0), P<const float>(absmax1), P<const float>(absmax2)};
+    const int rows[3] = {static_cast<int>(rows0), static_cast<int>(rows1), static_cast<int>(rows2)};
+    return finish(h, "nf4_retile16_kernel",
+                  kc::nf4_retile16(mode, packed, absmax, rows, static_cast<int>(k), static_cast<int>(head_dim),
+                                   P<uint8_t>(out_units), S(stream)));
+}
+
+int64_t kudacuda_sm100_decode_rows_scratch_bytes(void* raw, int64_t layers, int64_t hidden, int64_t q_heads,
+                                                int64_t kv_heads, int64_t head_dim, int64_t intermediate,
+                                                int64_t kv_capacity) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_decode_rows_scratch_bytes")) return -1;
+    kc::PersistDims d;
+    if (!persist_dims(layers, hidden, q_heads, kv_heads, head_dim, intermediate, kv_capacity, d)) return -1;
+    const int sms = kc::device_sm_count();
+    if (const char* why = kc::decode_rows_check(d, sms)) {
+        h->set_error(why);
+        return -1;
+    }
+    return kc::decode_rows_scratch_bytes(d, sms);
+}
+
+int kudacuda_sm100_decode_layers_rows(void* raw, uint64_t layer_table, int64_t layers, uint64_t x, uint64_t state,
+                                      uint64_t rope_cos, uint64_t rope_sin, int64_t max_pos, uint64_t scratch,
+                                      int64_t scratch_bytes, int64_t hidden, int64_t q_heads, int64_t kv_heads,
+                                      int64_t head_dim, int64_t intermediate, int64_t kv_capacity, float eps,
+                                      float scale, uint64_t taps, int64_t taps_bytes, int64_t spin_limit,
+                                      int64_t stall_counter, uint64_t stream) {
+    Handle* h = as_handle(raw);
+    if (!ready(h, "kudacuda_sm100_decode_layers_rows")) return 1;
+    kc::PersistDims d;
+    if (!persist_dims(layers, hidden, q_heads, kv_heads, head_dim, intermediate, kv_capacity, d) || max_pos < 1 ||
+        max_pos > (1 << 24) || !(eps > 0.0F) || !(scale > 0.0F)) {
+        h->set_error("sm100_decode_layers_rows requires positive shapes, max_pos, eps and scale");
+        return 1;
+    }
+    if (layer_table == 0 || x == 0 || state == 0 || rope_cos == 0 || rope_sin == 0 || scratch == 0) {
+        h->set_error("sm100_decode_layers_rows requires non-null device pointers");
+        return 1;
+    }
+    const int sms = kc::device_sm_count();
+    if (const char* why = kc::decode_rows_check(d, sms)) {
+        h->set_error(why);
+        return 1;
+    }
+    if (scratch_bytes < kc::decode_rows_scratch_bytes(d, sms)) {
+        h->set_error("sm100_decode_layers_rows scratch is smaller than kudacuda_sm100_decode_rows_scratch_bytes()");
+        return 1;
+    }
+    if (taps != 0 && taps_bytes < 2 * layers * kc::decode_rows_tap_stride(d)) {
+        h->set_error("sm100_decode_layers_rows: taps buffer is smaller than 2 * kudacuda_sm100_decode_persistent_tap_elements() bytes");
+        return 1;
+    }
+    if (spin_limit < 0 || spin_limit > (int64_t{1} << 30) || stall_counter < -1 || stall_counter >= layers * 16) {
+        h->set_error("sm100_decode_layers_rows: spin_limit must be 0..2^30 (0: default) and stall_counter -1 or a "
+                     "counter index below layers * 16");
+        return 1;
+    }
+    kc::PersistLaunch p;
+    p.layer_table = P<const uint64_t>(layer_table);
+    p.dims = d;
+    p.max_pos = static_cast<int>(max_pos);
+    p.eps = eps;
+    p.scale = scale;
+    p.state = P<const int32_t>(state);
+    p.x = P<uint16_t>(x);
+    p.rope_cos = P<const uint16_t>(rope_cos);
+    p.rope_sin = P<const uint16_t>(rope_sin);
+    p.scratch = P<void>(scratch);
+    p.err = h->err_word;
+    p.taps = P<uint16_t>(taps);
+    p.spin_limit = static_cast<uint32_t>(spin_limit);
+    p.stall_counter = static_cast<int>(stall_counter);
+    return finish(h, "decode_rows_kernel", kc::decode_layers_rows(p, S(stream)));
+}
+
 // ---------------------------------------------------------------- batched decode
 namespace {
 bool npad_ok(int64_t n_pad) { return n_pad == 16 || n_pad == 32 || n_pad == 64; }

@@ -416,17 +416,26 @@ def _buffer_ptrs(t: Any) -> list[int]:
 class PersistentLayers:
     """Device data of the persistent decode path for one plan: every layer's
     q/k/v, o, gate/up and down weights copied once into the stream layout of
-    ``kudacuda_sm100_decode_layers_persistent`` (the bitsandbytes tensors stay
-    as they are for the per-op ABI), the device layer table and the kernel's
-    self-resetting scratch."""
+    the persistent kernel (the bitsandbytes tensors stay as they are for the
+    per-op ABI), the device layer table and the kernel's self-resetting
+    scratch.
+
+    ``layout="rows"`` (default): kudacuda_sm100_decode_layers_rows -- 16-row
+    tiles, each owned by one CTA that finishes its rows (576-byte units from
+    kudacuda_sm100_nf4_retile16).  ``layout="groups"``:
+    kudacuda_sm100_decode_layers_persistent -- 64-row groups split over CTAs
+    along K, partial sums summed by the consumers."""
 
     SLOTS = 16
 
-    def __init__(self, plan: "StaticDecodePlan") -> None:
+    def __init__(self, plan: "StaticDecodePlan", layout: str = "rows") -> None:
+        if layout not in ("rows", "groups"):
+            raise ValueError(f"unknown persistent layout {layout!r}")
         torch = plan.torch
         br, c, w, b = plan.bridge, plan.config, plan.weights, plan.buffers
         dev = plan.device
         self.plan = plan
+        self.layout = layout
         sp = int(torch.cuda.current_stream(dev).cuda_stream)
         d = c.head_dim
         self.tiles: list[tuple[Any, ...]] = []
@@ -443,42 +452,55 @@ class PersistentLayers:
             row: list[int] = []
             for mode, mats, k in ops:
                 rows = tuple(m[2] for m in mats) + (0,) * (3 - len(mats))
-                groups = br.retile_groups(mode, rows, d)
-                if groups < 1:
-                    raise NativeCudaError(f"persistent decode cannot re-tile layer {li} (mode {mode}, rows {rows})")
-                codes = torch.empty(groups * 64 * k // 2, dtype=torch.uint8, device=dev)
-                absm = torch.empty(groups * 64 * k // 64, dtype=torch.float32, device=dev)
-                br.dispatch_nf4_retile(mode, mats, codes, absm, k=k, head_dim=d, stream_ptr=sp)
-                self.tiles.append((codes, absm))
-                row += [codes.data_ptr(), absm.data_ptr()]
+                if layout == "rows":
+                    tiles = br.retile16_tiles(mode, rows, d)
+                    if tiles < 1:
+                        raise NativeCudaError(f"persistent decode cannot re-tile layer {li} (mode {mode}, rows {rows})")
+                    units = torch.empty(tiles * (k // 64) * 576, dtype=torch.uint8, device=dev)
+                    br.dispatch_nf4_retile16(mode, mats, units, k=k, head_dim=d, stream_ptr=sp)
+                    self.tiles.append((units,))
+                    row.append(units.data_ptr())
+                else:
+                    groups = br.retile_groups(mode, rows, d)
+                    if groups < 1:
+                        raise NativeCudaError(f"persistent decode cannot re-tile layer {li} (mode {mode}, rows {rows})")
+                    codes = torch.empty(groups * 64 * k // 2, dtype=torch.uint8, device=dev)
+                    absm = torch.empty(groups * 64 * k // 64, dtype=torch.float32, device=dev)
+                    br.dispatch_nf4_retile(mode, mats, codes, absm, k=k, head_dim=d, stream_ptr=sp)
+                    self.tiles.append((codes, absm))
+                    row += [codes.data_ptr(), absm.data_ptr()]
             ptr = lambda t: 0 if t is None else int(t.data_ptr())  # noqa: E731
             row += [ptr(L.in_norm), ptr(L.post_norm), ptr(L.q_bias), ptr(L.k_bias), ptr(L.v_bias),
-                    int(b.kcache[li].data_ptr()), int(b.vcache[li].data_ptr()), 0]
+                    int(b.kcache[li].data_ptr()), int(b.vcache[li].data_ptr())]
+            row += [0] * (self.SLOTS - len(row))
             table[li] = torch.tensor(row, dtype=torch.int64)
         self.table = table.to(dev)
-        nbytes = br.persistent_scratch_bytes(layers=c.layers, hidden=c.hidden, q_heads=plan.q_heads,
-                                             kv_heads=plan.kv_heads, head_dim=d, intermediate=plan.inter,
-                                             kv_capacity=plan.kv_bucket)
+        dims = dict(layers=c.layers, hidden=c.hidden, q_heads=plan.q_heads, kv_heads=plan.kv_heads, head_dim=d,
+                    intermediate=plan.inter, kv_capacity=plan.kv_bucket)
+        nbytes = br.rows_scratch_bytes(**dims) if layout == "rows" else br.persistent_scratch_bytes(**dims)
         self.scratch = torch.zeros((nbytes + 3) // 4, dtype=torch.int32, device=dev)
         torch.cuda.synchronize(dev)
 
     def pointers(self) -> list[int]:
         out = [int(self.table.data_ptr()), int(self.scratch.data_ptr())]
-        for codes, absm in self.tiles:
-            out += [int(codes.data_ptr()), int(absm.data_ptr())]
+        for tensors in self.tiles:
+            out += [int(t.data_ptr()) for t in tensors]
         return out
 
     def record(self, stream_ptr: int, *, taps: Any = None, spin_limit: int = 0, stall_counter: int = -1) -> int:
         """Launch the kernel (one launch).  ``taps``/``spin_limit``/``stall_counter``
-        are the test hooks of kudacuda_sm100_decode_layers_persistent_debug."""
+        are the kernel's test hooks."""
 
         p, b, c = self.plan, self.plan.buffers, self.plan.config
-        p.bridge.dispatch_decode_layers_persistent(
-            self.table, b.x, b.state, b.rope_cos, b.rope_sin, self.scratch, layers=c.layers,
-            max_pos=int(b.rope_cos.shape[0]), hidden=c.hidden, q_heads=p.q_heads, kv_heads=p.kv_heads,
-            head_dim=c.head_dim, intermediate=p.inter, kv_capacity=p.kv_bucket, epsilon=c.eps,
-            scale=1.0 / math.sqrt(c.head_dim), stream_ptr=stream_ptr, taps=taps, spin_limit=spin_limit,
-            stall_counter=stall_counter)
+        kw = dict(layers=c.layers, max_pos=int(b.rope_cos.shape[0]), hidden=c.hidden, q_heads=p.q_heads,
+                  kv_heads=p.kv_heads, head_dim=c.head_dim, intermediate=p.inter, kv_capacity=p.kv_bucket,
+                  epsilon=c.eps, scale=1.0 / math.sqrt(c.head_dim), stream_ptr=stream_ptr, taps=taps,
+                  spin_limit=spin_limit, stall_counter=stall_counter)
+        if self.layout == "rows":
+            p.bridge.dispatch_decode_layers_rows(self.table, b.x, b.state, b.rope_cos, b.rope_sin, self.scratch, **kw)
+        else:
+            p.bridge.dispatch_decode_layers_persistent(self.table, b.x, b.state, b.rope_cos, b.rope_sin, self.scratch,
+                                                       **kw)
         return 1
 
     def tap_layout(self) -> dict[str, tuple[int, int]]:
@@ -512,7 +534,7 @@ class StaticDecodePlan:
     def __init__(self, bridge: KudaCudaBridge, weights: ModelWeights, *, kv_bucket: int = 512,
                  max_tokens: Optional[int] = None, device: Any = "cuda:0", torch_module: Any = None,
                  allreduce: Any = None, keep_logits: bool = True, persistent: bool = False,
-                 kv_cache: Optional[tuple[list, list]] = None) -> None:
+                 kv_cache: Optional[tuple[list, list]] = None, persistent_layout: str = "rows") -> None:
         """``kv_cache=(keys, values)``: caller-owned per-layer caches (bf16,
         contiguous, [1 or absent, kv_heads, kv_bucket, head_dim]) used in
         place of the plan's own -- e.g. a Transformers prefill cache."""
@@ -592,7 +614,7 @@ class StaticDecodePlan:
         if persistent:
             if self.tp is not None:
                 raise NativeCudaError("the persistent decode path has no tensor-parallel variant")
-            self.persistent = PersistentLayers(self)
+            self.persistent = PersistentLayers(self, layout=persistent_layout)
 
     @property
     def captured(self) -> bool:
@@ -616,7 +638,8 @@ class StaticDecodePlan:
         d = c.head_dim
         return DecodeGraphKey(
             device_id=int(self.torch.device(self.device).index or 0),
-            tactic_name="decode_step_sm100_persistent_v1" if self.persistent is not None else "decode_step_sm100_v1",
+            tactic_name=("decode_step_sm100_v1" if self.persistent is None else
+                         f"decode_step_sm100_persistent_{self.persistent.layout}_v1"),
             layer_count=c.layers,
             query_shape=(1, self.q_heads, 1, d),
             key_shape=(1, self.kv_heads, self.kv_bucket, d),

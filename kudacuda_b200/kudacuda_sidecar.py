@@ -1112,6 +1112,54 @@ class KudaCudaBridge:
                    self._tensor_pointer(out_codes, "out_codes"), self._tensor_pointer(out_absmax, "out_absmax"),
                    _normalize_cuda_handle(stream_ptr))
 
+    def retile16_tiles(self, mode: int, rows: tuple[int, int, int], head_dim: int = 0) -> int:
+        """16-row tiles of the row-split persistent layout, or -1 for an unsupported shape."""
+
+        self._check_open()
+        return int(self.lib.kudacuda_sm100_nf4_retile16_tiles(int(mode), int(rows[0]), int(rows[1]), int(rows[2]),
+                                                              int(head_dim)))
+
+    def dispatch_nf4_retile16(self, mode: int, mats: list[tuple[Any, Any, int]], out_units: Any, *, k: int,
+                              head_dim: int = 0, stream_ptr: int) -> None:
+        """Copy bitsandbytes NF4 matrices ``(packed, absmax, rows)`` into the
+        row-split persistent kernel's 576-byte units (tile-major)."""
+
+        args: list[int] = []
+        for i in range(3):
+            if i < len(mats):
+                packed, absmax, rows = mats[i]
+                args += [self._tensor_pointer(packed, "packed"), self._tensor_pointer(absmax, "absmax"), int(rows)]
+            else:
+                args += [0, 0, 0]
+        self._call("kudacuda_sm100_nf4_retile16", int(mode), *args, int(k), int(head_dim),
+                   self._tensor_pointer(out_units, "out_units"), int(out_units.numel()) * int(out_units.element_size()),
+                   _normalize_cuda_handle(stream_ptr))
+
+    def rows_scratch_bytes(self, *, layers: int, hidden: int, q_heads: int, kv_heads: int, head_dim: int,
+                           intermediate: int, kv_capacity: int) -> int:
+        self._check_open()
+        n = int(self.lib.kudacuda_sm100_decode_rows_scratch_bytes(
+            self.engine_handle, int(layers), int(hidden), int(q_heads), int(kv_heads), int(head_dim),
+            int(intermediate), int(kv_capacity)))
+        if n < 0:
+            raise NativeCudaError(f"kudacuda_sm100_decode_rows_scratch_bytes: {self._native_error()}")
+        return n
+
+    def dispatch_decode_layers_rows(self, layer_table: Any, x: Any, state: Any, rope_cos: Any, rope_sin: Any,
+                                    scratch: Any, *, layers: int, max_pos: int, hidden: int, q_heads: int,
+                                    kv_heads: int, head_dim: int, intermediate: int, kv_capacity: int, epsilon: float,
+                                    scale: float, stream_ptr: int, taps: Any = None, spin_limit: int = 0,
+                                    stall_counter: int = -1) -> None:
+        tp = 0 if taps is None else self._tensor_pointer(taps, "taps")
+        tb = 0 if taps is None else int(taps.numel()) * int(taps.element_size())
+        self._call("kudacuda_sm100_decode_layers_rows", self._tensor_pointer(layer_table, "layer_table"), int(layers),
+                   self._tensor_pointer(x, "x"), self._tensor_pointer(state, "state"),
+                   self._tensor_pointer(rope_cos, "rope_cos"), self._tensor_pointer(rope_sin, "rope_sin"),
+                   int(max_pos), self._tensor_pointer(scratch, "scratch"),
+                   int(scratch.numel()) * int(scratch.element_size()), int(hidden), int(q_heads), int(kv_heads),
+                   int(head_dim), int(intermediate), int(kv_capacity), float(epsilon), float(scale), tp, tb,
+                   int(spin_limit), int(stall_counter), _normalize_cuda_handle(stream_ptr))
+
     def persistent_scratch_bytes(self, *, layers: int, hidden: int, q_heads: int, kv_heads: int, head_dim: int,
                                  intermediate: int, kv_capacity: int) -> int:
         self._check_open()

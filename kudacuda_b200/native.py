@@ -79,6 +79,16 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         [_p, _u64, _i64, _u64, _u64, _u64, _u64, _i64, _u64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _f32,
          _u64, _i64, _i64, _i64, _u64],
     ),
+    "kudacuda_sm100_nf4_retile16_tiles": (_i64, [_i32, _i64, _i64, _i64, _i64]),
+    "kudacuda_sm100_nf4_retile16": (
+        _i32, [_p, _i32, _u64, _u64, _i64, _u64, _u64, _i64, _u64, _u64, _i64, _i64, _i64, _u64, _i64, _u64]
+    ),
+    "kudacuda_sm100_decode_rows_scratch_bytes": (_i64, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _i64]),
+    "kudacuda_sm100_decode_layers_rows": (
+        _i32,
+        [_p, _u64, _i64, _u64, _u64, _u64, _u64, _i64, _u64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _f32,
+         _u64, _i64, _i64, _i64, _u64],
+    ),
     "kudacuda_sm100_batch_gemm_ksplit": (_i64, [_i64, _i64]),
     "kudacuda_sm100_batch_gemm": (_i32, [_p, _i32, _u64, _u64, _i64, _i64, _u64, _i64, _i64, _u64, _i64, _i64, _u64]),
     "kudacuda_sm100_batch_retile_bytes": (_i64, [_i64, _i64]),

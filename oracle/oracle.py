@@ -361,6 +361,71 @@ def retile_nf4(mode: int, mats: list[tuple[np.ndarray, np.ndarray, int]], k: int
     return codes.reshape(-1), ab.reshape(-1)
 
 
+def tile16_rows(mode: int, rows: tuple[int, int, int], head_dim: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """(matrix index, source row) of every row of every 16-row tile, shaped
+    [tiles, 16] -- the row-complete layout of the persistent decode kernel.
+
+    plain: tile t rows 16t .. 16t+15; SwiGLU: rows 0..7 are gate rows 8t..8t+7,
+    rows 8..15 the matching up rows; q/k/v: each q head, then each k head, in
+    tiles of 8 RoPE pairs (row r < 8 is element 8m + r of the head's first
+    half, row r + 8 its partner in the second half), then tiles of 16
+    consecutive v rows."""
+
+    r16 = np.arange(16)
+    if mode == RETILE_PLAIN:
+        t = rows[0] // 16
+        return np.zeros((t, 16), dtype=np.int64), np.arange(t)[:, None] * 16 + r16[None, :]
+    if mode == RETILE_SWIGLU:
+        t = rows[0] // 8
+        m = np.broadcast_to((r16 >= 8).astype(np.int64), (t, 16)).copy()
+        return m, np.arange(t)[:, None] * 8 + (r16 & 7)[None, :]
+    if mode == RETILE_QKV_ROPE:
+        hd = head_dim
+        per = hd // 16  # tiles per head: hd/2 first-half elements, 8 per tile
+        qt, kt, vt = rows[0] // hd * per, rows[1] // hd * per, rows[2] // 16
+        ms, rs = [], []
+        for tile in range(qt + kt + vt):
+            if tile < qt + kt:
+                mat = 0 if tile < qt else 1
+                u = tile if tile < qt else tile - qt
+                head, mm = divmod(u, per)
+                ms.append(np.full(16, mat))
+                rs.append(head * hd + 8 * mm + (r16 & 7) + np.where(r16 >= 8, hd // 2, 0))
+            else:
+                ms.append(np.full(16, 2))
+                rs.append(16 * (tile - qt - kt) + r16)
+        return np.stack(ms).astype(np.int64), np.stack(rs).astype(np.int64)
+    raise ValueError(f"unknown re-tile mode {mode}")
+
+
+def retile_tiles16(mode: int, mats: list[tuple[np.ndarray, np.ndarray, int]], k: int, head_dim: int = 0) -> np.ndarray:
+    """bitsandbytes matrices -> units u8 [tiles * (k/64) * 576], tile-major.
+
+    Unit (tile, block b): 512 code bytes, lane 4g + t holding bytes
+    [32b + 8t, +8) of tile row g then of tile row g + 8 (its m16n8k16 A
+    fragments), then the 16 rows' fp32 absmax of block b in row order."""
+
+    rows = tuple(m[2] for m in mats) + (0,) * (3 - len(mats))
+    msel, rsel = tile16_rows(mode, rows, head_dim)
+    tiles, nbpt = msel.shape[0], k // 64
+    packed = [np.asarray(pk, dtype=np.uint8).reshape(n, k // 2) for pk, _, n in mats]
+    absm = [np.asarray(a, dtype=np.float32).reshape(n, nbpt) for _, a, n in mats]
+    data = np.zeros((tiles, 16, k // 2), dtype=np.uint8)
+    amax = np.zeros((tiles, 16, nbpt), dtype=np.float32)
+    for mi in range(len(mats)):
+        sel = msel == mi
+        data[sel] = packed[mi][rsel[sel]]
+        amax[sel] = absm[mi][rsel[sel]]
+    d = data.reshape(tiles, 16, nbpt, 4, 8)  # [tile][row][block][t][8 bytes]
+    codes = np.empty((tiles, nbpt, 8, 4, 16), dtype=np.uint8)  # [tile][block][g][t][16]
+    codes[..., :8] = d[:, :8].transpose(0, 2, 1, 3, 4)
+    codes[..., 8:] = d[:, 8:].transpose(0, 2, 1, 3, 4)
+    units = np.empty((tiles, nbpt, 576), dtype=np.uint8)
+    units[:, :, :512] = codes.reshape(tiles, nbpt, 512)
+    units[:, :, 512:] = np.ascontiguousarray(amax.transpose(0, 2, 1)).view(np.uint8).reshape(tiles, nbpt, 64)
+    return units.reshape(-1)
+
+
 # ---------------------------------------------------------------- batched decode GEMM
 def batch_gemm_ref(packed: np.ndarray, absmax: np.ndarray | None, rows: int, k: int, x_bits: np.ndarray,
                    weight_type: int = 0) -> tuple[np.ndarray, np.ndarray]:

@@ -43,8 +43,48 @@ def tiny_persistent():
 
 
 @pytest.mark.parametrize("which", ["qkv", "o", "gate_up", "down"])
-def test_device_retile_matches_oracle(tiny_persistent, which):
+def test_device_retile16_matches_oracle(tiny_persistent, which):
+    """The row-split layout (default): 576-byte units, bit-exact."""
+
     cfg, bridge, w, plan, stream = tiny_persistent
+    assert plan.persistent.layout == "rows"
+    L = w.layers[1]
+    idx = {"qkv": 0, "o": 1, "gate_up": 2, "down": 3}[which]
+    (units,) = plan.persistent.tiles[4 + idx]  # layer 1
+    mode, lins = {
+        "qkv": (O.RETILE_QKV_ROPE, [L.q, L.k, L.v]),
+        "o": (O.RETILE_PLAIN, [L.o]),
+        "gate_up": (O.RETILE_SWIGLU, [L.gate, L.up]),
+        "down": (O.RETILE_PLAIN, [L.down]),
+    }[which]
+    mats = [(lin.packed.reshape(-1).cpu().numpy(), lin.absmax.cpu().numpy(), lin.rows) for lin in lins]
+    np.testing.assert_array_equal(units.cpu().numpy(), O.retile_tiles16(mode, mats, lins[0].k, cfg.head_dim))
+
+
+@pytest.fixture(scope="module")
+def tiny_groups():
+    import torch
+
+    from kudacuda_b200.decode_engine import StaticDecodePlan, random_weights, tiny_config
+    from kudacuda_b200.kudacuda_sidecar import KudaCudaBridge
+
+    cfg = tiny_config(layers=2, vocab=4096)
+    bridge = KudaCudaBridge(device_id=0)
+    weights = random_weights(bridge, cfg, seed=11, device="cuda:0")
+    plan = StaticDecodePlan(bridge, weights, kv_bucket=64, max_tokens=64, device="cuda:0", persistent=True,
+                            persistent_layout="groups")
+    stream = torch.cuda.Stream()
+    plan.capture(stream)
+    yield cfg, bridge, weights, plan, stream
+    bridge.reset_graph()
+    bridge.shutdown()
+
+
+@pytest.mark.parametrize("which", ["qkv", "o", "gate_up", "down"])
+def test_device_retile_matches_oracle(tiny_groups, which):
+    """The K-split group layout (kudacuda_sm100_decode_layers_persistent)."""
+
+    cfg, bridge, w, plan, stream = tiny_groups
     L = w.layers[1]
     idx = {"qkv": 0, "o": 1, "gate_up": 2, "down": 3}[which]
     codes, absm = plan.persistent.tiles[4 + idx]  # layer 1
@@ -180,3 +220,25 @@ def test_persistent_rejects_unsupported_shapes(tiny_persistent):
                                         intermediate=11008, kv_capacity=64)
     assert bridge.retile_groups(O.RETILE_PLAIN, (100, 0, 0)) == -1
     assert bridge.retile_groups(O.RETILE_SWIGLU, (64, 96, 0)) == -1
+
+
+def test_groups_layout_layer_against_oracle(tiny_groups):
+    """The K-split persistent kernel (layout "groups") still computes a layer
+    within the composed-output bound."""
+
+    cfg, bridge, w, plan, stream = tiny_groups
+    plan.reset_cache()
+    plan.set_state(321, 0, stream)
+    plan.replay(stream)
+    stream.synchronize()
+    assert bridge.error_word(clear=True) == 0
+    emb = _b16(w.embedding).reshape(cfg.vocab, cfg.hidden)
+    x = emb[321].copy()
+    cos, sin = _b16(plan.buffers.rope_cos), _b16(plan.buffers.rope_sin)
+    ocfg = dict(hidden=cfg.hidden, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                inter=cfg.intermediate, eps=cfg.eps)
+    for L in w.layers:
+        kc = np.zeros((cfg.kv_heads, plan.kv_bucket, cfg.head_dim), dtype=np.uint16)
+        vc = np.zeros_like(kc)
+        O.layer_step_hf(_layer_np(L), ocfg, x, kc, vc, plan.kv_bucket, 0, cos[0], sin[0])
+    norm_close(O.bf16_to_f32(_b16(plan.buffers.x)), O.bf16_to_f32(x))
