@@ -72,10 +72,16 @@ namespace {
 
 constexpr int kRW = 16;  // warps per CTA
 constexpr int kRT = kRW * 32;
-constexpr int kRMaxSlots = 3;
+#ifndef KC_ROWS_RING_MAX
+#define KC_ROWS_RING_MAX 3
+#endif
+constexpr int kRMaxSlots = KC_ROWS_RING_MAX;
 constexpr int kUnitCodes = 512;
 constexpr int kUnitBytes = 576;
-constexpr int kSlotUnits = 4;
+#ifndef KC_ROWS_SLOT_UNITS
+#define KC_ROWS_SLOT_UNITS 4
+#endif
+constexpr int kSlotUnits = KC_ROWS_SLOT_UNITS;  // units per bulk copy / ring slot
 constexpr int kSlotBytes = kSlotUnits * kUnitBytes;
 constexpr int kRLutBytes = 65536;  // 256 entry rows x 256 B, lane replicas in the first 128 B of a row
 constexpr int kMaxCtaTiles = 16;   // tiles of one op one CTA may own (checked on the host)
@@ -284,8 +290,9 @@ __device__ __noinline__ void rring_drain(uint64_t* bars, int ring_slots, int slo
 // sums of the warp go to part[tile][warp][16]; then the CTA sums the warps in
 // fixed order and hands every (tile, row pair) to `epi` (rows r and r + 8).
 template <int OP, class Epi>
-__device__ void rgemv(const RowArgs& a, const int* rng, const uint8_t* lut, uint8_t* ring, uint64_t* bars, RStream& ps,
-                      RCons& cs, const uint16_t* xs, float* part, Epi epi) {
+__device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t* lut, uint8_t* ring, uint64_t* bars,
+                      RStream& ps, RCons& cs, const uint16_t* xs, float* part, Epi epi) {
+    [[maybe_unused]] constexpr int kSt = 16 + 3 * OP;  // stamps: first slot ready, warp 0 done, all warps done
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int* rr = rng + OP * kRngStride;
     const int t0 = rr[0], ntiles = rr[1] - rr[0];
@@ -307,9 +314,12 @@ __device__ void rgemv(const RowArgs& a, const int* rng, const uint8_t* lut, uint
             }
             __syncwarp();
         }
+        if (u == uw0) KR_STAMP(layer, kSt);
         const uint8_t* st = ring + cs.slot * kSlotBytes;
         const int n = min(kSlotUnits, uw1 - u);
-        for (int k = 0; k < n; ++k) {
+#pragma unroll
+        for (int k = 0; k < kSlotUnits; ++k) {  // unrolled: consecutive units' loads and mma chains overlap
+            if (k >= n) break;
             if (g == 0) {  // only batch column 0 of B matters: lanes 0..3 carry x
                 const uint4* xp = reinterpret_cast<const uint4*>(xs + blk * 64 + 16 * t);
                 x0 = xp[0];
@@ -352,7 +362,9 @@ __device__ void rgemv(const RowArgs& a, const int* rng, const uint8_t* lut, uint
         pp[g] = acc_lo;
         pp[8 + g] = acc_hi;
     }
+    KR_STAMP(layer, kSt + 1);
     __syncthreads();
+    KR_STAMP(layer, kSt + 2);
     for (int idx = tid; idx < ntiles * 8; idx += kRT) {
         const int tl = idx >> 3, r = idx & 7;
         float lo = 0.F, hi = 0.F;
@@ -466,32 +478,55 @@ __device__ __forceinline__ RAttPlan ratt_plan(const RowArgs& a, int kv_len) {
     return p;
 }
 struct RAttSmem {
-    uint16_t* kt;  // [kATile][kKRow]
+    uint16_t* kt;  // [kATile][kKRow]  (a region of its own: the first tile is fetched at layer start)
     uint16_t* vt;  // [kATile][kKRow]
-    uint16_t* qb;  // [8][kKRow]: the group's q rows (bf16), rows >= gq zero
+    uint16_t* qb;  // [8][kKRow]: the group's q rows (bf16), rows >= gq zero   (in the work region)
     float* ss;     // [2][8][kATile]: score halves, then probabilities in [0]; the merge's weights
     float* ml;     // [8][4]: running max, sum, correction
+    float* mb;     // [8][ns * nd <= 160]: the merge's slice of every split's accumulator, [hq][split][dim]
 };
-constexpr int kRAttSmemBytes = 2 * kATile * kKRow * 2 + 8 * kKRow * 2 + 2 * 8 * kATile * 4 + 8 * 4 * 4;
-__device__ __forceinline__ RAttSmem ratt_smem(uint8_t* work) {
+constexpr int kRKvTileBytes = 2 * kATile * kKRow * 2;
+constexpr int kRAttWorkBytes = 8 * kKRow * 2 + 2 * 8 * kATile * 4 + 8 * 4 * 4 + 8 * 160 * 4;
+__device__ __forceinline__ RAttSmem ratt_smem(uint8_t* work, uint8_t* kvt) {
     RAttSmem s;
-    s.kt = reinterpret_cast<uint16_t*>(work);
+    s.kt = reinterpret_cast<uint16_t*>(kvt);
     s.vt = s.kt + kATile * kKRow;
-    s.qb = s.vt + kATile * kKRow;
+    s.qb = reinterpret_cast<uint16_t*>(work);
     s.ss = reinterpret_cast<float*>(s.qb + 8 * kKRow);
     s.ml = s.ss + 2 * 8 * kATile;
+    s.mb = s.ml + 8 * 4;
     return s;
 }
 // Warp 0 (all lanes) issues the bulk copies of K and V rows [t0, t0 + nt) of
 // one KV head into the padded tile rows, completing on `bar`.
-__device__ __forceinline__ void ratt_issue(const uint16_t* kc, const uint16_t* vc, int t0, int nt, const RAttSmem& sm,
-                                           uint64_t* bar) {
-    const int lane = threadIdx.x & 31;
-    if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nt) * 512u);
-    __syncwarp();
-    for (int r = lane; r < nt; r += 32) {
-        bulk_g2s(sm.kt + r * kKRow, kc + static_cast<int64_t>(t0 + r) * 128, 256u, bar);
-        bulk_g2s(sm.vt + r * kKRow, vc + static_cast<int64_t>(t0 + r) * 128, 256u, bar);
+// K and V rows t0 .. t0+nt-1 of one head into the padded tile rows: 16-byte
+// cp.async by every thread of the CTA (thousands of small copies would queue
+// behind the weight rings on the bulk-copy engine).  Row skip (this step's
+// position, still being written by the q/k/v owners) is left out; the caller
+// loads it with plain loads once it is final.  One commit group per call.
+__device__ __forceinline__ void ratt_fetch(const uint16_t* kc, const uint16_t* vc, int t0, int nt, int skip,
+                                           const RAttSmem& sm) {
+    for (int i = threadIdx.x; i < nt * 16; i += kRT) {
+        const int r = i >> 4, c = i & 15;
+        if (t0 + r == skip) continue;
+        const int64_t src = static_cast<int64_t>(t0 + r) * 128 + 8 * c;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sm.kt + r * kKRow + 8 * c)),
+                     "l"(kc + src)
+                     : "memory");
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sm.vt + r * kKRow + 8 * c)),
+                     "l"(vc + src)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// Row pos of the cache (final once the q/k/v owners signalled) into tile row pos - t0, if the tile holds it.
+__device__ __forceinline__ void ratt_pos_row(const uint16_t* kc, const uint16_t* vc, int t0, int nt, int pos,
+                                             const RAttSmem& sm) {
+    if (pos < t0 || pos >= t0 + nt) return;
+    for (int i = threadIdx.x; i < 2 * 16; i += kRT) {
+        const uint16_t* src = (i < 16 ? kc : vc) + static_cast<int64_t>(pos) * 128;
+        uint16_t* dst = (i < 16 ? sm.kt : sm.vt) + (pos - t0) * kKRow;
+        reinterpret_cast<uint4*>(dst)[i & 15] = __ldcg(reinterpret_cast<const uint4*>(src) + (i & 15));
     }
 }
 __device__ __forceinline__ void rldsm_x2_trans(uint32_t& r0, uint32_t& r1, uint32_t addr) {
@@ -503,11 +538,12 @@ __device__ __forceinline__ void rsplit_pair(float p0, float p1, uint32_t& hi, ui
     lo = static_cast<uint32_t>(f32_to_bf16_bits(p0 - h0)) | (static_cast<uint32_t>(f32_to_bf16_bits(p1 - h1)) << 16);
 }
 
-// One split (KV head hk, tokens [tok0, tok1)) of one layer; then the split
-// that arrives last for its KV head (a ticket) merges every split of the head
-// into the attention output, written once for all o_proj owners.
+// One split (KV head hk, tokens [tok0, tok1)) of one layer; then, once every
+// split of the head has published its partial, each split merges its slice of
+// the head dims (all ns splits, all gq query heads) into the attention
+// output, written once for all o_proj owners.
 __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int pos, int kv_len, const RAttPlan& ap,
-                           const RAttSmem& sm, uint64_t* bar, uint32_t& phase, int* flag) {
+                           const RAttSmem& sm) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int gq = a.qh / a.kvh, hd = a.hd;
     const int hk = static_cast<int>(blockIdx.x) / ap.ns, s = static_cast<int>(blockIdx.x) - hk * ap.ns;
@@ -520,12 +556,14 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
         const uint32_t v = row < gq ? __ldcg(reinterpret_cast<const uint32_t*>(a.qg) + ((hk * gq + row) * hd) / 2 + c) : 0u;
         reinterpret_cast<uint32_t*>(sm.qb + row * kKRow)[c] = v;
     }
+    ratt_pos_row(kc, vc, tok0, min(kATile, tok1 - tok0), pos, sm);  // the first tile was fetched at layer start
     if (tid < 8) {
         sm.ml[tid * 4 + 0] = -INFINITY;
         sm.ml[tid * 4 + 1] = 0.F;
         sm.ml[tid * 4 + 2] = 1.F;
     }
     __syncthreads();
+    KR_STAMP(layer, 28);
     uint32_t qa[8][2];
     {
         const uint32_t* qw = reinterpret_cast<const uint32_t*>(sm.qb + g * kKRow);
@@ -539,33 +577,18 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
     const uint32_t vbase = smem_u32(sm.vt) + static_cast<uint32_t>((lane & 15) * kKRow * 2 + 16 * warp);
     for (int t0 = tok0; t0 < tok1; t0 += kATile) {
         const int nt = min(kATile, tok1 - t0);
-        if (t0 != tok0) {  // every thread is done with the previous tile's rows
-            fence_proxy_async_smem();
-            __syncthreads();
-            if (warp == 0) ratt_issue(kc, vc, t0, nt, sm, bar);
+        if (t0 != tok0) {
+            __syncthreads();  // every thread is done with the previous tile's rows
+            ratt_fetch(kc, vc, t0, nt, pos, sm);
+            ratt_pos_row(kc, vc, t0, nt, pos, sm);
         }
-        if (!mbar_wait_bounded(bar, phase)) {
-            if (tid == 0) {
-                atomicExch(a.misc, 1u);
-                atomicOr(a.err, 16);
-            }
-            for (int retry = 0; retry < 8 && !mbar_wait_bounded(bar, phase); ++retry) {
-            }
-        }
-        phase ^= 1u;
         const int n16 = (nt + 15) & ~15;
-        if (pos >= t0 && pos < t0 + nt) {  // this step's row, written by the k/v owners after the copy may have run
-            for (int i = tid; i < hd / 8; i += kRT) {
-                reinterpret_cast<uint4*>(sm.kt + (pos - t0) * kKRow)[i] =
-                    __ldcg(reinterpret_cast<const uint4*>(kc + static_cast<int64_t>(pos) * hd) + i);
-                reinterpret_cast<uint4*>(sm.vt + (pos - t0) * kKRow)[i] =
-                    __ldcg(reinterpret_cast<const uint4*>(vc + static_cast<int64_t>(pos) * hd) + i);
-            }
-        }
         // V rows nt .. n16-1 take part in the last P.V k-step with P = 0: make them finite
         for (int i = tid; i < (n16 - nt) * (hd / 2); i += kRT)
             reinterpret_cast<uint32_t*>(sm.vt + (nt + i / (hd / 2)) * kKRow)[i % (hd / 2)] = 0u;
+        asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's copies of the tile
         __syncthreads();
+        if (t0 == tok0) KR_STAMP(layer, 29);
         if (warp < (n16 >> 3) * 2) {  // scores: unit (n-tile of 8 tokens, dim half) per warp
             const int ntl = warp >> 1, hf = warp & 1;
             float c0[4] = {0.F, 0.F, 0.F, 0.F}, c1[4] = {0.F, 0.F, 0.F, 0.F};
@@ -655,19 +678,24 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
         mine[tid * rec + 0] = sm.ml[tid * 4 + 0];
         mine[tid * rec + 1] = sm.ml[tid * 4 + 1];
     }
-    // ---- the last split of this KV head to arrive merges all of them
+    // ---- every split of the head out -> each split merges dims [d0, d1) of the gq heads
     unsigned* ctr = a.counters + layer * kRStride;
-    __syncthreads();
-    if (tid == 0) {
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
-        const unsigned old = atomicAdd(ctr + kCTicket + hk, 1u);
-        const int last = old + 1u == static_cast<unsigned>(ap.ns);
-        if (last) asm volatile("fence.acq_rel.gpu;" ::: "memory");
-        *flag = last;
-    }
-    __syncthreads();
-    if (!*flag) return;
+    rsignal(ctr + kCTicket + hk);
+    KR_STAMP(layer, 30);
+    if (ap.ns > 1) rwait(a, ctr + kCTicket + hk, static_cast<unsigned>(ap.ns));
+    KR_STAMP(layer, 31);
+    // the slice's accumulators (gq x ns x nd <= 8 x 160 floats, at most three per
+    // thread) go out together with the split maxima and sums: one round trip
     float* wn = sm.ss;  // [gq][kAMaxSplits] normalised split weights
+    const int d0 = s * hd / ap.ns, nd = (s + 1) * hd / ap.ns - d0, per = ap.ns * nd;
+    float accv[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const int v = tid + k * kRT, hq = v / per, rem = v - hq * per, sp = rem / nd;
+        accv[k] = hq < gq ? __ldcg(a.apart + ((static_cast<size_t>(hk) * kAMaxSplits + sp) * gq + hq) * rec + 4 + d0 +
+                                   (rem - sp * nd))
+                          : 0.F;
+    }
     if (warp < gq) {
         const float* p = a.apart + ((static_cast<size_t>(hk) * kAMaxSplits + lane) * gq + warp) * rec;
         const bool live = lane < ap.ns;
@@ -678,28 +706,23 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
         const float den = warp_sum(e * l);
         wn[warp * kAMaxSplits + lane] = den > 0.F ? e / den : 0.F;
     }
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+        if (tid + k * kRT < gq * per) sm.mb[tid + k * kRT] = accv[k];
     __syncthreads();
     uint16_t* tap = rtap(a, layer);
     const int att_off = tap != nullptr ? rtaps(a.hidden, a.qh, a.kvh, hd, a.inter).att : 0;
     bool overflow = false;
-    for (int idx = tid; idx < gq * hd / 2; idx += kRT) {  // two dims per thread
-        const int hq = idx / (hd / 2), d = 2 * (idx - hq * (hd / 2));
-        const float* base = a.apart + (static_cast<size_t>(hk) * kAMaxSplits * gq + hq) * rec + 4 + d;
-        float acc0 = 0.F, acc1 = 0.F;
-        for (int sp = 0; sp < ap.ns; ++sp) {
-            const float w = wn[hq * kAMaxSplits + sp];
-            const float2 v = __ldcg(reinterpret_cast<const float2*>(base + static_cast<size_t>(sp) * gq * rec));
-            acc0 = fmaf(w, v.x, acc0);
-            acc1 = fmaf(w, v.y, acc1);
-        }
-        const uint16_t b0 = f32_to_bf16_bits(acc0), b1 = f32_to_bf16_bits(acc1);
-        const int o = (hk * gq + hq) * hd + d;
-        reinterpret_cast<uint32_t*>(a.attg)[o / 2] = static_cast<uint32_t>(b0) | (static_cast<uint32_t>(b1) << 16);
-        overflow |= !(fabsf(bf16_bits_to_f32(b0)) <= 65504.F) || !(fabsf(bf16_bits_to_f32(b1)) <= 65504.F);
-        if (tap != nullptr) {
-            tap[att_off + o] = b0;
-            tap[att_off + o + 1] = b1;
-        }
+    for (int idx = tid; idx < gq * nd; idx += kRT) {
+        const int hq = idx / nd, dd = idx - hq * nd;
+        const float* mrow = sm.mb + hq * per + dd;
+        float acc = 0.F;
+        for (int sp = 0; sp < ap.ns; ++sp) acc = fmaf(wn[hq * kAMaxSplits + sp], mrow[sp * nd], acc);
+        const uint16_t b = f32_to_bf16_bits(acc);
+        const int o = (hk * gq + hq) * hd + d0 + dd;
+        a.attg[o] = b;
+        overflow |= !(fabsf(bf16_bits_to_f32(b)) <= 65504.F);
+        if (tap != nullptr) tap[att_off + o] = b;
     }
     if (overflow) atomicOr(a.err, 1);
     rsignal(ctr + kCAtt);
@@ -709,10 +732,8 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
 __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
     extern __shared__ __align__(128) uint8_t dsm[];
     __shared__ __align__(8) uint64_t bars_all[kRW * kRMaxSlots];
-    __shared__ __align__(8) uint64_t att_bar;
     __shared__ float red[kRW];
     __shared__ int rng[4 * kRngStride];
-    __shared__ int flag;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     uint8_t* lut = dsm;
@@ -720,7 +741,8 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
     uint8_t* work = rings + kRW * a.ring_slots * kSlotBytes;
     uint16_t* xs = reinterpret_cast<uint16_t*>(work);
     float* part = reinterpret_cast<float*>(work + a.xs_bytes);
-    uint16_t* xres = reinterpret_cast<uint16_t*>(work + a.work_bytes);
+    uint8_t* kvt = work + a.work_bytes;  // attention K/V tile rows
+    uint16_t* xres = reinterpret_cast<uint16_t*>(kvt + kRKvTileBytes);
     uint16_t* bias_s = xres + ((a.hidden + 63) & ~63);
     float* rope_s = reinterpret_cast<float*>(bias_s + ((a.bias_rows + 63) & ~63));
     uint8_t* ring = rings + warp * a.ring_slots * kSlotBytes;
@@ -737,7 +759,6 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
     ps.done = a.nlayers < 1;
     if (lane == 0) {
         for (int s = 0; s < a.ring_slots; ++s) mbar_init(&bars[s], 1);
-        if (warp == 0) mbar_init(&att_bar, 1);
         fence_mbar_init();
         for (int s = 0; s < a.ring_slots; ++s) rstream_issue(a, rng, ps, warp, ring, bars, s);
     }
@@ -765,7 +786,6 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
     __syncthreads();
     const RAttPlan ap = ratt_plan(a, kv_len);
     const bool att_cta = static_cast<int>(blockIdx.x) < a.kvh * ap.ns;
-    uint32_t att_phase = 0;
     const bool own_o = rng[kOO * kRngStride + 1] > rng[kOO * kRngStride];
     const bool own_dn = rng[kODn * kRngStride + 1] > rng[kODn * kRngStride];
     const bool own_qkv = rng[kOQkv * kRngStride + 1] > rng[kOQkv * kRngStride];
@@ -784,6 +804,15 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
         uint16_t* tap = rtap(a, l);
         const bool tap0 = tap != nullptr && blockIdx.x == 0;
         KR_STAMP(l, 0);
+        const RAttSmem att_sm = ratt_smem(work, kvt);
+        if (att_cta) {  // this layer's first K/V tile: rows before pos are final (row pos is reloaded after q)
+            const int hk = static_cast<int>(blockIdx.x) / ap.ns, sp = static_cast<int>(blockIdx.x) - hk * ap.ns;
+            const int tok0 = sp * ap.ts;
+            const uint16_t* kc = reinterpret_cast<const uint16_t*>(L[kTKCache]) + static_cast<int64_t>(hk) * a.cap * hd;
+            const uint16_t* vc = reinterpret_cast<const uint16_t*>(L[kTVCache]) + static_cast<int64_t>(hk) * a.cap * hd;
+            __syncthreads();  // the previous layer's reads of the tile rows are done
+            ratt_fetch(kc, vc, tok0, min(kATile, kv_len - tok0), pos_c, att_sm);
+        }
         // ---- x ready -> RMSNorm -> q/k/v owners (bias, RoPE, k/v into the cache row)
         rnorm_prefetch(a, reinterpret_cast<const uint16_t*>(L[kTInNorm]), wv);
         if (a.bias_rows > 0) {
@@ -806,7 +835,7 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             uint16_t* vcl = reinterpret_cast<uint16_t*>(L[kTVCache]);
             const int qt = a.qh * hd / 16, kt = a.kvh * hd / 16, per = hd / 16;
             const bool bias = a.bias_rows > 0;
-            rgemv<kOQkv>(a, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
+            rgemv<kOQkv>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
                 if (T < qt + kt) {  // q or k: RoPE pair (i, i + half)
                     const bool isq = T < qt;
                     const int u = isq ? T : T - qt, head = u / per, i = 8 * (u - head * per) + r;
@@ -850,27 +879,19 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
         KR_STAMP(l, 3);
         // ---- attention splits, merged once per KV head
         if (att_cta) {
-            const RAttSmem sm = ratt_smem(work);
-            const int hk = static_cast<int>(blockIdx.x) / ap.ns, sp = static_cast<int>(blockIdx.x) - hk * ap.ns;
-            const int tok0 = sp * ap.ts;
-            const uint16_t* kc = reinterpret_cast<const uint16_t*>(L[kTKCache]) + static_cast<int64_t>(hk) * a.cap * hd;
-            const uint16_t* vc = reinterpret_cast<const uint16_t*>(L[kTVCache]) + static_cast<int64_t>(hk) * a.cap * hd;
-            fence_proxy_async_smem();  // the tile rows' earlier generic accesses (xs, partials) before the copies
-            __syncthreads();
-            if (warp == 0) ratt_issue(kc, vc, tok0, min(kATile, kv_len - tok0), sm, &att_bar);
             rwait(a, ctr + kCQkv, static_cast<unsigned>(a.ctas[kOQkv]));
             KR_STAMP(l, 4);
-            rattention(a, l, L, pos_c, kv_len, ap, sm, &att_bar, att_phase, &flag);
+            rattention(a, l, L, pos_c, kv_len, ap, att_sm);
             KR_STAMP(l, 5);
         }
         // ---- o_proj owners: x1 = x + o_proj(attention)
         rnorm_prefetch(a, reinterpret_cast<const uint16_t*>(L[kTPostNorm]), wv);
         if (own_o) {
-            rwait(a, ctr + kCAtt, static_cast<unsigned>(a.kvh));
+            rwait(a, ctr + kCAtt, static_cast<unsigned>(a.kvh * ap.ns));
             KR_STAMP(l, 6);
             rstage_f16(a, xs, a.attg, a.qh * hd);
             KR_STAMP(l, 7);
-            rgemv<kOO>(a, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
+            rgemv<kOO>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
 #pragma unroll
                 for (int k = 0; k < 2; ++k) {
                     const int row = 16 * T + r + 8 * k;
@@ -892,7 +913,7 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
         KR_STAMP(l, 10);
         {
             bool overflow = false;
-            rgemv<kOGu>(a, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
+            rgemv<kOGu>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
                 const int j = 8 * T + r;
                 const float gv = round_bf16(ylo), uv = round_bf16(yhi);
                 const float act = round_bf16(gv / (1.0F + expf(-gv)));
@@ -911,7 +932,7 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             KR_STAMP(l, 12);
             rstage_f16(a, xs, a.hg, a.inter);
             KR_STAMP(l, 13);
-            rgemv<kODn>(a, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
+            rgemv<kODn>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
 #pragma unroll
                 for (int k = 0; k < 2; ++k) {
                     const int row = 16 * T + r + 8 * k;
@@ -1017,9 +1038,9 @@ RowGeom row_geom(const PersistDims& d, int sms) {
     kmax = kmax > d.q_heads * d.head_dim ? kmax : d.q_heads * d.head_dim;
     g.xs_bytes = (kmax * 2 + 127) & ~127;
     const int work = g.xs_bytes + kMaxCtaTiles * kRW * 16 * 4;
-    g.work_bytes = ((work > kRAttSmemBytes ? work : kRAttSmemBytes) + 127) & ~127;
+    g.work_bytes = ((work > kRAttWorkBytes ? work : kRAttWorkBytes) + 127) & ~127;
     g.bias_rows = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
-    const int tail = ((d.hidden + 63) & ~63) * 2 + ((g.bias_rows + 63) & ~63) * 2 + d.head_dim * 4;
+    const int tail = kRKvTileBytes + ((d.hidden + 63) & ~63) * 2 + ((g.bias_rows + 63) & ~63) * 2 + d.head_dim * 4;
     const int limit = 232448 - kRStaticSmemBudget;
     g.ring_slots = kRMaxSlots;
     while (g.ring_slots > 1 && kRLutBytes + kRW * g.ring_slots * kSlotBytes + g.work_bytes + tail > limit) --g.ring_slots;
