@@ -301,10 +301,17 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
     for (int i = tid; i < kMaxCtaTiles * kRW * 16; i += kRT) part[i] = 0.F;
     __syncthreads();
     const uint32_t lane4 = static_cast<uint32_t>(lane) << 2;
+#ifdef KC_PERSIST_STAMPS
+    long long wcyc = 0;
+    const long long tloop = clock64();
+#endif
     int tile = uw0 / nbpt, blk = uw0 - (uw0 / nbpt) * nbpt;
     float acc_lo = 0.F, acc_hi = 0.F;
     uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0;
     for (int u = uw0; u < uw1;) {
+#ifdef KC_PERSIST_STAMPS
+        const long long tw0 = clock64();
+#endif
         if (!cs.failed && !mbar_wait_bounded(&bars[cs.slot], cs.parity)) {
             cs.failed = true;
             if (lane == 0) {
@@ -314,6 +321,9 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
             }
             __syncwarp();
         }
+#ifdef KC_PERSIST_STAMPS
+        wcyc += clock64() - tw0;
+#endif
         if (u == uw0) KR_STAMP(layer, kSt);
         const uint8_t* st = ring + cs.slot * kSlotBytes;
         const int n = min(kSlotUnits, uw1 - u);
@@ -363,6 +373,12 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
         pp[8 + g] = acc_hi;
     }
     KR_STAMP(layer, kSt + 1);
+#ifdef KC_PERSIST_STAMPS
+    if (layer == KC_STAMP_LAYER && lane == 0) {  // ring-wait and loop cycles of every warp
+        g_rows_stamps[(256 + blockIdx.x) * 64 + OP * 16 + warp] = static_cast<unsigned long long>(wcyc);
+        g_rows_stamps[(512 + blockIdx.x) * 64 + OP * 16 + warp] = static_cast<unsigned long long>(clock64() - tloop);
+    }
+#endif
     __syncthreads();
     KR_STAMP(layer, kSt + 2);
     for (int idx = tid; idx < ntiles * 8; idx += kRT) {
@@ -805,14 +821,6 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
         const bool tap0 = tap != nullptr && blockIdx.x == 0;
         KR_STAMP(l, 0);
         const RAttSmem att_sm = ratt_smem(work, kvt);
-        if (att_cta) {  // this layer's first K/V tile: rows before pos are final (row pos is reloaded after q)
-            const int hk = static_cast<int>(blockIdx.x) / ap.ns, sp = static_cast<int>(blockIdx.x) - hk * ap.ns;
-            const int tok0 = sp * ap.ts;
-            const uint16_t* kc = reinterpret_cast<const uint16_t*>(L[kTKCache]) + static_cast<int64_t>(hk) * a.cap * hd;
-            const uint16_t* vc = reinterpret_cast<const uint16_t*>(L[kTVCache]) + static_cast<int64_t>(hk) * a.cap * hd;
-            __syncthreads();  // the previous layer's reads of the tile rows are done
-            ratt_fetch(kc, vc, tok0, min(kATile, kv_len - tok0), pos_c, att_sm);
-        }
         // ---- x ready -> RMSNorm -> q/k/v owners (bias, RoPE, k/v into the cache row)
         rnorm_prefetch(a, reinterpret_cast<const uint16_t*>(L[kTInNorm]), wv);
         if (a.bias_rows > 0) {
@@ -826,8 +834,16 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
         }
         if (l > 0) rwait(a, a.counters + (l - 1) * kRStride + kCDn, static_cast<unsigned>(a.ctas[kODn]));
         rload_bf16(xres, a.x, a.hidden);
-        __syncthreads();
+        __syncthreads();  // (also: every thread is past the previous layer's reads of the K/V tile rows)
         KR_STAMP(l, 1);
+        if (att_cta) {  // this layer's first K/V tile, after x (whose loads would queue behind these copies):
+                        // rows before pos are final (row pos is loaded with q)
+            const int hk = static_cast<int>(blockIdx.x) / ap.ns, sp = static_cast<int>(blockIdx.x) - hk * ap.ns;
+            const int tok0 = sp * ap.ts;
+            const uint16_t* kc = reinterpret_cast<const uint16_t*>(L[kTKCache]) + static_cast<int64_t>(hk) * a.cap * hd;
+            const uint16_t* vc = reinterpret_cast<const uint16_t*>(L[kTVCache]) + static_cast<int64_t>(hk) * a.cap * hd;
+            ratt_fetch(kc, vc, tok0, min(kATile, kv_len - tok0), pos_c, att_sm);
+        }
         rstage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn : nullptr);
         KR_STAMP(l, 2);
         {
