@@ -94,6 +94,11 @@ constexpr int kRngStride = kRW + 3;  // per op: t0, t1, warp unit bounds 0..16
 
 enum RowOp { kOQkv = 0, kOO = 1, kOGu = 2, kODn = 3 };
 enum RowCtr { kCQkv = 0, kCAtt = 1, kCO = 2, kCGu = 3, kCDn = 4, kCTicket = 5 };
+// hops between ops, the low 3 bits of a tag (7: never written, the test hook's unreachable tag)
+enum RowHop { kHX = 0, kHQ = 1, kHK = 2, kHV = 3, kHAtt = 4, kHX1 = 5, kHH = 6 };
+__host__ __device__ constexpr int hop_counter(int hop) {  // the op counter a hop replaces (stall_counter hook)
+    return hop == kHX ? kCDn : hop <= kHV ? kCQkv : hop == kHAtt ? kCAtt : hop == kHX1 ? kCO : kCGu;
+}
 enum RowSlot { kTUnits0 = 0, kTInNorm = 4, kTPostNorm, kTQBias, kTKBias, kTVBias, kTKCache, kTVCache, kTSlots = 16 };
 
 struct RowArgs {
@@ -105,11 +110,19 @@ struct RowArgs {
     const uint16_t* rope_cos;
     const uint16_t* rope_sin;
     unsigned* counters;  // [nlayers * kRStride]
-    unsigned* misc;      // [0] abort flag, [1] final ticket
-    uint16_t* qg;        // bf16 [qh * hd]: this layer's q after bias and RoPE
-    uint16_t* attg;      // bf16 [qh * hd]: attention output
-    uint16_t* x1g;       // bf16 [hidden]: x + o_proj
-    uint16_t* hg;        // bf16 [inter]: SwiGLU output
+    unsigned* misc;      // [0] abort flag, [1] final ticket, [2] launch count (the tags' epoch)
+    // Tagged words carry one op's output to the next: two 16-bit values
+    // (element 2 i in the low half) and, in the high 32 bits, the tag of the
+    // (launch, layer, hop) that wrote them.  A consumer polls the words it
+    // needs until each carries the tag it expects, so the producer publishes
+    // with plain relaxed 8-byte stores: no fence, no counter, one round trip.
+    uint64_t* qw;   // [qh * hd / 2] q after bias and RoPE (bf16)
+    uint64_t* kw;   // [kvh * hd / 2] this step's k row (bf16; also written to the cache)
+    uint64_t* vw;   // [kvh * hd / 2] this step's v row (bf16; also written to the cache)
+    uint64_t* aw;   // [qh * hd / 2] attention output (f16 of the bf16 value)
+    uint64_t* x1w;  // [hidden / 2] x + o_proj (bf16)
+    uint64_t* hw;   // [inter / 2] SwiGLU output (f16 of the bf16 value)
+    uint64_t* xw;   // [hidden / 2] x2, the next layer's input (bf16)
     float* apart;        // [kvh][kAMaxSplits][gq][hd + 4] attention partials
     int* err;
     int ring_slots;
@@ -217,6 +230,58 @@ __device__ __forceinline__ void rsignal(unsigned* ctr) {
     __syncthreads();
     if (threadIdx.x == 0)
         asm volatile("fence.acq_rel.gpu;\n\tred.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+}
+// Tagged words (RowArgs): aligned 8-byte strong accesses are single-copy
+// atomic, so a word read with the expected tag carries that write's payload.
+__device__ __forceinline__ void st_tagged(uint64_t* p, uint32_t tag, uint32_t payload) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"((static_cast<uint64_t>(tag) << 32) | payload)
+                 : "memory");
+}
+__device__ __forceinline__ uint64_t ld_tagged(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p));
+    return v;
+}
+// Every thread polls words i = tid + k * kRT (k < KMAX, i < n) at src(i)
+// until each carries tag(i), hands each payload to sink(i, payload), then the
+// CTA synchronises.  All of a thread's outstanding words are read in one
+// round; a poll that runs out raises the abort flag and error bit 4, as rwait.
+template <int KMAX, class Src, class Tag, class Sink>
+__device__ void rpoll(const RowArgs& a, int n, Src src, Tag tag, Sink sink) {
+    const int tid = threadIdx.x;
+    uint32_t pending = 0u;
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k)
+        if (tid + k * kRT < n) pending |= 1u << k;
+    uint32_t rounds = 0;
+    while (pending != 0u) {
+        uint64_t v[KMAX];
+#pragma unroll
+        for (int k = 0; k < KMAX; ++k) v[k] = (pending >> k & 1u) != 0u ? ld_tagged(src(tid + k * kRT)) : 0ull;
+#pragma unroll
+        for (int k = 0; k < KMAX; ++k) {
+            const int i = tid + k * kRT;
+            if ((pending >> k & 1u) != 0u && static_cast<uint32_t>(v[k] >> 32) == tag(i)) {
+                sink(i, static_cast<uint32_t>(v[k]));
+                pending &= ~(1u << k);
+            }
+        }
+        if (pending != 0u && (++rounds & 31u) == 0u) {
+            if (ld_relaxed_r(a.misc) != 0u) break;
+            if (rounds > a.spin_limit) {
+                atomicExch(a.misc, 1u);
+                atomicOr(a.err, 16);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+}
+// Pairs of consecutive rows r, r + 1 sit in lanes r, r + 1 of an 8-lane group
+// of the GEMV epilogue (`lanes`: the warp's lanes in that epilogue call): the
+// even lane gets its partner's 16-bit value in the high half.
+__device__ __forceinline__ uint32_t pair_up(uint32_t v, unsigned lanes) {
+    return v | (__shfl_down_sync(lanes, v, 1, 8) << 16);
 }
 
 // ------------------------------------------------------------------ ownership
@@ -383,14 +448,17 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
     KR_STAMP(layer, kSt + 2);
     for (int idx = tid; idx < ntiles * 8; idx += kRT) {
         const int tl = idx >> 3, r = idx & 7;
+        const int left = ntiles * 8 - (idx - lane);  // this warp's lanes in the call: whole 8-lane groups
+        const unsigned lanes = left >= 32 ? 0xffffffffu : (1u << left) - 1u;
         float lo = 0.F, hi = 0.F;
 #pragma unroll 4
         for (int w = 0; w < kRW; ++w) {
             lo += part[(tl * kRW + w) * 16 + r];
             hi += part[(tl * kRW + w) * 16 + 8 + r];
         }
-        epi(t0 + tl, r, lo, hi);
+        epi(t0 + tl, r, lo, hi, lanes);
     }
+    __syncthreads();  // the epilogues' reads of shared memory (xres, part) before its next writers
 }
 
 // ------------------------------------------------------------------ staging
@@ -454,24 +522,6 @@ __device__ __forceinline__ void rload_bf16(uint16_t* dst, const uint16_t* src, i
     for (int i = threadIdx.x; i < n / 8; i += kRT)
         reinterpret_cast<uint4*>(dst)[i] = __ldcg(reinterpret_cast<const uint4*>(src) + i);
 }
-// xs (shared, n f16) = f16(src (global bf16)); values beyond f16 range flag bit 1
-__device__ void rstage_f16(const RowArgs& a, uint16_t* xs, const uint16_t* src, int n) {
-    bool overflow = false;
-    for (int i = threadIdx.x; i < n / 8; i += kRT) {
-        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src) + i);
-        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-        uint32_t out[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float f0 = __uint_as_float(vv[j] << 16), f1 = __uint_as_float(vv[j] & 0xffff0000u);
-            overflow |= !(fabsf(f0) <= 65504.F) || !(fabsf(f1) <= 65504.F);
-            out[j] = static_cast<uint32_t>(f32_to_f16_bits(f0)) | (static_cast<uint32_t>(f32_to_f16_bits(f1)) << 16);
-        }
-        reinterpret_cast<uint4*>(xs)[i] = make_uint4(out[0], out[1], out[2], out[3]);
-    }
-    if (overflow) atomicOr(a.err, 1);
-    __syncthreads();
-}
 
 // ------------------------------------------------------------------ attention
 // A split of one KV head covers ts tokens (a multiple of kATile) in tiles of
@@ -500,9 +550,10 @@ struct RAttSmem {
     float* ss;     // [2][8][kATile]: score halves, then probabilities in [0]; the merge's weights
     float* ml;     // [8][4]: running max, sum, correction
     float* mb;     // [8][ns * nd <= 160]: the merge's slice of every split's accumulator, [hq][split][dim]
+    uint16_t* kvpos;  // [2][128]: this step's k and v rows (bf16), from the q/k/v owners' tagged words
 };
 constexpr int kRKvTileBytes = 2 * kATile * kKRow * 2;
-constexpr int kRAttWorkBytes = 8 * kKRow * 2 + 2 * 8 * kATile * 4 + 8 * 4 * 4 + 8 * 160 * 4;
+constexpr int kRAttWorkBytes = 8 * kKRow * 2 + 2 * 8 * kATile * 4 + 8 * 4 * 4 + 8 * 160 * 4 + 2 * 128 * 2;
 __device__ __forceinline__ RAttSmem ratt_smem(uint8_t* work, uint8_t* kvt) {
     RAttSmem s;
     s.kt = reinterpret_cast<uint16_t*>(kvt);
@@ -511,6 +562,7 @@ __device__ __forceinline__ RAttSmem ratt_smem(uint8_t* work, uint8_t* kvt) {
     s.ss = reinterpret_cast<float*>(s.qb + 8 * kKRow);
     s.ml = s.ss + 2 * 8 * kATile;
     s.mb = s.ml + 8 * 4;
+    s.kvpos = reinterpret_cast<uint16_t*>(s.mb + 8 * 160);
     return s;
 }
 // Warp 0 (all lanes) issues the bulk copies of K and V rows [t0, t0 + nt) of
@@ -535,14 +587,12 @@ __device__ __forceinline__ void ratt_fetch(const uint16_t* kc, const uint16_t* v
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
-// Row pos of the cache (final once the q/k/v owners signalled) into tile row pos - t0, if the tile holds it.
-__device__ __forceinline__ void ratt_pos_row(const uint16_t* kc, const uint16_t* vc, int t0, int nt, int pos,
-                                             const RAttSmem& sm) {
+// This step's k and v rows (staged from the tagged words) into tile row pos - t0, if the tile holds it.
+__device__ __forceinline__ void ratt_pos_row(int t0, int nt, int pos, const RAttSmem& sm) {
     if (pos < t0 || pos >= t0 + nt) return;
     for (int i = threadIdx.x; i < 2 * 16; i += kRT) {
-        const uint16_t* src = (i < 16 ? kc : vc) + static_cast<int64_t>(pos) * 128;
         uint16_t* dst = (i < 16 ? sm.kt : sm.vt) + (pos - t0) * kKRow;
-        reinterpret_cast<uint4*>(dst)[i & 15] = __ldcg(reinterpret_cast<const uint4*>(src) + (i & 15));
+        reinterpret_cast<uint4*>(dst)[i & 15] = reinterpret_cast<const uint4*>(sm.kvpos + (i < 16 ? 0 : 128))[i & 15];
     }
 }
 __device__ __forceinline__ void rldsm_x2_trans(uint32_t& r0, uint32_t& r1, uint32_t addr) {
@@ -559,20 +609,29 @@ __device__ __forceinline__ void rsplit_pair(float p0, float p1, uint32_t& hi, ui
 // the head dims (all ns splits, all gq query heads) into the attention
 // output, written once for all o_proj owners.
 __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int pos, int kv_len, const RAttPlan& ap,
-                           const RAttSmem& sm) {
+                           const RAttSmem& sm, uint32_t tq, uint32_t tk, uint32_t tv, uint32_t tatt) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int gq = a.qh / a.kvh, hd = a.hd;
     const int hk = static_cast<int>(blockIdx.x) / ap.ns, s = static_cast<int>(blockIdx.x) - hk * ap.ns;
     const int tok0 = s * ap.ts, tok1 = min(kv_len, tok0 + ap.ts);
     const uint16_t* kc = reinterpret_cast<const uint16_t*>(L[kTKCache]) + static_cast<int64_t>(hk) * a.cap * hd;
     const uint16_t* vc = reinterpret_cast<const uint16_t*>(L[kTVCache]) + static_cast<int64_t>(hk) * a.cap * hd;
-    // the group's q rows (bf16 pairs) from the QKV owners; rows >= gq zero
-    for (int i = tid; i < 8 * hd / 2; i += kRT) {
-        const int row = i / (hd / 2), c = i - row * (hd / 2);
-        const uint32_t v = row < gq ? __ldcg(reinterpret_cast<const uint32_t*>(a.qg) + ((hk * gq + row) * hd) / 2 + c) : 0u;
-        reinterpret_cast<uint32_t*>(sm.qb + row * kKRow)[c] = v;
-    }
-    ratt_pos_row(kc, vc, tok0, min(kATile, tok1 - tok0), pos, sm);  // the first tile was fetched at layer start
+    // the group's q rows (bf16 pairs, rows >= gq zero) and, for the split that
+    // holds pos, this step's k and v rows: the q/k/v owners' tagged words
+    const int hp = hd / 2, nq = gq * hp;
+    const bool has_pos = pos >= tok0 && pos < tok1;
+    for (int i = nq + tid; i < 8 * hp; i += kRT) reinterpret_cast<uint32_t*>(sm.qb + (i / hp) * kKRow)[i % hp] = 0u;
+    rpoll<2>(
+        a, nq + (has_pos ? 2 * hp : 0),
+        [&](int i) -> const uint64_t* {
+            return i < nq ? a.qw + hk * nq + i : i < nq + hp ? a.kw + hk * hp + (i - nq) : a.vw + hk * hp + (i - nq - hp);
+        },
+        [&](int i) { return i < nq ? tq : i < nq + hp ? tk : tv; },
+        [&](int i, uint32_t p) {
+            if (i < nq) reinterpret_cast<uint32_t*>(sm.qb + (i / hp) * kKRow)[i % hp] = p;
+            else reinterpret_cast<uint32_t*>(sm.kvpos)[i - nq] = p;
+        });
+    ratt_pos_row(tok0, min(kATile, tok1 - tok0), pos, sm);  // the rest of the first tile was fetched at layer start
     if (tid < 8) {
         sm.ml[tid * 4 + 0] = -INFINITY;
         sm.ml[tid * 4 + 1] = 0.F;
@@ -596,7 +655,7 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
         if (t0 != tok0) {
             __syncthreads();  // every thread is done with the previous tile's rows
             ratt_fetch(kc, vc, t0, nt, pos, sm);
-            ratt_pos_row(kc, vc, t0, nt, pos, sm);
+            ratt_pos_row(t0, nt, pos, sm);
         }
         const int n16 = (nt + 15) & ~15;
         // V rows nt .. n16-1 take part in the last P.V k-step with P = 0: make them finite
@@ -700,10 +759,10 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
     KR_STAMP(layer, 30);
     if (ap.ns > 1) rwait(a, ctr + kCTicket + hk, static_cast<unsigned>(ap.ns));
     KR_STAMP(layer, 31);
-    // the slice's accumulators (gq x ns x nd <= 8 x 160 floats, at most three per
+    // the slice's accumulators (gq x ns x nd <= 8 x 132 floats, at most three per
     // thread) go out together with the split maxima and sums: one round trip
     float* wn = sm.ss;  // [gq][kAMaxSplits] normalised split weights
-    const int d0 = s * hd / ap.ns, nd = (s + 1) * hd / ap.ns - d0, per = ap.ns * nd;
+    const int d0 = 2 * (s * hp / ap.ns), nd = 2 * ((s + 1) * hp / ap.ns) - d0, per = ap.ns * nd;  // even slices
     float accv[3];
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
@@ -729,19 +788,28 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
     uint16_t* tap = rtap(a, layer);
     const int att_off = tap != nullptr ? rtaps(a.hidden, a.qh, a.kvh, hd, a.inter).att : 0;
     bool overflow = false;
-    for (int idx = tid; idx < gq * nd; idx += kRT) {
-        const int hq = idx / nd, dd = idx - hq * nd;
+    const int np = nd / 2;
+    for (int idx = tid; idx < gq * np; idx += kRT) {  // dims d, d + 1 of head hq: one tagged word
+        const int hq = idx / np, dd = 2 * (idx - hq * np);
         const float* mrow = sm.mb + hq * per + dd;
-        float acc = 0.F;
-        for (int sp = 0; sp < ap.ns; ++sp) acc = fmaf(wn[hq * kAMaxSplits + sp], mrow[sp * nd], acc);
-        const uint16_t b = f32_to_bf16_bits(acc);
+        float acc0 = 0.F, acc1 = 0.F;
+        for (int sp = 0; sp < ap.ns; ++sp) {
+            const float w = wn[hq * kAMaxSplits + sp];
+            acc0 = fmaf(w, mrow[sp * nd], acc0);
+            acc1 = fmaf(w, mrow[sp * nd + 1], acc1);
+        }
+        const uint16_t b0 = f32_to_bf16_bits(acc0), b1 = f32_to_bf16_bits(acc1);
+        const float f0 = bf16_bits_to_f32(b0), f1 = bf16_bits_to_f32(b1);
+        overflow |= !(fabsf(f0) <= 65504.F) || !(fabsf(f1) <= 65504.F);
         const int o = (hk * gq + hq) * hd + d0 + dd;
-        a.attg[o] = b;
-        overflow |= !(fabsf(bf16_bits_to_f32(b)) <= 65504.F);
-        if (tap != nullptr) tap[att_off + o] = b;
+        st_tagged(a.aw + o / 2, tatt,
+                  static_cast<uint32_t>(f32_to_f16_bits(f0)) | (static_cast<uint32_t>(f32_to_f16_bits(f1)) << 16));
+        if (tap != nullptr) {
+            tap[att_off + o] = b0;
+            tap[att_off + o + 1] = b1;
+        }
     }
     if (overflow) atomicOr(a.err, 1);
-    rsignal(ctr + kCAtt);
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -804,8 +872,6 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
     const bool att_cta = static_cast<int>(blockIdx.x) < a.kvh * ap.ns;
     const bool own_o = rng[kOO * kRngStride + 1] > rng[kOO * kRngStride];
     const bool own_dn = rng[kODn * kRngStride + 1] > rng[kODn * kRngStride];
-    const bool own_qkv = rng[kOQkv * kRngStride + 1] > rng[kOQkv * kRngStride];
-    const bool own_gu = rng[kOGu * kRngStride + 1] > rng[kOGu * kRngStride];
     const RTaps to = rtaps(a.hidden, a.qh, a.kvh, a.hd, a.inter);
     const int hd = a.hd, half = hd / 2;
 
@@ -814,9 +880,16 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
     cs.parity = 0;
     cs.failed = false;
     uint4 wv[kNormPer];
+    // tags of this launch: epoch in [1, 65535], layer, hop
+    const uint32_t e16 = 1u + (__ldcg(a.misc + 2) % 65535u);
+    auto ptag = [&](int layer, int hop) {
+        return (e16 << 16) | (static_cast<uint32_t>(layer) << 3) | static_cast<uint32_t>(hop);
+    };
+    auto ctag = [&](int layer, int hop) {  // the test hook makes one hop's tag unreachable
+        return a.stall_counter == hop_counter(hop) ? (ptag(layer, hop) | 7u) : ptag(layer, hop);
+    };
     for (int l = 0; l < a.nlayers; ++l) {
         const uint64_t* L = a.layers + static_cast<int64_t>(l) * kTSlots;
-        unsigned* ctr = a.counters + l * kRStride;
         uint16_t* tap = rtap(a, l);
         const bool tap0 = tap != nullptr && blockIdx.x == 0;
         KR_STAMP(l, 0);
@@ -832,9 +905,16 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
                 bias_s[i] = b != nullptr ? b[j] : static_cast<uint16_t>(0);
             }
         }
-        if (l > 0) rwait(a, a.counters + (l - 1) * kRStride + kCDn, static_cast<unsigned>(a.ctas[kODn]));
-        rload_bf16(xres, a.x, a.hidden);
-        __syncthreads();  // (also: every thread is past the previous layer's reads of the K/V tile rows)
+        if (l == 0) {
+            rload_bf16(xres, a.x, a.hidden);
+            __syncthreads();
+        } else {  // the previous layer's x2
+            const uint32_t tg = ctag(l, kHX);
+            rpoll<8>(
+                a, a.hidden / 2, [&](int i) { return a.xw + i; }, [&](int) { return tg; },
+                [&](int i, uint32_t p) { reinterpret_cast<uint32_t*>(xres)[i] = p; });
+        }
+        // (every thread is now past the previous layer's reads of the K/V tile rows)
         KR_STAMP(l, 1);
         if (att_cta) {  // this layer's first K/V tile, after x (whose loads would queue behind these copies):
                         // rows before pos are final (row pos is loaded with q)
@@ -851,10 +931,14 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             uint16_t* vcl = reinterpret_cast<uint16_t*>(L[kTVCache]);
             const int qt = a.qh * hd / 16, kt = a.kvh * hd / 16, per = hd / 16;
             const bool bias = a.bias_rows > 0;
-            rgemv<kOQkv>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
-                if (T < qt + kt) {  // q or k: RoPE pair (i, i + half)
-                    const bool isq = T < qt;
-                    const int u = isq ? T : T - qt, head = u / per, i = 8 * (u - head * per) + r;
+            const uint32_t tq = ptag(l, kHQ), tk = ptag(l, kHK), tv = ptag(l, kHV);
+            rgemv<kOQkv>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi, unsigned lanes) {
+                // q/k: RoPE pair (dims i, i + half) of a head; v: rows d, d + 8 of a 16-row tile
+                const bool qk = T < qt + kt, isq = T < qt;
+                const int u = isq ? T : T - qt, head = u / per, i = 8 * (u - head * per) + r;
+                const int d = 16 * (T - qt - kt) + r;
+                uint16_t o0, o1;
+                if (qk) {
                     const int row0 = (isq ? 0 : a.qh * hd) + head * hd + i;
                     float y0 = round_bf16(ylo), y1 = round_bf16(yhi);
                     if (bias) {
@@ -862,103 +946,136 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
                         y1 = round_bf16(y1 + bf16_bits_to_f32(bias_s[row0 + half]));
                     }
                     const float c = rope_s[i], sn = rope_s[half + i];
-                    const uint16_t lo = f32_to_bf16_bits(round_bf16(round_bf16(y0 * c) + round_bf16(-y1 * sn)));
-                    const uint16_t hi = f32_to_bf16_bits(round_bf16(round_bf16(y1 * c) + round_bf16(y0 * sn)));
-                    if (isq) {
-                        a.qg[head * hd + i] = lo;
-                        a.qg[head * hd + i + half] = hi;
-                    } else {
-                        kcl[(static_cast<int64_t>(head) * a.cap + pos_c) * hd + i] = lo;
-                        kcl[(static_cast<int64_t>(head) * a.cap + pos_c) * hd + i + half] = hi;
+                    o0 = f32_to_bf16_bits(round_bf16(round_bf16(y0 * c) + round_bf16(-y1 * sn)));
+                    o1 = f32_to_bf16_bits(round_bf16(round_bf16(y1 * c) + round_bf16(y0 * sn)));
+                } else {
+                    float y0 = round_bf16(ylo), y1 = round_bf16(yhi);
+                    if (bias) {
+                        y0 = round_bf16(y0 + bf16_bits_to_f32(bias_s[(a.qh + a.kvh) * hd + d]));
+                        y1 = round_bf16(y1 + bf16_bits_to_f32(bias_s[(a.qh + a.kvh) * hd + d + 8]));
+                    }
+                    o0 = f32_to_bf16_bits(y0);
+                    o1 = f32_to_bf16_bits(y1);
+                }
+                const uint32_t p0 = pair_up(o0, lanes), p1 = pair_up(o1, lanes);  // every lane of the 8-lane group
+                if (qk) {
+                    if (!isq) {  // the cache row, read by later steps
+                        kcl[(static_cast<int64_t>(head) * a.cap + pos_c) * hd + i] = o0;
+                        kcl[(static_cast<int64_t>(head) * a.cap + pos_c) * hd + i + half] = o1;
+                    }
+                    if ((r & 1) == 0) {
+                        uint64_t* w = (isq ? a.qw : a.kw) + (head * hd + i) / 2;
+                        st_tagged(w, isq ? tq : tk, p0);
+                        st_tagged(w + half / 2, isq ? tq : tk, p1);
                     }
                     if (tap != nullptr) {
                         uint16_t* tp = tap + (isq ? to.q : to.k) + head * hd + i;
-                        tp[0] = lo;
-                        tp[half] = hi;
+                        tp[0] = o0;
+                        tp[half] = o1;
                     }
-                } else {  // v: rows d and d + 8 of a 16-row tile
-                    const int d0 = 16 * (T - qt - kt) + r;
+                } else {
 #pragma unroll
                     for (int k = 0; k < 2; ++k) {
-                        const int d = d0 + 8 * k;
-                        float y = round_bf16(k == 0 ? ylo : yhi);
-                        if (bias) y = round_bf16(y + bf16_bits_to_f32(bias_s[(a.qh + a.kvh) * hd + d]));
-                        const uint16_t vb = f32_to_bf16_bits(y);
-                        const int hv = d / hd;
-                        vcl[(static_cast<int64_t>(hv) * a.cap + pos_c) * hd + (d - hv * hd)] = vb;
-                        if (tap != nullptr) tap[to.v + d] = vb;
+                        const int dd = d + 8 * k, hv = dd / hd;
+                        vcl[(static_cast<int64_t>(hv) * a.cap + pos_c) * hd + (dd - hv * hd)] = k == 0 ? o0 : o1;
+                        if (tap != nullptr) tap[to.v + dd] = k == 0 ? o0 : o1;
+                    }
+                    if ((r & 1) == 0) {
+                        st_tagged(a.vw + d / 2, tv, p0);
+                        st_tagged(a.vw + (d + 8) / 2, tv, p1);
                     }
                 }
             });
-            if (own_qkv) rsignal(ctr + kCQkv);
         }
         KR_STAMP(l, 3);
         // ---- attention splits, merged once per KV head
         if (att_cta) {
-            rwait(a, ctr + kCQkv, static_cast<unsigned>(a.ctas[kOQkv]));
             KR_STAMP(l, 4);
-            rattention(a, l, L, pos_c, kv_len, ap, att_sm);
+            rattention(a, l, L, pos_c, kv_len, ap, att_sm, ctag(l, kHQ), ctag(l, kHK), ctag(l, kHV), ptag(l, kHAtt));
             KR_STAMP(l, 5);
         }
         // ---- o_proj owners: x1 = x + o_proj(attention)
         rnorm_prefetch(a, reinterpret_cast<const uint16_t*>(L[kTPostNorm]), wv);
         if (own_o) {
-            rwait(a, ctr + kCAtt, static_cast<unsigned>(a.kvh * ap.ns));
             KR_STAMP(l, 6);
-            rstage_f16(a, xs, a.attg, a.qh * hd);
+            {
+                const uint32_t tg = ctag(l, kHAtt);
+                rpoll<8>(
+                    a, a.qh * hd / 2, [&](int i) { return a.aw + i; }, [&](int) { return tg; },
+                    [&](int i, uint32_t p) { reinterpret_cast<uint32_t*>(xs)[i] = p; });
+            }
             KR_STAMP(l, 7);
-            rgemv<kOO>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
+            const uint32_t tx1 = ptag(l, kHX1);
+            rgemv<kOO>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi, unsigned lanes) {
+                uint16_t x1[2];
 #pragma unroll
                 for (int k = 0; k < 2; ++k) {
                     const int row = 16 * T + r + 8 * k;
-                    const float o = round_bf16(k == 0 ? ylo : yhi);
-                    const uint16_t x1 = f32_to_bf16_bits(bf16_bits_to_f32(xres[row]) + o);
-                    a.x1g[row] = x1;
-                    if (tap != nullptr) tap[to.x1 + row] = x1;
+                    x1[k] = f32_to_bf16_bits(bf16_bits_to_f32(xres[row]) + round_bf16(k == 0 ? ylo : yhi));
+                    if (tap != nullptr) tap[to.x1 + row] = x1[k];
+                }
+                const uint32_t p0 = pair_up(x1[0], lanes), p1 = pair_up(x1[1], lanes);
+                if ((r & 1) == 0) {
+                    st_tagged(a.x1w + (16 * T + r) / 2, tx1, p0);
+                    st_tagged(a.x1w + (16 * T + r + 8) / 2, tx1, p1);
                 }
             });
-            rsignal(ctr + kCO);
             KR_STAMP(l, 8);
         }
         // ---- x1 ready -> RMSNorm -> gate/up owners (SwiGLU)
-        rwait(a, ctr + kCO, static_cast<unsigned>(a.ctas[kOO]));
+        {
+            const uint32_t tg = ctag(l, kHX1);
+            rpoll<8>(
+                a, a.hidden / 2, [&](int i) { return a.x1w + i; }, [&](int) { return tg; },
+                [&](int i, uint32_t p) { reinterpret_cast<uint32_t*>(xres)[i] = p; });
+        }
         KR_STAMP(l, 9);
-        rload_bf16(xres, a.x1g, a.hidden);
-        __syncthreads();
         rstage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn2 : nullptr);
         KR_STAMP(l, 10);
         {
             bool overflow = false;
-            rgemv<kOGu>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
+            const uint32_t th = ptag(l, kHH);
+            rgemv<kOGu>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi, unsigned lanes) {
                 const int j = 8 * T + r;
                 const float gv = round_bf16(ylo), uv = round_bf16(yhi);
                 const float act = round_bf16(gv / (1.0F + expf(-gv)));
                 const uint16_t h = f32_to_bf16_bits(act * uv);
-                a.hg[j] = h;
-                overflow |= !(fabsf(bf16_bits_to_f32(h)) <= 65504.F);
+                const float hf = bf16_bits_to_f32(h);
+                overflow |= !(fabsf(hf) <= 65504.F);
                 if (tap != nullptr) tap[to.h + j] = h;
+                const uint32_t p = pair_up(f32_to_f16_bits(hf), lanes);  // the down GEMV's f16 input
+                if ((r & 1) == 0) st_tagged(a.hw + j / 2, th, p);
             });
             if (overflow) atomicOr(a.err, 1);
-            if (own_gu) rsignal(ctr + kCGu);
         }
         KR_STAMP(l, 11);
         // ---- down owners: x2 = x1 + down(h), the next layer's input
         if (own_dn) {
-            rwait(a, ctr + kCGu, static_cast<unsigned>(a.ctas[kOGu]));
             KR_STAMP(l, 12);
-            rstage_f16(a, xs, a.hg, a.inter);
+            {
+                const uint32_t tg = ctag(l, kHH);
+                rpoll<16>(
+                    a, a.inter / 2, [&](int i) { return a.hw + i; }, [&](int) { return tg; },
+                    [&](int i, uint32_t p) { reinterpret_cast<uint32_t*>(xs)[i] = p; });
+            }
             KR_STAMP(l, 13);
-            rgemv<kODn>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi) {
+            const uint32_t tx = ptag(l + 1, kHX);
+            const bool last = l == a.nlayers - 1;
+            rgemv<kODn>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi, unsigned lanes) {
+                uint16_t x2[2];
 #pragma unroll
                 for (int k = 0; k < 2; ++k) {
                     const int row = 16 * T + r + 8 * k;
-                    const float d = round_bf16(k == 0 ? ylo : yhi);
-                    const uint16_t x2 = f32_to_bf16_bits(bf16_bits_to_f32(xres[row]) + d);
-                    a.x[row] = x2;
-                    if (tap != nullptr) tap[to.x2 + row] = x2;
+                    x2[k] = f32_to_bf16_bits(bf16_bits_to_f32(xres[row]) + round_bf16(k == 0 ? ylo : yhi));
+                    if (last) a.x[row] = x2[k];  // the step's output, read by the lm_head after the kernel
+                    if (tap != nullptr) tap[to.x2 + row] = x2[k];
+                }
+                const uint32_t p0 = pair_up(x2[0], lanes), p1 = pair_up(x2[1], lanes);
+                if ((r & 1) == 0 && !last) {
+                    st_tagged(a.xw + (16 * T + r) / 2, tx, p0);
+                    st_tagged(a.xw + (16 * T + r + 8) / 2, tx, p1);
                 }
             });
-            rsignal(ctr + kCDn);
             KR_STAMP(l, 14);
         }
     }
@@ -973,6 +1090,7 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             for (int i = 0; i < a.nlayers * kRStride; ++i) a.counters[i] = 0u;
             a.misc[0] = 0u;
             a.misc[1] = 0u;
+            a.misc[2] += 1u;  // the next launch's tags differ from every word written here
             __threadfence();
         }
     }
@@ -1035,7 +1153,7 @@ __global__ void nf4_retile16_kernel(const Retile16Args r) {
 struct RowGeom {
     int tiles[4], nbpt[4], ctas[4];
     int xs_bytes, work_bytes, bias_rows, ring_slots, smem;
-    int64_t off_misc, off_qg, off_attg, off_x1g, off_hg, off_apart, total;
+    int64_t off_misc, off_qw, off_kw, off_vw, off_aw, off_x1w, off_hw, off_xw, off_apart, total;
 };
 constexpr int kRStaticSmemBudget = 3072;
 
@@ -1066,14 +1184,20 @@ RowGeom row_geom(const PersistDims& d, int sms) {
     int64_t off = up(static_cast<int64_t>(d.layers) * kRStride * 4);
     g.off_misc = off;
     off = up(off + 64);
-    g.off_qg = off;
-    off = up(off + static_cast<int64_t>(d.q_heads) * d.head_dim * 2);
-    g.off_attg = off;
-    off = up(off + static_cast<int64_t>(d.q_heads) * d.head_dim * 2);
-    g.off_x1g = off;
-    off = up(off + static_cast<int64_t>(d.hidden) * 2);
-    g.off_hg = off;
-    off = up(off + static_cast<int64_t>(d.intermediate) * 2);
+    g.off_qw = off;  // tagged words: 8 bytes per two values
+    off = up(off + static_cast<int64_t>(d.q_heads) * d.head_dim * 4);
+    g.off_kw = off;
+    off = up(off + static_cast<int64_t>(d.kv_heads) * d.head_dim * 4);
+    g.off_vw = off;
+    off = up(off + static_cast<int64_t>(d.kv_heads) * d.head_dim * 4);
+    g.off_aw = off;
+    off = up(off + static_cast<int64_t>(d.q_heads) * d.head_dim * 4);
+    g.off_x1w = off;
+    off = up(off + static_cast<int64_t>(d.hidden) * 4);
+    g.off_hw = off;
+    off = up(off + static_cast<int64_t>(d.intermediate) * 4);
+    g.off_xw = off;
+    off = up(off + static_cast<int64_t>(d.hidden) * 4);
     g.off_apart = off;
     off = up(off + static_cast<int64_t>(d.kv_heads) * kAMaxSplits * gq * (d.head_dim + 4) * 4);
     g.total = off;
@@ -1119,9 +1243,10 @@ int64_t decode_rows_scratch_bytes(const PersistDims& d, int sms) { return row_ge
 const char* decode_rows_check(const PersistDims& d, int sms) {
     if (d.layers < 1 || d.hidden < 64 || d.hidden % 64 != 0 || d.head_dim != 128 || d.q_heads < 1 || d.kv_heads < 1 ||
         d.q_heads % d.kv_heads != 0 || d.q_heads / d.kv_heads > 8 || d.intermediate % 64 != 0 ||
-        d.hidden > 8 * kRT * kNormPer || d.kv_capacity < 1 || d.kv_heads > sms || d.kv_heads + kCTicket > kRStride)
-        return "row-split persistent decode requires hidden % 64 == 0 (<= 16384), head_dim 128, q_heads/kv_heads <= 8, "
-               "kv_heads <= 11, intermediate % 64 == 0";
+        d.hidden > 8 * kRT * kNormPer || d.kv_capacity < 1 || d.kv_heads > sms || d.kv_heads + kCTicket > kRStride ||
+        d.hidden > 16 * kRT || d.q_heads * d.head_dim > 16 * kRT || d.intermediate > 32 * kRT || d.layers >= 8192)
+        return "row-split persistent decode requires hidden % 64 == 0 (<= 8192), head_dim 128, q_heads/kv_heads <= 8, "
+               "q_heads * head_dim <= 8192, kv_heads <= 11, intermediate % 64 == 0 (<= 16384), layers < 8192";
     const RowGeom g = row_geom(d, sms);
     if (g.smem > 232448 - kRStaticSmemBudget) return "row-split persistent decode: shapes need more shared memory than one SM has";
     for (int i = 0; i < 4; ++i) {
@@ -1157,10 +1282,13 @@ cudaError_t decode_layers_rows(const PersistLaunch& p, cudaStream_t stream) {
     char* s = static_cast<char*>(p.scratch);
     a.counters = reinterpret_cast<unsigned*>(s);
     a.misc = reinterpret_cast<unsigned*>(s + g.off_misc);
-    a.qg = reinterpret_cast<uint16_t*>(s + g.off_qg);
-    a.attg = reinterpret_cast<uint16_t*>(s + g.off_attg);
-    a.x1g = reinterpret_cast<uint16_t*>(s + g.off_x1g);
-    a.hg = reinterpret_cast<uint16_t*>(s + g.off_hg);
+    a.qw = reinterpret_cast<uint64_t*>(s + g.off_qw);
+    a.kw = reinterpret_cast<uint64_t*>(s + g.off_kw);
+    a.vw = reinterpret_cast<uint64_t*>(s + g.off_vw);
+    a.aw = reinterpret_cast<uint64_t*>(s + g.off_aw);
+    a.x1w = reinterpret_cast<uint64_t*>(s + g.off_x1w);
+    a.hw = reinterpret_cast<uint64_t*>(s + g.off_hw);
+    a.xw = reinterpret_cast<uint64_t*>(s + g.off_xw);
     a.apart = reinterpret_cast<float*>(s + g.off_apart);
     a.err = p.err;
     a.ring_slots = g.ring_slots;
