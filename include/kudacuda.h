@@ -374,9 +374,13 @@ KUDACUDA_API int kudacuda_sm100_decode_layers_persistent_debug(void* handle, uin
  * units, gate/up units, down units, input norm, post norm, q bias, k bias,
  * v bias (0 when absent), K cache, V cache, then zeros.  taps / spin_limit /
  * stall_counter are the test hooks of decode_layers_persistent_debug (the
- * same tap layout; counter index = layer * 16 + {0 qkv, 1 attention,
- * 2 o_proj, 3 gate/up, 4 down}).  Deterministic (fixed summation order);
- * every device wait is bounded and reports bit 4 of the error word. */
+ * same tap layout; stall index = layer * 16 + {0 qkv, 1 attention,
+ * 2 o_proj, 3 gate/up, 4 down, 5 attention partials}).  Ops hand their
+ * outputs to the next op as tagged 8-byte words in the scratch (two 16-bit
+ * values, or one f32, plus a launch/layer/hop tag) that consumers poll
+ * directly, so the scratch starts zeroed and is kept across steps (it also
+ * counts the launches).  Deterministic (fixed summation order); every
+ * device wait is bounded and reports bit 4 of the error word. */
 KUDACUDA_API int64_t kudacuda_sm100_nf4_retile16_tiles(int mode, int64_t rows0, int64_t rows1, int64_t rows2,
                                                        int64_t head_dim);
 KUDACUDA_API int kudacuda_sm100_nf4_retile16(void* handle, int mode, uint64_t packed0, uint64_t absmax0, int64_t rows0,

@@ -41,7 +41,7 @@
 #include "kc_launch.h"
 
 // Phase timestamps for profiling builds only (-DKC_PERSIST_STAMPS; off in the
-// library): thread 0 of every CTA records %globaltimer and clock64 at fixed
+// library): thread 0 of every CTA records %globaltimer at up to 64 fixed
 // points of one layer (KC_STAMP_LAYER) into g_rows_stamps[cta][64], read back
 // with kc_rows_read_stamps.  No work is skipped or added to the product build.
 #ifdef KC_PERSIST_STAMPS
@@ -55,7 +55,6 @@ __device__ unsigned long long g_rows_stamps[1024 * 64];
             unsigned long long t_;                                              \
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)::"memory");    \
             g_rows_stamps[blockIdx.x * 64 + (i)] = t_;                          \
-            g_rows_stamps[blockIdx.x * 64 + 32 + (i)] = clock64();              \
         }                                                                       \
     } while (0)
 extern "C" __attribute__((visibility("default"))) int kc_rows_read_stamps(unsigned long long* out, int n) {
@@ -85,19 +84,26 @@ constexpr int kSlotUnits = KC_ROWS_SLOT_UNITS;  // units per bulk copy / ring sl
 constexpr int kSlotBytes = kSlotUnits * kUnitBytes;
 constexpr int kRLutBytes = 65536;  // 256 entry rows x 256 B, lane replicas in the first 128 B of a row
 constexpr int kMaxCtaTiles = 16;   // tiles of one op one CTA may own (checked on the host)
-constexpr int kRStride = 16;       // counters per layer: 0 qkv, 1 attention, 2 o_proj, 3 gate/up, 4 down, 5.. tickets
 constexpr uint32_t kRSpinLimit = 1u << 21;
 constexpr int kATile = 64;         // tokens per attention tile
+constexpr int kSs = kATile + 8;    // score row stride (floats): P reads of the 8 heads fall in distinct bank pairs
 constexpr int kAMaxSplits = 32;    // splits per KV head
 constexpr int kKRow = 136;         // padded K/V/q row in shared memory (bf16): 272 bytes
 constexpr int kRngStride = kRW + 3;  // per op: t0, t1, warp unit bounds 0..16
 
 enum RowOp { kOQkv = 0, kOO = 1, kOGu = 2, kODn = 3 };
+// stall_counter test hook: the op whose output a consumer never sees (0 q/k/v, 1 attention, 2 o_proj,
+// 3 gate/up, 4 down, 5 the attention splits' partials)
 enum RowCtr { kCQkv = 0, kCAtt = 1, kCO = 2, kCGu = 3, kCDn = 4, kCTicket = 5 };
-// hops between ops, the low 3 bits of a tag (7: never written, the test hook's unreachable tag)
-enum RowHop { kHX = 0, kHQ = 1, kHK = 2, kHV = 3, kHAtt = 4, kHX1 = 5, kHH = 6 };
-__host__ __device__ constexpr int hop_counter(int hop) {  // the op counter a hop replaces (stall_counter hook)
-    return hop == kHX ? kCDn : hop <= kHV ? kCQkv : hop == kHAtt ? kCAtt : hop == kHX1 ? kCO : kCGu;
+// hops between ops, the low 4 bits of a tag (15: never written, the test hook's unreachable tag)
+enum RowHop { kHX = 0, kHQ = 1, kHK = 2, kHV = 3, kHAtt = 4, kHX1 = 5, kHH = 6, kHPart = 7 };
+__host__ __device__ constexpr int hop_counter(int hop) {  // the stall_counter index of a hop
+    return hop == kHX     ? kCDn
+           : hop <= kHV   ? kCQkv
+           : hop == kHAtt ? kCAtt
+           : hop == kHX1  ? kCO
+           : hop == kHH   ? kCGu
+                          : kCTicket;
 }
 enum RowSlot { kTUnits0 = 0, kTInNorm = 4, kTPostNorm, kTQBias, kTKBias, kTVBias, kTKCache, kTVCache, kTSlots = 16 };
 
@@ -109,7 +115,6 @@ struct RowArgs {
     uint16_t* x;           // bf16 [hidden]: the step's input, then every layer's x2 (the last is the output)
     const uint16_t* rope_cos;
     const uint16_t* rope_sin;
-    unsigned* counters;  // [nlayers * kRStride]
     unsigned* misc;      // [0] abort flag, [1] final ticket, [2] launch count (the tags' epoch)
     // Tagged words carry one op's output to the next: two 16-bit values
     // (element 2 i in the low half) and, in the high 32 bits, the tag of the
@@ -123,7 +128,7 @@ struct RowArgs {
     uint64_t* x1w;  // [hidden / 2] x + o_proj (bf16)
     uint64_t* hw;   // [inter / 2] SwiGLU output (f16 of the bf16 value)
     uint64_t* xw;   // [hidden / 2] x2, the next layer's input (bf16)
-    float* apart;        // [kvh][kAMaxSplits][gq][hd + 4] attention partials
+    uint64_t* pw;   // [kvh][kAMaxSplits][gq][2 + hd] attention partials: max, sum, accumulator (f32 bits)
     int* err;
     int ring_slots;
     int tiles[4], nbpt[4], ctas[4];
@@ -202,34 +207,6 @@ __device__ __forceinline__ unsigned ld_relaxed_r(const unsigned* p) {
     unsigned v;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
-}
-// Thread 0 waits until *ctr >= target (or the step was aborted), polling with
-// relaxed loads (the abort flag every 32 polls) and acquiring once at the
-// end; then the whole CTA continues.  A wait that runs out raises the abort
-// flag and error bit 4.
-__device__ void rwait(const RowArgs& a, const unsigned* ctr, unsigned target) {
-    if (threadIdx.x == 0) {
-        if (a.stall_counter >= 0 && ctr == a.counters + a.stall_counter) ++target;  // test hook: never reached
-        uint32_t n = 0;
-        while (ld_relaxed_r(ctr) < target) {
-            if ((++n & 31u) == 0u) {
-                if (ld_relaxed_r(a.misc) != 0u) break;
-                if (n > a.spin_limit) {
-                    atomicExch(a.misc, 1u);
-                    atomicOr(a.err, 16);
-                    break;
-                }
-            }
-        }
-        (void)ld_acquire_r(ctr);
-    }
-    __syncthreads();
-}
-// After every thread of the CTA wrote its results: one release increment.
-__device__ __forceinline__ void rsignal(unsigned* ctr) {
-    __syncthreads();
-    if (threadIdx.x == 0)
-        asm volatile("fence.acq_rel.gpu;\n\tred.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
 }
 // Tagged words (RowArgs): aligned 8-byte strong accesses are single-copy
 // atomic, so a word read with the expected tag carries that write's payload.
@@ -547,20 +524,20 @@ struct RAttSmem {
     uint16_t* kt;  // [kATile][kKRow]  (a region of its own: the first tile is fetched at layer start)
     uint16_t* vt;  // [kATile][kKRow]
     uint16_t* qb;  // [8][kKRow]: the group's q rows (bf16), rows >= gq zero   (in the work region)
-    float* ss;     // [2][8][kATile]: score halves, then probabilities in [0]; the merge's weights
+    float* ss;     // [2][8][kSs]: score halves, then probabilities in [0]; the merge's weights and split max/sum
     float* ml;     // [8][4]: running max, sum, correction
     float* mb;     // [8][ns * nd <= 160]: the merge's slice of every split's accumulator, [hq][split][dim]
     uint16_t* kvpos;  // [2][128]: this step's k and v rows (bf16), from the q/k/v owners' tagged words
 };
 constexpr int kRKvTileBytes = 2 * kATile * kKRow * 2;
-constexpr int kRAttWorkBytes = 8 * kKRow * 2 + 2 * 8 * kATile * 4 + 8 * 4 * 4 + 8 * 160 * 4 + 2 * 128 * 2;
+constexpr int kRAttWorkBytes = 8 * kKRow * 2 + 2 * 8 * kSs * 4 + 8 * 4 * 4 + 8 * 160 * 4 + 2 * 128 * 2;
 __device__ __forceinline__ RAttSmem ratt_smem(uint8_t* work, uint8_t* kvt) {
     RAttSmem s;
     s.kt = reinterpret_cast<uint16_t*>(kvt);
     s.vt = s.kt + kATile * kKRow;
     s.qb = reinterpret_cast<uint16_t*>(work);
     s.ss = reinterpret_cast<float*>(s.qb + 8 * kKRow);
-    s.ml = s.ss + 2 * 8 * kATile;
+    s.ml = s.ss + 2 * 8 * kSs;
     s.mb = s.ml + 8 * 4;
     s.kvpos = reinterpret_cast<uint16_t*>(s.mb + 8 * 160);
     return s;
@@ -609,7 +586,8 @@ __device__ __forceinline__ void rsplit_pair(float p0, float p1, uint32_t& hi, ui
 // the head dims (all ns splits, all gq query heads) into the attention
 // output, written once for all o_proj owners.
 __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int pos, int kv_len, const RAttPlan& ap,
-                           const RAttSmem& sm, uint32_t tq, uint32_t tk, uint32_t tv, uint32_t tatt) {
+                           const RAttSmem& sm, uint32_t tq, uint32_t tk, uint32_t tv, uint32_t tatt, uint32_t tpart,
+                           uint32_t tpart_c) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int gq = a.qh / a.kvh, hd = a.hd;
     const int hk = static_cast<int>(blockIdx.x) / ap.ns, s = static_cast<int>(blockIdx.x) - hk * ap.ns;
@@ -678,17 +656,18 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
                          *reinterpret_cast<const uint32_t*>(krow + 32 * s4 + 48));
             }
             if (g < gq)
-                *reinterpret_cast<float2*>(sm.ss + (hf * 8 + g) * kATile + ntl * 8 + 2 * t) =
+                *reinterpret_cast<float2*>(sm.ss + (hf * 8 + g) * kSs + ntl * 8 + 2 * t) =
                     make_float2((c0[0] + c1[0]) * a.scale_log2, (c0[1] + c1[1]) * a.scale_log2);
         }
         __syncthreads();
+        if (t0 == tok0) KR_STAMP(layer, 32);
         if (warp < gq) {  // online softmax per head over the tile (log2 domain); probabilities zero past nt
             float v[2];
             float mx = -INFINITY;
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
                 const int j = lane + 32 * k;
-                v[k] = j < nt ? sm.ss[warp * kATile + j] + sm.ss[(8 + warp) * kATile + j] : -INFINITY;
+                v[k] = j < nt ? sm.ss[warp * kSs + j] + sm.ss[(8 + warp) * kSs + j] : -INFINITY;
                 mx = fmaxf(mx, v[k]);
             }
             mx = warp_max(mx);
@@ -699,7 +678,7 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
             for (int k = 0; k < 2; ++k) {
                 const int j = lane + 32 * k;
                 const float p = j < nt ? exp2f(v[k] - m_new) : 0.F;
-                if (j < n16) sm.ss[warp * kATile + j] = p;
+                if (j < n16) sm.ss[warp * kSs + j] = p;
                 ls += p;
             }
             ls = warp_sum(ls);
@@ -711,13 +690,14 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
             }
         }
         __syncthreads();
+        if (t0 == tok0) KR_STAMP(layer, 33);
         if (warp < hd / 8) {  // P.V: warp w owns dims 8w .. 8w+7
             const float corr = g < gq ? sm.ml[g * 4 + 2] : 1.F;
             o0[0] *= corr;
             o0[1] *= corr;
             o1[0] *= corr;
             o1[1] *= corr;
-            const float* prow = sm.ss + (g < gq ? g : 0) * kATile + 2 * t;
+            const float* prow = sm.ss + (g < gq ? g : 0) * kSs + 2 * t;
             const int nk = n16 >> 4;
             for (int kk = 0; kk < nk; kk += 2) {
                 const bool two = kk + 1 < nk;
@@ -745,46 +725,51 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
             }
         }
     }
-    const int rec = hd + 4;
-    float* mine = a.apart + ((static_cast<size_t>(hk) * kAMaxSplits + s) * gq) * rec;
-    if (warp < hd / 8 && g < gq)
-        *reinterpret_cast<float2*>(mine + g * rec + 4 + 8 * warp + 2 * t) = make_float2(o0[0] + o1[0], o0[1] + o1[1]);
+    KR_STAMP(layer, 34);
+    // ---- this split's partial as tagged words: max, sum, then the accumulator of each head
+    const int rec = hd + 2;
+    uint64_t* mine = a.pw + (static_cast<size_t>(hk) * kAMaxSplits + s) * gq * rec;
+    if (warp < hd / 8 && g < gq) {
+        st_tagged(mine + g * rec + 2 + 8 * warp + 2 * t, tpart, __float_as_uint(o0[0] + o1[0]));
+        st_tagged(mine + g * rec + 3 + 8 * warp + 2 * t, tpart, __float_as_uint(o0[1] + o1[1]));
+    }
     if (tid < gq) {
-        mine[tid * rec + 0] = sm.ml[tid * 4 + 0];
-        mine[tid * rec + 1] = sm.ml[tid * 4 + 1];
+        st_tagged(mine + tid * rec + 0, tpart, __float_as_uint(sm.ml[tid * 4 + 0]));
+        st_tagged(mine + tid * rec + 1, tpart, __float_as_uint(sm.ml[tid * 4 + 1]));
     }
-    // ---- every split of the head out -> each split merges dims [d0, d1) of the gq heads
-    unsigned* ctr = a.counters + layer * kRStride;
-    rsignal(ctr + kCTicket + hk);
-    KR_STAMP(layer, 30);
-    if (ap.ns > 1) rwait(a, ctr + kCTicket + hk, static_cast<unsigned>(ap.ns));
-    KR_STAMP(layer, 31);
-    // the slice's accumulators (gq x ns x nd <= 8 x 132 floats, at most three per
-    // thread) go out together with the split maxima and sums: one round trip
-    float* wn = sm.ss;  // [gq][kAMaxSplits] normalised split weights
+    KR_STAMP(layer, 35);
+    // ---- each split merges dims [d0, d0 + nd) of the gq heads: the max, sum and
+    // that slice of every split's accumulator, polled as tagged words
+    // (ns x gq x (2 + nd) <= 2048 words, at most four per thread)
+    float* wn = sm.ss;          // [gq][kAMaxSplits] normalised split weights
+    float* mls = sm.ss + 256;   // [gq][kAMaxSplits][2] split max and sum
     const int d0 = 2 * (s * hp / ap.ns), nd = 2 * ((s + 1) * hp / ap.ns) - d0, per = ap.ns * nd;  // even slices
-    float accv[3];
-#pragma unroll
-    for (int k = 0; k < 3; ++k) {
-        const int v = tid + k * kRT, hq = v / per, rem = v - hq * per, sp = rem / nd;
-        accv[k] = hq < gq ? __ldcg(a.apart + ((static_cast<size_t>(hk) * kAMaxSplits + sp) * gq + hq) * rec + 4 + d0 +
-                                   (rem - sp * nd))
-                          : 0.F;
-    }
+    const int nrec = 2 + nd;
+    __syncthreads();  // every thread is past its reads of ss (P.V) before the sink writes it
+    rpoll<4>(
+        a, ap.ns * gq * nrec,
+        [&](int i) -> const uint64_t* {
+            const int sp = i / (gq * nrec), rem = i - sp * gq * nrec, hq = rem / nrec, j = rem - hq * nrec;
+            return a.pw + ((static_cast<size_t>(hk) * kAMaxSplits + sp) * gq + hq) * rec + (j < 2 ? j : d0 + j);
+        },
+        [&](int) { return tpart_c; },
+        [&](int i, uint32_t p) {
+            const int sp = i / (gq * nrec), rem = i - sp * gq * nrec, hq = rem / nrec, j = rem - hq * nrec;
+            if (j < 2) mls[(hq * kAMaxSplits + sp) * 2 + j] = __uint_as_float(p);
+            else sm.mb[hq * per + sp * nd + (j - 2)] = __uint_as_float(p);
+        });
+    KR_STAMP(layer, 31);
     if (warp < gq) {
-        const float* p = a.apart + ((static_cast<size_t>(hk) * kAMaxSplits + lane) * gq + warp) * rec;
         const bool live = lane < ap.ns;
-        const float m = live ? __ldcg(p) : -INFINITY;
-        const float l = live ? __ldcg(p + 1) : 0.F;
+        const float m = live ? mls[(warp * kAMaxSplits + lane) * 2] : -INFINITY;
+        const float l = live ? mls[(warp * kAMaxSplits + lane) * 2 + 1] : 0.F;
         const float M = warp_max(m);
         const float e = live && m != -INFINITY ? exp2f(m - M) : 0.F;
         const float den = warp_sum(e * l);
         wn[warp * kAMaxSplits + lane] = den > 0.F ? e / den : 0.F;
     }
-#pragma unroll
-    for (int k = 0; k < 3; ++k)
-        if (tid + k * kRT < gq * per) sm.mb[tid + k * kRT] = accv[k];
     __syncthreads();
+    KR_STAMP(layer, 36);
     uint16_t* tap = rtap(a, layer);
     const int att_off = tap != nullptr ? rtaps(a.hidden, a.qh, a.kvh, hd, a.inter).att : 0;
     bool overflow = false;
@@ -810,6 +795,7 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
         }
     }
     if (overflow) atomicOr(a.err, 1);
+    __syncthreads();  // the merge's reads of wn / mb before the caller's next writes to the work area
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -883,10 +869,10 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
     // tags of this launch: epoch in [1, 65535], layer, hop
     const uint32_t e16 = 1u + (__ldcg(a.misc + 2) % 65535u);
     auto ptag = [&](int layer, int hop) {
-        return (e16 << 16) | (static_cast<uint32_t>(layer) << 3) | static_cast<uint32_t>(hop);
+        return (e16 << 16) | (static_cast<uint32_t>(layer) << 4) | static_cast<uint32_t>(hop);
     };
-    auto ctag = [&](int layer, int hop) {  // the test hook makes one hop's tag unreachable
-        return a.stall_counter == hop_counter(hop) ? (ptag(layer, hop) | 7u) : ptag(layer, hop);
+    auto ctag = [&](int layer, int hop) {  // test hook: stall_counter = layer * 16 + op makes that tag unreachable
+        return a.stall_counter == layer * 16 + hop_counter(hop) ? (ptag(layer, hop) | 15u) : ptag(layer, hop);
     };
     for (int l = 0; l < a.nlayers; ++l) {
         const uint64_t* L = a.layers + static_cast<int64_t>(l) * kTSlots;
@@ -991,7 +977,8 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
         // ---- attention splits, merged once per KV head
         if (att_cta) {
             KR_STAMP(l, 4);
-            rattention(a, l, L, pos_c, kv_len, ap, att_sm, ctag(l, kHQ), ctag(l, kHK), ctag(l, kHV), ptag(l, kHAtt));
+            rattention(a, l, L, pos_c, kv_len, ap, att_sm, ctag(l, kHQ), ctag(l, kHK), ctag(l, kHV), ptag(l, kHAtt),
+                       ptag(l, kHPart), ctag(l, kHPart));
             KR_STAMP(l, 5);
         }
         // ---- o_proj owners: x1 = x + o_proj(attention)
@@ -1079,7 +1066,7 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             KR_STAMP(l, 14);
         }
     }
-    // ---- the last CTA to finish resets the counters for the next step
+    // ---- the last CTA to finish resets the step flags and advances the epoch
     // (every issued copy has been consumed: the stream and the consumers walk
     // the same unit sequence); the kernel's end makes x final for the lm_head
     __syncthreads();
@@ -1087,7 +1074,6 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
         __threadfence();
         const unsigned old = atomicAdd(a.misc + 1, 1u);
         if (old == gridDim.x - 1) {
-            for (int i = 0; i < a.nlayers * kRStride; ++i) a.counters[i] = 0u;
             a.misc[0] = 0u;
             a.misc[1] = 0u;
             a.misc[2] += 1u;  // the next launch's tags differ from every word written here
@@ -1153,7 +1139,7 @@ __global__ void nf4_retile16_kernel(const Retile16Args r) {
 struct RowGeom {
     int tiles[4], nbpt[4], ctas[4];
     int xs_bytes, work_bytes, bias_rows, ring_slots, smem;
-    int64_t off_misc, off_qw, off_kw, off_vw, off_aw, off_x1w, off_hw, off_xw, off_apart, total;
+    int64_t off_misc, off_qw, off_kw, off_vw, off_aw, off_x1w, off_hw, off_xw, off_pw, total;
 };
 constexpr int kRStaticSmemBudget = 3072;
 
@@ -1181,7 +1167,7 @@ RowGeom row_geom(const PersistDims& d, int sms) {
     g.smem = kRLutBytes + kRW * g.ring_slots * kSlotBytes + g.work_bytes + tail;
     auto up = [](int64_t v) { return (v + 255) & ~static_cast<int64_t>(255); };
     const int gq = d.kv_heads > 0 ? d.q_heads / d.kv_heads : 1;
-    int64_t off = up(static_cast<int64_t>(d.layers) * kRStride * 4);
+    int64_t off = 0;
     g.off_misc = off;
     off = up(off + 64);
     g.off_qw = off;  // tagged words: 8 bytes per two values
@@ -1198,8 +1184,8 @@ RowGeom row_geom(const PersistDims& d, int sms) {
     off = up(off + static_cast<int64_t>(d.intermediate) * 4);
     g.off_xw = off;
     off = up(off + static_cast<int64_t>(d.hidden) * 4);
-    g.off_apart = off;
-    off = up(off + static_cast<int64_t>(d.kv_heads) * kAMaxSplits * gq * (d.head_dim + 4) * 4);
+    g.off_pw = off;
+    off = up(off + static_cast<int64_t>(d.kv_heads) * kAMaxSplits * gq * (d.head_dim + 2) * 8);
     g.total = off;
     return g;
 }
@@ -1243,10 +1229,10 @@ int64_t decode_rows_scratch_bytes(const PersistDims& d, int sms) { return row_ge
 const char* decode_rows_check(const PersistDims& d, int sms) {
     if (d.layers < 1 || d.hidden < 64 || d.hidden % 64 != 0 || d.head_dim != 128 || d.q_heads < 1 || d.kv_heads < 1 ||
         d.q_heads % d.kv_heads != 0 || d.q_heads / d.kv_heads > 8 || d.intermediate % 64 != 0 ||
-        d.hidden > 8 * kRT * kNormPer || d.kv_capacity < 1 || d.kv_heads > sms || d.kv_heads + kCTicket > kRStride ||
-        d.hidden > 16 * kRT || d.q_heads * d.head_dim > 16 * kRT || d.intermediate > 32 * kRT || d.layers >= 8192)
+        d.hidden > 8 * kRT * kNormPer || d.kv_capacity < 1 || d.kv_heads > sms ||
+        d.hidden > 16 * kRT || d.q_heads * d.head_dim > 16 * kRT || d.intermediate > 32 * kRT || d.layers >= 4096)
         return "row-split persistent decode requires hidden % 64 == 0 (<= 8192), head_dim 128, q_heads/kv_heads <= 8, "
-               "q_heads * head_dim <= 8192, kv_heads <= 11, intermediate % 64 == 0 (<= 16384), layers < 8192";
+               "q_heads * head_dim <= 8192, kv_heads <= SM count, intermediate % 64 == 0 (<= 16384), layers < 4096";
     const RowGeom g = row_geom(d, sms);
     if (g.smem > 232448 - kRStaticSmemBudget) return "row-split persistent decode: shapes need more shared memory than one SM has";
     for (int i = 0; i < 4; ++i) {
@@ -1280,7 +1266,6 @@ cudaError_t decode_layers_rows(const PersistLaunch& p, cudaStream_t stream) {
     a.rope_cos = p.rope_cos;
     a.rope_sin = p.rope_sin;
     char* s = static_cast<char*>(p.scratch);
-    a.counters = reinterpret_cast<unsigned*>(s);
     a.misc = reinterpret_cast<unsigned*>(s + g.off_misc);
     a.qw = reinterpret_cast<uint64_t*>(s + g.off_qw);
     a.kw = reinterpret_cast<uint64_t*>(s + g.off_kw);
@@ -1289,7 +1274,7 @@ cudaError_t decode_layers_rows(const PersistLaunch& p, cudaStream_t stream) {
     a.x1w = reinterpret_cast<uint64_t*>(s + g.off_x1w);
     a.hw = reinterpret_cast<uint64_t*>(s + g.off_hw);
     a.xw = reinterpret_cast<uint64_t*>(s + g.off_xw);
-    a.apart = reinterpret_cast<float*>(s + g.off_apart);
+    a.pw = reinterpret_cast<uint64_t*>(s + g.off_pw);
     a.err = p.err;
     a.ring_slots = g.ring_slots;
     for (int i = 0; i < 4; ++i) {
