@@ -323,8 +323,8 @@ def direct_decode_profile(torch, weights, device: str, local: int, lengths=(512,
 
 
 def persistent_kernel_roofline(torch, bridge, plan, stream, pos: int) -> dict:
-    """Average duration of decode_layers_kernel (all 36 layers of one step in
-    one cooperative launch), launched directly on the decode stream at the
+    """Average duration of decode_rows_kernel (the row-split persistent kernel:
+    all 36 layers of one step in one cooperative launch), launched directly on the decode stream at the
     state the e2e loop left (position ``pos``), timed with CUDA events on that
     stream.  Algorithmic bytes: every layer's NF4 codes + absmax, norms and
     biases, and the K/V rows attention reads (kv_len = pos + 1)."""
@@ -354,9 +354,9 @@ def persistent_kernel_roofline(torch, bridge, plan, stream, pos: int) -> dict:
     algo = wb["nf4_absmax"] + (wb["norms_bias"] - cfg.hidden * 2) + kv + 2 * cfg.hidden * 2
     peak, src = _peaks()
     achieved = algo / (us * 1e-6) / 1e9
-    traffic = _profiled_traffic("decode_layers_persistent_qwen25_3b.md")
+    traffic = _profiled_traffic("decode_rows_persistent_qwen25_3b.md")
     return {
-        "kernel": "decode_layers_kernel (all 36 layers of one decode step, persistent cooperative launch)",
+        "kernel": "decode_rows_kernel (all 36 layers of one decode step, row-split persistent cooperative launch)",
         "bound": "hbm",
         "achieved": round(achieved, 1),
         "peak": peak,
@@ -367,7 +367,7 @@ def persistent_kernel_roofline(torch, bridge, plan, stream, pos: int) -> dict:
         "us_per_launch": round(us, 3),
         "kv_len": kv_len,
         "traffic": traffic,
-        "traffic_source": "profiles/decode_layers_persistent_qwen25_3b.md (ncu dram__bytes_read.sum + "
+        "traffic_source": "profiles/decode_rows_persistent_qwen25_3b.md (ncu dram__bytes_read.sum + "
                           "dram__bytes_write.sum of a 4-layer launch at kv 512, scaled x9 to 36 layers)",
     }
 

@@ -219,30 +219,40 @@ __device__ __forceinline__ uint64_t ld_tagged(const uint64_t* p) {
     asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p));
     return v;
 }
-// Every thread polls words i = tid + k * kRT (k < KMAX, i < n) at src(i)
-// until each carries tag(i), hands each payload to sink(i, payload), then the
-// CTA synchronises.  All of a thread's outstanding words are read in one
-// round; a poll that runs out raises the abort flag and error bit 4, as rwait.
-template <int KMAX, class Src, class Tag, class Sink>
-__device__ void rpoll(const RowArgs& a, int n, Src src, Tag tag, Sink sink) {
+// Every thread polls words i = tid + k * kRT (k < KMAX, i < n) until each
+// carries its tag, hands each payload to sink(slot, payload), then the CTA
+// synchronises.  locate(i, tag, slot) gives word i's address, expected tag
+// and sink slot (computed once per word).  All of a thread's outstanding
+// words are read in one round; a poll that runs out raises the abort flag and
+// error bit 4 of the error word.
+template <int KMAX, class Locate, class Sink>
+__device__ void rpoll(const RowArgs& a, int n, Locate locate, Sink sink) {
     const int tid = threadIdx.x;
+    const uint64_t* src[KMAX];
+    uint32_t tag[KMAX];
+    int slot[KMAX];
     uint32_t pending = 0u;
 #pragma unroll
-    for (int k = 0; k < KMAX; ++k)
-        if (tid + k * kRT < n) pending |= 1u << k;
+    for (int k = 0; k < KMAX; ++k) {
+        src[k] = nullptr;
+        tag[k] = 0u;
+        slot[k] = 0;
+        if (tid + k * kRT < n) {
+            src[k] = locate(tid + k * kRT, tag[k], slot[k]);
+            pending |= 1u << k;
+        }
+    }
     uint32_t rounds = 0;
     while (pending != 0u) {
         uint64_t v[KMAX];
 #pragma unroll
-        for (int k = 0; k < KMAX; ++k) v[k] = (pending >> k & 1u) != 0u ? ld_tagged(src(tid + k * kRT)) : 0ull;
+        for (int k = 0; k < KMAX; ++k) v[k] = (pending >> k & 1u) != 0u ? ld_tagged(src[k]) : 0ull;
 #pragma unroll
-        for (int k = 0; k < KMAX; ++k) {
-            const int i = tid + k * kRT;
-            if ((pending >> k & 1u) != 0u && static_cast<uint32_t>(v[k] >> 32) == tag(i)) {
-                sink(i, static_cast<uint32_t>(v[k]));
+        for (int k = 0; k < KMAX; ++k)
+            if ((pending >> k & 1u) != 0u && static_cast<uint32_t>(v[k] >> 32) == tag[k]) {
+                sink(slot[k], static_cast<uint32_t>(v[k]));
                 pending &= ~(1u << k);
             }
-        }
         if (pending != 0u && (++rounds & 31u) == 0u) {
             if (ld_relaxed_r(a.misc) != 0u) break;
             if (rounds > a.spin_limit) {
@@ -253,6 +263,18 @@ __device__ void rpoll(const RowArgs& a, int n, Src src, Tag tag, Sink sink) {
         }
     }
     __syncthreads();
+}
+// The common form: words base[0 .. n) with one tag, payloads to dst[i] (32-bit shared words).
+template <int KMAX>
+__device__ __forceinline__ void rpoll_vec(const RowArgs& a, const uint64_t* base, int n, uint32_t tg, uint32_t* dst) {
+    rpoll<KMAX>(
+        a, n,
+        [&](int i, uint32_t& t, int& sl) {
+            t = tg;
+            sl = i;
+            return base + i;
+        },
+        [&](int sl, uint32_t p) { dst[sl] = p; });
 }
 // Pairs of consecutive rows r, r + 1 sit in lanes r, r + 1 of an 8-lane group
 // of the GEMV epilogue (`lanes`: the warp's lanes in that epilogue call): the
@@ -433,15 +455,17 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
             lo += part[(tl * kRW + w) * 16 + r];
             hi += part[(tl * kRW + w) * 16 + 8 + r];
         }
+        if (idx == 0) KR_STAMP(layer, 37 + 2 * OP);
         epi(t0 + tl, r, lo, hi, lanes);
     }
+    KR_STAMP(layer, 38 + 2 * OP);
     __syncthreads();  // the epilogues' reads of shared memory (xres, part) before its next writers
 }
 
 // ------------------------------------------------------------------ staging
 // xs = f16(RMSNorm_HF(x) * w): x_norm = bf16(w * bf16(x * rsqrt(mean(x^2) + eps)));
 // w was loaded into registers before the dependency wait.
-constexpr int kNormPer = 4;  // hidden <= 8 * 512 * 4
+constexpr int kNormPer = 2;  // hidden <= 8 * 512 * 2
 __device__ __forceinline__ void rnorm_prefetch(const RowArgs& a, const uint16_t* w, uint4* wv) {
 #pragma unroll
     for (int i = 0; i < kNormPer; ++i) {
@@ -599,15 +623,23 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
     const int hp = hd / 2, nq = gq * hp;
     const bool has_pos = pos >= tok0 && pos < tok1;
     for (int i = nq + tid; i < 8 * hp; i += kRT) reinterpret_cast<uint32_t*>(sm.qb + (i / hp) * kKRow)[i % hp] = 0u;
+    uint32_t* qb32 = reinterpret_cast<uint32_t*>(sm.qb);
+    uint32_t* kv32 = reinterpret_cast<uint32_t*>(sm.kvpos);
     rpoll<2>(
         a, nq + (has_pos ? 2 * hp : 0),
-        [&](int i) -> const uint64_t* {
-            return i < nq ? a.qw + hk * nq + i : i < nq + hp ? a.kw + hk * hp + (i - nq) : a.vw + hk * hp + (i - nq - hp);
+        [&](int i, uint32_t& tg, int& sl) -> const uint64_t* {
+            if (i < nq) {  // q row i / 64 of the group, padded shared rows
+                tg = tq;
+                sl = (i >> 6) * (kKRow / 2) + (i & 63);
+                return a.qw + hk * nq + i;
+            }
+            tg = i < nq + hp ? tk : tv;
+            sl = -1 - (i - nq);  // k then v words of this step's row
+            return i < nq + hp ? a.kw + hk * hp + (i - nq) : a.vw + hk * hp + (i - nq - hp);
         },
-        [&](int i) { return i < nq ? tq : i < nq + hp ? tk : tv; },
-        [&](int i, uint32_t p) {
-            if (i < nq) reinterpret_cast<uint32_t*>(sm.qb + (i / hp) * kKRow)[i % hp] = p;
-            else reinterpret_cast<uint32_t*>(sm.kvpos)[i - nq] = p;
+        [&](int sl, uint32_t p) {
+            if (sl >= 0) qb32[sl] = p;
+            else kv32[-1 - sl] = p;
         });
     ratt_pos_row(tok0, min(kATile, tok1 - tok0), pos, sm);  // the rest of the first tile was fetched at layer start
     if (tid < 8) {
@@ -748,15 +780,15 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
     __syncthreads();  // every thread is past its reads of ss (P.V) before the sink writes it
     rpoll<4>(
         a, ap.ns * gq * nrec,
-        [&](int i) -> const uint64_t* {
+        [&](int i, uint32_t& tg, int& sl) -> const uint64_t* {
             const int sp = i / (gq * nrec), rem = i - sp * gq * nrec, hq = rem / nrec, j = rem - hq * nrec;
+            tg = tpart_c;
+            sl = j < 2 ? -1 - ((hq * kAMaxSplits + sp) * 2 + j) : hq * per + sp * nd + (j - 2);
             return a.pw + ((static_cast<size_t>(hk) * kAMaxSplits + sp) * gq + hq) * rec + (j < 2 ? j : d0 + j);
         },
-        [&](int) { return tpart_c; },
-        [&](int i, uint32_t p) {
-            const int sp = i / (gq * nrec), rem = i - sp * gq * nrec, hq = rem / nrec, j = rem - hq * nrec;
-            if (j < 2) mls[(hq * kAMaxSplits + sp) * 2 + j] = __uint_as_float(p);
-            else sm.mb[hq * per + sp * nd + (j - 2)] = __uint_as_float(p);
+        [&](int sl, uint32_t p) {
+            if (sl < 0) mls[-1 - sl] = __uint_as_float(p);
+            else sm.mb[sl] = __uint_as_float(p);
         });
     KR_STAMP(layer, 31);
     if (warp < gq) {
@@ -895,10 +927,7 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             rload_bf16(xres, a.x, a.hidden);
             __syncthreads();
         } else {  // the previous layer's x2
-            const uint32_t tg = ctag(l, kHX);
-            rpoll<8>(
-                a, a.hidden / 2, [&](int i) { return a.xw + i; }, [&](int) { return tg; },
-                [&](int i, uint32_t p) { reinterpret_cast<uint32_t*>(xres)[i] = p; });
+            rpoll_vec<8>(a, a.xw, a.hidden / 2, ctag(l, kHX), reinterpret_cast<uint32_t*>(xres));
         }
         // (every thread is now past the previous layer's reads of the K/V tile rows)
         KR_STAMP(l, 1);
@@ -911,6 +940,10 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             ratt_fetch(kc, vc, tok0, min(kATile, kv_len - tok0), pos_c, att_sm);
         }
         rstage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn : nullptr);
+#ifdef KC_ROWS_NORM_TWICE
+        KR_STAMP(l, 45);
+        rstage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn : nullptr);
+#endif
         KR_STAMP(l, 2);
         {
             uint16_t* kcl = reinterpret_cast<uint16_t*>(L[kTKCache]);
@@ -985,12 +1018,7 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
         rnorm_prefetch(a, reinterpret_cast<const uint16_t*>(L[kTPostNorm]), wv);
         if (own_o) {
             KR_STAMP(l, 6);
-            {
-                const uint32_t tg = ctag(l, kHAtt);
-                rpoll<8>(
-                    a, a.qh * hd / 2, [&](int i) { return a.aw + i; }, [&](int) { return tg; },
-                    [&](int i, uint32_t p) { reinterpret_cast<uint32_t*>(xs)[i] = p; });
-            }
+            rpoll_vec<8>(a, a.aw, a.qh * hd / 2, ctag(l, kHAtt), reinterpret_cast<uint32_t*>(xs));
             KR_STAMP(l, 7);
             const uint32_t tx1 = ptag(l, kHX1);
             rgemv<kOO>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi, unsigned lanes) {
@@ -1010,12 +1038,7 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             KR_STAMP(l, 8);
         }
         // ---- x1 ready -> RMSNorm -> gate/up owners (SwiGLU)
-        {
-            const uint32_t tg = ctag(l, kHX1);
-            rpoll<8>(
-                a, a.hidden / 2, [&](int i) { return a.x1w + i; }, [&](int) { return tg; },
-                [&](int i, uint32_t p) { reinterpret_cast<uint32_t*>(xres)[i] = p; });
-        }
+        rpoll_vec<8>(a, a.x1w, a.hidden / 2, ctag(l, kHX1), reinterpret_cast<uint32_t*>(xres));
         KR_STAMP(l, 9);
         rstage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn2 : nullptr);
         KR_STAMP(l, 10);
@@ -1039,12 +1062,7 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
         // ---- down owners: x2 = x1 + down(h), the next layer's input
         if (own_dn) {
             KR_STAMP(l, 12);
-            {
-                const uint32_t tg = ctag(l, kHH);
-                rpoll<16>(
-                    a, a.inter / 2, [&](int i) { return a.hw + i; }, [&](int) { return tg; },
-                    [&](int i, uint32_t p) { reinterpret_cast<uint32_t*>(xs)[i] = p; });
-            }
+            rpoll_vec<16>(a, a.hw, a.inter / 2, ctag(l, kHH), reinterpret_cast<uint32_t*>(xs));
             KR_STAMP(l, 13);
             const uint32_t tx = ptag(l + 1, kHX);
             const bool last = l == a.nlayers - 1;
