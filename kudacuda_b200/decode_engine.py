@@ -620,6 +620,26 @@ class StaticDecodePlan:
     def captured(self) -> bool:
         return self.graph_plan.captured
 
+    def release_source_weights(self) -> int:
+        """Free the bitsandbytes copies of the decoder layers' NF4 tensors of a
+        persistent plan, whose step streams only its own re-tiled copy; until
+        then the plan holds the layer weights twice.  Build every other
+        consumer of the source weights first (a BatchedPrefill re-tiles its own
+        copy at construction): afterwards the tensors are empty and any later
+        use of them (the per-op path, a new prefill) fails the NF4 shape
+        checks.  Returns the bytes released."""
+
+        if self.persistent is None:
+            raise NativeCudaError("release_source_weights: only a persistent plan streams its own weight copy")
+        freed = 0
+        for L in self.weights.layers:
+            for name in ("q", "k", "v", "o", "gate", "up", "down"):
+                lin = getattr(L, name)
+                freed += lin.packed.numel() * lin.packed.element_size() + lin.absmax.numel() * lin.absmax.element_size()
+                lin.packed = lin.packed.new_empty((0,))
+                lin.absmax = lin.absmax.new_empty((0,))
+        return int(freed)
+
     def make_graph_key(self) -> DecodeGraphKey:
         """The static contract of the captured step: shapes, bucket and every
         device pointer the graph bakes in (buffers, caches, weights)."""
@@ -632,8 +652,9 @@ class StaticDecodePlan:
             ptrs += self.persistent.pointers()
         for L in w.layers:
             ptrs += [L.in_norm.data_ptr(), L.post_norm.data_ptr()]
-            for lin in (L.q, L.k, L.v, L.o, L.gate, L.up, L.down):
-                ptrs += [lin.packed.data_ptr(), lin.absmax.data_ptr()]
+            if self.persistent is None:  # the persistent step reads only its re-tiled copy
+                for lin in (L.q, L.k, L.v, L.o, L.gate, L.up, L.down):
+                    ptrs += [lin.packed.data_ptr(), lin.absmax.data_ptr()]
             ptrs += [0 if t is None else t.data_ptr() for t in (L.q_bias, L.k_bias, L.v_bias)]
         d = c.head_dim
         return DecodeGraphKey(

@@ -211,6 +211,46 @@ def test_persistent_greedy_teacher_forced_top1(tiny_persistent):
     assert rate >= 0.75, f"teacher-forced top-1 agreement {rate:.2f}"
 
 
+def test_release_source_weights_keeps_the_step(tiny_persistent):
+    """After the bitsandbytes copies are freed the persistent step (which
+    streams its own re-tiled copy) gives the same tokens, and the memory
+    comes back."""
+
+    import torch
+
+    from kudacuda_b200.decode_engine import StaticDecodePlan, random_weights, tiny_config
+    from kudacuda_b200.kudacuda_sidecar import KudaCudaBridge, NativeCudaError
+
+    cfg, bridge0, w0, plan0, stream0 = tiny_persistent
+    bridge = KudaCudaBridge(device_id=0)
+    w = random_weights(bridge, tiny_config(layers=2, vocab=4096), seed=12, device="cuda:0")
+    with pytest.raises(NativeCudaError):  # a per-op plan streams the source weights themselves
+        StaticDecodePlan(bridge, w, kv_bucket=64, max_tokens=64, device="cuda:0").release_source_weights()
+    plan = StaticDecodePlan(bridge, w, kv_bucket=64, max_tokens=64, device="cuda:0", persistent=True)
+    stream = torch.cuda.Stream()
+    plan.capture(stream)
+
+    def tokens():
+        out = []
+        plan.reset_cache()
+        tok = 42
+        for pos in range(6):
+            tok = plan.step_host(tok, pos, stream)
+            out.append(tok)
+        return out
+
+    before = tokens()
+    torch.cuda.synchronize()
+    m0 = torch.cuda.memory_allocated()
+    freed = plan.release_source_weights()
+    torch.cuda.synchronize()
+    assert freed > 0 and torch.cuda.memory_allocated() <= m0 - freed // 2
+    assert tokens() == before
+    assert bridge.error_word(clear=True) == 0
+    bridge.reset_graph()
+    bridge.shutdown()
+
+
 def test_persistent_rejects_unsupported_shapes(tiny_persistent):
     from kudacuda_b200.kudacuda_sidecar import NativeCudaError
 
