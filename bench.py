@@ -134,13 +134,7 @@ def run_gpu(args) -> dict | None:
 
     rank, world, local = _dist_env()
     torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dist = _init_dist(world, local)
     device = f"cuda:{local}"
     cfg = QWEN25_3B
     bridge = KudaCudaBridge(device_id=local)
@@ -273,10 +267,18 @@ def run_gpu(args) -> dict | None:
             out["direct_decode_profile"] = direct_decode_profile(torch, weights, device, local)
         if not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline_sample(weights_to_host=(weights, plan), seconds=args.cpu_seconds)
+    bridge.reset_graph()
+    if not args.no_tp:  # every rank takes part in the tensor-parallel runs
+        del plan, weights
+        torch.cuda.empty_cache()
+        if dist is not None:
+            dist.barrier()
+        tp = tp_object(args, dist)
+        if out is not None:
+            out["tp"] = tp
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
-    bridge.reset_graph()
     return out
 
 
@@ -568,10 +570,23 @@ def run_reference(args) -> dict | None:
     }
 
 
-def run_tp(args) -> dict | None:
-    """Config 5: Llama-3-8B-architecture NF4 decode, tensor-parallel over the ranks."""
+def _init_dist(world: int, local: int):
+    """The NCCL process group of a multi-rank run (None at world 1)."""
 
+    if world == 1:
+        return None
     import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return dist
+
+
+def run_tp(args, dist_in=None) -> dict | None:
+    """Config 5: Llama-3-8B-architecture NF4 decode, tensor-parallel over the
+    ranks.  dist_in: an already initialised torch.distributed (left open)."""
 
     import torch
 
@@ -581,13 +596,8 @@ def run_tp(args) -> dict | None:
     rank, world, local = _dist_env()
     torch.cuda.set_device(local)
     device = f"cuda:{local}"
-    dist = None
-    group = None
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-        group = dist.group.WORLD
+    dist = dist_in if dist_in is not None else _init_dist(world, local)
+    group = dist.group.WORLD if dist is not None else None
     cfg = LLAMA3_8B
     if cfg.kv_heads % world or cfg.q_heads % world or cfg.intermediate % world or cfg.vocab % world:
         raise SystemExit(f"Llama-3-8B does not shard over {world} ranks")
@@ -680,11 +690,14 @@ def run_tp(args) -> dict | None:
         }
     if dist is not None:
         dist.barrier()
-        dist.destroy_process_group()
+        if dist_in is None:
+            dist.destroy_process_group()
+    bridge.reset_graph()
+    bridge.shutdown()
     return out
 
 
-def run_tp_batched(args) -> dict | None:
+def run_tp_batched(args, dist_in=None) -> dict | None:
     """Config 5 at batch B (BASELINE: batch 32): the Llama-3-8B-architecture
     NF4 model tensor-parallel over the ranks with the batched tensor-core
     path -- column-parallel q/k/v and gate/up, row-parallel o_proj and down
@@ -694,8 +707,6 @@ def run_tp_batched(args) -> dict | None:
     prompts); a step advances every sequence by one token; value = B * K /
     time (strong scaling: the same work at every world size)."""
 
-    import datetime
-
     import torch
 
     from kudacuda_b200.decode_engine import LLAMA3_8B, BatchedDecodePlan, random_weights
@@ -704,13 +715,8 @@ def run_tp_batched(args) -> dict | None:
     rank, world, local = _dist_env()
     torch.cuda.set_device(local)
     device = f"cuda:{local}"
-    dist = None
-    group = None
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-        group = dist.group.WORLD
+    dist = dist_in if dist_in is not None else _init_dist(world, local)
+    group = dist.group.WORLD if dist is not None else None
     cfg = LLAMA3_8B
     if cfg.kv_heads % world or cfg.q_heads % world or cfg.intermediate % world or cfg.vocab % world:
         raise SystemExit(f"Llama-3-8B does not shard over {world} ranks")
@@ -834,8 +840,88 @@ def run_tp_batched(args) -> dict | None:
         }
     if dist is not None:
         dist.barrier()
-        dist.destroy_process_group()
+        if dist_in is None:
+            dist.destroy_process_group()
+    bridge.shutdown()
     return out
+
+
+def allreduce_cost(torch, dist, device: str, numel: int, calls: int = 64, reps: int = 5) -> float | None:
+    """Device time (µs, max over ranks) of one NCCL allreduce of `numel` fp32,
+    averaged over `calls` back-to-back calls on the current stream; None at
+    world 1 (no collective)."""
+
+    if dist is None:
+        return None
+    buf = torch.zeros(numel, dtype=torch.float32, device=device)
+    for _ in range(8):
+        dist.all_reduce(buf)
+    torch.cuda.synchronize(device)
+    best = None
+    for _ in range(reps):
+        dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(calls):
+            dist.all_reduce(buf)
+        e.record()
+        e.synchronize()
+        us = s.elapsed_time(e) * 1e3 / calls
+        best = us if best is None else min(best, us)
+    t = torch.tensor([best], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def tp_object(args, dist) -> dict | None:
+    """The config-5 tensor-parallel run at this job's world size, attached to
+    the default bench line as "tp" so that the driver's 1..8 GPU scaling run
+    records config 5 at every N: the Llama-3-8B architecture at batch 1 and
+    batch 32 (short timed windows), ms per step, the allreduce share of a step
+    (64 fp32 allreduces per token, each timed alone on this group: an
+    estimate, since inside the graph nothing overlaps them) and whether all
+    ranks produced the same tokens."""
+
+    import copy
+
+    import torch
+
+    from kudacuda_b200.decode_engine import LLAMA3_8B
+
+    rank, world, local = _dist_env()
+    device = f"cuda:{local}"
+    a1 = copy.copy(args)
+    a1.steps, a1.warmup, a1.batch = 16, 3, 1
+    r1 = run_tp(a1, dist_in=dist)
+    torch.cuda.empty_cache()
+    a32 = copy.copy(args)
+    a32.steps, a32.warmup, a32.batch = 8, 3, 32
+    r32 = run_tp_batched(a32, dist_in=dist)
+    torch.cuda.empty_cache()
+    cfg = LLAMA3_8B
+    ar1 = allreduce_cost(torch, dist, device, cfg.hidden)
+    ar32 = allreduce_cost(torch, dist, device, cfg.hidden * 32)
+    if rank != 0:
+        return None
+    per_token = 2 * cfg.layers  # o_proj and down of every layer
+
+    def share(us, ms_step):
+        return None if us is None else round(per_token * us / 1e3 / ms_step, 4)
+
+    return {
+        "world": world,
+        "model": "Llama-3-8B architecture, NF4, random-init",
+        "batch1": {"tok_s": r1["value"], "ms_per_step": r1["ms_per_step"], "steps": a1.steps,
+                   "ranks_agree_on_tokens": r1["ranks_agree_on_tokens"], "device_error_word": r1["device_error_word"],
+                   "allreduce_us_each": None if ar1 is None else round(ar1, 2),
+                   "allreduce_share_est": share(ar1, r1["ms_per_step"])},
+        "batch32": {"tok_s": r32["value"], "ms_per_step": r32["ms_per_step"], "steps": a32.steps,
+                    "ranks_agree_on_tokens": r32["ranks_agree_on_tokens"],
+                    "device_error_word": r32["device_error_word"],
+                    "allreduce_us_each": None if ar32 is None else round(ar32, 2),
+                    "allreduce_share_est": share(ar32, r32["ms_per_step"])},
+        "scaling": "strong (the same model and batch at every world size)",
+    }
 
 
 def run_batched(args) -> dict | None:
@@ -1062,6 +1148,8 @@ def main(argv=None) -> int:
     p.add_argument("--impl", choices=["kudacuda_b200", "reference"], default="kudacuda_b200")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-tp", action="store_true",
+                   help="default workload: skip the config-5 tensor-parallel object (\"tp\") of the line")
     p.add_argument("--workload", choices=["qwen3b", "llama8b-tp", "qwen3b-batched"], default="qwen3b")
     p.add_argument("--batch", type=int, default=None,
                    help="sequences per step: --workload qwen3b-batched (default 64) or llama8b-tp (default 1)")
