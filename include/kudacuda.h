@@ -398,6 +398,39 @@ KUDACUDA_API int kudacuda_sm100_decode_layers_rows(void* handle, uint64_t layer_
                                                    uint64_t taps, int64_t taps_bytes, int64_t spin_limit,
                                                    int64_t stall_counter, uint64_t stream);
 
+/* Tensor-parallel row-split decode (no reference counterpart; the reference
+ * runs one GPU): rank `rank` of `world` (<= 8) runs decode_layers_rows over
+ * its shard -- column-parallel q/k/v (its kv_heads / world heads) and gate/up,
+ * row-parallel o_proj and down (K split on 64-element blocks) -- with q_heads,
+ * kv_heads and intermediate the per-rank values.  The owner CTA of each
+ * o_proj / down tile pushes its fp32 partial rows as tagged words straight
+ * into every rank's exchange buffer over NVLink (plain peer stores, no
+ * multicast), then polls its own buffer for the world partials of its rows,
+ * sums them in rank order and finishes the residual add: the allreduce is
+ * fused into the GEMV tile by tile, no collective library call.  tp_peers is
+ * a device array of `world` uint64 addresses: every rank's exchange buffer
+ * (tp_exchange_bytes(world, hidden) bytes, zeroed once, kept across steps)
+ * as mapped in this process (ipc_alloc on the owner, ipc_open on the
+ * others).  Every rank must launch the same steps in the same order; a peer
+ * that never arrives ends the wait with bit 4 of the error word. */
+KUDACUDA_API int kudacuda_sm100_decode_layers_rows_tp(void* handle, uint64_t layer_table, int64_t layers, uint64_t x,
+                                                      uint64_t state, uint64_t rope_cos, uint64_t rope_sin,
+                                                      int64_t max_pos, uint64_t scratch, int64_t scratch_bytes,
+                                                      int64_t hidden, int64_t q_heads, int64_t kv_heads,
+                                                      int64_t head_dim, int64_t intermediate, int64_t kv_capacity,
+                                                      float eps, float scale, int64_t world, int64_t rank,
+                                                      uint64_t tp_peers, uint64_t stream);
+KUDACUDA_API int64_t kudacuda_sm100_tp_exchange_bytes(int64_t world, int64_t hidden);
+/* CUDA IPC for the exchange buffers: ipc_alloc makes a zeroed device
+ * allocation of its own and writes its 64-byte IPC handle; ipc_open maps a
+ * peer's handle into this process; ipc_close unmaps (owned 0) or frees
+ * (owned 1). */
+KUDACUDA_API int kudacuda_sm100_ipc_alloc(void* handle, int64_t bytes, uint64_t* out_ptr, void* out_handle,
+                                          int64_t handle_bytes);
+KUDACUDA_API int kudacuda_sm100_ipc_open(void* handle, const void* ipc_handle, int64_t handle_bytes,
+                                         uint64_t* out_ptr);
+KUDACUDA_API int kudacuda_sm100_ipc_close(void* handle, uint64_t ptr, int owned);
+
 /* Batched decode: B independent sequences advance one token per step.  No
  * reference counterpart (the reference's projections and its GQA contract,
  * python/kudacuda_sidecar.py:145-153, are batch 1); the arithmetic is what

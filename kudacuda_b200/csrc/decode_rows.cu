@@ -96,14 +96,14 @@ enum RowOp { kOQkv = 0, kOO = 1, kOGu = 2, kODn = 3 };
 // 3 gate/up, 4 down, 5 the attention splits' partials)
 enum RowCtr { kCQkv = 0, kCAtt = 1, kCO = 2, kCGu = 3, kCDn = 4, kCTicket = 5 };
 // hops between ops, the low 4 bits of a tag (15: never written, the test hook's unreachable tag)
-enum RowHop { kHX = 0, kHQ = 1, kHK = 2, kHV = 3, kHAtt = 4, kHX1 = 5, kHH = 6, kHPart = 7 };
+enum RowHop { kHX = 0, kHQ = 1, kHK = 2, kHV = 3, kHAtt = 4, kHX1 = 5, kHH = 6, kHPart = 7, kHTpO = 8, kHTpD = 9 };
 __host__ __device__ constexpr int hop_counter(int hop) {  // the stall_counter index of a hop
-    return hop == kHX     ? kCDn
-           : hop <= kHV   ? kCQkv
-           : hop == kHAtt ? kCAtt
-           : hop == kHX1  ? kCO
-           : hop == kHH   ? kCGu
-                          : kCTicket;
+    return hop == kHX                      ? kCDn
+           : hop <= kHV                    ? kCQkv
+           : hop == kHAtt || hop == kHTpO  ? kCAtt
+           : hop == kHX1                   ? kCO
+           : hop == kHH || hop == kHTpD    ? kCGu
+                                           : kCTicket;
 }
 enum RowSlot { kTUnits0 = 0, kTInNorm = 4, kTPostNorm, kTQBias, kTKBias, kTVBias, kTKCache, kTVCache, kTSlots = 16 };
 
@@ -128,6 +128,11 @@ struct RowArgs {
     uint64_t* x1w;  // [hidden / 2] x + o_proj (bf16)
     uint64_t* hw;   // [inter / 2] SwiGLU output (f16 of the bf16 value)
     uint64_t* xw;   // [hidden / 2] x2, the next layer's input (bf16)
+    // tensor parallelism: rank `rank` of `world`; peers[p] = rank p's exchange
+    // buffer (this process's mapping of its peer memory): o_proj partials
+    // [world][hidden] then down partials [world][hidden], tagged f32 words
+    int world, rank;
+    const uint64_t* peers;
     uint64_t* pw;   // [kvh][kAMaxSplits][gq][2 + hd] attention partials: max, sum, accumulator (f32 bits)
     int* err;
     int ring_slots;
@@ -198,11 +203,6 @@ __device__ __forceinline__ float2 unit_dot_r(const uint8_t* lut, uint32_t lane4,
             lut_pair_r(lut, w.y, 0x5534u, lane4), lut_pair_r(lut, w.w, 0x5534u, lane4), x1.z, x1.w);
     return make_float2(c[0], c[2]);
 }
-__device__ __forceinline__ unsigned ld_acquire_r(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 __device__ __forceinline__ unsigned ld_relaxed_r(const unsigned* p) {
     unsigned v;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -219,13 +219,23 @@ __device__ __forceinline__ uint64_t ld_tagged(const uint64_t* p) {
     asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p));
     return v;
 }
+// the same across GPUs: a peer's store into this GPU's memory over NVLink
+__device__ __forceinline__ void st_tagged_sys(uint64_t* p, uint32_t tag, uint32_t payload) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"((static_cast<uint64_t>(tag) << 32) | payload)
+                 : "memory");
+}
+__device__ __forceinline__ uint64_t ld_tagged_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p));
+    return v;
+}
 // Every thread polls words i = tid + k * kRT (k < KMAX, i < n) until each
 // carries its tag, hands each payload to sink(slot, payload), then the CTA
 // synchronises.  locate(i, tag, slot) gives word i's address, expected tag
 // and sink slot (computed once per word).  All of a thread's outstanding
 // words are read in one round; a poll that runs out raises the abort flag and
 // error bit 4 of the error word.
-template <int KMAX, class Locate, class Sink>
+template <int KMAX, bool SYS = false, class Locate, class Sink>
 __device__ void rpoll(const RowArgs& a, int n, Locate locate, Sink sink) {
     const int tid = threadIdx.x;
     const uint64_t* src[KMAX];
@@ -246,7 +256,8 @@ __device__ void rpoll(const RowArgs& a, int n, Locate locate, Sink sink) {
     while (pending != 0u) {
         uint64_t v[KMAX];
 #pragma unroll
-        for (int k = 0; k < KMAX; ++k) v[k] = (pending >> k & 1u) != 0u ? ld_tagged(src[k]) : 0ull;
+        for (int k = 0; k < KMAX; ++k)
+            v[k] = (pending >> k & 1u) != 0u ? (SYS ? ld_tagged_sys(src[k]) : ld_tagged(src[k])) : 0ull;
 #pragma unroll
         for (int k = 0; k < KMAX; ++k)
             if ((pending >> k & 1u) != 0u && static_cast<uint32_t>(v[k] >> 32) == tag[k]) {
@@ -275,6 +286,42 @@ __device__ __forceinline__ void rpoll_vec(const RowArgs& a, const uint64_t* base
             return base + i;
         },
         [&](int sl, uint32_t p) { dst[sl] = p; });
+}
+// Tensor-parallel row-parallel op (o_proj or down): every rank pushed its fp32
+// partial of this CTA's tiles into every rank's exchange buffer `ex`
+// ([world][hidden] tagged words; the tile owners are the same CTA index on
+// every rank).  Poll the world partials of each owned row from this GPU's
+// buffer, sum them in rank order (every rank gets the same value), and hand
+// each row to fin(row, sum, lanes) with consecutive rows in consecutive lanes.
+template <class Fin>
+__device__ void rtp_finish(const RowArgs& a, const int* rr, const uint64_t* ex, uint32_t tag, float* buf, Fin fin) {
+    const int t0 = rr[0], nrows = 16 * (rr[1] - rr[0]), world = a.world;
+    const int lane = threadIdx.x & 31;
+    rpoll<4, true>(
+        a, nrows * world,
+        [&](int i, uint32_t& tg, int& sl) {
+            const int rl = i / world, src = i - rl * world;
+            tg = tag;
+            sl = i;
+            return ex + static_cast<int64_t>(src) * a.hidden + 16 * t0 + rl;
+        },
+        [&](int sl, uint32_t p) { buf[sl] = __uint_as_float(p); });
+    for (int idx = threadIdx.x; idx < nrows; idx += kRT) {
+        const int left = nrows - (idx - lane);
+        const unsigned lanes = left >= 32 ? 0xffffffffu : (1u << left) - 1u;
+        float sum = 0.F;
+        for (int src = 0; src < world; ++src) sum += buf[idx * world + src];
+        fin(16 * t0 + idx, sum, lanes);
+    }
+    __syncthreads();
+}
+// This rank's partial of rows row and row + 8 into every rank's exchange buffer.
+__device__ __forceinline__ void rtp_push(const RowArgs& a, int part_off, int row, float lo, float hi, uint32_t tag) {
+    for (int p = 0; p < a.world; ++p) {
+        uint64_t* dst = reinterpret_cast<uint64_t*>(a.peers[p]) + part_off + static_cast<int64_t>(a.rank) * a.hidden;
+        st_tagged_sys(dst + row, tag, __float_as_uint(lo));
+        st_tagged_sys(dst + row + 8, tag, __float_as_uint(hi));
+    }
 }
 // Pairs of consecutive rows r, r + 1 sit in lanes r, r + 1 of an 8-lane group
 // of the GEMV epilogue (`lanes`: the warp's lanes in that epilogue call): the
@@ -1021,7 +1068,13 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             rpoll_vec<8>(a, a.aw, a.qh * hd / 2, ctag(l, kHAtt), reinterpret_cast<uint32_t*>(xs));
             KR_STAMP(l, 7);
             const uint32_t tx1 = ptag(l, kHX1);
+            const bool tp = a.world > 1;
+            const uint32_t tpo = ptag(l, kHTpO);
             rgemv<kOO>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi, unsigned lanes) {
+                if (tp) {  // this rank's partial: the sum over ranks comes after every push
+                    rtp_push(a, 0, 16 * T + r, ylo, yhi, tpo);
+                    return;
+                }
                 uint16_t x1[2];
 #pragma unroll
                 for (int k = 0; k < 2; ++k) {
@@ -1035,6 +1088,15 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
                     st_tagged(a.x1w + (16 * T + r + 8) / 2, tx1, p1);
                 }
             });
+            if (tp)
+                rtp_finish(a, rng + kOO * kRngStride, reinterpret_cast<const uint64_t*>(a.peers[a.rank]),
+                           ctag(l, kHTpO), part, [&](int row, float sum, unsigned lanes) {
+                               const uint16_t x1 =
+                                   f32_to_bf16_bits(bf16_bits_to_f32(xres[row]) + round_bf16(sum));
+                               if (tap != nullptr) tap[to.x1 + row] = x1;
+                               const uint32_t p = pair_up(x1, lanes);
+                               if ((row & 1) == 0) st_tagged(a.x1w + row / 2, tx1, p);
+                           });
             KR_STAMP(l, 8);
         }
         // ---- x1 ready -> RMSNorm -> gate/up owners (SwiGLU)
@@ -1066,7 +1128,13 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             KR_STAMP(l, 13);
             const uint32_t tx = ptag(l + 1, kHX);
             const bool last = l == a.nlayers - 1;
+            const bool tp = a.world > 1;
+            const uint32_t tpd = ptag(l, kHTpD);
             rgemv<kODn>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi, unsigned lanes) {
+                if (tp) {
+                    rtp_push(a, a.world * a.hidden, 16 * T + r, ylo, yhi, tpd);
+                    return;
+                }
                 uint16_t x2[2];
 #pragma unroll
                 for (int k = 0; k < 2; ++k) {
@@ -1081,6 +1149,17 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
                     st_tagged(a.xw + (16 * T + r + 8) / 2, tx, p1);
                 }
             });
+            if (tp)
+                rtp_finish(a, rng + kODn * kRngStride,
+                           reinterpret_cast<const uint64_t*>(a.peers[a.rank]) + static_cast<int64_t>(a.world) * a.hidden,
+                           ctag(l, kHTpD), part, [&](int row, float sum, unsigned lanes) {
+                               const uint16_t x2 =
+                                   f32_to_bf16_bits(bf16_bits_to_f32(xres[row]) + round_bf16(sum));
+                               if (last) a.x[row] = x2;
+                               if (tap != nullptr) tap[to.x2 + row] = x2;
+                               const uint32_t p = pair_up(x2, lanes);
+                               if ((row & 1) == 0 && !last) st_tagged(a.xw + row / 2, tx, p);
+                           });
             KR_STAMP(l, 14);
         }
     }
@@ -1307,6 +1386,9 @@ cudaError_t decode_layers_rows(const PersistLaunch& p, cudaStream_t stream) {
     a.tap_stride = rtaps(p.dims.hidden, p.dims.q_heads, p.dims.kv_heads, p.dims.head_dim, p.dims.intermediate).stride;
     a.spin_limit = p.spin_limit > 0 ? p.spin_limit : kRSpinLimit;
     a.stall_counter = p.stall_counter;
+    a.world = p.world;
+    a.rank = p.rank;
+    a.peers = p.tp_peers;
     cudaError_t st = cudaFuncSetAttribute(decode_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, g.smem);
     if (st != cudaSuccess) return st;
     cudaLaunchConfig_t cfg = {};

@@ -190,6 +190,10 @@ struct PersistLaunch {
     uint16_t* taps = nullptr;
     uint32_t spin_limit = 0;
     int stall_counter = -1;
+    // tensor parallelism (row-split kernel only): this rank of `world`, and
+    // the device array of every rank's exchange buffer address (peer memory)
+    int world = 1, rank = 0;
+    const uint64_t* tp_peers = nullptr;
 };
 // elements of one layer's tap record of the persistent kernel
 int64_t decode_persistent_tap_stride(const PersistDims& d);

@@ -1126,14 +1126,19 @@ int64_t kudacuda_sm100_decode_rows_scratch_bytes(void* raw, int64_t layers, int6
     return kc::decode_rows_scratch_bytes(d, sms);
 }
 
-int kudacuda_sm100_decode_layers_rows(void* raw, uint64_t layer_table, int64_t layers, uint64_t x, uint64_t state,
-                                      uint64_t rope_cos, uint64_t rope_sin, int64_t max_pos, uint64_t scratch,
-                                      int64_t scratch_bytes, int64_t hidden, int64_t q_heads, int64_t kv_heads,
-                                      int64_t head_dim, int64_t intermediate, int64_t kv_capacity, float eps,
-                                      float scale, uint64_t taps, int64_t taps_bytes, int64_t spin_limit,
-                                      int64_t stall_counter, uint64_t stream) {
+namespace {
+int decode_rows_common(void* raw, uint64_t layer_table, int64_t layers, uint64_t x, uint64_t state, uint64_t rope_cos,
+                       uint64_t rope_sin, int64_t max_pos, uint64_t scratch, int64_t scratch_bytes, int64_t hidden,
+                       int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t intermediate,
+                       int64_t kv_capacity, float eps, float scale, uint64_t taps, int64_t taps_bytes,
+                       int64_t spin_limit, int64_t stall_counter, int64_t world, int64_t rank, uint64_t tp_peers,
+                       uint64_t stream) {
     Handle* h = as_handle(raw);
-    if (!ready(h, "kudacuda_sm100_decode_layers_rows")) return 1;
+    if (!ready(h, world == 1 ? "kudacuda_sm100_decode_layers_rows" : "kudacuda_sm100_decode_layers_rows_tp")) return 1;
+    if (world < 1 || world > 8 || rank < 0 || rank >= world || (world > 1 && tp_peers == 0)) {
+        h->set_error("sm100_decode_layers_rows_tp requires 1 <= world <= 8, 0 <= rank < world and the peer table");
+        return 1;
+    }
     kc::PersistDims d;
     if (!persist_dims(layers, hidden, q_heads, kv_heads, head_dim, intermediate, kv_capacity, d) || max_pos < 1 ||
         max_pos > (1 << 24) || !(eps > 0.0F) || !(scale > 0.0F)) {
@@ -1177,7 +1182,99 @@ int kudacuda_sm100_decode_layers_rows(void* raw, uint64_t layer_table, int64_t l
     p.taps = P<uint16_t>(taps);
     p.spin_limit = static_cast<uint32_t>(spin_limit);
     p.stall_counter = static_cast<int>(stall_counter);
+    p.world = static_cast<int>(world);
+    p.rank = static_cast<int>(rank);
+    p.tp_peers = P<const uint64_t>(tp_peers);
     return finish(h, "decode_rows_kernel", kc::decode_layers_rows(p, S(stream)));
+}
+}  // namespace
+
+int kudacuda_sm100_decode_layers_rows(void* raw, uint64_t layer_table, int64_t layers, uint64_t x, uint64_t state,
+                                      uint64_t rope_cos, uint64_t rope_sin, int64_t max_pos, uint64_t scratch,
+                                      int64_t scratch_bytes, int64_t hidden, int64_t q_heads, int64_t kv_heads,
+                                      int64_t head_dim, int64_t intermediate, int64_t kv_capacity, float eps,
+                                      float scale, uint64_t taps, int64_t taps_bytes, int64_t spin_limit,
+                                      int64_t stall_counter, uint64_t stream) {
+    return decode_rows_common(raw, layer_table, layers, x, state, rope_cos, rope_sin, max_pos, scratch, scratch_bytes,
+                              hidden, q_heads, kv_heads, head_dim, intermediate, kv_capacity, eps, scale, taps,
+                              taps_bytes, spin_limit, stall_counter, 1, 0, 0, stream);
+}
+
+int kudacuda_sm100_decode_layers_rows_tp(void* raw, uint64_t layer_table, int64_t layers, uint64_t x, uint64_t state,
+                                         uint64_t rope_cos, uint64_t rope_sin, int64_t max_pos, uint64_t scratch,
+                                         int64_t scratch_bytes, int64_t hidden, int64_t q_heads, int64_t kv_heads,
+                                         int64_t head_dim, int64_t intermediate, int64_t kv_capacity, float eps,
+                                         float scale, int64_t world, int64_t rank, uint64_t tp_peers,
+                                         uint64_t stream) {
+    return decode_rows_common(raw, layer_table, layers, x, state, rope_cos, rope_sin, max_pos, scratch, scratch_bytes,
+                              hidden, q_heads, kv_heads, head_dim, intermediate, kv_capacity, eps, scale, 0, 0, 0, -1,
+                              world, rank, tp_peers, stream);
+}
+
+int64_t kudacuda_sm100_tp_exchange_bytes(int64_t world, int64_t hidden) {
+    if (world < 1 || world > 8 || hidden < 16 || hidden > (1 << 16)) return -1;
+    return 2 * world * hidden * 8;
+}
+
+// Exchange buffers live in their own cudaMalloc allocations so that a CUDA IPC
+// handle maps exactly the buffer into the peer processes.
+int kudacuda_sm100_ipc_alloc(void* raw, int64_t bytes, uint64_t* out_ptr, void* out_handle, int64_t handle_bytes) {
+    Handle* h = as_handle(raw);
+    if (h == nullptr || out_ptr == nullptr || out_handle == nullptr || bytes < 1 || bytes > (int64_t{1} << 32) ||
+        handle_bytes < static_cast<int64_t>(sizeof(cudaIpcMemHandle_t))) {
+        if (h != nullptr) h->set_error("sm100_ipc_alloc requires 1 <= bytes <= 4 GiB and a 64-byte handle buffer");
+        return 1;
+    }
+    void* p = nullptr;
+    cudaError_t st = cudaSetDevice(h->device_id);
+    if (st == cudaSuccess) st = cudaMalloc(&p, static_cast<size_t>(bytes));
+    if (st == cudaSuccess) st = cudaMemset(p, 0, static_cast<size_t>(bytes));
+    cudaIpcMemHandle_t ih;
+    if (st == cudaSuccess) st = cudaIpcGetMemHandle(&ih, p);
+    if (st != cudaSuccess) {
+        if (p != nullptr) cudaFree(p);
+        h->set_error(std::string("sm100_ipc_alloc: ") + cudaGetErrorString(st));
+        return 1;
+    }
+    std::memcpy(out_handle, &ih, sizeof(ih));
+    *out_ptr = reinterpret_cast<uint64_t>(p);
+    h->last_error.clear();
+    return 0;
+}
+
+int kudacuda_sm100_ipc_open(void* raw, const void* ipc_handle, int64_t handle_bytes, uint64_t* out_ptr) {
+    Handle* h = as_handle(raw);
+    if (h == nullptr || ipc_handle == nullptr || out_ptr == nullptr ||
+        handle_bytes < static_cast<int64_t>(sizeof(cudaIpcMemHandle_t))) {
+        if (h != nullptr) h->set_error("sm100_ipc_open requires a 64-byte handle and an output pointer");
+        return 1;
+    }
+    cudaIpcMemHandle_t ih;
+    std::memcpy(&ih, ipc_handle, sizeof(ih));
+    void* p = nullptr;
+    cudaError_t st = cudaSetDevice(h->device_id);
+    if (st == cudaSuccess) st = cudaIpcOpenMemHandle(&p, ih, cudaIpcMemLazyEnablePeerAccess);
+    if (st != cudaSuccess) {
+        h->set_error(std::string("sm100_ipc_open: ") + cudaGetErrorString(st));
+        return 1;
+    }
+    *out_ptr = reinterpret_cast<uint64_t>(p);
+    h->last_error.clear();
+    return 0;
+}
+
+int kudacuda_sm100_ipc_close(void* raw, uint64_t ptr, int owned) {
+    Handle* h = as_handle(raw);
+    if (h == nullptr || ptr == 0) return 1;
+    cudaError_t st = cudaSetDevice(h->device_id);
+    if (st == cudaSuccess)
+        st = owned != 0 ? cudaFree(reinterpret_cast<void*>(ptr)) : cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr));
+    if (st != cudaSuccess) {
+        h->set_error(std::string("sm100_ipc_close: ") + cudaGetErrorString(st));
+        return 1;
+    }
+    h->last_error.clear();
+    return 0;
 }
 
 // ---------------------------------------------------------------- batched decode

@@ -413,6 +413,50 @@ def _buffer_ptrs(t: Any) -> list[int]:
     return t.data_ptrs() if isinstance(t, LayerCaches) else [int(t.data_ptr())]
 
 
+class TPExchange:
+    """The exchange buffers of the tensor-parallel row-split kernel: every rank
+    allocates one (kudacuda_sm100_tp_exchange_bytes: o_proj then down partials,
+    [world][hidden] tagged words each, zeroed once), exports a CUDA IPC
+    handle, gathers the others' handles over the process group and maps them;
+    ``peers`` is the device table of the world buffer addresses as this
+    process sees them (plain peer memory over NVLink, no multicast object).
+    ``close`` is collective: every rank unmaps the peers' buffers, then frees
+    its own."""
+
+    def __init__(self, bridge: KudaCudaBridge, torch: Any, *, rank: int, world: int, group: Any, hidden: int,
+                 device: Any) -> None:
+        import torch.distributed as dist
+
+        self.bridge, self.rank, self.world, self.group = bridge, int(rank), int(world), group
+        nbytes = bridge.tp_exchange_bytes(world, hidden)
+        self.own, handle = bridge.ipc_alloc(nbytes)
+        handles: list[Any] = [None] * world
+        dist.all_gather_object(handles, handle, group=group)
+        addrs = []
+        self.opened: list[int] = []
+        for p_, h in enumerate(handles):
+            if p_ == self.rank:
+                addrs.append(self.own)
+            else:
+                ptr = bridge.ipc_open(h)
+                self.opened.append(ptr)
+                addrs.append(ptr)
+        self.peers = torch.tensor(addrs, dtype=torch.int64, device=device)
+        self.closed = False
+
+    def close(self) -> None:
+        if self.closed:
+            return
+        import torch.distributed as dist
+
+        dist.barrier(group=self.group)
+        for ptr in self.opened:
+            self.bridge.ipc_close(ptr, owned=False)
+        dist.barrier(group=self.group)
+        self.bridge.ipc_close(self.own, owned=True)
+        self.closed = True
+
+
 class PersistentLayers:
     """Device data of the persistent decode path for one plan: every layer's
     q/k/v, o, gate/up and down weights copied once into the stream layout of
@@ -428,9 +472,12 @@ class PersistentLayers:
 
     SLOTS = 16
 
-    def __init__(self, plan: "StaticDecodePlan", layout: str = "rows") -> None:
+    def __init__(self, plan: "StaticDecodePlan", layout: str = "rows", exchange: Optional[TPExchange] = None) -> None:
         if layout not in ("rows", "groups"):
             raise ValueError(f"unknown persistent layout {layout!r}")
+        if exchange is not None and layout != "rows":
+            raise NativeCudaError("tensor parallelism runs on the row-split persistent kernel only")
+        self.exchange = exchange
         torch = plan.torch
         br, c, w, b = plan.bridge, plan.config, plan.weights, plan.buffers
         dev = plan.device
@@ -483,6 +530,8 @@ class PersistentLayers:
 
     def pointers(self) -> list[int]:
         out = [int(self.table.data_ptr()), int(self.scratch.data_ptr())]
+        if self.exchange is not None:
+            out.append(int(self.exchange.peers.data_ptr()))
         for tensors in self.tiles:
             out += [int(t.data_ptr()) for t in tensors]
         return out
@@ -496,7 +545,15 @@ class PersistentLayers:
                   kv_heads=p.kv_heads, head_dim=c.head_dim, intermediate=p.inter, kv_capacity=p.kv_bucket,
                   epsilon=c.eps, scale=1.0 / math.sqrt(c.head_dim), stream_ptr=stream_ptr, taps=taps,
                   spin_limit=spin_limit, stall_counter=stall_counter)
-        if self.layout == "rows":
+        if self.exchange is not None:
+            if taps is not None or spin_limit or stall_counter != -1:
+                raise NativeCudaError("the tensor-parallel persistent launch has no test hooks")
+            for k in ("taps", "spin_limit", "stall_counter"):
+                kw.pop(k)
+            ex = self.exchange
+            p.bridge.dispatch_decode_layers_rows_tp(self.table, b.x, b.state, b.rope_cos, b.rope_sin, self.scratch,
+                                                    world=ex.world, rank=ex.rank, peers=ex.peers, **kw)
+        elif self.layout == "rows":
             p.bridge.dispatch_decode_layers_rows(self.table, b.x, b.state, b.rope_cos, b.rope_sin, self.scratch, **kw)
         else:
             p.bridge.dispatch_decode_layers_persistent(self.table, b.x, b.state, b.rope_cos, b.rope_sin, self.scratch,
@@ -611,10 +668,13 @@ class StaticDecodePlan:
         # persistent path: all layers of a step in one cooperative launch over
         # weights re-tiled once into the kernel's stream layout
         self.persistent: Optional[PersistentLayers] = None
+        self.tp_exchange: Optional[TPExchange] = None
         if persistent:
-            if self.tp is not None:
-                raise NativeCudaError("the persistent decode path has no tensor-parallel variant")
-            self.persistent = PersistentLayers(self, layout=persistent_layout)
+            if self.tp is not None and self.tp.world > 1:
+                # o_proj / down partials are exchanged inside the kernel (peer memory)
+                self.tp_exchange = TPExchange(bridge, torch, rank=self.tp.rank, world=self.tp.world,
+                                              group=self.tp.group, hidden=c.hidden, device=device)
+            self.persistent = PersistentLayers(self, layout=persistent_layout, exchange=self.tp_exchange)
 
     @property
     def captured(self) -> bool:

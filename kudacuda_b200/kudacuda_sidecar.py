@@ -1160,6 +1160,63 @@ class KudaCudaBridge:
                    int(head_dim), int(intermediate), int(kv_capacity), float(epsilon), float(scale), tp, tb,
                    int(spin_limit), int(stall_counter), _normalize_cuda_handle(stream_ptr))
 
+    def dispatch_decode_layers_rows_tp(self, layer_table: Any, x: Any, state: Any, rope_cos: Any, rope_sin: Any,
+                                       scratch: Any, *, layers: int, max_pos: int, hidden: int, q_heads: int,
+                                       kv_heads: int, head_dim: int, intermediate: int, kv_capacity: int,
+                                       epsilon: float, scale: float, world: int, rank: int, peers: Any,
+                                       stream_ptr: int) -> None:
+        """The row-split kernel over this rank's tensor-parallel shard; o_proj
+        and down partials are exchanged with the other ranks inside the kernel
+        (``peers``: device int64 [world] exchange-buffer addresses)."""
+
+        self._call("kudacuda_sm100_decode_layers_rows_tp", self._tensor_pointer(layer_table, "layer_table"),
+                   int(layers), self._tensor_pointer(x, "x"), self._tensor_pointer(state, "state"),
+                   self._tensor_pointer(rope_cos, "rope_cos"), self._tensor_pointer(rope_sin, "rope_sin"),
+                   int(max_pos), self._tensor_pointer(scratch, "scratch"),
+                   int(scratch.numel()) * int(scratch.element_size()), int(hidden), int(q_heads), int(kv_heads),
+                   int(head_dim), int(intermediate), int(kv_capacity), float(epsilon), float(scale), int(world),
+                   int(rank), self._tensor_pointer(peers, "peers"), _normalize_cuda_handle(stream_ptr))
+
+    def tp_exchange_bytes(self, world: int, hidden: int) -> int:
+        self._check_open()
+        n = int(self.lib.kudacuda_sm100_tp_exchange_bytes(int(world), int(hidden)))
+        if n < 0:
+            raise NativeCudaError("kudacuda_sm100_tp_exchange_bytes: unsupported world or hidden")
+        return n
+
+    def ipc_alloc(self, nbytes: int) -> tuple[int, bytes]:
+        """A zeroed device allocation of its own and its 64-byte CUDA IPC handle."""
+
+        import ctypes
+
+        ptr = ctypes.c_uint64(0)
+        buf = ctypes.create_string_buffer(64)
+        self._check_open()
+        fn = self._symbol("kudacuda_sm100_ipc_alloc")
+        if fn is None:
+            raise NativeCudaError("native library does not export kudacuda_sm100_ipc_alloc")
+        self._raise_if_failed(fn(self.engine_handle, int(nbytes), ctypes.byref(ptr), buf, 64), "kudacuda_sm100_ipc_alloc")
+        return int(ptr.value), bytes(buf.raw)
+
+    def ipc_open(self, handle: bytes) -> int:
+        import ctypes
+
+        ptr = ctypes.c_uint64(0)
+        buf = ctypes.create_string_buffer(bytes(handle), 64)
+        self._check_open()
+        fn = self._symbol("kudacuda_sm100_ipc_open")
+        if fn is None:
+            raise NativeCudaError("native library does not export kudacuda_sm100_ipc_open")
+        self._raise_if_failed(fn(self.engine_handle, buf, 64, ctypes.byref(ptr)), "kudacuda_sm100_ipc_open")
+        return int(ptr.value)
+
+    def ipc_close(self, ptr: int, *, owned: bool) -> None:
+        self._check_open()
+        fn = self._symbol("kudacuda_sm100_ipc_close")
+        if fn is None:
+            raise NativeCudaError("native library does not export kudacuda_sm100_ipc_close")
+        self._raise_if_failed(fn(self.engine_handle, int(ptr), 1 if owned else 0), "kudacuda_sm100_ipc_close")
+
     def persistent_scratch_bytes(self, *, layers: int, hidden: int, q_heads: int, kv_heads: int, head_dim: int,
                                  intermediate: int, kv_capacity: int) -> int:
         self._check_open()

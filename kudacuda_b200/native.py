@@ -89,6 +89,15 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         [_p, _u64, _i64, _u64, _u64, _u64, _u64, _i64, _u64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _f32,
          _u64, _i64, _i64, _i64, _u64],
     ),
+    "kudacuda_sm100_decode_layers_rows_tp": (
+        _i32,
+        [_p, _u64, _i64, _u64, _u64, _u64, _u64, _i64, _u64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _f32,
+         _i64, _i64, _u64, _u64],
+    ),
+    "kudacuda_sm100_tp_exchange_bytes": (_i64, [_i64, _i64]),
+    "kudacuda_sm100_ipc_alloc": (_i32, [_p, _i64, ctypes.POINTER(_u64), _p, _i64]),
+    "kudacuda_sm100_ipc_open": (_i32, [_p, _p, _i64, ctypes.POINTER(_u64)]),
+    "kudacuda_sm100_ipc_close": (_i32, [_p, _u64, _i32]),
     "kudacuda_sm100_batch_gemm_ksplit": (_i64, [_i64, _i64]),
     "kudacuda_sm100_batch_gemm": (_i32, [_p, _i32, _u64, _u64, _i64, _i64, _u64, _i64, _i64, _u64, _i64, _i64, _u64]),
     "kudacuda_sm100_batch_retile_bytes": (_i64, [_i64, _i64]),
