@@ -584,9 +584,12 @@ def _init_dist(world: int, local: int):
     return dist
 
 
-def run_tp(args, dist_in=None) -> dict | None:
+def run_tp(args, dist_in=None, persistent: bool | None = None) -> dict | None:
     """Config 5: Llama-3-8B-architecture NF4 decode, tensor-parallel over the
-    ranks.  dist_in: an already initialised torch.distributed (left open)."""
+    ranks.  dist_in: an already initialised torch.distributed (left open).
+    persistent (default: --path persistent): the row-split persistent kernel
+    with the o_proj / down allreduce fused in (peer memory); otherwise the
+    per-op path with NCCL allreduces."""
 
     import torch
 
@@ -607,8 +610,10 @@ def run_tp(args, dist_in=None) -> dict | None:
     bucket = 512
     if prompt_len + args.warmup + args.steps + 2 > bucket:
         raise SystemExit(f"prompt + warmup + steps must fit the KV bucket of {bucket}")
+    if persistent is None:
+        persistent = getattr(args, "path", "persistent") == "persistent"
     plan = StaticDecodePlan(bridge, weights, kv_bucket=bucket, max_tokens=bucket, device=device,
-                            allreduce=(rank, world, group))
+                            allreduce=(rank, world, group), persistent=persistent)
     stream = torch.cuda.Stream(device=device)
     plan.capture(stream)
     g = torch.Generator().manual_seed(SEED)
@@ -649,6 +654,8 @@ def run_tp(args, dist_in=None) -> dict | None:
         agree = bool(flag.item())
     plan.graph_plan.invalidate()  # release the graph (it holds NCCL work) before the process group
     plan._torch_graph.reset() if plan._torch_graph is not None else None
+    if plan.tp_exchange is not None:
+        plan.tp_exchange.close()
     out = None
     if rank == 0:
         wb = cfg.weight_bytes_per_token()
@@ -672,6 +679,8 @@ def run_tp(args, dist_in=None) -> dict | None:
             "data": "synthetic (random-init weights N(0,0.02) NF4-quantised on device; uniform-random prompt)",
             "config": {
                 "workload": "config5: Llama-3-8B-architecture NF4 decode, batch 1, tensor-parallel, static CUDA graph",
+                "path": ("persistent (row-split kernel, o_proj/down allreduce fused over peer memory)" if persistent
+                         else "per-op (NCCL allreduce)"),
                 "prompt_len": prompt_len,
                 "kv_bucket": bucket,
                 "parallelism": f"tp{world}",
@@ -686,6 +695,7 @@ def run_tp(args, dist_in=None) -> dict | None:
             },
             "ranks_agree_on_tokens": agree,
             "device_error_word": err,
+            "launches_per_step": plan.launches_per_step,
             "clocks": clocks.summary(),
         }
     if dist is not None:
@@ -892,7 +902,9 @@ def tp_object(args, dist) -> dict | None:
     device = f"cuda:{local}"
     a1 = copy.copy(args)
     a1.steps, a1.warmup, a1.batch = 16, 3, 1
-    r1 = run_tp(a1, dist_in=dist)
+    r1 = run_tp(a1, dist_in=dist, persistent=True)
+    torch.cuda.empty_cache()
+    r1_ops = run_tp(a1, dist_in=dist, persistent=False)
     torch.cuda.empty_cache()
     a32 = copy.copy(args)
     a32.steps, a32.warmup, a32.batch = 8, 3, 32
@@ -912,9 +924,15 @@ def tp_object(args, dist) -> dict | None:
         "world": world,
         "model": "Llama-3-8B architecture, NF4, random-init",
         "batch1": {"tok_s": r1["value"], "ms_per_step": r1["ms_per_step"], "steps": a1.steps,
-                   "ranks_agree_on_tokens": r1["ranks_agree_on_tokens"], "device_error_word": r1["device_error_word"],
-                   "allreduce_us_each": None if ar1 is None else round(ar1, 2),
-                   "allreduce_share_est": share(ar1, r1["ms_per_step"])},
+                   "path": "persistent row-split kernel, o_proj/down allreduce fused over NVLink peer memory",
+                   "launches_per_step": r1["launches_per_step"],
+                   "ranks_agree_on_tokens": r1["ranks_agree_on_tokens"], "device_error_word": r1["device_error_word"]},
+        "batch1_per_op": {"tok_s": r1_ops["value"], "ms_per_step": r1_ops["ms_per_step"], "steps": a1.steps,
+                          "path": "per-op kernels, NCCL allreduce", "launches_per_step": r1_ops["launches_per_step"],
+                          "ranks_agree_on_tokens": r1_ops["ranks_agree_on_tokens"],
+                          "device_error_word": r1_ops["device_error_word"],
+                          "allreduce_us_each": None if ar1 is None else round(ar1, 2),
+                          "allreduce_share_est": share(ar1, r1_ops["ms_per_step"])},
         "batch32": {"tok_s": r32["value"], "ms_per_step": r32["ms_per_step"], "steps": a32.steps,
                     "ranks_agree_on_tokens": r32["ranks_agree_on_tokens"],
                     "device_error_word": r32["device_error_word"],
