@@ -208,6 +208,13 @@ __device__ __forceinline__ unsigned ld_relaxed_r(const unsigned* p) {
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+// Error bit 0 (an activation outside the f16 range) from a whole-CTA point:
+// one vote per warp and one atomic from a warp that saw it, so the common
+// case costs no memory operation at all.
+__device__ __forceinline__ void rflag_overflow(const RowArgs& a, bool overflow) {
+    if (__any_sync(0xffffffffu, overflow) && (threadIdx.x & 31) == 0)
+        asm volatile("red.relaxed.gpu.global.or.b32 [%0], %1;" ::"l"(a.err), "r"(1) : "memory");
+}
 // Tagged words (RowArgs): aligned 8-byte strong accesses are single-copy
 // atomic, so a word read with the expected tag carries that write's payload.
 __device__ __forceinline__ void st_tagged(uint64_t* p, uint32_t tag, uint32_t payload) {
@@ -506,7 +513,15 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
         epi(t0 + tl, r, lo, hi, lanes);
     }
     KR_STAMP(layer, 38 + 2 * OP);
+#ifdef KC_PERSIST_STAMPS
+    if (OP == kOGu && lane == 0 && layer == KC_STAMP_LAYER) {  // every warp's end of the GU epilogue loop
+        unsigned long long t_;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)::"memory");
+        g_rows_stamps[blockIdx.x * 64 + 46 + (threadIdx.x >> 5)] = t_;
+    }
+#endif
     __syncthreads();  // the epilogues' reads of shared memory (xres, part) before its next writers
+    if (OP == kOGu) KR_STAMP(layer, 62);
 }
 
 // ------------------------------------------------------------------ staging
@@ -562,7 +577,7 @@ __device__ void rstage_norm(const RowArgs& a, const uint16_t* xres, const uint4*
             reinterpret_cast<uint4*>(xs)[o] = make_uint4(out[0], out[1], out[2], out[3]);
         }
     }
-    if (overflow) atomicOr(a.err, 1);
+    rflag_overflow(a, overflow);
     __syncthreads();
 }
 // dst (shared, n bf16) = src (global, written by other CTAs before the acquire)
@@ -873,7 +888,7 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
             tap[att_off + o + 1] = b1;
         }
     }
-    if (overflow) atomicOr(a.err, 1);
+    rflag_overflow(a, overflow);
     __syncthreads();  // the merge's reads of wn / mb before the caller's next writes to the work area
 }
 
@@ -987,10 +1002,6 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             ratt_fetch(kc, vc, tok0, min(kATile, kv_len - tok0), pos_c, att_sm);
         }
         rstage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn : nullptr);
-#ifdef KC_ROWS_NORM_TWICE
-        KR_STAMP(l, 45);
-        rstage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn : nullptr);
-#endif
         KR_STAMP(l, 2);
         {
             uint16_t* kcl = reinterpret_cast<uint16_t*>(L[kTKCache]);
@@ -1118,7 +1129,8 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
                 const uint32_t p = pair_up(f32_to_f16_bits(hf), lanes);  // the down GEMV's f16 input
                 if ((r & 1) == 0) st_tagged(a.hw + j / 2, th, p);
             });
-            if (overflow) atomicOr(a.err, 1);
+            KR_STAMP(l, 63);
+            rflag_overflow(a, overflow);
         }
         KR_STAMP(l, 11);
         // ---- down owners: x2 = x1 + down(h), the next layer's input
