@@ -137,7 +137,7 @@ struct RowArgs {
     int* err;
     int ring_slots;
     int tiles[4], nbpt[4], ctas[4];
-    int xs_bytes, work_bytes, bias_rows;
+    int kvt_off, work_bytes, bias_rows;
     uint16_t* taps;  // test hooks, as decode_persistent.cu
     int tap_stride;
     uint32_t spin_limit;
@@ -902,11 +902,14 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     uint8_t* lut = dsm;
     uint8_t* rings = dsm + kRLutBytes;
+    // work: the GEMV input xs from 0; the attention's small arrays from 0 and
+    // its K/V tile rows from kvt_off (above any QKV input, which the rows'
+    // layer-start fetch overlaps; later inputs are staged after the attention)
     uint8_t* work = rings + kRW * a.ring_slots * kSlotBytes;
     uint16_t* xs = reinterpret_cast<uint16_t*>(work);
-    float* part = reinterpret_cast<float*>(work + a.xs_bytes);
-    uint8_t* kvt = work + a.work_bytes;  // attention K/V tile rows
-    uint16_t* xres = reinterpret_cast<uint16_t*>(kvt + kRKvTileBytes);
+    uint8_t* kvt = work + a.kvt_off;  // attention K/V tile rows
+    float* part = reinterpret_cast<float*>(work + a.work_bytes);
+    uint16_t* xres = reinterpret_cast<uint16_t*>(work + a.work_bytes + kMaxCtaTiles * kRW * 16 * 4);
     uint16_t* bias_s = xres + ((a.hidden + 63) & ~63);
     float* rope_s = reinterpret_cast<float*>(bias_s + ((a.bias_rows + 63) & ~63));
     uint8_t* ring = rings + warp * a.ring_slots * kSlotBytes;
@@ -1247,7 +1250,7 @@ __global__ void nf4_retile16_kernel(const Retile16Args r) {
 // ------------------------------------------------------------------ launch geometry
 struct RowGeom {
     int tiles[4], nbpt[4], ctas[4];
-    int xs_bytes, work_bytes, bias_rows, ring_slots, smem;
+    int kvt_off, work_bytes, bias_rows, ring_slots, smem;
     int64_t off_misc, off_qw, off_kw, off_vw, off_aw, off_x1w, off_hw, off_xw, off_pw, total;
 };
 constexpr int kRStaticSmemBudget = 3072;
@@ -1265,11 +1268,12 @@ RowGeom row_geom(const PersistDims& d, int sms) {
     for (int i = 0; i < 4; ++i) g.ctas[i] = g.tiles[i] < sms ? g.tiles[i] : sms;
     int kmax = d.hidden > d.intermediate ? d.hidden : d.intermediate;
     kmax = kmax > d.q_heads * d.head_dim ? kmax : d.q_heads * d.head_dim;
-    g.xs_bytes = (kmax * 2 + 127) & ~127;
-    const int work = g.xs_bytes + kMaxCtaTiles * kRW * 16 * 4;
-    g.work_bytes = ((work > kRAttWorkBytes ? work : kRAttWorkBytes) + 127) & ~127;
+    const int xs_bytes = (kmax * 2 + 127) & ~127;
+    g.kvt_off = ((kRAttWorkBytes > d.hidden * 2 ? kRAttWorkBytes : d.hidden * 2) + 127) & ~127;
+    g.work_bytes = ((xs_bytes > g.kvt_off + kRKvTileBytes ? xs_bytes : g.kvt_off + kRKvTileBytes) + 127) & ~127;
     g.bias_rows = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
-    const int tail = kRKvTileBytes + ((d.hidden + 63) & ~63) * 2 + ((g.bias_rows + 63) & ~63) * 2 + d.head_dim * 4;
+    const int tail = kMaxCtaTiles * kRW * 16 * 4 + ((d.hidden + 63) & ~63) * 2 + ((g.bias_rows + 63) & ~63) * 2 +
+                     d.head_dim * 4;
     const int limit = 232448 - kRStaticSmemBudget;
     g.ring_slots = kRMaxSlots;
     while (g.ring_slots > 1 && kRLutBytes + kRW * g.ring_slots * kSlotBytes + g.work_bytes + tail > limit) --g.ring_slots;
@@ -1391,7 +1395,7 @@ cudaError_t decode_layers_rows(const PersistLaunch& p, cudaStream_t stream) {
         a.nbpt[i] = g.nbpt[i];
         a.ctas[i] = g.ctas[i];
     }
-    a.xs_bytes = g.xs_bytes;
+    a.kvt_off = g.kvt_off;
     a.work_bytes = g.work_bytes;
     a.bias_rows = g.bias_rows;
     a.taps = p.taps;
