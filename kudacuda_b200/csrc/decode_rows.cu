@@ -513,13 +513,6 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
         epi(t0 + tl, r, lo, hi, lanes);
     }
     KR_STAMP(layer, 38 + 2 * OP);
-#ifdef KC_PERSIST_STAMPS
-    if (OP == kOGu && lane == 0 && layer == KC_STAMP_LAYER) {  // every warp's end of the GU epilogue loop
-        unsigned long long t_;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)::"memory");
-        g_rows_stamps[blockIdx.x * 64 + 46 + (threadIdx.x >> 5)] = t_;
-    }
-#endif
     __syncthreads();  // the epilogues' reads of shared memory (xres, part) before its next writers
     if (OP == kOGu) KR_STAMP(layer, 62);
 }
