@@ -81,6 +81,10 @@ constexpr int kUnitBytes = 576;
 #define KC_ROWS_SLOT_UNITS 4
 #endif
 constexpr int kSlotUnits = KC_ROWS_SLOT_UNITS;  // units per bulk copy / ring slot
+// per-tile partial sums of the warps, part[tile][warp][16]; a tile's block is
+// padded by 16 floats so the two tiles a warp reduces fall in different banks
+constexpr int kPartTile = 16 * 16 + 16;
+constexpr int kPartFloats = 16 * kPartTile;  // kMaxCtaTiles tiles
 constexpr int kSlotBytes = kSlotUnits * kUnitBytes;
 constexpr int kRLutBytes = 65536;  // 256 entry rows x 256 B, lane replicas in the first 128 B of a row
 constexpr int kMaxCtaTiles = 16;   // tiles of one op one CTA may own (checked on the host)
@@ -416,7 +420,7 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
     const int t0 = rr[0], ntiles = rr[1] - rr[0];
     const int nbpt = a.nbpt[OP];
     const int uw0 = rr[2 + warp], uw1 = rr[3 + warp];
-    for (int i = tid; i < kMaxCtaTiles * kRW * 16; i += kRT) part[i] = 0.F;
+    for (int i = tid; i < kPartFloats; i += kRT) part[i] = 0.F;
     __syncthreads();
     const uint32_t lane4 = static_cast<uint32_t>(lane) << 2;
 #ifdef KC_PERSIST_STAMPS
@@ -465,7 +469,7 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
             acc_hi = fmaf(pr.y, aB, acc_hi);
             if (++blk == nbpt) {  // tile done for this warp
                 if (t == 0) {
-                    float* pp = part + (tile * kRW + warp) * 16;
+                    float* pp = part + tile * kPartTile + warp * 16;
                     pp[g] = acc_lo;
                     pp[8 + g] = acc_hi;
                 }
@@ -486,7 +490,7 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
         u += n;
     }
     if (uw1 > uw0 && blk != 0 && t == 0) {
-        float* pp = part + (tile * kRW + warp) * 16;
+        float* pp = part + tile * kPartTile + warp * 16;
         pp[g] = acc_lo;
         pp[8 + g] = acc_hi;
     }
@@ -499,18 +503,18 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
 #endif
     __syncthreads();
     KR_STAMP(layer, kSt + 2);
-    for (int idx = tid; idx < ntiles * 8; idx += kRT) {
-        const int tl = idx >> 3, r = idx & 7;
-        const int left = ntiles * 8 - (idx - lane);  // this warp's lanes in the call: whole 8-lane groups
-        const unsigned lanes = left >= 32 ? 0xffffffffu : (1u << left) - 1u;
-        float lo = 0.F, hi = 0.F;
+    // one thread per tile row sums the 16 warps in fixed order; the row r + 8
+    // partner's sum comes over by shuffle and rows r < 8 run the epilogue
+    for (int idx = tid; idx < ntiles * 16; idx += kRT) {
+        const int tl = idx >> 4, rr = idx & 15;
+        const int left = ntiles * 16 - (idx - lane);  // this warp's lanes in the loop: whole 16-lane tiles
+        const unsigned active = left >= 32 ? 0xffffffffu : (1u << left) - 1u;
+        float sum = 0.F;
 #pragma unroll 4
-        for (int w = 0; w < kRW; ++w) {
-            lo += part[(tl * kRW + w) * 16 + r];
-            hi += part[(tl * kRW + w) * 16 + 8 + r];
-        }
+        for (int w = 0; w < kRW; ++w) sum += part[tl * kPartTile + w * 16 + rr];
+        const float hi = __shfl_down_sync(active, sum, 8, 16);
         if (idx == 0) KR_STAMP(layer, 37 + 2 * OP);
-        epi(t0 + tl, r, lo, hi, lanes);
+        if (rr < 8) epi(t0 + tl, rr, sum, hi, active & 0x00ff00ffu);
     }
     KR_STAMP(layer, 38 + 2 * OP);
     __syncthreads();  // the epilogues' reads of shared memory (xres, part) before its next writers
@@ -902,7 +906,7 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
     uint16_t* xs = reinterpret_cast<uint16_t*>(work);
     uint8_t* kvt = work + a.kvt_off;  // attention K/V tile rows
     float* part = reinterpret_cast<float*>(work + a.work_bytes);
-    uint16_t* xres = reinterpret_cast<uint16_t*>(work + a.work_bytes + kMaxCtaTiles * kRW * 16 * 4);
+    uint16_t* xres = reinterpret_cast<uint16_t*>(work + a.work_bytes + kPartFloats * 4);
     uint16_t* bias_s = xres + ((a.hidden + 63) & ~63);
     float* rope_s = reinterpret_cast<float*>(bias_s + ((a.bias_rows + 63) & ~63));
     uint8_t* ring = rings + warp * a.ring_slots * kSlotBytes;
@@ -1265,7 +1269,7 @@ RowGeom row_geom(const PersistDims& d, int sms) {
     g.kvt_off = ((kRAttWorkBytes > d.hidden * 2 ? kRAttWorkBytes : d.hidden * 2) + 127) & ~127;
     g.work_bytes = ((xs_bytes > g.kvt_off + kRKvTileBytes ? xs_bytes : g.kvt_off + kRKvTileBytes) + 127) & ~127;
     g.bias_rows = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
-    const int tail = kMaxCtaTiles * kRW * 16 * 4 + ((d.hidden + 63) & ~63) * 2 + ((g.bias_rows + 63) & ~63) * 2 +
+    const int tail = kPartFloats * 4 + ((d.hidden + 63) & ~63) * 2 + ((g.bias_rows + 63) & ~63) * 2 +
                      d.head_dim * 4;
     const int limit = 232448 - kRStaticSmemBudget;
     g.ring_slots = kRMaxSlots;
