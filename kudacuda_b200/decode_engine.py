@@ -528,6 +528,26 @@ class PersistentLayers:
         self.scratch = torch.zeros((nbytes + 3) // 4, dtype=torch.int32, device=dev)
         torch.cuda.synchronize(dev)
 
+    # the row-split kernel's launch counter (the tags' epoch): int32 word 2 of its scratch
+    _EPOCH_WORD = 2
+
+    def epoch(self) -> int:
+        if self.layout != "rows":
+            raise NativeCudaError("only the row-split kernel keeps a launch epoch")
+        return int(self.scratch[self._EPOCH_WORD].item())
+
+    def set_epoch(self, value: int) -> None:
+        """Recovery after a step that did not run on every rank (tensor
+        parallelism): the ranks agree on one epoch above every rank's own --
+        for example the max over ranks plus one -- so that no word written
+        before the failure carries a tag a later step expects."""
+
+        if self.layout != "rows":
+            raise NativeCudaError("only the row-split kernel keeps a launch epoch")
+        self.plan.torch.cuda.synchronize(self.plan.device)
+        self.scratch[self._EPOCH_WORD] = int(value)
+        self.plan.torch.cuda.synchronize(self.plan.device)
+
     def pointers(self) -> list[int]:
         out = [int(self.table.data_ptr()), int(self.scratch.data_ptr())]
         if self.exchange is not None:

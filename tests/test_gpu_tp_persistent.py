@@ -40,3 +40,28 @@ def test_tp2_persistent_matches_per_op_and_one_gpu():
     assert res["rel_x_tp_vs_per_op"] <= 1e-2, res
     assert res["rel_x_tp_vs_one_gpu"] <= 1e-2, res
     assert res["teacher_forced_agreement"] >= 0.75, res
+
+
+def test_tp2_missing_rank_ends_with_error_then_recovers():
+    """A rank that misses a step: the other rank's persistent kernel ends its
+    bounded waits with error bit 4 instead of hanging; after the ranks agree
+    on a fresh launch epoch a normal step runs on both, identical to the steps
+    before the failure."""
+
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    out = Path(tempfile.mkstemp(suffix=".json")[1])
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2", "--master-addr",
+           "127.0.0.1", "--master-port", "29534", str(ROOT / "tests" / "tp_failure_worker.py"), str(out)]
+    r = subprocess.run(cmd, cwd=ROOT, env=env, timeout=600, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    res = json.loads(out.read_text())
+    print(res)
+    assert res["err_before"] == 0 and res["err_after"] == 0, res
+    assert res["err_missed_step"] & 16, res
+    assert res["missed_step_seconds"] < 60, res
+    assert res["ranks_agree_after"], res
+    assert res["tokens_after"] == res["tokens_before"], res
