@@ -533,7 +533,7 @@ __device__ __forceinline__ void rnorm_prefetch(const RowArgs& a, const uint16_t*
     }
 }
 __device__ void rstage_norm(const RowArgs& a, const uint16_t* xres, const uint4* wv, uint16_t* xs, float* red,
-                            uint16_t* tap) {
+                            uint16_t* tap, [[maybe_unused]] int layer, [[maybe_unused]] int stamp) {
     const int tid = threadIdx.x;
     const int n8 = a.hidden / 8;
     float ss = 0.F;
@@ -544,6 +544,7 @@ __device__ void rstage_norm(const RowArgs& a, const uint16_t* xres, const uint4*
     ss = warp_sum(ss);
     if ((tid & 31) == 0) red[tid >> 5] = ss;
     __syncthreads();
+    KR_STAMP(layer, stamp);
     float tot = 0.F;
 #pragma unroll
     for (int i = 0; i < kRW; ++i) tot += red[i];
@@ -890,6 +891,9 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
 }
 
 // ------------------------------------------------------------------ the kernel
+// kTP: the tensor-parallel form (world > 1: o_proj and down summed over the
+// ranks' exchange buffers); the single-GPU form carries none of that code.
+template <bool kTP>
 __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
     extern __shared__ __align__(128) uint8_t dsm[];
     __shared__ __align__(8) uint64_t bars_all[kRW * kRMaxSlots];
@@ -1001,7 +1005,7 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             const uint16_t* vc = reinterpret_cast<const uint16_t*>(L[kTVCache]) + static_cast<int64_t>(hk) * a.cap * hd;
             ratt_fetch(kc, vc, tok0, min(kATile, kv_len - tok0), pos_c, att_sm);
         }
-        rstage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn : nullptr);
+        rstage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn : nullptr, l, 45);
         KR_STAMP(l, 2);
         {
             uint16_t* kcl = reinterpret_cast<uint16_t*>(L[kTKCache]);
@@ -1079,27 +1083,27 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             rpoll_vec<8>(a, a.aw, a.qh * hd / 2, ctag(l, kHAtt), reinterpret_cast<uint32_t*>(xs));
             KR_STAMP(l, 7);
             const uint32_t tx1 = ptag(l, kHX1);
-            const bool tp = a.world > 1;
+            constexpr bool tp = kTP;
             const uint32_t tpo = ptag(l, kHTpO);
             rgemv<kOO>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi, unsigned lanes) {
-                if (tp) {  // this rank's partial: the sum over ranks comes after every push
+                if constexpr (tp) {  // this rank's partial: the sum over ranks comes after every push
                     rtp_push(a, 0, 16 * T + r, ylo, yhi, tpo);
-                    return;
-                }
-                uint16_t x1[2];
+                } else {
+                    uint16_t x1[2];
 #pragma unroll
-                for (int k = 0; k < 2; ++k) {
-                    const int row = 16 * T + r + 8 * k;
-                    x1[k] = f32_to_bf16_bits(bf16_bits_to_f32(xres[row]) + round_bf16(k == 0 ? ylo : yhi));
-                    if (tap != nullptr) tap[to.x1 + row] = x1[k];
-                }
-                const uint32_t p0 = pair_up(x1[0], lanes), p1 = pair_up(x1[1], lanes);
-                if ((r & 1) == 0) {
-                    st_tagged(a.x1w + (16 * T + r) / 2, tx1, p0);
-                    st_tagged(a.x1w + (16 * T + r + 8) / 2, tx1, p1);
+                    for (int k = 0; k < 2; ++k) {
+                        const int row = 16 * T + r + 8 * k;
+                        x1[k] = f32_to_bf16_bits(bf16_bits_to_f32(xres[row]) + round_bf16(k == 0 ? ylo : yhi));
+                        if (tap != nullptr) tap[to.x1 + row] = x1[k];
+                    }
+                    const uint32_t p0 = pair_up(x1[0], lanes), p1 = pair_up(x1[1], lanes);
+                    if ((r & 1) == 0) {
+                        st_tagged(a.x1w + (16 * T + r) / 2, tx1, p0);
+                        st_tagged(a.x1w + (16 * T + r + 8) / 2, tx1, p1);
+                    }
                 }
             });
-            if (tp)
+            if constexpr (tp)
                 rtp_finish(a, rng + kOO * kRngStride, reinterpret_cast<const uint64_t*>(a.peers[a.rank]),
                            ctag(l, kHTpO), part, [&](int row, float sum, unsigned lanes) {
                                const uint16_t x1 =
@@ -1113,7 +1117,7 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
         // ---- x1 ready -> RMSNorm -> gate/up owners (SwiGLU)
         rpoll_vec<8>(a, a.x1w, a.hidden / 2, ctag(l, kHX1), reinterpret_cast<uint32_t*>(xres));
         KR_STAMP(l, 9);
-        rstage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn2 : nullptr);
+        rstage_norm(a, xres, wv, xs, red, tap0 ? tap + to.xn2 : nullptr, l, 46);
         KR_STAMP(l, 10);
         {
             bool overflow = false;
@@ -1131,6 +1135,7 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             });
             KR_STAMP(l, 63);
             rflag_overflow(a, overflow);
+            KR_STAMP(l, 61);
         }
         KR_STAMP(l, 11);
         // ---- down owners: x2 = x1 + down(h), the next layer's input
@@ -1140,28 +1145,28 @@ __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
             KR_STAMP(l, 13);
             const uint32_t tx = ptag(l + 1, kHX);
             const bool last = l == a.nlayers - 1;
-            const bool tp = a.world > 1;
+            constexpr bool tp = kTP;
             const uint32_t tpd = ptag(l, kHTpD);
             rgemv<kODn>(a, l, rng, lut, ring, bars, ps, cs, xs, part, [&](int T, int r, float ylo, float yhi, unsigned lanes) {
-                if (tp) {
+                if constexpr (tp) {
                     rtp_push(a, a.world * a.hidden, 16 * T + r, ylo, yhi, tpd);
-                    return;
-                }
-                uint16_t x2[2];
+                } else {
+                    uint16_t x2[2];
 #pragma unroll
-                for (int k = 0; k < 2; ++k) {
-                    const int row = 16 * T + r + 8 * k;
-                    x2[k] = f32_to_bf16_bits(bf16_bits_to_f32(xres[row]) + round_bf16(k == 0 ? ylo : yhi));
-                    if (last) a.x[row] = x2[k];  // the step's output, read by the lm_head after the kernel
-                    if (tap != nullptr) tap[to.x2 + row] = x2[k];
-                }
-                const uint32_t p0 = pair_up(x2[0], lanes), p1 = pair_up(x2[1], lanes);
-                if ((r & 1) == 0 && !last) {
-                    st_tagged(a.xw + (16 * T + r) / 2, tx, p0);
-                    st_tagged(a.xw + (16 * T + r + 8) / 2, tx, p1);
+                    for (int k = 0; k < 2; ++k) {
+                        const int row = 16 * T + r + 8 * k;
+                        x2[k] = f32_to_bf16_bits(bf16_bits_to_f32(xres[row]) + round_bf16(k == 0 ? ylo : yhi));
+                        if (last) a.x[row] = x2[k];  // the step's output, read by the lm_head after the kernel
+                        if (tap != nullptr) tap[to.x2 + row] = x2[k];
+                    }
+                    const uint32_t p0 = pair_up(x2[0], lanes), p1 = pair_up(x2[1], lanes);
+                    if ((r & 1) == 0 && !last) {
+                        st_tagged(a.xw + (16 * T + r) / 2, tx, p0);
+                        st_tagged(a.xw + (16 * T + r + 8) / 2, tx, p1);
+                    }
                 }
             });
-            if (tp)
+            if constexpr (tp)
                 rtp_finish(a, rng + kODn * kRngStride,
                            reinterpret_cast<const uint64_t*>(a.peers[a.rank]) + static_cast<int64_t>(a.world) * a.hidden,
                            ctag(l, kHTpD), part, [&](int row, float sum, unsigned lanes) {
@@ -1402,7 +1407,8 @@ cudaError_t decode_layers_rows(const PersistLaunch& p, cudaStream_t stream) {
     a.world = p.world;
     a.rank = p.rank;
     a.peers = p.tp_peers;
-    cudaError_t st = cudaFuncSetAttribute(decode_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, g.smem);
+    void (*kern)(RowArgs) = a.world > 1 ? decode_rows_kernel<true> : decode_rows_kernel<false>;
+    cudaError_t st = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, g.smem);
     if (st != cudaSuccess) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(sms));
@@ -1414,7 +1420,7 @@ cudaError_t decode_layers_rows(const PersistLaunch& p, cudaStream_t stream) {
     at[0].val.cooperative = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, decode_rows_kernel, a);
+    return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 }  // namespace kc
