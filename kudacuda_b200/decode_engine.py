@@ -916,11 +916,19 @@ class StaticDecodePlan:
         if getattr(self, "_host_in", None) is None:
             self._host_in = torch.zeros(4, dtype=torch.int32).pin_memory()
             self._host_out = torch.zeros(1, dtype=torch.int32).pin_memory()
+            self._host_in_np, self._host_out_np = self._host_in.numpy(), self._host_out.numpy()
+            self._bound_step, self._bound_stream = None, None
         hi, ho = self._host_in, self._host_out
-        hi[0], hi[1], hi[2] = int(token), int(position), int(position) + 1
+        hin = self._host_in_np  # a view of the pinned buffer: no tensor indexing per step
+        hin[0], hin[1], hin[2] = int(token), int(position), int(position) + 1
         sp = int(stream.cuda_stream)
         if self._torch_graph is None:
-            self.bridge.graph_step_host(hi, self.buffers.state, ho, self.buffers.next_token, stream_ptr=sp)
+            if self._bound_stream != sp:
+                self._bound_step = self.bridge.bind_graph_step_host(hi, self.buffers.state, ho, self.buffers.next_token,
+                                                                    stream_ptr=sp)
+                self._bound_stream = sp
+            self._bound_step()
+            return int(self._host_out_np[0])
         else:
             with torch.cuda.stream(stream):
                 self.buffers.state.copy_(hi, non_blocking=True)

@@ -1471,6 +1471,36 @@ class KudaCudaBridge:
             out_bytes, _normalize_cuda_handle(stream_ptr))
         self._raise_if_failed(status, "kudacuda_sm100_graph_step_host")
 
+    def bind_graph_step_host(self, host_in: Any, device_in: Any, host_out: Any, device_out: Any, *,
+                             stream_ptr: int) -> Any:
+        """graph_step_host with its four buffers and the stream resolved once,
+        for a decode loop.
+
+        Returns a callable that runs one step through the same C entry
+        (kudacuda_sm100_graph_step_host: H2D of host_in, graph replay, D2H into
+        host_out, stream synchronise) and raises on a non-zero status.  The
+        callable keeps the tensors alive; write each step's input into host_in
+        (``host_in.numpy()`` is a view of pinned memory) before the call and
+        read host_out after it.  The graph itself is looked up at each call, so
+        a re-instantiated graph needs no new binding.
+        """
+
+        in_bytes = int(host_in.numel()) * int(host_in.element_size())
+        out_bytes = int(host_out.numel()) * int(host_out.element_size())
+        args = (self.engine_handle, ctypes.c_void_p(int(host_in.data_ptr())),
+                self._tensor_pointer(device_in, "device_in"), in_bytes, ctypes.c_void_p(int(host_out.data_ptr())),
+                self._tensor_pointer(device_out, "device_out"), out_bytes, _normalize_cuda_handle(stream_ptr))
+        fn = self.lib.kudacuda_sm100_graph_step_host
+        buffers = (host_in, device_in, host_out, device_out)
+
+        def step() -> None:
+            status = fn(*args)
+            if status != 0:
+                self._raise_if_failed(status, "kudacuda_sm100_graph_step_host")
+
+        step.buffers = buffers  # type: ignore[attr-defined]
+        return step
+
     # ---------------------------------------------------------------- lifetime
     def shutdown(self) -> None:
         if not self._closed:

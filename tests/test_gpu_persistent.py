@@ -282,3 +282,41 @@ def test_groups_layout_layer_against_oracle(tiny_groups):
         vc = np.zeros_like(kc)
         O.layer_step_hf(_layer_np(L), ocfg, x, kc, vc, plan.kv_bucket, 0, cos[0], sin[0])
     norm_close(O.bf16_to_f32(_b16(plan.buffers.x)), O.bf16_to_f32(x))
+
+
+@pytest.mark.gpu
+def test_bound_host_step_matches_graph_step_host(tiny_persistent):
+    """The pre-bound host step (buffers and stream resolved once, the form a
+    decode loop uses) calls the same C entry as graph_step_host: the same
+    tokens from the same start, also through the plan's step_host."""
+
+    import torch
+
+    cfg, bridge, w, plan, stream = tiny_persistent
+    sp = int(stream.cuda_stream)
+
+    def run(bound):
+        plan.reset_cache()
+        hi = torch.zeros(4, dtype=torch.int32).pin_memory()
+        ho = torch.zeros(1, dtype=torch.int32).pin_memory()
+        step = bridge.bind_graph_step_host(hi, plan.buffers.state, ho, plan.buffers.next_token, stream_ptr=sp)
+        tok, out = 7, []
+        for pos in range(5):
+            hi[0], hi[1], hi[2] = tok, pos, pos + 1
+            if bound:
+                step()
+            else:
+                bridge.graph_step_host(hi, plan.buffers.state, ho, plan.buffers.next_token, stream_ptr=sp)
+            tok = int(ho[0])
+            out.append(tok)
+        return out
+
+    ref = run(False)
+    assert run(True) == ref
+    plan.reset_cache()
+    got, tok = [], 7
+    for pos in range(5):
+        tok = plan.step_host(tok, pos, stream)
+        got.append(tok)
+    assert got == ref
+    assert bridge.error_word(clear=True) == 0
