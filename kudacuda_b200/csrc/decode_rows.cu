@@ -608,7 +608,7 @@ struct RAttSmem {
     uint16_t* kt;  // [kATile][kKRow]  (a region of its own: the first tile is fetched at layer start)
     uint16_t* vt;  // [kATile][kKRow]
     uint16_t* qb;  // [8][kKRow]: the group's q rows (bf16), rows >= gq zero   (in the work region)
-    float* ss;     // [2][8][kSs]: score halves, then probabilities in [0]; the merge's weights and split max/sum
+    float* ss;     // [2][8][kSs]: score halves, then in row 8 + h head h's probabilities as bf16 hi/lo token pairs; the merge's weights and split max/sum
     float* ml;     // [8][4]: running max, sum, correction
     float* mb;     // [8][ns * nd <= 160]: the merge's slice of every split's accumulator, [hq][split][dim]
     uint16_t* kvpos;  // [2][128]: this step's k and v rows (bf16), from the q/k/v owners' tagged words
@@ -765,12 +765,21 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
             mx = warp_max(mx);
             const float m_old = sm.ml[warp * 4 + 0];
             const float m_new = fmaxf(m_old, mx);
+            // the probabilities as bf16 hi + lo pairs of consecutive tokens, split once here for every
+            // P.V warp: row 8 + head of ss (its scores are consumed), hi pair i at word i, lo at 32 + i
+            uint32_t* pk = reinterpret_cast<uint32_t*>(sm.ss + (8 + warp) * kSs);
             float ls = 0.F;
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
                 const int j = lane + 32 * k;
                 const float p = j < nt ? exp2f(v[k] - m_new) : 0.F;
-                if (j < n16) sm.ss[warp * kSs + j] = p;
+                const float pn = __shfl_down_sync(0xffffffffu, p, 1);
+                if ((lane & 1) == 0 && j < n16) {
+                    uint32_t hi, lo;
+                    rsplit_pair(p, pn, hi, lo);
+                    pk[j >> 1] = hi;
+                    pk[32 + (j >> 1)] = lo;
+                }
                 ls += p;
             }
             ls = warp_sum(ls);
@@ -789,27 +798,27 @@ __device__ void rattention(const RowArgs& a, int layer, const uint64_t* L, int p
             o0[1] *= corr;
             o1[0] *= corr;
             o1[1] *= corr;
-            const float* prow = sm.ss + (g < gq ? g : 0) * kSs + 2 * t;
+            const uint32_t* prow = reinterpret_cast<const uint32_t*>(sm.ss + (8 + (g < gq ? g : 0)) * kSs) + t;
             const int nk = n16 >> 4;
             for (int kk = 0; kk < nk; kk += 2) {
                 const bool two = kk + 1 < nk;
                 uint32_t b0, b1, b2 = 0u, b3 = 0u;
                 rldsm_x2_trans(b0, b1, vbase + static_cast<uint32_t>(kk * 16 * kKRow * 2));
                 if (two) rldsm_x2_trans(b2, b3, vbase + static_cast<uint32_t>((kk + 1) * 16 * kKRow * 2));
-                float2 pa = make_float2(0.F, 0.F), pb = pa, pc = pa, pd = pa;
+                // tokens kk*16 + 2t (+1) are pair kk*8 + t; + 8 tokens is + 4 pairs (zero for rows >= gq)
+                uint32_t ah0 = 0u, al0 = 0u, ah2 = 0u, al2 = 0u, ch0 = 0u, cl0 = 0u, ch2 = 0u, cl2 = 0u;
                 if (g < gq) {
-                    pa = *reinterpret_cast<const float2*>(prow + kk * 16);
-                    pb = *reinterpret_cast<const float2*>(prow + kk * 16 + 8);
+                    ah0 = prow[kk * 8];
+                    al0 = prow[32 + kk * 8];
+                    ah2 = prow[kk * 8 + 4];
+                    al2 = prow[32 + kk * 8 + 4];
                     if (two) {
-                        pc = *reinterpret_cast<const float2*>(prow + kk * 16 + 16);
-                        pd = *reinterpret_cast<const float2*>(prow + kk * 16 + 24);
+                        ch0 = prow[kk * 8 + 8];
+                        cl0 = prow[32 + kk * 8 + 8];
+                        ch2 = prow[kk * 8 + 12];
+                        cl2 = prow[32 + kk * 8 + 12];
                     }
                 }
-                uint32_t ah0, al0, ah2, al2, ch0, cl0, ch2, cl2;
-                rsplit_pair(pa.x, pa.y, ah0, al0);
-                rsplit_pair(pb.x, pb.y, ah2, al2);
-                rsplit_pair(pc.x, pc.y, ch0, cl0);
-                rsplit_pair(pd.x, pd.y, ch2, cl2);
                 mma_bf16(o0, ah0, 0u, ah2, 0u, b0, b1);
                 if (two) mma_bf16(o1, ch0, 0u, ch2, 0u, b2, b3);
                 mma_bf16(o0, al0, 0u, al2, 0u, b0, b1);
