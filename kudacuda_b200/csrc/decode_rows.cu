@@ -81,8 +81,9 @@ constexpr int kUnitBytes = 576;
 #define KC_ROWS_SLOT_UNITS 4
 #endif
 constexpr int kSlotUnits = KC_ROWS_SLOT_UNITS;  // units per bulk copy / ring slot
-// per-tile partial sums of the warps, part[tile][warp][16]; a tile's block is
-// padded by 16 floats so the two tiles a warp reduces fall in different banks
+// per-tile partial sums of the warps, part[tile][row][warp] (a row's 16 warps
+// contiguous: the reducing thread reads them as four 16-byte loads); a tile's
+// block is padded by 16 floats
 constexpr int kPartTile = 16 * 16 + 16;
 constexpr int kPartFloats = 16 * kPartTile;  // kMaxCtaTiles tiles
 constexpr int kSlotBytes = kSlotUnits * kUnitBytes;
@@ -409,7 +410,7 @@ __device__ __noinline__ void rring_drain(uint64_t* bars, int ring_slots, int slo
 // ------------------------------------------------------------------ one GEMV op: this CTA's tiles
 // xs holds the f16 input vector.  Each warp consumes its unit range slot by
 // slot, refilling each slot from the stream as soon as it is read; per-tile
-// sums of the warp go to part[tile][warp][16]; then the CTA sums the warps in
+// sums of the warp go to part[tile][row][warp]; then the CTA sums the warps in
 // fixed order and hands every (tile, row pair) to `epi` (rows r and r + 8).
 template <int OP, class Epi>
 __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t* lut, uint8_t* ring, uint64_t* bars,
@@ -469,9 +470,9 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
             acc_hi = fmaf(pr.y, aB, acc_hi);
             if (++blk == nbpt) {  // tile done for this warp
                 if (t == 0) {
-                    float* pp = part + tile * kPartTile + warp * 16;
-                    pp[g] = acc_lo;
-                    pp[8 + g] = acc_hi;
+                    float* pp = part + tile * kPartTile + warp;
+                    pp[g * 16] = acc_lo;
+                    pp[(8 + g) * 16] = acc_hi;
                 }
                 acc_lo = acc_hi = 0.F;
                 blk = 0;
@@ -490,9 +491,9 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
         u += n;
     }
     if (uw1 > uw0 && blk != 0 && t == 0) {
-        float* pp = part + tile * kPartTile + warp * 16;
-        pp[g] = acc_lo;
-        pp[8 + g] = acc_hi;
+        float* pp = part + tile * kPartTile + warp;
+        pp[g * 16] = acc_lo;
+        pp[(8 + g) * 16] = acc_hi;
     }
     KR_STAMP(layer, kSt + 1);
 #ifdef KC_PERSIST_STAMPS
@@ -509,9 +510,13 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
         const int tl = idx >> 4, rr = idx & 15;
         const int left = ntiles * 16 - (idx - lane);  // this warp's lanes in the loop: whole 16-lane tiles
         const unsigned active = left >= 32 ? 0xffffffffu : (1u << left) - 1u;
-        float sum = 0.F;
-#pragma unroll 4
-        for (int w = 0; w < kRW; ++w) sum += part[tl * kPartTile + w * 16 + rr];
+        const float4* pr = reinterpret_cast<const float4*>(part + tl * kPartTile + rr * 16);  // the row's 16 warps
+        const float4 p0 = pr[0], p1 = pr[1], p2 = pr[2], p3 = pr[3];
+        float sum = 0.F;  // warps in order 0 .. 15
+        sum += p0.x; sum += p0.y; sum += p0.z; sum += p0.w;
+        sum += p1.x; sum += p1.y; sum += p1.z; sum += p1.w;
+        sum += p2.x; sum += p2.y; sum += p2.z; sum += p2.w;
+        sum += p3.x; sum += p3.y; sum += p3.z; sum += p3.w;
         const float hi = __shfl_down_sync(active, sum, 8, 16);
         if (idx == 0) KR_STAMP(layer, 37 + 2 * OP);
         if (rr < 8) epi(t0 + tl, rr, sum, hi, active & 0x00ff00ffu);
