@@ -366,8 +366,8 @@ KUDACUDA_API int kudacuda_sm100_decode_layers_persistent_debug(void* handle, uin
  * into the cache row, x + o_proj, SwiGLU, x + down), so consumers read
  * finished vectors instead of partial sums.  nf4_retile16 copies
  * bitsandbytes NF4 tensors into its units (tile, 64-element block): 512 code
- * bytes in m16n8k16 lane order then the tile rows' 16 fp32 absmax, 576 bytes,
- * tile-major; modes as nf4_retile (0 plain, rows % 16 == 0; 1 gate/up in
+ * bytes in m16n8k16 lane order then the tile rows' 16 fp32 absmax as
+ * (row g, row g + 8) pairs, 576 bytes, tile-major; modes as nf4_retile (0 plain, rows % 16 == 0; 1 gate/up in
  * tiles of 8 pairs; 2 q/k/v with q/k heads in tiles of 8 RoPE pairs, then
  * 16-row v tiles); nf4_retile16_tiles returns the tile count (-1 when
  * unsupported).  layer_table is a device int64 [layers][16]: qkv units, o

@@ -22,7 +22,8 @@
 //
 // Unit (tile, block b): 512 code bytes -- lane 4g + t holds bytes
 // [32b + 8t, +8) of tile rows g and g + 8, exactly its m16n8k16 A fragments --
-// then the 16 rows' fp32 absmax of block b (576 bytes; nf4_retile16_kernel
+// then the 16 rows' fp32 absmax of block b as (row g, row g + 8) pairs, one
+// 8-byte load per lane (576 bytes; nf4_retile16_kernel
 // writes them tile-major from the bitsandbytes layout).  Tile rows: q/k heads
 // in tiles of 8 RoPE pairs (row r and its partner r + 8), gate/up pairs, or
 // 16 consecutive rows.
@@ -460,9 +461,9 @@ __device__ void rgemv(const RowArgs& a, int layer, const int* rng, const uint8_t
             }
             float aA = 0.F, aB = 0.F;
             if (t == 0) {
-                const float* am = reinterpret_cast<const float*>(st + k * kUnitBytes + kUnitCodes);
-                aA = am[g];
-                aB = am[8 + g];
+                const float2 am = reinterpret_cast<const float2*>(st + k * kUnitBytes + kUnitCodes)[g];
+                aA = am.x;  // row g
+                aB = am.y;  // row g + 8
             }
             const uint4 w = reinterpret_cast<const uint4*>(st + k * kUnitBytes)[lane];
             const float2 pr = unit_dot_r(lut, lane4, w, x0, x1);
@@ -1258,7 +1259,8 @@ __global__ void nf4_retile16_kernel(const Retile16Args r) {
         if (l < 16) {
             int m, row;
             tile16_row(r, tile, l, m, row);
-            reinterpret_cast<float*>(u + kUnitCodes)[l] = r.absmax[m][static_cast<int64_t>(row) * nbpt + b];
+            reinterpret_cast<float*>(u + kUnitCodes)[l < 8 ? 2 * l : 2 * (l - 8) + 1] =
+                r.absmax[m][static_cast<int64_t>(row) * nbpt + b];
         }
     }
 }

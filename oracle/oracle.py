@@ -403,7 +403,8 @@ def retile_tiles16(mode: int, mats: list[tuple[np.ndarray, np.ndarray, int]], k:
 
     Unit (tile, block b): 512 code bytes, lane 4g + t holding bytes
     [32b + 8t, +8) of tile row g then of tile row g + 8 (its m16n8k16 A
-    fragments), then the 16 rows' fp32 absmax of block b in row order."""
+    fragments), then the 16 rows' fp32 absmax of block b as (row g, row g + 8)
+    pairs for g = 0..7 (rows 0, 8, 1, 9, ...: lane g's two scales together)."""
 
     rows = tuple(m[2] for m in mats) + (0,) * (3 - len(mats))
     msel, rsel = tile16_rows(mode, rows, head_dim)
@@ -422,7 +423,8 @@ def retile_tiles16(mode: int, mats: list[tuple[np.ndarray, np.ndarray, int]], k:
     codes[..., 8:] = d[:, 8:].transpose(0, 2, 1, 3, 4)
     units = np.empty((tiles, nbpt, 576), dtype=np.uint8)
     units[:, :, :512] = codes.reshape(tiles, nbpt, 512)
-    units[:, :, 512:] = np.ascontiguousarray(amax.transpose(0, 2, 1)).view(np.uint8).reshape(tiles, nbpt, 64)
+    pairs = [r for g in range(8) for r in (g, g + 8)]
+    units[:, :, 512:] = np.ascontiguousarray(amax.transpose(0, 2, 1)[:, :, pairs]).view(np.uint8).reshape(tiles, nbpt, 64)
     return units.reshape(-1)
 
 
