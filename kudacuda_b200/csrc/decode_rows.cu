@@ -543,6 +543,7 @@ __device__ void rstage_norm(const RowArgs& a, const uint16_t* xres, const uint4*
     const int tid = threadIdx.x;
     const int n8 = a.hidden / 8;
     float ss = 0.F;
+#pragma unroll 4
     for (int i = tid; i < a.hidden; i += kRT) {
         const float v = bf16_bits_to_f32(xres[i]);
         ss += v * v;
@@ -551,10 +552,17 @@ __device__ void rstage_norm(const RowArgs& a, const uint16_t* xres, const uint4*
     if ((tid & 31) == 0) red[tid >> 5] = ss;
     __syncthreads();
     KR_STAMP(layer, stamp);
+    const float4* r4 = reinterpret_cast<const float4*>(red);  // the 16 warp sums, added in order
+    const float4 q0 = r4[0], q1 = r4[1], q2 = r4[2], q3 = r4[3];
     float tot = 0.F;
-#pragma unroll
-    for (int i = 0; i < kRW; ++i) tot += red[i];
-    const float inv = 1.0F / sqrtf(tot / static_cast<float>(a.hidden) + a.eps);
+    tot += q0.x; tot += q0.y; tot += q0.z; tot += q0.w;
+    tot += q1.x; tot += q1.y; tot += q1.z; tot += q1.w;
+    tot += q2.x; tot += q2.y; tot += q2.z; tot += q2.w;
+    tot += q3.x; tot += q3.y; tot += q3.z; tot += q3.w;
+    // the mean: a power-of-two hidden size divides exactly by multiplying with its reciprocal
+    const float nh = static_cast<float>(a.hidden);
+    const float mean = (a.hidden & (a.hidden - 1)) == 0 ? tot * (1.0F / nh) : tot / nh;
+    const float inv = 1.0F / sqrtf(mean + a.eps);
     bool overflow = false;
 #pragma unroll
     for (int i = 0; i < kNormPer; ++i) {
@@ -912,7 +920,7 @@ template <bool kTP>
 __global__ void __launch_bounds__(kRT, 1) decode_rows_kernel(const RowArgs a) {
     extern __shared__ __align__(128) uint8_t dsm[];
     __shared__ __align__(8) uint64_t bars_all[kRW * kRMaxSlots];
-    __shared__ float red[kRW];
+    __shared__ __align__(16) float red[kRW];
     __shared__ int rng[4 * kRngStride];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
